@@ -1,0 +1,291 @@
+// Shared device helpers for the brain_b200 sm_100a kernels.
+//
+// Everything here is written for Blackwell (sm_100a): mbarrier/TMA/tcgen05 wrappers in inline
+// PTX, bounded spin-waits that report through a device status word instead of hanging, and small
+// vector/reduction utilities used by the memory-bound kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+
+#define BRAIN_API extern "C" __attribute__((visibility("default")))
+
+// ---------------------------------------------------------------------------------------------
+// Status word. Kernels never trap: a wait that runs out of time records a code here and returns.
+// The host reads (and clears) it with brain_status_read().
+// ---------------------------------------------------------------------------------------------
+enum BrainStatus : int {
+  BRAIN_OK = 0,
+  BRAIN_ERR_TIMEOUT_FULL = 1,      // consumer waited too long for a producer stage
+  BRAIN_ERR_TIMEOUT_EMPTY = 2,     // producer waited too long for a free stage
+  BRAIN_ERR_TIMEOUT_ACC = 3,       // accumulator hand-off timed out
+  BRAIN_ERR_TIMEOUT_PEER = 4,      // a peer rank's flag never arrived
+  BRAIN_ERR_BAD_ARG = 5,           // device-side argument check failed
+  BRAIN_ERR_BOUNDS = 6,            // debug bounds check failed
+};
+
+namespace brain {
+
+// One status word per translation unit (static linkage); each .cu file exports a reader through
+// BRAIN_STATUS_READER so the host can poll every library without relocatable device code.
+static __device__ int g_status = 0;        // first error code recorded (0 = ok)
+static __device__ int g_status_where = 0;  // kernel-specific location tag of the first error
+
+__device__ __forceinline__ void set_status(int code, int where) {
+  if (atomicCAS(&g_status, 0, code) == 0) g_status_where = where;
+}
+
+__device__ __forceinline__ uint64_t globaltimer() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wall-clock budget of one spin-wait before it gives up (nanoseconds).
+constexpr uint64_t kWaitBudgetNs = 2000000000ull;  // 2 s
+
+// ---------------------------------------------------------------------------------------------
+// Math helpers
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// 8 x bf16 packed in 16 bytes.
+struct alignas(16) bf16x8 {
+  __nv_bfloat162 h[4];
+};
+
+__device__ __forceinline__ void load8(const __nv_bfloat16* p, float* f) {
+  bf16x8 v = *reinterpret_cast<const bf16x8*>(p);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(v.h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* f) {
+  bf16x8 v;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) v.h[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+  *reinterpret_cast<bf16x8*>(p) = v;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Shared-memory addressing, mbarriers and TMA (cp.async.bulk.tensor, no multicast anywhere).
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("{ .reg .b64 st; mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1; }" ::"r"(bar),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait on an mbarrier phase. Returns false (and records `code`) when the budget runs out
+// or when `abort_flag` (shared memory, may be null) was raised by another role of the CTA.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int code, int where,
+                                          volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  uint64_t t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (abort_flag && *abort_flag) return false;
+      if (globaltimer() - t0 > kWaitBudgetNs) {
+        set_status(code, where);
+        if (abort_flag) *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// 2-D tiled TMA load into this CTA's shared memory, completing on `bar` (complete_tx::bytes).
+__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint32_t dst, uint32_t bar, int x,
+                                            int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+// 3-D tiled TMA load.
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint32_t dst, uint32_t bar, int x,
+                                            int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, "
+      "%4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{ .reg .b32 rx; .reg .pred px; elect.sync rx|px, %1; selp.b32 %0, 1, 0, px; }"
+      : "=r"(pred)
+      : "r"(0xffffffffu));
+  return pred != 0;
+}
+
+// ---------------------------------------------------------------------------------------------
+// tcgen05 (5th-generation tensor core) wrappers. TMEM addresses: bits [31:16] lane, [15:0] column.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::f16 (bf16/f16 inputs, f32 accumulate).
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// kind::f8f6f4 (e4m3/e5m2 inputs, f32 accumulate).
+__device__ __forceinline__ void tc_mma_f8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on an mbarrier once all previously issued tcgen05 ops of this thread complete.
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 columns of 32-bit from TMEM: thread t of the warp gets row (lane base + t),
+// columns [col, col+32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+// 32 lanes x 16 columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+      "[%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15])
+      : "r"(taddr));
+}
+
+// Shared-memory matrix descriptor for tcgen05 (SWIZZLE_128B canonical layouts).
+//   start: smem byte address; lbo/sbo: leading/stride byte offsets; layout 2 = SWIZZLE_128B.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t start, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((start >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;  // descriptor version for sm_100
+  d |= (uint64_t)2u << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor for kind::f16 with f32 accumulation.
+//   ab_fmt: 0 = f16, 1 = bf16. a_mn/b_mn: 1 if the operand is MN-major in shared memory.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, uint32_t ab_fmt, uint32_t a_mn, uint32_t b_mn) {
+  return (1u << 4)                       // D format f32
+         | (ab_fmt << 7) | (ab_fmt << 10)  // A, B format
+         | (a_mn << 15) | (b_mn << 16)     // majorness
+         | ((uint32_t)(N >> 3) << 17)      // N / 8
+         | ((uint32_t)(M >> 4) << 24);     // M / 16
+}
+// Instruction descriptor for kind::f8f6f4 (e4m3 = 0, e5m2 = 1) with f32 accumulation.
+__host__ __device__ constexpr uint32_t idesc_f8(int M, int N, uint32_t a_fmt, uint32_t b_fmt, uint32_t a_mn,
+                                                uint32_t b_mn) {
+  return (1u << 4) | (a_fmt << 7) | (b_fmt << 10) | (a_mn << 15) | (b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+
+}  // namespace brain
+
+// Exported reader of this translation unit's status word: returns the code, writes the location
+// tag to *where, and clears both when `clear` is non-zero. Synchronous (cudaMemcpyFromSymbol).
+#define BRAIN_STATUS_READER(name)                                                     \
+  BRAIN_API int brain_status_##name(int* where, int clear) {                          \
+    int code = 0, w = 0;                                                              \
+    if (cudaMemcpyFromSymbol(&code, brain::g_status, sizeof(int)) != cudaSuccess) return -1; \
+    cudaMemcpyFromSymbol(&w, brain::g_status_where, sizeof(int));                     \
+    if (where) *where = w;                                                            \
+    if (clear && code) {                                                              \
+      int z = 0;                                                                      \
+      cudaMemcpyToSymbol(brain::g_status, &z, sizeof(int));                           \
+      cudaMemcpyToSymbol(brain::g_status_where, &z, sizeof(int));                     \
+    }                                                                                 \
+    return code;                                                                      \
+  }
+
+// Host-side helpers ---------------------------------------------------------------------------
+namespace brain_host {
+// Number of SMs of the current device (cached per device).
+int num_sms();
+// cuTensorMapEncodeTiled resolved through the runtime's driver entry point (no -lcuda needed).
+bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, void* base, const uint64_t* dims,
+                  const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz);
+}  // namespace brain_host

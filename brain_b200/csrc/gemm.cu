@@ -1,0 +1,465 @@
+// Dense bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+//   C[M,N] = alpha * op(A)[M,K] * op(B)[K,N]  (+ beta * C_old) (+ bias[N]) (+ R[M,N])
+//
+// op(A): A stored [M,K] row-major ("K-major") or [K,M] row-major ("M-major").
+// op(B): B stored [N,K] row-major ("K-major", i.e. a PyTorch Linear weight) or [K,N] ("N-major").
+// These four combinations cover Linear forward (x W^T), data-gradient (dy W) and weight-gradient
+// (dy^T x) without any transpose copies: the tensor core reads MN-major shared-memory tiles directly.
+//
+// Design (one persistent CTA per SM, 6 warps):
+//   warp 0      TMA producer: cp.async.bulk.tensor 2-D tiles (SWIZZLE_128B) into a S-stage ring.
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128, N=BN, K=16) into a TMEM
+//               accumulator, tcgen05.commit frees the smem stage; TMEM is double-buffered so the
+//               epilogue of tile i overlaps the main loop of tile i+1. Warp 1 also owns TMEM alloc.
+//   warps 2..5  epilogue: tcgen05.ld 32x32b -> registers -> alpha/beta/bias/residual -> bf16/f32.
+// Every wait is bounded (globaltimer); a timeout records a status code and all roles drain and
+// return, releasing TMEM. No TMA load uses cluster multicast.
+//
+// Reference parity: brain-core `matmul` / `blas::gemm` (crates/brain-core/src/tensor/arithmetic.rs:174,
+// crates/brain-core/src/tensor/blas.rs:227) compute the same product in f64 on the CPU.
+#include "common.cuh"
+
+#include <mutex>
+#include <unordered_map>
+
+using namespace brain;
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 B = one swizzle row
+constexpr int kThreads = 192;
+constexpr int kGroupM = 16;  // tile rasterisation group (L2 reuse)
+
+struct GemmArgs {
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles;
+  void* C;
+  int64_t ldc;
+  int c_f32;
+  int accumulate;
+  float alpha, beta;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* R;
+  int64_t ldr;
+};
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFFSET = STAGES * STAGE_BYTES;
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], drain[1]; then tmem base + abort flag
+  static constexpr int TOTAL = BAR_OFFSET + (2 * STAGES + 5) * 8 + 16 + 1024 /*alignment slack*/;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int& tm, int& tn) {
+  int group_size = kGroupM * tiles_n;
+  int group = t / group_size;
+  int first_m = group * kGroupM;
+  int gm = min(tiles_m - first_m, kGroupM);
+  int r = t - group * group_size;
+  tm = first_m + r % gm;
+  tn = r / gm;
+}
+
+template <int BN, int STAGES, int A_MN, int B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   GemmArgs args) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar_base = sbase + S::BAR_OFFSET;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * STAGES + 2 + a); };
+  const uint32_t drain_bar = bar_base + 8u * (2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::BAR_OFFSET + (2 * STAGES + 5) * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  constexpr uint32_t kTmemCols = 2 * BN;  // double-buffered f32 accumulator (power of two >= 32)
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int num_kb = (args.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    // ------------------------------- TMA producer -------------------------------
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t round = it / STAGES;
+          if (!mbar_wait(empty_bar(s), (round & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 10, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = sbase + s * S::STAGE_BYTES;
+          const uint32_t sb = sa + S::A_BYTES;
+          mbar_arrive_expect_tx(full_bar(s), S::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(&tmA, sa + j * (64 * BK * 2), full_bar(s), m0 + 64 * j, k0);
+          } else {
+            tma_load_2d(&tmA, sa, full_bar(s), k0, m0);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(&tmB, sb + j * (64 * BK * 2), full_bar(s), n0 + 64 * j, k0);
+          } else {
+            tma_load_2d(&tmB, sb, full_bar(s), k0, n0);
+          }
+        }
+      }
+      if (!ok) {
+        // Drain: let the copies already issued land before the CTA exits.
+        uint32_t first = it > (uint32_t)STAGES ? it - STAGES : 0;
+        for (uint32_t j = first; j < it; ++j) {
+          uint32_t s = j % STAGES, round = j / STAGES;
+          uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(full_bar(s), round & 1) && globaltimer() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer -------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(BM, BN, 1u, (uint32_t)A_MN, (uint32_t)B_MN);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int t = blockIdx.x; t < args.num_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_round = (uint32_t)(local >> 1);
+        if (!mbar_wait(tempty_bar(acc), (acc_round & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 20, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t round = it / STAGES;
+          if (!mbar_wait(full_bar(s), round & 1, BRAIN_ERR_TIMEOUT_FULL, 21, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = sbase + s * S::STAGE_BYTES;
+          const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t adesc = A_MN ? smem_desc_sw128(sa + kk * 2048, 64 * BK * 2, 1024)
+                                  : smem_desc_sw128(sa + kk * 32, 16, 1024);
+            uint64_t bdesc = B_MN ? smem_desc_sw128(sb + kk * 2048, 64 * BK * 2, 1024)
+                                  : smem_desc_sw128(sb + kk * 32, 16, 1024);
+            tc_mma_f16(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued = true;
+          tc_commit(empty_bar(s));  // smem stage free once these MMAs have read it
+        }
+        if (!ok) break;
+        tc_commit(tfull_bar(acc));  // accumulator ready for the epilogue
+      }
+      if (!ok && issued) {
+        // Drain outstanding tensor-core work before the CTA releases TMEM.
+        tc_commit(drain_bar);
+        uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(drain_bar, 0) && globaltimer() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ------------------------------- epilogue (warps 2..5) -------------------------------
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < args.num_tiles; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_round = (uint32_t)(local >> 1);
+      if (!mbar_wait(tfull_bar(acc), acc_round & 1, BRAIN_ERR_TIMEOUT_ACC, 30, abort_flag)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+      const int gm = tm * BM + row_in_tile;
+      const int n0 = tn * BN;
+      const bool row_ok = gm < args.M;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld32(tmem_base + (uint32_t)(acc * BN + c * 32) + ((uint32_t)(q * 32) << 16), r);
+        tc_wait_ld();
+        const int gn0 = n0 + c * 32;
+        if (row_ok && gn0 < args.N) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
+        const bool full = gn0 + 32 <= args.N;
+        if (args.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (full || gn0 + j < args.N) v[j] += __bfloat162float(args.bias[gn0 + j]);
+        }
+        if (args.R) {
+          const __nv_bfloat16* rp = args.R + (int64_t)gm * args.ldr + gn0;
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (full || gn0 + j < args.N) v[j] += __bfloat162float(rp[j]);
+        }
+        if (args.c_f32) {
+          float* cp = reinterpret_cast<float*>(args.C) + (int64_t)gm * args.ldc + gn0;
+          if (full && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              if (args.accumulate) {
+                float4 old = *reinterpret_cast<const float4*>(cp + j);
+                o.x += args.beta * old.x; o.y += args.beta * old.y; o.z += args.beta * old.z; o.w += args.beta * old.w;
+              }
+              *reinterpret_cast<float4*>(cp + j) = o;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (gn0 + j < args.N) cp[j] = v[j] + (args.accumulate ? args.beta * cp[j] : 0.f);
+          }
+        } else {
+          __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(args.C) + (int64_t)gm * args.ldc + gn0;
+          if (full && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              if (args.accumulate) {
+                float old[8];
+                load8(cp + j, old);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) v[j + u] += args.beta * old[u];
+              }
+              store8(cp + j, v + j);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (gn0 + j < args.N) {
+                float o = v[j] + (args.accumulate ? args.beta * __bfloat162float(cp[j]) : 0.f);
+                cp[j] = __float2bfloat16_rn(o);
+              }
+            }
+          }
+        }
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      mbar_arrive(tempty_bar(acc));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// Tensor-map cache: encoding is cheap but not free, and training re-uses the same operands.
+struct MapKey {
+  uintptr_t ptr;
+  uint64_t d0, d1, s1;
+  uint32_t b0, b1;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && d0 == o.d0 && d1 == o.d1 && s1 == o.s1 && b0 == o.b0 && b1 == o.b1;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    size_t h = k.ptr * 0x9E3779B97F4A7C15ull;
+    h ^= (k.d0 + 0x632BE59BD9B4E019ull + (h << 6) + (h >> 2));
+    h ^= (k.d1 * 31 + k.s1 * 131 + k.b0 * 7 + k.b1 + (h << 6) + (h >> 2));
+    return h;
+  }
+};
+
+bool get_map_2d(CUtensorMap* out, const void* ptr, uint64_t inner, uint64_t outer, uint64_t ld_elems,
+                uint32_t box_inner, uint32_t box_outer, CUtensorMapDataType dt, int elem_bytes) {
+  static std::mutex mu;
+  static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  MapKey key{reinterpret_cast<uintptr_t>(ptr) ^ ((uintptr_t)dev << 56), inner, outer, ld_elems, box_inner, box_outer};
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto itr = cache.find(key);
+    if (itr != cache.end()) {
+      *out = itr->second;
+      return true;
+    }
+  }
+  uint64_t dims[2] = {inner, outer};
+  uint64_t strides[1] = {ld_elems * (uint64_t)elem_bytes};
+  uint32_t box[2] = {box_inner, box_outer};
+  if (!brain_host::encode_tiled(out, dt, 2, const_cast<void*>(ptr), dims, strides, box,
+                                CU_TENSOR_MAP_SWIZZLE_128B))
+    return false;
+  std::lock_guard<std::mutex> g(mu);
+  if (cache.size() > 4096) cache.clear();
+  cache[key] = *out;
+  return true;
+}
+
+template <int BN, int STAGES, int A_MN, int B_MN>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+  using S = Smem<BN, STAGES>;
+  auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
+    attr_set[dev & 63] = true;
+  }
+  int grid = std::min(a.num_tiles, brain_host::num_sms());
+  kern<<<grid, kThreads, S::TOTAL, st>>>(ta, tb, a);
+  return (int)cudaGetLastError();
+}
+
+// Simple SIMT fallback for shapes the TMA path cannot describe (unaligned strides). f32 accumulate.
+__global__ void gemm_simt_kernel(const __nv_bfloat16* A, int64_t lda, int a_mn, const __nv_bfloat16* B,
+                                 int64_t ldb, int b_mn, GemmArgs args) {
+  __shared__ float As[32][33];
+  __shared__ float Bs[32][33];
+  const int tx = threadIdx.x % 32, ty = threadIdx.x / 32;  // 32 x 8 threads
+  const int m0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int k0 = 0; k0 < args.K; k0 += 32) {
+    for (int i = ty; i < 32; i += 8) {
+      int m = m0 + i, k = k0 + tx;
+      float av = 0.f;
+      if (m < args.M && k < args.K) av = __bfloat162float(a_mn ? A[(int64_t)k * lda + m] : A[(int64_t)m * lda + k]);
+      As[i][tx] = av;
+      int n = n0 + i;
+      float bv = 0.f;
+      if (n < args.N && k < args.K) bv = __bfloat162float(b_mn ? B[(int64_t)k * ldb + n] : B[(int64_t)n * ldb + k]);
+      Bs[i][tx] = bv;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < 32; ++kk) {
+      float b = Bs[tx][kk];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) acc[r] += As[ty + 8 * r][kk] * b;
+    }
+    __syncthreads();
+  }
+  const int n = n0 + tx;
+  if (n >= args.N) return;
+  for (int r = 0; r < 4; ++r) {
+    int m = m0 + ty + 8 * r;
+    if (m >= args.M) continue;
+    float v = acc[r] * args.alpha;
+    if (args.bias) v += __bfloat162float(args.bias[n]);
+    if (args.R) v += __bfloat162float(args.R[(int64_t)m * args.ldr + n]);
+    if (args.c_f32) {
+      float* cp = reinterpret_cast<float*>(args.C) + (int64_t)m * args.ldc + n;
+      *cp = v + (args.accumulate ? args.beta * *cp : 0.f);
+    } else {
+      __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(args.C) + (int64_t)m * args.ldc + n;
+      *cp = __float2bfloat16_rn(v + (args.accumulate ? args.beta * __bfloat162float(*cp) : 0.f));
+    }
+  }
+}
+
+}  // namespace
+
+BRAIN_STATUS_READER(gemm)
+
+// C = alpha * op(A) op(B) (+ beta*C if accumulate) (+ bias) (+ R).
+//   a_mn = 0: A is [M,K] with row stride lda; a_mn = 1: A is [K,M] with row stride lda.
+//   b_mn = 0: B is [N,K] with row stride ldb; b_mn = 1: B is [K,N] with row stride ldb.
+//   force_simt: 1 = use the SIMT fallback (tests), 0 = tensor cores when the layout allows.
+BRAIN_API int brain_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn, void* C,
+                              int64_t ldc, int c_f32, int M, int N, int K, float alpha, int accumulate, float beta,
+                              const void* bias, const void* R, int64_t ldr, int force_simt, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return 0;
+  GemmArgs a;
+  a.M = M; a.N = N; a.K = K;
+  a.C = C; a.ldc = ldc; a.c_f32 = c_f32; a.accumulate = accumulate;
+  a.alpha = alpha; a.beta = beta;
+  a.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  a.R = reinterpret_cast<const __nv_bfloat16*>(R);
+  a.ldr = ldr;
+  const bool aligned = (lda % 8 == 0) && (ldb % 8 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0) &&
+                       ((reinterpret_cast<uintptr_t>(B) & 15) == 0) && K >= 16;
+  if (K <= 0) {
+    // Degenerate K: result is the epilogue of a zero product; use the SIMT kernel (loops zero times).
+    force_simt = 1;
+  }
+  if (force_simt || !aligned) {
+    dim3 grid((N + 31) / 32, (M + 31) / 32);
+    gemm_simt_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(A), lda, a_mn,
+                                              reinterpret_cast<const __nv_bfloat16*>(B), ldb, b_mn, a);
+    return (int)cudaGetLastError();
+  }
+  const int BN = (N <= 128) ? 128 : 256;
+  a.tiles_m = (M + BM - 1) / BM;
+  a.tiles_n = (N + BN - 1) / BN;
+  a.num_tiles = a.tiles_m * a.tiles_n;
+  CUtensorMap ta, tb;
+  bool ok;
+  // A operand
+  if (a_mn) ok = get_map_2d(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, BK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+  else ok = get_map_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+  if (!ok) return (int)cudaErrorInvalidValue;
+  if (b_mn) ok = get_map_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+  else ok = get_map_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, (uint32_t)BN, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+  if (!ok) return (int)cudaErrorInvalidValue;
+#define BRAIN_GEMM_CASE(BN_, ST_)                                                   \
+  if (a_mn == 0 && b_mn == 0) return launch_tc<BN_, ST_, 0, 0>(ta, tb, a, stream); \
+  if (a_mn == 0 && b_mn == 1) return launch_tc<BN_, ST_, 0, 1>(ta, tb, a, stream); \
+  if (a_mn == 1 && b_mn == 0) return launch_tc<BN_, ST_, 1, 0>(ta, tb, a, stream); \
+  return launch_tc<BN_, ST_, 1, 1>(ta, tb, a, stream);
+  if (BN == 128) {
+    BRAIN_GEMM_CASE(128, 6)
+  } else {
+    BRAIN_GEMM_CASE(256, 4)
+  }
+#undef BRAIN_GEMM_CASE
+}

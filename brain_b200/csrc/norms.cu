@@ -1,0 +1,264 @@
+// Row normalisations (RMSNorm, LayerNorm) forward and backward, bf16 in/out, f32 statistics.
+//
+// One CTA per row for the forward pass: each thread keeps its slice of the row in registers
+// (16-byte vector loads, up to 4 vectors = 32 values per thread), so a row is read from HBM once.
+// The optional residual input is added first and the sum is written out (fused add+norm).
+// Backward is a persistent grid: each CTA walks rows blockIdx.x, blockIdx.x + gridDim.x, ... and
+// accumulates dgamma/dbeta for its fixed columns in registers, then writes one f32 partial row;
+// a column-reduction kernel sums the partials (deterministic, no atomics).
+//
+// Reference semantics (f64 in the reference):
+//   RMSNorm  y = x * (mean(x^2) + eps)^-1/2 * w       crates/brain-transformer/src/ops.rs:103-131,
+//            fused_add_rmsnorm returns (norm, sum)      crates/brain-core/src/tensor/ops_fused.rs:77-125
+//   LayerNorm y = (x - mean) / sqrt(var + eps) * w + b, biased variance
+//                                                      crates/brain-transformer/src/ops.rs:57-101
+#include "common.cuh"
+
+using namespace brain;
+
+namespace {
+
+constexpr int VPT = 4;  // 8-element vectors per thread
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32, nw = (blockDim.x + 31) / 32;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (l < nw) ? red[l] : 0.f;
+  return warp_sum(t);
+}
+
+// ---------------------------------------------------------------- forward
+template <bool LAYERNORM>
+__global__ void norm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ res,
+                                int64_t ldres, const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ b,
+                                __nv_bfloat16* __restrict__ y, int64_t ldy, __nv_bfloat16* __restrict__ sum_out,
+                                int64_t ldsum, float* __restrict__ mean_out, float* __restrict__ rstd_out, int D,
+                                float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int nvec = D / 8;
+  float v[VPT][8];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) {
+      load8(x + row * ldx + vi * 8, v[i]);
+      if (res) {
+        float r[8];
+        load8(res + row * ldres + vi * 8, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] += r[j];
+        // the sum is rounded to bf16 before normalisation, exactly what a separate add would store
+        store8(sum_out + row * ldsum + vi * 8, v[i]);
+        load8(sum_out + row * ldsum + vi * 8, v[i]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) s += LAYERNORM ? v[i][j] : v[i][j] * v[i][j];
+    }
+  }
+  float mean = 0.f, rstd;
+  if (LAYERNORM) {
+    mean = block_sum(s, red) / D;
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = threadIdx.x + i * blockDim.x;
+      if (vi < nvec) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float d = v[i][j] - mean;
+          q += d * d;
+        }
+      }
+    }
+    rstd = rsqrtf(block_sum(q, red) / D + eps);
+  } else {
+    rstd = rsqrtf(block_sum(s, red) / D + eps);
+  }
+  if (threadIdx.x == 0) {
+    if (rstd_out) rstd_out[row] = rstd;
+    if (LAYERNORM && mean_out) mean_out[row] = mean;
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) {
+      float wv[8], o[8];
+      load8(w + vi * 8, wv);
+      if (LAYERNORM && b) {
+        float bv[8];
+        load8(b + vi * 8, bv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = (v[i][j] - mean) * rstd * wv[j] + bv[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = (v[i][j] - mean) * rstd * wv[j];
+      }
+      store8(y + row * ldy + vi * 8, o);
+    }
+  }
+}
+
+// ---------------------------------------------------------------- backward
+// dx = rstd * (g - [mean(g)] - xhat * mean(g * xhat)),  g = w * dy
+// dw += dy * xhat ; db += dy    (per-CTA partials, f32)
+template <bool LAYERNORM>
+__global__ void norm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t lddy, const __nv_bfloat16* __restrict__ x,
+                                int64_t ldx, const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean_in,
+                                const float* __restrict__ rstd_in, __nv_bfloat16* __restrict__ dx, int64_t lddx,
+                                const __nv_bfloat16* __restrict__ dres, int64_t lddres, float* __restrict__ dw_part,
+                                float* __restrict__ db_part, int M, int D) {
+  __shared__ float red[32];
+  const int nvec = D / 8;
+  float dwacc[VPT][8], dbacc[VPT][8];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dwacc[i][j] = dbacc[i][j] = 0.f;
+  float wv[VPT][8];
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) load8(w + vi * 8, wv[i]);
+  }
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x) {
+    const float rstd = rstd_in[row];
+    const float mean = LAYERNORM ? mean_in[row] : 0.f;
+    float xh[VPT][8], g[VPT][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = threadIdx.x + i * blockDim.x;
+      if (vi < nvec) {
+        float dv[8];
+        load8(x + row * ldx + vi * 8, xh[i]);
+        load8(dy + row * lddy + vi * 8, dv);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          xh[i][j] = (xh[i][j] - mean) * rstd;
+          g[i][j] = dv[j] * wv[i][j];
+          dwacc[i][j] += dv[j] * xh[i][j];
+          if (LAYERNORM) dbacc[i][j] += dv[j];
+          s1 += g[i][j];
+          s2 += g[i][j] * xh[i][j];
+        }
+      }
+    }
+    const float c2 = block_sum(s2, red) / D;
+    const float c1 = LAYERNORM ? block_sum(s1, red) / D : 0.f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int vi = threadIdx.x + i * blockDim.x;
+      if (vi < nvec) {
+        float o[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] = rstd * (g[i][j] - c1 - xh[i][j] * c2);
+        if (dres) {
+          float r[8];
+          load8(dres + row * lddres + vi * 8, r);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) o[j] += r[j];
+        }
+        store8(dx + row * lddx + vi * 8, o);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) {
+      float* p = dw_part + (int64_t)blockIdx.x * D + vi * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) p[j] = dwacc[i][j];
+      if (LAYERNORM && db_part) {
+        float* q = db_part + (int64_t)blockIdx.x * D + vi * 8;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = dbacc[i][j];
+      }
+    }
+  }
+}
+
+// out[d] (+)= sum_p part[p, d]; out dtype bf16 (out_f32 = 0) or f32.
+__global__ void colsum_kernel(const float* __restrict__ part, int P, int D, void* out, int out_f32, int accumulate) {
+  const int d = blockIdx.x * blockDim.x + threadIdx.x;
+  if (d >= D) return;
+  float s = 0.f;
+  for (int p = 0; p < P; ++p) s += part[(int64_t)p * D + d];
+  if (out_f32) {
+    float* o = reinterpret_cast<float*>(out);
+    o[d] = accumulate ? o[d] + s : s;
+  } else {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
+    o[d] = __float2bfloat16_rn(accumulate ? __bfloat162float(o[d]) + s : s);
+  }
+}
+
+int threads_for(int D) {
+  int nvec = D / 8;
+  int t = (nvec + VPT - 1) / VPT;
+  t = ((t + 31) / 32) * 32;
+  return t < 32 ? 32 : t;
+}
+
+}  // namespace
+
+BRAIN_STATUS_READER(norms)
+
+// kind: 0 = RMSNorm, 1 = LayerNorm.  res/sum_out optional (fused residual add).
+BRAIN_API int brain_norm_fwd(int kind, const void* x, int64_t ldx, const void* res, int64_t ldres, const void* w,
+                             const void* b, void* y, int64_t ldy, void* sum_out, int64_t ldsum, float* mean_out,
+                             float* rstd_out, int M, int D, float eps, cudaStream_t st) {
+  if (M == 0) return 0;
+  if (D % 8 != 0 || D > 1024 * VPT * 8) return (int)cudaErrorInvalidValue;
+  const int T = threads_for(D);
+  if (T > 1024) return (int)cudaErrorInvalidValue;
+  auto X = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto R = reinterpret_cast<const __nv_bfloat16*>(res);
+  auto W = reinterpret_cast<const __nv_bfloat16*>(w);
+  auto Bp = reinterpret_cast<const __nv_bfloat16*>(b);
+  auto Y = reinterpret_cast<__nv_bfloat16*>(y);
+  auto S = reinterpret_cast<__nv_bfloat16*>(sum_out);
+  if (kind == 0)
+    norm_fwd_kernel<false><<<M, T, 0, st>>>(X, ldx, R, ldres, W, Bp, Y, ldy, S, ldsum, mean_out, rstd_out, D, eps);
+  else
+    norm_fwd_kernel<true><<<M, T, 0, st>>>(X, ldx, R, ldres, W, Bp, Y, ldy, S, ldsum, mean_out, rstd_out, D, eps);
+  return (int)cudaGetLastError();
+}
+
+// Number of f32 partial rows the backward pass needs in its workspace (per gamma/beta).
+BRAIN_API int brain_norm_bwd_partials(int M) {
+  int p = 2 * brain_host::num_sms();
+  return M < p ? (M > 0 ? M : 1) : p;
+}
+
+// dres optional: gradient flowing into the residual stream, added to dx.
+// dw/db: outputs (bf16 or f32 via dw_f32), accumulated when accumulate != 0. db may be null.
+// workspace: f32 [2 * partials * D].
+BRAIN_API int brain_norm_bwd(int kind, const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
+                             const float* mean_in, const float* rstd_in, void* dx, int64_t lddx, const void* dres,
+                             int64_t lddres, void* dw, void* db, int dw_f32, int accumulate, float* workspace, int M,
+                             int D, cudaStream_t st) {
+  if (M == 0) return 0;
+  if (D % 8 != 0 || D > 1024 * VPT * 8) return (int)cudaErrorInvalidValue;
+  const int T = threads_for(D);
+  const int P = brain_norm_bwd_partials(M);
+  float* dwp = workspace;
+  float* dbp = workspace + (int64_t)P * D;
+  auto DY = reinterpret_cast<const __nv_bfloat16*>(dy);
+  auto X = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto W = reinterpret_cast<const __nv_bfloat16*>(w);
+  auto DX = reinterpret_cast<__nv_bfloat16*>(dx);
+  auto DR = reinterpret_cast<const __nv_bfloat16*>(dres);
+  if (kind == 0)
+    norm_bwd_kernel<false><<<P, T, 0, st>>>(DY, lddy, X, ldx, W, mean_in, rstd_in, DX, lddx, DR, lddres, dwp, nullptr, M, D);
+  else
+    norm_bwd_kernel<true><<<P, T, 0, st>>>(DY, lddy, X, ldx, W, mean_in, rstd_in, DX, lddx, DR, lddres, dwp, dbp, M, D);
+  colsum_kernel<<<(D + 255) / 256, 256, 0, st>>>(dwp, P, D, dw, dw_f32, accumulate);
+  if (kind == 1 && db) colsum_kernel<<<(D + 255) / 256, 256, 0, st>>>(dbp, P, D, db, dw_f32, accumulate);
+  return (int)cudaGetLastError();
+}

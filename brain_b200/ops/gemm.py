@@ -1,0 +1,106 @@
+"""GEMM front-end over the tcgen05 kernel (``csrc/gemm.cu``).
+
+``gemm(a, b, trans_a, trans_b)`` computes ``op(a) @ op(b)`` with ``op(x) = x.T`` when the flag is
+set, reading transposed operands in place (the kernel consumes MN-major shared-memory tiles), so
+Linear forward, data-gradient and weight-gradient all run without transpose copies.
+Epilogue options: ``alpha`` scaling, ``out`` accumulation (``beta * out``), ``bias`` [N] and a
+``residual`` [M, N] added in the same pass.
+
+On CPU tensors the same contract is evaluated with ``torch.matmul`` in float32 (the oracle path);
+CUDA tensors always take the native kernel.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _native
+
+
+def _row_major(x: torch.Tensor) -> torch.Tensor:
+    if x.dim() != 2:
+        raise ValueError("gemm operands must be 2-D")
+    if x.stride(1) != 1 or x.stride(0) < x.size(1):
+        x = x.contiguous()
+    return x
+
+
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    trans_a: bool = False,
+    trans_b: bool = False,
+    *,
+    out: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+    alpha: float = 1.0,
+    beta: float = 0.0,
+    bias: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    force_simt: bool = False,
+) -> torch.Tensor:
+    """C = alpha * op(a) @ op(b) [+ beta * out] [+ bias] [+ residual].
+
+    ``beta`` is only used when ``out`` is given (accumulation into an existing buffer).
+    """
+    a = _row_major(a)
+    b = _row_major(b)
+    M, K = (a.size(1), a.size(0)) if trans_a else (a.size(0), a.size(1))
+    Kb, N = (b.size(1), b.size(0)) if trans_b else (b.size(0), b.size(1))
+    if K != Kb:
+        raise ValueError(f"gemm shape mismatch: op(a) is {M}x{K}, op(b) is {Kb}x{N}")
+    accumulate = out is not None and beta != 0.0
+    if out is None:
+        out = torch.empty((M, N), device=a.device, dtype=out_dtype)
+    if out.shape != (M, N):
+        raise ValueError(f"out has shape {tuple(out.shape)}, expected {(M, N)}")
+    if not a.is_cuda:
+        return _gemm_cpu(a, b, trans_a, trans_b, out, alpha, beta if accumulate else 0.0, bias, residual)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise TypeError("CUDA gemm takes bfloat16 operands")
+    if out.dtype not in (torch.bfloat16, torch.float32) or out.stride(1) != 1:
+        raise TypeError("gemm output must be row-major bfloat16 or float32")
+    if bias is not None:
+        bias = bias.contiguous()
+        if bias.dtype != torch.bfloat16 or bias.numel() != N:
+            raise TypeError("bias must be a bfloat16 vector of length N")
+    if residual is not None:
+        residual = _row_major(residual)
+        if residual.dtype != torch.bfloat16 or residual.shape != (M, N):
+            raise TypeError("residual must be bfloat16 [M, N]")
+    _native.call(
+        "brain_gemm_bf16",
+        a.data_ptr(), a.stride(0), int(trans_a),
+        b.data_ptr(), b.stride(0), int(not trans_b),
+        out.data_ptr(), out.stride(0), int(out.dtype == torch.float32),
+        M, N, K, float(alpha), int(accumulate), float(beta),
+        bias.data_ptr() if bias is not None else None,
+        residual.data_ptr() if residual is not None else None,
+        residual.stride(0) if residual is not None else 0,
+        int(force_simt),
+        _native.stream_ptr(a.device),
+    )
+    return out
+
+
+def _gemm_cpu(a, b, ta, tb, out, alpha, beta, bias, residual):
+    A = a.float().t() if ta else a.float()
+    B = b.float().t() if tb else b.float()
+    r = alpha * (A @ B)
+    if beta:
+        r = r + beta * out.float()
+    if bias is not None:
+        r = r + bias.float()
+    if residual is not None:
+        r = r + residual.float()
+    out.copy_(r.to(out.dtype))
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None,
+           residual: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ w.T (+ bias) (+ residual) for x [..., K] and a [N, K] weight."""
+    shp = x.shape
+    y = gemm(x.reshape(-1, shp[-1]), w, trans_b=True, bias=bias,
+             residual=None if residual is None else residual.reshape(-1, w.size(0)),
+             out_dtype=x.dtype if not x.is_cuda else torch.bfloat16)
+    return y.reshape(*shp[:-1], w.size(0))

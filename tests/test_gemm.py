@@ -1,0 +1,71 @@
+"""tcgen05 GEMM numerics against a float32 PyTorch oracle (all four operand majornesses)."""
+import pytest
+import torch
+
+from brain_b200.ops.gemm import gemm
+
+
+def _ref(a, b, ta, tb, alpha=1.0, bias=None, residual=None, out=None, beta=0.0):
+    A = a.float().t() if ta else a.float()
+    B = b.float().t() if tb else b.float()
+    r = alpha * (A @ B)
+    if out is not None and beta:
+        r = r + beta * out.float()
+    if bias is not None:
+        r = r + bias.float()
+    if residual is not None:
+        r = r + residual.float()
+    return r
+
+
+def _mk(shape, device, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return torch.randn(shape, generator=g).to(device=device, dtype=torch.bfloat16)
+
+
+def test_gemm_cpu_contract():
+    a = _mk((33, 40), "cpu", 0)
+    b = _mk((40, 17), "cpu", 1)
+    c = gemm(a, b, out_dtype=torch.float32)
+    torch.testing.assert_close(c, _ref(a, b, False, False), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("tb", [False, True])
+@pytest.mark.parametrize("shape", [(128, 256, 64), (256, 512, 192), (300, 200, 136), (1024, 1024, 1024), (64, 96, 40)])
+def test_gemm_tc_layouts(ta, tb, shape):
+    M, N, K = shape
+    a = _mk((K, M) if ta else (M, K), "cuda", 1)
+    b = _mk((N, K) if tb else (K, N), "cuda", 2)
+    c = gemm(a, b, ta, tb, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    ref = _ref(a, b, ta, tb)
+    torch.testing.assert_close(c, ref, rtol=2e-3, atol=2e-3 * K ** 0.5)
+    from brain_b200 import _native
+    assert _native.status("gemm")[0] == 0
+
+
+@pytest.mark.gpu
+def test_gemm_epilogue_bias_residual_accumulate():
+    M, N, K = 512, 384, 256
+    a = _mk((M, K), "cuda", 3)
+    w = _mk((N, K), "cuda", 4)
+    bias = _mk((N,), "cuda", 5)
+    res = _mk((M, N), "cuda", 6)
+    y = gemm(a, w, trans_b=True, bias=bias, residual=res, alpha=0.5)
+    ref = _ref(a, w, False, True, alpha=0.5, bias=bias, residual=res)
+    torch.testing.assert_close(y.float(), ref, rtol=1e-2, atol=0.1)
+    acc = torch.randn(M, N, device="cuda")
+    acc0 = acc.clone()
+    gemm(a, w, trans_b=True, out=acc, beta=1.0)
+    torch.testing.assert_close(acc, acc0 + _ref(a, w, False, True), rtol=2e-3, atol=2e-2)
+
+
+@pytest.mark.gpu
+def test_gemm_simt_fallback_matches():
+    M, N, K = 100, 70, 48
+    a = _mk((M, K), "cuda", 7)
+    b = _mk((K, N), "cuda", 8)
+    c = gemm(a, b, out_dtype=torch.float32, force_simt=True)
+    torch.testing.assert_close(c, _ref(a, b, False, False), rtol=2e-3, atol=2e-2)
