@@ -35,7 +35,10 @@ CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-Wall", "-Wno
 
 # library name -> list of sources (relative to csrc/). Every CUDA library links host_utils.cu.
 LIBRARIES = {
-    "brain_kernels": ["host_utils.cu", "gemm.cu"],
+    "brain_kernels": [
+        "host_utils.cu", "gemm.cu", "norms.cu", "elementwise.cu", "cross_entropy.cu", "optim.cu",
+        "attention.cu",
+    ],
 }
 # Host-only C++ libraries (g++): the checkpoint codec and the runtime helpers.
 CXX_LIBRARIES: dict = {}

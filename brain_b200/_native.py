@@ -29,7 +29,7 @@ _CODES = {"p": _P, "i": _I, "l": _L, "f": _F, "d": _D, "s": _P}
 # name -> (library, argument codes). 's' marks the trailing cudaStream_t.
 SIGNATURES: dict[str, tuple[str, str]] = {
     "brain_error_string": ("brain_kernels", "i"),
-    "brain_gemm_bf16": ("brain_kernels", "plipliplliiififpplis"),
+    "brain_gemm_bf16": ("brain_kernels", "pliplipliiiififpplis"),
     "brain_status_gemm": ("brain_kernels", "pi"),
 }
 

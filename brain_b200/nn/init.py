@@ -1,0 +1,90 @@
+"""Weight initialisers (crates/brain-nn/src/init/*.rs): kaiming/xavier uniform+normal, normal,
+uniform, zeros/ones, orthogonal, scaled residual init and the seeded N(0, std) used by the
+benchmark configurations. All take an optional ``torch.Generator`` for reproducibility."""
+from __future__ import annotations
+
+import math
+
+import torch
+
+
+def _fan(t: torch.Tensor):
+    if t.dim() < 2:
+        return t.numel(), t.numel()
+    recept = t[0][0].numel() if t.dim() > 2 else 1
+    return t.shape[1] * recept, t.shape[0] * recept
+
+
+@torch.no_grad()
+def _fill(t, sample):
+    tmp = sample.to(dtype=torch.float32)
+    t.copy_(tmp.to(device=t.device, dtype=t.dtype))
+    return t
+
+
+def normal_(t, mean=0.0, std=0.02, generator=None):
+    return _fill(t, torch.randn(t.shape, generator=generator) * std + mean)
+
+
+def uniform_(t, a=-1.0, b=1.0, generator=None):
+    return _fill(t, torch.rand(t.shape, generator=generator) * (b - a) + a)
+
+
+def zeros_(t):
+    with torch.no_grad():
+        return t.zero_()
+
+
+def ones_(t):
+    with torch.no_grad():
+        return t.fill_(1.0)
+
+
+def kaiming_uniform_(t, a=math.sqrt(5), generator=None):
+    fan_in, _ = _fan(t)
+    gain = math.sqrt(2.0 / (1 + a * a))
+    bound = gain * math.sqrt(3.0 / max(1, fan_in))
+    return uniform_(t, -bound, bound, generator)
+
+
+def kaiming_normal_(t, generator=None):
+    fan_in, _ = _fan(t)
+    return normal_(t, 0.0, math.sqrt(2.0 / max(1, fan_in)), generator)
+
+
+def xavier_uniform_(t, gain=1.0, generator=None):
+    fan_in, fan_out = _fan(t)
+    bound = gain * math.sqrt(6.0 / max(1, fan_in + fan_out))
+    return uniform_(t, -bound, bound, generator)
+
+
+def xavier_normal_(t, gain=1.0, generator=None):
+    fan_in, fan_out = _fan(t)
+    return normal_(t, 0.0, gain * math.sqrt(2.0 / max(1, fan_in + fan_out)), generator)
+
+
+def orthogonal_(t, gain=1.0, generator=None):
+    rows, cols = t.shape[0], t.numel() // t.shape[0]
+    a = torch.randn(max(rows, cols), min(rows, cols), generator=generator)
+    q, r = torch.linalg.qr(a)
+    q = q * torch.sign(torch.diagonal(r))
+    if rows < cols:
+        q = q.t()
+    return _fill(t, (gain * q[:rows, :cols]).reshape(t.shape))
+
+
+def scaled_residual_(t, num_layers, std=0.02, generator=None):
+    """N(0, std / sqrt(2 * num_layers)) for residual output projections (GPT-2 style)."""
+    return normal_(t, 0.0, std / math.sqrt(2.0 * num_layers), generator)
+
+
+def init_normal_(module: torch.nn.Module, std: float = 0.02, seed: int = 0) -> None:
+    """Seeded N(0, std) for every weight matrix / embedding; norms to one, biases to zero."""
+    g = torch.Generator().manual_seed(seed)
+    for name, p in module.named_parameters():
+        if p.dim() >= 2:
+            normal_(p, 0.0, std, g)
+        elif name.endswith("bias"):
+            zeros_(p)
+        else:
+            ones_(p)

@@ -1,0 +1,321 @@
+"""Core layers with the reference's names, running on the sm_100a ops.
+
+Linear ([out, in] weight, kaiming-uniform init, optional zero bias; crates/brain-nn/src/layers/linear.rs:13-63),
+Embedding (crates/brain-nn/src/layers/embedding.rs:34-60), LayerNorm / RMSNorm
+(crates/brain-nn/src/normalization/*.rs — here differentiable end to end, where the reference's
+LayerNorm module breaks the tape), MultiheadAttention with q/k/v/out projections
+(crates/brain-nn/src/layers/multihead.rs:40-149), GroupedQueryAttention, FeedForward (SwiGLU /
+GELU), Dropout and the usual activation modules.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import ops
+from . import init as _init
+from .module import Module
+
+
+class Linear(Module):
+    def __init__(self, in_features: int, out_features: int, bias: bool = True, device=None, dtype=None,
+                 generator=None):
+        super().__init__()
+        self.in_features, self.out_features = in_features, out_features
+        self.weight = torch.nn.Parameter(torch.empty(out_features, in_features, device=device, dtype=dtype))
+        self.bias = torch.nn.Parameter(torch.zeros(out_features, device=device, dtype=dtype)) if bias else None
+        _init.kaiming_uniform_(self.weight, generator=generator)
+
+    def forward(self, x, residual=None):
+        return ops.linear(x, self.weight, self.bias, residual)
+
+    def extra_repr(self):
+        return f"in={self.in_features}, out={self.out_features}, bias={self.bias is not None}"
+
+
+class Embedding(Module):
+    def __init__(self, num_embeddings: int, embedding_dim: int, device=None, dtype=None, generator=None):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.empty(num_embeddings, embedding_dim, device=device, dtype=dtype))
+        _init.normal_(self.weight, 0.0, 1.0, generator)
+
+    def forward(self, ids):
+        return ops.embedding(ids, self.weight)
+
+    forward_indices = forward
+
+
+class RMSNorm(Module):
+    def __init__(self, dim: int, eps: float = 1e-6, device=None, dtype=None):
+        super().__init__()
+        self.eps = eps
+        self.weight = torch.nn.Parameter(torch.ones(dim, device=device, dtype=dtype))
+
+    def forward(self, x):
+        return ops.rms_norm(x, self.weight, self.eps)
+
+
+class LayerNorm(Module):
+    def __init__(self, dim: int, eps: float = 1e-5, bias: bool = True, device=None, dtype=None):
+        super().__init__()
+        self.eps = eps
+        self.weight = torch.nn.Parameter(torch.ones(dim, device=device, dtype=dtype))
+        self.bias = torch.nn.Parameter(torch.zeros(dim, device=device, dtype=dtype)) if bias else None
+
+    def forward(self, x):
+        return ops.layer_norm(x, self.weight, self.bias, self.eps)
+
+
+class Dropout(Module):
+    def __init__(self, p: float = 0.1):
+        super().__init__()
+        self.p = p
+
+    def forward(self, x):
+        return torch.nn.functional.dropout(x, self.p, self.training)
+
+
+class GELU(Module):
+    """tanh-approximate GELU (the reference's only GELU, crates/brain-core/src/tensor/math.rs:284-287)."""
+
+    def forward(self, x):
+        return ops.gelu(x)
+
+
+class SiLU(Module):
+    def forward(self, x):
+        return torch.nn.functional.silu(x)
+
+
+Swish = SiLU
+
+
+class ReLU(Module):
+    def forward(self, x):
+        return torch.relu(x)
+
+
+class LeakyReLU(Module):
+    def __init__(self, negative_slope=0.01):
+        super().__init__()
+        self.negative_slope = negative_slope
+
+    def forward(self, x):
+        return torch.nn.functional.leaky_relu(x, self.negative_slope)
+
+
+class Tanh(Module):
+    def forward(self, x):
+        return torch.tanh(x)
+
+
+class Sigmoid(Module):
+    def forward(self, x):
+        return torch.sigmoid(x)
+
+
+class Softmax(Module):
+    def __init__(self, dim=-1):
+        super().__init__()
+        self.dim = dim
+
+    def forward(self, x):
+        return torch.softmax(x.float() - x.float().amax(self.dim, keepdim=True), self.dim).to(x.dtype)
+
+
+class LogSoftmax(Softmax):
+    def forward(self, x):
+        return torch.log_softmax(x.float(), self.dim).to(x.dtype)
+
+
+class SwiGLU(Module):
+    """silu(gate) * up over a fused [..., 2F] input."""
+
+    def forward(self, gu):
+        return ops.swiglu(gu)
+
+
+class ELU(Module):
+    def __init__(self, alpha=1.0):
+        super().__init__()
+        self.alpha = alpha
+
+    def forward(self, x):
+        return torch.nn.functional.elu(x, self.alpha)
+
+
+class SELU(Module):
+    def forward(self, x):
+        return torch.nn.functional.selu(x)
+
+
+class Mish(Module):
+    def forward(self, x):
+        return torch.nn.functional.mish(x)
+
+
+class Softplus(Module):
+    def forward(self, x):
+        return torch.nn.functional.softplus(x)
+
+
+class Hardswish(Module):
+    def forward(self, x):
+        return torch.nn.functional.hardswish(x)
+
+
+class Hardsigmoid(Module):
+    def forward(self, x):
+        return torch.nn.functional.hardsigmoid(x)
+
+
+class PReLU(Module):
+    def __init__(self, num_parameters=1, init=0.25):
+        super().__init__()
+        self.weight = torch.nn.Parameter(torch.full((num_parameters,), init))
+
+    def forward(self, x):
+        return torch.nn.functional.prelu(x, self.weight.to(x.dtype))
+
+
+class GLU(Module):
+    def __init__(self, dim=-1):
+        super().__init__()
+        self.dim = dim
+
+    def forward(self, x):
+        return torch.nn.functional.glu(x, self.dim)
+
+
+class QuickGELU(Module):
+    def forward(self, x):
+        return x * torch.sigmoid(1.702 * x)
+
+
+class FeedForward(Module):
+    """Transformer FFN: gated (SwiGLU over a fused gate/up weight) or plain (GELU)."""
+
+    def __init__(self, dim: int, hidden: int, gated: bool = True, bias: bool = False, device=None, dtype=None):
+        super().__init__()
+        self.gated = gated
+        if gated:
+            self.gate_up = Linear(dim, 2 * hidden, bias=bias, device=device, dtype=dtype)
+        else:
+            self.up = Linear(dim, hidden, bias=bias, device=device, dtype=dtype)
+        self.down = Linear(hidden, dim, bias=bias, device=device, dtype=dtype)
+
+    def forward(self, x, residual=None):
+        if self.gated:
+            if self.down.bias is None:
+                return ops.swiglu_linear(self.gate_up(x), self.down.weight, residual)
+            return self.down(ops.swiglu(self.gate_up(x)), residual)
+        return self.down(ops.gelu(self.up(x)), residual)
+
+
+class MultiheadAttention(Module):
+    """Multi-head (or grouped-query, when num_kv_heads < num_heads) self-attention.
+
+    One fused [q; k; v] projection feeds the flash-attention kernel directly through strides.
+    ``causal`` selects the decoder mask; RoPE is applied when a rope table is passed.
+    """
+
+    def __init__(self, dim: int, num_heads: int, num_kv_heads: int | None = None, bias: bool = True,
+                 causal: bool = False, device=None, dtype=None):
+        super().__init__()
+        self.dim, self.num_heads = dim, num_heads
+        self.num_kv_heads = num_kv_heads or num_heads
+        self.head_dim = dim // num_heads
+        self.causal = causal
+        qkv_out = (self.num_heads + 2 * self.num_kv_heads) * self.head_dim
+        self.qkv = Linear(dim, qkv_out, bias=bias, device=device, dtype=dtype)
+        self.out = Linear(num_heads * self.head_dim, dim, bias=bias, device=device, dtype=dtype)
+
+    def forward(self, x, rope_table=None, residual=None, causal=None):
+        c = self.causal if causal is None else causal
+        qkv = self.qkv(x)
+        o = ops.qkv_attention(qkv, self.num_heads, self.num_kv_heads, rope_table, causal=c)
+        return self.out(o, residual)
+
+
+class GroupedQueryAttention(MultiheadAttention):
+    def __init__(self, dim, num_heads, num_kv_heads, bias=False, causal=True, device=None, dtype=None):
+        super().__init__(dim, num_heads, num_kv_heads, bias, causal, device, dtype)
+
+
+class MultiQueryAttention(MultiheadAttention):
+    def __init__(self, dim, num_heads, bias=False, causal=True, device=None, dtype=None):
+        super().__init__(dim, num_heads, 1, bias, causal, device, dtype)
+
+
+def scaled_dot_product_attention(q, k, v, causal=False, scale=None):
+    """[B, S, H, D] attention (reference: crates/brain-transformer/src/attention/scaled.rs:41-139)."""
+    return ops.flash_attention(q, k, v, causal, scale)
+
+
+class Conv2d(torch.nn.Conv2d, Module):
+    """2-D convolution (cuDNN through PyTorch; crates/brain-nn/src/layers/conv*.rs)."""
+
+
+class Conv1d(torch.nn.Conv1d, Module):
+    pass
+
+
+class ConvTranspose2d(torch.nn.ConvTranspose2d, Module):
+    pass
+
+
+class MaxPool2d(torch.nn.MaxPool2d, Module):
+    pass
+
+
+class AvgPool2d(torch.nn.AvgPool2d, Module):
+    pass
+
+
+class AdaptiveAvgPool2d(torch.nn.AdaptiveAvgPool2d, Module):
+    pass
+
+
+class BatchNorm2d(torch.nn.BatchNorm2d, Module):
+    pass
+
+
+class GroupNorm(torch.nn.GroupNorm, Module):
+    pass
+
+
+class InstanceNorm2d(torch.nn.InstanceNorm2d, Module):
+    pass
+
+
+class Flatten(torch.nn.Flatten, Module):
+    pass
+
+
+class PixelShuffle(torch.nn.PixelShuffle, Module):
+    pass
+
+
+class LSTM(torch.nn.LSTM, Module):
+    pass
+
+
+class GRU(torch.nn.GRU, Module):
+    pass
+
+
+class RNN(torch.nn.RNN, Module):
+    pass
+
+
+class Bilinear(torch.nn.Bilinear, Module):
+    pass
+
+
+def num_params(m: torch.nn.Module) -> int:
+    return sum(p.numel() for p in m.parameters())
+
+
+__all__ = [n for n in dir() if not n.startswith("_") and n[0].isupper()] + ["scaled_dot_product_attention",
+                                                                             "num_params", "math"]

@@ -1,0 +1,76 @@
+"""Helpers shared by the op modules: signatures, streams, parameter-gradient accumulation."""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from .. import _native
+
+# Signatures of the kernel entry points (see csrc/*.cu). Codes: p pointer, i int32, l int64,
+# f float32, s cudaStream_t.
+_native.register({
+    "brain_norm_fwd": ("brain_kernels", "iplplppplplppiifs"),
+    "brain_norm_bwd_partials": ("brain_kernels", "i"),
+    "brain_norm_bwd": ("brain_kernels", "iplplpppplplppiipiis"),
+    "brain_swiglu_fwd": ("brain_kernels", "plpllis"),
+    "brain_swiglu_bwd": ("brain_kernels", "plplpllis"),
+    "brain_gelu_fwd": ("brain_kernels", "ppls"),
+    "brain_gelu_bwd": ("brain_kernels", "pppls"),
+    "brain_rope": ("brain_kernels", "piiiilllppifs"),
+    "brain_embedding_fwd": ("brain_kernels", "pppiplils"),
+    "brain_embedding_bwd": ("brain_kernels", "ppppilils"),
+    "brain_pos_grad": ("brain_kernels", "ppilii" + "s"),
+    "brain_ce_fwd": ("brain_kernels", "plppplilfs"),
+    "brain_ce_bwd": ("brain_kernels", "plppppfpllilfs"),
+    "brain_adamw": ("brain_kernels", "pppppiplffffffffips"),
+    "brain_sgd": ("brain_kernels", "pppiplffffiifps"),
+    "brain_sumsq": ("brain_kernels", "pilfpipps"),
+    "brain_scale": ("brain_kernels", "pilpfs"),
+    "brain_clip_coef": ("brain_kernels", "pfps"),
+    "brain_cast_bf16": ("brain_kernels", "ppls"),
+    "brain_attn_fwd": ("brain_kernels", "pppppppiiiiiifis"),
+    "brain_attn_bwd": ("brain_kernels", "pppppppppppppppp" + "iiiiiifis"),
+    "brain_status_norms": ("brain_kernels", "pi"),
+    "brain_status_elementwise": ("brain_kernels", "pi"),
+    "brain_status_ce": ("brain_kernels", "pi"),
+    "brain_status_optim": ("brain_kernels", "pi"),
+    "brain_status_attention": ("brain_kernels", "pi"),
+})
+
+STATUS_TAGS = ["gemm", "norms", "elementwise", "ce", "optim", "attention"]
+
+
+def stream(t: torch.Tensor) -> int:
+    return _native.stream_ptr(t.device)
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def i64_array(vals) -> ctypes.Array:
+    arr = (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
+    return arr
+
+
+def check_status() -> list[tuple[str, int, int]]:
+    """Read and clear every kernel status word; returns the non-zero entries (tag, code, where)."""
+    bad = []
+    for tag in STATUS_TAGS:
+        code, where = _native.status(tag, clear=True)
+        if code:
+            bad.append((tag, code, where))
+    return bad
+
+
+def has_main_grad(p: torch.Tensor) -> bool:
+    return getattr(p, "main_grad", None) is not None
+
+
+def rows2d(x: torch.Tensor) -> torch.Tensor:
+    """View x as [rows, last] with unit last-dim stride (copying only if needed)."""
+    x2 = x.reshape(-1, x.shape[-1])
+    if x2.stride(-1) != 1:
+        x2 = x2.contiguous()
+    return x2

@@ -1,0 +1,133 @@
+"""Linear layers on the tcgen05 GEMM, with gradient accumulation into flat ``main_grad`` buffers.
+
+``linear(x, w, b, residual)`` computes ``x @ w.T (+ b) (+ residual)`` in one GEMM (bias and residual
+are epilogue adds). Backward: ``dx = dy @ w`` and ``dw = dy.T @ x`` both read their transposed
+operands in place. When ``w`` has a ``main_grad`` attribute (a view into the flat gradient buffer of
+the data-parallel engine / fused optimizer) the weight gradient GEMM accumulates straight into it
+(``beta = 1``) and autograd gets ``None`` — no separate gradient tensor, no extra add.
+
+Fused variants used by the transformer blocks keep activation memory low by recomputing cheap
+elementwise producers in the backward pass:
+* ``norm_linear``: ``rms_norm(x) @ w.T`` saving only x (the normalised input is recomputed);
+* ``swiglu_linear``: ``swiglu(gu) @ w.T (+ residual)`` saving only gu.
+Reference: brain-nn Linear ``x·Wᵀ + b`` (crates/brain-nn/src/layers/linear.rs:13-63).
+"""
+from __future__ import annotations
+
+import torch
+
+from .activations import swiglu_bwd_only, swiglu_fwd_only
+from .gemm import gemm
+from ._common import has_main_grad, rows2d
+from . import norms as _norms
+
+
+def _wgrad(dy2, x2, w):
+    """Weight gradient dy^T x: into w.main_grad (returns None) or as a new tensor."""
+    if has_main_grad(w):
+        gemm(dy2, x2, trans_a=True, out=w.main_grad, beta=1.0)
+        return None
+    return gemm(dy2, x2, trans_a=True, out_dtype=torch.float32).to(w.dtype)
+
+
+def _bgrad(dy2, b):
+    if b is None:
+        return None
+    g = dy2.float().sum(0)
+    if has_main_grad(b):
+        b.main_grad.add_(g.to(b.main_grad.dtype))
+        return None
+    return g.to(b.dtype)
+
+
+class _LinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, b, residual):
+        x2 = rows2d(x)
+        r2 = rows2d(residual) if residual is not None else None
+        y = gemm(x2, w, trans_b=True, bias=b, residual=r2)
+        ctx.save_for_backward(x2, w, b)
+        ctx.xshape = x.shape
+        ctx.has_res = residual is not None
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w, b = ctx.saved_tensors
+        dy2 = rows2d(dy)
+        dx = gemm(dy2, w).view(ctx.xshape) if ctx.needs_input_grad[0] else None
+        dw = _wgrad(dy2, x2, w) if ctx.needs_input_grad[1] else None
+        db = _bgrad(dy2, b) if (b is not None and ctx.needs_input_grad[2]) else None
+        dres = dy if ctx.has_res else None
+        return dx, dw, db, dres
+
+
+def linear(x, w, b=None, residual=None):
+    """y = x @ w.T (+ b) (+ residual)."""
+    if x.is_cuda:
+        return _LinearFn.apply(x, w, b, residual)
+    y = torch.nn.functional.linear(x.float(), w.float(), None if b is None else b.float())
+    if residual is not None:
+        y = y + residual.float()
+    return y.to(x.dtype)
+
+
+class _NormLinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, nw, w, eps):
+        x2 = rows2d(x)
+        xn, _, _, rstd = _norms._fwd(_norms._RMS, x2, nw, None, eps)
+        y = gemm(xn, w, trans_b=True)
+        ctx.save_for_backward(x2, nw, w, rstd)
+        ctx.eps = eps
+        ctx.xshape = x.shape
+        return y.view(*x.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, nw, w, rstd = ctx.saved_tensors
+        dy2 = rows2d(dy)
+        xn, _, _, _ = _norms._fwd(_norms._RMS, x2, nw, None, ctx.eps)  # recompute
+        dxn = gemm(dy2, w)
+        dw = _wgrad(dy2, xn, w)
+        del xn
+        dx, dnw, _ = _norms._bwd(_norms._RMS, dxn, x2, nw, None, None, rstd)
+        return dx.view(ctx.xshape), dnw, dw, None
+
+
+def norm_linear(x, norm_w, w, eps=1e-6):
+    """rms_norm(x, norm_w) @ w.T with the normalised activations recomputed in backward."""
+    if x.is_cuda:
+        return _NormLinearFn.apply(x, norm_w, w, eps)
+    return linear(_norms.rms_norm_ref(x, norm_w, eps), w)
+
+
+class _SwiGLULinearFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu, w, residual):
+        g2 = rows2d(gu)
+        a = swiglu_fwd_only(g2)
+        r2 = rows2d(residual) if residual is not None else None
+        y = gemm(a, w, trans_b=True, residual=r2)
+        ctx.save_for_backward(g2, w)
+        ctx.gshape = gu.shape
+        ctx.has_res = residual is not None
+        return y.view(*gu.shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        g2, w = ctx.saved_tensors
+        dy2 = rows2d(dy)
+        a = swiglu_fwd_only(g2)  # recompute the activation
+        dw = _wgrad(dy2, a, w)
+        da = gemm(dy2, w, out=a)  # reuse the activation buffer for its gradient
+        dgu = swiglu_bwd_only(da, g2)
+        return dgu.view(ctx.gshape), dw, (dy if ctx.has_res else None)
+
+
+def swiglu_linear(gu, w, residual=None):
+    """swiglu(gu) @ w.T (+ residual), recomputing swiglu(gu) in backward."""
+    if gu.is_cuda:
+        return _SwiGLULinearFn.apply(gu, w, residual)
+    from .activations import swiglu_ref
+    return linear(swiglu_ref(gu), w, residual=residual)

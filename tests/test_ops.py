@@ -1,0 +1,288 @@
+"""Numerics of the sm_100a kernels against float32 PyTorch restatements of the same ops.
+
+Each GPU test runs the op on CUDA (native kernel) and the oracle on the same bf16 inputs promoted
+to float32, forward and backward (gradients through torch autograd of the oracle).
+"""
+import math
+
+import pytest
+import torch
+
+from brain_b200 import ops
+from brain_b200.ops import activations as act
+from brain_b200.ops import attention as attn
+from brain_b200.ops import norms
+from brain_b200.ops import rope as rope_mod
+from brain_b200.ops.optim_kernels import adamw_, sumsq
+
+gpu = pytest.mark.gpu
+
+
+def rnd(*shape, seed=0, scale=1.0, device="cuda", dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(device=device, dtype=dtype)
+
+
+def close(a, b, rtol=2e-2, atol=2e-2):
+    torch.testing.assert_close(a.float(), b.float(), rtol=rtol, atol=atol)
+
+
+def grads(fn, *inputs):
+    ins = [x.detach().clone().requires_grad_(True) for x in inputs]
+    out = fn(*ins)
+    return out, ins
+
+
+def _no_status():
+    assert ops.check_status() == []
+
+
+# ------------------------------------------------------------------ CPU-side contracts
+def test_cpu_paths_match_reference_definitions():
+    x = rnd(4, 16, device="cpu", dtype=torch.float32)
+    w = rnd(16, seed=1, device="cpu", dtype=torch.float32)
+    y = ops.rms_norm(x, w, 1e-6)
+    ref = x * (x.pow(2).mean(-1, keepdim=True) + 1e-6).rsqrt() * w
+    close(y, ref, 1e-5, 1e-5)
+    gu = rnd(3, 8, device="cpu", dtype=torch.float32)
+    close(ops.swiglu(gu), torch.nn.functional.silu(gu[:, :4]) * gu[:, 4:], 1e-5, 1e-5)
+    t = rope_mod.rope_table(8, 16, 10000.0)
+    q = rnd(1, 5, 2, 8, device="cpu", dtype=torch.float32)
+    back = rope_mod.rope_ref(rope_mod.rope_ref(q, t), t, inverse=True)
+    close(back, q, 1e-5, 1e-5)
+
+
+# ------------------------------------------------------------------ norms
+@gpu
+@pytest.mark.parametrize("D", [128, 4096, 768, 8192])
+def test_rms_norm(D):
+    x = rnd(67, D, seed=1)
+    w = rnd(D, seed=2, scale=0.1) + 1
+    dy = rnd(67, D, seed=3)
+    y, (xg, wg) = grads(lambda a, b: ops.rms_norm(a, b, 1e-5), x, w)
+    y.backward(dy)
+    yr, (xr, wr) = grads(lambda a, b: norms.rms_norm_ref(a.float(), b.float(), 1e-5), x, w)
+    yr.backward(dy.float())
+    close(y, yr)
+    close(xg.grad, xr.grad, 3e-2, 3e-2)
+    close(wg.grad, wr.grad, 3e-2, 0.5)
+    _no_status()
+
+
+@gpu
+@pytest.mark.parametrize("D", [128, 768])
+def test_layer_norm(D):
+    x = rnd(33, D, seed=4)
+    w = rnd(D, seed=5, scale=0.1) + 1
+    b = rnd(D, seed=6, scale=0.1)
+    dy = rnd(33, D, seed=7)
+    y, (xg, wg, bg) = grads(lambda a, c, d: ops.layer_norm(a, c, d, 1e-5), x, w, b)
+    y.backward(dy)
+    yr, (xr, wr, br) = grads(lambda a, c, d: norms.layer_norm_ref(a.float(), c.float(), d.float(), 1e-5), x, w, b)
+    yr.backward(dy.float())
+    close(y, yr)
+    close(xg.grad, xr.grad, 3e-2, 3e-2)
+    close(wg.grad, wr.grad, 3e-2, 0.3)
+    close(bg.grad, br.grad, 3e-2, 0.3)
+
+
+@gpu
+def test_add_rms_norm():
+    x, r = rnd(20, 256, seed=8), rnd(20, 256, seed=9)
+    w = rnd(256, seed=10, scale=0.1) + 1
+    y, s = ops.add_rms_norm(x, r, w, 1e-6)
+    sr = (x.float() + r.float())
+    close(s, sr)
+    close(y, norms.rms_norm_ref(sr.bfloat16().float(), w.float(), 1e-6))
+
+
+# ------------------------------------------------------------------ activations
+@gpu
+def test_swiglu_and_gelu():
+    gu = rnd(37, 2 * 344, seed=11)
+    dy = rnd(37, 344, seed=12)
+    y, (g1,) = grads(ops.swiglu, gu)
+    y.backward(dy)
+    yr, (g2,) = grads(lambda t: act.swiglu_ref(t.float()), gu)
+    yr.backward(dy.float())
+    close(y, yr)
+    close(g1.grad, g2.grad)
+    x = rnd(1001, seed=13, scale=2)
+    dx = rnd(1001, seed=14)
+    y, (x1,) = grads(ops.gelu, x)
+    y.backward(dx)
+    yr, (x2,) = grads(lambda t: act.gelu_ref(t.float()), x)
+    yr.backward(dx.float())
+    close(y, yr)
+    close(x1.grad, x2.grad)
+
+
+# ------------------------------------------------------------------ rope
+@gpu
+def test_rope_inplace_strided_and_inverse():
+    B, S, Hq, Hkv, D = 2, 19, 4, 2, 64
+    qkv = rnd(B, S, (Hq + 2 * Hkv) * D, seed=15)
+    t = ops.rope_table(D, 64, 500000.0, device="cuda")
+    q, k, v = attn.split_qkv(qkv.clone(), Hq, Hkv)
+    ref_q = rope_mod.rope_ref(q.cpu(), t.cpu())
+    ops.apply_rope_(q, t)
+    close(q.cpu(), ref_q, 1e-2, 1e-2)
+    ops.apply_rope_(q, t, inverse=True)
+    close(q, attn.split_qkv(qkv, Hq, Hkv)[0], 2e-2, 2e-2)
+
+
+# ------------------------------------------------------------------ embedding
+@gpu
+def test_embedding_with_positions():
+    V, D, B, S = 97, 64, 3, 11
+    w = rnd(V, D, seed=16)
+    p = rnd(S, D, seed=17)
+    ids = torch.randint(0, V, (B, S), generator=torch.Generator().manual_seed(0)).cuda()
+    ids[0, :4] = 5  # repeated ids exercise the segment sums
+    dy = rnd(B, S, D, seed=18)
+    y, (wg, pg) = grads(lambda a, b: ops.embedding(ids, a, b), w, p)
+    y.backward(dy)
+    yr, (wr, pr) = grads(lambda a, b: torch.nn.functional.embedding(ids, a.float()) + b.float(), w, p)
+    yr.backward(dy.float())
+    close(y, yr)
+    close(wg.grad, wr.grad)
+    close(pg.grad, pr.grad, 3e-2, 5e-2)
+
+
+# ------------------------------------------------------------------ cross-entropy
+@gpu
+@pytest.mark.parametrize("V,smooth", [(1024, 0.0), (32000, 0.1), (1000, 0.0)])
+def test_cross_entropy(V, smooth):
+    M = 45
+    z = rnd(M, V, seed=19, scale=3)
+    lab = torch.randint(0, V, (M,), generator=torch.Generator().manual_seed(1)).cuda()
+    lab[3] = -100
+    l, (zg,) = grads(lambda t: ops.cross_entropy(t, lab, label_smoothing=smooth), z)
+    l.backward()
+    lr_, (zr,) = grads(lambda t: torch.nn.functional.cross_entropy(t.float(), lab, label_smoothing=smooth), z)
+    lr_.backward()
+    close(l, lr_, 1e-3, 1e-3)
+    close(zg.grad, zr.grad, 2e-2, 1e-4)
+
+
+@gpu
+def test_linear_cross_entropy_fused():
+    M, K, V = 300, 256, 4096
+    h = rnd(M, K, seed=20)
+    w = rnd(V, K, seed=21, scale=0.05)
+    lab = torch.randint(0, V, (M,), generator=torch.Generator().manual_seed(2)).cuda()
+    l, (hg, wg) = grads(lambda a, b: ops.linear_cross_entropy(a, b, lab, chunk=128), h, w)
+    (2.0 * l).backward()
+    lr_, (hr, wr) = grads(lambda a, b: torch.nn.functional.cross_entropy(a.float() @ b.float().t(), lab), h, w)
+    (2.0 * lr_).backward()
+    close(l, lr_, 2e-3, 2e-3)
+    close(hg.grad, hr.grad, 3e-2, 2e-3)
+    close(wg.grad, wr.grad, 3e-2, 2e-3)
+
+
+# ------------------------------------------------------------------ attention
+@gpu
+@pytest.mark.parametrize("D", [32, 64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("Sq,Sk,Hq,Hkv", [(128, 128, 4, 4), (200, 200, 8, 2), (77, 150, 4, 1), (1, 65, 4, 2)])
+def test_flash_attention(D, causal, Sq, Sk, Hq, Hkv):
+    B = 2
+    q = rnd(B, Sq, Hq, D, seed=22)
+    k = rnd(B, Sk, Hkv, D, seed=23)
+    v = rnd(B, Sk, Hkv, D, seed=24)
+    do = rnd(B, Sq, Hq, D, seed=25)
+    o, (qg, kg, vg) = grads(lambda a, b, c: ops.flash_attention(a, b, c, causal), q, k, v)
+    o.backward(do)
+    orf, (qr, kr, vr) = grads(lambda a, b, c: attn.sdpa_ref(a.float(), b.float(), c.float(), causal), q, k, v)
+    orf.backward(do.float())
+    close(o, orf, 2e-2, 2e-2)
+    close(qg.grad, qr.grad, 3e-2, 3e-2)
+    close(kg.grad, kr.grad, 3e-2, 3e-2)
+    close(vg.grad, vr.grad, 3e-2, 3e-2)
+    _no_status()
+
+
+@gpu
+def test_qkv_attention_with_rope():
+    B, S, Hq, Hkv, D = 2, 96, 8, 2, 64
+    qkv = rnd(B, S, (Hq + 2 * Hkv) * D, seed=26)
+    do = rnd(B, S, Hq * D, seed=27)
+    t = ops.rope_table(D, 128, 10000.0, device="cuda")
+    o, (g1,) = grads(lambda x: ops.qkv_attention(x * 1, Hq, Hkv, t), qkv)
+    o.backward(do)
+    tc = t.cpu()
+    orf, (g2,) = grads(lambda x: ops.qkv_attention(x.cpu().float(), Hq, Hkv, tc), qkv)
+    orf.backward(do.cpu().float())
+    close(o.cpu(), orf, 2e-2, 2e-2)
+    close(g1.grad.cpu(), g2.grad.cpu(), 4e-2, 4e-2)
+
+
+# ------------------------------------------------------------------ linear family
+@gpu
+def test_linear_main_grad_and_fused_variants():
+    M, K, N, F = 130, 256, 192, 128
+    x = rnd(M, K, seed=28)
+    w = rnd(N, K, seed=29, scale=0.05)
+    res = rnd(M, N, seed=30)
+    dy = rnd(M, N, seed=31)
+    wp = w.clone().requires_grad_(True)
+    wp.main_grad = torch.zeros(N, K, device="cuda", dtype=torch.float32)
+    xg = x.clone().requires_grad_(True)
+    y = ops.linear(xg, wp, residual=res)
+    y.backward(dy)
+    assert wp.grad is None
+    xr, wr = x.float().requires_grad_(True), w.float().requires_grad_(True)
+    yr = xr @ wr.t() + res.float()
+    yr.backward(dy.float())
+    close(y, yr)
+    close(xg.grad, xr.grad, 2e-2, 5e-2)
+    close(wp.main_grad, wr.grad, 2e-2, 5e-2)
+    # norm_linear
+    nw = rnd(K, seed=32, scale=0.1) + 1
+    y, (a1, n1, w1) = grads(lambda a, b, c: ops.norm_linear(a, b, c, 1e-6), x, nw, w)
+    y.backward(dy)
+    yr, (a2, n2, w2) = grads(lambda a, b, c: norms.rms_norm_ref(a.float(), b.float(), 1e-6) @ c.float().t(), x, nw, w)
+    yr.backward(dy.float())
+    close(y, yr)
+    close(a1.grad, a2.grad, 3e-2, 5e-2)
+    close(w1.grad, w2.grad, 3e-2, 0.2)
+    close(n1.grad, n2.grad, 3e-2, 0.5)
+    # swiglu_linear
+    gu = rnd(M, 2 * F, seed=33)
+    wd = rnd(N, F, seed=34, scale=0.05)
+    y, (g1, wd1) = grads(lambda a, b: ops.swiglu_linear(a, b, residual=res), gu, wd)
+    y.backward(dy)
+    yr, (g2, wd2) = grads(lambda a, b: act.swiglu_ref(a.float()) @ b.float().t() + res.float(), gu, wd)
+    yr.backward(dy.float())
+    close(y, yr)
+    close(g1.grad, g2.grad, 3e-2, 5e-2)
+    close(wd1.grad, wd2.grad, 3e-2, 0.1)
+
+
+# ------------------------------------------------------------------ optimizer kernels
+@gpu
+def test_adamw_flat_matches_reference_order():
+    n = 10007
+    p = rnd(n, seed=35, dtype=torch.float32)
+    g = rnd(n, seed=36, dtype=torch.bfloat16)
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    p16 = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    pc, mc, vc = p.cpu().clone(), m.cpu().clone(), v.cpu().clone()
+    for step in (1, 2, 3):
+        adamw_(p, m, v, g, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=step, grad_scale=0.5,
+               p16=p16)
+        adamw_(pc, mc, vc, g.cpu(), lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=step,
+               grad_scale=0.5)
+    close(p.cpu(), pc, 1e-5, 1e-6)
+    close(p16.float().cpu(), pc, 1e-2, 1e-2)
+    flag = torch.zeros(1, device="cuda", dtype=torch.int32)
+    s = sumsq(g, 2.0, found_inf=flag)
+    close(s.cpu(), (g.float().cpu() * 2).pow(2).sum().reshape(1), 1e-4, 1e-2)
+    assert int(flag.item()) == 0
+    g[5] = float("inf")
+    sumsq(g, found_inf=flag)
+    assert int(flag.item()) == 1
+    before = p.clone()
+    adamw_(p, m, v, g, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=4, found_inf=flag)
+    assert torch.equal(p, before)
