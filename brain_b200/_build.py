@@ -41,7 +41,9 @@ LIBRARIES = {
     ],
 }
 # Host-only C++ libraries (g++): the checkpoint codec and the runtime helpers.
-CXX_LIBRARIES: dict = {}
+CXX_LIBRARIES = {
+    "brain_runtime": ["codec.cpp"],
+}
 
 
 def _headers():

@@ -88,7 +88,33 @@ def stream_ptr(device: torch.device | None = None) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+# Kernels launched by one call of each multi-kernel entry point (default 1); used to count this
+# library's launches inside a timed region (``launch_counter``).
+KERNELS_PER_CALL = {
+    "brain_norm_bwd": 2, "brain_attn_bwd": 4, "brain_sumsq": 2, "brain_error_string": 0,
+    "brain_norm_bwd_partials": 0,
+}
+_launches = {"on": False, "n": 0}
+
+
+class launch_counter:
+    """Context manager counting native kernel launches issued through :func:`call`."""
+
+    def __enter__(self):
+        _launches["on"], _launches["n"] = True, 0
+        return self
+
+    def __exit__(self, *exc):
+        _launches["on"] = False
+
+    @property
+    def count(self) -> int:
+        return _launches["n"]
+
+
 def call(name: str, *args) -> int:
+    if _launches["on"]:
+        _launches["n"] += KERNELS_PER_CALL.get(name, 1)
     rc = fn(name)(*args)
     if rc != 0:
         try:

@@ -1,0 +1,5 @@
+"""Model families: LlamaLite (GQA + RoPE + SwiGLU), GptLite, BertLite, T5Lite, ViT."""
+from .config import LlamaLiteConfig, GptLiteConfig, BertLiteConfig, T5LiteConfig, ViTConfig, TransformerConfig  # noqa: F401
+from .llama import LlamaLite, LlamaBlock  # noqa: F401
+from .kv_cache import KvCache, KvCacheConfig, PagedKvCache  # noqa: F401
+from .generate import GenerationConfig, sample_next_token  # noqa: F401

@@ -78,12 +78,23 @@ def scaled_residual_(t, num_layers, std=0.02, generator=None):
     return normal_(t, 0.0, std / math.sqrt(2.0 * num_layers), generator)
 
 
+@torch.no_grad()
 def init_normal_(module: torch.nn.Module, std: float = 0.02, seed: int = 0) -> None:
-    """Seeded N(0, std) for every weight matrix / embedding; norms to one, biases to zero."""
-    g = torch.Generator().manual_seed(seed)
+    """Seeded N(0, std) for every weight matrix / embedding; norms to one, biases to zero.
+
+    Samples are drawn on the parameter's own device from a generator seeded with ``seed`` (one
+    stream over the parameters in registration order), so an 8B-parameter model initialises in
+    seconds on a GPU and identically on every rank.
+    """
+    gens = {}
     for name, p in module.named_parameters():
         if p.dim() >= 2:
-            normal_(p, 0.0, std, g)
+            dev = p.device
+            g = gens.get(str(dev))
+            if g is None:
+                g = torch.Generator(device=dev).manual_seed(seed)
+                gens[str(dev)] = g
+            p.copy_((torch.randn(p.shape, generator=g, device=dev, dtype=torch.float32) * std).to(p.dtype))
         elif name.endswith("bias"):
             zeros_(p)
         else:

@@ -1,0 +1,84 @@
+"""Data-parallel training engine (``brain_b200.parallel.DataParallel``).
+
+Replicates the model on every rank, reduces gradients by the **mean** (the reference's reduction,
+crates/brain-distributed/src/data_parallel.rs:48-63) and shards the AdamW state across ranks:
+  * parameters live in one flat bf16 buffer and gradients in one flat ``main_grad`` buffer
+    (``parallel.flat``), written in place by the backward kernels;
+  * the optimizer step is a reduce-scatter of the gradient bucket, the fused AdamW over the local
+    shard and an all-gather of the updated bf16 shards (``optim.flat_adamw``);
+  * with the NVLink backend (``comm="nvlink"``) the reduce-scatter, un-scaling and AdamW update run
+    as one kernel that pulls peers' gradient shards over NVLink (``parallel.symm``).
+
+The reference's helpers are kept: ``sync_gradients`` (scale by 1/world after a sum) and
+``sync_ensemble_gradients`` (average per-parameter gradients of in-process "ranks").
+"""
+from __future__ import annotations
+
+import torch
+
+from ..optim.flat_adamw import FlatAdamW
+from . import dist as _dist
+from .comm import NcclComm
+from .flat import FlatParams
+
+
+class DataParallel:
+    def __init__(self, model: torch.nn.Module, lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8,
+                 weight_decay: float = 0.0, grad_dtype: torch.dtype = torch.float32, comm: str | object = "nccl",
+                 loss_fn=None):
+        ctx = _dist.context()
+        self.ctx = ctx
+        self.model = model
+        if isinstance(comm, str):
+            if comm == "nvlink" and ctx.world_size > 1:
+                from .symm import NvlinkComm
+                comm = NvlinkComm()
+            else:
+                comm = NcclComm()
+        self.comm = comm
+        self.flat = FlatParams(list(model.parameters()), ctx.world_size, ctx.rank, grad_dtype)
+        if ctx.world_size > 1:
+            self.comm.broadcast(self.flat.param_buf, 0)
+        self.optimizer = FlatAdamW(self.flat, lr, betas, eps, weight_decay, comm=self.comm)
+        self.loss_fn = loss_fn
+        self.steps = 0
+
+    @property
+    def world_size(self) -> int:
+        return self.ctx.world_size
+
+    @property
+    def rank(self) -> int:
+        return self.ctx.rank
+
+    def forward_loss(self, *batch):
+        if self.loss_fn is not None:
+            return self.loss_fn(self.model, *batch)
+        return self.model.loss(*batch)
+
+    def train_step(self, *batch, loss_scale: float = 1.0) -> torch.Tensor:
+        """zero grads -> forward -> backward -> reduce-scatter + sharded AdamW -> all-gather.
+
+        Returns the local loss (device scalar, not synchronised).
+        """
+        self.optimizer.zero_grad()
+        loss = self.forward_loss(*batch)
+        (loss * loss_scale if loss_scale != 1.0 else loss).backward()
+        self.optimizer.step(grad_scale=1.0 / loss_scale)
+        self.steps += 1
+        return loss.detach()
+
+    def sync_gradients(self) -> None:
+        """All-reduce gradients as the mean over ranks (flat bucket, in place)."""
+        if self.world_size > 1:
+            self.comm.all_reduce(self.flat.grad_buf)
+            self.flat.grad_buf.mul_(1.0 / self.world_size)
+
+    @staticmethod
+    def sync_ensemble_gradients(rank_grads: list[list[torch.Tensor]]) -> None:
+        """Average gradients of in-process replicas in place (reference behaviour, for tests)."""
+        n = len(rank_grads)
+        for i in range(len(rank_grads[0])):
+            mean = sum(r[i] for r in rank_grads) / n
+            for r in rank_grads:
+                r[i].copy_(mean)
