@@ -74,7 +74,11 @@ size_t format_one(double v, char* out) {
     if (*p != '.') digits[nd++] = *p;
     ++p;
   }
-  int exp10 = std::atoi(p + 1);  // value = 0.d1d2... * 10^(exp10 + 1)
+  // exponent: to_chars does not NUL-terminate, so parse only up to r.ptr
+  const char* q = p + 1;
+  if (q < r.ptr && *q == '+') ++q;
+  int exp10 = 0;  // value = d.ddd * 10^exp10
+  std::from_chars(q, r.ptr, exp10);
   const int point = exp10 + 1;     // digits before the decimal point
   if (point <= 0) {
     out[n++] = '0';
