@@ -25,14 +25,26 @@ def _strides3(t):
     return [t.stride(0), t.stride(1), t.stride(2)]
 
 
-def _fwd(q, k, v, causal, scale):
+_NOT_SUPPORTED = 801  # cudaErrorNotSupported: layout outside the tensor-core kernel's domain
+USE_TC = True  # tcgen05 forward when the layout allows; the mma.sync kernel otherwise
+
+
+def _fwd(q, k, v, causal, scale, impl=None):
     B, Sq, Hq, D = q.shape
     Sk, Hkv = k.shape[1], k.shape[2]
     o = torch.empty(B, Sq, Hq, D, device=q.device, dtype=q.dtype)
     lse = torch.empty(B, Hq, Sq, device=q.device, dtype=torch.float32)
-    _native.call("brain_attn_fwd", q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                 i64_array(_strides3(q) + _strides3(k) + _strides3(v)), o.data_ptr(), i64_array(_strides3(o)),
-                 lse.data_ptr(), B, Hq, Hkv, Sq, Sk, D, float(scale), int(causal), stream(q))
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), i64_array(_strides3(q) + _strides3(k) + _strides3(v)),
+            o.data_ptr(), i64_array(_strides3(o)), lse.data_ptr(), B, Hq, Hkv, Sq, Sk, D, float(scale), int(causal),
+            stream(q))
+    use_tc = USE_TC if impl is None else impl == "tc"
+    if use_tc:
+        rc = _native.fn("brain_attn_fwd_tc")(*args)
+        if rc == 0:
+            return o, lse
+        if rc != _NOT_SUPPORTED or impl == "tc":
+            raise _native.NativeError(f"brain_attn_fwd_tc failed with status {rc}")
+    _native.call("brain_attn_fwd", *args)
     return o, lse
 
 

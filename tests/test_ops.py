@@ -203,6 +203,32 @@ def test_flash_attention(D, causal, Sq, Sk, Hq, Hkv):
 
 
 @gpu
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("B,Sq,Sk,Hq,Hkv", [(1, 128, 128, 2, 2), (2, 300, 300, 8, 2), (1, 200, 517, 4, 1),
+                                            (2, 1, 333, 4, 2), (1, 1024, 1024, 4, 4)])
+def test_flash_attention_tcgen05_forward(D, causal, B, Sq, Sk, Hq, Hkv):
+    q = rnd(B, Sq, Hq, D, seed=40, scale=2.0)
+    k = rnd(B, Sk, Hkv, D, seed=41, scale=2.0)
+    v = rnd(B, Sk, Hkv, D, seed=42)
+    o_tc, lse_tc = attn._fwd(q, k, v, causal, 1.0 / math.sqrt(D), impl="tc")
+    o_mma, lse_mma = attn._fwd(q, k, v, causal, 1.0 / math.sqrt(D), impl="mma")
+    ref = attn.sdpa_ref(q.float(), k.float(), v.float(), causal)
+    close(o_tc, ref, 2e-2, 2e-2)
+    close(lse_tc, lse_mma, 1e-3, 1e-3)
+    assert ops.check_status() == []
+
+
+@gpu
+def test_flash_attention_tcgen05_strided_qkv():
+    B, S, Hq, Hkv, D = 2, 384, 8, 2, 128
+    qkv = rnd(B, S, (Hq + 2 * Hkv) * D, seed=43)
+    q, k, v = attn.split_qkv(qkv, Hq, Hkv)
+    o_tc, _ = attn._fwd(q, k, v, True, D ** -0.5, impl="tc")
+    close(o_tc, attn.sdpa_ref(q.float(), k.float(), v.float(), True), 2e-2, 2e-2)
+
+
+@gpu
 def test_qkv_attention_with_rope():
     B, S, Hq, Hkv, D = 2, 96, 8, 2, 64
     qkv = rnd(B, S, (Hq + 2 * Hkv) * D, seed=26)
