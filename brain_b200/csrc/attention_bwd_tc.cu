@@ -1,0 +1,501 @@
+// Flash-attention backward on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
+//
+// Two deterministic passes built from one templated kernel (no atomics):
+//   DKDV: a CTA owns 128 keys of one kv head and streams 64-query blocks of every q head of the
+//         GQA group:   S^T = K Q^T,  dP^T = V dO^T            (TMEM, double-buffered)
+//                      P^T = exp2(S^T * c - lse[q]),  dS^T = P^T (dP^T - delta[q])   (CUDA cores)
+//                      dV += P^T dO,  dK += dS^T Q            (TMEM accumulators)
+//   DQ:   a CTA owns 128 queries of one q head and streams 64-key blocks:
+//                      S = Q K^T, dP = dO V^T,  P = exp2(S * c - lse[row]),  dS = P (dP - delta[row])
+//                      dQ += dS K
+// Roles per CTA (6 warps): warp 0 TMA (4-D tensor maps over the caller's strides, SWIZZLE_128B, no
+// multicast), warp 1 single-thread MMA issuer, warps 2..5 elementwise (thread = TMEM lane = row),
+// which write P/dS as bf16 K-major tiles that the accumulate MMAs read from shared memory; the
+// streamed operand is read a second time as an MN-major B operand, so nothing is transposed.
+// Bounded waits report through the status word. Reference: the Value-graph attention VJPs
+// (crates/brain-autograd/src/grad_fns/mod.rs:327-420); mask/scale conventions as in attention_tc.cu.
+#include "common.cuh"
+
+using namespace brain;
+
+namespace {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kThreads = 192;
+constexpr int SUB128 = 128 * 128;  // 128 rows x 64 bf16 (16 KB)
+constexpr int SUB64 = 64 * 128;    // 64 rows x 64 bf16 (8 KB)
+
+enum { DKDV = 0, DQ = 1 };
+
+struct BwdArgs {
+  const float* lse;    // [B, Hq, Sq] natural log
+  const float* delta;  // [B, Hq, Sq]
+  __nv_bfloat16 *out1, *out2;  // DKDV: dV, dK   DQ: dQ
+  int64_t o1b, o1s, o1h, o2b, o2s, o2h;
+  int B, Hq, Hkv, Sq, Sk;
+  float scale, scale_log2;
+  int causal;
+};
+
+template <int D, int MODE>
+struct BwdLayout {
+  static constexpr int NSUB = D / 64;
+  static constexpr int STAGES = D == 64 ? 4 : 2;
+  static constexpr int A_BYTES = NSUB * SUB128;  // one row operand [128, D]
+  static constexpr int B_BYTES = NSUB * SUB64;   // one streamed operand [64, D]
+  static constexpr int A_OFF = 0;                // A1, A2
+  static constexpr int B_OFF = 2 * A_BYTES;      // stages of (B1, B2)
+  static constexpr int STAGE_BYTES = 2 * B_BYTES;
+  static constexpr int NC = MODE == DKDV ? 2 : 1;  // C tiles (P^T, dS^T) or (dS)
+  static constexpr int C_OFF = B_OFF + STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = C_OFF + NC * SUB128;
+  // a_full, b_full[S], b_empty[S], sd_full[2], sd_free[2], c_full, c_free, acc_done, drain
+  static constexpr int NBAR = 1 + 2 * STAGES + 4 + 4;
+  static constexpr int TOTAL = BAR_OFF + NBAR * 8 + 16 + 1024;
+};
+
+template <int D, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap mA1, const __grid_constant__ CUtensorMap mA2,
+                     const __grid_constant__ CUtensorMap mB1, const __grid_constant__ CUtensorMap mB2, BwdArgs a) {
+  using L = BwdLayout<D, MODE>;
+  constexpr int ST = L::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t sA1 = sbase + L::A_OFF, sA2 = sA1 + L::A_BYTES;
+  const uint32_t sB = sbase + L::B_OFF, sC = sbase + L::C_OFF;
+  const uint32_t bars = sbase + L::BAR_OFF;
+  const uint32_t a_full = bars;
+  auto b_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto b_empty = [&](int s) { return bars + 8u * (1 + ST + s); };
+  auto sd_full = [&](int i) { return bars + 8u * (1 + 2 * ST + i); };
+  auto sd_free = [&](int i) { return bars + 8u * (3 + 2 * ST + i); };
+  const uint32_t c_full = bars + 8u * (5 + 2 * ST);
+  const uint32_t c_free = bars + 8u * (6 + 2 * ST);
+  const uint32_t acc_done = bars + 8u * (7 + 2 * ST);
+  const uint32_t drain = bars + 8u * (8 + 2 * ST);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBAR * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int group = a.Hq / a.Hkv;
+  const int off = a.Sk - a.Sq;
+
+  // ---- work decomposition
+  int b, hrow;      // batch and head of the row operand (kv head for DKDV, q head for DQ)
+  int r0;           // first row (key for DKDV, query for DQ)
+  int first_blk;    // first streamed 64-block index
+  int nblk;         // streamed blocks per head
+  int niter;        // total iterations (DKDV: x group)
+  if (MODE == DKDV) {
+    const int bh = blockIdx.y;
+    b = bh / a.Hkv;
+    hrow = bh % a.Hkv;
+    r0 = blockIdx.x * 128;
+    int qstart = 0;
+    if (a.causal) qstart = max(0, r0 - off);
+    first_blk = qstart / 64;
+    const int tot = (a.Sq + 63) / 64;
+    nblk = max(0, tot - first_blk);
+    niter = nblk * group;
+  } else {
+    const int nmb = (a.Sq + 127) / 128;
+    const int mb = a.causal ? (nmb - 1 - (int)blockIdx.x) : (int)blockIdx.x;
+    const int bh = blockIdx.y;
+    b = bh / a.Hq;
+    hrow = bh % a.Hq;
+    r0 = mb * 128;
+    first_blk = 0;
+    int kend = a.Sk;
+    if (a.causal) kend = min(a.Sk, r0 + 128 + off);
+    nblk = kend > 0 ? (kend + 63) / 64 : 0;
+    niter = nblk;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(a_full, 1);
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(b_full(s), 1);
+      mbar_init(b_empty(s), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(sd_full(i), 1);
+      mbar_init(sd_free(i), 128);
+    }
+    mbar_init(c_full, 128);
+    mbar_init(c_free, 1);
+    mbar_init(acc_done, 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // buf b: S at b*128, dP at b*128+64; acc1 at 256; acc2 at 256 + D
+
+  if (warp == 0) {
+    if (lane == 0 && niter > 0) {
+      // ---------------- TMA producer
+      mbar_arrive_expect_tx(a_full, 2 * L::A_BYTES);
+      const int ha = MODE == DKDV ? hrow : hrow;
+      for (int c = 0; c < L::NSUB; ++c) {
+        tma_load_4d(&mA1, sA1 + c * SUB128, a_full, c * 64, r0, ha, b);
+        tma_load_4d(&mA2, sA2 + c * SUB128, a_full, c * 64, r0, ha, b);
+      }
+      int i = 0;
+      for (; i < niter; ++i) {
+        const int s = i % ST;
+        if (!mbar_wait(b_empty(s), ((i / ST) & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 210, abort_flag)) break;
+        int hb, row;
+        if (MODE == DKDV) {
+          hb = hrow * group + i / nblk;
+          row = (first_blk + i % nblk) * 64;
+        } else {
+          hb = hrow / group;
+          row = i * 64;
+        }
+        const uint32_t st = sB + s * L::STAGE_BYTES;
+        mbar_arrive_expect_tx(b_full(s), L::STAGE_BYTES);
+        for (int c = 0; c < L::NSUB; ++c) {
+          tma_load_4d(&mB1, st + c * SUB64, b_full(s), c * 64, row, hb, b);
+          tma_load_4d(&mB2, st + L::B_BYTES + c * SUB64, b_full(s), c * 64, row, hb, b);
+        }
+      }
+      if (i < niter) {
+        for (int j = max(0, i - ST); j < i; ++j) {
+          uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(b_full(j % ST), (j / ST) & 1) && globaltimer() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && niter > 0) {
+      // ---------------- MMA issuer
+      constexpr uint32_t IDESC_S = idesc_f16(128, 64, 1u, 0u, 0u);
+      constexpr uint32_t IDESC_ACC = idesc_f16(128, D, 1u, 0u, 1u);
+      bool ok = mbar_wait(a_full, 0, BRAIN_ERR_TIMEOUT_FULL, 220, abort_flag);
+      bool issued = false;
+      auto issue_scores = [&](int i) {
+        const uint32_t st = sB + (i % ST) * L::STAGE_BYTES;
+        const uint32_t d = tmem + (uint32_t)((i & 1) * 128);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t oa = (kk / 4) * SUB128 + (kk % 4) * 32;
+          const uint32_t ob = (kk / 4) * SUB64 + (kk % 4) * 32;
+          tc_mma_f16(d, smem_desc_sw128(sA1 + oa, 16, 1024), smem_desc_sw128(st + ob, 16, 1024), IDESC_S,
+                     kk > 0 ? 1u : 0u);
+          tc_mma_f16(d + 64, smem_desc_sw128(sA2 + oa, 16, 1024), smem_desc_sw128(st + L::B_BYTES + ob, 16, 1024),
+                     IDESC_S, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(sd_full(i & 1));
+      };
+      if (ok) ok = mbar_wait(b_full(0), 0, BRAIN_ERR_TIMEOUT_FULL, 221, abort_flag);
+      if (ok) {
+        tc_fence_after();
+        issue_scores(0);
+        issued = true;
+      }
+      for (int i = 0; ok && i < niter; ++i) {
+        if (i + 1 < niter) {
+          const int in = i + 1;
+          if (!mbar_wait(b_full(in % ST), (in / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 222, abort_flag) ||
+              !mbar_wait(sd_free(in & 1), ((in / 2) & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 223, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          issue_scores(in);
+        }
+        if (!mbar_wait(c_full, i & 1, BRAIN_ERR_TIMEOUT_ACC, 224, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t st = sB + (i % ST) * L::STAGE_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < 64 / 16; ++kk) {
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          const uint64_t c0 = smem_desc_sw128(sC + kk * 32, 16, 1024);
+          if (MODE == DKDV) {
+            const uint64_t c1 = smem_desc_sw128(sC + SUB128 + kk * 32, 16, 1024);
+            // dV += P^T dO   (dO = B2, MN-major);  dK += dS^T Q   (Q = B1, MN-major)
+            tc_mma_f16(tmem + 256, c0, smem_desc_sw128(st + L::B_BYTES + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
+            tc_mma_f16(tmem + 256 + D, c1, smem_desc_sw128(st + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
+          } else {
+            // dQ += dS K   (K = B1, MN-major)
+            tc_mma_f16(tmem + 256, c0, smem_desc_sw128(st + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
+          }
+        }
+        tc_commit(c_free);
+        tc_commit(b_empty(i % ST));
+      }
+      if (ok) {
+        tc_commit(acc_done);
+      } else if (issued) {
+        tc_commit(drain);
+        uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ---------------- elementwise warps (2..5)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const int row = r0 + r;
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    float row_lse2 = 0.f, row_delta = 0.f;
+    if (MODE == DQ && row < a.Sq) {
+      const int64_t idx = ((int64_t)b * a.Hq + hrow) * a.Sq + row;
+      row_lse2 = a.lse[idx] * kLog2e;
+      row_delta = a.delta[idx];
+    }
+    const bool row_valid_q = MODE == DQ ? (row < a.Sq) : true;
+    bool ok = true;
+    for (int i = 0; i < niter; ++i) {
+      int col0, hcol;
+      if (MODE == DKDV) {
+        hcol = hrow * group + i / nblk;
+        col0 = (first_blk + i % nblk) * 64;
+      } else {
+        hcol = hrow;
+        col0 = i * 64;
+      }
+      if (!mbar_wait(sd_full(i & 1), (i / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      float s[64], dp[64];
+      const uint32_t tb = tmem + (uint32_t)((i & 1) * 128) + lane_addr;
+      tmem_ld32(tb, reinterpret_cast<uint32_t*>(s));
+      tmem_ld32(tb + 32, reinterpret_cast<uint32_t*>(s + 32));
+      tmem_ld32(tb + 64, reinterpret_cast<uint32_t*>(dp));
+      tmem_ld32(tb + 96, reinterpret_cast<uint32_t*>(dp + 32));
+      tc_wait_ld();
+      tc_fence_before();
+      mbar_arrive(sd_free(i & 1));
+      uint32_t pk[32], dk[32];
+      if (MODE == DKDV) {
+        const float* lrow = a.lse + ((int64_t)b * a.Hq + hcol) * a.Sq;
+        const float* drow = a.delta + ((int64_t)b * a.Hq + hcol) * a.Sq;
+        const int key = row;
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          float pv[2], dv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int qi = col0 + c + e;
+            const bool valid = qi < a.Sq && !(a.causal && key > qi + off);
+            const float l2 = valid ? __ldg(lrow + qi) * kLog2e : 0.f;
+            const float de = valid ? __ldg(drow + qi) : 0.f;
+            const float p = valid ? ex2_fast(s[c + e] * a.scale_log2 - l2) : 0.f;
+            pv[e] = p;
+            dv[e] = p * (dp[c + e] - de);
+          }
+          __nv_bfloat162 hp = __floats2bfloat162_rn(pv[0], pv[1]);
+          __nv_bfloat162 hd = __floats2bfloat162_rn(dv[0], dv[1]);
+          pk[c / 2] = *reinterpret_cast<uint32_t*>(&hp);
+          dk[c / 2] = *reinterpret_cast<uint32_t*>(&hd);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          float dv[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int key = col0 + c + e;
+            const bool valid = row_valid_q && key < a.Sk && !(a.causal && key > row + off);
+            const float p = valid ? ex2_fast(s[c + e] * a.scale_log2 - row_lse2) : 0.f;
+            dv[e] = p * (dp[c + e] - row_delta);
+          }
+          __nv_bfloat162 hd = __floats2bfloat162_rn(dv[0], dv[1]);
+          dk[c / 2] = *reinterpret_cast<uint32_t*>(&hd);
+        }
+      }
+      if (i > 0 && !mbar_wait(c_free, (i - 1) & 1, BRAIN_ERR_TIMEOUT_ACC, 231, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 columns = 128 B per row
+        const uint32_t o = r * 128 + ((c ^ (r % 8)) * 16);
+        if (MODE == DKDV) {
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sC + o), "r"(pk[4 * c]), "r"(pk[4 * c + 1]),
+                       "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
+                       : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sC + SUB128 + o), "r"(dk[4 * c]),
+                       "r"(dk[4 * c + 1]), "r"(dk[4 * c + 2]), "r"(dk[4 * c + 3])
+                       : "memory");
+        } else {
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sC + o), "r"(dk[4 * c]), "r"(dk[4 * c + 1]),
+                       "r"(dk[4 * c + 2]), "r"(dk[4 * c + 3])
+                       : "memory");
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(c_full);
+    }
+    bool have = ok && niter > 0;
+    if (have && !mbar_wait(acc_done, 0, BRAIN_ERR_TIMEOUT_ACC, 232, abort_flag)) have = false;
+    tc_fence_after();
+    // epilogue: DKDV writes dV (acc1) and dK * scale (acc2); DQ writes dQ * scale (acc1)
+    const bool store = MODE == DKDV ? (row < a.Sk) : (row < a.Sq);
+#pragma unroll 1
+    for (int which = 0; which < (MODE == DKDV ? 2 : 1); ++which) {
+      __nv_bfloat16* base;
+      float mul;
+      if (MODE == DKDV) {
+        base = which == 0 ? a.out1 + (int64_t)b * a.o1b + (int64_t)hrow * a.o1h + (int64_t)row * a.o1s
+                          : a.out2 + (int64_t)b * a.o2b + (int64_t)hrow * a.o2h + (int64_t)row * a.o2s;
+        mul = which == 0 ? 1.f : a.scale;
+      } else {
+        base = a.out1 + (int64_t)b * a.o1b + (int64_t)hrow * a.o1h + (int64_t)row * a.o1s;
+        mul = a.scale;
+      }
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t ov[32];
+        if (have) {
+          tmem_ld32(tmem + 256 + (uint32_t)(which * D + c * 32) + lane_addr, ov);
+          tc_wait_ld();
+        } else {
+#pragma unroll
+          for (int k = 0; k < 32; ++k) ov[k] = 0u;
+        }
+        if (store) {
+          float v[32];
+#pragma unroll
+          for (int k = 0; k < 32; ++k) v[k] = __uint_as_float(ov[k]) * mul;
+#pragma unroll
+          for (int k = 0; k < 32; k += 8) store8(base + c * 32 + k, v + k);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// delta[b, h, i] = sum_d dO * O   (one warp per row, 16-byte loads)
+__global__ void bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t ob, int64_t os, int64_t oh,
+                                 const __nv_bfloat16* __restrict__ dO, int64_t db, int64_t ds, int64_t dh,
+                                 float* __restrict__ delta, int B, int H, int S, int D) {
+  const int64_t rowid = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (rowid >= (int64_t)B * H * S) return;
+  const int i = (int)(rowid % S);
+  const int bh = (int)(rowid / S);
+  const int b = bh / H, h = bh % H;
+  const __nv_bfloat16* po = o + b * ob + h * oh + (int64_t)i * os;
+  const __nv_bfloat16* pd = dO + b * db + h * dh + (int64_t)i * ds;
+  float acc = 0.f;
+  for (int d = lane * 8; d < D; d += 256) {
+    float x[8], y[8];
+    load8(po + d, x);
+    load8(pd + d, y);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc += x[k] * y[k];
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) delta[rowid] = acc;
+}
+
+bool map4(CUtensorMap* m, const void* base, int D, int S, int H, int B, int64_t ss, int64_t sh, int64_t sb,
+          int box_rows) {
+  uint64_t dims[4] = {(uint64_t)D, (uint64_t)S, (uint64_t)H, (uint64_t)B};
+  uint64_t strides[3] = {(uint64_t)ss * 2, (uint64_t)sh * 2, (uint64_t)sb * 2};
+  uint32_t box[4] = {64, (uint32_t)box_rows, 1, 1};
+  return brain_host::encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int D, int MODE>
+int launch_mode(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap& b1, const CUtensorMap& b2,
+                const BwdArgs& a, cudaStream_t st) {
+  using L = BwdLayout<D, MODE>;
+  auto kern = fa_bwd_tc_kernel<D, MODE>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
+  dim3 grid;
+  if (MODE == DKDV) grid = dim3((a.Sk + 127) / 128, a.B * a.Hkv);
+  else grid = dim3((a.Sq + 127) / 128, a.B * a.Hq);
+  kern<<<grid, kThreads, L::TOTAL, st>>>(a1, a2, b1, b2, a);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+BRAIN_STATUS_READER(attention_bwd_tc)
+
+// Same argument contract as brain_attn_bwd (attention.cu). Returns cudaErrorNotSupported without
+// launching when the layout is outside the tensor-core path (D not 64/128, unaligned strides).
+BRAIN_API int brain_attn_bwd_tc(const void* q, const void* k, const void* v, const int64_t* s9, const void* o,
+                                const int64_t* ostr, const float* lse, const void* dout, const int64_t* dostr,
+                                void* dq, const int64_t* dqstr, void* dk, const int64_t* dkstr, void* dv,
+                                const int64_t* dvstr, float* delta, int B, int Hq, int Hkv, int Sq, int Sk, int D,
+                                float scale, int causal, cudaStream_t st) {
+  if (Hkv <= 0 || Hq % Hkv) return (int)cudaErrorInvalidValue;
+  if (D != 64 && D != 128) return (int)cudaErrorNotSupported;
+  const int64_t* all[6] = {s9, s9 + 3, s9 + 6, dostr, ostr, dqstr};
+  for (int t = 0; t < 6; ++t)
+    for (int i = 0; i < 3; ++i)
+      if ((all[t][i] * 2) % 16) return (int)cudaErrorNotSupported;
+  for (int i = 0; i < 3; ++i)
+    if (dkstr[i] % 8 || dvstr[i] % 8) return (int)cudaErrorNotSupported;
+  if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)dout | (uintptr_t)dq | (uintptr_t)dk | (uintptr_t)dv) &
+      15)
+    return (int)cudaErrorNotSupported;
+  if (B * Hq == 0 || Sq == 0) return 0;
+  // delta = rowsum(dO * O)
+  {
+    const int64_t rows = (int64_t)B * Hq * Sq;
+    bwd_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(o), ostr[0], ostr[1], ostr[2],
+        reinterpret_cast<const __nv_bfloat16*>(dout), dostr[0], dostr[1], dostr[2], delta, B, Hq, Sq, D);
+  }
+  CUtensorMap mq128, mdo128, mk64, mv64, mk128, mv128, mq64, mdo64;
+  bool ok = map4(&mq128, q, D, Sq, Hq, B, s9[1], s9[2], s9[0], 128) &&
+            map4(&mdo128, dout, D, Sq, Hq, B, dostr[1], dostr[2], dostr[0], 128) &&
+            map4(&mk64, k, D, Sk, Hkv, B, s9[4], s9[5], s9[3], 64) &&
+            map4(&mv64, v, D, Sk, Hkv, B, s9[7], s9[8], s9[6], 64) &&
+            map4(&mk128, k, D, Sk, Hkv, B, s9[4], s9[5], s9[3], 128) &&
+            map4(&mv128, v, D, Sk, Hkv, B, s9[7], s9[8], s9[6], 128) &&
+            map4(&mq64, q, D, Sq, Hq, B, s9[1], s9[2], s9[0], 64) &&
+            map4(&mdo64, dout, D, Sq, Hq, B, dostr[1], dostr[2], dostr[0], 64);
+  if (!ok) return (int)cudaErrorNotSupported;
+  BwdArgs a{};
+  a.lse = lse;
+  a.delta = delta;
+  a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.Sq = Sq; a.Sk = Sk;
+  a.scale = scale;
+  a.scale_log2 = scale * kLog2e;
+  a.causal = causal;
+  // dK / dV
+  a.out1 = reinterpret_cast<__nv_bfloat16*>(dv);
+  a.o1b = dvstr[0]; a.o1s = dvstr[1]; a.o1h = dvstr[2];
+  a.out2 = reinterpret_cast<__nv_bfloat16*>(dk);
+  a.o2b = dkstr[0]; a.o2s = dkstr[1]; a.o2h = dkstr[2];
+  int rc = D == 64 ? launch_mode<64, DKDV>(mk128, mv128, mq64, mdo64, a, st)
+                   : launch_mode<128, DKDV>(mk128, mv128, mq64, mdo64, a, st);
+  if (rc) return rc;
+  // dQ
+  a.out1 = reinterpret_cast<__nv_bfloat16*>(dq);
+  a.o1b = dqstr[0]; a.o1s = dqstr[1]; a.o1h = dqstr[2];
+  a.out2 = nullptr;
+  return D == 64 ? launch_mode<64, DQ>(mq128, mdo128, mk64, mv64, a, st)
+                 : launch_mode<128, DQ>(mq128, mdo128, mk64, mv64, a, st);
+}

@@ -33,6 +33,8 @@ _native.register({
     "brain_attn_bwd": ("brain_kernels", "pppppppppppppppp" + "iiiiiifis"),
     "brain_attn_fwd_tc": ("brain_kernels", "pppppppiiiiiifis"),
     "brain_status_attention_tc": ("brain_kernels", "pi"),
+    "brain_attn_bwd_tc": ("brain_kernels", "pppppppppppppppp" + "iiiiiifis"),
+    "brain_status_attention_bwd_tc": ("brain_kernels", "pi"),
     "brain_status_norms": ("brain_kernels", "pi"),
     "brain_status_elementwise": ("brain_kernels", "pi"),
     "brain_status_ce": ("brain_kernels", "pi"),
@@ -40,7 +42,7 @@ _native.register({
     "brain_status_attention": ("brain_kernels", "pi"),
 })
 
-STATUS_TAGS = ["gemm", "norms", "elementwise", "ce", "optim", "attention", "attention_tc"]
+STATUS_TAGS = ["gemm", "norms", "elementwise", "ce", "optim", "attention", "attention_tc", "attention_bwd_tc"]
 
 
 def stream(t: torch.Tensor) -> int:

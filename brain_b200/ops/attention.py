@@ -48,15 +48,22 @@ def _fwd(q, k, v, causal, scale, impl=None):
     return o, lse
 
 
-def _bwd(q, k, v, o, lse, do, dq, dk, dv, causal, scale):
+def _bwd(q, k, v, o, lse, do, dq, dk, dv, causal, scale, impl=None):
     B, Sq, Hq, D = q.shape
     Sk, Hkv = k.shape[1], k.shape[2]
     delta = torch.empty(B * Hq * Sq, device=q.device, dtype=torch.float32)
-    _native.call("brain_attn_bwd", q.data_ptr(), k.data_ptr(), v.data_ptr(),
-                 i64_array(_strides3(q) + _strides3(k) + _strides3(v)), o.data_ptr(), i64_array(_strides3(o)),
-                 lse.data_ptr(), do.data_ptr(), i64_array(_strides3(do)), dq.data_ptr(), i64_array(_strides3(dq)),
-                 dk.data_ptr(), i64_array(_strides3(dk)), dv.data_ptr(), i64_array(_strides3(dv)), delta.data_ptr(),
-                 B, Hq, Hkv, Sq, Sk, D, float(scale), int(causal), stream(q))
+    args = (q.data_ptr(), k.data_ptr(), v.data_ptr(), i64_array(_strides3(q) + _strides3(k) + _strides3(v)),
+            o.data_ptr(), i64_array(_strides3(o)), lse.data_ptr(), do.data_ptr(), i64_array(_strides3(do)),
+            dq.data_ptr(), i64_array(_strides3(dq)), dk.data_ptr(), i64_array(_strides3(dk)), dv.data_ptr(),
+            i64_array(_strides3(dv)), delta.data_ptr(), B, Hq, Hkv, Sq, Sk, D, float(scale), int(causal), stream(q))
+    use_tc = USE_TC if impl is None else impl == "tc"
+    if use_tc:
+        rc = _native.fn("brain_attn_bwd_tc")(*args)
+        if rc == 0:
+            return
+        if rc != _NOT_SUPPORTED or impl == "tc":
+            raise _native.NativeError(f"brain_attn_bwd_tc failed with status {rc}")
+    _native.call("brain_attn_bwd", *args)
 
 
 def _check(t):

@@ -1,2 +1,6 @@
-"""Optimizers (fused AdamW / SGD kernels over flat buffers, plus the reference's optimizer family)."""
+"""Optimizers (brain-optim): fused AdamW / SGD kernels, the reference's optimizer family,
+schedulers, clipping, EMA/SWA, and the sharded flat AdamW used by the data-parallel engine."""
 from .flat_adamw import FlatAdamW  # noqa: F401
+from .optimizers import *  # noqa: F401,F403
+from .schedulers import *  # noqa: F401,F403
+from ..autograd.functional import GradScaler  # noqa: F401

@@ -16,11 +16,10 @@ from __future__ import annotations
 import torch
 
 from ..ops import optim_kernels as K
-from ..parallel.flat import FlatParams
 
 
 class FlatAdamW:
-    def __init__(self, flat: FlatParams, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
+    def __init__(self, flat, lr: float = 1e-3, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.0, amsgrad: bool = False, comm=None):
         self.flat = flat
         self.lr, self.betas, self.eps, self.weight_decay, self.amsgrad = lr, betas, eps, weight_decay, amsgrad

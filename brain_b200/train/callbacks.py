@@ -1,0 +1,121 @@
+"""Training callbacks, metrics and checkpoint tracking (crates/brain-train/src/callbacks.rs:19-131,
+metrics.rs, checkpointer.rs:9-62): ``EarlyStopping``, ``MetricHistoryLogger``, ``AccuracyMetric``,
+``RunningAverage``, ``TopKAccuracyMetric``, ``BestModelTracker``, ``CheckpointMeta``, plus a JSONL
+step logger with the rank prefix used by the distributed runs."""
+from __future__ import annotations
+
+import json
+import math
+from dataclasses import dataclass
+
+import torch
+
+
+class TrainingCallback:
+    def on_epoch_start(self, trainer, epoch: int) -> None:
+        pass
+
+    def on_step_end(self, trainer, step) -> None:
+        pass
+
+    def on_epoch_end(self, trainer, epoch: int, loss: float) -> bool:
+        """Return True to stop training."""
+        return False
+
+
+class EarlyStopping(TrainingCallback):
+    def __init__(self, patience: int = 3, min_delta: float = 0.0):
+        self.patience, self.min_delta = patience, min_delta
+        self.best = math.inf
+        self.bad = 0
+        self.stopped_epoch = None
+
+    def on_epoch_end(self, trainer, epoch, loss):
+        if loss < self.best - self.min_delta:
+            self.best, self.bad = loss, 0
+            return False
+        self.bad += 1
+        if self.bad >= self.patience:
+            self.stopped_epoch = epoch
+            return True
+        return False
+
+
+class MetricHistoryLogger(TrainingCallback):
+    def __init__(self):
+        self.losses: list[float] = []
+        self.accuracies: list[float] = []
+        self.epoch_losses: list[float] = []
+
+    def on_step_end(self, trainer, step):
+        self.losses.append(step.loss)
+        self.accuracies.append(step.accuracy)
+
+    def on_epoch_end(self, trainer, epoch, loss):
+        self.epoch_losses.append(loss)
+        return False
+
+
+class JsonlStepLogger(TrainingCallback):
+    def __init__(self, path: str, rank: int = 0):
+        self.f = open(path, "a")
+        self.rank = rank
+
+    def on_step_end(self, trainer, step):
+        self.f.write(json.dumps({"rank": self.rank, "step": trainer.steps, "loss": step.loss, "acc": step.accuracy,
+                                 "grad_norm": step.optimizer.grad_norm, "lr": step.optimizer.lr}) + "\n")
+        self.f.flush()
+
+
+class RunningAverage:
+    def __init__(self):
+        self.total, self.count = 0.0, 0
+
+    def update(self, v: float, n: int = 1):
+        self.total += v * n
+        self.count += n
+
+    def value(self) -> float:
+        return self.total / self.count if self.count else 0.0
+
+    def reset(self):
+        self.total, self.count = 0.0, 0
+
+
+class AccuracyMetric(RunningAverage):
+    def update_logits(self, logits: torch.Tensor, targets: torch.Tensor):
+        pred = logits.argmax(-1)
+        self.total += float((pred == targets).sum())
+        self.count += targets.numel()
+
+
+class TopKAccuracyMetric(RunningAverage):
+    def __init__(self, k: int = 5):
+        super().__init__()
+        self.k = k
+
+    def update_logits(self, logits, targets):
+        top = logits.topk(self.k, -1).indices
+        self.total += float((top == targets[..., None]).any(-1).sum())
+        self.count += targets.numel()
+
+
+@dataclass
+class CheckpointMeta:
+    epoch: int
+    step: int
+    metric: float
+    path: str
+
+
+class BestModelTracker:
+    def __init__(self, mode: str = "min"):
+        self.mode = mode
+        self.best: CheckpointMeta | None = None
+
+    def update(self, meta: CheckpointMeta) -> bool:
+        better = self.best is None or (meta.metric < self.best.metric if self.mode == "min"
+                                       else meta.metric > self.best.metric)
+        if better:
+            self.best = meta
+        return better

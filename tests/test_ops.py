@@ -220,6 +220,28 @@ def test_flash_attention_tcgen05_forward(D, causal, B, Sq, Sk, Hq, Hkv):
 
 
 @gpu
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("B,Sq,Sk,Hq,Hkv", [(1, 128, 128, 2, 2), (2, 300, 300, 8, 2), (1, 200, 517, 4, 1),
+                                            (1, 640, 640, 4, 4), (2, 1, 129, 4, 2)])
+def test_flash_attention_tcgen05_backward(D, causal, B, Sq, Sk, Hq, Hkv):
+    q = rnd(B, Sq, Hq, D, seed=44)
+    k = rnd(B, Sk, Hkv, D, seed=45)
+    v = rnd(B, Sk, Hkv, D, seed=46)
+    do = rnd(B, Sq, Hq, D, seed=47)
+    scale = D ** -0.5
+    o, lse = attn._fwd(q, k, v, causal, scale)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    attn._bwd(q, k, v, o, lse, do, dq, dk, dv, causal, scale, impl="tc")
+    _, (qr, kr, vr) = grads(lambda a, b, c: attn.sdpa_ref(a.float(), b.float(), c.float(), causal), q, k, v)
+    attn.sdpa_ref(qr.float(), kr.float(), vr.float(), causal).backward(do.float())
+    close(dq, qr.grad, 3e-2, 3e-2)
+    close(dk, kr.grad, 3e-2, 3e-2)
+    close(dv, vr.grad, 3e-2, 3e-2)
+    assert ops.check_status() == []
+
+
+@gpu
 def test_flash_attention_tcgen05_strided_qkv():
     B, S, Hq, Hkv, D = 2, 384, 8, 2, 128
     qkv = rnd(B, S, (Hq + 2 * Hkv) * D, seed=43)
