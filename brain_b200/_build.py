@@ -39,6 +39,7 @@ LIBRARIES = {
         "host_utils.cu", "gemm.cu", "norms.cu", "elementwise.cu", "cross_entropy.cu", "optim.cu",
         "attention.cu", "attention_tc.cu", "attention_bwd_tc.cu",
     ],
+    "brain_comm": ["host_utils.cu", "comm.cu"],
 }
 # Host-only C++ libraries (g++): the checkpoint codec and the runtime helpers.
 CXX_LIBRARIES = {

@@ -54,9 +54,11 @@ class FlatAdamW:
         self.flat.absorb_grads()
         self.step_count += 1
         b1, b2 = self.betas
-        if world > 1 and self.comm is not None and getattr(self.comm, "fused_rs_adamw", None) is not None:
-            # one kernel: reduce-scatter over NVLink + un-scale + AdamW + bf16 cast of the shard
+        if (world > 1 and self.comm is not None and getattr(self.comm, "fused_rs_adamw", None) is not None
+                and not check_finite and self.vmax is None):
+            # one kernel: NVLink reduce-scatter + un-scale + AdamW + bf16 weights pushed to every rank
             self.comm.fused_rs_adamw(self, grad_scale / world)
+            return
         else:
             if world > 1:
                 self.comm.reduce_scatter_flat(self.flat.grad_buf, self.grad_shard())

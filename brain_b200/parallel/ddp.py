@@ -36,7 +36,8 @@ class DataParallel:
             else:
                 comm = NcclComm()
         self.comm = comm
-        self.flat = FlatParams(list(model.parameters()), ctx.world_size, ctx.rank, grad_dtype)
+        alloc = comm.alloc if getattr(comm, "name", "") == "nvlink" else None
+        self.flat = FlatParams(list(model.parameters()), ctx.world_size, ctx.rank, grad_dtype, alloc=alloc)
         if ctx.world_size > 1:
             self.comm.broadcast(self.flat.param_buf, 0)
         self.optimizer = FlatAdamW(self.flat, lr, betas, eps, weight_decay, comm=self.comm)

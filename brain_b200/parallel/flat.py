@@ -17,7 +17,7 @@ import torch
 
 class FlatParams:
     def __init__(self, params: list[torch.nn.Parameter], world_size: int = 1, rank: int = 0,
-                 grad_dtype: torch.dtype = torch.float32, align: int = 64):
+                 grad_dtype: torch.dtype = torch.float32, align: int = 64, alloc=None):
         self.params = [p for p in params if p.requires_grad]
         if not self.params:
             raise ValueError("no trainable parameters")
@@ -33,8 +33,11 @@ class FlatParams:
         unit = world_size * align
         self.padded = -(-off // unit) * unit
         self.shard_size = self.padded // world_size
-        self.param_buf = torch.zeros(self.padded, device=dev, dtype=dtype)
-        self.grad_buf = torch.zeros(self.padded, device=dev, dtype=grad_dtype)
+        if alloc is None:  # plain device memory; the NVLink backend passes a symmetric allocator
+            def alloc(n, dt):
+                return torch.zeros(n, device=dev, dtype=dt)
+        self.param_buf = alloc(self.padded, dtype)
+        self.grad_buf = alloc(self.padded, grad_dtype)
         with torch.no_grad():
             for p, o in zip(self.params, self.offsets):
                 n = p.numel()

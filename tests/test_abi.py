@@ -3,6 +3,8 @@ import os
 import re
 
 import brain_b200.ops  # noqa: F401  (registers op signatures)
+import brain_b200.parallel.symm  # noqa: F401
+import brain_b200.checkpoint  # noqa: F401
 from brain_b200 import _native
 
 CSRC = os.path.join(os.path.dirname(_native.__file__), "csrc")

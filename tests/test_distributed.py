@@ -1,0 +1,221 @@
+"""Distributed runtime tests.
+
+CPU (Gloo, 2 ranks, always run): collectives, mean gradient reduction of the data-parallel engine
+against a single-process computation, the reference's in-process ring all-reduce, topologies,
+and host-side failure detection (a rank that never joins makes the others' collective fail within
+the process-group timeout, with no GPU involved).
+GPU (NCCL + the NVLink P2P kernels, 2 ranks, marked gpu + multigpu): collectives against exact
+sums, the fused reduce-scatter + AdamW + all-gather DDP step against the NCCL path, and a device-side
+barrier whose peer never arrives returning an error status within its 1 s budget (no trap, no hang).
+"""
+import os
+
+import pytest
+import torch
+
+from tests._mp import run_ranks
+
+
+# ------------------------------------------------------------------ CPU / Gloo
+def _cpu_collectives(rank, world):
+    import torch.distributed as dist
+    from brain_b200.parallel import dist as bdist
+    from brain_b200.parallel import collectives as C
+    bdist.init(device="cpu", timeout_s=60)
+    t = torch.arange(8, dtype=torch.float32) + rank * 100
+    C.all_reduce(t)
+    ar = t.tolist()
+    m = torch.full((4,), float(rank + 1))
+    C.all_reduce(m, op="mean")
+    g = C.all_gather(torch.tensor([rank, rank], dtype=torch.float32))
+    rs = C.reduce_scatter(torch.arange(4, dtype=torch.float32) * (rank + 1))
+    b = torch.tensor([rank * 1.0 + 5])
+    C.broadcast(b, src=1)
+    dist.barrier()
+    bdist.shutdown()
+    return ar, m.tolist(), g.tolist(), rs.tolist(), b.tolist()
+
+
+def test_gloo_collectives():
+    out = run_ranks(_cpu_collectives, 2)
+    for rank, (ar, m, g, rs, b) in enumerate(out):
+        assert ar == [float(2 * i + 100) for i in range(8)]
+        assert m == [1.5] * 4
+        assert g == [0.0, 0.0, 1.0, 1.0]
+        full = [3.0 * i for i in range(4)]
+        assert rs == full[rank * 2:(rank + 1) * 2]
+        assert b == [6.0]
+
+
+def _cpu_ddp(rank, world):
+    from brain_b200.models import LlamaLite, LlamaLiteConfig
+    from brain_b200.parallel import DataParallel, dist as bdist
+    bdist.init(device="cpu", timeout_s=60)
+    cfg = LlamaLiteConfig.tiny(vocab_size=64)
+    model = LlamaLite(cfg, dtype=torch.float32, seed=0)
+    dp = DataParallel(model, lr=1e-2, betas=(0.9, 0.999), weight_decay=0.01)
+    g = torch.Generator().manual_seed(123 + rank)
+    tok = torch.randint(0, 64, (2, 17), generator=g)
+    dp.train_step(tok[:, :-1], tok[:, 1:])
+    w = model.layers[0].wqkv.detach().clone().numpy()
+    bdist.shutdown()
+    return w
+
+
+def test_gloo_data_parallel_matches_mean_of_gradients():
+    outs = run_ranks(_cpu_ddp, 2)
+    outs = [torch.from_numpy(o) for o in outs]
+    assert torch.equal(outs[0], outs[1])  # replicas stay identical
+    # single-process reference: mean of the two ranks' gradients, one AdamW step
+    from brain_b200.models import LlamaLite, LlamaLiteConfig
+    from brain_b200.optim import AdamW
+    cfg = LlamaLiteConfig.tiny(vocab_size=64)
+    model = LlamaLite(cfg, dtype=torch.float32, seed=0)
+    grads = None
+    for rank in range(2):
+        model.zero_grad()
+        g = torch.Generator().manual_seed(123 + rank)
+        tok = torch.randint(0, 64, (2, 17), generator=g)
+        model.loss(tok[:, :-1], tok[:, 1:]).backward()
+        cur = [p.grad.clone() for p in model.parameters()]
+        grads = cur if grads is None else [a + b for a, b in zip(grads, cur)]
+    for p, gsum in zip(model.parameters(), grads):
+        p.grad = gsum / 2
+    opt = AdamW(model.parameters(), lr=1e-2, betas=(0.9, 0.999), weight_decay=0.01)
+    opt.step()
+    torch.testing.assert_close(outs[0], model.layers[0].wqkv.detach(), rtol=1e-5, atol=1e-6)
+
+
+def _cpu_missing_peer(rank, world):
+    import datetime
+    import torch.distributed as dist
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        return "skipped collective"  # leaves between steps, never joins the all-reduce
+    t = torch.ones(4)
+    try:
+        dist.all_reduce(t)
+    except Exception as e:  # timeout / peer gone surfaces as an error, not a hang
+        return f"error: {type(e).__name__}"
+    return "no error"
+
+
+def test_gloo_missing_peer_fails_fast():
+    outs = run_ranks(_cpu_missing_peer, 2, timeout=120)
+    assert outs[1] == "skipped collective"
+    assert outs[0].startswith("error"), outs[0]
+
+
+def test_ring_allreduce_simulate_and_topology():
+    from brain_b200.parallel.collectives import RingTopology, TreeTopology, ring_allreduce_simulate
+    ranks = [torch.arange(7, dtype=torch.float64) * (r + 1) for r in range(3)]
+    out = ring_allreduce_simulate(ranks)
+    for o in out:
+        assert torch.equal(o, torch.arange(7, dtype=torch.float64) * 6)
+    r = RingTopology(4)
+    assert (r.left_neighbor(0), r.right_neighbor(3)) == (3, 0)
+    t = TreeTopology(5)
+    assert t.parent(0) is None and t.parent(4) == 1 and t.children(1) == [3, 4]
+
+
+# ------------------------------------------------------------------ GPU / NVLink
+def _gpu_collectives(rank, world):
+    from brain_b200.parallel import dist as bdist
+    from brain_b200.parallel.symm import NvlinkComm
+    bdist.init(timeout_s=120)
+    comm = NvlinkComm(timeout_s=10)
+    res = {}
+    for dtype in (torch.float32, torch.bfloat16):
+        for n in (1000, 3_000_001):
+            t = (torch.arange(n, device="cuda", dtype=torch.float32) % 97 + rank).to(dtype)
+            comm.all_reduce(t)
+            exp = ((torch.arange(n, device="cuda", dtype=torch.float32) % 97) * world + sum(range(world))).to(dtype)
+            res[f"ar_{dtype}_{n}"] = bool(torch.equal(t, exp))
+    full = torch.arange(4096 * world, device="cuda", dtype=torch.float32) * (rank + 1)
+    out = torch.empty(4096, device="cuda")
+    comm.reduce_scatter_flat(full, out)
+    s = sum(range(1, world + 1))
+    res["rs"] = bool(torch.equal(out, torch.arange(4096 * rank, 4096 * (rank + 1), device="cuda", dtype=torch.float32) * s))
+    shard = torch.full((1024,), float(rank), device="cuda", dtype=torch.bfloat16)
+    fullg = torch.empty(1024 * world, device="cuda", dtype=torch.bfloat16)
+    comm.all_gather_flat(shard, fullg)
+    res["ag"] = bool(torch.equal(fullg.view(world, 1024)[:, 0].float(), torch.arange(world, device="cuda").float()))
+    b = torch.full((33,), float(rank + 7), device="cuda")
+    comm.broadcast(b, src=world - 1)
+    res["bc"] = bool(torch.equal(b, torch.full((33,), float(world + 6), device="cuda")))
+    comm.check()
+    comm.close()
+    bdist.shutdown()
+    return res
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_nvlink_collectives():
+    n = min(torch.cuda.device_count(), 8)
+    outs = run_ranks(_gpu_collectives, n, env={"NCCL_NVLS_ENABLE": "0"})
+    for o in outs:
+        assert all(o.values()), o
+
+
+def _gpu_ddp(rank, world, comm_kind):
+    from brain_b200.models import LlamaLite, LlamaLiteConfig
+    from brain_b200.parallel import DataParallel, dist as bdist
+    bdist.init(timeout_s=120)
+    cfg = LlamaLiteConfig(vocab_size=512, hidden_dim=256, num_layers=2, num_heads=4, num_kv_heads=2, head_dim=64,
+                          intermediate_dim=512, max_seq_len=128)
+    model = LlamaLite(cfg, device="cuda", dtype=torch.bfloat16, seed=0)
+    dp = DataParallel(model, lr=1e-3, grad_dtype=torch.bfloat16, comm=comm_kind)
+    g = torch.Generator(device="cuda").manual_seed(7 + rank)
+    losses = []
+    for _ in range(3):
+        tok = torch.randint(0, 512, (2, 129), device="cuda", generator=g)
+        losses.append(float(dp.train_step(tok[:, :-1], tok[:, 1:])))
+    if hasattr(dp.comm, "check"):
+        dp.comm.check()
+    w = dp.flat.param_buf.detach().float().cpu().numpy()
+    same = True
+    if comm_kind == "nvlink":
+        dp.comm.close()
+    bdist.shutdown()
+    return w, losses, same
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_fused_ddp_step_matches_nccl_path():
+    env = {"NCCL_NVLS_ENABLE": "0"}
+    nv = [(torch.from_numpy(w), l, s) for w, l, s in run_ranks(_gpu_ddp, 2, "nvlink", env=env)]
+    nc = [(torch.from_numpy(w), l, s) for w, l, s in run_ranks(_gpu_ddp, 2, "nccl", env=env)]
+    assert torch.equal(nv[0][0], nv[1][0])  # replicas identical after the fused push
+    torch.testing.assert_close(nv[0][0], nc[0][0], rtol=0, atol=2e-2)
+    for a, b in zip(nv[0][1], nc[0][1]):
+        assert abs(a - b) < 2e-2
+
+
+def _gpu_timeout(rank, world):
+    from brain_b200.parallel import dist as bdist
+    from brain_b200.parallel.symm import NvlinkComm, PeerTimeout
+    bdist.init(timeout_s=60)
+    comm = NvlinkComm(timeout_s=1.0)
+    import torch.distributed as dist
+    result = "no error"
+    if rank == 0:
+        comm.barrier(42)  # rank 1 never launches its side
+        try:
+            comm.check()
+        except PeerTimeout as e:
+            result = "timeout: " + str(e)
+    dist.barrier()  # both ranks alive and idle before teardown
+    comm.close()
+    bdist.shutdown()
+    return result
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_device_barrier_gives_up_on_missing_peer():
+    outs = run_ranks(_gpu_timeout, 2, env={"NCCL_NVLS_ENABLE": "0"})
+    assert outs[0].startswith("timeout"), outs[0]
+    assert outs[1] == "no error"
