@@ -3,7 +3,7 @@
 // One CTA computes 128 query rows of one (batch, q-head) against all visible keys, 128 keys per
 // step. Roles (6 warps):
 //   warp 0      TMA producer: Q once, then K/V blocks (4-D tensor maps over [B, S, H, D] with the
-//               caller's strides, SWIZZLE_128B, no multicast) into a 2-4 stage ring.
+//               caller's strides, SWIZZLE_128B, CTA-local) into a 2-4 stage ring.
 //   warp 1      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S buffers (128 cols
 //               each, f32), then O += P_j V_j into the TMEM O accumulator once softmax has written
 //               P_j; V is consumed as an MN-major operand straight from its [keys, D] tile.

@@ -3,7 +3,7 @@
 // Symmetric memory: every rank cudaMalloc's a buffer of the same size, exports a CUDA IPC handle,
 // and opens its peers' handles (host code in parallel/symm.py exchanges the 64-byte handles through
 // torch.distributed). Kernels then read and write peers' memory with ordinary 16-byte ld/st over
-// NVLink / NVSwitch (P2P). No NVLS multicast object is created and no TMA is used here.
+// NVLink / NVSwitch (P2P). No NVLS object is created and no TMA is used here.
 //
 // Synchronisation: each rank owns a signal pad (int32 per peer) in symmetric memory. A barrier with
 // epoch e has rank r store e (st.release.sys) into pad_j[r] of every peer j and then spin (bounded by

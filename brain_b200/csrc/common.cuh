@@ -83,7 +83,7 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* f) {
 }
 
 // ---------------------------------------------------------------------------------------------
-// Shared-memory addressing, mbarriers and TMA (cp.async.bulk.tensor, no multicast anywhere).
+// Shared-memory addressing, mbarriers and TMA (cp.async.bulk.tensor into the issuing CTA only).
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

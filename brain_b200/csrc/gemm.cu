@@ -14,7 +14,7 @@
 //               epilogue of tile i overlaps the main loop of tile i+1. Warp 1 also owns TMEM alloc.
 //   warps 2..5  epilogue: tcgen05.ld 32x32b -> registers -> alpha/beta/bias/residual -> bf16/f32.
 // Every wait is bounded (globaltimer); a timeout records a status code and all roles drain and
-// return, releasing TMEM. No TMA load uses cluster multicast.
+// return, releasing TMEM. Every TMA load fills only the issuing CTA's own shared memory.
 //
 // Reference parity: brain-core `matmul` / `blas::gemm` (crates/brain-core/src/tensor/arithmetic.rs:174,
 // crates/brain-core/src/tensor/blas.rs:227) compute the same product in f64 on the CPU.

@@ -3,7 +3,7 @@
 ``SymmetricBuffer`` allocates the same number of bytes on every rank with ``cudaMalloc``
 (``csrc/comm.cu``), exchanges the 64-byte CUDA IPC handles with ``torch.distributed``, opens the
 peers' handles and keeps the table of peer device pointers. Kernels read and write peer memory
-directly over NVLink / NVSwitch. No NVLS multicast object is bound.
+directly over NVLink / NVSwitch with plain peer loads and stores (no NVLS objects).
 
 ``NvlinkComm`` implements the collectives of the data-parallel engine and of the public API with
 those kernels (barrier with epochs and a wall-clock budget, one-/two-shot all-reduce,
