@@ -8,8 +8,8 @@
 //   DQ:   a CTA owns 128 queries of one q head and streams 64-key blocks:
 //                      S = Q K^T, dP = dO V^T,  P = exp2(S * c - lse[row]),  dS = P (dP - delta[row])
 //                      dQ += dS K
-// Roles per CTA (6 warps): warp 0 TMA (4-D tensor maps over the caller's strides, SWIZZLE_128B, no
-// per-CTA destinations only), warp 1 single-thread MMA issuer, warps 2..5 elementwise (thread = TMEM lane = row),
+// Roles per CTA (6 warps): warp 0 TMA (4-D tensor maps over the caller's strides, SWIZZLE_128B,
+// CTA-local destinations), warp 1 single-thread MMA issuer, warps 2..5 elementwise (thread = TMEM lane = row),
 // which write P/dS as bf16 K-major tiles that the accumulate MMAs read from shared memory; the
 // streamed operand is read a second time as an MN-major B operand, so nothing is transposed.
 // Bounded waits report through the status word. Reference: the Value-graph attention VJPs
