@@ -146,11 +146,11 @@ def main():
 
     # ---------------------------------------------------------------- device-timed loop
     clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
-    bdist.barrier()
-    torch.cuda.synchronize()
     if clocks:
         clocks.start()
-        time.sleep(0.3)
+    time.sleep(0.3)  # every rank: let the sampler start, then align all ranks before timing
+    bdist.barrier()
+    torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with _native.launch_counter() as lc:
         start.record()

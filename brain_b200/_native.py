@@ -31,6 +31,7 @@ SIGNATURES: dict[str, tuple[str, str]] = {
     "brain_error_string": ("brain_kernels", "i"),
     "brain_gemm_bf16": ("brain_kernels", "pliplipliiiififpplis"),
     "brain_status_gemm": ("brain_kernels", "pi"),
+    "brain_gemm_set_pair_mode": ("brain_kernels", "i"),
 }
 
 _lock = threading.Lock()

@@ -65,6 +65,65 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   tn = r / gm;
 }
 
+// Epilogue for one row x 32 columns of f32 accumulator: alpha, bias, residual, beta * C_old, store.
+__device__ __forceinline__ void store_chunk(const GemmArgs& args, int gm, int gn0, const uint32_t* r) {
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
+  const bool full = gn0 + 32 <= args.N;
+  if (args.bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (full || gn0 + j < args.N) v[j] += __bfloat162float(args.bias[gn0 + j]);
+  }
+  if (args.R) {
+    const __nv_bfloat16* rp = args.R + (int64_t)gm * args.ldr + gn0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (full || gn0 + j < args.N) v[j] += __bfloat162float(rp[j]);
+  }
+  if (args.c_f32) {
+    float* cp = reinterpret_cast<float*>(args.C) + (int64_t)gm * args.ldc + gn0;
+    if (full && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+        if (args.accumulate) {
+          float4 old = *reinterpret_cast<const float4*>(cp + j);
+          o.x += args.beta * old.x; o.y += args.beta * old.y; o.z += args.beta * old.z; o.w += args.beta * old.w;
+        }
+        *reinterpret_cast<float4*>(cp + j) = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (gn0 + j < args.N) cp[j] = v[j] + (args.accumulate ? args.beta * cp[j] : 0.f);
+    }
+  } else {
+    __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(args.C) + (int64_t)gm * args.ldc + gn0;
+    if (full && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        if (args.accumulate) {
+          float old[8];
+          load8(cp + j, old);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[j + u] += args.beta * old[u];
+        }
+        store8(cp + j, v + j);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        if (gn0 + j < args.N) {
+          float o = v[j] + (args.accumulate ? args.beta * __bfloat162float(cp[j]) : 0.f);
+          cp[j] = __float2bfloat16_rn(o);
+        }
+      }
+    }
+  }
+}
+
 template <int BN, int STAGES, int A_MN, int B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -228,63 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld32(tmem_base + (uint32_t)(acc * BN + c * 32) + ((uint32_t)(q * 32) << 16), r);
         tc_wait_ld();
         const int gn0 = n0 + c * 32;
-        if (row_ok && gn0 < args.N) {
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
-        const bool full = gn0 + 32 <= args.N;
-        if (args.bias) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (full || gn0 + j < args.N) v[j] += __bfloat162float(args.bias[gn0 + j]);
-        }
-        if (args.R) {
-          const __nv_bfloat16* rp = args.R + (int64_t)gm * args.ldr + gn0;
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (full || gn0 + j < args.N) v[j] += __bfloat162float(rp[j]);
-        }
-        if (args.c_f32) {
-          float* cp = reinterpret_cast<float*>(args.C) + (int64_t)gm * args.ldc + gn0;
-          if (full && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-              if (args.accumulate) {
-                float4 old = *reinterpret_cast<const float4*>(cp + j);
-                o.x += args.beta * old.x; o.y += args.beta * old.y; o.z += args.beta * old.z; o.w += args.beta * old.w;
-              }
-              *reinterpret_cast<float4*>(cp + j) = o;
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (gn0 + j < args.N) cp[j] = v[j] + (args.accumulate ? args.beta * cp[j] : 0.f);
-          }
-        } else {
-          __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(args.C) + (int64_t)gm * args.ldc + gn0;
-          if (full && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              if (args.accumulate) {
-                float old[8];
-                load8(cp + j, old);
-#pragma unroll
-                for (int u = 0; u < 8; ++u) v[j + u] += args.beta * old[u];
-              }
-              store8(cp + j, v + j);
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (gn0 + j < args.N) {
-                float o = v[j] + (args.accumulate ? args.beta * __bfloat162float(cp[j]) : 0.f);
-                cp[j] = __float2bfloat16_rn(o);
-              }
-            }
-          }
-        }
-        }
+        if (row_ok && gn0 < args.N) store_chunk(args, gm, gn0, r);
         __syncwarp();
       }
       tc_fence_before();
@@ -297,6 +300,206 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// CTA-pair variant: a cluster of 2 CTAs computes one 256 x 256 tile with tcgen05.mma.cta_group::2
+// issued by CTA 0. Each CTA stages its own 128 rows of A and its own 128 columns of B (32 KB per
+// stage), so an SM reads 8 KB of operands per 256x256x16 pair instruction instead of 12 KB per
+// 128x256x16 single-CTA one; the tensor core, not shared-memory bandwidth, becomes the limit.
+// Both CTAs' TMA copies complete on CTA 0's stage barrier; CTA 0's commits arrive on the stage /
+// accumulator barriers of both CTAs (one commit per CTA address); each CTA's epilogue drains its
+// own 128 TMEM lanes and releases the accumulator on CTA 0's barrier.
+// ---------------------------------------------------------------------------------------------
+constexpr int kPairStages = 6;
+struct PairSmem {
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = 128 * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFFSET = kPairStages * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFFSET + (2 * kPairStages + 5) * 8 + 16 + 1024;
+};
+
+template <int A_MN, int B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    GemmArgs args) {
+  using S = PairSmem;
+  constexpr int ST = kPairStages;
+  constexpr int TN = 256;  // pair tile: 256 x 256
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar_base = sbase + S::BAR_OFFSET;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (ST + s); };
+  auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * ST + a); };
+  auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * ST + 2 + a); };
+  const uint32_t drain_bar = bar_base + 8u * (2 * ST + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::BAR_OFFSET + (2 * ST + 5) * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t cta = cluster_ctarank();
+  const bool leader = cta == 0;
+  const int pid = blockIdx.x / 2, npairs = gridDim.x / 2;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < ST; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 256);  // 128 epilogue threads of each CTA arrive on CTA 0's barrier
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // both CTAs' barriers are initialised before anyone signals a peer
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = (args.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs): own A rows and own B columns
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = pid; t < args.num_tiles && ok; t += npairs) {
+        int tm, tn;
+        tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+        const int m0 = tm * 256 + (int)cta * 128, n0 = tn * TN + (int)cta * 128;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % ST;
+          const uint32_t round = it / ST;
+          if (!mbar_wait(empty_bar(s), (round & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 40, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = sbase + s * S::STAGE_BYTES;
+          const uint32_t sb = sa + S::A_BYTES;
+          const uint32_t fb = mapa_shared(full_bar(s), 0);
+          if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * S::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (A_MN) {
+            tma_load_2d_pair(&tmA, sa, fb, m0, k0);
+            tma_load_2d_pair(&tmA, sa + 64 * BK * 2, fb, m0 + 64, k0);
+          } else {
+            tma_load_2d_pair(&tmA, sa, fb, k0, m0);
+          }
+          if (B_MN) {
+            tma_load_2d_pair(&tmB, sb, fb, n0, k0);
+            tma_load_2d_pair(&tmB, sb + 64 * BK * 2, fb, n0 + 64, k0);
+          } else {
+            tma_load_2d_pair(&tmB, sb, fb, k0, n0);
+          }
+        }
+      }
+      if (!ok && leader) {
+        uint32_t first = it > (uint32_t)ST ? it - ST : 0;
+        for (uint32_t j = first; j < it; ++j) {
+          uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(full_bar(j % ST), (j / ST) & 1) && globaltimer() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- MMA issuer (CTA 0 only)
+      constexpr uint32_t idesc = idesc_f16(256, TN, 1u, (uint32_t)A_MN, (uint32_t)B_MN);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true, issued = false;
+      for (int t = pid; t < args.num_tiles && ok; t += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_round = (uint32_t)(local >> 1);
+        if (!mbar_wait(tempty_bar(acc), (acc_round & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 50, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * TN);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % ST;
+          if (!mbar_wait(full_bar(s), (it / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 51, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = sbase + s * S::STAGE_BYTES;
+          const uint32_t sb = sa + S::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            uint64_t adesc = A_MN ? smem_desc_sw128(sa + kk * 2048, 64 * BK * 2, 1024)
+                                  : smem_desc_sw128(sa + kk * 32, 16, 1024);
+            uint64_t bdesc = B_MN ? smem_desc_sw128(sb + kk * 2048, 64 * BK * 2, 1024)
+                                  : smem_desc_sw128(sb + kk * 32, 16, 1024);
+            tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          issued = true;
+          tc_commit_pair(empty_bar(s));
+          tc_commit_pair(mapa_shared(empty_bar(s), 1));
+        }
+        if (!ok) break;
+        tc_commit_pair(tfull_bar(acc));
+        tc_commit_pair(mapa_shared(tfull_bar(acc), 1));
+      }
+      if (!ok && issued) {
+        tc_commit_pair(drain_bar);
+        uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(drain_bar, 0) && globaltimer() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5 of both CTAs)
+    const int q = warp & 3;
+    const int row_in_tile = (int)cta * 128 + q * 32 + lane;
+    int local = 0;
+    for (int t = pid; t < args.num_tiles; t += npairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_round = (uint32_t)(local >> 1);
+      if (!mbar_wait(tfull_bar(acc), acc_round & 1, BRAIN_ERR_TIMEOUT_ACC, 60, abort_flag)) break;
+      tc_fence_after();
+      int tm, tn;
+      tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+      const int gm = tm * 256 + row_in_tile;
+      const int n0 = tn * TN;
+      const bool row_ok = gm < args.M;
+#pragma unroll 1
+      for (int c = 0; c < TN / 32; ++c) {
+        uint32_t r[32];
+        __syncwarp();
+        tmem_ld32(tmem_base + (uint32_t)(acc * TN + c * 32) + ((uint32_t)(q * 32) << 16), r);
+        tc_wait_ld();
+        const int gn0 = n0 + c * 32;
+        if (row_ok && gn0 < args.N) store_chunk(args, gm, gn0, r);
+        __syncwarp();
+      }
+      tc_fence_before();
+      mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its pair partner may still signal its barriers
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
   }
 }
 
@@ -361,6 +564,21 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, c
   return (int)cudaGetLastError();
 }
 
+template <int A_MN, int B_MN>
+int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+  auto kern = gemm_tc2_kernel<A_MN, B_MN>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PairSmem::TOTAL);
+    attr_set[dev & 63] = true;
+  }
+  int pairs = std::min(a.num_tiles, brain_host::num_sms() / 2);
+  kern<<<2 * pairs, kThreads, PairSmem::TOTAL, st>>>(ta, tb, a);
+  return (int)cudaGetLastError();
+}
+
 // Simple SIMT fallback for shapes the TMA path cannot describe (unaligned strides). f32 accumulate.
 __global__ void gemm_simt_kernel(const __nv_bfloat16* A, int64_t lda, int a_mn, const __nv_bfloat16* B,
                                  int64_t ldb, int b_mn, GemmArgs args) {
@@ -411,6 +629,17 @@ __global__ void gemm_simt_kernel(const __nv_bfloat16* A, int64_t lda, int a_mn, 
 
 BRAIN_STATUS_READER(gemm)
 
+namespace {
+int g_pair_mode = 1;  // 1: CTA-pair kernel for M, N >= 256; 0: single-CTA kernel only
+}
+
+// Select the GEMM kernel family (tests exercise both); returns the previous mode.
+BRAIN_API int brain_gemm_set_pair_mode(int mode) {
+  const int old = g_pair_mode;
+  g_pair_mode = mode;
+  return old;
+}
+
 // C = alpha * op(A) op(B) (+ beta*C if accumulate) (+ bias) (+ R).
 //   a_mn = 0: A is [M,K] with row stride lda; a_mn = 1: A is [K,M] with row stride lda.
 //   b_mn = 0: B is [N,K] with row stride ldb; b_mn = 1: B is [K,N] with row stride ldb.
@@ -437,6 +666,26 @@ BRAIN_API int brain_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
     gemm_simt_kernel<<<grid, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16*>(A), lda, a_mn,
                                               reinterpret_cast<const __nv_bfloat16*>(B), ldb, b_mn, a);
     return (int)cudaGetLastError();
+  }
+  if (g_pair_mode && M >= 256 && N >= 256) {
+    // CTA-pair kernel: 256 x 256 tiles, each CTA stages 128 rows of A and 128 columns of B
+    a.tiles_m = (M + 255) / 256;
+    a.tiles_n = (N + 255) / 256;
+    a.num_tiles = a.tiles_m * a.tiles_n;
+    CUtensorMap ta, tb;
+    bool ok = a_mn ? get_map_2d(&ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, BK,
+                                CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2)
+                   : get_map_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, 128,
+                                CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+    ok = ok && (b_mn ? get_map_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK,
+                                  CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2)
+                     : get_map_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, 128,
+                                  CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2));
+    if (!ok) return (int)cudaErrorInvalidValue;
+    if (a_mn == 0 && b_mn == 0) return launch_tc2<0, 0>(ta, tb, a, stream);
+    if (a_mn == 0 && b_mn == 1) return launch_tc2<0, 1>(ta, tb, a, stream);
+    if (a_mn == 1 && b_mn == 0) return launch_tc2<1, 0>(ta, tb, a, stream);
+    return launch_tc2<1, 1>(ta, tb, a, stream);
   }
   const int BN = (N <= 128) ? 128 : 256;
   a.tiles_m = (M + BM - 1) / BM;

@@ -82,6 +82,12 @@ def gemm(
     return out
 
 
+def set_pair_mode(mode: int) -> int:
+    """1: use the CTA-pair (cta_group::2, 256x256 tile) kernel for M, N >= 256; 0: single-CTA
+    kernel only. Returns the previous mode."""
+    return int(_native.fn("brain_gemm_set_pair_mode")(int(mode)))
+
+
 def _gemm_cpu(a, b, ta, tb, out, alpha, beta, bias, residual):
     A = a.float().t() if ta else a.float()
     B = b.float().t() if tb else b.float()

@@ -69,3 +69,28 @@ def test_gemm_simt_fallback_matches():
     b = _mk((K, N), "cuda", 8)
     c = gemm(a, b, out_dtype=torch.float32, force_simt=True)
     torch.testing.assert_close(c, _ref(a, b, False, False), rtol=2e-3, atol=2e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("pair", [0, 1])
+@pytest.mark.parametrize("ta", [False, True])
+@pytest.mark.parametrize("tb", [False, True])
+@pytest.mark.parametrize("shape", [(256, 256, 64), (512, 768, 320), (300, 520, 136), (2048, 1024, 1024)])
+def test_gemm_pair_and_single_cta(pair, ta, tb, shape):
+    from brain_b200.ops.gemm import set_pair_mode
+    M, N, K = shape
+    a = _mk((K, M) if ta else (M, K), "cuda", 11)
+    b = _mk((N, K) if tb else (K, N), "cuda", 12)
+    old = set_pair_mode(pair)
+    try:
+        c = gemm(a, b, ta, tb, out_dtype=torch.float32)
+        acc = torch.ones(M, N, device="cuda")
+        gemm(a, b, ta, tb, out=acc, beta=1.0)
+        torch.cuda.synchronize()
+    finally:
+        set_pair_mode(old)
+    ref = _ref(a, b, ta, tb)
+    torch.testing.assert_close(c, ref, rtol=2e-3, atol=2e-3 * K ** 0.5)
+    torch.testing.assert_close(acc, ref + 1, rtol=2e-3, atol=2e-3 * K ** 0.5)
+    from brain_b200 import _native
+    assert _native.status("gemm")[0] == 0
