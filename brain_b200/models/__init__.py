@@ -3,3 +3,5 @@ from .config import LlamaLiteConfig, GptLiteConfig, BertLiteConfig, T5LiteConfig
 from .llama import LlamaLite, LlamaBlock  # noqa: F401
 from .kv_cache import KvCache, KvCacheConfig, PagedKvCache  # noqa: F401
 from .generate import GenerationConfig, sample_next_token  # noqa: F401
+from .families import GptLite, BertLite, T5Lite, ViT  # noqa: F401
+from .blocks import TransformerBlock, TransformerStack  # noqa: F401

@@ -196,9 +196,11 @@ class QuickGELU(Module):
 class FeedForward(Module):
     """Transformer FFN: gated (SwiGLU over a fused gate/up weight) or plain (GELU)."""
 
-    def __init__(self, dim: int, hidden: int, gated: bool = True, bias: bool = False, device=None, dtype=None):
+    def __init__(self, dim: int, hidden: int, gated: bool = True, bias: bool = False, device=None, dtype=None,
+                 act: str = "gelu"):
         super().__init__()
         self.gated = gated
+        self.act = act
         if gated:
             self.gate_up = Linear(dim, 2 * hidden, bias=bias, device=device, dtype=dtype)
         else:
@@ -210,7 +212,9 @@ class FeedForward(Module):
             if self.down.bias is None:
                 return ops.swiglu_linear(self.gate_up(x), self.down.weight, residual)
             return self.down(ops.swiglu(self.gate_up(x)), residual)
-        return self.down(ops.gelu(self.up(x)), residual)
+        h = self.up(x)
+        h = torch.relu(h) if self.act == "relu" else ops.gelu(h)
+        return self.down(h, residual)
 
 
 class MultiheadAttention(Module):
