@@ -13,6 +13,7 @@
 //   LayerNorm y = (x - mean) / sqrt(var + eps) * w + b, biased variance
 //                                                      crates/brain-transformer/src/ops.rs:57-101
 #include "common.cuh"
+#include "no_alloc.h"
 
 using namespace brain;
 
@@ -249,6 +250,83 @@ BRAIN_API int brain_norm_bwd(int kind, const void* dy, int64_t lddy, const void*
   const int P = brain_norm_bwd_partials(M);
   float* dwp = workspace;
   float* dbp = workspace + (int64_t)P * D;
+  auto DY = reinterpret_cast<const __nv_bfloat16*>(dy);
+  auto X = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto W = reinterpret_cast<const __nv_bfloat16*>(w);
+  auto DX = reinterpret_cast<__nv_bfloat16*>(dx);
+  auto DR = reinterpret_cast<const __nv_bfloat16*>(dres);
+  if (kind == 0)
+    norm_bwd_kernel<false><<<P, T, 0, st>>>(DY, lddy, X, ldx, W, mean_in, rstd_in, DX, lddx, DR, lddres, dwp, nullptr, M, D);
+  else
+    norm_bwd_kernel<true><<<P, T, 0, st>>>(DY, lddy, X, ldx, W, mean_in, rstd_in, DX, lddx, DR, lddres, dwp, dbp, M, D);
+  colsum_kernel<<<(D + 255) / 256, 256, 0, st>>>(dwp, P, D, dw, dw_f32, accumulate);
+  if (kind == 1 && db) colsum_kernel<<<(D + 255) / 256, 256, 0, st>>>(dbp, P, D, db, dw_f32, accumulate);
+  return (int)cudaGetLastError();
+}
+
+// =============================================================================================
+// No-allocation variant of the normalisation backward (no counterpart in the reference; declared
+// in no_alloc.h). brain_norm_bwd above takes its f32 partial-sum workspace from the caller, which
+// usually means an allocation per call. Callers that must not allocate device memory while they
+// run - a C or C++ host that links this library without PyTorch or any allocator, or a serving
+// process that reserved the whole GPU up front under a fixed memory budget - use
+// brain_norm_bwd_noalloc instead: its partial sums live in the fixed array below.
+//
+// Limits: the array holds 2 x 64 x 8192 floats (4 MiB, held on every GPU that loads the library
+// until the process exits), so D must be <= 8192; larger D is rejected with BRAIN_NOALLOC_TOO_LARGE.
+// At most 64 partial rows are used (fewer when M < 64); every partial the column sums read is
+// written first by the same call, so nothing has to be cleared between calls.
+// Every call shares the array: two calls that overlap on the GPU (different streams, or another
+// host thread) race on it and must be serialised by the caller.
+// Set-up: the first call on each device resolves the array's device address with
+// cudaGetSymbolAddress while that device is current; make that first call before any stream
+// capture. Nothing here calls cudaMalloc, cudaFree or an allocating library routine.
+// =============================================================================================
+namespace {
+
+constexpr int kNoAllocPartials = 64;
+constexpr int kNoAllocMaxD = 8192;
+static __device__ __align__(256) float g_norm_bwd_scratch[2 * kNoAllocPartials * kNoAllocMaxD];
+
+float* noalloc_scratch_ptr(int* err) {
+  static float* ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = (e != cudaSuccess) ? (int)e : (int)cudaErrorInvalidDevice;
+    return nullptr;
+  }
+  if (!ptrs[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_norm_bwd_scratch);  // host-side stand-in -> device address
+    if (e != cudaSuccess) {
+      *err = (int)e;
+      return nullptr;
+    }
+    ptrs[dev] = static_cast<float*>(p);
+  }
+  *err = 0;
+  return ptrs[dev];
+}
+
+}  // namespace
+
+// Same arguments as brain_norm_bwd without the workspace (see no_alloc.h). Returns 0, a cudaError_t,
+// or BRAIN_NOALLOC_TOO_LARGE when D exceeds the fixed scratch (D > 8192).
+BRAIN_API int brain_norm_bwd_noalloc(int kind, const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
+                                     const float* mean_in, const float* rstd_in, void* dx, int64_t lddx,
+                                     const void* dres, int64_t lddres, void* dw, void* db, int dw_f32, int accumulate,
+                                     int M, int D, cudaStream_t st) {
+  if (M == 0) return 0;
+  if (D > kNoAllocMaxD) return -2;  // BRAIN_NOALLOC_TOO_LARGE
+  if (D % 8 != 0) return (int)cudaErrorInvalidValue;
+  int err = 0;
+  float* scratch = noalloc_scratch_ptr(&err);
+  if (!scratch) return err;
+  const int T = threads_for(D);
+  const int P = M < kNoAllocPartials ? M : kNoAllocPartials;
+  float* dwp = scratch;
+  float* dbp = scratch + (int64_t)P * D;
   auto DY = reinterpret_cast<const __nv_bfloat16*>(dy);
   auto X = reinterpret_cast<const __nv_bfloat16*>(x);
   auto W = reinterpret_cast<const __nv_bfloat16*>(w);
