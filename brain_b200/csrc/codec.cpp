@@ -164,3 +164,56 @@ BRAIN_API int64_t brain_parse_f64(const char* s, int64_t len, double* out, int64
   }
   return count;
 }
+
+// ---------------------------------------------------------------------------------------------
+// Reference RNG streams for oracle parity with the CPU framework (crates/brain-core/src/random.rs):
+// SplitMix64 (random.rs:118-124), BrainRng = xorshift128+ seeded by SplitMix64(seed + 1)
+// (random.rs:194-234), next_f64 = (u64 >> 11) * 2^-53, and Tensor::randn's Box-Muller cosine branch
+// with u1 = max(1 - next_f64, 1e-15) (crates/brain-core/src/tensor/impl.rs:222-236).
+// The state (two u64) is updated in place so streams continue across calls.
+// ---------------------------------------------------------------------------------------------
+namespace {
+inline uint64_t splitmix_next(uint64_t& s) {
+  s += 0x9E3779B97F4A7C15ull;
+  uint64_t z = s;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+inline uint64_t xorshift_next(uint64_t* st) {
+  uint64_t s1 = st[0];
+  const uint64_t s0 = st[1];
+  const uint64_t result = s0 + s1;
+  st[0] = s0;
+  s1 ^= s1 << 23;
+  st[1] = s1 ^ s0 ^ (s1 >> 17) ^ (s0 >> 26);
+  return result;
+}
+inline double next_f64(uint64_t* st) { return (double)(xorshift_next(st) >> 11) * (1.0 / 9007199254740992.0); }
+}  // namespace
+
+BRAIN_API void brain_rng_seed(uint64_t seed, uint64_t* state_out) {
+  uint64_t sm = seed + 1;
+  state_out[0] = splitmix_next(sm);
+  state_out[1] = splitmix_next(sm);
+  if (state_out[0] == 0 && state_out[1] == 0) {
+    state_out[0] = 0xDEADBEEFCAFEBABEull;
+    state_out[1] = 0x123456789ABCDEF0ull;
+  }
+}
+
+// mode 0: uniform [0,1) doubles; 1: standard normal (Box-Muller cosine branch); 2: raw u64 as doubles
+BRAIN_API void brain_rng_fill(uint64_t* state, int64_t n, double* out, int mode) {
+  for (int64_t i = 0; i < n; ++i) {
+    if (mode == 0) {
+      out[i] = next_f64(state);
+    } else if (mode == 1) {
+      double u1 = 1.0 - next_f64(state);
+      if (u1 < 1e-15) u1 = 1e-15;
+      const double u2 = next_f64(state);
+      out[i] = std::sqrt(-2.0 * std::log(u1)) * std::cos(2.0 * 3.14159265358979323846 * u2);
+    } else {
+      out[i] = (double)xorshift_next(state);
+    }
+  }
+}

@@ -1,0 +1,284 @@
+// Block-scaled FP8 (E4M3) GEMM on tcgen05 and the activation quantiser, sm_100a.
+//
+//   C[M,N] (bf16) = sum_kb  (Aq[M, kb] . Bq[N, kb]^T) * sa[m, kb] * sb[n / 128, kb]
+// with 1 x 128 activation scales sa [M, K/128] and 128 x 128 weight-block scales sb [N/128, K/128]
+// (f32). These are general f32 scales, not power-of-two MX scales, so the scaling cannot ride on the
+// tensor core's block-scale path: each 128-wide K block is accumulated by tcgen05.mma kind::f8f6f4
+// into one of two TMEM partial buffers, and the epilogue warps promote it in registers
+// (acc += partial * sa * sb) while the tensor core already computes the next block into the other
+// buffer. Roles (6 warps, persistent): warp 0 TMA (SWIZZLE_128B, 128 B = 128 fp8 per row), warp 1
+// single-thread MMA issuer, warps 2..5 promotion + bf16 epilogue (thread = output row). Waits are
+// bounded and report through the status word.
+//
+// Reference: the FP8E4M3 / FP8E5M2 dtypes are declared without arithmetic
+// (crates/brain-quantization/src/core.rs:19-31); group-wise scaling mirrors BlockQuantizer
+// (block_quant.rs:30-70) with blocks of 128.
+#include "common.cuh"
+
+using namespace brain;
+
+namespace {
+
+constexpr int kThreads = 192;
+constexpr int TM = 128, TN = 128, TK = 128;  // tile and scale-block sizes
+constexpr int STAGES = 4;
+constexpr int OP_BYTES = TM * TK;  // 16 KB of fp8 per operand per stage
+
+struct Fp8Args {
+  int M, N, K;
+  int tiles_m, tiles_n, num_tiles;
+  const float* sa;  // [M, K/128]
+  const float* sb;  // [ceil(N/128), K/128]
+  int ksb;          // K / 128 (scale columns)
+  __nv_bfloat16* C;
+  int64_t ldc;
+  const __nv_bfloat16* R;  // optional residual [M, N]
+  int64_t ldr;
+};
+
+__device__ __forceinline__ void fp8_tile(int t, int tiles_m, int& tm, int& tn) {
+  // column-major over tiles_m so consecutive CTAs share the B (weight) tile in L2
+  tm = t % tiles_m;
+  tn = t / tiles_m;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    fp8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Fp8Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + STAGES * 2 * OP_BYTES;
+  auto full = [&](int s) { return bars + 8u * s; };
+  auto empty = [&](int s) { return bars + 8u * (STAGES + s); };
+  auto pfull = [&](int b) { return bars + 8u * (2 * STAGES + b); };
+  auto pempty = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
+  const uint32_t drain = bars + 8u * (2 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * 2 * OP_BYTES + (2 * STAGES + 5) * 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(pfull(b), 1);
+      mbar_init(pempty(b), 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;  // partial buffer b at columns [b*128, b*128 + 128)
+  const int nkb = (a.K + TK - 1) / TK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        fp8_tile(t, a.tiles_m, tm, tn);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const int s = it % STAGES;
+          if (!mbar_wait(empty(s), ((it / STAGES) & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 310, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa_ = sbase + s * 2 * OP_BYTES;
+          mbar_arrive_expect_tx(full(s), 2 * OP_BYTES);
+          tma_load_2d(&tmA, sa_, full(s), kb * TK, tm * TM);
+          tma_load_2d(&tmB, sa_ + OP_BYTES, full(s), kb * TK, tn * TN);
+        }
+      }
+      if (!ok) {
+        for (uint32_t j = it > (uint32_t)STAGES ? it - STAGES : 0; j < it; ++j) {
+          uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(full(j % STAGES), (j / STAGES) & 1) && globaltimer() - t0 < 100000000ull) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f8(TM, TN, 0u, 0u, 0u, 0u);
+      uint32_t it = 0, pb = 0;  // pb: global K-block counter (partial buffer = pb & 1)
+      bool ok = true, issued = false;
+      for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x) {
+        for (int kb = 0; kb < nkb; ++kb, ++it, ++pb) {
+          const int s = it % STAGES;
+          const int b = pb & 1;
+          if (!mbar_wait(pempty(b), ((pb >> 1) & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 320, abort_flag) ||
+              !mbar_wait(full(s), (it / STAGES) & 1, BRAIN_ERR_TIMEOUT_FULL, 321, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa_ = sbase + s * 2 * OP_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < TK / 32; ++kk)  // K = 32 fp8 per instruction = 32 bytes
+            tc_mma_f8(tmem + (uint32_t)(b * 128), smem_desc_sw128(sa_ + kk * 32, 16, 1024),
+                      smem_desc_sw128(sa_ + OP_BYTES + kk * 32, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+          issued = true;
+          tc_commit(empty(s));
+          tc_commit(pfull(b));
+        }
+      }
+      if (!ok && issued) {
+        tc_commit(drain);
+        uint64_t t0 = globaltimer();
+        while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < 100000000ull) {
+        }
+      }
+    }
+  } else {
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    uint32_t pb = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x) {
+      int tm, tn;
+      fp8_tile(t, a.tiles_m, tm, tn);
+      const int gm = tm * TM + r;
+      const bool row_ok = gm < a.M;
+      float acc[TN];
+#pragma unroll
+      for (int j = 0; j < TN; ++j) acc[j] = 0.f;
+      for (int kb = 0; kb < nkb; ++kb, ++pb) {
+        const int b = pb & 1;
+        const float scale = (row_ok ? a.sa[(int64_t)gm * a.ksb + kb] : 0.f) * a.sb[(int64_t)tn * a.ksb + kb];
+        if (!mbar_wait(pfull(b), (pb >> 1) & 1, BRAIN_ERR_TIMEOUT_ACC, 330, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < TN / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem + (uint32_t)(b * 128 + c * 32) + lane_addr, v);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c * 32 + j] += scale * __uint_as_float(v[j]);
+        }
+        tc_fence_before();
+        mbar_arrive(pempty(b));
+      }
+      if (!ok) break;
+      if (row_ok) {
+        const int n0 = tn * TN;
+        __nv_bfloat16* crow = a.C + (int64_t)gm * a.ldc;
+        if (n0 + TN <= a.N) {
+          if (a.R) {
+            const __nv_bfloat16* rrow = a.R + (int64_t)gm * a.ldr + n0;
+#pragma unroll
+            for (int j = 0; j < TN; j += 8) {
+              float rv[8];
+              load8(rrow + j, rv);
+#pragma unroll
+              for (int u = 0; u < 8; ++u) acc[j + u] += rv[u];
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < TN; j += 8) store8(crow + n0 + j, acc + j);
+        } else {
+#pragma unroll
+          for (int j = 0; j < TN; ++j)
+            if (n0 + j < a.N)
+              crow[n0 + j] = __float2bfloat16_rn(acc[j] + (a.R ? __bfloat162float(a.R[(int64_t)gm * a.ldr + n0 + j]) : 0.f));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// Row-wise 1 x 128 quantiser: q = e4m3(x / s), s = amax(|x| over 128) / 448 (one warp per block of 128).
+__global__ void quant_fp8_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, __nv_fp8_e4m3* __restrict__ q,
+                                      int64_t ldq, float* __restrict__ s, int M, int K) {
+  const int kblocks = K / 128;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (wid >= (int64_t)M * kblocks) return;
+  const int m = (int)(wid / kblocks), kb = (int)(wid % kblocks);
+  const __nv_bfloat16* p = x + (int64_t)m * ldx + kb * 128 + lane * 4;
+  float v[4];
+  __nv_bfloat162 h0 = *reinterpret_cast<const __nv_bfloat162*>(p);
+  __nv_bfloat162 h1 = *reinterpret_cast<const __nv_bfloat162*>(p + 2);
+  v[0] = __low2float(h0); v[1] = __high2float(h0); v[2] = __low2float(h1); v[3] = __high2float(h1);
+  float amax = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+  amax = warp_max(amax);
+  const float scale = amax > 0.f ? amax / 448.f : 1.f;
+  const float inv = 1.f / scale;
+  __nv_fp8_e4m3* qp = q + (int64_t)m * ldq + kb * 128 + lane * 4;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) qp[i] = __nv_fp8_e4m3(v[i] * inv);
+  if (lane == 0) s[(int64_t)m * kblocks + kb] = scale;
+}
+
+bool map_fp8(CUtensorMap* m, const void* base, int64_t inner, int64_t outer, int64_t ld) {
+  uint64_t dims[2] = {(uint64_t)inner, (uint64_t)outer};
+  uint64_t strides[1] = {(uint64_t)ld};
+  uint32_t box[2] = {128, 128};
+  return brain_host::encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace
+
+BRAIN_STATUS_READER(fp8)
+
+// Aq [M, K] e4m3 (row stride lda bytes), Bq [N, K] e4m3 (ldb), sa [M, K/128], sb [ceil(N/128), K/128],
+// C [M, N] bf16 (ldc elements), R optional residual. K must be a multiple of 128, lda/ldb of 16.
+BRAIN_API int brain_fp8_gemm(const void* A, int64_t lda, const void* B, int64_t ldb, const float* sa, const float* sb,
+                             void* C, int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, cudaStream_t st) {
+  if (M <= 0 || N <= 0) return 0;
+  if (K % 128 || lda % 16 || ldb % 16 || ((uintptr_t)A & 15) || ((uintptr_t)B & 15)) return (int)cudaErrorInvalidValue;
+  CUtensorMap ta, tb;
+  if (!map_fp8(&ta, A, K, M, lda) || !map_fp8(&tb, B, K, N, ldb)) return (int)cudaErrorInvalidValue;
+  Fp8Args a;
+  a.M = M; a.N = N; a.K = K;
+  a.tiles_m = (M + TM - 1) / TM;
+  a.tiles_n = (N + TN - 1) / TN;
+  a.num_tiles = a.tiles_m * a.tiles_n;
+  a.sa = sa; a.sb = sb; a.ksb = K / 128;
+  a.C = reinterpret_cast<__nv_bfloat16*>(C);
+  a.ldc = ldc;
+  a.R = reinterpret_cast<const __nv_bfloat16*>(R);
+  a.ldr = ldr;
+  const int smem = STAGES * 2 * OP_BYTES + (2 * STAGES + 5) * 8 + 16 + 1024;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr[dev & 63] = true;
+  }
+  const int grid = std::min(a.num_tiles, brain_host::num_sms());
+  fp8_gemm_kernel<<<grid, kThreads, smem, st>>>(ta, tb, a);
+  return (int)cudaGetLastError();
+}
+
+// x [M, K] bf16 -> q [M, K] e4m3, s [M, K/128] (K % 128 == 0).
+BRAIN_API int brain_fp8_quant_rows(const void* x, int64_t ldx, void* q, int64_t ldq, float* s, int M, int K,
+                                   cudaStream_t st) {
+  if (K % 128) return (int)cudaErrorInvalidValue;
+  const int64_t warps = (int64_t)M * (K / 128);
+  if (warps == 0) return 0;
+  quant_fp8_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x), ldx, reinterpret_cast<__nv_fp8_e4m3*>(q), ldq, s, M, K);
+  return (int)cudaGetLastError();
+}
