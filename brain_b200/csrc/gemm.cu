@@ -43,6 +43,22 @@ struct GemmArgs {
   const __nv_bfloat16* bias;
   const __nv_bfloat16* R;
   int64_t ldr;
+  // Output push over NVLink (tensor-parallel GEMM -> reduce-scatter / all-reduce): row gm goes to
+  // slot `push_rank` of the receive buffer of rank gm / push_chunk_rows (mode 1) or of every rank
+  // (mode 2), at row gm % push_chunk_rows (mode 1) or gm (mode 2). bf16 output only.
+  int push;
+  int push_world, push_rank;
+  int push_chunk_rows;
+  int64_t push_slot_elems;
+  __nv_bfloat16* push_dst[8];
+  // All-gathered A operand (AG -> GEMM): rows [j * ag_chunk_rows, (j+1) * ag_chunk_rows) of A live
+  // on rank j and are loaded by TMA straight from its memory (tensor map j); 0 = off.
+  int ag_chunk_rows;
+};
+
+// One A tensor map per rank for the all-gathered operand (kernel parameter space, 64-B aligned).
+struct alignas(64) PeerMaps {
+  CUtensorMap m[8];
 };
 
 template <int BN, int STAGES>
@@ -65,8 +81,30 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   tn = r / gm;
 }
 
-// Epilogue for one row x 32 columns of f32 accumulator: alpha, bias, residual, beta * C_old, store.
+__device__ __forceinline__ void store_chunk_at(const GemmArgs& args, int gm, int gn0, const uint32_t* r, void* cbase,
+                                               int64_t crow);
+
+// Epilogue for one row x 32 columns of f32 accumulator: alpha, bias, residual, beta * C_old, store
+// (or push to the owning ranks' receive buffers).
 __device__ __forceinline__ void store_chunk(const GemmArgs& args, int gm, int gn0, const uint32_t* r) {
+  if (!args.push) {
+    store_chunk_at(args, gm, gn0, r, args.C, gm);
+    return;
+  }
+  if (args.push == 1) {
+    const int j = gm / args.push_chunk_rows;
+    store_chunk_at(args, gm, gn0, r, args.push_dst[j] + (int64_t)args.push_rank * args.push_slot_elems,
+                   gm - (int64_t)j * args.push_chunk_rows);
+  } else {
+    for (int j = 0; j < args.push_world; ++j) {
+      const int dst = (args.push_rank + 1 + j) % args.push_world;  // stagger the peers
+      store_chunk_at(args, gm, gn0, r, args.push_dst[dst] + (int64_t)args.push_rank * args.push_slot_elems, gm);
+    }
+  }
+}
+
+__device__ __forceinline__ void store_chunk_at(const GemmArgs& args, int gm, int gn0, const uint32_t* r, void* cbase,
+                                               int64_t crow) {
   float v[32];
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
@@ -83,7 +121,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& args, int gm, int gn
       if (full || gn0 + j < args.N) v[j] += __bfloat162float(rp[j]);
   }
   if (args.c_f32) {
-    float* cp = reinterpret_cast<float*>(args.C) + (int64_t)gm * args.ldc + gn0;
+    float* cp = reinterpret_cast<float*>(cbase) + crow * args.ldc + gn0;
     if (full && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
 #pragma unroll
       for (int j = 0; j < 32; j += 4) {
@@ -100,7 +138,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& args, int gm, int gn
         if (gn0 + j < args.N) cp[j] = v[j] + (args.accumulate ? args.beta * cp[j] : 0.f);
     }
   } else {
-    __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(args.C) + (int64_t)gm * args.ldc + gn0;
+    __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(cbase) + crow * args.ldc + gn0;
     if (full && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
 #pragma unroll
       for (int j = 0; j < 32; j += 8) {
@@ -124,10 +162,10 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& args, int gm, int gn
   }
 }
 
-template <int BN, int STAGES, int A_MN, int B_MN>
+template <int BN, int STAGES, int A_MN, int B_MN, int AG>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   GemmArgs args) {
+                   GemmArgs args, const __grid_constant__ PeerMaps pm) {
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -194,6 +232,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (A_MN) {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j) tma_load_2d(&tmA, sa + j * (64 * BK * 2), full_bar(s), m0 + 64 * j, k0);
+          } else if (AG) {
+            // rows of this tile live on rank `owner`: TMA reads its memory over NVLink (no multicast)
+            const int owner = m0 / args.ag_chunk_rows;
+            tma_load_2d(&pm.m[owner], sa, full_bar(s), k0, m0 - owner * args.ag_chunk_rows);
           } else {
             tma_load_2d(&tmA, sa, full_bar(s), k0, m0);
           }
@@ -290,6 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (row_ok && gn0 < args.N) store_chunk(args, gm, gn0, r);
         __syncwarp();
       }
+      if (args.push) __threadfence_system();  // pushed rows visible to peers before the next barrier
       tc_fence_before();
       mbar_arrive(tempty_bar(acc));
     }
@@ -489,6 +532,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (row_ok && gn0 < args.N) store_chunk(args, gm, gn0, r);
         __syncwarp();
       }
+      if (args.push) __threadfence_system();
       tc_fence_before();
       mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
     }
@@ -548,10 +592,11 @@ bool get_map_2d(CUtensorMap* out, const void* ptr, uint64_t inner, uint64_t oute
   return true;
 }
 
-template <int BN, int STAGES, int A_MN, int B_MN>
-int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+template <int BN, int STAGES, int A_MN, int B_MN, int AG = 0>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st,
+              const PeerMaps* pm = nullptr) {
   using S = Smem<BN, STAGES>;
-  auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN>;
+  auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, AG>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -559,8 +604,9 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, c
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
     attr_set[dev & 63] = true;
   }
+  static PeerMaps empty_maps;  // unused unless AG
   int grid = std::min(a.num_tiles, brain_host::num_sms());
-  kern<<<grid, kThreads, S::TOTAL, st>>>(ta, tb, a);
+  kern<<<grid, kThreads, S::TOTAL, st>>>(ta, tb, a, pm ? *pm : empty_maps);
   return (int)cudaGetLastError();
 }
 
@@ -648,7 +694,7 @@ BRAIN_API int brain_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
                               int64_t ldc, int c_f32, int M, int N, int K, float alpha, int accumulate, float beta,
                               const void* bias, const void* R, int64_t ldr, int force_simt, cudaStream_t stream) {
   if (M <= 0 || N <= 0) return 0;
-  GemmArgs a;
+  GemmArgs a{};
   a.M = M; a.N = N; a.K = K;
   a.C = C; a.ldc = ldc; a.c_f32 = c_f32; a.accumulate = accumulate;
   a.alpha = alpha; a.beta = beta;
@@ -711,4 +757,76 @@ BRAIN_API int brain_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
     BRAIN_GEMM_CASE(256, 4)
   }
 #undef BRAIN_GEMM_CASE
+}
+
+// Tensor-parallel GEMM with fused communication, C = op(A) B^T style (A [M, K] K-major, B [N, K]):
+//   a_world > 1 : all-gathered A. Rows [j * a_chunk_rows, (j+1) * a_chunk_rows) are read by TMA from
+//                 a_peers[j] (row stride lda) - the AG -> GEMM fusion; a_chunk_rows % 128 == 0.
+//   push_mode 1 : row gm of C goes to slot push_rank of rank (gm / push_chunk_rows)'s receive buffer
+//                 push_peers[j] (slot stride push_slot_elems, row gm % push_chunk_rows, stride ldc):
+//                 GEMM -> reduce-scatter fusion. push_mode 2: every rank receives every row (-> all-reduce).
+//   push_mode 0 : C written locally.
+// The receive side then reduces its slots after a peer barrier (parallel/tensor_parallel.py).
+BRAIN_API int brain_gemm_bf16_tp(const int64_t* a_peers, int a_world, int a_chunk_rows, const void* A, int64_t lda,
+                                 const void* B, int64_t ldb, int b_mn, void* C, int64_t ldc, const int64_t* push_peers,
+                                 int push_mode, int push_rank, int push_world, int push_chunk_rows,
+                                 int64_t push_slot_elems, const void* R, int64_t ldr, int M, int N, int K,
+                                 cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return 0;
+  if (a_world > 8 || push_world > 8) return (int)cudaErrorInvalidValue;
+  if ((lda % 8) || (ldb % 8) || K < 16) return (int)cudaErrorInvalidValue;
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K;
+  a.C = C; a.ldc = ldc; a.c_f32 = 0; a.accumulate = 0;
+  a.alpha = 1.f; a.beta = 0.f;
+  a.R = reinterpret_cast<const __nv_bfloat16*>(R);
+  a.ldr = ldr;
+  a.push = push_mode;
+  a.push_world = push_world;
+  a.push_rank = push_rank;
+  a.push_chunk_rows = push_chunk_rows > 0 ? push_chunk_rows : M;
+  a.push_slot_elems = push_slot_elems;
+  for (int j = 0; j < push_world && push_peers; ++j) a.push_dst[j] = reinterpret_cast<__nv_bfloat16*>(push_peers[j]);
+  const bool ag = a_world > 1;
+  if (ag && (a_chunk_rows % BM)) return (int)cudaErrorInvalidValue;
+  a.ag_chunk_rows = ag ? a_chunk_rows : 0;
+  if (!ag && g_pair_mode && M >= 256 && N >= 256) {
+    a.tiles_m = (M + 255) / 256;
+    a.tiles_n = (N + 255) / 256;
+    a.num_tiles = a.tiles_m * a.tiles_n;
+    CUtensorMap ta, tb;
+    bool ok = get_map_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, 128, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+    ok = ok && (b_mn ? get_map_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK,
+                                  CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2)
+                     : get_map_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, 128,
+                                  CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2));
+    if (!ok) return (int)cudaErrorInvalidValue;
+    return b_mn ? launch_tc2<0, 1>(ta, tb, a, stream) : launch_tc2<0, 0>(ta, tb, a, stream);
+  }
+  const int BN = (N <= 128) ? 128 : 256;
+  a.tiles_m = (M + BM - 1) / BM;
+  a.tiles_n = (N + BN - 1) / BN;
+  a.num_tiles = a.tiles_m * a.tiles_n;
+  CUtensorMap ta, tb;
+  PeerMaps pm;
+  bool ok = true;
+  if (ag) {
+    for (int j = 0; j < a_world && ok; ++j)
+      ok = get_map_2d(&pm.m[j], reinterpret_cast<const void*>(a_peers[j]), (uint64_t)K, (uint64_t)a_chunk_rows,
+                      (uint64_t)lda, BK, BM, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+    ta = pm.m[0];
+  } else {
+    ok = get_map_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+  }
+  if (ok)
+    ok = b_mn ? get_map_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2)
+              : get_map_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, (uint32_t)BN,
+                           CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+  if (!ok) return (int)cudaErrorInvalidValue;
+  if (BN == 128) {
+    if (ag) return b_mn ? launch_tc<128, 6, 0, 1, 1>(ta, tb, a, stream, &pm) : launch_tc<128, 6, 0, 0, 1>(ta, tb, a, stream, &pm);
+    return b_mn ? launch_tc<128, 6, 0, 1>(ta, tb, a, stream) : launch_tc<128, 6, 0, 0>(ta, tb, a, stream);
+  }
+  if (ag) return b_mn ? launch_tc<256, 4, 0, 1, 1>(ta, tb, a, stream, &pm) : launch_tc<256, 4, 0, 0, 1>(ta, tb, a, stream, &pm);
+  return b_mn ? launch_tc<256, 4, 0, 1>(ta, tb, a, stream) : launch_tc<256, 4, 0, 0>(ta, tb, a, stream);
 }

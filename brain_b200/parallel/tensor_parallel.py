@@ -1,0 +1,222 @@
+"""Tensor parallelism with communication fused into the tcgen05 GEMM (the reference's
+``TensorParallelLinear::forward`` returns zeros, crates/brain-distributed/src/tensor_parallel.rs:8-27).
+
+* ``ColumnParallelLinear`` (QKV / gate-up): weight shard [out/W, in]. With sequence parallelism the
+  input is this rank's token shard; the forward GEMM loads A tiles straight from the rank that owns
+  them (TMA over NVLink, one tensor map per rank: AG -> GEMM in one kernel). Backward: dx = dy W runs
+  as GEMM -> reduce-scatter (the epilogue pushes each row block to its owner's receive slot), dW =
+  dy^T x_full.
+* ``RowParallelLinear`` (out-proj / down): weight shard [out, in/W]. Forward GEMM -> reduce-scatter
+  (sequence parallel) or GEMM -> all-reduce (the epilogue pushes every row to every rank, used by
+  decode); the receiver sums its W slots after a peer barrier. Backward: dx = dy_full W via the
+  AG -> GEMM kernel, dW = dy_full^T x.
+Receive / staging buffers are symmetric (CUDA IPC) and double-buffered by call parity, so a fast
+rank never overwrites a buffer a slower peer is still reading (every call contains a barrier).
+With one rank the layers are plain GEMMs.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+import torch.distributed as dist
+
+from .. import _native
+from ..nn import init as _init
+from ..nn.module import Module
+from ..ops.gemm import gemm
+from ..ops.linear import _wgrad
+
+_native.register({"brain_gemm_bf16_tp": ("brain_kernels", "piiplpliplpiiiilpliiis")})
+
+
+class TPContext:
+    """Communicator + symmetric scratch shared by the tensor-parallel layers of one group."""
+
+    def __init__(self, group=None, comm=None):
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.comm = comm
+        if self.world > 1 and self.comm is None:
+            from .symm import NvlinkComm
+            self.comm = NvlinkComm(group)
+        self._bufs: dict = {}
+        self.calls = 0
+
+    def symm(self, name: str, nbytes: int, parity: int):
+        """Symmetric buffer `name` (double-buffered by parity) of at least nbytes."""
+        key = (name, parity)
+        buf = self._bufs.get(key)
+        if buf is None or buf.nbytes < nbytes:
+            from .symm import SymmetricBuffer
+            if buf is not None:
+                buf.close()
+            buf = SymmetricBuffer(max(nbytes, 1 << 16), self.group)
+            self._bufs[key] = buf
+        return buf
+
+    def next_parity(self) -> int:
+        self.calls += 1
+        return self.calls & 1
+
+    def close(self):
+        for b in self._bufs.values():
+            b.close()
+        self._bufs.clear()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _i64(vals):
+    return (ctypes.c_int64 * len(vals))(*[int(v) for v in vals])
+
+
+def gemm_push(ctx: TPContext, a: torch.Tensor, w: torch.Tensor, mode: int, rows_per_rank: int,
+              b_mn: int = 0) -> torch.Tensor:
+    """C = a @ w.T (w [N, K]; or a @ w for b_mn=1, w [K, N]), reduced over ranks in the GEMM epilogue.
+
+    mode 1 (reduce-scatter): returns this rank's rows [rank*rows_per_rank, ...) of the sum.
+    mode 2 (all-reduce): returns the full sum [M, N].
+    """
+    M, K = a.shape
+    N = w.shape[1] if b_mn else w.shape[0]
+    W = ctx.world
+    out_rows = rows_per_rank if mode == 1 else M
+    slot = out_rows * N
+    par = ctx.next_parity()
+    recv = ctx.symm("recv", W * slot * 2, par)
+    _native.call("brain_gemm_bf16_tp", None, 1, 0, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), b_mn,
+                 None, N, recv.peer_array(0), mode, ctx.rank, W, rows_per_rank if mode == 1 else M, slot,
+                 None, 0, M, N, K, _stream())
+    ctx.comm.barrier(20 + mode)
+    out = torch.empty(out_rows, N, device=a.device, dtype=torch.bfloat16)
+    slots = _i64([recv.local + s * slot * 2 for s in range(W)])
+    _native.call("brain_comm_reduce_pull", slots, 0, ctx.rank, W, out.data_ptr(), slot, 1, 1.0, _stream())
+    return out
+
+
+def gemm_allgather_a(ctx: TPContext, a_local: torch.Tensor, w: torch.Tensor, b_mn: int = 0) -> torch.Tensor:
+    """C = concat_ranks(a_local) @ w.T (or @ w for b_mn=1) with A tiles read from their owners
+    inside the GEMM (rows per rank must be a multiple of 128)."""
+    T, K = a_local.shape
+    N = w.shape[1] if b_mn else w.shape[0]
+    W = ctx.world
+    par = ctx.next_parity()
+    stage = ctx.symm("ag", T * K * 2, par)
+    sv = stage.view(torch.bfloat16, T * K).view(T, K)
+    sv.copy_(a_local)
+    ctx.comm.barrier(30)
+    out = torch.empty(T * W, N, device=a_local.device, dtype=torch.bfloat16)
+    _native.call("brain_gemm_bf16_tp", stage.peer_array(0), W, T, None, K, w.data_ptr(), w.stride(0), b_mn,
+                 out.data_ptr(), N, None, 0, ctx.rank, W, 0, 0, None, 0, T * W, N, K, _stream())
+    return out
+
+
+def all_gather_rows(ctx: TPContext, x: torch.Tensor) -> torch.Tensor:
+    """[T, K] per rank -> [W*T, K] (P2P pull), used where the gathered tensor itself is needed."""
+    T, K = x.shape
+    full = torch.empty(T * ctx.world, K, device=x.device, dtype=x.dtype)
+    return ctx.comm.all_gather_flat(x.contiguous().view(-1), full.view(-1)).view(T * ctx.world, K)
+
+
+class _ColumnSPFn(torch.autograd.Function):
+    @staticmethod
+    def forward(c, x_local, w, ctx):
+        c.save_for_backward(x_local, w)
+        c.tp = ctx
+        return gemm_allgather_a(ctx, x_local.contiguous(), w)
+
+    @staticmethod
+    def backward(c, dy):
+        x_local, w = c.saved_tensors
+        ctx = c.tp
+        T = x_local.shape[0]
+        dx = gemm_push(ctx, dy.contiguous(), w, 1, T, b_mn=1)  # (dy @ W) reduce-scattered by rows
+        x_full = all_gather_rows(ctx, x_local)
+        dw = _wgrad(dy.contiguous(), x_full, w)
+        return dx, dw, None
+
+
+class _RowFn(torch.autograd.Function):
+    @staticmethod
+    def forward(c, x, w, ctx, sp):
+        c.save_for_backward(x, w)
+        c.tp, c.sp = ctx, sp
+        M = x.shape[0]
+        if sp:
+            return gemm_push(ctx, x.contiguous(), w, 1, M // ctx.world)
+        return gemm_push(ctx, x.contiguous(), w, 2, M)
+
+    @staticmethod
+    def backward(c, dy):
+        x, w = c.saved_tensors
+        ctx = c.tp
+        if c.sp:
+            dx = gemm_allgather_a(ctx, dy.contiguous(), w, b_mn=1)
+            dy_full = all_gather_rows(ctx, dy.contiguous())
+        else:
+            dx = gemm(dy.contiguous(), w)
+            dy_full = dy.contiguous()
+        dw = _wgrad(dy_full, x, w)
+        return dx, dw, None, None
+
+
+class ColumnParallelLinear(Module):
+    def __init__(self, in_features: int, out_features: int, ctx: TPContext, sequence_parallel: bool = False,
+                 device=None, dtype=torch.bfloat16, init_std: float = 0.02, seed: int = 0):
+        super().__init__()
+        if out_features % ctx.world:
+            raise ValueError("out_features must divide by the tensor-parallel size")
+        self.ctx, self.sp = ctx, sequence_parallel
+        self.in_features, self.out_features = in_features, out_features
+        self.weight = torch.nn.Parameter(torch.empty(out_features // ctx.world, in_features, device=device,
+                                                     dtype=dtype))
+        g = torch.Generator(device=self.weight.device).manual_seed(seed * 1000 + ctx.rank)
+        with torch.no_grad():
+            self.weight.copy_(torch.randn(self.weight.shape, generator=g, device=self.weight.device) * init_std)
+
+    def forward(self, x):
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1])
+        if self.ctx.world == 1 or not self.sp:
+            y = gemm(x2, self.weight, trans_b=True) if x2.is_cuda else x2 @ self.weight.t()
+            return y.view(*shp[:-1], -1)
+        y = _ColumnSPFn.apply(x2, self.weight, self.ctx)
+        return y.view(-1, self.weight.shape[0])
+
+
+class RowParallelLinear(Module):
+    def __init__(self, in_features: int, out_features: int, ctx: TPContext, sequence_parallel: bool = False,
+                 device=None, dtype=torch.bfloat16, init_std: float = 0.02, seed: int = 0):
+        super().__init__()
+        if in_features % ctx.world:
+            raise ValueError("in_features must divide by the tensor-parallel size")
+        self.ctx, self.sp = ctx, sequence_parallel
+        self.weight = torch.nn.Parameter(torch.empty(out_features, in_features // ctx.world, device=device,
+                                                     dtype=dtype))
+        g = torch.Generator(device=self.weight.device).manual_seed(seed * 1000 + 500 + ctx.rank)
+        with torch.no_grad():
+            self.weight.copy_(torch.randn(self.weight.shape, generator=g, device=self.weight.device) * init_std)
+
+    def forward(self, x):
+        shp = x.shape
+        x2 = x.reshape(-1, shp[-1])
+        if self.ctx.world == 1:
+            y = gemm(x2, self.weight, trans_b=True) if x2.is_cuda else x2 @ self.weight.t()
+            return y.view(*shp[:-1], -1)
+        y = _RowFn.apply(x2, self.weight, self.ctx, self.sp)
+        return y if self.sp else y.view(*shp[:-1], -1)
+
+
+TensorParallelLinear = ColumnParallelLinear
+
+
+def shard_columns(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    return torch.tensor_split(w, world, dim=0)[rank].contiguous()
+
+
+def shard_rows(w: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    return torch.tensor_split(w, world, dim=1)[rank].contiguous()
