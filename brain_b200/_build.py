@@ -37,7 +37,7 @@ CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-Wall", "-Wno
 LIBRARIES = {
     "brain_kernels": [
         "host_utils.cu", "gemm.cu", "norms.cu", "elementwise.cu", "cross_entropy.cu", "optim.cu",
-        "attention.cu", "attention_tc.cu", "attention_bwd_tc.cu", "fp8.cu",
+        "attention.cu", "attention_tc.cu", "attention_bwd_tc.cu", "attention_decode.cu", "decode_tp.cu", "fp8.cu",
     ],
     "brain_comm": ["host_utils.cu", "comm.cu"],
 }

@@ -72,6 +72,10 @@ def available(name: str = "brain_kernels") -> bool:
         return False
 
 
+# entry points whose C return type is int64_t (all others return int status codes)
+RETURNS_I64: set[str] = set()
+
+
 def fn(name: str):
     f = _fns.get(name)
     if f is not None:
@@ -80,7 +84,7 @@ def fn(name: str):
     lib = load(libname)
     f = getattr(lib, name)
     f.argtypes = [_CODES[c] for c in codes]
-    f.restype = ctypes.c_char_p if name == "brain_error_string" else _I
+    f.restype = ctypes.c_char_p if name == "brain_error_string" else (_L if name in RETURNS_I64 else _I)
     _fns[name] = f
     return f
 

@@ -277,6 +277,14 @@ BRAIN_API int brain_comm_copy(int64_t src, int64_t dst, int64_t nbytes, cudaStre
   return (int)cudaGetLastError();
 }
 
+// Copy-engine copy (local or peer pointer, one cudaMemcpyAsync): overlaps with kernels on other
+// streams without taking SMs.
+BRAIN_API int brain_comm_copy_async(int64_t src, int64_t dst, int64_t nbytes, cudaStream_t st) {
+  if (nbytes == 0) return 0;
+  return (int)cudaMemcpyAsync(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), (size_t)nbytes,
+                              cudaMemcpyDeviceToDevice, st);
+}
+
 // Fused reduce-scatter + AdamW + bf16 all-gather push for the shard [off, off + n) of this rank.
 // grads/params: int64[world] peer pointers of the flat gradient (bf16 if grad_bf16 else f32) and
 // bf16 parameter buffers. n must be a multiple of 8 and off 8-aligned.

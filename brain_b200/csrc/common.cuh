@@ -367,6 +367,16 @@ bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, void*
 }  // namespace brain_host
 
 namespace brain {
+// System-scope flag store / load (peer GPUs observe them over NVLink in release/acquire order).
+__device__ __forceinline__ void sys_st_release(int* addr, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ int sys_ld_acquire(const int* addr) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
 // 2^x with the MUFU approximation (ex2.approx.ftz.f32); -inf maps to +0.
 __device__ __forceinline__ float ex2_fast(float x) {
   float y;

@@ -51,14 +51,6 @@ struct GemmArgs {
   int push_chunk_rows;
   int64_t push_slot_elems;
   __nv_bfloat16* push_dst[8];
-  // All-gathered A operand (AG -> GEMM): rows [j * ag_chunk_rows, (j+1) * ag_chunk_rows) of A live
-  // on rank j and are loaded by TMA straight from its memory (tensor map j); 0 = off.
-  int ag_chunk_rows;
-};
-
-// One A tensor map per rank for the all-gathered operand (kernel parameter space, 64-B aligned).
-struct alignas(64) PeerMaps {
-  CUtensorMap m[8];
 };
 
 template <int BN, int STAGES>
@@ -162,10 +154,10 @@ __device__ __forceinline__ void store_chunk_at(const GemmArgs& args, int gm, int
   }
 }
 
-template <int BN, int STAGES, int A_MN, int B_MN, int AG>
+template <int BN, int STAGES, int A_MN, int B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   GemmArgs args, const __grid_constant__ PeerMaps pm) {
+                   GemmArgs args) {
   using S = Smem<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -232,10 +224,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (A_MN) {
 #pragma unroll
             for (int j = 0; j < BM / 64; ++j) tma_load_2d(&tmA, sa + j * (64 * BK * 2), full_bar(s), m0 + 64 * j, k0);
-          } else if (AG) {
-            // rows of this tile live on rank `owner`: TMA reads its memory over NVLink (no multicast)
-            const int owner = m0 / args.ag_chunk_rows;
-            tma_load_2d(&pm.m[owner], sa, full_bar(s), k0, m0 - owner * args.ag_chunk_rows);
           } else {
             tma_load_2d(&tmA, sa, full_bar(s), k0, m0);
           }
@@ -592,11 +580,10 @@ bool get_map_2d(CUtensorMap* out, const void* ptr, uint64_t inner, uint64_t oute
   return true;
 }
 
-template <int BN, int STAGES, int A_MN, int B_MN, int AG = 0>
-int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st,
-              const PeerMaps* pm = nullptr) {
+template <int BN, int STAGES, int A_MN, int B_MN>
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
   using S = Smem<BN, STAGES>;
-  auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, AG>;
+  auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -604,9 +591,8 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, c
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::TOTAL);
     attr_set[dev & 63] = true;
   }
-  static PeerMaps empty_maps;  // unused unless AG
   int grid = std::min(a.num_tiles, brain_host::num_sms());
-  kern<<<grid, kThreads, S::TOTAL, st>>>(ta, tb, a, pm ? *pm : empty_maps);
+  kern<<<grid, kThreads, S::TOTAL, st>>>(ta, tb, a);
   return (int)cudaGetLastError();
 }
 
@@ -759,21 +745,20 @@ BRAIN_API int brain_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
 #undef BRAIN_GEMM_CASE
 }
 
-// Tensor-parallel GEMM with fused communication, C = op(A) B^T style (A [M, K] K-major, B [N, K]):
-//   a_world > 1 : all-gathered A. Rows [j * a_chunk_rows, (j+1) * a_chunk_rows) are read by TMA from
-//                 a_peers[j] (row stride lda) - the AG -> GEMM fusion; a_chunk_rows % 128 == 0.
+// Tensor-parallel GEMM with the communication in its epilogue, C = A B^T (A [M, K] K-major; B [N, K],
+// or [K, N] with b_mn = 1):
 //   push_mode 1 : row gm of C goes to slot push_rank of rank (gm / push_chunk_rows)'s receive buffer
 //                 push_peers[j] (slot stride push_slot_elems, row gm % push_chunk_rows, stride ldc):
 //                 GEMM -> reduce-scatter fusion. push_mode 2: every rank receives every row (-> all-reduce).
 //   push_mode 0 : C written locally.
-// The receive side then reduces its slots after a peer barrier (parallel/tensor_parallel.py).
-BRAIN_API int brain_gemm_bf16_tp(const int64_t* a_peers, int a_world, int a_chunk_rows, const void* A, int64_t lda,
-                                 const void* B, int64_t ldb, int b_mn, void* C, int64_t ldc, const int64_t* push_peers,
-                                 int push_mode, int push_rank, int push_world, int push_chunk_rows,
-                                 int64_t push_slot_elems, const void* R, int64_t ldr, int M, int N, int K,
-                                 cudaStream_t stream) {
+// The epilogue stores go straight to the peers' memory over NVLink; the receive side reduces its slots
+// after a peer barrier (parallel/tensor_parallel.py). Operands are always this GPU's own memory.
+BRAIN_API int brain_gemm_bf16_tp(const void* A, int64_t lda, const void* B, int64_t ldb, int b_mn, void* C,
+                                 int64_t ldc, const int64_t* push_peers, int push_mode, int push_rank, int push_world,
+                                 int push_chunk_rows, int64_t push_slot_elems, const void* R, int64_t ldr, int M, int N,
+                                 int K, cudaStream_t stream) {
   if (M <= 0 || N <= 0) return 0;
-  if (a_world > 8 || push_world > 8) return (int)cudaErrorInvalidValue;
+  if (push_world > 8) return (int)cudaErrorInvalidValue;
   if ((lda % 8) || (ldb % 8) || K < 16) return (int)cudaErrorInvalidValue;
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K;
@@ -787,10 +772,7 @@ BRAIN_API int brain_gemm_bf16_tp(const int64_t* a_peers, int a_world, int a_chun
   a.push_chunk_rows = push_chunk_rows > 0 ? push_chunk_rows : M;
   a.push_slot_elems = push_slot_elems;
   for (int j = 0; j < push_world && push_peers; ++j) a.push_dst[j] = reinterpret_cast<__nv_bfloat16*>(push_peers[j]);
-  const bool ag = a_world > 1;
-  if (ag && (a_chunk_rows % BM)) return (int)cudaErrorInvalidValue;
-  a.ag_chunk_rows = ag ? a_chunk_rows : 0;
-  if (!ag && g_pair_mode && M >= 256 && N >= 256) {
+  if (g_pair_mode && M >= 256 && N >= 256) {
     a.tiles_m = (M + 255) / 256;
     a.tiles_n = (N + 255) / 256;
     a.num_tiles = a.tiles_m * a.tiles_n;
@@ -808,25 +790,12 @@ BRAIN_API int brain_gemm_bf16_tp(const int64_t* a_peers, int a_world, int a_chun
   a.tiles_n = (N + BN - 1) / BN;
   a.num_tiles = a.tiles_m * a.tiles_n;
   CUtensorMap ta, tb;
-  PeerMaps pm;
-  bool ok = true;
-  if (ag) {
-    for (int j = 0; j < a_world && ok; ++j)
-      ok = get_map_2d(&pm.m[j], reinterpret_cast<const void*>(a_peers[j]), (uint64_t)K, (uint64_t)a_chunk_rows,
-                      (uint64_t)lda, BK, BM, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
-    ta = pm.m[0];
-  } else {
-    ok = get_map_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
-  }
+  bool ok = get_map_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, BM, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
   if (ok)
     ok = b_mn ? get_map_2d(&tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2)
               : get_map_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, (uint32_t)BN,
                            CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
   if (!ok) return (int)cudaErrorInvalidValue;
-  if (BN == 128) {
-    if (ag) return b_mn ? launch_tc<128, 6, 0, 1, 1>(ta, tb, a, stream, &pm) : launch_tc<128, 6, 0, 0, 1>(ta, tb, a, stream, &pm);
-    return b_mn ? launch_tc<128, 6, 0, 1>(ta, tb, a, stream) : launch_tc<128, 6, 0, 0>(ta, tb, a, stream);
-  }
-  if (ag) return b_mn ? launch_tc<256, 4, 0, 1, 1>(ta, tb, a, stream, &pm) : launch_tc<256, 4, 0, 0, 1>(ta, tb, a, stream, &pm);
+  if (BN == 128) return b_mn ? launch_tc<128, 6, 0, 1>(ta, tb, a, stream) : launch_tc<128, 6, 0, 0>(ta, tb, a, stream);
   return b_mn ? launch_tc<256, 4, 0, 1>(ta, tb, a, stream) : launch_tc<256, 4, 0, 0>(ta, tb, a, stream);
 }

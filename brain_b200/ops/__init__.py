@@ -13,4 +13,5 @@ from .attention import flash_attention, flash_attention_fwd, qkv_attention, sdpa
 from .linear import linear, norm_linear, swiglu_linear  # noqa: F401
 from .cross_entropy import cross_entropy, linear_cross_entropy  # noqa: F401
 from .embedding import embedding  # noqa: F401
+from .decode import paged_decode_attention, kv_append_rope  # noqa: F401
 from . import optim_kernels  # noqa: F401

@@ -42,7 +42,8 @@ _native.register({
     "brain_status_attention": ("brain_kernels", "pi"),
 })
 
-STATUS_TAGS = ["gemm", "norms", "elementwise", "ce", "optim", "attention", "attention_tc", "attention_bwd_tc"]
+STATUS_TAGS = ["gemm", "norms", "elementwise", "ce", "optim", "attention", "attention_tc", "attention_bwd_tc",
+               "attention_decode", "decode_tp"]
 
 
 def stream(t: torch.Tensor) -> int:

@@ -1,0 +1,196 @@
+"""Paged-KV decode attention and the fused RoPE + KV-append of the new token (``csrc/attention_decode.cu``).
+
+``paged_decode_attention(q, k_pool, v_pool, block_table, seq_lens)``: q [B, Hq, D] (one new token
+per sequence, any strides with unit stride on D), pools [num_blocks, block_size, Hkv, D],
+block_table [B, max_blocks] int32, seq_lens [B] int32 (cached tokens, the new one included).
+On CPU the cache is gathered per sequence and the reference SDPA is used.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from .. import _native
+from ._common import stream
+
+_native.register({
+    "brain_decode_workspace": ("brain_kernels", "iiiii"),
+    "brain_decode_splits": ("brain_kernels", "iii"),
+    "brain_decode_attention": ("brain_kernels", "pllpppipipllpiiiifis"),
+    "brain_kv_append_rope": ("brain_kernels", "pliiiipppppiis"),
+    "brain_status_attention_decode": ("brain_kernels", "pi"),
+})
+_native.RETURNS_I64.add("brain_decode_workspace")
+
+
+def paged_decode_attention(q, k_pool, v_pool, block_table, seq_lens, scale=None, splits=None, max_len=None,
+                           workspace=None, out=None):
+    B, Hq, D = q.shape
+    Hkv = k_pool.shape[2]
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    if not q.is_cuda:
+        return _decode_ref(q, k_pool, v_pool, block_table, seq_lens, scale)
+    if splits is None:
+        ml = max_len if max_len is not None else block_table.shape[1] * k_pool.shape[1]
+        splits = int(_native.fn("brain_decode_splits")(B, Hkv, ml))
+    if workspace is None:
+        n = int(_native.fn("brain_decode_workspace")(B, Hq, Hkv, D, splits))
+        workspace = torch.empty(n, device=q.device, dtype=torch.float32)
+    if out is None:
+        out = torch.empty(B, Hq, D, device=q.device, dtype=q.dtype)
+    _native.call("brain_decode_attention", q.data_ptr(), q.stride(0), q.stride(1), k_pool.data_ptr(),
+                 v_pool.data_ptr(), block_table.data_ptr(), block_table.shape[1], seq_lens.data_ptr(), k_pool.shape[1],
+                 out.data_ptr(), out.stride(0), out.stride(1), workspace.data_ptr(), B, Hq, Hkv, D, float(scale),
+                 int(splits), stream(q))
+    return out
+
+
+def _decode_ref(q, k_pool, v_pool, block_table, seq_lens, scale):
+    B, Hq, D = q.shape
+    Hkv = k_pool.shape[2]
+    bs = k_pool.shape[1]
+    out = torch.empty_like(q)
+    for b in range(B):
+        L = int(seq_lens[b])
+        nb = -(-L // bs)
+        idx = block_table[b, :nb].long()
+        k = k_pool[idx].reshape(-1, Hkv, D)[:L].float()
+        v = v_pool[idx].reshape(-1, Hkv, D)[:L].float()
+        rep = Hq // Hkv
+        kk, vv = k.repeat_interleave(rep, 1), v.repeat_interleave(rep, 1)  # [L, Hq, D]
+        s = torch.einsum("hd,lhd->hl", q[b].float(), kk) * scale
+        p = s.softmax(-1)
+        out[b] = torch.einsum("hl,lhd->hd", p, vv).to(q.dtype)
+    return out
+
+
+def kv_append_rope(qkv, Hq, Hkv, pos, rope_cs, k_pool, v_pool, block_table):
+    """qkv [B, (Hq+2Hkv)*D] of the new tokens: q and k rotated in place at positions pos [B] (int32),
+    k and v written into the paged pools."""
+    B = qkv.shape[0]
+    D = qkv.shape[1] // (Hq + 2 * Hkv)
+    if qkv.is_cuda:
+        _native.call("brain_kv_append_rope", qkv.data_ptr(), qkv.stride(0), B, Hq, Hkv, D, pos.data_ptr(),
+                     rope_cs.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), block_table.data_ptr(),
+                     block_table.shape[1], k_pool.shape[1], stream(qkv))
+        return
+    from .rope import rope_ref
+    x = qkv.view(B, 1, Hq + 2 * Hkv, D)
+    rot = rope_ref(x[:, :, :Hq + Hkv], rope_cs, pos.long()[:, None])
+    x[:, :, :Hq + Hkv] = rot
+    bs = k_pool.shape[1]
+    for b in range(B):
+        p = int(pos[b])
+        blk = int(block_table[b, p // bs])
+        k_pool[blk, p % bs] = x[b, 0, Hq:Hq + Hkv]
+        v_pool[blk, p % bs] = x[b, 0, Hq + Hkv:]
+
+
+# ---------------------------------------------------------------------------------------------
+# Skinny (decode) GEMM with fused epilogues and the tensor-parallel step kernels (csrc/decode_tp.cu)
+# ---------------------------------------------------------------------------------------------
+EPI_STORE, EPI_PUSH, EPI_SWIGLU, EPI_QKV, EPI_ARGMAX = 0, 2, 3, 4, 5
+
+_native.register({
+    "brain_skinny_splits": ("brain_kernels", "iii"),
+    "brain_skinny_workspace": ("brain_kernels", "iii"),
+    "brain_skinny_gemm": ("brain_kernels", "plpliiiifplplippps"),
+    "brain_tp_ar_norm": ("brain_kernels", "pppiliiplpfplls"),
+    "brain_tp_pick_embed": ("brain_kernels", "pppilipliippfpplppls"),
+    "brain_status_decode_tp": ("brain_kernels", "pi"),
+})
+_native.RETURNS_I64.add("brain_skinny_workspace")
+
+
+class SkinnyWorkspace:
+    """Split-K partial tiles (f32) and per-tile tickets (int32, zero between launches) for skinny GEMMs
+    issued one after another on one stream."""
+
+    def __init__(self, device, floats: int = 1 << 22, tiles: int = 8192):
+        self.ws = torch.empty(floats, device=device, dtype=torch.float32)
+        self.cnt = torch.zeros(tiles, device=device, dtype=torch.int32)
+
+    def fits(self, M, N, splits) -> bool:
+        need = int(_native.fn("brain_skinny_workspace")(M, N, splits))
+        return need <= self.ws.numel() and -(-N // 128) <= self.cnt.numel()
+
+
+_WS: dict = {}
+
+
+def _workspace(device) -> SkinnyWorkspace:
+    key = str(device)
+    if key not in _WS:
+        _WS[key] = SkinnyWorkspace(device)
+    return _WS[key]
+
+
+def skinny_splits(M: int, N: int, K: int) -> int:
+    return int(_native.fn("brain_skinny_splits")(M, N, K))
+
+
+def decode_ext(world=1, rank=0, slot_elems=0, ctrl=None, keys=None, vocab_offset=0, hq=0, hkv=0, pos=None,
+               rope_cs=None, k_pool=None, v_pool=None, block_table=None, peer_slots=(), peer_flags=()):
+    """The int64[32] side-argument block of ``brain_skinny_gemm`` (layout documented in the source)."""
+    import ctypes
+
+    def p(t):
+        return 0 if t is None else (t if isinstance(t, int) else t.data_ptr())
+    v = [0] * 32
+    v[0], v[1], v[2], v[3], v[4], v[5] = world, rank, slot_elems, p(ctrl), p(keys), vocab_offset
+    v[6], v[7], v[8], v[9], v[10], v[11] = hq, hkv, p(pos), p(rope_cs), p(k_pool), p(v_pool)
+    v[12] = p(block_table)
+    if block_table is not None:
+        v[13], v[14] = block_table.shape[1], k_pool.shape[1]
+    for i, s in enumerate(peer_slots):
+        v[16 + i] = int(s)
+    for i, f in enumerate(peer_flags):
+        v[24 + i] = int(f)
+    return (ctypes.c_int64 * 32)(*v)
+
+
+def skinny_gemm(x, w, epi=EPI_STORE, out=None, residual=None, alpha=1.0, splits=None, ws=None, ext=None,
+                out_cols=None):
+    """x [M, K] (M <= 64) times w [N, K]^T on the tensor cores with the operands swapped.
+
+    epi: EPI_STORE (out [M, N], + residual), EPI_SWIGLU (w rows interleaved [gate 64 | up 64] per 128;
+    out [M, N/2]), EPI_QKV / EPI_PUSH / EPI_ARGMAX (side arguments in ``ext``, see ``decode_ext``).
+    """
+    M, K = x.shape
+    N = w.shape[0]
+    if splits is None:
+        splits = skinny_splits(M, N, K)
+    ws = ws or _workspace(x.device)
+    if out is None and epi in (EPI_STORE, EPI_SWIGLU, EPI_QKV):
+        cols = out_cols if out_cols is not None else (N // 2 if epi == EPI_SWIGLU else N)
+        out = torch.empty(M, cols, device=x.device, dtype=torch.bfloat16)
+    _native.call("brain_skinny_gemm", x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), M, N, K, epi,
+                 float(alpha), 0 if out is None else out.data_ptr(), 0 if out is None else out.stride(0),
+                 0 if residual is None else residual.data_ptr(), 0 if residual is None else residual.stride(0),
+                 int(splits), ws.ws.data_ptr(), ws.cnt.data_ptr(), ext, stream(x))
+    return out
+
+
+def interleave_gate_up(w_gate, w_up, group: int = 64):
+    """[F, K] gate and up weights -> [2F, K] with rows [gate 64 | up 64] per 128 (EPI_SWIGLU layout)."""
+    F, K = w_gate.shape
+    return torch.stack([w_gate.view(F // group, group, K), w_up.view(F // group, group, K)], 1).reshape(2 * F, K)
+
+
+def ar_norm(slots, flags, ctrl, world, slot_elems, resid, gamma, eps, normed, budget_s=2.0):
+    """resid += sum of the `world` slots of the current epoch; normed = rmsnorm(resid) * gamma."""
+    M, N = resid.shape
+    _native.call("brain_tp_ar_norm", slots, flags, ctrl.data_ptr(), world, slot_elems, M, N, resid.data_ptr(),
+                 resid.stride(0), gamma.data_ptr(), float(eps), normed.data_ptr(), normed.stride(0),
+                 int(budget_s * 1e9), stream(resid))
+
+
+def pick_embed(key_slots, flags, ctrl, world, slot_elems, emb, resid, gamma, eps, normed, hist, pos, seq_lens,
+               budget_s=2.0):
+    """Greedy token from the ranks' argmax keys -> hist / pos / seq_lens, and the next layer-0 input."""
+    M, N = resid.shape
+    _native.call("brain_tp_pick_embed", key_slots, flags, ctrl.data_ptr(), world, slot_elems, M, emb.data_ptr(),
+                 emb.stride(0), emb.shape[0], N, resid.data_ptr(), gamma.data_ptr(), float(eps), normed.data_ptr(),
+                 hist.data_ptr(), hist.stride(0), pos.data_ptr(), seq_lens.data_ptr(), int(budget_s * 1e9),
+                 stream(resid))

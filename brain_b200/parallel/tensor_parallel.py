@@ -2,14 +2,14 @@
 ``TensorParallelLinear::forward`` returns zeros, crates/brain-distributed/src/tensor_parallel.rs:8-27).
 
 * ``ColumnParallelLinear`` (QKV / gate-up): weight shard [out/W, in]. With sequence parallelism the
-  input is this rank's token shard; the forward GEMM loads A tiles straight from the rank that owns
-  them (TMA over NVLink, one tensor map per rank: AG -> GEMM in one kernel). Backward: dx = dy W runs
-  as GEMM -> reduce-scatter (the epilogue pushes each row block to its owner's receive slot), dW =
-  dy^T x_full.
+  input is this rank's token shard; the forward is AG -> GEMM pipelined by row block: the local block
+  is multiplied at once while the copy engines pull the other ranks' blocks over NVLink, and each
+  remote block's GEMM starts when its copy lands. Backward: dx = dy W runs as GEMM -> reduce-scatter
+  (the epilogue pushes each row block to its owner's receive slot), dW = dy^T x_full.
 * ``RowParallelLinear`` (out-proj / down): weight shard [out, in/W]. Forward GEMM -> reduce-scatter
   (sequence parallel) or GEMM -> all-reduce (the epilogue pushes every row to every rank, used by
   decode); the receiver sums its W slots after a peer barrier. Backward: dx = dy_full W via the
-  AG -> GEMM kernel, dW = dy_full^T x.
+  pipelined AG -> GEMM, dW = dy_full^T x.
 Receive / staging buffers are symmetric (CUDA IPC) and double-buffered by call parity, so a fast
 rank never overwrites a buffer a slower peer is still reading (every call contains a barrier).
 With one rank the layers are plain GEMMs.
@@ -27,7 +27,10 @@ from ..nn.module import Module
 from ..ops.gemm import gemm
 from ..ops.linear import _wgrad
 
-_native.register({"brain_gemm_bf16_tp": ("brain_kernels", "piiplpliplpiiiilpliiis")})
+_native.register({
+    "brain_gemm_bf16_tp": ("brain_kernels", "plpliplpiiiilpliiis"),
+    "brain_comm_copy_async": ("brain_comm", "llls"),
+})
 
 
 class TPContext:
@@ -42,6 +45,8 @@ class TPContext:
             from .symm import NvlinkComm
             self.comm = NvlinkComm(group)
         self._bufs: dict = {}
+        self._local: dict = {}
+        self.side = None
         self.calls = 0
 
     def symm(self, name: str, nbytes: int, parity: int):
@@ -56,6 +61,22 @@ class TPContext:
             self._bufs[key] = buf
         return buf
 
+    def local(self, name: str, shape, dtype=torch.bfloat16) -> torch.Tensor:
+        """A reusable plain device buffer (not shared with peers)."""
+        n = 1
+        for x in shape:
+            n *= int(x)
+        buf = self._local.get(name)
+        if buf is None or buf.numel() < n or buf.dtype != dtype:
+            buf = torch.empty(n, device=torch.cuda.current_device(), dtype=dtype)
+            self._local[name] = buf
+        return buf[:n].view(*shape)
+
+    def side_stream(self) -> torch.cuda.Stream:
+        if self.side is None:
+            self.side = torch.cuda.Stream()
+        return self.side
+
     def next_parity(self) -> int:
         self.calls += 1
         return self.calls & 1
@@ -64,6 +85,7 @@ class TPContext:
         for b in self._bufs.values():
             b.close()
         self._bufs.clear()
+        self._local.clear()
 
 
 def _stream() -> int:
@@ -88,9 +110,9 @@ def gemm_push(ctx: TPContext, a: torch.Tensor, w: torch.Tensor, mode: int, rows_
     slot = out_rows * N
     par = ctx.next_parity()
     recv = ctx.symm("recv", W * slot * 2, par)
-    _native.call("brain_gemm_bf16_tp", None, 1, 0, a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), b_mn,
-                 None, N, recv.peer_array(0), mode, ctx.rank, W, rows_per_rank if mode == 1 else M, slot,
-                 None, 0, M, N, K, _stream())
+    _native.call("brain_gemm_bf16_tp", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), b_mn, None, N,
+                 recv.peer_array(0), mode, ctx.rank, W, rows_per_rank if mode == 1 else M, slot, None, 0, M, N, K,
+                 _stream())
     ctx.comm.barrier(20 + mode)
     out = torch.empty(out_rows, N, device=a.device, dtype=torch.bfloat16)
     slots = _i64([recv.local + s * slot * 2 for s in range(W)])
@@ -99,19 +121,36 @@ def gemm_push(ctx: TPContext, a: torch.Tensor, w: torch.Tensor, mode: int, rows_
 
 
 def gemm_allgather_a(ctx: TPContext, a_local: torch.Tensor, w: torch.Tensor, b_mn: int = 0) -> torch.Tensor:
-    """C = concat_ranks(a_local) @ w.T (or @ w for b_mn=1) with A tiles read from their owners
-    inside the GEMM (rows per rank must be a multiple of 128)."""
+    """C = concat_ranks(a_local) @ w.T (or @ w for b_mn=1), pipelined by row block.
+
+    The local block's GEMM starts at once; a side stream pulls every other rank's block from its
+    symmetric staging buffer with the copy engines (one copy per peer, nearest peers first), and
+    each remote block's GEMM waits only for its own copy. Compute and NVLink transfer overlap and
+    every GEMM reads this GPU's memory.
+    """
     T, K = a_local.shape
     N = w.shape[1] if b_mn else w.shape[0]
-    W = ctx.world
+    W, r = ctx.world, ctx.rank
     par = ctx.next_parity()
     stage = ctx.symm("ag", T * K * 2, par)
     sv = stage.view(torch.bfloat16, T * K).view(T, K)
     sv.copy_(a_local)
     ctx.comm.barrier(30)
     out = torch.empty(T * W, N, device=a_local.device, dtype=torch.bfloat16)
-    _native.call("brain_gemm_bf16_tp", stage.peer_array(0), W, T, None, K, w.data_ptr(), w.stride(0), b_mn,
-                 out.data_ptr(), N, None, 0, ctx.rank, W, 0, 0, None, 0, T * W, N, K, _stream())
+    gather = ctx.local("ag_gather", (W, T, K))
+    main, side = torch.cuda.current_stream(), ctx.side_stream()
+    side.wait_stream(main)
+    order = [(r + i) % W for i in range(1, W)]
+    events = []
+    for j in order:
+        _native.call("brain_comm_copy_async", stage.ptrs[j], gather[j].data_ptr(), T * K * 2, side.cuda_stream)
+        ev = torch.cuda.Event()
+        ev.record(side)
+        events.append(ev)
+    gemm(a_local, w, trans_b=not b_mn, out=out[r * T:(r + 1) * T])
+    for j, ev in zip(order, events):
+        main.wait_event(ev)
+        gemm(gather[j], w, trans_b=not b_mn, out=out[j * T:(j + 1) * T])
     return out
 
 

@@ -94,3 +94,32 @@ def test_gemm_pair_and_single_cta(pair, ta, tb, shape):
     torch.testing.assert_close(acc, ref + 1, rtol=2e-3, atol=2e-3 * K ** 0.5)
     from brain_b200 import _native
     assert _native.status("gemm")[0] == 0
+
+
+def _tp_call(A, lda, B, ldb, b_mn, C, ldc, push_peers, mode, rank, world, push_chunk, slot, M, N, K):
+    import brain_b200.parallel.tensor_parallel  # noqa: F401  (registers the entry point)
+    from brain_b200 import _native
+    from brain_b200.ops._common import i64_array, stream
+    _native.call("brain_gemm_bf16_tp", A, lda, B.data_ptr(), ldb, b_mn, C, ldc,
+                 None if push_peers is None else i64_array(push_peers), mode, rank, world, push_chunk, slot, None, 0,
+                 M, N, K, stream(B))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("mode", [1, 2])
+@pytest.mark.parametrize("M,N", [(256, 384), (512, 256), (256, 128)])
+def test_gemm_push_local_slots(mode, M, N):
+    """GEMM -> reduce-scatter (mode 1) / all-reduce (mode 2) pushes into W local receive buffers."""
+    K, W, rank = 256, 2, 1
+    a, w = _mk((M, K), "cuda", 30), _mk((N, K), "cuda", 31)
+    rows = M // W if mode == 1 else M
+    slot = rows * N
+    recv = [torch.zeros(W * slot, device="cuda", dtype=torch.bfloat16) for _ in range(W)]
+    _tp_call(a.data_ptr(), K, w, K, 0, 0, N, [r.data_ptr() for r in recv], mode, rank, W, rows if mode == 1 else M,
+             slot, M, N, K)
+    ref = a.float() @ w.float().t()
+    for j in range(W):
+        got = recv[j][rank * slot:(rank + 1) * slot].view(rows, N).float()
+        exp = ref[j * rows:(j + 1) * rows] if mode == 1 else ref
+        torch.testing.assert_close(got, exp, rtol=2e-2, atol=2e-1)
+        assert recv[j][(1 - rank) * slot:(2 - rank) * slot].abs().sum().item() == 0

@@ -11,7 +11,7 @@ def _tp_worker(rank, world):
     from brain_b200.parallel import dist as bdist
     from brain_b200.parallel.tensor_parallel import (ColumnParallelLinear, RowParallelLinear, TPContext,
                                                      shard_columns, shard_rows)
-    bdist.init(timeout_s=120)
+    bdist.init(timeout_s=60)
     ctx = TPContext()
     g = torch.Generator(device="cuda").manual_seed(0)
     K, N, T = 512, 768, 128
