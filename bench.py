@@ -98,6 +98,16 @@ def main():
     ap.add_argument("--layers", type=int, default=32, help="development only: fewer layers is not the benchmark")
     ap.add_argument("--comm", default="nccl", choices=["nccl", "nvlink"])
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--workload", default="train", choices=["train", "decode"],
+                    help="train: Llama-3-8B DDP (headline); decode: Llama-3-70B-shape TP=N greedy decode")
+    ap.add_argument("--decode", default="auto", choices=["auto", "on", "off"],
+                    help="also measure the 70B TP decode inside the train run (auto: when N == 8)")
+    ap.add_argument("--decode-batch", type=int, default=32)
+    ap.add_argument("--prompt-len", type=int, default=2048)
+    ap.add_argument("--new-tokens", type=int, default=256)
+    ap.add_argument("--decode-layers", type=int, default=80, help="development only")
+    ap.add_argument("--decode-shard-of", type=int, default=0,
+                    help="development only: run one rank's shard of an N-way TP group on a single GPU")
     args = ap.parse_args()
 
     if args.impl == "reference":
@@ -116,6 +126,19 @@ def main():
     if world != args.gpus:
         log(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}")
     dev = ctx.device
+    decode = None
+    if args.workload == "decode" or args.decode == "on" or (args.decode == "auto" and world == 8):
+        try:
+            decode = run_decode(args, rank, world, dev)
+        except Exception as e:  # the train measurement below still runs
+            log(f"{bdist.rank_prefix()} decode measurement failed: {type(e).__name__}: {e}")
+            decode = {"error": f"{type(e).__name__}: {e}"}
+        torch.cuda.empty_cache()
+        if args.workload == "decode":
+            if rank == 0:
+                print(json.dumps(decode), flush=True)
+            bdist.shutdown()
+            return 0
     cfg = LlamaLiteConfig.llama3_8b(max_seq_len=args.seq)
     if args.layers != cfg.num_layers:
         cfg = cfg.replace(num_layers=args.layers)
@@ -213,10 +236,113 @@ def main():
             "gpu_launches": lc.count,
             "impl": "brain",
         }
+        if decode is not None:
+            out["decode_70b"] = decode
         print(json.dumps(out), flush=True)
     del dp, model
     bdist.shutdown()
     return 0
+
+
+def run_decode(args, rank, world, dev) -> dict:
+    """Llama-3-70B-shaped greedy decode, tensor parallel over all ranks (TP = N): prefill B prompts of
+    S uniform tokens, then decode; the decode steps are CUDA-graph replays of the fused decode kernels.
+    Returns the decode measurement (decode tokens/s over all sequences, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from brain_b200.models import LlamaLiteConfig
+    from brain_b200.models.llama_tp import LlamaTPServe, decode_bytes_per_step
+    from brain_b200.parallel import dist as bdist
+
+    B, S, NEW = args.decode_batch, args.prompt_len, args.new_tokens
+    cfg = LlamaLiteConfig.llama3_70b(max_seq_len=S + NEW)
+    if args.decode_layers != cfg.num_layers:
+        cfg = cfg.replace(num_layers=args.decode_layers)
+    t0 = time.time()
+    shard_of = args.decode_shard_of or None
+    srv = LlamaTPServe(cfg, max_batch=B, max_len=S + NEW, block_size=64, seed=0, shard_of=shard_of)
+    torch.cuda.synchronize()
+    log(f"{bdist.rank_prefix()} 70B-shape TP={world} shard ready in {time.time() - t0:.1f}s, "
+        f"mem {torch.cuda.memory_allocated() / 2**30:.1f} GiB")
+    prompts = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(1))
+    warm = max(3, args.warmup)
+    timed = NEW - 1 - warm
+    if timed < 1:
+        raise ValueError("--new-tokens must exceed warm-up + 1")
+
+    def max_over_ranks(v):
+        t = torch.tensor([v], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-timed: prefill, then `warm` steps (1 eager + replays), then `timed` replays
+    dev_prompts = prompts.to(dev)
+    bdist.barrier()
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    srv.prefill(dev_prompts)
+    p1.record()
+    srv.step()
+    srv.capture()
+    for _ in range(warm - 1):
+        srv.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    time.sleep(0.3)
+    bdist.barrier()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(timed):
+        srv.replay()
+    s1.record()
+    torch.cuda.synchronize()
+    bdist.barrier()
+    clk = clocks.stop() if clocks else None
+    srv.check()
+    ms = max_over_ranks(s0.elapsed_time(s1) / timed)
+    prefill_ms = max_over_ranks(p0.elapsed_time(p1))
+    tokens = srv.hist[:, :S + NEW].cpu()
+
+    # ---- end to end through the public API: pinned prompt upload, generate, tokens back to the host
+    e2e = None
+    if not args.no_e2e:
+        pinned = prompts.pin_memory()
+        bdist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = srv.generate(pinned.to(dev, non_blocking=True), NEW, use_graph=True)
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+        e2e = {"value": B * NEW / (e2e_ms / 1e3), "unit": "generated tokens/s (prefill included)",
+               "ms_total": e2e_ms, "h2d_bytes_per_step": B * S * 8 / NEW, "d2h_bytes_per_step": B * (S + NEW) * 8 / NEW,
+               "api": "brain_b200.models.llama_tp.LlamaTPServe.generate",
+               "same_tokens_as_timed_run": bool(torch.equal(out, tokens.long()))}
+    avg_len = S + 1 + warm + timed / 2
+    hbm = decode_bytes_per_step(cfg, shard_of or world, B, avg_len)
+    res = {
+        "metric": "decode tok/s Llama-3-70B-shape TP=N", "value": B / (ms / 1e3), "unit": "tokens/s",
+        "ms_per_step": ms, "n_gpus": world, "steps": timed, "warmup": warm, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic prompts (uniform tokens, seeded); random-init N(0,0.02) weights",
+        "config": {"model": "Llama-3-70B-shape" + ("" if cfg.num_layers == 80 else f" ({cfg.num_layers} layers: NOT the benchmark)"),
+                   "batch": B, "prompt_len": S, "new_tokens": NEW,
+                   "parallelism": f"tp{world}" if not shard_of else f"one rank's shard of tp{shard_of} (NOT the benchmark)",
+                   "kv_cache": "paged, block 64", "decode_step": "one CUDA graph of hand-written kernels",
+                   "l2": "no flush: each step streams the rank's weights (>> 126 MB L2)"},
+        "prefill_ms": prefill_ms, "prefill_tok_s": B * S / (prefill_ms / 1e3),
+        "hbm_bytes_per_step_per_gpu": hbm, "hbm_gbs_achieved": hbm / (ms / 1e3) / 1e9,
+        "clocks": clk, "e2e": e2e, "gpu_launches": srv.launches_per_step() * timed, "impl": "brain",
+    }
+    srv.close()
+    del srv
+    return res
 
 
 if __name__ == "__main__":

@@ -22,7 +22,8 @@ namespace {
 
 constexpr int kBlock = 64;    // tokens per KV block handled per step (pool block_size must divide by it or equal it)
 constexpr int kThreads = 128;
-constexpr int kMaxG = 16;     // query heads per kv head supported
+constexpr int kWarpsDec = kThreads / 32;
+constexpr int kMaxG = 16;     // query heads per kv head supported (the M = 16 side of the MMA tiles)
 
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
   const int n = valid ? 16 : 0;
@@ -49,8 +50,57 @@ struct DecodeArgs {
   float* part_ml;  // [B, Hkv, splits, G, 2]
 };
 
+// ---- warp-level tensor-core helpers (mma.sync m16n8k16 bf16 -> f32, ldmatrix from swizzled rows)
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Byte offset of 16-byte unit `c` of row `r` in a [rows][D] bf16 tile whose units are XOR-swizzled
+// by (r & 7), so the 8 rows an ldmatrix reads at one column hit 8 different bank groups.
+template <int D>
+__device__ __forceinline__ uint32_t swz(int r, int c) {
+  return (uint32_t)(r * (D * 2) + ((c ^ (r & 7)) << 4));
+}
+
+constexpr int kStages = 3;  // K/V chunks in flight per CTA
+
+template <int D>
+struct DecSmem {
+  static constexpr int CHUNK = kBlock * D * 2;         // one K or V chunk
+  static constexpr int STAGE = 2 * CHUNK;              // K + V
+  static constexpr int Q_OFF = kStages * STAGE;        // Q tile [16][D] bf16, swizzled
+  static constexpr int TOTAL = Q_OFF + kMaxG * D * 2;  // merge scratch reuses the stages
+};
+
+// One CTA = (sequence b, kv head hk, split): the GQA group's G <= 16 query heads form the M = 16 side
+// of mma.sync tiles, so the 4 warps compute S = Q K^T and O += P V on tensor cores; warp w owns keys
+// [16 w, 16 w + 16) of every 64-key chunk with its own online-softmax state, and the warps merge
+// at the end. K/V chunks stream through a 3-stage cp.async ring gathered through the block table.
 template <int D>
 __global__ void __launch_bounds__(kThreads) decode_split_kernel(DecodeArgs a) {
+  using S = DecSmem<D>;
+  constexpr int DU = D / 8;  // 16-byte units per row
+  pdl_trigger();
+  pdl_wait();
   const int split = blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / a.Hkv, hk = bh % a.Hkv;
@@ -60,137 +110,187 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(DecodeArgs a) {
   const int per = (nchunks + a.splits - 1) / a.splits;
   const int c0 = split * per, c1 = min(nchunks, c0 + per);
 
-  extern __shared__ __align__(16) uint8_t dsmem[];  // K and V double buffers (2 x 2 x kBlock x D bf16)
-  auto sK = reinterpret_cast<__nv_bfloat16 (*)[kBlock][D]>(dsmem);
-  auto sV = reinterpret_cast<__nv_bfloat16 (*)[kBlock][D]>(dsmem + 2 * kBlock * D * 2);
-  __shared__ float sQ[kMaxG][D];
-  __shared__ float sP[kMaxG][kBlock];
-  __shared__ float sRedMax[kMaxG][2], sRedSum[kMaxG][2];
-  __shared__ float sM[kMaxG], sL[kMaxG], sAlpha[kMaxG];
+  extern __shared__ __align__(128) uint8_t dsmem[];
+  const uint32_t sbase = smem_u32(dsmem);
+  const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
 
-  const int tid = threadIdx.x;
-  for (int i = tid; i < G * D; i += kThreads) {
-    const int g = i / D, d = i % D;
-    sQ[g][d] = __bfloat162float(a.q[(int64_t)b * a.qb + (int64_t)(hk * G + g) * a.qh + d]) * a.scale_log2;
+  // Q (rows >= G zero) -> swizzled smem -> A fragments held for the whole kernel
+  for (int i = tid; i < kMaxG * DU; i += kThreads) {
+    const int g = i / DU, c = i % DU;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (g < G) v = *reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.qb + (int64_t)(hk * G + g) * a.qh + c * 8);
+    *reinterpret_cast<uint4*>(dsmem + S::Q_OFF + swz<D>(g, c)) = v;
   }
-  if (tid < G) {
-    sM[tid] = -INFINITY;
-    sL[tid] = 0.f;
-  }
-  // output accumulator: thread owns (g = tid / (D/8) ... ) 8 consecutive dims of one head
-  constexpr int DV = D / 8;              // 8-dim groups per head
-  const int og = tid / DV, od = (tid % DV) * 8;
-  const int outs_per_pass = kThreads / DV;  // heads covered per pass
-  float acc[2][8];
-#pragma unroll
-  for (int p = 0; p < 2; ++p)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) acc[p][j] = 0.f;
 
-  auto load_chunk = [&](int c, int buf) {
+  auto load_chunk = [&](int c, int stage) {
     const int tok0 = c * kBlock;
-    for (int i = tid; i < kBlock * (D / 8); i += kThreads) {
-      const int t = i / (D / 8), dv = (i % (D / 8)) * 8;
+    const uint32_t ks = sbase + stage * S::STAGE, vs = ks + S::CHUNK;
+    for (int i = tid; i < kBlock * DU; i += kThreads) {
+      const int t = i / DU, u = i % DU;
       const int tok = tok0 + t;
       const bool ok = tok < len;
       int64_t off = 0;
       if (ok) {
         const int blk = a.table[(int64_t)b * a.max_blocks + tok / a.block_size];
-        off = ((int64_t)blk * a.block_size + tok % a.block_size) * a.Hkv * D + (int64_t)hk * D + dv;
+        off = ((int64_t)blk * a.block_size + tok % a.block_size) * a.Hkv * D + (int64_t)hk * D + u * 8;
       }
-      cp_async16(smem_u32(&sK[buf][t][dv]), a.kp + off, ok);
-      cp_async16(smem_u32(&sV[buf][t][dv]), a.vp + off, ok);
+      cp_async16(ks + swz<D>(t, u), a.kp + off, ok);
+      cp_async16(vs + swz<D>(t, u), a.vp + off, ok);
     }
   };
-  __syncthreads();
-  if (c0 < c1) load_chunk(c0, 0);
-  cp_commit();
-  for (int c = c0; c < c1; ++c) {
-    const int buf = (c - c0) & 1;
-    if (c + 1 < c1) load_chunk(c + 1, buf ^ 1);
+#pragma unroll
+  for (int j = 0; j < kStages - 1; ++j) {
+    if (c0 + j < c1) load_chunk(c0 + j, j);
     cp_commit();
-    cp_wait<1>();
-    __syncthreads();
-    // scores: thread -> key (tid % 64), heads (tid / 64) * ... covering G heads in two halves
-    {
-      const int key = tid % kBlock;
-      const int gstart = tid / kBlock;  // 0 or 1
-      const bool kvalid = c * kBlock + key < len;
-      for (int g = gstart; g < G; g += kThreads / kBlock) {
-        float s = 0.f;
-#pragma unroll 8
-        for (int d = 0; d < D; d += 8) {
-          float kf[8];
-          load8(&sK[buf][key][d], kf);
+  }
+  __syncthreads();
+  uint32_t qa[D / 16][4];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) s += sQ[g][d + j] * kf[j];
-        }
-        sP[g][key] = kvalid ? s : -INFINITY;
-      }
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int row = (lane & 7) + ((lane >> 3) & 1) * 8, unit = kk * 2 + (lane >> 4);
+    ldsm_x4(sbase + S::Q_OFF + swz<D>(row, unit), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
+  }
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};  // rows lane/4 and lane/4 + 8
+  const int kw = warp * 16;                                     // this warp's keys inside a chunk
+
+  for (int c = c0; c < c1; ++c) {
+    cp_wait<kStages - 2>();
+    __syncthreads();  // chunk c landed; every warp is done with chunk c - 1's stage
+    if (c + kStages - 1 < c1) load_chunk(c + kStages - 1, (c - c0 + kStages - 1) % kStages);
+    cp_commit();
+    const uint32_t ks = sbase + ((c - c0) % kStages) * S::STAGE, vs = ks + S::CHUNK;
+    // S[16 x 16] = Q K^T over this warp's 16 keys (two n8 tiles)
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t b0, b1, b2, b3;
+      const int key = kw + (lane & 7) + (lane >> 4) * 8, unit = kk * 2 + ((lane >> 3) & 1);
+      ldsm_x4(ks + swz<D>(key, unit), b0, b1, b2, b3);
+      mma_bf16(sc[0], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
+      mma_bf16(sc[1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
     }
-    __syncthreads();
-    // online softmax per head (one warp per head, looping)
-    {
-      const int warp = tid / 32, lane = tid % 32;
-      for (int g = warp; g < G; g += kThreads / 32) {
-        float m = fmaxf(sP[g][lane], sP[g][lane + 32]);
-        m = warp_max(m);
-        const float mold = sM[g];
-        const float mnew = fmaxf(mold, m);
-        const float muse = mnew == -INFINITY ? 0.f : mnew;
-        const float p0 = ex2_fast(sP[g][lane] - muse), p1 = ex2_fast(sP[g][lane + 32] - muse);
-        sP[g][lane] = p0;
-        sP[g][lane + 32] = p1;
-        const float s = warp_sum(p0 + p1);
-        if (lane == 0) {
-          const float al = ex2_fast(mold - muse);
-          sAlpha[g] = al;
-          sL[g] = sL[g] * al + s;
-          sM[g] = mnew;
-        }
+    // online softmax (base 2) for rows r0 = lane/4 and r1 = r0 + 8
+    const int kbase = c * kBlock + kw + (lane & 3) * 2;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < 2; ++n)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const bool valid = kbase + n * 8 + (j & 1) < len;
+        sc[n][j] = valid ? sc[n][j] * a.scale_log2 : -INFINITY;
+        mx[j >> 1] = fmaxf(mx[j >> 1], sc[n][j]);
       }
+    float alpha[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      const float mnew = fmaxf(m_r[r], mx[r]);
+      const float muse = mnew == -INFINITY ? 0.f : mnew;
+      alpha[r] = ex2_fast(m_r[r] - muse);
+      m_r[r] = mnew;
+      mx[r] = muse;
     }
-    __syncthreads();
-    // O = alpha O + P V
+    float ps[2] = {0.f, 0.f};
 #pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const int g = og + p * outs_per_pass;
-      if (g < G) {
-        const float al = sAlpha[g];
+    for (int n = 0; n < 2; ++n)
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[p][j] *= al;
-        for (int t = 0; t < kBlock; ++t) {
-          const float pv = sP[g][t];
-          float vf[8];
-          load8(&sV[buf][t][od], vf);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) acc[p][j] += pv * vf[j];
-        }
+      for (int j = 0; j < 4; ++j) {
+        sc[n][j] = ex2_fast(sc[n][j] - mx[j >> 1]);
+        ps[j >> 1] += sc[n][j];
       }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) l_r[r] = l_r[r] * alpha[r] + ps[r];
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      o[n][0] *= alpha[0];
+      o[n][1] *= alpha[0];
+      o[n][2] *= alpha[1];
+      o[n][3] *= alpha[1];
     }
-    __syncthreads();
+    // O[16 x D] += P[16 x 16] V[16 x D]; P's accumulator layout is the A fragment of k16
+    const uint32_t pa0 = pack_bf16(sc[0][0], sc[0][1]), pa1 = pack_bf16(sc[0][2], sc[0][3]);
+    const uint32_t pa2 = pack_bf16(sc[1][0], sc[1][1]), pa3 = pack_bf16(sc[1][2], sc[1][3]);
+#pragma unroll
+    for (int n2 = 0; n2 < D / 16; ++n2) {
+      uint32_t b0, b1, b2, b3;
+      const int key = kw + (lane & 7) + ((lane >> 3) & 1) * 8, unit = n2 * 2 + (lane >> 4);
+      ldsm_x4_t(vs + swz<D>(key, unit), b0, b1, b2, b3);
+      mma_bf16(o[2 * n2], pa0, pa1, pa2, pa3, b0, b1);
+      mma_bf16(o[2 * n2 + 1], pa0, pa1, pa2, pa3, b2, b3);
+    }
   }
   cp_wait<0>();
-  // write the split's partial state
-  const int64_t base = (((int64_t)b * a.Hkv + hk) * a.splits + split) * G;
+  __syncthreads();  // stages free: reuse them as merge scratch
+
+  // ---- merge the 4 warps: row max over warps, rescale, sum O and l
 #pragma unroll
-  for (int p = 0; p < 2; ++p) {
-    const int g = og + p * outs_per_pass;
-    if (g < G) {
-      float* o = a.part_o + (base + g) * D + od;
+  for (int r = 0; r < 2; ++r) {
+    l_r[r] += __shfl_xor_sync(0xffffffffu, l_r[r], 1);
+    l_r[r] += __shfl_xor_sync(0xffffffffu, l_r[r], 2);
+  }
+  float* sm = reinterpret_cast<float*>(dsmem);                 // [4 warps][16 rows] max
+  float* sl = sm + kWarpsDec * kMaxG;                          // [4 warps][16 rows] sum
+  float* so = sl + kWarpsDec * kMaxG;                          // [4 warps][16][D] output
+  const int r0 = lane >> 2;
+  if ((lane & 3) == 0) {
+    sm[warp * kMaxG + r0] = m_r[0];
+    sm[warp * kMaxG + r0 + 8] = m_r[1];
+  }
+  __syncthreads();
 #pragma unroll
-      for (int j = 0; j < 8; ++j) o[j] = acc[p][j];
+  for (int r = 0; r < 2; ++r) {
+    const int row = r0 + 8 * r;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarpsDec; ++w) M = fmaxf(M, sm[w * kMaxG + row]);
+    const float f = m_r[r] == -INFINITY ? 0.f : ex2_fast(m_r[r] - M);
+    l_r[r] *= f;
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      o[n][2 * r] *= f;
+      o[n][2 * r + 1] *= f;
     }
   }
+  if ((lane & 3) == 0) {
+    sl[warp * kMaxG + r0] = l_r[0];
+    sl[warp * kMaxG + r0 + 8] = l_r[1];
+  }
+#pragma unroll
+  for (int n = 0; n < D / 8; ++n) {
+    const int col = n * 8 + (lane & 3) * 2;
+    *reinterpret_cast<float2*>(so + (warp * kMaxG + r0) * D + col) = make_float2(o[n][0], o[n][1]);
+    *reinterpret_cast<float2*>(so + (warp * kMaxG + r0 + 8) * D + col) = make_float2(o[n][2], o[n][3]);
+  }
+  __syncthreads();
+  const int64_t base = (((int64_t)b * a.Hkv + hk) * a.splits + split) * G;
+  for (int i = tid; i < G * D; i += kThreads) {
+    const int g = i / D, d = i % D;
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarpsDec; ++w) v += so[(w * kMaxG + g) * D + d];
+    a.part_o[(base + g) * D + d] = v;
+  }
   if (tid < G) {
-    a.part_ml[(base + tid) * 2] = sM[tid];
-    a.part_ml[(base + tid) * 2 + 1] = sL[tid];
+    float M = -INFINITY, L = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarpsDec; ++w) M = fmaxf(M, sm[w * kMaxG + tid]);
+#pragma unroll
+    for (int w = 0; w < kWarpsDec; ++w) L += sl[w * kMaxG + tid];
+    a.part_ml[(base + tid) * 2] = M;
+    a.part_ml[(base + tid) * 2 + 1] = L;
   }
 }
 
 // out[b, h, :] = sum_s w_s o_s / sum_s w_s l_s with w_s = exp2(m_s - max_s m_s)   (one warp per (b, h))
 template <int D>
 __global__ void decode_combine_kernel(DecodeArgs a, __nv_bfloat16* out, int64_t ob, int64_t oh) {
+  pdl_trigger();
+  pdl_wait();
   const int64_t wid = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (wid >= (int64_t)a.B * a.Hq) return;
@@ -255,6 +355,30 @@ __global__ void kv_append_rope_kernel(__nv_bfloat16* qkv, int64_t ld, int B, int
   }
 }
 
+template <int D>
+int launch_decode(const DecodeArgs& a, void* out, int64_t ob, int64_t oh, cudaStream_t st) {
+  constexpr int dyn = DecSmem<D>::TOTAL;
+  static bool attr[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
+    if (e != cudaSuccess) return (int)e;
+    // largest shared-memory carveout: two ~100 KB CTAs per SM
+    e = cudaFuncSetAttribute(decode_split_kernel<D>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             (int)cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return (int)e;
+    attr[dev & 63] = true;
+  }
+  const bool pdl = brain_host::g_decode_pdl != 0;
+  cudaError_t e = brain_host::launch(decode_split_kernel<D>, dim3(a.splits, a.B * a.Hkv), dim3(kThreads), dyn, st,
+                                     pdl, a);
+  if (e != cudaSuccess) return (int)e;
+  const int64_t warps = (int64_t)a.B * a.Hq;
+  return (int)brain_host::launch(decode_combine_kernel<D>, dim3((unsigned)((warps + 3) / 4)), dim3(128), 0, st, pdl,
+                                 a, reinterpret_cast<__nv_bfloat16*>(out), ob, oh);
+}
+
 }  // namespace
 
 BRAIN_STATUS_READER(attention_decode)
@@ -267,7 +391,7 @@ BRAIN_API int64_t brain_decode_workspace(int B, int Hq, int Hkv, int D, int spli
 // Pick a split count so that B * Hkv * splits fills the GPU (about two CTAs per SM).
 BRAIN_API int brain_decode_splits(int B, int Hkv, int max_len) {
   const int ctas = B * Hkv;
-  int want = (2 * brain_host::num_sms() + ctas - 1) / (ctas > 0 ? ctas : 1);
+  int want = (2 * brain_host::num_sms()) / (ctas > 0 ? ctas : 1);  // one wave at two CTAs per SM
   const int chunks = (max_len + kBlock - 1) / kBlock;
   if (want > chunks) want = chunks;
   return want < 1 ? 1 : want;
@@ -291,24 +415,8 @@ BRAIN_API int brain_decode_attention(const void* q, int64_t qb, int64_t qh, cons
   a.splits = splits;
   a.part_o = workspace;
   a.part_ml = workspace + (int64_t)B * Hq * splits * D;
-  dim3 grid(splits, B * Hkv);
-  const int64_t warps = (int64_t)B * Hq;
-  const int dyn = 4 * kBlock * D * 2;
-  if (D == 64) {
-    decode_split_kernel<64><<<grid, kThreads, dyn, st>>>(a);
-    decode_combine_kernel<64><<<(unsigned)((warps + 3) / 4), 128, 0, st>>>(a, reinterpret_cast<__nv_bfloat16*>(out), ob, oh);
-  } else {
-    static bool attr[64] = {false};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (!attr[dev & 63]) {
-      cudaFuncSetAttribute(decode_split_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
-      attr[dev & 63] = true;
-    }
-    decode_split_kernel<128><<<grid, kThreads, dyn, st>>>(a);
-    decode_combine_kernel<128><<<(unsigned)((warps + 3) / 4), 128, 0, st>>>(a, reinterpret_cast<__nv_bfloat16*>(out), ob, oh);
-  }
-  return (int)cudaGetLastError();
+  if (B * Hkv > 65535) return (int)cudaErrorInvalidValue;
+  return D == 64 ? launch_decode<64>(a, out, ob, oh, st) : launch_decode<128>(a, out, ob, oh, st);
 }
 
 BRAIN_API int brain_kv_append_rope(void* qkv, int64_t ld, int B, int Hq, int Hkv, int D, const int* pos,

@@ -300,6 +300,13 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
 }
 __device__ __forceinline__ void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// 32 lanes x 4 columns.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t* r) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+
 // 32 lanes x 16 columns.
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
   asm volatile(
@@ -364,9 +371,39 @@ int num_sms();
 // cuTensorMapEncodeTiled resolved through the runtime's driver entry point (no -lcuda needed).
 bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, void* base, const uint64_t* dims,
                   const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz);
+
+// Decode-step kernels launch with programmatic dependent launch while this is non-zero
+// (brain_decode_set_pdl; defined in decode_tp.cu).
+extern int g_decode_pdl;
+
+// Launch with programmatic stream serialization when `pdl` (the kernel must follow the pdl_wait()
+// contract above); a CUDA-graph capture records it as a programmatic dependency edge.
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                   Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 }  // namespace brain_host
 
 namespace brain {
+// Programmatic dependent launch. A kernel launched with programmatic stream serialization may start
+// while its predecessor in the stream is still running. It must call pdl_wait() before it touches
+// anything the predecessor writes (or reads and the kernel overwrites); pdl_wait() returns once the
+// predecessor grid has completed and its memory is visible. pdl_trigger() lets the successor launch
+// early. Both are no-ops for a normal launch.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // System-scope flag store / load (peer GPUs observe them over NVLink in release/acquire order).
 __device__ __forceinline__ void sys_st_release(int* addr, int v) {
   asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");

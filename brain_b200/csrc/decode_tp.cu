@@ -3,31 +3,39 @@
 // 1. skinny_gemm: out[M, N] = x[M, K] * W[N, K]^T with the operands swapped on the tensor core: the
 //    weight supplies the 128-row MMA M side and the tokens the N side (NT = 16 / 32 / 64), so a
 //    128 x NT f32 accumulator lives in TMEM while the weight streams through a TMA ring at HBM rate
-//    (decode is bound by reading the weights once per step). K is split over `splits` CTAs per
-//    128-row tile so every SM streams; the partial tiles meet in an f32 workspace and the last CTA of
-//    a tile (atomic ticket) sums them in split order (deterministic) and runs one of the epilogues:
+//    (decode is bound by reading the weights once per step). K is split over a cluster of `splits`
+//    (<= 8) CTAs per 128-row tile so every SM streams. The split-K reduction runs in distributed
+//    shared memory: CTA r finishes tokens [r * tper, (r + 1) * tper); every CTA stores its partials
+//    for those tokens straight into CTA r's receive buffer (remote shared-memory stores), one cluster
+//    barrier, then CTA r sums them in rank order (deterministic, no workspace, no atomics) and runs
+//    one of the epilogues for its tokens over all 128 rows of the tile:
 //      EPI_STORE   bf16 out (+ residual)
 //      EPI_PUSH    all-reduce push: the bf16 partial product goes to slot `rank` of every rank's
-//                  receive buffer over NVLink; the last tile to finish publishes the step's epoch in
-//                  every rank's flag word (release, system scope)
+//                  receive buffer over NVLink, then the CTA adds its arrival to every rank's counter
+//                  (red.release.sys, no round trip)
 //      EPI_SWIGLU  weight rows interleaved in 64-row groups [gate 64 | up 64]; writes silu(gate) * up
 //      EPI_QKV     one tile = one head of the fused [q | k | v] projection (head_dim 128): RoPE on
 //                  q / k at each token's position, q to `out`, k / v straight into their paged slots
 //      EPI_ARGMAX  greedy LM head: the per-token max over the tile's vocabulary rows folds into a
-//                  64-bit (value, -index) key with atomicMax; the last tile pushes the keys to every
-//                  rank and publishes the epoch
-// 2. ar_norm: waits for the epoch flags of all ranks, sums the `world` bf16 slots of a token row in
-//    f32, adds the residual stream (updated in place) and writes RMSNorm(h) * gamma for the next GEMM.
+//                  64-bit (value, -index) key with atomicMax; the last CTA (ticket) pushes the keys to
+//                  every rank and adds the whole push's arrivals
+//    The first weight stages are requested before the kernel waits for its predecessor
+//    (programmatic dependent launch), so the weight stream starts while the previous kernel ends.
+// 2. ar_norm: waits for every rank's arrivals, sums the `world` bf16 slots of a token row in f32,
+//    adds the residual stream (updated in place) and writes RMSNorm(h) * gamma for the next GEMM.
 // 3. pick_embed: waits for the argmax keys of all ranks, picks the token (lowest index on ties),
 //    records it, advances the positions, gathers its embedding row into the residual stream and
 //    RMS-normalises it for layer 0 of the next step.
 //
-// Epochs live in device memory (ctrl[0]) so a whole decode step can be captured in one CUDA graph
-// and replayed: the producer reads e = ctrl[0] + 1, writes slot parity e & 1, and its last tile
-// stores ctrl[0] = e before it publishes e to the peers' flags; the consumer reads ctrl[0] and waits
-// until every flag is >= e. Two parities suffice: a rank reaches epoch e + 2 only after every peer
-// published epoch e + 1, which each peer does after it consumed epoch e. Every wait is bounded and
-// reports through the status word.
+// Synchronisation state lives in device memory, so a whole decode step is one replayable CUDA graph:
+//   ctrl[0] = last epoch consumed (written by consumers), ctrl[1] = last epoch produced (written by
+//   producers), ctrl[2] = argmax ticket. A producer computes e = ctrl[0] + 1, writes slot parity e & 1
+//   and stores ctrl[1] = e; the consumer reads e = ctrl[1] and stores ctrl[0] = e. Each push adds
+//   exactly kArrivals to counter [e & 1][rank] of every rank (each CTA adds 1, CTA 0 also adds the
+//   remainder), so the consumer of epoch e waits until every counter of parity e & 1 reaches
+//   kArrivals * ((e + 1) / 2) (compared modulo 2^32). Two parities suffice: a rank reaches epoch
+//   e + 2 only after every peer's epoch e + 1 push, which each peer issues after consuming epoch e.
+//   Every wait is bounded and reports through the status word.
 //
 // Reference: the reference's TensorParallelLinear::forward returns zeros
 // (crates/brain-distributed/src/tensor_parallel.rs:8-27) and LlamaLite::generate re-runs the full
@@ -45,28 +53,27 @@ constexpr int kRows = 128;
 constexpr int kBK = 64;
 constexpr int kThreads = 128;
 constexpr int kMaxWorld = 8;
+constexpr int kMaxSplits = 8;        // portable cluster size
+constexpr uint32_t kArrivals = 4096;  // counter increment per push (>= CTAs of any push)
 
 enum Epi : int { EPI_STORE = 0, EPI_PUSH = 2, EPI_SWIGLU = 3, EPI_QKV = 4, EPI_ARGMAX = 5 };
 
 struct SkinnyArgs {
   int M, N, K;
   int num_kb, kb_per_split, splits;
-  int epi;
   float alpha;
   __nv_bfloat16* out;
   int64_t ldc;
   const __nv_bfloat16* R;
   int64_t ldr;
-  float* ws;
-  int* tile_cnt;
   // EPI_PUSH / EPI_ARGMAX
   int world, rank;
   int64_t slot_elems;
-  int* ctrl;                 // [0] epoch, [1] finished-tile count
+  int* ctrl;                 // [0] epoch consumed, [1] epoch produced, [2] argmax ticket
   unsigned long long* keys;  // EPI_ARGMAX running keys [M], zero between steps
   int64_t vocab_offset;
   void* peer_slots[kMaxWorld];
-  int* peer_flags[kMaxWorld];
+  unsigned int* peer_flags[kMaxWorld];  // each rank's counters [2 parities][kMaxWorld]
   // EPI_QKV
   int hq, hkv;
   const int* pos;
@@ -74,6 +81,8 @@ struct SkinnyArgs {
   __nv_bfloat16 *kpool, *vpool;
   const int* table;
   int max_blocks, block_size;
+  // optional per-CTA phase timestamps (globaltimer ns), [cta][8]; null = off
+  unsigned long long* trace;
 };
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int64_t idx) {
@@ -84,13 +93,33 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int64_t idx) {
 
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
-// Publish epoch e: every rank's flag[rank] = e (after this CTA's and, by the ticket, all other
-// tiles' pushed stores).
-__device__ __forceinline__ void publish_epoch(const SkinnyArgs& a, int e) {
-  a.ctrl[1] = 0;
-  a.ctrl[0] = e;
-  __threadfence_system();
-  for (int r = 0; r < a.world; ++r) sys_st_release(a.peer_flags[r] + a.rank, e);
+// f32 load from / store to the shared memory of a CTA of this cluster (address from mapa_shared).
+__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  return v;
+}
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v));
+}
+
+// Arrival on a (possibly remote) counter, ordered after the writes that happen before it.
+__device__ __forceinline__ void red_release_add(unsigned int* addr, unsigned int v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* addr) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// This CTA's arrivals for epoch e on every rank: one per CTA, plus the remainder up to kArrivals
+// from CTA 0 (so each push adds exactly kArrivals whatever its grid).
+__device__ __forceinline__ void arrive_all(const SkinnyArgs& a, int e, unsigned int inc) {
+  for (int r = 0; r < a.world; ++r) {
+    const int dst = (a.rank + 1 + r) % a.world;  // stagger the peers
+    red_release_add(a.peer_flags[dst] + (e & 1) * kMaxWorld + a.rank, inc);
+  }
 }
 
 template <int NT, int STAGES>
@@ -98,11 +127,13 @@ struct SkSmem {
   static constexpr uint32_t W_BYTES = kRows * kBK * 2;
   static constexpr uint32_t X_BYTES = NT * kBK * 2;
   static constexpr uint32_t STAGE = W_BYTES + X_BYTES;
-  static constexpr uint32_t BAR = STAGES * STAGE;
+  static constexpr uint32_t RECV = STAGES * STAGE;                  // [splits][tper][128] f32
+  static constexpr uint32_t RECV_BYTES = (NT + kMaxSplits) * kRows * 4;
+  static constexpr uint32_t BAR = RECV + RECV_BYTES;
   static constexpr uint32_t TOTAL = BAR + (2 * STAGES + 2) * 8 + 16 + 1024;
 };
 
-template <int NT, int STAGES>
+template <int NT, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_constant__ CUtensorMap tmW,
                                                                const __grid_constant__ CUtensorMap tmX,
                                                                const SkinnyArgs a) {
@@ -119,8 +150,12 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* ticket = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
+  pdl_trigger();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int split = blockIdx.x, tile = blockIdx.y;
+  unsigned long long* trace =
+      a.trace && threadIdx.x == 0 ? a.trace + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * 16 : nullptr;
+  if (trace) trace[0] = globaltimer();
   const int kb0 = split * a.kb_per_split;
   const int nkb = min(a.num_kb - kb0, a.kb_per_split);
   constexpr uint32_t kCols = NT < 32 ? 32 : NT;
@@ -145,10 +180,22 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (trace) trace[1] = globaltimer();
 
   if (warp == 0 && lane == 0) {
-    // ---- TMA producer: weight tile [128 rows, 64 k] and token tile [NT, 64 k] per stage
-    int i = 0;
+    // ---- TMA producer: weight tile [128 rows, 64 k] and token tile [NT, 64 k] per stage. The
+    // weights are never written by a predecessor, so the first ring of weight tiles is requested
+    // before pdl_wait(): under programmatic launch it streams while the previous kernel finishes.
+    const int pre = nkb < STAGES ? nkb : STAGES;
+    for (int j = 0; j < pre; ++j) {
+      mbar_arrive_expect_tx(full_bar(j), S::STAGE);
+      tma_load_2d(&tmW, sbase + j * S::STAGE, full_bar(j), (kb0 + j) * kBK, tile * kRows);
+    }
+    pdl_wait();
+    if (trace) trace[2] = globaltimer();
+    for (int j = 0; j < pre; ++j)
+      tma_load_2d(&tmX, sbase + j * S::STAGE + S::W_BYTES, full_bar(j), (kb0 + j) * kBK, 0);
+    int i = pre;
     bool ok = true;
     for (; i < nkb; ++i) {
       const int s = i % STAGES;
@@ -204,27 +251,40 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
   }
   __syncwarp();
 
-  // ---- accumulator -> registers (thread = weight row `row`, acc[t] = token t)
+  // The tail below runs once per CTA, so it is written as compact rolled loops: fully unrolled
+  // straight-line code here was dominated by cold instruction fetch.
   const bool ok = mbar_wait(done_bar, 0, BRAIN_ERR_TIMEOUT_ACC, 112, abort_flag);
   tc_fence_after();
+  if (trace) {
+    trace[3] = globaltimer();
+    trace[8] = clock64();
+  }
   const int row = warp * 32 + lane;
-  float acc[NT];
+  pdl_wait();  // predecessor complete: its writes (residual, epochs, cache, outputs) are visible
+  if (trace) trace[9] = clock64();
+
+  // ---- split-K reduction: TMEM columns (tokens) go straight to the CTA that finishes that token
+  const int nsplit = a.splits;
+  const int tper = (a.M + nsplit - 1) / nsplit;
+  const int t0 = split * tper;
+  const int nt = max(0, min(a.M - t0, tper));
+  float* recv = reinterpret_cast<float*>(smem + S::RECV);  // [nsplit][tper][128]
   {
     const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16);
-    if (NT == 16) {
-      uint32_t r[16];
-      tmem_ld16(taddr, r);
+    const uint32_t rbase = smem_u32(recv) + (uint32_t)((split * tper * kRows + row) * 4);
+#pragma unroll 1
+    for (int t = 0; t < a.M; t += 4) {
+      uint32_t r[4];
+      tmem_ld4(taddr + (uint32_t)t, r);
       tc_wait_ld();
 #pragma unroll
-      for (int t = 0; t < 16; ++t) acc[t] = ok ? __uint_as_float(r[t]) : 0.f;
-    } else {
-#pragma unroll
-      for (int c = 0; c < NT / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(taddr + c * 32, r);
-        tc_wait_ld();
-#pragma unroll
-        for (int t = 0; t < 32; ++t) acc[c * 32 + t] = ok ? __uint_as_float(r[t]) : 0.f;
+      for (int j = 0; j < 4; ++j) {
+        const int tt = t + j;
+        if (tt < a.M) {
+          const int dst = tt / tper;
+          st_dsmem_f32(mapa_shared(rbase + (uint32_t)((tt - dst * tper) * kRows * 4), (uint32_t)dst),
+                       ok ? __uint_as_float(r[j]) : 0.f);
+        }
       }
     }
   }
@@ -234,126 +294,113 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
     tc_fence_after();
     tmem_dealloc(tmem_base, kCols);
   }
-  if (!ok) return;
-
-  // ---- split-K fix-up: the last CTA of the tile sums the partials in split order
-  if (a.splits > 1) {
-    float* part = a.ws + ((int64_t)tile * a.splits + split) * NT * kRows;
-#pragma unroll
-    for (int t = 0; t < NT; ++t) part[t * kRows + row] = acc[t];
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      const int old = atomicAdd(a.tile_cnt + tile, 1);
-      *ticket = (old == a.splits - 1);
-      if (old == a.splits - 1) a.tile_cnt[tile] = 0;
-    }
-    __syncthreads();
-    if (!*ticket) return;
-    __threadfence();
-#pragma unroll
-    for (int t = 0; t < NT; ++t) acc[t] = 0.f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float* p = a.ws + ((int64_t)tile * a.splits + s) * NT * kRows;
-#pragma unroll
-      for (int t = 0; t < NT; ++t) acc[t] += __ldcg(p + t * kRows + row);
-    }
+  if (trace) trace[10] = clock64();
+  // A CTA whose pipeline gave up still joins the cluster barrier (with zero partials), so the other
+  // CTAs of its cluster never wait for it; the status word already records the failure.
+  cluster_sync();  // release / acquire: every partial for this CTA's tokens has landed
+  if (trace) {
+    trace[4] = globaltimer();
+    trace[11] = clock64();
   }
+  if (!ok) return;
+  auto reduced = [&](int i) {  // sum of the partials of local token i for this row, in rank order
+    float sum = 0.f;
+#pragma unroll 1
+    for (int r = 0; r < nsplit; ++r) sum += recv[(r * tper + i) * kRows + row];
+    return sum;
+  };
 
-  float* sx = reinterpret_cast<float*>(smem);  // stage memory is free once every MMA completed
+  float* sx = reinterpret_cast<float*>(smem);  // stage memory: free once every MMA completed
   const int n = tile * kRows + row;
-  if (a.epi == EPI_STORE) {
+  const int total_ctas = (int)(gridDim.x * gridDim.y);
+  if constexpr (EPI == EPI_STORE) {
     if (n < a.N) {
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (t < a.M) {
-          float v = acc[t] * a.alpha;
-          if (a.R) v += __bfloat162float(a.R[t * a.ldr + n]);
-          a.out[t * a.ldc + n] = __float2bfloat16_rn(v);
-        }
+#pragma unroll 1
+      for (int i = 0; i < nt; ++i) {
+        const int t = t0 + i;
+        float x = reduced(i) * a.alpha;
+        if (a.R) x += __bfloat162float(a.R[t * a.ldr + n]);
+        a.out[t * a.ldc + n] = __float2bfloat16_rn(x);
       }
     }
-  } else if (a.epi == EPI_PUSH) {
+  } else if constexpr (EPI == EPI_PUSH) {
     const int e = ld_volatile(a.ctrl) + 1;
     const int64_t off = ((int64_t)(e & 1) * a.world + a.rank) * a.slot_elems;
     if (n < a.N) {
-      for (int r = 0; r < a.world; ++r) {
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.peer_slots[r]) + off;
-#pragma unroll
-        for (int t = 0; t < NT; ++t)
-          if (t < a.M) dst[t * a.N + n] = __float2bfloat16_rn(acc[t] * a.alpha);
+#pragma unroll 1
+      for (int i = 0; i < nt; ++i) {
+        const __nv_bfloat16 x = __float2bfloat16_rn(reduced(i) * a.alpha);
+#pragma unroll 1
+        for (int r = 0; r < a.world; ++r)
+          reinterpret_cast<__nv_bfloat16*>(a.peer_slots[(a.rank + 1 + r) % a.world])[off + (t0 + i) * a.N + n] = x;
       }
     }
-    __threadfence_system();
-    __syncthreads();
+    __syncthreads();  // the CTA's pushed stores happen before thread 0's release arrivals
     if (threadIdx.x == 0) {
-      const int old = atomicAdd(a.ctrl + 1, 1);
-      if (old == (int)gridDim.y - 1) publish_epoch(a, e);
+      const unsigned int inc = (blockIdx.x == 0 && blockIdx.y == 0) ? 1u + kArrivals - (unsigned)total_ctas : 1u;
+      arrive_all(a, e, inc);
+      a.ctrl[1] = e;  // same value from every CTA; read by the consumer after this grid completes
     }
-  } else if (a.epi == EPI_SWIGLU) {
-    if (row >= 64) {
-#pragma unroll
-      for (int t = 0; t < NT; ++t) sx[t * 64 + row - 64] = acc[t];
-    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+    for (int i = 0; i < nt; ++i) sx[i * kRows + row] = reduced(i) * a.alpha;
     __syncthreads();
     const int j = tile * 64 + row;
     if (row < 64 && j < a.N / 2) {
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        if (t < a.M) {
-          const float g = acc[t] * a.alpha, u = sx[t * 64 + row] * a.alpha;
-          a.out[t * a.ldc + j] = __float2bfloat16_rn(g / (1.f + __expf(-g)) * u);
-        }
+#pragma unroll 1
+      for (int i = 0; i < nt; ++i) {
+        const float g = sx[i * kRows + row], u = sx[i * kRows + row + 64];
+        a.out[(t0 + i) * a.ldc + j] = __float2bfloat16_rn(g / (1.f + __expf(-g)) * u);
       }
     }
-  } else if (a.epi == EPI_QKV) {
-#pragma unroll
-    for (int t = 0; t < NT; ++t) sx[t * kRows + row] = acc[t];
+  } else if constexpr (EPI == EPI_QKV) {
+#pragma unroll 1
+    for (int i = 0; i < nt; ++i) sx[i * kRows + row] = reduced(i) * a.alpha;
     __syncthreads();
     const int h = tile, d = row, dj = row & 63;
     const bool rot = h < a.hq + a.hkv;
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      if (t < a.M) {
-        const int p = a.pos[t];
-        float x = acc[t] * a.alpha;
-        if (rot) {
-          const float y = sx[t * kRows + (row ^ 64)] * a.alpha;
-          const float c = a.cs[(int64_t)p * kRows + dj], s = a.cs[(int64_t)p * kRows + 64 + dj];
-          x = d < 64 ? x * c - y * s : x * c + y * s;
-        }
-        if (h < a.hq) {
-          a.out[t * a.ldc + h * kRows + d] = __float2bfloat16_rn(x);
-        } else {
-          const int64_t slot = (int64_t)a.table[(int64_t)t * a.max_blocks + p / a.block_size] * a.block_size +
-                               p % a.block_size;
-          __nv_bfloat16* pool = rot ? a.kpool : a.vpool;
-          const int hh = rot ? h - a.hq : h - a.hq - a.hkv;
-          pool[(slot * a.hkv + hh) * kRows + d] = __float2bfloat16_rn(x);
-        }
+    __nv_bfloat16* pool = rot ? a.kpool : a.vpool;
+    const int hh = rot ? h - a.hq : h - a.hq - a.hkv;
+#pragma unroll 1
+    for (int i = 0; i < nt; ++i) {
+      const int t = t0 + i;
+      const int p = a.pos[t];
+      float x = sx[i * kRows + row];
+      if (rot) {
+        const float y = sx[i * kRows + (row ^ 64)];
+        const float c = a.cs[(int64_t)p * kRows + dj], sn = a.cs[(int64_t)p * kRows + 64 + dj];
+        x = d < 64 ? x * c - y * sn : x * c + y * sn;
+      }
+      if (h < a.hq) {
+        a.out[t * a.ldc + h * kRows + d] = __float2bfloat16_rn(x);
+      } else {
+        const int64_t slot = (int64_t)a.table[(int64_t)t * a.max_blocks + p / a.block_size] * a.block_size +
+                             p % a.block_size;
+        pool[(slot * a.hkv + hh) * kRows + d] = __float2bfloat16_rn(x);
       }
     }
-  } else if (a.epi == EPI_ARGMAX) {
-    unsigned long long* red = reinterpret_cast<unsigned long long*>(smem);  // [4 warps][NT]
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      unsigned long long k = n < a.N ? argmax_key(acc[t] * a.alpha, a.vocab_offset + n) : 0ull;
+  } else if constexpr (EPI == EPI_ARGMAX) {
+    unsigned long long* kred = reinterpret_cast<unsigned long long*>(smem);  // [4 warps][NT]
+#pragma unroll 1
+    for (int i = 0; i < nt; ++i) {
+      const float x = reduced(i) * a.alpha;
+      unsigned long long k = n < a.N ? argmax_key(x, a.vocab_offset + n) : 0ull;
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const unsigned long long other = __shfl_xor_sync(0xffffffffu, k, o);
         k = other > k ? other : k;
       }
-      if (lane == 0) red[warp * NT + t] = k;
+      if (lane == 0) kred[warp * NT + i] = k;
     }
     __syncthreads();
-    if (threadIdx.x < a.M) {
-      unsigned long long k = red[threadIdx.x];
-      for (int w = 1; w < 4; ++w) k = red[w * NT + threadIdx.x] > k ? red[w * NT + threadIdx.x] : k;
-      atomicMax(a.keys + threadIdx.x, k);
+    if (threadIdx.x < nt) {
+      unsigned long long k = kred[threadIdx.x];
+      for (int w = 1; w < 4; ++w) k = kred[w * NT + threadIdx.x] > k ? kred[w * NT + threadIdx.x] : k;
+      atomicMax(a.keys + t0 + threadIdx.x, k);
     }
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) *ticket = (atomicAdd(a.ctrl + 1, 1) == (int)gridDim.y - 1);
+    if (threadIdx.x == 0) *ticket = (atomicAdd(a.ctrl + 2, 1) == total_ctas - 1);
     __syncthreads();
     if (*ticket) {
       __threadfence();
@@ -364,22 +411,32 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
         for (int r = 0; r < a.world; ++r)
           reinterpret_cast<unsigned long long*>(a.peer_slots[r])[off + threadIdx.x] = k;
       }
-      __threadfence_system();
       __syncthreads();
-      if (threadIdx.x == 0) publish_epoch(a, e);
+      if (threadIdx.x == 0) {
+        a.ctrl[2] = 0;
+        a.ctrl[1] = e;
+        arrive_all(a, e, kArrivals);
+      }
     }
+  }
+  if (trace) {
+    trace[6] = globaltimer();
+    trace[15] = clock64();
   }
 }
 
-// Wait (thread j < world) until flag j reaches the epoch in ctrl[0]; returns the epoch or -1.
-__device__ int wait_epoch(const int* flags, const int* ctrl, int world, int64_t budget_ns, int where) {
+// Consumer side: wait (thread j < world) until rank j's arrivals for the epoch produced last
+// (ctrl[1]) are complete. Returns the epoch, or -1 after the budget ran out.
+__device__ int wait_epoch(const unsigned int* flags, const int* ctrl, int world, int64_t budget_ns, int where) {
   __shared__ int s_e, s_bad;
   if (threadIdx.x == 0) s_bad = 0;
   __syncthreads();
-  const int e = ld_volatile(ctrl);
+  const int e = ld_volatile(ctrl + 1);
   if (threadIdx.x < world) {
+    const unsigned int target = kArrivals * (unsigned int)((e + 1) / 2);
+    const unsigned int* f = flags + (e & 1) * kMaxWorld + threadIdx.x;
     const uint64_t t0 = globaltimer();
-    while (sys_ld_acquire(flags + threadIdx.x) < e) {
+    while ((int)(ld_acquire_u32(f) - target) < 0) {
       if (globaltimer() - t0 > (uint64_t)budget_ns) {
         set_status(BRAIN_ERR_TIMEOUT_PEER, where * 16 + threadIdx.x);
         s_bad = 1;
@@ -393,7 +450,7 @@ __device__ int wait_epoch(const int* flags, const int* ctrl, int world, int64_t 
 }
 
 constexpr int kNormThreads = 256;
-constexpr int kMaxChunks = 8;  // N <= 256 * 8 * 8 = 16384
+constexpr int kMaxChunks = 8;  // pick_embed: N <= 256 * 8 * 8 = 16384
 
 __device__ __forceinline__ float block_sum(float v) {
   __shared__ float red[kNormThreads / 32];
@@ -407,56 +464,87 @@ __device__ __forceinline__ float block_sum(float v) {
 }
 
 // residual[row] += sum_j slot_j[row]; normed[row] = rmsnorm(residual[row]) * gamma.
-__global__ void __launch_bounds__(kNormThreads) ar_norm_kernel(const __nv_bfloat16* slots, const int* flags,
-                                                               const int* ctrl, int world, int64_t slot_elems, int N,
+// A cluster of kArParts CTAs shares one token row (each owns N / kArParts columns, one 8-element chunk
+// per thread for N = 8192); the row's sum of squares is combined through distributed shared memory.
+// The residual and gamma loads are issued before the wait for the peers' arrivals.
+constexpr int kArParts = 4;
+constexpr int kArChunks = 2;  // N <= kArParts * kNormThreads * 8 * kArChunks = 16384
+
+__global__ void __launch_bounds__(kNormThreads) ar_norm_kernel(const __nv_bfloat16* slots, const unsigned int* flags,
+                                                               int* ctrl, int world, int64_t slot_elems, int N,
                                                                __nv_bfloat16* resid, int64_t ldr,
                                                                const __nv_bfloat16* gamma, float eps,
                                                                __nv_bfloat16* normed, int64_t ldn,
                                                                int64_t budget_ns) {
-  const int row = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();
+  __shared__ float s_part;
+  const int part = blockIdx.x, row = blockIdx.y;
+  const int cols = N / kArParts;
+  float h[kArChunks][8], g[kArChunks][8];
+#pragma unroll
+  for (int c = 0; c < kArChunks; ++c) {
+    const int k = (c * kNormThreads + threadIdx.x) * 8;
+    if (k < cols) {
+      load8(resid + row * ldr + part * cols + k, h[c]);
+      load8(gamma + part * cols + k, g[c]);
+    }
+  }
   const int e = wait_epoch(flags, ctrl, world, budget_ns, 12);
-  if (e < 0) return;
-  const __nv_bfloat16* base = slots + (int64_t)(e & 1) * world * slot_elems + (int64_t)row * N;
-  float h[kMaxChunks][8];
+  const __nv_bfloat16* base = slots + (int64_t)(e & 1) * world * slot_elems + (int64_t)row * N + part * cols;
   float ss = 0.f;
+  if (e >= 0) {
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int i = (c * kNormThreads + threadIdx.x) * 8;
-    if (i < N) {
-      load8(resid + row * ldr + i, h[c]);
-      for (int j = 0; j < world; ++j) {
-        float f[8];
-        load8(base + j * slot_elems + i, f);
+    for (int c = 0; c < kArChunks; ++c) {
+      const int k = (c * kNormThreads + threadIdx.x) * 8;
+      if (k < cols) {
+        float f[kMaxWorld][8];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) h[c][u] += f[u];
-      }
-      store8(resid + row * ldr + i, h[c]);
+        for (int j = 0; j < kMaxWorld; ++j)
+          if (j < world) load8(base + j * slot_elems + k, f[j]);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        h[c][u] = __bfloat162float(__float2bfloat16_rn(h[c][u]));  // normalise the stored stream
-        ss += h[c][u] * h[c][u];
+        for (int j = 0; j < kMaxWorld; ++j)
+          if (j < world) {
+#pragma unroll
+            for (int u = 0; u < 8; ++u) h[c][u] += f[j][u];
+          }
+        store8(resid + row * ldr + part * cols + k, h[c]);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          h[c][u] = __bfloat162float(__float2bfloat16_rn(h[c][u]));  // normalise the stored stream
+          ss += h[c][u] * h[c][u];
+        }
       }
     }
   }
-  const float rstd = rsqrtf(block_sum(ss) / N + eps);
+  ss = block_sum(ss);
+  if (threadIdx.x == 0) s_part = ss;
+  cluster_sync();
+  float tot = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
-    const int i = (c * kNormThreads + threadIdx.x) * 8;
-    if (i < N) {
-      float g[8];
-      load8(gamma + i, g);
+  for (int r = 0; r < kArParts; ++r) tot += ld_dsmem_f32(mapa_shared(smem_u32(&s_part), (uint32_t)r));
+  cluster_sync();  // peers have read s_part
+  if (e < 0) return;
+  if (threadIdx.x == 0) ctrl[0] = e;  // same value from every CTA; read after this grid completes
+  const float rstd = rsqrtf(tot / N + eps);
 #pragma unroll
-      for (int u = 0; u < 8; ++u) g[u] *= h[c][u] * rstd;
-      store8(normed + row * ldn + i, g);
+  for (int c = 0; c < kArChunks; ++c) {
+    const int k = (c * kNormThreads + threadIdx.x) * 8;
+    if (k < cols) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) g[c][u] *= h[c][u] * rstd;
+      store8(normed + row * ldn + part * cols + k, g[c]);
     }
   }
 }
 
 // Greedy pick over the ranks' argmax keys, then the next step's layer-0 input.
 __global__ void __launch_bounds__(kNormThreads) pick_embed_kernel(
-    const unsigned long long* key_slots, const int* flags, const int* ctrl, int world, int64_t slot_elems,
+    const unsigned long long* key_slots, const unsigned int* flags, int* ctrl, int world, int64_t slot_elems,
     const __nv_bfloat16* emb, int64_t lde, int vocab, int N, __nv_bfloat16* resid, const __nv_bfloat16* gamma,
     float eps, __nv_bfloat16* normed, int* hist, int64_t hist_ld, int* pos, int* seq_lens, int64_t budget_ns) {
+  pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x;
   const int e = wait_epoch(flags, ctrl, world, budget_ns, 13);
   if (e < 0) return;
@@ -478,6 +566,7 @@ __global__ void __launch_bounds__(kNormThreads) pick_embed_kernel(
     pos[row] = p;
     seq_lens[row] = p + 1;
     s_tok = tok;
+    ctrl[0] = e;
   }
   __syncthreads();
   const __nv_bfloat16* src = emb + (int64_t)s_tok * lde;
@@ -509,20 +598,58 @@ __global__ void __launch_bounds__(kNormThreads) pick_embed_kernel(
 
 int nt_for(int M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
-template <int NT, int STAGES>
+// Dynamic shared memory size plus the largest shared-memory carveout, so two ~100 KB CTAs fit on an
+// SM (the default carveout left room for one).
+template <typename K>
+cudaError_t set_smem_attrs(K kern, int bytes) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  return cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                              (int)cudaSharedmemCarveoutMaxShared);
+}
+
+template <int NT, int STAGES, int EPI>
 int launch_skinny(const CUtensorMap& tw, const CUtensorMap& tx, const SkinnyArgs& a, int tiles, cudaStream_t st) {
   using S = SkSmem<NT, STAGES>;
-  auto kern = skinny_gemm_kernel<NT, STAGES>;
+  auto kern = skinny_gemm_kernel<NT, STAGES, EPI>;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)S::TOTAL);
+    cudaError_t e = set_smem_attrs(kern, (int)S::TOTAL);
     if (e != cudaSuccess) return (int)e;
     attr[dev & 63] = true;
   }
-  kern<<<dim3(a.splits, tiles), kThreads, S::TOTAL, st>>>(tw, tx, a);
-  return (int)cudaGetLastError();
+  // grid (splits, tiles), one cluster of `splits` CTAs per 128-row tile (the split-K reduction runs
+  // over distributed shared memory); programmatic dependent launch when enabled
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(a.splits, tiles);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = S::TOTAL;
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = a.splits;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = brain_host::g_decode_pdl ? 2 : 1;
+  return (int)cudaLaunchKernelEx(&cfg, kern, tw, tx, a);
+}
+
+template <int NT, int STAGES>
+int launch_by_epi(int epi, const CUtensorMap& tw, const CUtensorMap& tx, const SkinnyArgs& a, int tiles,
+                  cudaStream_t st) {
+  switch (epi) {
+    case EPI_STORE: return launch_skinny<NT, STAGES, EPI_STORE>(tw, tx, a, tiles, st);
+    case EPI_PUSH: return launch_skinny<NT, STAGES, EPI_PUSH>(tw, tx, a, tiles, st);
+    case EPI_SWIGLU: return launch_skinny<NT, STAGES, EPI_SWIGLU>(tw, tx, a, tiles, st);
+    case EPI_QKV: return launch_skinny<NT, STAGES, EPI_QKV>(tw, tx, a, tiles, st);
+    case EPI_ARGMAX: return launch_skinny<NT, STAGES, EPI_ARGMAX>(tw, tx, a, tiles, st);
+    default: return (int)cudaErrorInvalidValue;
+  }
 }
 
 bool map_2d(CUtensorMap* m, const void* p, uint64_t inner, uint64_t outer, uint64_t ld, uint32_t box_outer) {
@@ -535,31 +662,44 @@ bool map_2d(CUtensorMap* m, const void* p, uint64_t inner, uint64_t outer, uint6
 
 }  // namespace
 
+namespace brain_host {
+int g_decode_pdl = 1;
+}
+
 BRAIN_STATUS_READER(decode_tp)
 
-// Split count for a skinny GEMM: fill about two CTAs per SM, at least 4 k-blocks per split.
+// Programmatic dependent launch for the decode-step kernels on (1) or off (0); returns the old value.
+BRAIN_API int brain_decode_set_pdl(int on) {
+  const int old = brain_host::g_decode_pdl;
+  brain_host::g_decode_pdl = on;
+  return old;
+}
+
+// Split count (= cluster size, at most 8) for a skinny GEMM: about two CTAs per SM in one wave (the
+// ~100 KB CTAs fit two per SM; measured residency, not the occupancy API, which reports one), at least
+// 4 k-blocks per split, no empty split.
 BRAIN_API int brain_skinny_splits(int M, int N, int K) {
   (void)M;
   const int tiles = (N + kRows - 1) / kRows;
   const int num_kb = (K + kBK - 1) / kBK;
   int s = std::max(1, (2 * brain_host::num_sms()) / std::max(tiles, 1));
+  s = std::min(s, kMaxSplits);
   s = std::min(s, std::max(1, num_kb / 4));
   const int per = (num_kb + s - 1) / s;
-  return (num_kb + per - 1) / per;  // no empty split
+  return (num_kb + per - 1) / per;
 }
 
-// f32 elements of split-K workspace for (M, N, splits).
-BRAIN_API int64_t brain_skinny_workspace(int M, int N, int splits) {
-  return (int64_t)((N + kRows - 1) / kRows) * splits * nt_for(M) * kRows;
-}
+// Per-push arrival count added to each rank's counter (consumers wait for multiples of it).
+BRAIN_API int brain_decode_arrivals() { return (int)kArrivals; }
 
 // ext (int64[32], may be null for EPI_STORE / EPI_SWIGLU):
 //   [0] world [1] rank [2] slot_elems [3] ctrl* [4] keys* [5] vocab_offset [6] hq [7] hkv [8] pos*
 //   [9] cos|sin table* [10] k pool* [11] v pool* [12] block table* [13] max_blocks [14] block_size
-//   [16..24) peer slot bases  [24..32) peer flag arrays
+//   [15] optional phase-timestamp buffer (uint64 [ctas][16]: globaltimer ns [0..7), SM clocks [8..16)) [16..24) peer slot bases
+//   [24..32) peer counter arrays (uint32 [2][8] each)
 BRAIN_API int brain_skinny_gemm(const void* X, int64_t ldx, const void* W, int64_t ldw, int M, int N, int K, int epi,
                                 float alpha, void* out, int64_t ldc, const void* R, int64_t ldr, int splits,
-                                float* ws, int* tile_cnt, const int64_t* ext, cudaStream_t st) {
+                                const int64_t* ext, cudaStream_t st) {
   if (M <= 0 || M > 64 || N <= 0 || K <= 0 || (K % 8) || (ldx % 8) || (ldw % 8)) return (int)cudaErrorInvalidValue;
   SkinnyArgs a{};
   a.M = M;
@@ -567,17 +707,15 @@ BRAIN_API int brain_skinny_gemm(const void* X, int64_t ldx, const void* W, int64
   a.K = K;
   a.num_kb = (K + kBK - 1) / kBK;
   if (splits < 1) splits = 1;
+  if (splits > kMaxSplits) splits = kMaxSplits;
   a.kb_per_split = (a.num_kb + splits - 1) / splits;
   a.splits = (a.num_kb + a.kb_per_split - 1) / a.kb_per_split;
-  if (a.splits > 1 && (!ws || !tile_cnt)) return (int)cudaErrorInvalidValue;
-  a.epi = epi;
   a.alpha = alpha;
   a.out = reinterpret_cast<__nv_bfloat16*>(out);
   a.ldc = ldc;
   a.R = reinterpret_cast<const __nv_bfloat16*>(R);
   a.ldr = ldr;
-  a.ws = ws;
-  a.tile_cnt = tile_cnt;
+  if (ext) a.trace = reinterpret_cast<unsigned long long*>(ext[15]);
   if (epi == EPI_PUSH || epi == EPI_ARGMAX || epi == EPI_QKV) {
     if (!ext) return (int)cudaErrorInvalidValue;
     a.world = (int)ext[0];
@@ -598,45 +736,60 @@ BRAIN_API int brain_skinny_gemm(const void* X, int64_t ldx, const void* W, int64
     if (a.world < 1 || a.world > kMaxWorld) return (int)cudaErrorInvalidValue;
     for (int r = 0; r < a.world; ++r) {
       a.peer_slots[r] = reinterpret_cast<void*>(ext[16 + r]);
-      a.peer_flags[r] = reinterpret_cast<int*>(ext[24 + r]);
+      a.peer_flags[r] = reinterpret_cast<unsigned int*>(ext[24 + r]);
     }
   }
+  const int tiles = (N + kRows - 1) / kRows;
+  if ((int64_t)tiles * a.splits > (int64_t)kArrivals || tiles > 65535) return (int)cudaErrorInvalidValue;
   if (epi == EPI_QKV && N != (a.hq + 2 * a.hkv) * kRows) return (int)cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU && (N % kRows)) return (int)cudaErrorInvalidValue;
   if (epi == EPI_ARGMAX && !a.keys) return (int)cudaErrorInvalidValue;
-  const int tiles = (N + kRows - 1) / kRows;
   const int NT = nt_for(M);
   CUtensorMap tw, tx;
   if (!map_2d(&tw, W, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, kRows) ||
       !map_2d(&tx, X, (uint64_t)K, (uint64_t)M, (uint64_t)ldx, (uint32_t)NT))
     return (int)cudaErrorInvalidValue;
-  if (NT == 16) return launch_skinny<16, 6>(tw, tx, a, tiles, st);
-  if (NT == 32) return launch_skinny<32, 5>(tw, tx, a, tiles, st);
-  return launch_skinny<64, 4>(tw, tx, a, tiles, st);
+  if (NT == 16) return launch_by_epi<16, 5>(epi, tw, tx, a, tiles, st);
+  if (NT == 32) return launch_by_epi<32, 4>(epi, tw, tx, a, tiles, st);
+  return launch_by_epi<64, 3>(epi, tw, tx, a, tiles, st);
 }
 
-BRAIN_API int brain_tp_ar_norm(const void* slots, const int* flags, const int* ctrl, int world, int64_t slot_elems,
-                               int M, int N, void* resid, int64_t ldr, const void* gamma, float eps, void* normed,
+BRAIN_API int brain_tp_ar_norm(const void* slots, const void* flags, void* ctrl, int world, int64_t slot_elems, int M,
+                               int N, void* resid, int64_t ldr, const void* gamma, float eps, void* normed,
                                int64_t ldn, int64_t budget_ns, cudaStream_t st) {
-  if (N % 8 || N > kNormThreads * 8 * kMaxChunks || world < 1 || world > kMaxWorld) return (int)cudaErrorInvalidValue;
+  if (N % (8 * kArParts) || N > kArParts * kNormThreads * 8 * kArChunks || world < 1 || world > kMaxWorld)
+    return (int)cudaErrorInvalidValue;
   if (M == 0) return 0;
-  ar_norm_kernel<<<M, kNormThreads, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(slots), flags, ctrl, world,
-                                             slot_elems, N, reinterpret_cast<__nv_bfloat16*>(resid), ldr,
-                                             reinterpret_cast<const __nv_bfloat16*>(gamma), eps,
-                                             reinterpret_cast<__nv_bfloat16*>(normed), ldn, budget_ns);
-  return (int)cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kArParts, M);
+  cfg.blockDim = dim3(kNormThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute at[2];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = kArParts;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = brain_host::g_decode_pdl ? 2 : 1;
+  return (int)cudaLaunchKernelEx(&cfg, ar_norm_kernel, reinterpret_cast<const __nv_bfloat16*>(slots),
+                                 reinterpret_cast<const unsigned int*>(flags), reinterpret_cast<int*>(ctrl), world,
+                                 slot_elems, N, reinterpret_cast<__nv_bfloat16*>(resid), ldr,
+                                 reinterpret_cast<const __nv_bfloat16*>(gamma), eps,
+                                 reinterpret_cast<__nv_bfloat16*>(normed), ldn, budget_ns);
 }
 
-BRAIN_API int brain_tp_pick_embed(const void* key_slots, const int* flags, const int* ctrl, int world,
-                                  int64_t slot_elems, int M, const void* emb, int64_t lde, int vocab, int N,
-                                  void* resid, const void* gamma, float eps, void* normed, int* hist, int64_t hist_ld,
-                                  int* pos, int* seq_lens, int64_t budget_ns, cudaStream_t st) {
+BRAIN_API int brain_tp_pick_embed(const void* key_slots, const void* flags, void* ctrl, int world, int64_t slot_elems,
+                                  int M, const void* emb, int64_t lde, int vocab, int N, void* resid, const void* gamma,
+                                  float eps, void* normed, int* hist, int64_t hist_ld, int* pos, int* seq_lens,
+                                  int64_t budget_ns, cudaStream_t st) {
   if (N % 8 || N > kNormThreads * 8 * kMaxChunks || world < 1 || world > kMaxWorld) return (int)cudaErrorInvalidValue;
   if (M == 0) return 0;
-  pick_embed_kernel<<<M, kNormThreads, 0, st>>>(
-      reinterpret_cast<const unsigned long long*>(key_slots), flags, ctrl, world, slot_elems,
-      reinterpret_cast<const __nv_bfloat16*>(emb), lde, vocab, N, reinterpret_cast<__nv_bfloat16*>(resid),
-      reinterpret_cast<const __nv_bfloat16*>(gamma), eps, reinterpret_cast<__nv_bfloat16*>(normed), hist, hist_ld,
-      pos, seq_lens, budget_ns);
-  return (int)cudaGetLastError();
+  return (int)brain_host::launch(
+      pick_embed_kernel, dim3(M), dim3(kNormThreads), 0, st, brain_host::g_decode_pdl != 0,
+      reinterpret_cast<const unsigned long long*>(key_slots), reinterpret_cast<const unsigned int*>(flags),
+      reinterpret_cast<int*>(ctrl), world, slot_elems, reinterpret_cast<const __nv_bfloat16*>(emb), lde, vocab, N,
+      reinterpret_cast<__nv_bfloat16*>(resid), reinterpret_cast<const __nv_bfloat16*>(gamma), eps,
+      reinterpret_cast<__nv_bfloat16*>(normed), hist, hist_ld, pos, seq_lens, budget_ns);
 }

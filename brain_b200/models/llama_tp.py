@@ -9,8 +9,8 @@ replicated. Per layer the weights are ``wqkv`` [(Hq/W + 2 Hkv/W) * D, d] (this r
 Prefill (``prefill``): sequence parallel when the token count allows it - the residual stream is
 sharded by tokens, QKV and gate/up run as all-gather -> GEMM pipelined by row block (copy-engine
 pulls over NVLink overlapped with the GEMMs of blocks already present), out- and down-projections
-as GEMM -> reduce-scatter (the epilogue pushes rows to their owners over NVLink); attention is the tcgen05 flash-attention kernel over the local
-heads, and K/V land in the paged cache.
+as GEMM -> reduce-scatter (the epilogue pushes rows to their owners over NVLink); attention is the
+tcgen05 flash-attention kernel over the local heads, and K/V land in the paged cache.
 
 Decode (``step``; one token per sequence): every launch is a hand-written kernel and the whole step
 is capturable as one CUDA graph (``capture``), because all per-step state (positions, sequence
@@ -33,7 +33,7 @@ import torch
 import torch.distributed as dist
 
 from .. import _native, ops
-from ..ops.decode import (EPI_ARGMAX, EPI_PUSH, EPI_QKV, EPI_SWIGLU, SkinnyWorkspace, ar_norm, decode_ext,
+from ..ops.decode import (EPI_ARGMAX, EPI_PUSH, EPI_QKV, EPI_SWIGLU, ar_norm, decode_ext,
                           interleave_gate_up, paged_decode_attention, pick_embed, skinny_gemm, skinny_splits)
 from .config import LlamaLiteConfig
 
@@ -65,7 +65,7 @@ class _StepComm:
             self._keep = torch.zeros(total, device=device, dtype=torch.uint8)
             self.local = self._keep.data_ptr()
             self.bases = [self.local]
-        self.ctrl = torch.zeros(2, device=device, dtype=torch.int32)
+        self.ctrl = torch.zeros(4, device=device, dtype=torch.int32)  # epoch consumed, produced, ticket
         self.keys = torch.zeros(batch, device=device, dtype=torch.int64)
         self.flags_local = self.local
         self.ar_local = self.local + self.ar_off
@@ -90,12 +90,17 @@ class LlamaTPServe:
     """Greedy batched generation of a Llama-shaped model, tensor-parallel over ``group``."""
 
     def __init__(self, cfg: LlamaLiteConfig, max_batch: int, max_len: int, block_size: int = 64, group=None,
-                 seed: int = 0, init: bool = True, device=None):
+                 seed: int = 0, init: bool = True, device=None, shard_of: int | None = None):
+        """``shard_of`` (performance work on one GPU only): give this single rank the weight shard of one
+        rank of a ``shard_of``-way group; the all-reduces then sum this shard alone, so the outputs are
+        not the model's, but every kernel runs at the per-rank shapes of the larger group."""
         self.cfg = cfg
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
-        W, c = self.world, cfg
+        if shard_of is not None and self.world != 1:
+            raise ValueError("shard_of emulates a larger group on a single rank")
+        W, c = (shard_of or self.world), cfg
         if c.num_heads % W or c.num_kv_heads % W or c.intermediate_dim % (64 * W):
             raise ValueError("heads, kv heads and FFN width / 64 must divide by the tensor-parallel size")
         if c.head_dim != 128:
@@ -140,11 +145,10 @@ class LlamaTPServe:
         self.q = torch.empty(B, self.hq * self.D, device=dev, dtype=torch.bfloat16)
         self.attn = torch.empty(B, self.hq * self.D, device=dev, dtype=torch.bfloat16)
         self.act = torch.empty(B, self.F, device=dev, dtype=torch.bfloat16)
-        self.ws = SkinnyWorkspace(dev)
         self.attn_splits = int(_native.fn("brain_decode_splits")(B, self.hkv, max_len))
         n_ws = int(_native.fn("brain_decode_workspace")(B, self.hq, self.hkv, self.D, self.attn_splits))
         self.attn_ws = torch.empty(n_ws, device=dev, dtype=torch.float32)
-        self.comm = _StepComm(B, d, W, self.rank, group, dev)
+        self.comm = _StepComm(B, d, self.world, self.rank, group, dev)
         self.tp = None  # TPContext for the sequence-parallel prefill (created on first use)
         self.graph = None
         self._build_launch_args()
@@ -203,8 +207,7 @@ class LlamaTPServe:
     # ------------------------------------------------------------------ decode
     def _head_and_pick(self):
         c = self.cfg
-        skinny_gemm(self.normed, self.head[:self.v_rows], EPI_ARGMAX, ext=self.ext_argmax, splits=self.sp["head"],
-                    ws=self.ws)
+        skinny_gemm(self.normed, self.head[:self.v_rows], EPI_ARGMAX, ext=self.ext_argmax, splits=self.sp["head"])
         cm = self.comm
         pick_embed(cm.key_local, cm.flags_local, cm.ctrl, self.world, cm.key_elems, self.emb, self.resid,
                    self.attn_norm[0], c.norm_eps, self.normed, self.hist, self.pos, self.seq_lens)
@@ -213,16 +216,15 @@ class LlamaTPServe:
         """One decode step for every sequence (eager launches; ``capture`` records the same launches)."""
         c, B, cm = self.cfg, self.B, self.comm
         for i in range(c.num_layers):
-            skinny_gemm(self.normed, self.wqkv[i], EPI_QKV, out=self.q, ext=self.ext_qkv[i], splits=self.sp["qkv"],
-                        ws=self.ws)
+            skinny_gemm(self.normed, self.wqkv[i], EPI_QKV, out=self.q, ext=self.ext_qkv[i], splits=self.sp["qkv"])
             paged_decode_attention(self.q.view(B, self.hq, self.D), self.kv[i, 0], self.kv[i, 1], self.table,
                                    self.seq_lens, splits=self.attn_splits, workspace=self.attn_ws,
                                    out=self.attn.view(B, self.hq, self.D))
-            skinny_gemm(self.attn, self.wo[i], EPI_PUSH, ext=self.ext_push, splits=self.sp["o"], ws=self.ws)
+            skinny_gemm(self.attn, self.wo[i], EPI_PUSH, ext=self.ext_push, splits=self.sp["o"])
             ar_norm(cm.ar_local, cm.flags_local, cm.ctrl, self.world, cm.ar_elems, self.resid, self.ffn_norm[i],
                     c.norm_eps, self.normed)
-            skinny_gemm(self.normed, self.w_gu[i], EPI_SWIGLU, out=self.act, splits=self.sp["gu"], ws=self.ws)
-            skinny_gemm(self.act, self.w_down[i], EPI_PUSH, ext=self.ext_push, splits=self.sp["down"], ws=self.ws)
+            skinny_gemm(self.normed, self.w_gu[i], EPI_SWIGLU, out=self.act, splits=self.sp["gu"])
+            skinny_gemm(self.act, self.w_down[i], EPI_PUSH, ext=self.ext_push, splits=self.sp["down"])
             ar_norm(cm.ar_local, cm.flags_local, cm.ctrl, self.world, cm.ar_elems, self.resid, self.gammas_after[i],
                     c.norm_eps, self.normed)
         self._head_and_pick()

@@ -46,6 +46,14 @@ STATUS_TAGS = ["gemm", "norms", "elementwise", "ce", "optim", "attention", "atte
                "attention_decode", "decode_tp"]
 
 
+def same_device(ref: torch.Tensor, *others) -> None:
+    """Raise unless every tensor in ``others`` (None skipped) lives on ``ref``'s device: a kernel given a
+    pointer into another device's (or the host's) memory would fault."""
+    for t in others:
+        if t is not None and t.device != ref.device:
+            raise ValueError(f"tensor on {t.device} passed to a kernel running on {ref.device}")
+
+
 def stream(t: torch.Tensor) -> int:
     return _native.stream_ptr(t.device)
 

@@ -12,7 +12,7 @@ import math
 import torch
 
 from .. import _native
-from ._common import stream
+from ._common import same_device, stream
 
 _native.register({
     "brain_decode_workspace": ("brain_kernels", "iiiii"),
@@ -29,6 +29,7 @@ def paged_decode_attention(q, k_pool, v_pool, block_table, seq_lens, scale=None,
     B, Hq, D = q.shape
     Hkv = k_pool.shape[2]
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    same_device(q, k_pool, v_pool, block_table, seq_lens, workspace, out)
     if not q.is_cuda:
         return _decode_ref(q, k_pool, v_pool, block_table, seq_lens, scale)
     if splits is None:
@@ -94,36 +95,18 @@ EPI_STORE, EPI_PUSH, EPI_SWIGLU, EPI_QKV, EPI_ARGMAX = 0, 2, 3, 4, 5
 
 _native.register({
     "brain_skinny_splits": ("brain_kernels", "iii"),
-    "brain_skinny_workspace": ("brain_kernels", "iii"),
-    "brain_skinny_gemm": ("brain_kernels", "plpliiiifplplippps"),
+    "brain_skinny_gemm": ("brain_kernels", "plpliiiifplplips"),
+    "brain_decode_set_pdl": ("brain_kernels", "i"),
+    "brain_decode_arrivals": ("brain_kernels", ""),
     "brain_tp_ar_norm": ("brain_kernels", "pppiliiplpfplls"),
     "brain_tp_pick_embed": ("brain_kernels", "pppilipliippfpplppls"),
     "brain_status_decode_tp": ("brain_kernels", "pi"),
 })
-_native.RETURNS_I64.add("brain_skinny_workspace")
 
 
-class SkinnyWorkspace:
-    """Split-K partial tiles (f32) and per-tile tickets (int32, zero between launches) for skinny GEMMs
-    issued one after another on one stream."""
-
-    def __init__(self, device, floats: int = 1 << 22, tiles: int = 8192):
-        self.ws = torch.empty(floats, device=device, dtype=torch.float32)
-        self.cnt = torch.zeros(tiles, device=device, dtype=torch.int32)
-
-    def fits(self, M, N, splits) -> bool:
-        need = int(_native.fn("brain_skinny_workspace")(M, N, splits))
-        return need <= self.ws.numel() and -(-N // 128) <= self.cnt.numel()
-
-
-_WS: dict = {}
-
-
-def _workspace(device) -> SkinnyWorkspace:
-    key = str(device)
-    if key not in _WS:
-        _WS[key] = SkinnyWorkspace(device)
-    return _WS[key]
+def set_pdl(on: bool) -> bool:
+    """Programmatic dependent launch for the decode-step kernels; returns the previous setting."""
+    return bool(_native.fn("brain_decode_set_pdl")(int(bool(on))))
 
 
 def skinny_splits(M: int, N: int, K: int) -> int:
@@ -131,7 +114,7 @@ def skinny_splits(M: int, N: int, K: int) -> int:
 
 
 def decode_ext(world=1, rank=0, slot_elems=0, ctrl=None, keys=None, vocab_offset=0, hq=0, hkv=0, pos=None,
-               rope_cs=None, k_pool=None, v_pool=None, block_table=None, peer_slots=(), peer_flags=()):
+               rope_cs=None, k_pool=None, v_pool=None, block_table=None, peer_slots=(), peer_flags=(), trace=None):
     """The int64[32] side-argument block of ``brain_skinny_gemm`` (layout documented in the source)."""
     import ctypes
 
@@ -140,7 +123,7 @@ def decode_ext(world=1, rank=0, slot_elems=0, ctrl=None, keys=None, vocab_offset
     v = [0] * 32
     v[0], v[1], v[2], v[3], v[4], v[5] = world, rank, slot_elems, p(ctrl), p(keys), vocab_offset
     v[6], v[7], v[8], v[9], v[10], v[11] = hq, hkv, p(pos), p(rope_cs), p(k_pool), p(v_pool)
-    v[12] = p(block_table)
+    v[12], v[15] = p(block_table), p(trace)
     if block_table is not None:
         v[13], v[14] = block_table.shape[1], k_pool.shape[1]
     for i, s in enumerate(peer_slots):
@@ -150,8 +133,7 @@ def decode_ext(world=1, rank=0, slot_elems=0, ctrl=None, keys=None, vocab_offset
     return (ctypes.c_int64 * 32)(*v)
 
 
-def skinny_gemm(x, w, epi=EPI_STORE, out=None, residual=None, alpha=1.0, splits=None, ws=None, ext=None,
-                out_cols=None):
+def skinny_gemm(x, w, epi=EPI_STORE, out=None, residual=None, alpha=1.0, splits=None, ext=None, out_cols=None):
     """x [M, K] (M <= 64) times w [N, K]^T on the tensor cores with the operands swapped.
 
     epi: EPI_STORE (out [M, N], + residual), EPI_SWIGLU (w rows interleaved [gate 64 | up 64] per 128;
@@ -159,16 +141,16 @@ def skinny_gemm(x, w, epi=EPI_STORE, out=None, residual=None, alpha=1.0, splits=
     """
     M, K = x.shape
     N = w.shape[0]
+    same_device(x, w, out, residual)
     if splits is None:
         splits = skinny_splits(M, N, K)
-    ws = ws or _workspace(x.device)
     if out is None and epi in (EPI_STORE, EPI_SWIGLU, EPI_QKV):
         cols = out_cols if out_cols is not None else (N // 2 if epi == EPI_SWIGLU else N)
         out = torch.empty(M, cols, device=x.device, dtype=torch.bfloat16)
     _native.call("brain_skinny_gemm", x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), M, N, K, epi,
                  float(alpha), 0 if out is None else out.data_ptr(), 0 if out is None else out.stride(0),
                  0 if residual is None else residual.data_ptr(), 0 if residual is None else residual.stride(0),
-                 int(splits), ws.ws.data_ptr(), ws.cnt.data_ptr(), ext, stream(x))
+                 int(splits), ext, stream(x))
     return out
 
 

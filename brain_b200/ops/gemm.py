@@ -14,6 +14,7 @@ from __future__ import annotations
 import torch
 
 from .. import _native
+from ._common import same_device
 
 
 def _row_major(x: torch.Tensor) -> torch.Tensor:
@@ -55,6 +56,7 @@ def gemm(
         raise ValueError(f"out has shape {tuple(out.shape)}, expected {(M, N)}")
     if not a.is_cuda:
         return _gemm_cpu(a, b, trans_a, trans_b, out, alpha, beta if accumulate else 0.0, bias, residual)
+    same_device(a, b, out, bias, residual)
     if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
         raise TypeError("CUDA gemm takes bfloat16 operands")
     if out.dtype not in (torch.bfloat16, torch.float32) or out.stride(1) != 1:

@@ -24,6 +24,7 @@ import torch.distributed as dist
 from .. import _native
 from ..nn import init as _init
 from ..nn.module import Module
+from ..ops._common import same_device
 from ..ops.gemm import gemm
 from ..ops.linear import _wgrad
 
@@ -106,6 +107,7 @@ def gemm_push(ctx: TPContext, a: torch.Tensor, w: torch.Tensor, mode: int, rows_
     M, K = a.shape
     N = w.shape[1] if b_mn else w.shape[0]
     W = ctx.world
+    same_device(a, w)
     out_rows = rows_per_rank if mode == 1 else M
     slot = out_rows * N
     par = ctx.next_parity()
@@ -203,6 +205,13 @@ class _RowFn(torch.autograd.Function):
         return dx, dw, None, None
 
 
+def _default_device(ctx: TPContext, device):
+    """Sharded layers of a multi-rank group live on the rank's GPU unless told otherwise."""
+    if device is None and ctx.world > 1:
+        return torch.device("cuda", torch.cuda.current_device())
+    return device
+
+
 class ColumnParallelLinear(Module):
     def __init__(self, in_features: int, out_features: int, ctx: TPContext, sequence_parallel: bool = False,
                  device=None, dtype=torch.bfloat16, init_std: float = 0.02, seed: int = 0):
@@ -211,6 +220,7 @@ class ColumnParallelLinear(Module):
             raise ValueError("out_features must divide by the tensor-parallel size")
         self.ctx, self.sp = ctx, sequence_parallel
         self.in_features, self.out_features = in_features, out_features
+        device = _default_device(ctx, device)
         self.weight = torch.nn.Parameter(torch.empty(out_features // ctx.world, in_features, device=device,
                                                      dtype=dtype))
         g = torch.Generator(device=self.weight.device).manual_seed(seed * 1000 + ctx.rank)
@@ -234,6 +244,7 @@ class RowParallelLinear(Module):
         if in_features % ctx.world:
             raise ValueError("in_features must divide by the tensor-parallel size")
         self.ctx, self.sp = ctx, sequence_parallel
+        device = _default_device(ctx, device)
         self.weight = torch.nn.Parameter(torch.empty(out_features, in_features // ctx.world, device=device,
                                                      dtype=dtype))
         g = torch.Generator(device=self.weight.device).manual_seed(seed * 1000 + 500 + ctx.rank)

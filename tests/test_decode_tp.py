@@ -80,7 +80,7 @@ def test_push_ar_norm_single_rank():
     slot_elems = M * N
     slots = torch.zeros(2 * slot_elems, device="cuda", dtype=torch.bfloat16)
     flags = torch.zeros(64, device="cuda", dtype=torch.int32)
-    ctrl = torch.zeros(2, device="cuda", dtype=torch.int32)
+    ctrl = torch.zeros(4, device="cuda", dtype=torch.int32)
     ext = decode_ext(world=1, rank=0, slot_elems=slot_elems, ctrl=ctrl, peer_slots=[slots.data_ptr()],
                      peer_flags=[flags.data_ptr()])
     normed = torch.empty_like(resid)
@@ -93,7 +93,11 @@ def test_push_ar_norm_single_rank():
         hn = resid.float()
         ref = hn * torch.rsqrt(hn.pow(2).mean(-1, keepdim=True) + 1e-5) * gamma.float()
         assert (normed.float() - ref).abs().max().item() < 5e-2
-    assert int(ctrl[0]) == 3 and int(flags[0]) == 3 and int(ctrl[1]) == 0
+    # epochs 1..3 consumed and produced; counters per parity hold the pushes' fixed arrival totals
+    from brain_b200 import _native
+    arrivals = int(_native.fn("brain_decode_arrivals")())
+    assert int(ctrl[0]) == 3 and int(ctrl[1]) == 3
+    assert int(flags[8].item()) == 2 * arrivals and int(flags[0].item()) == arrivals
 
 
 def test_argmax_pick_embed_single_rank():
@@ -104,7 +108,7 @@ def test_argmax_pick_embed_single_rank():
     keys = torch.zeros(M, device="cuda", dtype=torch.int64)
     key_slots = torch.zeros(2 * M, device="cuda", dtype=torch.int64)
     flags = torch.zeros(64, device="cuda", dtype=torch.int32)
-    ctrl = torch.zeros(2, device="cuda", dtype=torch.int32)
+    ctrl = torch.zeros(4, device="cuda", dtype=torch.int32)
     ext = decode_ext(world=1, rank=0, slot_elems=M, ctrl=ctrl, keys=keys, peer_slots=[key_slots.data_ptr()],
                      peer_flags=[flags.data_ptr()])
     hist = torch.zeros(M, 16, device="cuda", dtype=torch.int32)

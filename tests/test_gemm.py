@@ -123,3 +123,11 @@ def test_gemm_push_local_slots(mode, M, N):
         exp = ref[j * rows:(j + 1) * rows] if mode == 1 else ref
         torch.testing.assert_close(got, exp, rtol=2e-2, atol=2e-1)
         assert recv[j][(1 - rank) * slot:(2 - rank) * slot].abs().sum().item() == 0
+
+
+@pytest.mark.gpu
+def test_gemm_rejects_operand_on_other_device():
+    a = _mk((128, 64), "cuda", 40)
+    b = _mk((64, 128), "cpu", 41)
+    with pytest.raises(ValueError):
+        gemm(a, b)
