@@ -42,7 +42,7 @@ def main(argv=None) -> int:
     from ..models import LlamaLiteConfig
     from ..ops import check_status
     from ..ops.decode import (EPI_ARGMAX, EPI_PUSH, EPI_QKV, EPI_STORE, EPI_SWIGLU, ar_norm, decode_ext,
-                              paged_decode_attention, set_pdl, skinny_gemm, skinny_splits)
+                              init_ar_slots, paged_decode_attention, set_pdl, skinny_gemm, skinny_splits)
     from ..ops.rope import rope_table
 
     cfg = LlamaLiteConfig.llama3_70b()
@@ -122,8 +122,10 @@ def main(argv=None) -> int:
                 if len(col):
                     d = (col - base) / 1e3
                     phases[nm] = [round(float(d.median()), 2), round(float(d.max()), 2)]
-            steps = [("pdl_wait", 8, 9), ("tmem_scatter_dealloc", 9, 10), ("cluster_barrier", 10, 11),
+            steps = [("pdl_wait", 8, 9), ("stage_and_send", 9, 10), ("receive_wait", 10, 11),
                      ("reduce_epilogue", 11, 15)]
+            if epi == EPI_PUSH:
+                steps += [("push_stores", 11, 12), ("push_syncthreads", 12, 13), ("push_release_arrive", 13, 14)]
             cyc = {nm: round(float((t[:, b] - t[:, a_]).median()), 0) for nm, a_, b in steps}
             print(json.dumps({"trace": name, "us_median_max_since_first_start": phases,
                               "sm_cycles_median_per_step": cyc}), flush=True)
@@ -149,12 +151,10 @@ def main(argv=None) -> int:
         report("paged_decode_attention", us, B * a.kv_len * hkv * D * 2 * 2, kv_len=a.kv_len)
     # ---- out projection with all-reduce push (single rank: pushes to itself)
     slot = B * d
-    slots = torch.zeros(2 * slot, device=dev, dtype=torch.bfloat16)
-    flags = torch.zeros(64, device=dev, dtype=torch.int32)
+    slots = init_ar_slots(torch.empty(2 * slot, device=dev, dtype=torch.bfloat16))
     ctrl = torch.zeros(4, device=dev, dtype=torch.int32)
     def push_ext(tr=None):
-        return decode_ext(world=1, rank=0, slot_elems=slot, ctrl=ctrl, peer_slots=[slots.data_ptr()],
-                          peer_flags=[flags.data_ptr()], trace=tr)
+        return decode_ext(world=1, rank=0, slot_elems=slot, ctrl=ctrl, peer_slots=[slots.data_ptr()], trace=tr)
     ext_push = push_ext()
     resid = rnd(B, d, std=1.0)
     gamma = torch.ones(d, device=dev, dtype=torch.bfloat16)
@@ -162,12 +162,8 @@ def main(argv=None) -> int:
 
     def o_and_norm(i, w=copies((d, hq * D)) if want("o_push+ar_norm") else None):
         skinny_gemm(xa, w[i % len(w)], EPI_PUSH, ext=ext_push, splits=a.splits or skinny_splits(B, d, hq * D))
-        ar_norm(slots.data_ptr(), flags.data_ptr(), ctrl, 1, slot, resid, gamma, 1e-5, normed)
+        ar_norm(slots.data_ptr(), ctrl, 1, slot, resid, gamma, 1e-5, normed)
     gemm_case("skinny_gemm_o_push", d, hq * D, EPI_PUSH, xa, push_ext)
-    if want("ar_norm_1rank"):
-        us = timeit(lambda i: ar_norm(slots.data_ptr(), flags.data_ptr(), ctrl, 1, slot, resid, gamma, 1e-5, normed),
-                    a.iters)
-        report("ar_norm_1rank", us, 2 * B * d * 4)
     if want("o_push+ar_norm"):
         us = timeit(o_and_norm, a.iters)
         report("o_push+ar_norm", us, 2 * d * hq * D)
@@ -181,7 +177,7 @@ def main(argv=None) -> int:
     kslots = torch.zeros(2 * B, device=dev, dtype=torch.int64)
     gemm_case("skinny_gemm_head_argmax", Vs, d, EPI_ARGMAX, x,
               lambda tr: decode_ext(world=1, rank=0, slot_elems=B, ctrl=ctrl, keys=keys,
-                                    peer_slots=[kslots.data_ptr()], peer_flags=[flags.data_ptr()], trace=tr))
+                                    peer_slots=[kslots.data_ptr()], trace=tr))
     bad = check_status()
     if bad:
         print(json.dumps({"error": f"kernel status {bad}"}), flush=True)

@@ -11,31 +11,31 @@
 //    one of the epilogues for its tokens over all 128 rows of the tile:
 //      EPI_STORE   bf16 out (+ residual)
 //      EPI_PUSH    all-reduce push: the bf16 partial product goes to slot `rank` of every rank's
-//                  receive buffer over NVLink, then the CTA adds its arrival to every rank's counter
-//                  (red.release.sys, no round trip)
+//                  receive buffer over NVLink with plain stores; no fence or flag follows them
 //      EPI_SWIGLU  weight rows interleaved in 64-row groups [gate 64 | up 64]; writes silu(gate) * up
 //      EPI_QKV     one tile = one head of the fused [q | k | v] projection (head_dim 128): RoPE on
 //                  q / k at each token's position, q to `out`, k / v straight into their paged slots
 //      EPI_ARGMAX  greedy LM head: the per-token max over the tile's vocabulary rows folds into a
 //                  64-bit (value, -index) key with atomicMax; the last CTA (ticket) pushes the keys to
-//                  every rank and adds the whole push's arrivals
+//                  every rank
 //    The first weight stages are requested before the kernel waits for its predecessor
 //    (programmatic dependent launch), so the weight stream starts while the previous kernel ends.
-// 2. ar_norm: waits for every rank's arrivals, sums the `world` bf16 slots of a token row in f32,
-//    adds the residual stream (updated in place) and writes RMSNorm(h) * gamma for the next GEMM.
+// 2. ar_norm: sums the `world` bf16 slots of a token row in f32 as they arrive, adds the residual
+//    stream (updated in place) and writes RMSNorm(h) * gamma for the next GEMM.
 // 3. pick_embed: waits for the argmax keys of all ranks, picks the token (lowest index on ties),
 //    records it, advances the positions, gathers its embedding row into the residual stream and
 //    RMS-normalises it for layer 0 of the next step.
 //
-// Synchronisation state lives in device memory, so a whole decode step is one replayable CUDA graph:
-//   ctrl[0] = last epoch consumed (written by consumers), ctrl[1] = last epoch produced (written by
-//   producers), ctrl[2] = argmax ticket. A producer computes e = ctrl[0] + 1, writes slot parity e & 1
-//   and stores ctrl[1] = e; the consumer reads e = ctrl[1] and stores ctrl[0] = e. Each push adds
-//   exactly kArrivals to counter [e & 1][rank] of every rank (each CTA adds 1, CTA 0 also adds the
-//   remainder), so the consumer of epoch e waits until every counter of parity e & 1 reaches
-//   kArrivals * ((e + 1) / 2) (compared modulo 2^32). Two parities suffice: a rank reaches epoch
-//   e + 2 only after every peer's epoch e + 1 push, which each peer issues after consuming epoch e.
-//   Every wait is bounded and reports through the status word.
+// Synchronisation without fences or flags ("the data is the flag"): every receive slot holds a
+// sentinel until its value arrives - bf16 -0.0 for the all-reduce slots (a -0.0 result is sent as
+// +0.0) and 0 for the argmax keys (never a valid key). Consumers poll their 16-byte pieces with
+// relaxed system-scope loads until no sentinel is left, use them, and write the sentinel back for the
+// next use of that slot parity. Epochs live in device memory so a whole decode step is one replayable
+// CUDA graph: ctrl[0] = last epoch consumed (written by consumers), ctrl[1] = last epoch produced
+// (written by producers), ctrl[2] = argmax ticket; a producer uses e = ctrl[0] + 1 and slot parity
+// e & 1, the consumer reads e = ctrl[1]. Two parities suffice: a rank pushes epoch e + 2 only after
+// it consumed epoch e + 1, which needs every peer's epoch e + 1 push, which each peer issues after
+// it consumed (and reset) epoch e. Every poll is bounded and reports through the status word.
 //
 // Reference: the reference's TensorParallelLinear::forward returns zeros
 // (crates/brain-distributed/src/tensor_parallel.rs:8-27) and LlamaLite::generate re-runs the full
@@ -54,7 +54,7 @@ constexpr int kBK = 64;
 constexpr int kThreads = 128;
 constexpr int kMaxWorld = 8;
 constexpr int kMaxSplits = 8;        // portable cluster size
-constexpr uint32_t kArrivals = 4096;  // counter increment per push (>= CTAs of any push)
+constexpr unsigned short kSentinel = 0x8000;  // bf16 -0.0: "not written yet" in a receive slot
 
 enum Epi : int { EPI_STORE = 0, EPI_PUSH = 2, EPI_SWIGLU = 3, EPI_QKV = 4, EPI_ARGMAX = 5 };
 
@@ -73,7 +73,6 @@ struct SkinnyArgs {
   unsigned long long* keys;  // EPI_ARGMAX running keys [M], zero between steps
   int64_t vocab_offset;
   void* peer_slots[kMaxWorld];
-  unsigned int* peer_flags[kMaxWorld];  // each rank's counters [2 parities][kMaxWorld]
   // EPI_QKV
   int hq, hkv;
   const int* pos;
@@ -103,23 +102,41 @@ __device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v));
 }
 
-// Arrival on a (possibly remote) counter, ordered after the writes that happen before it.
-__device__ __forceinline__ void red_release_add(unsigned int* addr, unsigned int v) {
-  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory to shared memory of a CTA of
+// this cluster (`dst` and `bar` from mapa_shared), completing transactions on that CTA's mbarrier.
+// A unicast copy between CTAs of one cluster; global memory is not involved.
+__device__ __forceinline__ void bulk_s2s(uint32_t dst, uint32_t src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(dst), "r"(src), "r"(bytes), "r"(bar)
+               : "memory");
 }
-__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* addr) {
-  unsigned int v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+
+// Polling load of 16 bytes that peers write over NVLink (system scope, no L1 caching).
+__device__ __forceinline__ uint4 ld_relaxed_sys_v4(const void* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.sys.global.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
-
-// This CTA's arrivals for epoch e on every rank: one per CTA, plus the remainder up to kArrivals
-// from CTA 0 (so each push adds exactly kArrivals whatever its grid).
-__device__ __forceinline__ void arrive_all(const SkinnyArgs& a, int e, unsigned int inc) {
-  for (int r = 0; r < a.world; ++r) {
-    const int dst = (a.rank + 1 + r) % a.world;  // stagger the peers
-    red_release_add(a.peer_flags[dst] + (e & 1) * kMaxWorld + a.rank, inc);
-  }
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool has_sentinel(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  bool any = false;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) any |= (w[i] & 0xFFFFu) == kSentinel || (w[i] >> 16) == kSentinel;
+  return any;
 }
 
 template <int NT, int STAGES>
@@ -130,7 +147,11 @@ struct SkSmem {
   static constexpr uint32_t RECV = STAGES * STAGE;                  // [splits][tper][128] f32
   static constexpr uint32_t RECV_BYTES = (NT + kMaxSplits) * kRows * 4;
   static constexpr uint32_t BAR = RECV + RECV_BYTES;
-  static constexpr uint32_t TOTAL = BAR + (2 * STAGES + 2) * 8 + 16 + 1024;
+  static constexpr uint32_t TOTAL = BAR + (2 * STAGES + 3) * 8 + 16 + 1024;
+  // after the main loop the stage memory holds the outgoing partials [M][128] f32 at 0 and the
+  // epilogue scratch [tper][128] f32 at SX
+  static constexpr uint32_t SX = NT * kRows * 4;
+  static_assert(2 * NT * kRows * 4 <= STAGES * STAGE, "stage memory too small for the tail buffers");
 };
 
 template <int NT, int STAGES, int EPI>
@@ -146,7 +167,8 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
   auto empty_bar = [&](int s) { return bars + 8u * (STAGES + s); };
   const uint32_t done_bar = bars + 16u * STAGES;
   const uint32_t drain_bar = done_bar + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::BAR + (2 * STAGES + 2) * 8);
+  const uint32_t recv_bar = done_bar + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::BAR + (2 * STAGES + 3) * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* ticket = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
@@ -159,6 +181,11 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
   const int kb0 = split * a.kb_per_split;
   const int nkb = min(a.num_kb - kb0, a.kb_per_split);
   constexpr uint32_t kCols = NT < 32 ? 32 : NT;
+  // tokens finished by this CTA: [t0, t0 + nt)
+  const int nsplit = a.splits;
+  const int tper = (a.M + nsplit - 1) / nsplit;
+  const int t0 = split * tper;
+  const int nt = max(0, min(a.M - t0, tper));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -167,8 +194,11 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
     }
     mbar_init(done_bar, 1);
     mbar_init(drain_bar, 1);
+    mbar_init(recv_bar, 1);
     *abort_flag = 0;
     fence_barrier_init();
+    // every CTA of the cluster (this one included) will copy nt tokens x 128 rows of partials here
+    mbar_arrive_expect_tx(recv_bar, (uint32_t)(nsplit * nt * kRows * 4));
     prefetch_tmap(&tmW);
     prefetch_tmap(&tmX);
   }
@@ -180,6 +210,7 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  cluster_arrive_relaxed();  // receive barriers initialised; the matching wait precedes the first copy
   if (trace) trace[1] = globaltimer();
 
   if (warp == 0 && lane == 0) {
@@ -263,54 +294,60 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
   pdl_wait();  // predecessor complete: its writes (residual, epochs, cache, outputs) are visible
   if (trace) trace[9] = clock64();
 
-  // ---- split-K reduction: TMEM columns (tokens) go straight to the CTA that finishes that token
-  const int nsplit = a.splits;
-  const int tper = (a.M + nsplit - 1) / nsplit;
-  const int t0 = split * tper;
-  const int nt = max(0, min(a.M - t0, tper));
+  // ---- split-K reduction: partials -> local staging [M][128] -> one bulk copy per finishing CTA
+  float* stg = reinterpret_cast<float*>(smem);             // stage memory is free once every MMA completed
   float* recv = reinterpret_cast<float*>(smem + S::RECV);  // [nsplit][tper][128]
   {
     const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16);
-    const uint32_t rbase = smem_u32(recv) + (uint32_t)((split * tper * kRows + row) * 4);
 #pragma unroll 1
-    for (int t = 0; t < a.M; t += 4) {
-      uint32_t r[4];
-      tmem_ld4(taddr + (uint32_t)t, r);
+    for (int c = 0; c < a.M; c += 32) {
+      uint32_t r[32];
+      tmem_ld32(taddr + (uint32_t)c, r);
       tc_wait_ld();
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int tt = t + j;
-        if (tt < a.M) {
-          const int dst = tt / tper;
-          st_dsmem_f32(mapa_shared(rbase + (uint32_t)((tt - dst * tper) * kRows * 4), (uint32_t)dst),
-                       ok ? __uint_as_float(r[j]) : 0.f);
-        }
-      }
+      for (int j = 0; j < 32; ++j) stg[(c + j) * kRows + row] = ok ? __uint_as_float(r[j]) : 0.f;
     }
   }
+  fence_proxy_async();  // staging writes visible to the bulk-copy (async) proxy
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem_base, kCols);
   }
+  cluster_wait();  // every CTA of the cluster has initialised its receive barrier
+  if (threadIdx.x == 0) {
+    const uint32_t src0 = smem_u32(stg), dst0 = smem_u32(recv) + (uint32_t)(split * tper * kRows * 4);
+    for (int d = 0; d < nsplit; ++d) {
+      const int ntd = min(a.M - d * tper, tper);
+      if (ntd > 0)
+        bulk_s2s(mapa_shared(dst0, (uint32_t)d), src0 + (uint32_t)(d * tper * kRows * 4), (uint32_t)(ntd * kRows * 4),
+                 mapa_shared(recv_bar, (uint32_t)d));
+    }
+    bulk_commit();
+  }
   if (trace) trace[10] = clock64();
-  // A CTA whose pipeline gave up still joins the cluster barrier (with zero partials), so the other
-  // CTAs of its cluster never wait for it; the status word already records the failure.
-  cluster_sync();  // release / acquire: every partial for this CTA's tokens has landed
+  // A CTA whose pipeline gave up still sends its (zero) partials, so the other CTAs of its cluster
+  // never wait for it; the status word already records the failure.
+  const bool got = mbar_wait(recv_bar, 0, BRAIN_ERR_TIMEOUT_ACC, 113, nullptr);
+  if (threadIdx.x == 0) bulk_wait_read0();  // outgoing copies have read the staging buffer
+  __syncthreads();
   if (trace) {
     trace[4] = globaltimer();
     trace[11] = clock64();
   }
-  if (!ok) return;
+  if (!ok || !got) return;
   auto reduced = [&](int i) {  // sum of the partials of local token i for this row, in rank order
+    float part[kMaxSplits];
+#pragma unroll
+    for (int r = 0; r < kMaxSplits; ++r) part[r] = r < nsplit ? recv[(r * tper + i) * kRows + row] : 0.f;
     float sum = 0.f;
-#pragma unroll 1
-    for (int r = 0; r < nsplit; ++r) sum += recv[(r * tper + i) * kRows + row];
+#pragma unroll
+    for (int r = 0; r < kMaxSplits; ++r) sum += part[r];
     return sum;
   };
 
-  float* sx = reinterpret_cast<float*>(smem);  // stage memory: free once every MMA completed
+  float* sx = reinterpret_cast<float*>(smem + S::SX);  // epilogue scratch [tper][128]
   const int n = tile * kRows + row;
   const int total_ctas = (int)(gridDim.x * gridDim.y);
   if constexpr (EPI == EPI_STORE) {
@@ -324,23 +361,21 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
       }
     }
   } else if constexpr (EPI == EPI_PUSH) {
+    // Receive slots hold the sentinel (bf16 -0.0) until written; a -0.0 result is sent as +0.0. The
+    // consumer polls the values themselves, so no fence or flag follows the stores.
     const int e = ld_volatile(a.ctrl) + 1;
     const int64_t off = ((int64_t)(e & 1) * a.world + a.rank) * a.slot_elems;
     if (n < a.N) {
 #pragma unroll 1
       for (int i = 0; i < nt; ++i) {
-        const __nv_bfloat16 x = __float2bfloat16_rn(reduced(i) * a.alpha);
+        __nv_bfloat16 x = __float2bfloat16_rn(reduced(i) * a.alpha);
+        if (__bfloat16_as_ushort(x) == kSentinel) x = __ushort_as_bfloat16((unsigned short)0);
 #pragma unroll 1
         for (int r = 0; r < a.world; ++r)
           reinterpret_cast<__nv_bfloat16*>(a.peer_slots[(a.rank + 1 + r) % a.world])[off + (t0 + i) * a.N + n] = x;
       }
     }
-    __syncthreads();  // the CTA's pushed stores happen before thread 0's release arrivals
-    if (threadIdx.x == 0) {
-      const unsigned int inc = (blockIdx.x == 0 && blockIdx.y == 0) ? 1u + kArrivals - (unsigned)total_ctas : 1u;
-      arrive_all(a, e, inc);
-      a.ctrl[1] = e;  // same value from every CTA; read by the consumer after this grid completes
-    }
+    if (threadIdx.x == 0) a.ctrl[1] = e;  // same value from every CTA; read after this grid completes
   } else if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
     for (int i = 0; i < nt; ++i) sx[i * kRows + row] = reduced(i) * a.alpha;
@@ -407,15 +442,14 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
       const int e = ld_volatile(a.ctrl) + 1;
       const int64_t off = ((int64_t)(e & 1) * a.world + a.rank) * a.slot_elems;
       if (threadIdx.x < a.M) {
+        // a key is never 0 (the value half of a finite max is non-zero), so 0 marks an empty slot
         const unsigned long long k = atomicExch(a.keys + threadIdx.x, 0ull);
         for (int r = 0; r < a.world; ++r)
           reinterpret_cast<unsigned long long*>(a.peer_slots[r])[off + threadIdx.x] = k;
       }
-      __syncthreads();
       if (threadIdx.x == 0) {
         a.ctrl[2] = 0;
         a.ctrl[1] = e;
-        arrive_all(a, e, kArrivals);
       }
     }
   }
@@ -423,30 +457,6 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
     trace[6] = globaltimer();
     trace[15] = clock64();
   }
-}
-
-// Consumer side: wait (thread j < world) until rank j's arrivals for the epoch produced last
-// (ctrl[1]) are complete. Returns the epoch, or -1 after the budget ran out.
-__device__ int wait_epoch(const unsigned int* flags, const int* ctrl, int world, int64_t budget_ns, int where) {
-  __shared__ int s_e, s_bad;
-  if (threadIdx.x == 0) s_bad = 0;
-  __syncthreads();
-  const int e = ld_volatile(ctrl + 1);
-  if (threadIdx.x < world) {
-    const unsigned int target = kArrivals * (unsigned int)((e + 1) / 2);
-    const unsigned int* f = flags + (e & 1) * kMaxWorld + threadIdx.x;
-    const uint64_t t0 = globaltimer();
-    while ((int)(ld_acquire_u32(f) - target) < 0) {
-      if (globaltimer() - t0 > (uint64_t)budget_ns) {
-        set_status(BRAIN_ERR_TIMEOUT_PEER, where * 16 + threadIdx.x);
-        s_bad = 1;
-        break;
-      }
-    }
-  }
-  if (threadIdx.x == 0) s_e = e;
-  __syncthreads();
-  return s_bad ? -1 : s_e;
 }
 
 constexpr int kNormThreads = 256;
@@ -463,19 +473,33 @@ __device__ __forceinline__ float block_sum(float v) {
   return s;
 }
 
+// Wait until none of the 8 bf16 at p is the sentinel (bounded); returns the values, or zeros after
+// the budget ran out (status recorded).
+__device__ __forceinline__ uint4 poll_slot(const __nv_bfloat16* p, uint4 v, int64_t budget_ns, int where) {
+  if (!has_sentinel(v)) return v;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 0;; ++it) {
+    v = ld_relaxed_sys_v4(p);
+    if (!has_sentinel(v)) return v;
+    if ((it & 63u) == 63u && globaltimer() - t0 > (uint64_t)budget_ns) {
+      set_status(BRAIN_ERR_TIMEOUT_PEER, where);
+      return make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
 // residual[row] += sum_j slot_j[row]; normed[row] = rmsnorm(residual[row]) * gamma.
 // A cluster of kArParts CTAs shares one token row (each owns N / kArParts columns, one 8-element chunk
 // per thread for N = 8192); the row's sum of squares is combined through distributed shared memory.
-// The residual and gamma loads are issued before the wait for the peers' arrivals.
+// Each thread polls its 16-byte piece of every rank's slot until the sentinel is gone, then writes the
+// sentinel back for the next use of this slot parity. The residual and gamma loads are issued first.
 constexpr int kArParts = 4;
 constexpr int kArChunks = 2;  // N <= kArParts * kNormThreads * 8 * kArChunks = 16384
 
-__global__ void __launch_bounds__(kNormThreads) ar_norm_kernel(const __nv_bfloat16* slots, const unsigned int* flags,
-                                                               int* ctrl, int world, int64_t slot_elems, int N,
-                                                               __nv_bfloat16* resid, int64_t ldr,
-                                                               const __nv_bfloat16* gamma, float eps,
-                                                               __nv_bfloat16* normed, int64_t ldn,
-                                                               int64_t budget_ns) {
+__global__ void __launch_bounds__(kNormThreads) ar_norm_kernel(__nv_bfloat16* slots, int* ctrl, int world,
+                                                               int64_t slot_elems, int N, __nv_bfloat16* resid,
+                                                               int64_t ldr, const __nv_bfloat16* gamma, float eps,
+                                                               __nv_bfloat16* normed, int64_t ldn, int64_t budget_ns) {
   pdl_trigger();
   pdl_wait();
   __shared__ float s_part;
@@ -490,30 +514,38 @@ __global__ void __launch_bounds__(kNormThreads) ar_norm_kernel(const __nv_bfloat
       load8(gamma + part * cols + k, g[c]);
     }
   }
-  const int e = wait_epoch(flags, ctrl, world, budget_ns, 12);
-  const __nv_bfloat16* base = slots + (int64_t)(e & 1) * world * slot_elems + (int64_t)row * N + part * cols;
+  const int e = ld_volatile(ctrl + 1);
+  __nv_bfloat16* base = slots + (int64_t)(e & 1) * world * slot_elems + (int64_t)row * N + part * cols;
+  const uint4 empty = make_uint4(0x80008000u, 0x80008000u, 0x80008000u, 0x80008000u);
   float ss = 0.f;
-  if (e >= 0) {
 #pragma unroll
-    for (int c = 0; c < kArChunks; ++c) {
-      const int k = (c * kNormThreads + threadIdx.x) * 8;
-      if (k < cols) {
-        float f[kMaxWorld][8];
+  for (int c = 0; c < kArChunks; ++c) {
+    const int k = (c * kNormThreads + threadIdx.x) * 8;
+    if (k < cols) {
+      uint4 v[kMaxWorld];
 #pragma unroll
-        for (int j = 0; j < kMaxWorld; ++j)
-          if (j < world) load8(base + j * slot_elems + k, f[j]);
+      for (int j = 0; j < kMaxWorld; ++j)
+        if (j < world) v[j] = ld_relaxed_sys_v4(base + j * slot_elems + k);
 #pragma unroll
-        for (int j = 0; j < kMaxWorld; ++j)
-          if (j < world) {
+      for (int j = 0; j < kMaxWorld; ++j) {
+        if (j < world) {
+          __nv_bfloat16* p = base + j * slot_elems + k;
+          v[j] = poll_slot(p, v[j], budget_ns, 12 * 16 + j);
+          *reinterpret_cast<uint4*>(p) = empty;  // ready for the next use of this parity
+          const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&v[j]);
 #pragma unroll
-            for (int u = 0; u < 8; ++u) h[c][u] += f[j][u];
+          for (int u = 0; u < 4; ++u) {
+            const float2 f = __bfloat1622float2(b2[u]);
+            h[c][2 * u] += f.x;
+            h[c][2 * u + 1] += f.y;
           }
-        store8(resid + row * ldr + part * cols + k, h[c]);
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          h[c][u] = __bfloat162float(__float2bfloat16_rn(h[c][u]));  // normalise the stored stream
-          ss += h[c][u] * h[c][u];
         }
+      }
+      store8(resid + row * ldr + part * cols + k, h[c]);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        h[c][u] = __bfloat162float(__float2bfloat16_rn(h[c][u]));  // normalise the stored stream
+        ss += h[c][u] * h[c][u];
       }
     }
   }
@@ -524,7 +556,6 @@ __global__ void __launch_bounds__(kNormThreads) ar_norm_kernel(const __nv_bfloat
 #pragma unroll
   for (int r = 0; r < kArParts; ++r) tot += ld_dsmem_f32(mapa_shared(smem_u32(&s_part), (uint32_t)r));
   cluster_sync();  // peers have read s_part
-  if (e < 0) return;
   if (threadIdx.x == 0) ctrl[0] = e;  // same value from every CTA; read after this grid completes
   const float rstd = rsqrtf(tot / N + eps);
 #pragma unroll
@@ -538,25 +569,35 @@ __global__ void __launch_bounds__(kNormThreads) ar_norm_kernel(const __nv_bfloat
   }
 }
 
-// Greedy pick over the ranks' argmax keys, then the next step's layer-0 input.
+// Greedy pick over the ranks' argmax keys (each polled until non-zero, then cleared), then the next
+// step's layer-0 input.
 __global__ void __launch_bounds__(kNormThreads) pick_embed_kernel(
-    const unsigned long long* key_slots, const unsigned int* flags, int* ctrl, int world, int64_t slot_elems,
-    const __nv_bfloat16* emb, int64_t lde, int vocab, int N, __nv_bfloat16* resid, const __nv_bfloat16* gamma,
-    float eps, __nv_bfloat16* normed, int* hist, int64_t hist_ld, int* pos, int* seq_lens, int64_t budget_ns) {
+    unsigned long long* key_slots, int* ctrl, int world, int64_t slot_elems, const __nv_bfloat16* emb, int64_t lde,
+    int vocab, int N, __nv_bfloat16* resid, const __nv_bfloat16* gamma, float eps, __nv_bfloat16* normed, int* hist,
+    int64_t hist_ld, int* pos, int* seq_lens, int64_t budget_ns) {
   pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x;
-  const int e = wait_epoch(flags, ctrl, world, budget_ns, 13);
-  if (e < 0) return;
+  const int e = ld_volatile(ctrl + 1);
   __shared__ int s_tok;
   if (threadIdx.x == 0) {
     unsigned long long best = 0;
+    const uint64_t t0 = globaltimer();
     for (int j = 0; j < world; ++j) {
-      const unsigned long long k = key_slots[((int64_t)(e & 1) * world + j) * slot_elems + row];
+      unsigned long long* p = key_slots + ((int64_t)(e & 1) * world + j) * slot_elems + row;
+      unsigned long long k = ld_relaxed_sys_u64(p);
+      while (k == 0ull) {
+        if (globaltimer() - t0 > (uint64_t)budget_ns) {
+          set_status(BRAIN_ERR_TIMEOUT_PEER, 13 * 16 + j);
+          break;
+        }
+        k = ld_relaxed_sys_u64(p);
+      }
+      *p = 0ull;
       best = k > best ? k : best;
     }
     int tok = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
-    if (tok < 0 || tok >= vocab) {
+    if (best == 0ull || tok < 0 || tok >= vocab) {
       set_status(BRAIN_ERR_BAD_ARG, 14);
       tok = 0;
     }
@@ -689,14 +730,12 @@ BRAIN_API int brain_skinny_splits(int M, int N, int K) {
   return (num_kb + per - 1) / per;
 }
 
-// Per-push arrival count added to each rank's counter (consumers wait for multiples of it).
-BRAIN_API int brain_decode_arrivals() { return (int)kArrivals; }
 
 // ext (int64[32], may be null for EPI_STORE / EPI_SWIGLU):
 //   [0] world [1] rank [2] slot_elems [3] ctrl* [4] keys* [5] vocab_offset [6] hq [7] hkv [8] pos*
 //   [9] cos|sin table* [10] k pool* [11] v pool* [12] block table* [13] max_blocks [14] block_size
-//   [15] optional phase-timestamp buffer (uint64 [ctas][16]: globaltimer ns [0..7), SM clocks [8..16)) [16..24) peer slot bases
-//   [24..32) peer counter arrays (uint32 [2][8] each)
+//   [15] optional phase-timestamp buffer (uint64 [ctas][16]: globaltimer ns [0..7), SM clocks [8..16))
+//   [16..24) peer slot bases
 BRAIN_API int brain_skinny_gemm(const void* X, int64_t ldx, const void* W, int64_t ldw, int M, int N, int K, int epi,
                                 float alpha, void* out, int64_t ldc, const void* R, int64_t ldr, int splits,
                                 const int64_t* ext, cudaStream_t st) {
@@ -734,13 +773,10 @@ BRAIN_API int brain_skinny_gemm(const void* X, int64_t ldx, const void* W, int64
     a.max_blocks = (int)ext[13];
     a.block_size = (int)ext[14];
     if (a.world < 1 || a.world > kMaxWorld) return (int)cudaErrorInvalidValue;
-    for (int r = 0; r < a.world; ++r) {
-      a.peer_slots[r] = reinterpret_cast<void*>(ext[16 + r]);
-      a.peer_flags[r] = reinterpret_cast<unsigned int*>(ext[24 + r]);
-    }
+    for (int r = 0; r < a.world; ++r) a.peer_slots[r] = reinterpret_cast<void*>(ext[16 + r]);
   }
   const int tiles = (N + kRows - 1) / kRows;
-  if ((int64_t)tiles * a.splits > (int64_t)kArrivals || tiles > 65535) return (int)cudaErrorInvalidValue;
+  if (tiles > 65535) return (int)cudaErrorInvalidValue;
   if (epi == EPI_QKV && N != (a.hq + 2 * a.hkv) * kRows) return (int)cudaErrorInvalidValue;
   if (epi == EPI_SWIGLU && (N % kRows)) return (int)cudaErrorInvalidValue;
   if (epi == EPI_ARGMAX && !a.keys) return (int)cudaErrorInvalidValue;
@@ -754,9 +790,9 @@ BRAIN_API int brain_skinny_gemm(const void* X, int64_t ldx, const void* W, int64
   return launch_by_epi<64, 3>(epi, tw, tx, a, tiles, st);
 }
 
-BRAIN_API int brain_tp_ar_norm(const void* slots, const void* flags, void* ctrl, int world, int64_t slot_elems, int M,
-                               int N, void* resid, int64_t ldr, const void* gamma, float eps, void* normed,
-                               int64_t ldn, int64_t budget_ns, cudaStream_t st) {
+BRAIN_API int brain_tp_ar_norm(void* slots, void* ctrl, int world, int64_t slot_elems, int M, int N, void* resid,
+                               int64_t ldr, const void* gamma, float eps, void* normed, int64_t ldn, int64_t budget_ns,
+                               cudaStream_t st) {
   if (N % (8 * kArParts) || N > kArParts * kNormThreads * 8 * kArChunks || world < 1 || world > kMaxWorld)
     return (int)cudaErrorInvalidValue;
   if (M == 0) return 0;
@@ -773,23 +809,23 @@ BRAIN_API int brain_tp_ar_norm(const void* slots, const void* flags, void* ctrl,
   at[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = at;
   cfg.numAttrs = brain_host::g_decode_pdl ? 2 : 1;
-  return (int)cudaLaunchKernelEx(&cfg, ar_norm_kernel, reinterpret_cast<const __nv_bfloat16*>(slots),
-                                 reinterpret_cast<const unsigned int*>(flags), reinterpret_cast<int*>(ctrl), world,
-                                 slot_elems, N, reinterpret_cast<__nv_bfloat16*>(resid), ldr,
+  return (int)cudaLaunchKernelEx(&cfg, ar_norm_kernel, reinterpret_cast<__nv_bfloat16*>(slots),
+                                 reinterpret_cast<int*>(ctrl), world, slot_elems, N,
+                                 reinterpret_cast<__nv_bfloat16*>(resid), ldr,
                                  reinterpret_cast<const __nv_bfloat16*>(gamma), eps,
                                  reinterpret_cast<__nv_bfloat16*>(normed), ldn, budget_ns);
 }
 
-BRAIN_API int brain_tp_pick_embed(const void* key_slots, const void* flags, void* ctrl, int world, int64_t slot_elems,
-                                  int M, const void* emb, int64_t lde, int vocab, int N, void* resid, const void* gamma,
-                                  float eps, void* normed, int* hist, int64_t hist_ld, int* pos, int* seq_lens,
-                                  int64_t budget_ns, cudaStream_t st) {
+BRAIN_API int brain_tp_pick_embed(void* key_slots, void* ctrl, int world, int64_t slot_elems, int M, const void* emb,
+                                  int64_t lde, int vocab, int N, void* resid, const void* gamma, float eps,
+                                  void* normed, int* hist, int64_t hist_ld, int* pos, int* seq_lens, int64_t budget_ns,
+                                  cudaStream_t st) {
   if (N % 8 || N > kNormThreads * 8 * kMaxChunks || world < 1 || world > kMaxWorld) return (int)cudaErrorInvalidValue;
   if (M == 0) return 0;
   return (int)brain_host::launch(
       pick_embed_kernel, dim3(M), dim3(kNormThreads), 0, st, brain_host::g_decode_pdl != 0,
-      reinterpret_cast<const unsigned long long*>(key_slots), reinterpret_cast<const unsigned int*>(flags),
-      reinterpret_cast<int*>(ctrl), world, slot_elems, reinterpret_cast<const __nv_bfloat16*>(emb), lde, vocab, N,
-      reinterpret_cast<__nv_bfloat16*>(resid), reinterpret_cast<const __nv_bfloat16*>(gamma), eps,
-      reinterpret_cast<__nv_bfloat16*>(normed), hist, hist_ld, pos, seq_lens, budget_ns);
+      reinterpret_cast<unsigned long long*>(key_slots), reinterpret_cast<int*>(ctrl), world, slot_elems,
+      reinterpret_cast<const __nv_bfloat16*>(emb), lde, vocab, N, reinterpret_cast<__nv_bfloat16*>(resid),
+      reinterpret_cast<const __nv_bfloat16*>(gamma), eps, reinterpret_cast<__nv_bfloat16*>(normed), hist, hist_ld,
+      pos, seq_lens, budget_ns);
 }

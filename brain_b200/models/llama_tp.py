@@ -33,7 +33,7 @@ import torch
 import torch.distributed as dist
 
 from .. import _native, ops
-from ..ops.decode import (EPI_ARGMAX, EPI_PUSH, EPI_QKV, EPI_SWIGLU, ar_norm, decode_ext,
+from ..ops.decode import (EPI_ARGMAX, EPI_PUSH, EPI_QKV, EPI_SWIGLU, ar_norm, decode_ext, init_ar_slots,
                           interleave_gate_up, paged_decode_attention, pick_embed, skinny_gemm, skinny_splits)
 from .config import LlamaLiteConfig
 
@@ -43,7 +43,8 @@ def _randn(shape, gen, std, device):
 
 
 class _StepComm:
-    """Flags, all-reduce slots and argmax-key slots of the decode step (symmetric when world > 1)."""
+    """All-reduce and argmax-key receive slots of the decode step (symmetric when world > 1). Both are
+    [2 parities][world][elems]; unwritten elements hold a sentinel that the consumers poll for."""
 
     def __init__(self, batch: int, hidden: int, world: int, rank: int, group, device):
         self.world, self.rank = world, rank
@@ -51,8 +52,8 @@ class _StepComm:
         self.key_elems = batch
         ar_bytes = 2 * world * self.ar_elems * 2
         key_bytes = 2 * world * self.key_elems * 8
-        self.ar_off = 256
-        self.key_off = self.ar_off + -(-ar_bytes // 256) * 256
+        self.ar_off = 0
+        self.key_off = -(-ar_bytes // 256) * 256
         total = self.key_off + key_bytes
         if world > 1:
             from ..parallel.symm import SymmetricBuffer
@@ -67,18 +68,22 @@ class _StepComm:
             self.bases = [self.local]
         self.ctrl = torch.zeros(4, device=device, dtype=torch.int32)  # epoch consumed, produced, ticket
         self.keys = torch.zeros(batch, device=device, dtype=torch.int64)
-        self.flags_local = self.local
         self.ar_local = self.local + self.ar_off
         self.key_local = self.local + self.key_off
+        slots = (self.buf.view(torch.bfloat16, 2 * world * self.ar_elems, self.ar_off) if self.buf is not None
+                 else self._keep[self.ar_off:self.ar_off + ar_bytes].view(torch.bfloat16))
+        init_ar_slots(slots)
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier(group)  # every rank's slots hold the sentinel before any push
 
     def ext_push(self):
         return decode_ext(world=self.world, rank=self.rank, slot_elems=self.ar_elems, ctrl=self.ctrl,
-                          peer_slots=[b + self.ar_off for b in self.bases], peer_flags=self.bases)
+                          peer_slots=[b + self.ar_off for b in self.bases])
 
     def ext_argmax(self, vocab_offset: int):
         return decode_ext(world=self.world, rank=self.rank, slot_elems=self.key_elems, ctrl=self.ctrl, keys=self.keys,
-                          vocab_offset=vocab_offset, peer_slots=[b + self.key_off for b in self.bases],
-                          peer_flags=self.bases)
+                          vocab_offset=vocab_offset, peer_slots=[b + self.key_off for b in self.bases])
 
     def close(self):
         if self.buf is not None:
@@ -209,7 +214,7 @@ class LlamaTPServe:
         c = self.cfg
         skinny_gemm(self.normed, self.head[:self.v_rows], EPI_ARGMAX, ext=self.ext_argmax, splits=self.sp["head"])
         cm = self.comm
-        pick_embed(cm.key_local, cm.flags_local, cm.ctrl, self.world, cm.key_elems, self.emb, self.resid,
+        pick_embed(cm.key_local, cm.ctrl, self.world, cm.key_elems, self.emb, self.resid,
                    self.attn_norm[0], c.norm_eps, self.normed, self.hist, self.pos, self.seq_lens)
 
     def step(self):
@@ -221,11 +226,11 @@ class LlamaTPServe:
                                    self.seq_lens, splits=self.attn_splits, workspace=self.attn_ws,
                                    out=self.attn.view(B, self.hq, self.D))
             skinny_gemm(self.attn, self.wo[i], EPI_PUSH, ext=self.ext_push, splits=self.sp["o"])
-            ar_norm(cm.ar_local, cm.flags_local, cm.ctrl, self.world, cm.ar_elems, self.resid, self.ffn_norm[i],
+            ar_norm(cm.ar_local, cm.ctrl, self.world, cm.ar_elems, self.resid, self.ffn_norm[i],
                     c.norm_eps, self.normed)
             skinny_gemm(self.normed, self.w_gu[i], EPI_SWIGLU, out=self.act, splits=self.sp["gu"])
             skinny_gemm(self.act, self.w_down[i], EPI_PUSH, ext=self.ext_push, splits=self.sp["down"])
-            ar_norm(cm.ar_local, cm.flags_local, cm.ctrl, self.world, cm.ar_elems, self.resid, self.gammas_after[i],
+            ar_norm(cm.ar_local, cm.ctrl, self.world, cm.ar_elems, self.resid, self.gammas_after[i],
                     c.norm_eps, self.normed)
         self._head_and_pick()
 

@@ -97,9 +97,8 @@ _native.register({
     "brain_skinny_splits": ("brain_kernels", "iii"),
     "brain_skinny_gemm": ("brain_kernels", "plpliiiifplplips"),
     "brain_decode_set_pdl": ("brain_kernels", "i"),
-    "brain_decode_arrivals": ("brain_kernels", ""),
-    "brain_tp_ar_norm": ("brain_kernels", "pppiliiplpfplls"),
-    "brain_tp_pick_embed": ("brain_kernels", "pppilipliippfpplppls"),
+    "brain_tp_ar_norm": ("brain_kernels", "ppiliiplpfplls"),
+    "brain_tp_pick_embed": ("brain_kernels", "ppilipliippfpplppls"),
     "brain_status_decode_tp": ("brain_kernels", "pi"),
 })
 
@@ -114,7 +113,7 @@ def skinny_splits(M: int, N: int, K: int) -> int:
 
 
 def decode_ext(world=1, rank=0, slot_elems=0, ctrl=None, keys=None, vocab_offset=0, hq=0, hkv=0, pos=None,
-               rope_cs=None, k_pool=None, v_pool=None, block_table=None, peer_slots=(), peer_flags=(), trace=None):
+               rope_cs=None, k_pool=None, v_pool=None, block_table=None, peer_slots=(), trace=None):
     """The int64[32] side-argument block of ``brain_skinny_gemm`` (layout documented in the source)."""
     import ctypes
 
@@ -128,8 +127,6 @@ def decode_ext(world=1, rank=0, slot_elems=0, ctrl=None, keys=None, vocab_offset
         v[13], v[14] = block_table.shape[1], k_pool.shape[1]
     for i, s in enumerate(peer_slots):
         v[16 + i] = int(s)
-    for i, f in enumerate(peer_flags):
-        v[24 + i] = int(f)
     return (ctypes.c_int64 * 32)(*v)
 
 
@@ -160,19 +157,27 @@ def interleave_gate_up(w_gate, w_up, group: int = 64):
     return torch.stack([w_gate.view(F // group, group, K), w_up.view(F // group, group, K)], 1).reshape(2 * F, K)
 
 
-def ar_norm(slots, flags, ctrl, world, slot_elems, resid, gamma, eps, normed, budget_s=2.0):
-    """resid += sum of the `world` slots of the current epoch; normed = rmsnorm(resid) * gamma."""
+AR_SENTINEL = -0.0  # bf16 value marking an all-reduce receive slot element as not yet written
+
+
+def init_ar_slots(slots: torch.Tensor) -> torch.Tensor:
+    """Fill bf16 all-reduce receive slots with the sentinel (argmax key slots start at 0)."""
+    return slots.view(torch.int16).fill_(-32768)
+
+
+def ar_norm(slots, ctrl, world, slot_elems, resid, gamma, eps, normed, budget_s=2.0):
+    """resid += sum of the `world` slots of the current epoch (polled until written, then reset to the
+    sentinel); normed = rmsnorm(resid) * gamma."""
     M, N = resid.shape
-    _native.call("brain_tp_ar_norm", slots, flags, ctrl.data_ptr(), world, slot_elems, M, N, resid.data_ptr(),
+    _native.call("brain_tp_ar_norm", slots, ctrl.data_ptr(), world, slot_elems, M, N, resid.data_ptr(),
                  resid.stride(0), gamma.data_ptr(), float(eps), normed.data_ptr(), normed.stride(0),
                  int(budget_s * 1e9), stream(resid))
 
 
-def pick_embed(key_slots, flags, ctrl, world, slot_elems, emb, resid, gamma, eps, normed, hist, pos, seq_lens,
-               budget_s=2.0):
+def pick_embed(key_slots, ctrl, world, slot_elems, emb, resid, gamma, eps, normed, hist, pos, seq_lens, budget_s=2.0):
     """Greedy token from the ranks' argmax keys -> hist / pos / seq_lens, and the next layer-0 input."""
     M, N = resid.shape
-    _native.call("brain_tp_pick_embed", key_slots, flags, ctrl.data_ptr(), world, slot_elems, M, emb.data_ptr(),
+    _native.call("brain_tp_pick_embed", key_slots, ctrl.data_ptr(), world, slot_elems, M, emb.data_ptr(),
                  emb.stride(0), emb.shape[0], N, resid.data_ptr(), gamma.data_ptr(), float(eps), normed.data_ptr(),
                  hist.data_ptr(), hist.stride(0), pos.data_ptr(), seq_lens.data_ptr(), int(budget_s * 1e9),
                  stream(resid))

@@ -4,7 +4,7 @@ import pytest
 import torch
 
 from brain_b200.ops import check_status
-from brain_b200.ops.decode import (EPI_ARGMAX, EPI_PUSH, EPI_QKV, EPI_SWIGLU, ar_norm, decode_ext,
+from brain_b200.ops.decode import (EPI_ARGMAX, EPI_PUSH, EPI_QKV, EPI_SWIGLU, ar_norm, decode_ext, init_ar_slots,
                                    interleave_gate_up, pick_embed, skinny_gemm)
 from brain_b200.ops.rope import rope_ref, rope_table
 
@@ -78,26 +78,22 @@ def test_push_ar_norm_single_rank():
     gamma = (1.0 + 0.1 * _rand(N, seed=14).float()).bfloat16()
     resid0 = resid.clone()
     slot_elems = M * N
-    slots = torch.zeros(2 * slot_elems, device="cuda", dtype=torch.bfloat16)
-    flags = torch.zeros(64, device="cuda", dtype=torch.int32)
+    slots = init_ar_slots(torch.empty(2 * slot_elems, device="cuda", dtype=torch.bfloat16))
     ctrl = torch.zeros(4, device="cuda", dtype=torch.int32)
-    ext = decode_ext(world=1, rank=0, slot_elems=slot_elems, ctrl=ctrl, peer_slots=[slots.data_ptr()],
-                     peer_flags=[flags.data_ptr()])
+    ext = decode_ext(world=1, rank=0, slot_elems=slot_elems, ctrl=ctrl, peer_slots=[slots.data_ptr()])
     normed = torch.empty_like(resid)
-    for step in range(3):  # both slot parities and a reused ticket counter
+    for step in range(3):  # both slot parities, each reused
         skinny_gemm(x, w, epi=EPI_PUSH, ext=ext)
-        ar_norm(slots.data_ptr(), flags.data_ptr(), ctrl, 1, slot_elems, resid, gamma, 1e-5, normed)
+        ar_norm(slots.data_ptr(), ctrl, 1, slot_elems, resid, gamma, 1e-5, normed)
         h = resid0.float() + (step + 1) * (x.float() @ w.float().t())
         assert not check_status()
         assert (resid.float() - h).abs().max().item() < 0.1 * (step + 1)
         hn = resid.float()
         ref = hn * torch.rsqrt(hn.pow(2).mean(-1, keepdim=True) + 1e-5) * gamma.float()
         assert (normed.float() - ref).abs().max().item() < 5e-2
-    # epochs 1..3 consumed and produced; counters per parity hold the pushes' fixed arrival totals
-    from brain_b200 import _native
-    arrivals = int(_native.fn("brain_decode_arrivals")())
+    # epochs 1..3 produced and consumed; every slot is back to the sentinel
     assert int(ctrl[0]) == 3 and int(ctrl[1]) == 3
-    assert int(flags[8].item()) == 2 * arrivals and int(flags[0].item()) == arrivals
+    assert bool((slots.view(torch.int16) == -32768).all())
 
 
 def test_argmax_pick_embed_single_rank():
@@ -107,18 +103,15 @@ def test_argmax_pick_embed_single_rank():
     gamma = torch.ones(N, device="cuda", dtype=torch.bfloat16)
     keys = torch.zeros(M, device="cuda", dtype=torch.int64)
     key_slots = torch.zeros(2 * M, device="cuda", dtype=torch.int64)
-    flags = torch.zeros(64, device="cuda", dtype=torch.int32)
     ctrl = torch.zeros(4, device="cuda", dtype=torch.int32)
-    ext = decode_ext(world=1, rank=0, slot_elems=M, ctrl=ctrl, keys=keys, peer_slots=[key_slots.data_ptr()],
-                     peer_flags=[flags.data_ptr()])
+    ext = decode_ext(world=1, rank=0, slot_elems=M, ctrl=ctrl, keys=keys, peer_slots=[key_slots.data_ptr()])
     hist = torch.zeros(M, 16, device="cuda", dtype=torch.int32)
     pos = torch.full((M,), 4, device="cuda", dtype=torch.int32)
     seq_lens = pos + 1
     resid = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     normed = torch.empty_like(resid)
     skinny_gemm(x, w, epi=EPI_ARGMAX, ext=ext)
-    pick_embed(key_slots.data_ptr(), flags.data_ptr(), ctrl, 1, M, emb, resid, gamma, 1e-5, normed, hist, pos,
-               seq_lens)
+    pick_embed(key_slots.data_ptr(), ctrl, 1, M, emb, resid, gamma, 1e-5, normed, hist, pos, seq_lens)
     assert not check_status()
     logits = x.float() @ w.float().t()
     tok = hist[:, 5].long()
@@ -128,4 +121,4 @@ def test_argmax_pick_embed_single_rank():
     assert torch.equal(pos.cpu(), torch.full((M,), 5, dtype=torch.int32))
     assert torch.equal(seq_lens.cpu(), torch.full((M,), 6, dtype=torch.int32))
     assert torch.equal(resid, emb[tok])
-    assert int(keys.abs().sum()) == 0
+    assert int(keys.abs().sum()) == 0 and int(key_slots.abs().sum()) == 0
