@@ -96,7 +96,8 @@ def main():
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--micro-batch", type=int, default=2)
     ap.add_argument("--layers", type=int, default=32, help="development only: fewer layers is not the benchmark")
-    ap.add_argument("--comm", default="nccl", choices=["nccl", "nvlink"])
+    ap.add_argument("--comm", default="nvlink", choices=["nccl", "nvlink"],
+                    help="gradient reduction: fused NVLink kernels (default) or NCCL")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--workload", default="train", choices=["train", "decode"],
                     help="train: Llama-3-8B DDP (headline); decode: Llama-3-70B-shape TP=N greedy decode")
