@@ -145,7 +145,7 @@ def main(argv=None) -> int:
     kv.normal_()
     q = rnd(B, hq, D, std=1.0)
     ao = torch.empty(B, hq, D, device=dev, dtype=torch.bfloat16)
-    aws = torch.empty(1 << 22, device=dev, dtype=torch.float32)
+    aws = torch.zeros(1 << 22, device=dev, dtype=torch.float32)
     if want("paged_decode_attention"):
         us = timeit(lambda i: paged_decode_attention(q, kv[0], kv[1], table, lens, out=ao, workspace=aws), a.iters)
         report("paged_decode_attention", us, B * a.kv_len * hkv * D * 2 * 2, kv_len=a.kv_len)

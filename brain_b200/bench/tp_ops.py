@@ -1,0 +1,86 @@
+"""Tensor-parallel prefill operations timed on every rank of the launch (one GPU per rank): the
+pipelined all-gather -> GEMM (peer row blocks pulled by a copy kernel or by the copy engines), the
+GEMM -> reduce-scatter epilogue push, the row all-gather, and the same GEMMs on local data for
+comparison. Shapes default to one rank of Llama-3-70B at TP = N with 8192 tokens per rank.
+
+Run: ``python -m torch.distributed.run --nproc-per-node N --master-addr 127.0.0.1 -m brain_b200.bench.tp_ops``.
+Rank 0 prints one JSON line per operation: milliseconds (CUDA events, max over ranks) and the NVLink
+bytes each rank receives.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import sys
+
+import torch
+import torch.distributed as dist
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--tokens-per-rank", type=int, default=8192)
+    ap.add_argument("--hidden", type=int, default=8192)
+    ap.add_argument("--qkv-cols", type=int, default=0, help="per-rank QKV width (default: 70B shape at TP = N)")
+    ap.add_argument("--iters", type=int, default=5)
+    a = ap.parse_args(argv)
+
+    from ..parallel import dist as bdist
+    from ..parallel.tensor_parallel import TPContext, all_gather_rows, gemm_allgather_a, gemm_push
+    from ..ops.gemm import gemm
+    ctx = bdist.init(timeout_s=120)
+    W, rank, dev = ctx.world_size, ctx.rank, ctx.device
+    tp = TPContext()
+    T, d = a.tokens_per_rank, a.hidden
+    qkv = a.qkv_cols or (64 + 16) * 128 // W
+    attn = 64 * 128 // W
+    g = torch.Generator(device=dev).manual_seed(rank)
+    x = torch.randn(T, d, device=dev, generator=g).bfloat16()
+    w_qkv = (torch.randn(qkv, d, device=dev, generator=g) * 0.02).bfloat16()
+    a_full = torch.randn(T * W, attn, device=dev, generator=g).bfloat16()
+    w_o = (torch.randn(d, attn, device=dev, generator=g) * 0.02).bfloat16()
+
+    def timed(fn):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(a.iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([s.elapsed_time(e) / a.iters], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def report(name, ms, nvlink_bytes, **extra):
+        if rank == 0:
+            print(json.dumps({"op": name, "world": W, "ms": round(ms, 3), "nvlink_in_bytes_per_rank": nvlink_bytes,
+                              "nvlink_in_gbs": round(nvlink_bytes / (ms / 1e3) / 1e9, 1) if nvlink_bytes else None,
+                              **extra}), flush=True)
+
+    xf = torch.randn(T * W, d, device=dev, generator=g).bfloat16()
+    report("local_gemm_qkv_all_rows", timed(lambda: gemm(xf, w_qkv, trans_b=True)), 0, M=T * W, N=qkv, K=d)
+    for mode in ("sm", "ce"):
+        tp.ag_copy = mode
+        report(f"ag_gemm_qkv_{mode}", timed(lambda: gemm_allgather_a(tp, x, w_qkv)), (W - 1) * T * d * 2,
+               M=T * W, N=qkv, K=d)
+    tp.ag_copy = "sm"
+    report("local_gemm_o_all_rows", timed(lambda: gemm(a_full, w_o, trans_b=True)), 0, M=T * W, N=d, K=attn)
+    for mode in ("pull", "push"):
+        tp.rs_mode = mode
+        report(f"gemm_rs_{mode}_o", timed(lambda: gemm_push(tp, a_full, w_o, 1, T)), (W - 1) * T * d * 2,
+               M=T * W, N=d, K=attn)
+    tp.rs_mode = "pull"
+    report("all_gather_rows", timed(lambda: all_gather_rows(tp, x)), (W - 1) * T * d * 2)
+    tp.comm.check()
+    tp.close()
+    tp.comm.close()
+    bdist.shutdown()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -5,13 +5,13 @@
 // token included). q [B, Hq, D] (row stride qs elements), out [B, Hq, D].
 //
 // Split-K flash decoding, GQA-packed: a CTA owns one (sequence, kv head) and a contiguous slice of
-// the sequence's KV blocks; the G = Hq / Hkv query heads of the group are processed together, so
-// every K/V block is read from HBM once (decode is bound by reading the cache and the weights).
-// K/V blocks stream through a cp.async double buffer; scores and the P.V product run on CUDA cores
-// in f32 (a G x 64 x 128 block is too small for tensor-core tiles to pay); each split writes its
-// running (max, sum, unnormalised output) and a combine kernel merges the splits with the
-// log-sum-exp rule. The KV append kernel applies RoPE (NeoX half split) to the new token's q and k
-// and writes k / v into their paged slots.
+// the sequence's KV blocks; the G = Hq / Hkv query heads of the group form the M = 16 side of
+// mma.sync tiles, so every K/V block is read from HBM once (decode is bound by reading the cache and
+// the weights) and S = Q K^T and O += P V run on tensor cores. K/V chunks of 64 keys stream through
+// a 3-stage cp.async ring gathered through the block table into XOR-swizzled shared memory. Each split
+// writes its running (max, sum, unnormalised output); the last split CTA of a (sequence, kv head)
+// (atomic ticket) merges the splits with the log-sum-exp rule. The KV append kernel applies RoPE
+// (NeoX half split) to the new token's q and k and writes k / v into their paged slots.
 // Reference: the contiguous, realloc-per-append KvCache::update (crates/brain-transformer/src/kv_cache.rs:83-158)
 // and SDPA (attention/scaled.rs:41-139); LlamaLite::generate recomputes everything instead.
 #include "common.cuh"
@@ -48,7 +48,12 @@ struct DecodeArgs {
   int splits;
   float* part_o;   // [B, Hkv, splits, G, D]
   float* part_ml;  // [B, Hkv, splits, G, 2]
+  int* tickets;    // [B, Hkv] split arrivals, zero between launches
+  __nv_bfloat16* out;
+  int64_t ob, oh;  // strides of out [B, Hq, D]
 };
+
+constexpr int kMaxSplitsDec = 64;
 
 // ---- warp-level tensor-core helpers (mma.sync m16n8k16 bf16 -> f32, ldmatrix from swizzled rows)
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -284,39 +289,82 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(DecodeArgs a) {
     a.part_ml[(base + tid) * 2] = M;
     a.part_ml[(base + tid) * 2 + 1] = L;
   }
-}
 
-// out[b, h, :] = sum_s w_s o_s / sum_s w_s l_s with w_s = exp2(m_s - max_s m_s)   (one warp per (b, h))
-template <int D>
-__global__ void decode_combine_kernel(DecodeArgs a, __nv_bfloat16* out, int64_t ob, int64_t oh) {
-  pdl_trigger();
-  pdl_wait();
-  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  const int lane = threadIdx.x % 32;
-  if (wid >= (int64_t)a.B * a.Hq) return;
-  const int b = (int)(wid / a.Hq), h = (int)(wid % a.Hq);
-  const int G = a.Hq / a.Hkv;
-  const int hk = h / G, g = h % G;
-  float mmax = -INFINITY;
-  for (int s = 0; s < a.splits; ++s)
-    mmax = fmaxf(mmax, a.part_ml[((((int64_t)b * a.Hkv + hk) * a.splits + s) * G + g) * 2]);
-  const float muse = mmax == -INFINITY ? 0.f : mmax;
-  float num[D / 32];
-#pragma unroll
-  for (int j = 0; j < D / 32; ++j) num[j] = 0.f;
-  float den = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
-    const int64_t idx = (((int64_t)b * a.Hkv + hk) * a.splits + s) * G + g;
-    const float m = a.part_ml[idx * 2], l = a.part_ml[idx * 2 + 1];
-    const float w = m == -INFINITY ? 0.f : ex2_fast(m - muse);
-    den += w * l;
-#pragma unroll
-    for (int j = 0; j < D / 32; ++j) num[j] += w * a.part_o[idx * D + lane + 32 * j];
+  // ---- the last split CTA of (b, hk) merges all splits: out = sum_s w_s o_s / sum_s w_s l_s with
+  // w_s = exp2(m_s - max_s m_s) (atomic ticket; no separate combine launch)
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) {
+    const int old = atomicAdd(a.tickets + bh, 1);
+    s_last = old == a.splits - 1;
+    if (s_last) a.tickets[bh] = 0;  // ready for the next launch
   }
-  const float inv = den > 0.f ? 1.f / den : 0.f;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  float* sw = so;                             // [G][kMaxSplitsDec] split weights (merge scratch is free)
+  float* sm2 = sw + kMaxG * kMaxSplitsDec;    // [G][kMaxSplitsDec] split maxima, then sums
+  float* sl2 = sm2 + kMaxG * kMaxSplitsDec;
+  float* sinv = sl2 + kMaxG * kMaxSplitsDec;  // [G] 1 / denominator
+  const int64_t base0 = ((int64_t)b * a.Hkv + hk) * a.splits * G;
+  // every (head, split) statistic is loaded at once (one L2 round trip), then reduced from smem
+  for (int idx = tid; idx < G * a.splits; idx += kThreads) {
+    const int sp = idx / G, g = idx % G;
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + base0 + idx);
+    sm2[g * kMaxSplitsDec + sp] = ml.x;
+    sl2[g * kMaxSplitsDec + sp] = ml.y;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float M = -INFINITY;
+    for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, sm2[tid * kMaxSplitsDec + sp]);
+    const float muse = M == -INFINITY ? 0.f : M;
+    float den = 0.f;
+    for (int sp = 0; sp < a.splits; ++sp) {
+      const float m = sm2[tid * kMaxSplitsDec + sp];
+      const float w = m == -INFINITY ? 0.f : ex2_fast(m - muse);
+      sw[tid * kMaxSplitsDec + sp] = w;
+      den += w * sl2[tid * kMaxSplitsDec + sp];
+    }
+    sinv[tid] = den > 0.f ? 1.f / den : 0.f;
+  }
+  __syncthreads();
+  // outputs: thread -> 4 consecutive dims of one head per pass; the splits' loads are batched 4 deep
+  for (int i = tid * 4; i < G * D; i += kThreads * 4) {
+    const int g = i / D, d = i % D;
+    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float4* src = reinterpret_cast<const float4*>(a.part_o + (base0 + g) * D + d);
+    const int64_t stride4 = (int64_t)G * D / 4;  // one split further
+    int sp = 0;
+    for (; sp + 4 <= a.splits; sp += 4) {
+      float4 v[4];
 #pragma unroll
-  for (int j = 0; j < D / 32; ++j)
-    out[(int64_t)b * ob + (int64_t)h * oh + lane + 32 * j] = __float2bfloat16_rn(num[j] * inv);
+      for (int u = 0; u < 4; ++u) v[u] = __ldcg(src + (sp + u) * stride4);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float w = sw[g * kMaxSplitsDec + sp + u];
+        num.x += w * v[u].x;
+        num.y += w * v[u].y;
+        num.z += w * v[u].z;
+        num.w += w * v[u].w;
+      }
+    }
+    for (; sp < a.splits; ++sp) {
+      const float4 v = __ldcg(src + sp * stride4);
+      const float w = sw[g * kMaxSplitsDec + sp];
+      num.x += w * v.x;
+      num.y += w * v.y;
+      num.z += w * v.z;
+      num.w += w * v.w;
+    }
+    const float inv = sinv[g];
+    __nv_bfloat16* o = a.out + (int64_t)b * a.ob + (int64_t)(hk * G + g) * a.oh + d;
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(num.x * inv, num.y * inv);
+    const __nv_bfloat162 hi = __floats2bfloat162_rn(num.z * inv, num.w * inv);
+    reinterpret_cast<__nv_bfloat162*>(o)[0] = lo;
+    reinterpret_cast<__nv_bfloat162*>(o)[1] = hi;
+  }
 }
 
 // New token: rotate q (in place) and k, write k and v into their paged slots.
@@ -371,21 +419,22 @@ int launch_decode(const DecodeArgs& a, void* out, int64_t ob, int64_t oh, cudaSt
     attr[dev & 63] = true;
   }
   const bool pdl = brain_host::g_decode_pdl != 0;
-  cudaError_t e = brain_host::launch(decode_split_kernel<D>, dim3(a.splits, a.B * a.Hkv), dim3(kThreads), dyn, st,
-                                     pdl, a);
-  if (e != cudaSuccess) return (int)e;
-  const int64_t warps = (int64_t)a.B * a.Hq;
-  return (int)brain_host::launch(decode_combine_kernel<D>, dim3((unsigned)((warps + 3) / 4)), dim3(128), 0, st, pdl,
-                                 a, reinterpret_cast<__nv_bfloat16*>(out), ob, oh);
+  (void)out;
+  (void)ob;
+  (void)oh;
+  return (int)brain_host::launch(decode_split_kernel<D>, dim3(a.splits, a.B * a.Hkv), dim3(kThreads), dyn, st, pdl,
+                                 a);
 }
 
 }  // namespace
 
 BRAIN_STATUS_READER(attention_decode)
 
-// Number of f32 elements of the split workspace: o part B*Hkv*splits*G*D, ml part B*Hkv*splits*G*2.
+// Number of 4-byte elements of the workspace: split outputs B*Hkv*splits*G*D f32, split (max, sum)
+// B*Hkv*splits*G*2 f32, then B*Hkv int32 tickets that must be zero before the first call (every call
+// leaves them zero).
 BRAIN_API int64_t brain_decode_workspace(int B, int Hq, int Hkv, int D, int splits) {
-  return (int64_t)B * Hq * splits * (D + 2);
+  return (int64_t)B * Hq * splits * (D + 2) + (int64_t)B * Hkv;
 }
 
 // Pick a split count so that B * Hkv * splits fills the GPU (about two CTAs per SM).
@@ -394,6 +443,7 @@ BRAIN_API int brain_decode_splits(int B, int Hkv, int max_len) {
   int want = (2 * brain_host::num_sms()) / (ctas > 0 ? ctas : 1);  // one wave at two CTAs per SM
   const int chunks = (max_len + kBlock - 1) / kBlock;
   if (want > chunks) want = chunks;
+  if (want > kMaxSplitsDec) want = kMaxSplitsDec;
   return want < 1 ? 1 : want;
 }
 
@@ -412,9 +462,14 @@ BRAIN_API int brain_decode_attention(const void* q, int64_t qb, int64_t qh, cons
   a.table = table; a.max_blocks = max_blocks; a.seq_lens = seq_lens; a.block_size = block_size;
   a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.D = D;
   a.scale_log2 = scale * 1.4426950408889634f;
+  if (splits < 1 || splits > kMaxSplitsDec) return (int)cudaErrorInvalidValue;
   a.splits = splits;
   a.part_o = workspace;
   a.part_ml = workspace + (int64_t)B * Hq * splits * D;
+  a.tickets = reinterpret_cast<int*>(workspace + (int64_t)B * Hq * splits * (D + 2));
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.ob = ob;
+  a.oh = oh;
   if (B * Hkv > 65535) return (int)cudaErrorInvalidValue;
   return D == 64 ? launch_decode<64>(a, out, ob, oh, st) : launch_decode<128>(a, out, ob, oh, st);
 }

@@ -53,7 +53,7 @@ constexpr int kRows = 128;
 constexpr int kBK = 64;
 constexpr int kThreads = 128;
 constexpr int kMaxWorld = 8;
-constexpr int kMaxSplits = 8;        // portable cluster size
+constexpr int kMaxSplits = 16;       // cluster size: 8 is portable, 16 needs the non-portable opt-in
 constexpr unsigned short kSentinel = 0x8000;  // bf16 -0.0: "not written yet" in a receive slot
 
 enum Epi : int { EPI_STORE = 0, EPI_PUSH = 2, EPI_SWIGLU = 3, EPI_QKV = 4, EPI_ARGMAX = 5 };
@@ -92,12 +92,7 @@ __device__ __forceinline__ unsigned long long argmax_key(float v, int64_t idx) {
 
 __device__ __forceinline__ int ld_volatile(const int* p) { return *reinterpret_cast<const volatile int*>(p); }
 
-// f32 load from / store to the shared memory of a CTA of this cluster (address from mapa_shared).
-__device__ __forceinline__ float ld_dsmem_f32(uint32_t addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
-  return v;
-}
+// f32 store to the shared memory of a CTA of this cluster (address from mapa_shared).
 __device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
   asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v));
 }
@@ -502,7 +497,7 @@ __global__ void __launch_bounds__(kNormThreads) ar_norm_kernel(__nv_bfloat16* sl
                                                                __nv_bfloat16* normed, int64_t ldn, int64_t budget_ns) {
   pdl_trigger();
   pdl_wait();
-  __shared__ float s_part;
+  __shared__ float s_parts[kArParts];
   const int part = blockIdx.x, row = blockIdx.y;
   const int cols = N / kArParts;
   float h[kArChunks][8], g[kArChunks][8];
@@ -550,12 +545,13 @@ __global__ void __launch_bounds__(kNormThreads) ar_norm_kernel(__nv_bfloat16* sl
     }
   }
   ss = block_sum(ss);
-  if (threadIdx.x == 0) s_part = ss;
+  // every CTA of the row's cluster stores its partial sum of squares into every CTA's s_parts; one
+  // barrier, then each sums locally (no remote reads, so no second barrier before exit)
+  if (threadIdx.x < kArParts) st_dsmem_f32(mapa_shared(smem_u32(&s_parts[part]), (uint32_t)threadIdx.x), ss);
   cluster_sync();
   float tot = 0.f;
 #pragma unroll
-  for (int r = 0; r < kArParts; ++r) tot += ld_dsmem_f32(mapa_shared(smem_u32(&s_part), (uint32_t)r));
-  cluster_sync();  // peers have read s_part
+  for (int r = 0; r < kArParts; ++r) tot += s_parts[r];
   if (threadIdx.x == 0) ctrl[0] = e;  // same value from every CTA; read after this grid completes
   const float rstd = rsqrtf(tot / N + eps);
 #pragma unroll
@@ -645,8 +641,31 @@ template <typename K>
 cudaError_t set_smem_attrs(K kern, int bytes) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
   return cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
                               (int)cudaSharedmemCarveoutMaxShared);
+}
+
+// Whether a cluster of `splits` skinny-GEMM CTAs can be resident on this GPU at all.
+template <int NT, int STAGES>
+bool cluster_fits(int splits) {
+  using S = SkSmem<NT, STAGES>;
+  auto kern = skinny_gemm_kernel<NT, STAGES, EPI_STORE>;
+  if (set_smem_attrs(kern, (int)S::TOTAL) != cudaSuccess) return false;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(splits, 1);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = S::TOTAL;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = splits;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  int n = 0;
+  return cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0;
 }
 
 template <int NT, int STAGES, int EPI>
@@ -716,15 +735,27 @@ BRAIN_API int brain_decode_set_pdl(int on) {
   return old;
 }
 
-// Split count (= cluster size, at most 8) for a skinny GEMM: about two CTAs per SM in one wave (the
+// Split count (= cluster size, at most 16) for a skinny GEMM: about two CTAs per SM in one wave (the
 // ~100 KB CTAs fit two per SM; measured residency, not the occupancy API, which reports one), at least
-// 4 k-blocks per split, no empty split.
+// 4 k-blocks per split, no empty split; above 8 only where a 16-CTA cluster fits on this GPU.
 BRAIN_API int brain_skinny_splits(int M, int N, int K) {
-  (void)M;
   const int tiles = (N + kRows - 1) / kRows;
   const int num_kb = (K + kBK - 1) / kBK;
   int s = std::max(1, (2 * brain_host::num_sms()) / std::max(tiles, 1));
   s = std::min(s, kMaxSplits);
+  if (s > 8) {
+    static int fits16[64][3];  // [device][token tile]: 0 unknown, 1 yes, 2 no
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int NT = nt_for(M), nti = NT == 16 ? 0 : (NT == 32 ? 1 : 2);
+    int& f = fits16[dev & 63][nti];
+    if (f == 0) {
+      const bool ok = NT == 16 ? cluster_fits<16, 5>(kMaxSplits)
+                               : (NT == 32 ? cluster_fits<32, 4>(kMaxSplits) : cluster_fits<64, 3>(kMaxSplits));
+      f = ok ? 1 : 2;
+    }
+    if (f != 1) s = 8;
+  }
   s = std::min(s, std::max(1, num_kb / 4));
   const int per = (num_kb + s - 1) / s;
   return (num_kb + per - 1) / per;

@@ -152,7 +152,7 @@ class LlamaTPServe:
         self.act = torch.empty(B, self.F, device=dev, dtype=torch.bfloat16)
         self.attn_splits = int(_native.fn("brain_decode_splits")(B, self.hkv, max_len))
         n_ws = int(_native.fn("brain_decode_workspace")(B, self.hq, self.hkv, self.D, self.attn_splits))
-        self.attn_ws = torch.empty(n_ws, device=dev, dtype=torch.float32)
+        self.attn_ws = torch.zeros(n_ws, device=dev, dtype=torch.float32)
         self.comm = _StepComm(B, d, self.world, self.rank, group, dev)
         self.tp = None  # TPContext for the sequence-parallel prefill (created on first use)
         self.graph = None

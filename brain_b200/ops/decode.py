@@ -3,7 +3,9 @@
 ``paged_decode_attention(q, k_pool, v_pool, block_table, seq_lens)``: q [B, Hq, D] (one new token
 per sequence, any strides with unit stride on D), pools [num_blocks, block_size, Hkv, D],
 block_table [B, max_blocks] int32, seq_lens [B] int32 (cached tokens, the new one included).
-On CPU the cache is gathered per sequence and the reference SDPA is used.
+A caller-provided ``workspace`` (f32, ``brain_decode_workspace`` elements) must start zeroed: its tail
+holds per-(sequence, kv head) tickets that every call leaves at zero. On CPU the cache is gathered per
+sequence and the reference SDPA is used.
 """
 from __future__ import annotations
 
@@ -37,7 +39,7 @@ def paged_decode_attention(q, k_pool, v_pool, block_table, seq_lens, scale=None,
         splits = int(_native.fn("brain_decode_splits")(B, Hkv, ml))
     if workspace is None:
         n = int(_native.fn("brain_decode_workspace")(B, Hq, Hkv, D, splits))
-        workspace = torch.empty(n, device=q.device, dtype=torch.float32)
+        workspace = torch.zeros(n, device=q.device, dtype=torch.float32)
     if out is None:
         out = torch.empty(B, Hq, D, device=q.device, dtype=q.dtype)
     _native.call("brain_decode_attention", q.data_ptr(), q.stride(0), q.stride(1), k_pool.data_ptr(),

@@ -49,6 +49,14 @@ class TPContext:
         self._local: dict = {}
         self.side = None
         self.calls = 0
+        # how AG -> GEMM pulls the peers' row blocks: "sm" = copy kernel of NVLink peer loads on a side
+        # stream, "ce" = copy engines (cudaMemcpyAsync per peer)
+        self.ag_copy = "sm"
+        # GEMM -> reduce-scatter: "pull" = GEMM into symmetric memory, barrier, every rank pulls and sums
+        # its own rows from all peers with coalesced NVLink loads; "push" = the GEMM epilogue stores
+        # each row into its owner's receive slot (scattered 16-byte remote stores: efficient only for
+        # small outputs)
+        self.rs_mode = "pull"
 
     def symm(self, name: str, nbytes: int, parity: int):
         """Symmetric buffer `name` (double-buffered by parity) of at least nbytes."""
@@ -99,10 +107,12 @@ def _i64(vals):
 
 def gemm_push(ctx: TPContext, a: torch.Tensor, w: torch.Tensor, mode: int, rows_per_rank: int,
               b_mn: int = 0) -> torch.Tensor:
-    """C = a @ w.T (w [N, K]; or a @ w for b_mn=1, w [K, N]), reduced over ranks in the GEMM epilogue.
+    """C = a @ w.T (w [N, K]; or a @ w for b_mn=1, w [K, N]), reduced over ranks.
 
-    mode 1 (reduce-scatter): returns this rank's rows [rank*rows_per_rank, ...) of the sum.
-    mode 2 (all-reduce): returns the full sum [M, N].
+    mode 1 (reduce-scatter): returns this rank's rows [rank*rows_per_rank, ...) of the sum; by default
+    (``ctx.rs_mode == "pull"``) each rank pulls its rows from the peers' products, otherwise the GEMM
+    epilogue pushes them.
+    mode 2 (all-reduce): returns the full sum [M, N]; the GEMM epilogue pushes every row to every rank.
     """
     M, K = a.shape
     N = w.shape[1] if b_mn else w.shape[0]
@@ -111,6 +121,14 @@ def gemm_push(ctx: TPContext, a: torch.Tensor, w: torch.Tensor, mode: int, rows_
     out_rows = rows_per_rank if mode == 1 else M
     slot = out_rows * N
     par = ctx.next_parity()
+    if mode == 1 and ctx.rs_mode == "pull":
+        full = ctx.symm("rs_full", M * N * 2, par)
+        gemm(a, w, trans_b=not b_mn, out=full.view(torch.bfloat16, M * N).view(M, N))
+        ctx.comm.barrier(40)
+        out = torch.empty(out_rows, N, device=a.device, dtype=torch.bfloat16)
+        _native.call("brain_comm_reduce_pull", full.peer_array(0), ctx.rank * slot, ctx.rank, W, out.data_ptr(), slot,
+                     1, 1.0, _stream())
+        return out
     recv = ctx.symm("recv", W * slot * 2, par)
     _native.call("brain_gemm_bf16_tp", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), b_mn, None, N,
                  recv.peer_array(0), mode, ctx.rank, W, rows_per_rank if mode == 1 else M, slot, None, 0, M, N, K,
@@ -126,9 +144,9 @@ def gemm_allgather_a(ctx: TPContext, a_local: torch.Tensor, w: torch.Tensor, b_m
     """C = concat_ranks(a_local) @ w.T (or @ w for b_mn=1), pipelined by row block.
 
     The local block's GEMM starts at once; a side stream pulls every other rank's block from its
-    symmetric staging buffer with the copy engines (one copy per peer, nearest peers first), and
-    each remote block's GEMM waits only for its own copy. Compute and NVLink transfer overlap and
-    every GEMM reads this GPU's memory.
+    symmetric staging buffer (nearest peers first; a copy kernel of NVLink peer loads, or the copy
+    engines with ``ctx.ag_copy = "ce"``), and each remote block's GEMM waits only for its own copy.
+    Compute and NVLink transfer overlap and every GEMM reads this GPU's memory.
     """
     T, K = a_local.shape
     N = w.shape[1] if b_mn else w.shape[0]
@@ -144,8 +162,9 @@ def gemm_allgather_a(ctx: TPContext, a_local: torch.Tensor, w: torch.Tensor, b_m
     side.wait_stream(main)
     order = [(r + i) % W for i in range(1, W)]
     events = []
+    fn = "brain_comm_copy_async" if ctx.ag_copy == "ce" else "brain_comm_copy"
     for j in order:
-        _native.call("brain_comm_copy_async", stage.ptrs[j], gather[j].data_ptr(), T * K * 2, side.cuda_stream)
+        _native.call(fn, stage.ptrs[j], gather[j].data_ptr(), T * K * 2, side.cuda_stream)
         ev = torch.cuda.Event()
         ev.record(side)
         events.append(ev)
