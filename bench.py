@@ -99,8 +99,9 @@ def main():
     ap.add_argument("--comm", default="nvlink", choices=["nccl", "nvlink"],
                     help="gradient reduction: fused NVLink kernels (default) or NCCL")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--workload", default="train", choices=["train", "decode"],
-                    help="train: Llama-3-8B DDP (headline); decode: Llama-3-70B-shape TP=N greedy decode")
+    ap.add_argument("--workload", default="train", choices=["train", "decode", "vit", "gptlite-cpu"],
+                    help="train: Llama-3-8B DDP (headline); decode: Llama-3-70B-shape TP=N greedy decode; "
+                         "vit: ViT-B/16 DDP images/s; gptlite-cpu: the GPT-lite data-parallel config on CPU ranks")
     ap.add_argument("--decode", default="auto", choices=["auto", "on", "off"],
                     help="also measure the 70B TP decode inside the train run (auto: when N == 8)")
     ap.add_argument("--decode-batch", type=int, default=32)
@@ -122,11 +123,15 @@ def main():
     from brain_b200.models import LlamaLite, LlamaLiteConfig
     from brain_b200.parallel import DataParallel, dist as bdist
 
+    if args.workload == "gptlite-cpu":
+        return run_gptlite_cpu(args)
     ctx = bdist.init(timeout_s=300)
     rank, world = ctx.rank, ctx.world_size
     if world != args.gpus:
         log(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}")
     dev = ctx.device
+    if args.workload == "vit":
+        return run_vit(args, ctx)
     decode = None
     if args.workload == "decode" or args.decode == "on" or (args.decode == "auto" and world == 8):
         try:
@@ -241,6 +246,146 @@ def main():
             out["decode_70b"] = decode
         print(json.dumps(out), flush=True)
     del dp, model
+    bdist.shutdown()
+    return 0
+
+
+def _max_over_ranks(v, dev):
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], device=dev)
+    if dist.is_initialized() and dist.get_world_size() > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_vit(args, ctx) -> int:
+    """ViT-B/16 DDP training throughput (images/s): 224x224x3 images ~N(0,1), 1000 classes with
+    uniform labels, batch 256 per GPU (weak scaling), AdamW, bf16; gradients through the same
+    data-parallel engine (fused NVLink reduce-scatter + AdamW by default)."""
+    import torch
+
+    from brain_b200 import _native
+    from brain_b200.models.config import ViTConfig
+    from brain_b200.models.families import ViT
+    from brain_b200.parallel import DataParallel, dist as bdist
+
+    rank, world, dev = ctx.rank, ctx.world_size, ctx.device
+    cfg = ViTConfig.vit_b16()
+    B = 256
+    model = ViT(cfg, device=dev, dtype=torch.bfloat16, seed=0)
+    dp = DataParallel(model, lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.05, grad_dtype=torch.bfloat16,
+                      comm=args.comm)
+    gen = torch.Generator(device=dev).manual_seed(10 + rank)
+    pool = [(torch.randn(B, 3, cfg.image_size, cfg.image_size, device=dev, generator=gen).bfloat16(),
+             torch.randint(0, cfg.num_classes, (B,), device=dev, generator=gen)) for _ in range(2)]
+    for i in range(max(3, args.warmup)):
+        loss = dp.train_step(*pool[i % 2])
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    time.sleep(0.3)
+    bdist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with _native.launch_counter() as lc:
+        s.record()
+        for i in range(args.steps):
+            loss = dp.train_step(*pool[i % 2])
+        e.record()
+    torch.cuda.synchronize()
+    bdist.barrier()
+    clk = clocks.stop() if clocks else None
+    ms = _max_over_ranks(s.elapsed_time(e) / args.steps, dev)
+    # end to end: pinned host images uploaded every step, loss read back
+    host = [(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in pool]
+    xb = torch.empty_like(pool[0][0])
+    yb = torch.empty_like(pool[0][1])
+    bdist.barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for i in range(args.steps):
+        xb.copy_(host[i % 2][0], non_blocking=True)
+        yb.copy_(host[i % 2][1], non_blocking=True)
+        lv = dp.train_step(xb, yb).item()
+    e2.record()
+    torch.cuda.synchronize()
+    ms2 = _max_over_ranks(s2.elapsed_time(e2) / args.steps, dev)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "train images/s ViT-B/16 DDP", "value": B * world / (ms / 1e3), "unit": "images/s",
+            "n_gpus": world, "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (images ~N(0,1), uniform labels, seeded; random-init weights)",
+            "config": {"model": "ViT-B/16", "global_batch": B * world, "image_size": cfg.image_size,
+                       "parallelism": f"dp{world}", "comm": args.comm,
+                       "l2": "no flush: activations of 256 images >> 126 MB L2"},
+            "final_loss": float(loss.item()), "clocks": clk,
+            "e2e": {"value": B * world / (ms2 / 1e3), "unit": "images/s", "ms_per_step": ms2,
+                    "h2d_bytes_per_step": B * 3 * cfg.image_size ** 2 * 2 + B * 8, "d2h_bytes_per_step": 4,
+                    "api": "brain_b200.parallel.DataParallel.train_step", "last_loss": lv},
+            "gpu_launches": lc.count, "impl": "brain"}), flush=True)
+    del dp, model
+    bdist.shutdown()
+    return 0
+
+
+def run_gptlite_cpu(args) -> int:
+    """The GPT-lite data-parallel configuration on CPU ranks (Gloo): 2 decoder layers, d 128, 4 heads,
+    FFN 512 GELU, LayerNorm, learned positions, vocab 1024, seq 64, batch 8 per rank, f32, weights
+    N(0, 0.02) seed 0, tokens uniform seed 1, next-token CE, AdamW lr 3e-4, 20 steps, gradients
+    all-reduced as the mean. Wall-clock timed (CPU), max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from brain_b200.models.config import GptLiteConfig
+    from brain_b200.models.families import GptLite
+    from brain_b200.optim.optimizers import AdamW
+    from brain_b200.parallel import dist as bdist
+
+    ctx = bdist.init(backend="gloo", device="cpu", timeout_s=300)
+    rank, world = ctx.rank, ctx.world_size
+    cfg = GptLiteConfig.baseline_dp()
+    model = GptLite(cfg, device="cpu", dtype=torch.float32, seed=0)
+    opt = AdamW(list(model.parameters()), lr=3e-4)
+    g = torch.Generator().manual_seed(1 + rank)
+    B, S = 8, cfg.max_seq_len
+    steps = 20
+    data = [torch.randint(0, cfg.vocab_size, (B, S + 1), generator=g) for _ in range(steps)]
+
+    def step(t):
+        opt.zero_grad()
+        loss = model.loss(t[:, :-1], t[:, 1:])
+        loss.backward()
+        for p in model.parameters():
+            if p.grad is not None and world > 1:
+                dist.all_reduce(p.grad)
+                p.grad.div_(world)
+        opt.step()
+        return float(loss)
+
+    step(data[0])  # warm-up (first-call allocations)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    losses = [step(t) for t in data]
+    if world > 1:
+        dist.barrier()
+    ms = (time.perf_counter() - t0) * 1e3 / steps
+    t = torch.tensor([ms])
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if rank == 0:
+        print(json.dumps({
+            "metric": "train tok/s GPT-lite DP on CPU (gloo)", "value": B * S * world / (ms / 1e3),
+            "unit": "tokens/s", "n_ranks": world, "steps": steps, "warmup": 1, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "dtype": "f32", "device": "cpu",
+            "data": "synthetic (uniform tokens seed 1; N(0,0.02) weights seed 0)",
+            "config": {"model": "GPT-lite 2x128", "batch_per_rank": B, "seq_len": S, "parallelism": f"dp{world}"},
+            "first_loss": losses[0], "last_loss": losses[-1], "impl": "brain"}), flush=True)
     bdist.shutdown()
     return 0
 

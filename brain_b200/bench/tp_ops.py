@@ -75,6 +75,20 @@ def main(argv=None) -> int:
                M=T * W, N=d, K=attn)
     tp.rs_mode = "pull"
     report("all_gather_rows", timed(lambda: all_gather_rows(tp, x)), (W - 1) * T * d * 2)
+    # block-scaled fp8 row-parallel Linear d x d (K split over ranks), GEMM -> reduce-scatter
+    from ..parallel.tensor_parallel import fp8_gemm_rs
+    from ..quantization.fp8 import quantize_fp8_weight_blocks
+    kr = d // W
+    x8 = torch.randn(T * W, kr, device=dev, generator=g).bfloat16()
+    w8 = (torch.randn(d, kr, device=dev, generator=g) * 0.02).bfloat16()
+    w8q, w8s = quantize_fp8_weight_blocks(w8)
+    flops = 2.0 * T * W * d * kr
+    ms = timed(lambda: fp8_gemm_rs(tp, x8, w8q, w8s, T))
+    report("fp8_linear_gemm_rs", ms, (W - 1) * T * d * 2, M=T * W, N=d, K=kr,
+           tflops_per_rank=round(flops / (ms / 1e3) / 1e12, 1))
+    ms_bf = timed(lambda: gemm_push(tp, x8, w8, 1, T))
+    report("bf16_linear_gemm_rs", ms_bf, (W - 1) * T * d * 2, M=T * W, N=d, K=kr,
+           tflops_per_rank=round(flops / (ms_bf / 1e3) / 1e12, 1))
     tp.comm.check()
     tp.close()
     tp.comm.close()

@@ -140,6 +140,31 @@ def gemm_push(ctx: TPContext, a: torch.Tensor, w: torch.Tensor, mode: int, rows_
     return out
 
 
+def fp8_gemm_rs(ctx: TPContext, x_local: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
+                rows_per_rank: int) -> torch.Tensor:
+    """Row-parallel block-scaled fp8 Linear with reduce-scatter: x_local [M, K/W] (bf16, this rank's
+    input columns) is quantised 1 x 128 on the fly, multiplied by this rank's pre-quantised weight
+    shard wq [N, K/W] (128 x 128 scales ws) on the tcgen05 fp8 kernel straight into symmetric memory,
+    and after a peer barrier each rank pulls and sums its rows [rank * rows_per_rank, ...) from all
+    ranks' products with coalesced NVLink loads. Returns [rows_per_rank, N] bf16."""
+    from ..quantization.fp8 import quantize_fp8_blockwise
+    M = x_local.shape[0]
+    N = wq.shape[0]
+    W = ctx.world
+    same_device(x_local, wq, ws)
+    xq, sx = quantize_fp8_blockwise(x_local)
+    par = ctx.next_parity()
+    full = ctx.symm("rs_full", M * N * 2, par)
+    _native.call("brain_fp8_gemm", xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), sx.data_ptr(),
+                 ws.data_ptr(), full.local, N, None, 0, M, N, xq.shape[1], _stream())
+    ctx.comm.barrier(41)
+    slot = rows_per_rank * N
+    out = torch.empty(rows_per_rank, N, device=x_local.device, dtype=torch.bfloat16)
+    _native.call("brain_comm_reduce_pull", full.peer_array(0), ctx.rank * slot, ctx.rank, W, out.data_ptr(), slot, 1,
+                 1.0, _stream())
+    return out
+
+
 def gemm_allgather_a(ctx: TPContext, a_local: torch.Tensor, w: torch.Tensor, b_mn: int = 0) -> torch.Tensor:
     """C = concat_ranks(a_local) @ w.T (or @ w for b_mn=1), pipelined by row block.
 

@@ -72,3 +72,40 @@ def test_tensor_parallel_fused_linears():
         for k, v in r.items():
             tol = 0.25 if "dw" in k else 0.1
             assert v < tol, (k, v, r)
+
+
+def _fp8_rs_worker(rank, world):
+    from brain_b200.parallel import dist as bdist
+    from brain_b200.parallel.tensor_parallel import TPContext, fp8_gemm_rs
+    from brain_b200.quantization.fp8 import dequantize_fp8_blockwise, quantize_fp8_blockwise, quantize_fp8_weight_blocks
+    bdist.init(timeout_s=60)
+    ctx = TPContext()
+    g = torch.Generator(device="cuda").manual_seed(7)
+    T, K, N = 256, 512, 384  # K split over ranks
+    x_full = torch.randn(T * world, K, device="cuda", generator=g).bfloat16()
+    w_full = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    kr = K // world
+    x_local = x_full[:, rank * kr:(rank + 1) * kr].contiguous()
+    wq, ws = quantize_fp8_weight_blocks(w_full[:, rank * kr:(rank + 1) * kr].contiguous())
+    y = fp8_gemm_rs(ctx, x_local, wq, ws, T)
+    # oracle: sum over ranks of the dequantised products, rows of this rank
+    ref = torch.zeros(T * world, N, device="cuda")
+    for r in range(world):
+        xq, sx = quantize_fp8_blockwise(x_full[:, r * kr:(r + 1) * kr].contiguous())
+        wq_r, ws_r = quantize_fp8_weight_blocks(w_full[:, r * kr:(r + 1) * kr].contiguous())
+        ref += dequantize_fp8_blockwise(xq, sx, 1) @ dequantize_fp8_blockwise(wq_r, ws_r, 128).t()
+    err = float((y.float() - ref[rank * T:(rank + 1) * T]).abs().max())
+    scale = float(ref.abs().max())
+    ctx.comm.check()
+    ctx.close()
+    ctx.comm.close()
+    bdist.shutdown()
+    return err, scale
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_fp8_row_parallel_gemm_reduce_scatter():
+    outs = run_ranks(_fp8_rs_worker, 2, env={"NCCL_NVLS_ENABLE": "0"})
+    for err, scale in outs:
+        assert err < 2e-2 * max(1.0, scale), (err, scale)
