@@ -99,6 +99,12 @@ def main():
     ap.add_argument("--comm", default="nvlink", choices=["nccl", "nvlink"],
                     help="gradient reduction: fused NVLink kernels (default) or NCCL")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="reduce gradients after backward instead of per bucket during backward")
+    ap.add_argument("--overlap", action="store_true",
+                    help="reduce per bucket during backward also below 4 GPUs (where little is exposed)")
+    ap.add_argument("--overlap-mode", default="ce", choices=["ce", "sm"],
+                    help="overlapped reduction: copy engines move the data (ce) or SM kernels do (sm)")
     ap.add_argument("--workload", default="train", choices=["train", "decode", "vit", "gptlite-cpu"],
                     help="train: Llama-3-8B DDP (headline); decode: Llama-3-70B-shape TP=N greedy decode; "
                          "vit: ViT-B/16 DDP images/s; gptlite-cpu: the GPT-lite data-parallel config on CPU ranks")
@@ -152,7 +158,8 @@ def main():
     t0 = time.time()
     model = LlamaLite(cfg, device=dev, dtype=torch.bfloat16, seed=0)
     dp = DataParallel(model, lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, grad_dtype=torch.bfloat16,
-                      comm=args.comm)
+                      comm=args.comm, overlap=(world >= 4 or args.overlap) and not args.no_overlap,
+                      overlap_mode=args.overlap_mode)
     log(f"{bdist.rank_prefix()} model {cfg.num_params() / 1e9:.2f}B params ready in {time.time() - t0:.1f}s; "
         f"mem {torch.cuda.memory_allocated() / 2**30:.1f} GiB")
 
@@ -234,6 +241,8 @@ def main():
                        "params": cfg.num_params(), "global_batch": B * world, "micro_batch_per_gpu": B,
                        "seq_len": S, "parallelism": f"dp{world}", "optimizer": "sharded AdamW (ZeRO-1), fused kernel",
                        "grad_dtype": "bf16", "comm": args.comm,
+                       "grad_reduction": (f"per bucket during backward ({args.overlap_mode})" if dp.overlapped is not None
+                                          else "after backward"),
                        "l2": "no flush: working set (weights+optimizer+activations) >> 126 MB L2"},
             "mfu_model_tflops_per_gpu": flops_tok * tok_s / world / 1e12,
             "final_loss": final_loss,

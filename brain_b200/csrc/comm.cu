@@ -126,7 +126,7 @@ __global__ void gather_pull_kernel(Peers bufs, int rank, int world, int64_t chun
 //   AdamW (decay, moments, bias-corrected update) on the f32 master shard
 //   w16 = bf16(master) written to every rank's parameter buffer at [off + i] (local + P2P push)
 template <typename G>
-__global__ void ddp_step_kernel(Peers grads, Peers params, int rank, int world, int64_t off, int64_t n,
+__global__ void ddp_step_kernel(Peers grads, Peers params, int rank, int world, int pworld, int64_t off, int64_t n,
                                 float* __restrict__ master, float* __restrict__ m, float* __restrict__ v, float lr,
                                 float b1, float b2, float eps, float wd, float inv_bc1, float inv_bc2,
                                 float grad_scale) {
@@ -175,8 +175,8 @@ __global__ void ddp_step_kernel(Peers grads, Peers params, int rank, int world, 
     bf16x8 w;
 #pragma unroll
     for (int k = 0; k < 4; ++k) w.h[k] = __floats2bfloat162_rn(pm[2 * k], pm[2 * k + 1]);
-    for (int jj = 0; jj < world; ++jj) {
-      const int j = (rank + jj) % world;
+    for (int jj = 0; jj < pworld; ++jj) {
+      const int j = (rank + jj) % pworld;
       *reinterpret_cast<bf16x8*>(reinterpret_cast<__nv_bfloat16*>(params.p[j]) + off + e) = w;
     }
   }
@@ -288,19 +288,39 @@ BRAIN_API int brain_comm_copy_async(int64_t src, int64_t dst, int64_t nbytes, cu
 // Fused reduce-scatter + AdamW + bf16 all-gather push for the shard [off, off + n) of this rank.
 // grads/params: int64[world] peer pointers of the flat gradient (bf16 if grad_bf16 else f32) and
 // bf16 parameter buffers. n must be a multiple of 8 and off 8-aligned.
+BRAIN_API int brain_comm_ddp_step_ctas(const int64_t* grads, const int64_t* params, int grad_bf16, int rank,
+                                       int world, int64_t off, int64_t n, float* master, float* m, float* v, float lr,
+                                       float b1, float b2, float eps, float wd, float bc1, float bc2, float grad_scale,
+                                       int max_ctas, int push_world, cudaStream_t st);
+
 BRAIN_API int brain_comm_ddp_step(const int64_t* grads, const int64_t* params, int grad_bf16, int rank, int world,
                                   int64_t off, int64_t n, float* master, float* m, float* v, float lr, float b1,
                                   float b2, float eps, float wd, float bc1, float bc2, float grad_scale,
                                   cudaStream_t st) {
+  return brain_comm_ddp_step_ctas(grads, params, grad_bf16, rank, world, off, n, master, m, v, lr, b1, b2, eps, wd, bc1,
+                                  bc2, grad_scale, 0, world, st);
+}
+
+// Same step with at most max_ctas CTAs (0 = as many as the work needs, up to 4 per SM): a capped grid
+// leaves the SMs to the backward kernels when the step runs on a side stream during backward. The
+// updated bf16 weights go to params[0 .. push_world) (push_world = 1: this rank's buffer only, when
+// the copy engines publish them).
+BRAIN_API int brain_comm_ddp_step_ctas(const int64_t* grads, const int64_t* params, int grad_bf16, int rank,
+                                       int world, int64_t off, int64_t n, float* master, float* m, float* v, float lr,
+                                       float b1, float b2, float eps, float wd, float bc1, float bc2, float grad_scale,
+                                       int max_ctas, int push_world, cudaStream_t st) {
   if (n % 8 || off % 8) return (int)cudaErrorInvalidValue;
   if (n == 0) return 0;
   Peers g = to_peers(grads, world), p = to_peers(params, world);
-  const int grid = grid_for(n / 8);
+  int grid = grid_for(n / 8);
+  if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
+  if (push_world < 1 || push_world > world) return (int)cudaErrorInvalidValue;
   if (grad_bf16)
-    ddp_step_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(g, p, rank, world, off, n, master, m, v, lr, b1, b2, eps, wd,
-                                                        1.f / bc1, 1.f / bc2, grad_scale);
+    ddp_step_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(g, p, rank, world, push_world, off, n, master, m, v, lr, b1,
+                                                        b2, eps, wd, 1.f / bc1, 1.f / bc2, grad_scale);
   else
-    ddp_step_kernel<float><<<grid, 256, 0, st>>>(g, p, rank, world, off, n, master, m, v, lr, b1, b2, eps, wd,
-                                                1.f / bc1, 1.f / bc2, grad_scale);
+    ddp_step_kernel<float><<<grid, 256, 0, st>>>(g, p, rank, world, push_world, off, n, master, m, v, lr, b1, b2,
+                                                eps, wd, 1.f / bc1, 1.f / bc2, grad_scale);
+
   return (int)cudaGetLastError();
 }

@@ -7,7 +7,8 @@ crates/brain-distributed/src/data_parallel.rs:48-63) and shards the AdamW state 
   * the optimizer step is a reduce-scatter of the gradient bucket, the fused AdamW over the local
     shard and an all-gather of the updated bf16 shards (``optim.flat_adamw``);
   * with the NVLink backend (``comm="nvlink"``) the reduce-scatter, un-scaling and AdamW update run
-    as one kernel that pulls peers' gradient shards over NVLink (``parallel.symm``).
+    as one kernel that pulls peers' gradient shards over NVLink (``parallel.symm``); with
+    ``overlap=True`` that kernel runs per bucket of blocks during backward (``parallel.overlap``).
 
 The reference's helpers are kept: ``sync_gradients`` (scale by 1/world after a sum) and
 ``sync_ensemble_gradients`` (average per-parameter gradients of in-process "ranks").
@@ -25,7 +26,7 @@ from .flat import FlatParams
 class DataParallel:
     def __init__(self, model: torch.nn.Module, lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.0, grad_dtype: torch.dtype = torch.float32, comm: str | object = "nccl",
-                 loss_fn=None):
+                 loss_fn=None, overlap: bool = False, bucket_bytes: int = 512 << 20, overlap_mode: str = "ce"):
         ctx = _dist.context()
         self.ctx = ctx
         self.model = model
@@ -43,6 +44,10 @@ class DataParallel:
         self.optimizer = FlatAdamW(self.flat, lr, betas, eps, weight_decay, comm=self.comm)
         self.loss_fn = loss_fn
         self.steps = 0
+        self.overlapped = None
+        if overlap and ctx.world_size > 1 and getattr(self.comm, "name", "") == "nvlink":
+            from .overlap import OverlappedStep
+            self.overlapped = OverlappedStep(self, bucket_bytes=bucket_bytes, mode=overlap_mode)
 
     @property
     def world_size(self) -> int:
@@ -63,9 +68,15 @@ class DataParallel:
         Returns the local loss (device scalar, not synchronised).
         """
         self.optimizer.zero_grad()
+        if self.overlapped is not None:
+            # reduction + AdamW of each bucket start during backward (parallel.overlap)
+            self.overlapped.arm(1.0 / loss_scale / self.world_size)
         loss = self.forward_loss(*batch)
         (loss * loss_scale if loss_scale != 1.0 else loss).backward()
-        self.optimizer.step(grad_scale=1.0 / loss_scale)
+        if self.overlapped is not None:
+            self.overlapped.finish()
+        else:
+            self.optimizer.step(grad_scale=1.0 / loss_scale)
         self.steps += 1
         return loss.detach()
 

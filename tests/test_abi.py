@@ -6,6 +6,7 @@ import brain_b200.ops  # noqa: F401  (registers op signatures)
 import brain_b200.parallel.symm  # noqa: F401
 import brain_b200.parallel.tensor_parallel  # noqa: F401
 import brain_b200.models.llama_tp  # noqa: F401
+import brain_b200.parallel.overlap  # noqa: F401
 import brain_b200.checkpoint  # noqa: F401
 from brain_b200 import _native
 

@@ -166,7 +166,12 @@ def _gpu_ddp(rank, world, comm_kind):
     cfg = LlamaLiteConfig(vocab_size=512, hidden_dim=256, num_layers=2, num_heads=4, num_kv_heads=2, head_dim=64,
                           intermediate_dim=512, max_seq_len=128)
     model = LlamaLite(cfg, device="cuda", dtype=torch.bfloat16, seed=0)
-    dp = DataParallel(model, lr=1e-3, grad_dtype=torch.bfloat16, comm=comm_kind)
+    overlap = comm_kind.startswith("nvlink-overlap")
+    dp = DataParallel(model, lr=1e-3, grad_dtype=torch.bfloat16, comm="nvlink" if overlap else comm_kind,
+                      overlap=overlap, bucket_bytes=64 << 10,  # small buckets: one per block
+                      overlap_mode="sm" if comm_kind.endswith("-sm") else "ce")
+    if overlap:
+        assert dp.overlapped is not None and len(dp.overlapped.buckets) == 3
     g = torch.Generator(device="cuda").manual_seed(7 + rank)
     losses = []
     for _ in range(3):
@@ -176,7 +181,7 @@ def _gpu_ddp(rank, world, comm_kind):
         dp.comm.check()
     w = dp.flat.param_buf.detach().float().cpu().numpy()
     same = True
-    if comm_kind == "nvlink":
+    if comm_kind.startswith("nvlink"):
         dp.comm.close()
     bdist.shutdown()
     return w, losses, same
@@ -191,6 +196,21 @@ def test_fused_ddp_step_matches_nccl_path():
     assert torch.equal(nv[0][0], nv[1][0])  # replicas identical after the fused push
     torch.testing.assert_close(nv[0][0], nc[0][0], rtol=0, atol=2e-2)
     for a, b in zip(nv[0][1], nc[0][1]):
+        assert abs(a - b) < 2e-2
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+@pytest.mark.parametrize("mode", ["ce", "sm"])
+def test_overlapped_ddp_step_matches_fused_step(mode):
+    """Per-bucket reduction + AdamW during backward gives the same training as the step after backward."""
+    env = {"NCCL_NVLS_ENABLE": "0"}
+    kind = "nvlink-overlap" + ("-sm" if mode == "sm" else "")
+    ov = [(torch.from_numpy(w), l) for w, l, _ in run_ranks(_gpu_ddp, 2, kind, env=env)]
+    nv = [(torch.from_numpy(w), l) for w, l, _ in run_ranks(_gpu_ddp, 2, "nvlink", env=env)]
+    assert torch.equal(ov[0][0], ov[1][0])  # replicas identical
+    torch.testing.assert_close(ov[0][0], nv[0][0], rtol=0, atol=2e-2)
+    for a, b in zip(ov[0][1], nv[0][1]):
         assert abs(a - b) < 2e-2
 
 
