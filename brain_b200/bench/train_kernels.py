@@ -1,0 +1,135 @@
+"""Training-kernel microbenchmark on one GPU at Llama-3-8B shapes (micro-batch 2 x seq 4096 = 8192
+tokens): the tcgen05 GEMMs of a layer (forward, data and weight gradients), flash attention forward and
+backward (32 q / 8 kv heads, head_dim 128, causal), RMSNorm, SwiGLU, RoPE, the fused LM-head
+cross-entropy and AdamW. Each is timed with CUDA events over a few calls after warm-up and reported as
+TFLOP/s or GB/s against the measured peaks (``MEASURED_PEAKS.json`` at the repository root).
+
+Run: ``python -m brain_b200.bench.train_kernels [--only name,...] [--iters N]``; one JSON line per case.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+
+def _peaks():
+    here = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    try:
+        with open(os.path.join(here, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["bf16_tflops"]), float(d["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return 1590.0, 6650.0
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="")
+    ap.add_argument("--iters", type=int, default=10)
+    a = ap.parse_args(argv)
+    only = set(x for x in a.only.split(",") if x)
+
+    from .. import ops
+    from ..ops import attention as attn
+    from ..ops.optim_kernels import adamw_
+
+    dev = torch.device("cuda")
+    tflops_peak, hbm_peak = _peaks()
+    g = torch.Generator(device=dev).manual_seed(0)
+    T, d, F, V = 8192, 4096, 14336, 128256
+    B, S, Hq, Hkv, D = 2, 4096, 32, 8, 128
+
+    def rnd(*shape, std=1.0):
+        return (torch.randn(*shape, device=dev, generator=g) * std).bfloat16()
+
+    def timeit(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(a.iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / a.iters
+
+    def report(name, ms, flops=None, nbytes=None, **extra):
+        out = {"kernel": name, "ms": round(ms, 4)}
+        if flops:
+            tf = flops / (ms / 1e3) / 1e12
+            out.update(tflops=round(tf, 1), frac_of_measured_bf16=round(tf / tflops_peak, 3))
+        if nbytes:
+            gbs = nbytes / (ms / 1e3) / 1e9
+            out.update(gbs=round(gbs, 1), frac_of_measured_hbm=round(gbs / hbm_peak, 3))
+        out.update(extra)
+        print(json.dumps(out), flush=True)
+
+    def want(n):
+        return not only or n in only
+
+    # ---- GEMMs of one layer: x W^T forward, dy W (dgrad), dy^T x (wgrad, f32 accumulate)
+    x = rnd(T, d)
+    for name, N, K in (("qkv", (Hq + 2 * Hkv) * D, d), ("o", d, Hq * D), ("gate_up", 2 * F, d), ("down", d, F)):
+        w = rnd(N, K, std=0.02)
+        xi = x if K == d else rnd(T, K)
+        dy = rnd(T, N)
+        fl = 2.0 * T * N * K
+        if want(f"gemm_fwd_{name}"):
+            report(f"gemm_fwd_{name}", timeit(lambda: ops.gemm(xi, w, trans_b=True)), fl, M=T, N=N, K=K)
+        if want(f"gemm_dgrad_{name}"):
+            report(f"gemm_dgrad_{name}", timeit(lambda: ops.gemm(dy, w)), fl, M=T, N=K, K=N)
+        if want(f"gemm_wgrad_{name}"):
+            acc = torch.zeros(N, K, device=dev, dtype=torch.float32)
+            report(f"gemm_wgrad_{name}", timeit(lambda: ops.gemm(dy, xi, trans_a=True, out=acc, beta=1.0)), fl,
+                   M=N, N=K, K=T)
+    # ---- flash attention (causal): forward 2 GEMMs of S x S x D per head over half the square
+    q, k, v = rnd(B, S, Hq, D), rnd(B, S, Hkv, D), rnd(B, S, Hkv, D)
+    fwd_flops = 4.0 * B * Hq * S * S * D / 2
+    if want("attention_fwd"):
+        report("attention_fwd", timeit(lambda: attn._fwd(q, k, v, True, D ** -0.5)), fwd_flops)
+    if want("attention_bwd"):
+        o, lse = attn._fwd(q, k, v, True, D ** -0.5)
+        do = rnd(B, S, Hq, D)
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        report("attention_bwd", timeit(lambda: attn._bwd(q, k, v, o, lse, do, dq, dk, dv, True, D ** -0.5)),
+               2.5 * fwd_flops)
+    # ---- memory-bound ops
+    if want("rms_norm_fwd"):
+        wn = torch.ones(d, device=dev, dtype=torch.bfloat16)
+        report("rms_norm_fwd", timeit(lambda: ops.rms_norm(x, wn)), nbytes=2 * T * d * 2)
+    if want("swiglu_fwd"):
+        gu = rnd(T, 2 * F)
+        report("swiglu_fwd", timeit(lambda: ops.activations.swiglu_fwd_only(gu)), nbytes=T * 3 * F * 2)
+    if want("rope_inplace"):
+        qkv = rnd(B, S, (Hq + 2 * Hkv) * D)
+        table = ops.rope_table(D, S, 500000.0, device=dev)
+        qv = qkv.view(B, S, Hq + 2 * Hkv, D)[:, :, :Hq + Hkv]
+        report("rope_inplace", timeit(lambda: ops.apply_rope_(qv, table)), nbytes=2 * B * S * (Hq + Hkv) * D * 2)
+    if want("lm_head_cross_entropy"):
+        hw = rnd(V, d, std=0.02)
+        labels = torch.randint(0, V, (T,), device=dev, generator=g)
+        h = rnd(T, d).requires_grad_(True)
+
+        def ce():
+            loss = ops.linear_cross_entropy(h, hw, labels)
+            loss.backward()
+        report("lm_head_cross_entropy_fwd_bwd", timeit(ce), 3 * 2.0 * T * V * d)
+    if want("adamw"):
+        n = 1 << 28
+        p = torch.zeros(n, device=dev)
+        m, vv = torch.zeros_like(p), torch.zeros_like(p)
+        gr = torch.zeros(n, device=dev, dtype=torch.bfloat16)
+        p16 = torch.zeros(n, device=dev, dtype=torch.bfloat16)
+        report("adamw_flat", timeit(lambda: adamw_(p, m, vv, gr, lr=1e-3, beta1=0.9, beta2=0.95, eps=1e-8,
+                                                    weight_decay=0.1, step=1, p16=p16)),
+               nbytes=n * (12 + 12 + 2 + 2), elems=n)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
