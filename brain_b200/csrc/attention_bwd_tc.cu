@@ -48,7 +48,8 @@ struct BwdLayout {
   static constexpr int STAGE_BYTES = 2 * B_BYTES;
   static constexpr int NC = MODE == DKDV ? 2 : 1;  // C tiles (P^T, dS^T) or (dS)
   static constexpr int C_OFF = B_OFF + STAGES * STAGE_BYTES;
-  static constexpr int BAR_OFF = C_OFF + NC * SUB128;
+  static constexpr int LD_OFF = C_OFF + NC * SUB128;  // DKDV: per block lse*log2e and delta, 2 buffers
+  static constexpr int BAR_OFF = LD_OFF + 2 * 128 * 4;
   // a_full, b_full[S], b_empty[S], sd_full[2], sd_free[2], c_full, c_free, acc_done, drain
   static constexpr int NBAR = 1 + 2 * STAGES + 4 + 4;
   static constexpr int TOTAL = BAR_OFF + NBAR * 8 + 16 + 1024;
@@ -268,7 +269,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         hcol = hrow;
         col0 = i * 64;
       }
-      if (!mbar_wait(sd_full(i & 1), (i / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag)) {
+      float* sld = reinterpret_cast<float*>(smem + L::LD_OFF) + (i & 1) * 128;
+      if (MODE == DKDV) {
+        // the block's 64 query statistics, loaded once by the 128 elementwise threads (instead of every
+        // thread loading all 64 from global memory) and read back as shared-memory broadcasts. The
+        // barrier also makes the give-up decision uniform: every thread reaches it after bounded waits
+        // and all of them leave the loop together when any wait gave up.
+        const float* lrow = a.lse + ((int64_t)b * a.Hq + hcol) * a.Sq;
+        const float* drow = a.delta + ((int64_t)b * a.Hq + hcol) * a.Sq;
+        const int qi = col0 + (r & 63);
+        const float v = qi < a.Sq ? (r < 64 ? __ldg(lrow + qi) * kLog2e : __ldg(drow + qi)) : 0.f;
+        if (ok) ok = mbar_wait(sd_full(i & 1), (i / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag);
+        sld[r] = v;
+        if (!bar_sync_and(1, 128, ok)) {
+          ok = false;
+          break;
+        }
+      } else if (!mbar_wait(sd_full(i & 1), (i / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag)) {
         ok = false;
         break;
       }
@@ -284,8 +301,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(sd_free(i & 1));
       uint32_t pk[32], dk[32];
       if (MODE == DKDV) {
-        const float* lrow = a.lse + ((int64_t)b * a.Hq + hcol) * a.Sq;
-        const float* drow = a.delta + ((int64_t)b * a.Hq + hcol) * a.Sq;
         const int key = row;
 #pragma unroll
         for (int c = 0; c < 64; c += 2) {
@@ -294,8 +309,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 2; ++e) {
             const int qi = col0 + c + e;
             const bool valid = qi < a.Sq && !(a.causal && key > qi + off);
-            const float l2 = valid ? __ldg(lrow + qi) * kLog2e : 0.f;
-            const float de = valid ? __ldg(drow + qi) : 0.f;
+            const float l2 = valid ? sld[c + e] : 0.f;
+            const float de = valid ? sld[64 + c + e] : 0.f;
             const float p = valid ? ex2_fast(s[c + e] * a.scale_log2 - l2) : 0.f;
             pv[e] = p;
             dv[e] = p * (dp[c + e] - de);
@@ -322,6 +337,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (i > 0 && !mbar_wait(c_free, (i - 1) & 1, BRAIN_ERR_TIMEOUT_ACC, 231, abort_flag)) {
         ok = false;
+        if (MODE == DKDV) continue;  // leaves at the next barrier, together with the other threads
         break;
       }
       tc_fence_after();

@@ -219,35 +219,44 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(s_free(j & 1));
       const int n0 = j * 128;
       const bool need_mask = (n0 + 127 > a.Sk - 1) || (a.causal && n0 + 127 > m0 + off);
-      float mx = -INFINITY;
+      // Row max and row sum use 8 independent partial accumulators: one warp per SMSP runs this loop,
+      // so a single dependency chain of 128 max / add operations would be pure latency.
+      float mxp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
       if (need_mask) {
 #pragma unroll
         for (int k = 0; k < 128; ++k) {
           s[k] = (n0 + k > limit) ? -INFINITY : s[k] * a.scale_log2;
-          mx = fmaxf(mx, s[k]);
+          mxp[k & 7] = fmaxf(mxp[k & 7], s[k]);
         }
       } else {
 #pragma unroll
         for (int k = 0; k < 128; ++k) {
           s[k] *= a.scale_log2;
-          mx = fmaxf(mx, s[k]);
+          mxp[k & 7] = fmaxf(mxp[k & 7], s[k]);
         }
       }
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       float alpha = 1.f;
       if (mx > m_used + kRescaleThreshold || (m_used == -INFINITY && mx > -INFINITY)) {
         alpha = exp2f(m_used - mx);  // 0 when m_used == -inf
         m_used = mx;
       }
       const float mu = m_used == -INFINITY ? 0.f : m_used;
-      float sum = 0.f;
+      float sp[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) sp[u] = 0.f;
       uint32_t pk[64];
 #pragma unroll
       for (int k = 0; k < 128; k += 2) {
         const float p0 = ex2_fast(s[k] - mu), p1 = ex2_fast(s[k + 1] - mu);
-        sum += p0 + p1;
+        sp[(k >> 1) & 7] += p0 + p1;
         __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
         pk[k / 2] = *reinterpret_cast<uint32_t*>(&hv);
       }
+      const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       l = l * alpha + sum;
       // P buffer and O are free once PV_{j-1} has completed
       if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, BRAIN_ERR_TIMEOUT_ACC, 131, abort_flag)) {

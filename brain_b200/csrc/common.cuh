@@ -135,6 +135,17 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int cod
   }
 }
 
+// Named barrier `id` over `nthreads` threads (a multiple of 32) that also returns the AND of `v` over them.
+__device__ __forceinline__ bool bar_sync_and(int id, int nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.and.pred q, %2, %3, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // 2-D tiled TMA load into this CTA's shared memory, completing on `bar` (complete_tx::bytes).
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint32_t dst, uint32_t bar, int x,
                                             int y) {
