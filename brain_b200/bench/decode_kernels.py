@@ -33,6 +33,8 @@ def main(argv=None) -> int:
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--splits", type=int, default=0, help="force a split-K count (0 = automatic)")
     ap.add_argument("--only", default="", help="comma-separated kernel names to run (default: all)")
+    ap.add_argument("--attn-splits", default="", help="comma-separated decode-attention split counts to add")
+    ap.add_argument("--pdl", type=int, default=2, help="programmatic dependent launch mode (see set_pdl)")
     ap.add_argument("--no-pdl", action="store_true", help="launch without programmatic dependent launch")
     ap.add_argument("--trace", action="store_true",
                     help="also run each GEMM once with per-CTA phase timestamps and print their spread")
@@ -42,7 +44,8 @@ def main(argv=None) -> int:
     from ..models import LlamaLiteConfig
     from ..ops import check_status
     from ..ops.decode import (EPI_ARGMAX, EPI_PUSH, EPI_QKV, EPI_STORE, EPI_SWIGLU, ar_norm, decode_ext,
-                              init_ar_slots, paged_decode_attention, set_pdl, skinny_gemm, skinny_splits)
+                              decode_splits, init_ar_slots, paged_decode_attention, set_pdl, skinny_gemm,
+                              skinny_splits)
     from ..ops.rope import rope_table
 
     cfg = LlamaLiteConfig.llama3_70b()
@@ -51,7 +54,7 @@ def main(argv=None) -> int:
     hq, hkv, F = cfg.num_heads // W, cfg.num_kv_heads // W, cfg.intermediate_dim // W
     Vs = -(-cfg.vocab_size // W)
     peak = _peak_hbm()
-    set_pdl(not a.no_pdl)
+    set_pdl(0 if a.no_pdl else a.pdl)
     g = torch.Generator(device=dev).manual_seed(0)
 
     def rnd(*shape, std=0.02):
@@ -109,10 +112,15 @@ def main(argv=None) -> int:
         if a.trace:
             ctas = sp * -(-N // 128)
             tr = torch.zeros(ctas * 16, device=dev, dtype=torch.int64)
-            fn(0)
+            tr_prev = torch.zeros_like(tr)
+            torch.cuda.synchronize()
+            fn(0, ext=ext_fn(tr_prev))
             fn(1, ext=ext_fn(tr))
             torch.cuda.synchronize()
             t = tr.view(ctas, 16).cpu().double()
+            tp = tr_prev.view(ctas, 16).cpu().double()
+            gap = {"prev_last_end_to_first_start_us": round(float(t[:, 0].min() - tp[:, 6].max()) / 1e3, 2),
+                   "prev_span_us": round(float(tp[:, 6].max() - tp[:, 0].min()) / 1e3, 2)}
             base = t[:, 0].min()
             phases = {}
             for k, nm in enumerate(["start", "setup", "pdl_wait", "mma_done", "cluster_sync1", "cluster_sync2",
@@ -128,7 +136,7 @@ def main(argv=None) -> int:
                 steps += [("push_stores", 11, 12), ("push_syncthreads", 12, 13), ("push_release_arrive", 13, 14)]
             cyc = {nm: round(float((t[:, b] - t[:, a_]).median()), 0) for nm, a_, b in steps}
             print(json.dumps({"trace": name, "us_median_max_since_first_start": phases,
-                              "sm_cycles_median_per_step": cyc}), flush=True)
+                              "sm_cycles_median_per_step": cyc, "launch_gap": gap}), flush=True)
 
     # ---- QKV + RoPE + paged KV append
     bs = 64
@@ -145,10 +153,46 @@ def main(argv=None) -> int:
     kv.normal_()
     q = rnd(B, hq, D, std=1.0)
     ao = torch.empty(B, hq, D, device=dev, dtype=torch.bfloat16)
-    aws = torch.zeros(1 << 22, device=dev, dtype=torch.float32)
     if want("paged_decode_attention"):
-        us = timeit(lambda i: paged_decode_attention(q, kv[0], kv[1], table, lens, out=ao, workspace=aws), a.iters)
-        report("paged_decode_attention", us, B * a.kv_len * hkv * D * 2 * 2, kv_len=a.kv_len)
+        # one layer's cache per call, rotating over caches larger than L2 together (as the 80 layers of a
+        # decode step are): the K/V come from HBM
+        ncache = max(2, math.ceil(512e6 / kv.numel() / 2))
+        caches = [kv] + [torch.randn_like(kv) for _ in range(ncache - 1)]
+        nbytes = B * a.kv_len * hkv * D * 2 * 2
+        for sp in [None] + [int(x) for x in a.attn_splits.split(",") if x]:
+            us = timeit(lambda i, sp=sp: paged_decode_attention(q, caches[i % ncache][0], caches[i % ncache][1], table,
+                                                                lens, out=ao, splits=sp), a.iters)
+            spn = sp or decode_splits(B, hkv, D, max_blocks * bs)
+            report("paged_decode_attention", us, nbytes, kv_len=a.kv_len, splits=spn)
+            if a.trace:
+                tr = torch.zeros(B * hkv * spn * 8, device=dev, dtype=torch.int64)
+                names = ["start", "len_read", "pdl_wait", "q_loaded", "first_chunk", "loop_end", "cluster_sync",
+                         "end"]
+                tr_prev = torch.zeros_like(tr)
+                for mode in ("isolated", "after_previous"):
+                    torch.cuda.synchronize()
+                    if mode == "after_previous":
+                        paged_decode_attention(q, caches[1][0], caches[1][1], table, lens, out=ao, splits=spn,
+                                               trace=tr_prev)
+                    paged_decode_attention(q, caches[2][0], caches[2][1], table, lens, out=ao, splits=spn, trace=tr)
+                    torch.cuda.synchronize()
+                    t = tr.view(-1, 8).cpu().double()
+                    gap = None
+                    if mode == "after_previous":
+                        tp = tr_prev.view(-1, 8).cpu().double()
+                        gap = {"prev_last_end_to_first_start_us": round(float(t[:, 0].min() - tp[:, 7].max()) / 1e3, 2),
+                               "prev_first_end_to_first_start_us": round(float(t[:, 0].min() - tp[:, 7].min()) / 1e3, 2),
+                               "prev_span_us": round(float(tp[:, 7].max() - tp[:, 0].min()) / 1e3, 2)}
+                    base = t[:, 0].min()
+                    rel = (t - base) / 1e3
+                    phases = {nm: [round(float(rel[:, k].median()), 2), round(float(rel[:, k].max()), 2)]
+                              for k, nm in enumerate(names)}
+                    steps = {f"{names[k]}->{names[k + 1]}": round(float((t[:, k + 1] - t[:, k]).median()) / 1e3, 2)
+                             for k in range(7)}
+                    print(json.dumps({"trace": "paged_decode_attention", "splits": spn, "mode": mode,
+                                      "us_median_max_since_first_start": phases, "us_median_per_step": steps,
+                                      "launch_gap": gap}), flush=True)
+        del caches
     # ---- out projection with all-reduce push (single rank: pushes to itself)
     slot = B * d
     slots = init_ar_slots(torch.empty(2 * slot, device=dev, dtype=torch.bfloat16))

@@ -4,14 +4,19 @@
 // a sequence's logical block to a pool block; seq_lens [B] int32 counts the cached tokens (the new
 // token included). q [B, Hq, D] (row stride qs elements), out [B, Hq, D].
 //
-// Split-K flash decoding, GQA-packed: a CTA owns one (sequence, kv head) and a contiguous slice of
-// the sequence's KV blocks; the G = Hq / Hkv query heads of the group form the M = 16 side of
-// mma.sync tiles, so every K/V block is read from HBM once (decode is bound by reading the cache and
-// the weights) and S = Q K^T and O += P V run on tensor cores. K/V chunks of 64 keys stream through
-// a 3-stage cp.async ring gathered through the block table into XOR-swizzled shared memory. Each split
-// writes its running (max, sum, unnormalised output); the last split CTA of a (sequence, kv head)
-// (atomic ticket) merges the splits with the log-sum-exp rule. The KV append kernel applies RoPE
-// (NeoX half split) to the new token's q and k and writes k / v into their paged slots.
+// Split-K flash decoding, GQA-packed: a CTA owns one (sequence, kv head) and a contiguous range of
+// the sequence's tokens (16-token granules, so the splits are balanced); the G = Hq / Hkv query heads
+// of the group form the M = 16 side of mma.sync tiles, so every K/V row is read from HBM once (decode
+// is bound by reading the cache and the weights) and S = Q K^T and O += P V run on tensor cores.
+// K/V chunks of 64 keys stream through a 3-stage ring of TMA loads (one 16-key x 64-column box per
+// block-table lookup, 128-byte swizzle) completing on mbarriers. The splits of one (sequence, kv
+// head) are one thread-block cluster: after the main loop every CTA pushes its running (max, sum,
+// unnormalised output) into the shared memory of the CTA that owns each output slice, and after one
+// cluster barrier each CTA merges its slice with the log-sum-exp rule (no global workspace, no
+// atomics, no second launch). Under programmatic dependent launch the chunks that hold only tokens
+// older than the newest one are requested before the kernel waits on its predecessor. The KV append
+// kernel applies RoPE (NeoX half split) to the new token's q and k and writes k / v into their paged
+// slots.
 // Reference: the contiguous, realloc-per-append KvCache::update (crates/brain-transformer/src/kv_cache.rs:83-158)
 // and SDPA (attention/scaled.rs:41-139); LlamaLite::generate recomputes everything instead.
 #include "common.cuh"
@@ -20,40 +25,29 @@ using namespace brain;
 
 namespace {
 
-constexpr int kBlock = 64;    // tokens per KV block handled per step (pool block_size must divide by it or equal it)
+constexpr int kBlock = 64;    // keys per chunk
+constexpr int kRowsBox = 16;  // keys per TMA box and granule of the split ranges (block_size must be a multiple)
 constexpr int kThreads = 128;
 constexpr int kWarpsDec = kThreads / 32;
 constexpr int kMaxG = 16;     // query heads per kv head supported (the M = 16 side of the MMA tiles)
 
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  const int n = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
 struct DecodeArgs {
   const __nv_bfloat16* q;
   int64_t qb, qh;  // strides of q [B, Hq, D]
-  const __nv_bfloat16 *kp, *vp;
   const int* table;
   int max_blocks;
   const int* seq_lens;
   int block_size;
   int B, Hq, Hkv, D;
   float scale_log2;
-  int splits;
-  float* part_o;   // [B, Hkv, splits, G, D]
-  float* part_ml;  // [B, Hkv, splits, G, 2]
-  int* tickets;    // [B, Hkv] split arrivals, zero between launches
+  int splits;      // CTAs per cluster, one cluster per (sequence, kv head)
   __nv_bfloat16* out;
   int64_t ob, oh;  // strides of out [B, Hq, D]
+  unsigned long long* trace;  // optional [grid][8] per-CTA phase timestamps (globaltimer ns), else null
+  int pdl_late;               // let dependents launch after the main loop instead of at the start
 };
 
-constexpr int kMaxSplitsDec = 64;
+constexpr int kMaxSplitsDec = 16;  // cluster size limit (non-portable above 8)
 
 // ---- warp-level tensor-core helpers (mma.sync m16n8k16 bf16 -> f32, ldmatrix from swizzled rows)
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -90,34 +84,144 @@ constexpr int kStages = 3;  // K/V chunks in flight per CTA
 
 template <int D>
 struct DecSmem {
-  static constexpr int CHUNK = kBlock * D * 2;         // one K or V chunk
+  static constexpr int HALF = kBlock * 128;            // 64 keys x 64 columns, rows of 128 B
+  static constexpr int CHUNK = (D / 64) * HALF;        // one K or V chunk
   static constexpr int STAGE = 2 * CHUNK;              // K + V
   static constexpr int Q_OFF = kStages * STAGE;        // Q tile [16][D] bf16, swizzled
-  static constexpr int TOTAL = Q_OFF + kMaxG * D * 2;  // merge scratch reuses the stages
+  static constexpr int BAR_OFF = Q_OFF + kMaxG * D * 2;
+  static constexpr int TOTAL = BAR_OFF + kStages * 8 + 1024;  // + slack to align the base to 1 KB
+  // after the main loop the stages hold the merge data
+  static constexpr int WM_OFF = 0;                                    // [4 warps][16] row max
+  static constexpr int WL_OFF = WM_OFF + kWarpsDec * kMaxG * 4;       // [4 warps][16] row sum
+  static constexpr int WO_LD = D + 8;                                 // row stride: 8 rows of a warp's store hit 2 wavefronts
+  static constexpr int WO_OFF = WL_OFF + kWarpsDec * kMaxG * 4;       // [4 warps][16][WO_LD] output
+  static constexpr int RML_OFF = WO_OFF + kWarpsDec * kMaxG * WO_LD * 4;  // [split][16] (max, sum) received
+  static constexpr int RO_OFF = RML_OFF + kMaxSplitsDec * kMaxG * 8;  // [split][slot][128] outputs received
+  static constexpr int RO_FLOATS = kMaxG * D + kMaxSplitsDec * kThreads;
+  static_assert(RO_OFF + RO_FLOATS * 4 <= Q_OFF, "merge data must fit in the stages");
 };
 
-// One CTA = (sequence b, kv head hk, split): the GQA group's G <= 16 query heads form the M = 16 side
-// of mma.sync tiles, so the 4 warps compute S = Q K^T and O += P V on tensor cores; warp w owns keys
-// [16 w, 16 w + 16) of every 64-key chunk with its own online-softmax state, and the warps merge
-// at the end. K/V chunks stream through a 3-stage cp.async ring gathered through the block table.
+// Byte offset of 16-byte unit `c` of key row `r` in a K/V chunk: column halves of 64 (128 B rows),
+// unit index XOR (r & 7) inside each half, i.e. the TMA 128-byte swizzle of a 1 KB-aligned tile.
+__device__ __forceinline__ uint32_t kv_off(int r, int c) {
+  return (uint32_t)((c >> 3) * (kBlock * 128) + r * 128 + (((c & 7) ^ (r & 7)) << 4));
+}
+
+__device__ __forceinline__ void dec_trace(const DecodeArgs& a, int slot) {
+  if (a.trace != nullptr && threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    a.trace[((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 + slot] = t;
+  }
+}
+
+__device__ __forceinline__ int ld_relaxed_gpu(const int* p) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_dsmem_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_dsmem_f2(uint32_t addr, float x, float y) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(x), "f"(y) : "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// One CTA = (sequence b, kv head hk, split); the splits of (b, hk) are one cluster (cluster rank =
+// split). The GQA group's G <= 16 query heads form the M = 16 side of mma.sync tiles, so the 4 warps
+// compute S = Q K^T and O += P V on tensor cores; warp w owns keys [16 w, 16 w + 16) of every 64-key
+// chunk with its own online-softmax state, and the warps merge at the end.
 template <int D>
-__global__ void __launch_bounds__(kThreads) decode_split_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_constant__ CUtensorMap tk,
+                                                                const __grid_constant__ CUtensorMap tv,
+                                                                DecodeArgs a) {
   using S = DecSmem<D>;
   constexpr int DU = D / 8;  // 16-byte units per row
-  pdl_trigger();
-  pdl_wait();
+  constexpr int NH = D / 64;  // 64-column halves
+  if (!a.pdl_late) pdl_trigger();
+  dec_trace(a, 0);
   const int split = blockIdx.x;
   const int bh = blockIdx.y;
   const int b = bh / a.Hkv, hk = bh % a.Hkv;
   const int G = a.Hq / a.Hkv;
-  const int len = a.seq_lens[b];
-  const int nchunks = (len + kBlock - 1) / kBlock;
-  const int per = (nchunks + a.splits - 1) / a.splits;
-  const int c0 = split * per, c1 = min(nchunks, c0 + per);
 
-  extern __shared__ __align__(128) uint8_t dsmem[];
-  const uint32_t sbase = smem_u32(dsmem);
+  extern __shared__ uint8_t dsmem_raw[];
+  __shared__ int s_len;
+  const uint32_t raw = smem_u32(dsmem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;  // the 128-byte swizzle repeats every 1 KB
+  uint8_t* dsmem = dsmem_raw + (sbase - raw);
+  const uint32_t bars = sbase + S::BAR_OFF;
   const int tid = threadIdx.x, warp = tid / 32, lane = tid % 32;
+
+  // this split's tokens [t0, t1) of a sequence of `len` tokens, in 16-token granules
+  auto range = [&](int len, int& t0, int& t1) {
+    const int units = (len + kRowsBox - 1) / kRowsBox;
+    t0 = min(len, (int)((int64_t)split * units / a.splits) * kRowsBox);
+    t1 = min(len, (int)((int64_t)(split + 1) * units / a.splits) * kRowsBox);
+  };
+  // (warp 0) chunk c of the range into stage st: lane i < 4 loads key group i (16 keys, one block-table
+  // lookup) of K and V, one box per 64-column half; groups past t1 are not loaded
+  auto issue = [&](int t0, int t1, int c, int st) {
+    const int c_start = t0 + c * kBlock;
+    const int groups = min(kBlock / kRowsBox, (t1 - c_start + kRowsBox - 1) / kRowsBox);
+    const uint32_t bar = bars + st * 8;
+    if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(groups * 2 * NH * kRowsBox * 128));
+    __syncwarp();
+    if (lane < groups) {
+      const int tok = c_start + lane * kRowsBox;
+      const int blk = a.table[(int64_t)b * a.max_blocks + tok / a.block_size];
+      const int y = blk * a.block_size + tok % a.block_size;
+      const uint32_t ks = sbase + st * S::STAGE, vs = ks + S::CHUNK;
+#pragma unroll
+      for (int h = 0; h < NH; ++h) {
+        const int x = hk * D + h * 64;
+        tma_load_2d(&tk, ks + h * S::HALF + lane * kRowsBox * 128, bar, x, y);
+        tma_load_2d(&tv, vs + h * S::HALF + lane * kRowsBox * 128, bar, x, y);
+      }
+    }
+  };
+
+  if (tid == 0) {
+    for (int st = 0; st < kStages; ++st) mbar_init(bars + st * 8, 1);
+    fence_barrier_init();
+    s_len = ld_relaxed_gpu(a.seq_lens + b);
+  }
+  __syncthreads();
+  // Tokens older than the newest one are final while the predecessor may still run (it writes at most
+  // the newest token's K/V and the lengths), so the first full chunks of the range are requested before
+  // the wait, sized from a length read that may be one step stale: only chunks that end at or below
+  // guess - 1 are taken, and the choice is checked against the real length after the wait.
+  const int len_guess = s_len;
+  int g0, g1;
+  range(len_guess, g0, g1);
+  int pre = 0;
+  for (; pre < kStages - 1; ++pre) {
+    const int end = g0 + (pre + 1) * kBlock;
+    if (end > g1 || end > len_guess - 1) break;
+    if (warp == 0) issue(g0, g1, pre, pre);
+  }
+  dec_trace(a, 1);
+  pdl_wait();
+  dec_trace(a, 2);
+  const int len = a.seq_lens[b];
+  int t0, t1;
+  range(len, t0, t1);
+  const int nch = (t1 - t0 + kBlock - 1) / kBlock;
+  uint32_t par = 0;  // bit st: parity of the next phase of stage st's barrier
+  if (pre > 0 && !(g0 == t0 && t0 + pre * kBlock <= t1 && t0 + pre * kBlock <= len - 1)) {
+    // the guess was wrong: let what it fetched land, then load the range from its start
+    for (int st = 0; st < pre; ++st) mbar_wait(bars + st * 8, 0, BRAIN_ERR_TIMEOUT_FULL, 241, nullptr);
+    par = (1u << pre) - 1u;
+    pre = 0;
+  }
+  for (int j = pre; j < kStages - 1 && j < nch; ++j)
+    if (warp == 0) issue(t0, t1, j, j);
 
   // Q (rows >= G zero) -> swizzled smem -> A fragments held for the whole kernel
   for (int i = tid; i < kMaxG * DU; i += kThreads) {
@@ -126,28 +230,6 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(DecodeArgs a) {
     if (g < G) v = *reinterpret_cast<const uint4*>(a.q + (int64_t)b * a.qb + (int64_t)(hk * G + g) * a.qh + c * 8);
     *reinterpret_cast<uint4*>(dsmem + S::Q_OFF + swz<D>(g, c)) = v;
   }
-
-  auto load_chunk = [&](int c, int stage) {
-    const int tok0 = c * kBlock;
-    const uint32_t ks = sbase + stage * S::STAGE, vs = ks + S::CHUNK;
-    for (int i = tid; i < kBlock * DU; i += kThreads) {
-      const int t = i / DU, u = i % DU;
-      const int tok = tok0 + t;
-      const bool ok = tok < len;
-      int64_t off = 0;
-      if (ok) {
-        const int blk = a.table[(int64_t)b * a.max_blocks + tok / a.block_size];
-        off = ((int64_t)blk * a.block_size + tok % a.block_size) * a.Hkv * D + (int64_t)hk * D + u * 8;
-      }
-      cp_async16(ks + swz<D>(t, u), a.kp + off, ok);
-      cp_async16(vs + swz<D>(t, u), a.vp + off, ok);
-    }
-  };
-#pragma unroll
-  for (int j = 0; j < kStages - 1; ++j) {
-    if (c0 + j < c1) load_chunk(c0 + j, j);
-    cp_commit();
-  }
   __syncthreads();
   uint32_t qa[D / 16][4];
 #pragma unroll
@@ -155,6 +237,7 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(DecodeArgs a) {
     const int row = (lane & 7) + ((lane >> 3) & 1) * 8, unit = kk * 2 + (lane >> 4);
     ldsm_x4(sbase + S::Q_OFF + swz<D>(row, unit), qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3]);
   }
+  dec_trace(a, 3);
 
   float o[D / 8][4];
 #pragma unroll
@@ -162,30 +245,41 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(DecodeArgs a) {
   float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};  // rows lane/4 and lane/4 + 8
   const int kw = warp * 16;                                     // this warp's keys inside a chunk
 
-  for (int c = c0; c < c1; ++c) {
-    cp_wait<kStages - 2>();
-    __syncthreads();  // chunk c landed; every warp is done with chunk c - 1's stage
-    if (c + kStages - 1 < c1) load_chunk(c + kStages - 1, (c - c0 + kStages - 1) % kStages);
-    cp_commit();
-    const uint32_t ks = sbase + ((c - c0) % kStages) * S::STAGE, vs = ks + S::CHUNK;
+  for (int c = 0; c < nch; ++c) {
+    const int st = c % kStages;
+    mbar_wait(bars + st * 8, (par >> st) & 1u, BRAIN_ERR_TIMEOUT_FULL, 240, nullptr);
+    par ^= 1u << st;
+    const uint32_t ks = sbase + st * S::STAGE, vs = ks + S::CHUNK;
+    const int c_start = t0 + c * kBlock;
+    if (c_start + kBlock > t1) {
+      // V rows past the range may be unloaded or hold anything (0 * NaN would poison O): zero them
+      const int r0v = t1 - c_start;
+      for (int i = tid; i < (kBlock - r0v) * DU; i += kThreads) {
+        const int r = r0v + i / DU, u = i % DU;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %1, %1, %1};" ::"r"(vs + kv_off(r, u)), "r"(0) : "memory");
+      }
+    }
+    __syncthreads();  // chunk c visible to every warp; every warp is done with chunk c - 1's stage
+    if (c == 0) dec_trace(a, 4);
+    if (warp == 0 && c + kStages - 1 < nch) issue(t0, t1, c + kStages - 1, (c + kStages - 1) % kStages);
     // S[16 x 16] = Q K^T over this warp's 16 keys (two n8 tiles)
     float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       uint32_t b0, b1, b2, b3;
       const int key = kw + (lane & 7) + (lane >> 4) * 8, unit = kk * 2 + ((lane >> 3) & 1);
-      ldsm_x4(ks + swz<D>(key, unit), b0, b1, b2, b3);
+      ldsm_x4(ks + kv_off(key, unit), b0, b1, b2, b3);
       mma_bf16(sc[0], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b0, b1);
       mma_bf16(sc[1], qa[kk][0], qa[kk][1], qa[kk][2], qa[kk][3], b2, b3);
     }
     // online softmax (base 2) for rows r0 = lane/4 and r1 = r0 + 8
-    const int kbase = c * kBlock + kw + (lane & 3) * 2;
+    const int kbase = c_start + kw + (lane & 3) * 2;
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int n = 0; n < 2; ++n)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const bool valid = kbase + n * 8 + (j & 1) < len;
+        const bool valid = kbase + n * 8 + (j & 1) < t1;
         sc[n][j] = valid ? sc[n][j] * a.scale_log2 : -INFINITY;
         mx[j >> 1] = fmaxf(mx[j >> 1], sc[n][j]);
       }
@@ -224,23 +318,26 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(DecodeArgs a) {
     for (int n2 = 0; n2 < D / 16; ++n2) {
       uint32_t b0, b1, b2, b3;
       const int key = kw + (lane & 7) + ((lane >> 3) & 1) * 8, unit = n2 * 2 + (lane >> 4);
-      ldsm_x4_t(vs + swz<D>(key, unit), b0, b1, b2, b3);
+      ldsm_x4_t(vs + kv_off(key, unit), b0, b1, b2, b3);
       mma_bf16(o[2 * n2], pa0, pa1, pa2, pa3, b0, b1);
       mma_bf16(o[2 * n2 + 1], pa0, pa1, pa2, pa3, b2, b3);
     }
   }
-  cp_wait<0>();
-  __syncthreads();  // stages free: reuse them as merge scratch
+  __syncthreads();  // every warp is done with the stages
+  if (a.pdl_late) pdl_trigger();
+  // peers may push into this CTA's stages once every CTA of the cluster has passed this point
+  if (a.splits > 1) cluster_arrive_release();
+  dec_trace(a, 5);
 
-  // ---- merge the 4 warps: row max over warps, rescale, sum O and l
+  // ---- merge the 4 warps into this split's (max, sum, output): row max over warps, rescale, sum
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     l_r[r] += __shfl_xor_sync(0xffffffffu, l_r[r], 1);
     l_r[r] += __shfl_xor_sync(0xffffffffu, l_r[r], 2);
   }
-  float* sm = reinterpret_cast<float*>(dsmem);                 // [4 warps][16 rows] max
-  float* sl = sm + kWarpsDec * kMaxG;                          // [4 warps][16 rows] sum
-  float* so = sl + kWarpsDec * kMaxG;                          // [4 warps][16][D] output
+  float* sm = reinterpret_cast<float*>(dsmem + S::WM_OFF);
+  float* sl = reinterpret_cast<float*>(dsmem + S::WL_OFF);
+  float* so = reinterpret_cast<float*>(dsmem + S::WO_OFF);
   const int r0 = lane >> 2;
   if ((lane & 3) == 0) {
     sm[warp * kMaxG + r0] = m_r[0];
@@ -265,106 +362,86 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(DecodeArgs a) {
     sl[warp * kMaxG + r0] = l_r[0];
     sl[warp * kMaxG + r0 + 8] = l_r[1];
   }
+  constexpr int LD = S::WO_LD;
 #pragma unroll
   for (int n = 0; n < D / 8; ++n) {
     const int col = n * 8 + (lane & 3) * 2;
-    *reinterpret_cast<float2*>(so + (warp * kMaxG + r0) * D + col) = make_float2(o[n][0], o[n][1]);
-    *reinterpret_cast<float2*>(so + (warp * kMaxG + r0 + 8) * D + col) = make_float2(o[n][2], o[n][3]);
+    *reinterpret_cast<float2*>(so + (warp * kMaxG + r0) * LD + col) = make_float2(o[n][0], o[n][1]);
+  }
+  if (G > 8) {  // rows 8..15 are padding for groups of up to 8 heads
+#pragma unroll
+    for (int n = 0; n < D / 8; ++n) {
+      const int col = n * 8 + (lane & 3) * 2;
+      *reinterpret_cast<float2*>(so + (warp * kMaxG + r0 + 8) * LD + col) = make_float2(o[n][2], o[n][3]);
+    }
   }
   __syncthreads();
-  const int64_t base = (((int64_t)b * a.Hkv + hk) * a.splits + split) * G;
-  for (int i = tid; i < G * D; i += kThreads) {
-    const int g = i / D, d = i % D;
-    float v = 0.f;
+  // this split's output elements i = tid + 128 j (j < G*D/128), and the (max, sum) of head tid < G
+  constexpr int kMaxPer = kMaxG * D / kThreads;
+  const int per = (G * D + kThreads - 1) / kThreads;
+  float v[kMaxPer];
 #pragma unroll
-    for (int w = 0; w < kWarpsDec; ++w) v += so[(w * kMaxG + g) * D + d];
-    a.part_o[(base + g) * D + d] = v;
+  for (int j = 0; j < kMaxPer; ++j) {
+    v[j] = 0.f;
+    const int i = tid + j * kThreads;
+    if (j < per && i < G * D) {
+      const int g = i / D, d = i % D;
+#pragma unroll
+      for (int w = 0; w < kWarpsDec; ++w) v[j] += so[(w * kMaxG + g) * LD + d];
+    }
   }
+  float Mh = -INFINITY, Lh = 0.f;
   if (tid < G) {
-    float M = -INFINITY, L = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarpsDec; ++w) M = fmaxf(M, sm[w * kMaxG + tid]);
+    for (int w = 0; w < kWarpsDec; ++w) Mh = fmaxf(Mh, sm[w * kMaxG + tid]);
 #pragma unroll
-    for (int w = 0; w < kWarpsDec; ++w) L += sl[w * kMaxG + tid];
-    a.part_ml[(base + tid) * 2] = M;
-    a.part_ml[(base + tid) * 2 + 1] = L;
+    for (int w = 0; w < kWarpsDec; ++w) Lh += sl[w * kMaxG + tid];
   }
 
-  // ---- the last split CTA of (b, hk) merges all splits: out = sum_s w_s o_s / sum_s w_s l_s with
-  // w_s = exp2(m_s - max_s m_s) (atomic ticket; no separate combine launch)
-  __shared__ int s_last;
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) {
-    const int old = atomicAdd(a.tickets + bh, 1);
-    s_last = old == a.splits - 1;
-    if (s_last) a.tickets[bh] = 0;  // ready for the next launch
+  // ---- push to the owners: element i belongs to CTA (i / 128) % splits, slot (i / 128) / splits
+  const int E = (per + a.splits - 1) / a.splits;  // slots per CTA
+  if (a.splits > 1) cluster_wait_acquire();       // every CTA's stages are free
+  else __syncthreads();
+  const uint32_t rml = sbase + S::RML_OFF, ro = sbase + S::RO_OFF;
+#pragma unroll
+  for (int j = 0; j < kMaxPer; ++j) {
+    if (j < per) {
+      const int owner = j % a.splits, slot = j / a.splits;
+      st_dsmem_f32(mapa_shared(ro + (uint32_t)(((split * E + slot) * kThreads + tid) * 4), (uint32_t)owner), v[j]);
+    }
   }
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
-  float* sw = so;                             // [G][kMaxSplitsDec] split weights (merge scratch is free)
-  float* sm2 = sw + kMaxG * kMaxSplitsDec;    // [G][kMaxSplitsDec] split maxima, then sums
-  float* sl2 = sm2 + kMaxG * kMaxSplitsDec;
-  float* sinv = sl2 + kMaxG * kMaxSplitsDec;  // [G] 1 / denominator
-  const int64_t base0 = ((int64_t)b * a.Hkv + hk) * a.splits * G;
-  // every (head, split) statistic is loaded at once (one L2 round trip), then reduced from smem
-  for (int idx = tid; idx < G * a.splits; idx += kThreads) {
-    const int sp = idx / G, g = idx % G;
-    const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.part_ml) + base0 + idx);
-    sm2[g * kMaxSplitsDec + sp] = ml.x;
-    sl2[g * kMaxSplitsDec + sp] = ml.y;
+  if (tid < G)
+    for (int p = 0; p < a.splits; ++p)
+      st_dsmem_f2(mapa_shared(rml + (uint32_t)((split * kMaxG + tid) * 8), (uint32_t)p), Mh, Lh);
+  if (a.splits > 1) {
+    cluster_arrive_release();  // the pushes are visible to their owners after the wait
+    cluster_wait_acquire();
+  } else {
+    __syncthreads();
   }
-  __syncthreads();
-  if (tid < G) {
+  dec_trace(a, 6);
+
+  // ---- merge the owned slice: out = sum_s w_s o_s / sum_s w_s l_s with w_s = exp2(m_s - max_s m_s)
+  const float* rmlp = reinterpret_cast<const float*>(dsmem + S::RML_OFF);
+  const float* rop = reinterpret_cast<const float*>(dsmem + S::RO_OFF);
+  for (int slot = 0; slot < E; ++slot) {
+    const int j = slot * a.splits + split;  // this thread's element i = tid + 128 j
+    if (j >= per) break;
+    const int i = tid + j * kThreads, g = i / D, d = i % D;
+    if (i >= G * D) break;
     float M = -INFINITY;
-    for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, sm2[tid * kMaxSplitsDec + sp]);
+    for (int sp = 0; sp < a.splits; ++sp) M = fmaxf(M, rmlp[(sp * kMaxG + g) * 2]);
     const float muse = M == -INFINITY ? 0.f : M;
-    float den = 0.f;
+    float num = 0.f, den = 0.f;
     for (int sp = 0; sp < a.splits; ++sp) {
-      const float m = sm2[tid * kMaxSplitsDec + sp];
+      const float m = rmlp[(sp * kMaxG + g) * 2];
       const float w = m == -INFINITY ? 0.f : ex2_fast(m - muse);
-      sw[tid * kMaxSplitsDec + sp] = w;
-      den += w * sl2[tid * kMaxSplitsDec + sp];
+      num += w * rop[(sp * E + slot) * kThreads + tid];
+      den += w * rmlp[(sp * kMaxG + g) * 2 + 1];
     }
-    sinv[tid] = den > 0.f ? 1.f / den : 0.f;
+    a.out[(int64_t)b * a.ob + (int64_t)(hk * G + g) * a.oh + d] = __float2bfloat16_rn(den > 0.f ? num / den : 0.f);
   }
-  __syncthreads();
-  // outputs: thread -> 4 consecutive dims of one head per pass; the splits' loads are batched 4 deep
-  for (int i = tid * 4; i < G * D; i += kThreads * 4) {
-    const int g = i / D, d = i % D;
-    float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
-    const float4* src = reinterpret_cast<const float4*>(a.part_o + (base0 + g) * D + d);
-    const int64_t stride4 = (int64_t)G * D / 4;  // one split further
-    int sp = 0;
-    for (; sp + 4 <= a.splits; sp += 4) {
-      float4 v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = __ldcg(src + (sp + u) * stride4);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const float w = sw[g * kMaxSplitsDec + sp + u];
-        num.x += w * v[u].x;
-        num.y += w * v[u].y;
-        num.z += w * v[u].z;
-        num.w += w * v[u].w;
-      }
-    }
-    for (; sp < a.splits; ++sp) {
-      const float4 v = __ldcg(src + sp * stride4);
-      const float w = sw[g * kMaxSplitsDec + sp];
-      num.x += w * v.x;
-      num.y += w * v.y;
-      num.z += w * v.z;
-      num.w += w * v.w;
-    }
-    const float inv = sinv[g];
-    __nv_bfloat16* o = a.out + (int64_t)b * a.ob + (int64_t)(hk * G + g) * a.oh + d;
-    const __nv_bfloat162 lo = __floats2bfloat162_rn(num.x * inv, num.y * inv);
-    const __nv_bfloat162 hi = __floats2bfloat162_rn(num.z * inv, num.w * inv);
-    reinterpret_cast<__nv_bfloat162*>(o)[0] = lo;
-    reinterpret_cast<__nv_bfloat162*>(o)[1] = hi;
-  }
+  dec_trace(a, 7);
 }
 
 // New token: rotate q (in place) and k, write k and v into their paged slots.
@@ -404,74 +481,121 @@ __global__ void kv_append_rope_kernel(__nv_bfloat16* qkv, int64_t ld, int B, int
 }
 
 template <int D>
-int launch_decode(const DecodeArgs& a, void* out, int64_t ob, int64_t oh, cudaStream_t st) {
-  constexpr int dyn = DecSmem<D>::TOTAL;
+cudaError_t decode_attrs() {
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!attr[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(decode_split_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn);
-    if (e != cudaSuccess) return (int)e;
-    // largest shared-memory carveout: two ~100 KB CTAs per SM
-    e = cudaFuncSetAttribute(decode_split_kernel<D>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                             (int)cudaSharedmemCarveoutMaxShared);
-    if (e != cudaSuccess) return (int)e;
-    attr[dev & 63] = true;
+  if (attr[dev & 63]) return cudaSuccess;
+  auto kern = decode_split_kernel<D>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DecSmem<D>::TOTAL);
+  if (e != cudaSuccess) return e;
+  // largest shared-memory carveout: two ~100 KB CTAs per SM; clusters of up to 16 splits
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return e;
+  attr[dev & 63] = true;
+  return cudaSuccess;
+}
+
+template <int D>
+cudaLaunchConfig_t decode_config(int splits, int pairs, cudaLaunchAttribute* at, cudaStream_t st, bool pdl) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(splits, pairs);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = DecSmem<D>::TOTAL;
+  cfg.stream = st;
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = splits;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cfg;
+}
+
+// How many clusters of `splits` CTAs can be resident at once (0 when none fits).
+template <int D>
+int decode_active_clusters(int splits) {
+  if (decode_attrs<D>() != cudaSuccess) return 0;
+  cudaLaunchAttribute at[2];
+  cudaLaunchConfig_t cfg = decode_config<D>(splits, 1, at, 0, false);
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, decode_split_kernel<D>, &cfg) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return 0;
   }
-  const bool pdl = brain_host::g_decode_pdl != 0;
-  (void)out;
-  (void)ob;
-  (void)oh;
-  return (int)brain_host::launch(decode_split_kernel<D>, dim3(a.splits, a.B * a.Hkv), dim3(kThreads), dyn, st, pdl,
-                                 a);
+  return n;
+}
+
+// K or V pool [num_blocks * block_size rows, Hkv * D columns] bf16 as 16-row x 64-column boxes with the
+// 128-byte swizzle.
+bool encode_pool(CUtensorMap* m, const void* pool, int64_t rows, int cols) {
+  uint64_t dims[2] = {(uint64_t)cols, (uint64_t)rows};
+  uint64_t strides[1] = {(uint64_t)cols * 2};
+  uint32_t box[2] = {64, (uint32_t)kRowsBox};
+  return brain_host::encode_tiled(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(pool), dims, strides, box,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int D>
+int launch_decode(const CUtensorMap& tk, const CUtensorMap& tv, const DecodeArgs& a, cudaStream_t st) {
+  cudaError_t e = decode_attrs<D>();
+  if (e != cudaSuccess) return (int)e;
+  cudaLaunchAttribute at[2];
+  cudaLaunchConfig_t cfg = decode_config<D>(a.splits, a.B * a.Hkv, at, st, brain_host::g_decode_pdl != 0);
+  return (int)cudaLaunchKernelEx(&cfg, decode_split_kernel<D>, tk, tv, a);
 }
 
 }  // namespace
 
 BRAIN_STATUS_READER(attention_decode)
 
-// Number of 4-byte elements of the workspace: split outputs B*Hkv*splits*G*D f32, split (max, sum)
-// B*Hkv*splits*G*2 f32, then B*Hkv int32 tickets that must be zero before the first call (every call
-// leaves them zero).
-BRAIN_API int64_t brain_decode_workspace(int B, int Hq, int Hkv, int D, int splits) {
-  return (int64_t)B * Hq * splits * (D + 2) + (int64_t)B * Hkv;
-}
-
-// Pick a split count so that B * Hkv * splits fills the GPU (about two CTAs per SM).
-BRAIN_API int brain_decode_splits(int B, int Hkv, int max_len) {
-  const int ctas = B * Hkv;
-  int want = (2 * brain_host::num_sms()) / (ctas > 0 ? ctas : 1);  // one wave at two CTAs per SM
+// Split count (= cluster size) for B sequences x Hkv kv heads of up to max_len tokens with head dim D:
+// the largest count whose B * Hkv clusters are resident in one wave at about two CTAs per SM.
+BRAIN_API int brain_decode_splits(int B, int Hkv, int D, int max_len) {
+  const int pairs = B * Hkv > 0 ? B * Hkv : 1;
   const int chunks = (max_len + kBlock - 1) / kBlock;
-  if (want > chunks) want = chunks;
-  if (want > kMaxSplitsDec) want = kMaxSplitsDec;
-  return want < 1 ? 1 : want;
+  int c = std::min(kMaxSplitsDec, std::max(chunks, 1));
+  for (; c > 1; --c) {
+    if (c * pairs > 2 * brain_host::num_sms()) continue;
+    if (c <= 8) break;  // portable cluster size
+    const int fit = D == 64 ? decode_active_clusters<64>(c) : decode_active_clusters<128>(c);
+    if (fit >= pairs) break;
+  }
+  return c;
 }
 
+// K/V pools are contiguous [num_blocks, block_size, Hkv, D] bf16 with block_size a multiple of 16.
 BRAIN_API int brain_decode_attention(const void* q, int64_t qb, int64_t qh, const void* kpool, const void* vpool,
-                                     const int* table, int max_blocks, const int* seq_lens, int block_size, void* out,
-                                     int64_t ob, int64_t oh, float* workspace, int B, int Hq, int Hkv, int D,
-                                     float scale, int splits, cudaStream_t st) {
+                                     int num_blocks, const int* table, int max_blocks, const int* seq_lens,
+                                     int block_size, void* out, int64_t ob, int64_t oh, int B, int Hq, int Hkv, int D,
+                                     float scale, int splits, unsigned long long* trace, cudaStream_t st) {
   if (Hkv <= 0 || Hq % Hkv || Hq / Hkv > kMaxG) return (int)cudaErrorInvalidValue;
   if (D != 64 && D != 128) return (int)cudaErrorInvalidValue;
+  if (block_size <= 0 || block_size % kRowsBox) return (int)cudaErrorInvalidValue;
   if (B == 0) return 0;
+  if (splits < 1 || splits > kMaxSplitsDec) return (int)cudaErrorInvalidValue;
+  if (B * Hkv > 65535) return (int)cudaErrorInvalidValue;
+  CUtensorMap tk, tv;
+  const int64_t rows = (int64_t)num_blocks * block_size;
+  if (!encode_pool(&tk, kpool, rows, Hkv * D) || !encode_pool(&tv, vpool, rows, Hkv * D))
+    return (int)cudaErrorInvalidValue;
   DecodeArgs a;
   a.q = reinterpret_cast<const __nv_bfloat16*>(q);
   a.qb = qb; a.qh = qh;
-  a.kp = reinterpret_cast<const __nv_bfloat16*>(kpool);
-  a.vp = reinterpret_cast<const __nv_bfloat16*>(vpool);
   a.table = table; a.max_blocks = max_blocks; a.seq_lens = seq_lens; a.block_size = block_size;
   a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.D = D;
   a.scale_log2 = scale * 1.4426950408889634f;
-  if (splits < 1 || splits > kMaxSplitsDec) return (int)cudaErrorInvalidValue;
   a.splits = splits;
-  a.part_o = workspace;
-  a.part_ml = workspace + (int64_t)B * Hq * splits * D;
-  a.tickets = reinterpret_cast<int*>(workspace + (int64_t)B * Hq * splits * (D + 2));
   a.out = reinterpret_cast<__nv_bfloat16*>(out);
   a.ob = ob;
   a.oh = oh;
-  if (B * Hkv > 65535) return (int)cudaErrorInvalidValue;
-  return D == 64 ? launch_decode<64>(a, out, ob, oh, st) : launch_decode<128>(a, out, ob, oh, st);
+  a.trace = trace;
+  a.pdl_late = brain_host::g_decode_pdl == 2;
+  return D == 64 ? launch_decode<64>(tk, tv, a, st) : launch_decode<128>(tk, tv, a, st);
 }
 
 BRAIN_API int brain_kv_append_rope(void* qkv, int64_t ld, int B, int Hq, int Hkv, int D, const int* pos,

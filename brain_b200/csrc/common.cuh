@@ -383,7 +383,8 @@ int num_sms();
 bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, void* base, const uint64_t* dims,
                   const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swz);
 
-// Decode-step kernels launch with programmatic dependent launch while this is non-zero
+// Decode-step kernels launch with programmatic dependent launch while this is non-zero (2: the main
+// kernels let their successors launch after their main loop)
 // (brain_decode_set_pdl; defined in decode_tp.cu).
 extern int g_decode_pdl;
 

@@ -82,6 +82,7 @@ struct SkinnyArgs {
   int max_blocks, block_size;
   // optional per-CTA phase timestamps (globaltimer ns), [cta][8]; null = off
   unsigned long long* trace;
+  int pdl_late;  // let dependents launch after the main loop instead of at the start
 };
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int64_t idx) {
@@ -167,7 +168,7 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* ticket = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
-  pdl_trigger();
+  if (!a.pdl_late) pdl_trigger();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int split = blockIdx.x, tile = blockIdx.y;
   unsigned long long* trace =
@@ -281,6 +282,7 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
   // straight-line code here was dominated by cold instruction fetch.
   const bool ok = mbar_wait(done_bar, 0, BRAIN_ERR_TIMEOUT_ACC, 112, abort_flag);
   tc_fence_after();
+  if (a.pdl_late) pdl_trigger();  // every weight tile consumed: the successor may take the SM slots
   if (trace) {
     trace[3] = globaltimer();
     trace[8] = clock64();
@@ -723,12 +725,15 @@ bool map_2d(CUtensorMap* m, const void* p, uint64_t inner, uint64_t outer, uint6
 }  // namespace
 
 namespace brain_host {
-int g_decode_pdl = 1;
+int g_decode_pdl = 2;
 }
 
 BRAIN_STATUS_READER(decode_tp)
 
-// Programmatic dependent launch for the decode-step kernels on (1) or off (0); returns the old value.
+// Programmatic dependent launch for the decode-step kernels: 0 off; 1 on, dependents may launch as soon
+// as a kernel starts; 2 on, the skinny GEMM and the decode attention let them launch only after their
+// main loop (their early-launched successors would otherwise take SM slots they still need). Returns
+// the old value.
 BRAIN_API int brain_decode_set_pdl(int on) {
   const int old = brain_host::g_decode_pdl;
   brain_host::g_decode_pdl = on;
@@ -786,6 +791,7 @@ BRAIN_API int brain_skinny_gemm(const void* X, int64_t ldx, const void* W, int64
   a.R = reinterpret_cast<const __nv_bfloat16*>(R);
   a.ldr = ldr;
   if (ext) a.trace = reinterpret_cast<unsigned long long*>(ext[15]);
+  a.pdl_late = brain_host::g_decode_pdl == 2;
   if (epi == EPI_PUSH || epi == EPI_ARGMAX || epi == EPI_QKV) {
     if (!ext) return (int)cudaErrorInvalidValue;
     a.world = (int)ext[0];

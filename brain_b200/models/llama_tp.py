@@ -32,9 +32,10 @@ import math
 import torch
 import torch.distributed as dist
 
-from .. import _native, ops
-from ..ops.decode import (EPI_ARGMAX, EPI_PUSH, EPI_QKV, EPI_SWIGLU, ar_norm, decode_ext, init_ar_slots,
-                          interleave_gate_up, paged_decode_attention, pick_embed, skinny_gemm, skinny_splits)
+from .. import ops
+from ..ops.decode import (EPI_ARGMAX, EPI_PUSH, EPI_QKV, EPI_SWIGLU, ar_norm, decode_ext, decode_splits,
+                          init_ar_slots, interleave_gate_up, paged_decode_attention, pick_embed, skinny_gemm,
+                          skinny_splits)
 from .config import LlamaLiteConfig
 
 
@@ -150,9 +151,7 @@ class LlamaTPServe:
         self.q = torch.empty(B, self.hq * self.D, device=dev, dtype=torch.bfloat16)
         self.attn = torch.empty(B, self.hq * self.D, device=dev, dtype=torch.bfloat16)
         self.act = torch.empty(B, self.F, device=dev, dtype=torch.bfloat16)
-        self.attn_splits = int(_native.fn("brain_decode_splits")(B, self.hkv, max_len))
-        n_ws = int(_native.fn("brain_decode_workspace")(B, self.hq, self.hkv, self.D, self.attn_splits))
-        self.attn_ws = torch.zeros(n_ws, device=dev, dtype=torch.float32)
+        self.attn_splits = decode_splits(B, self.hkv, self.D, max_len)
         self.comm = _StepComm(B, d, self.world, self.rank, group, dev)
         self.tp = None  # TPContext for the sequence-parallel prefill (created on first use)
         self.graph = None
@@ -223,7 +222,7 @@ class LlamaTPServe:
         for i in range(c.num_layers):
             skinny_gemm(self.normed, self.wqkv[i], EPI_QKV, out=self.q, ext=self.ext_qkv[i], splits=self.sp["qkv"])
             paged_decode_attention(self.q.view(B, self.hq, self.D), self.kv[i, 0], self.kv[i, 1], self.table,
-                                   self.seq_lens, splits=self.attn_splits, workspace=self.attn_ws,
+                                   self.seq_lens, splits=self.attn_splits,
                                    out=self.attn.view(B, self.hq, self.D))
             skinny_gemm(self.attn, self.wo[i], EPI_PUSH, ext=self.ext_push, splits=self.sp["o"])
             ar_norm(cm.ar_local, cm.ctrl, self.world, cm.ar_elems, self.resid, self.ffn_norm[i],
@@ -235,7 +234,7 @@ class LlamaTPServe:
         self._head_and_pick()
 
     def launches_per_step(self) -> int:
-        return self.cfg.num_layers * 8 + 2  # decode attention is two launches (splits + combine)
+        return self.cfg.num_layers * 7 + 2
 
     def capture(self):
         """Record one decode step as a CUDA graph (run ``prefill`` first: the kernels see real state)."""

@@ -3,9 +3,12 @@
 ``paged_decode_attention(q, k_pool, v_pool, block_table, seq_lens)``: q [B, Hq, D] (one new token
 per sequence, any strides with unit stride on D), pools [num_blocks, block_size, Hkv, D],
 block_table [B, max_blocks] int32, seq_lens [B] int32 (cached tokens, the new one included).
-A caller-provided ``workspace`` (f32, ``brain_decode_workspace`` elements) must start zeroed: its tail
-holds per-(sequence, kv head) tickets that every call leaves at zero. On CPU the cache is gathered per
-sequence and the reference SDPA is used.
+The splits of a sequence merge inside one thread-block cluster, so no workspace is needed. With
+programmatic dependent launch on (``set_pdl``), K/V older than the newest token are read before the
+kernel waits on the preceding launch: a launch that may still run then must not write K/V below
+position seq_lens[b] - 1 (the decode step writes only the newest token). On CPU the cache is gathered
+per sequence and the reference SDPA is used. On the GPU the pool block size must be a multiple of 16
+(K/V rows arrive as TMA boxes of 16 tokens).
 """
 from __future__ import annotations
 
@@ -17,35 +20,41 @@ from .. import _native
 from ._common import same_device, stream
 
 _native.register({
-    "brain_decode_workspace": ("brain_kernels", "iiiii"),
-    "brain_decode_splits": ("brain_kernels", "iii"),
-    "brain_decode_attention": ("brain_kernels", "pllpppipipllpiiiifis"),
+    "brain_decode_splits": ("brain_kernels", "iiii"),
+    "brain_decode_attention": ("brain_kernels", "pllppipipiplliiiifips"),
     "brain_kv_append_rope": ("brain_kernels", "pliiiipppppiis"),
     "brain_status_attention_decode": ("brain_kernels", "pi"),
 })
-_native.RETURNS_I64.add("brain_decode_workspace")
+
+
+def decode_splits(B: int, Hkv: int, D: int, max_len: int) -> int:
+    """Split count (cluster size) of the decode attention for this batch shape on the current GPU."""
+    return int(_native.fn("brain_decode_splits")(B, Hkv, D, max_len))
 
 
 def paged_decode_attention(q, k_pool, v_pool, block_table, seq_lens, scale=None, splits=None, max_len=None,
-                           workspace=None, out=None):
+                           out=None, trace=None):
+    """``trace``: optional int64 CUDA tensor of (B * Hkv * splits * 8) elements that receives per-CTA
+    globaltimer stamps (start, length read, after the wait, Q loaded, first chunk, loop end, cluster
+    barrier, end) for profiling."""
     B, Hq, D = q.shape
     Hkv = k_pool.shape[2]
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
-    same_device(q, k_pool, v_pool, block_table, seq_lens, workspace, out)
+    same_device(q, k_pool, v_pool, block_table, seq_lens, out)
     if not q.is_cuda:
         return _decode_ref(q, k_pool, v_pool, block_table, seq_lens, scale)
     if splits is None:
         ml = max_len if max_len is not None else block_table.shape[1] * k_pool.shape[1]
-        splits = int(_native.fn("brain_decode_splits")(B, Hkv, ml))
-    if workspace is None:
-        n = int(_native.fn("brain_decode_workspace")(B, Hq, Hkv, D, splits))
-        workspace = torch.zeros(n, device=q.device, dtype=torch.float32)
+        splits = decode_splits(B, Hkv, D, ml)
     if out is None:
         out = torch.empty(B, Hq, D, device=q.device, dtype=q.dtype)
+    if not (k_pool.is_contiguous() and v_pool.is_contiguous() and block_table.is_contiguous()):
+        raise ValueError("paged_decode_attention: K/V pools and the block table must be contiguous")
     _native.call("brain_decode_attention", q.data_ptr(), q.stride(0), q.stride(1), k_pool.data_ptr(),
-                 v_pool.data_ptr(), block_table.data_ptr(), block_table.shape[1], seq_lens.data_ptr(), k_pool.shape[1],
-                 out.data_ptr(), out.stride(0), out.stride(1), workspace.data_ptr(), B, Hq, Hkv, D, float(scale),
-                 int(splits), stream(q))
+                 v_pool.data_ptr(), k_pool.shape[0], block_table.data_ptr(), block_table.shape[1],
+                 seq_lens.data_ptr(), k_pool.shape[1],
+                 out.data_ptr(), out.stride(0), out.stride(1), B, Hq, Hkv, D, float(scale),
+                 int(splits), trace.data_ptr() if trace is not None else 0, stream(q))
     return out
 
 
@@ -105,9 +114,11 @@ _native.register({
 })
 
 
-def set_pdl(on: bool) -> bool:
-    """Programmatic dependent launch for the decode-step kernels; returns the previous setting."""
-    return bool(_native.fn("brain_decode_set_pdl")(int(bool(on))))
+def set_pdl(mode) -> int:
+    """Programmatic dependent launch for the decode-step kernels: 0/False off; 1/True on, a kernel's
+    successor may launch as soon as it starts; 2 on, the skinny GEMM and the decode attention let their
+    successor launch only after their main loop. Returns the previous mode."""
+    return int(_native.fn("brain_decode_set_pdl")(int(mode)))
 
 
 def skinny_splits(M: int, N: int, K: int) -> int:

@@ -41,10 +41,18 @@ def test_decode_ref_matches_dense_cpu():
     (128, 8, 1, 64, [1, 64, 65, 700]),
     (128, 64, 8, 128, [300, 2048, 17, 1000]),
     (64, 16, 4, 64, [129, 5]),
+    (64, 6, 2, 16, [33, 200, 1]),      # 3 query heads per kv head, 16-token blocks
+    (128, 5, 5, 32, [100, 31]),        # one query head per kv head, 32-token blocks
 ])
 def test_paged_decode_attention_gpu(D, Hq, Hkv, bs, lens):
     B = len(lens)
     kp, vp, table, sl = _paged(B, Hkv, D, lens, bs, "cuda")
+    # rows past each sequence's end hold NaN: they must not leak into the output
+    for b, L in enumerate(lens):
+        if L % bs:
+            blk = int(table[b, L // bs])
+            kp[blk, L % bs:] = float("nan")
+            vp[blk, L % bs:] = float("nan")
     # q as a strided view of a fused qkv row, as the model produces it
     qkv = torch.randn(B, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
     q = qkv[:, :Hq * D].view(B, Hq, D)
@@ -53,9 +61,12 @@ def test_paged_decode_attention_gpu(D, Hq, Hkv, bs, lens):
     assert not check_status()
     err = (out.cpu().float() - ref.float()).abs().max().item()
     assert err < 2e-2, err
-    # a forced split count gives the same result
-    out1 = paged_decode_attention(q, kp, vp, table, sl, splits=1)
-    assert (out1.float() - out.float()).abs().max().item() < 2e-2
+    # every cluster size (split count) gives the same result, including splits that own no keys and
+    # the non-portable sizes above 8
+    for sp in (1, 2, 5, 8, 11, 16):
+        out1 = paged_decode_attention(q, kp, vp, table, sl, splits=sp)
+        assert not check_status()
+        assert (out1.float() - out.float()).abs().max().item() < 2e-2, sp
 
 
 @pytest.mark.gpu
