@@ -92,7 +92,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", default="brain", choices=["brain", "reference"])
+    ap.add_argument("--impl", default="brain", choices=["brain", "reference", "torch"],
+                    help="brain: this framework; reference: the reference's own code; torch: a plain PyTorch "
+                         "eager + cuBLAS + SDPA + NCCL DDP implementation of the same model and config")
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--micro-batch", type=int, default=2)
     ap.add_argument("--layers", type=int, default=32, help="development only: fewer layers is not the benchmark")
@@ -124,6 +126,9 @@ def main():
     if args.impl == "reference":
         print(json.dumps({"impl": "reference", "unavailable": REF_UNAVAILABLE}), flush=True)
         return 0
+
+    if args.impl == "torch":
+        return run_torch_baseline(args)
 
     import torch
     import torch.distributed as dist
@@ -259,6 +264,111 @@ def main():
         print(json.dumps(out), flush=True)
     del dp, model
     bdist.shutdown()
+    return 0
+
+
+def run_torch_baseline(args) -> int:
+    """The headline training config on plain PyTorch (``brain_b200.bench.torch_baseline``): eager
+    modules, cuBLAS, SDPA, fused torch AdamW, DistributedDataParallel over NCCL; same timing rules."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from brain_b200.bench.torch_baseline import build
+    from brain_b200.models.config import LlamaLiteConfig
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = LlamaLiteConfig.llama3_8b(max_seq_len=args.seq)
+    if args.layers != cfg.num_layers:
+        cfg = cfg.replace(num_layers=args.layers)
+    model = build(cfg, dev, seed=0)
+    ddp = (torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], gradient_as_bucket_view=True)
+           if world > 1 else model)
+    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, fused=True)
+    B, S, V = args.micro_batch, args.seq, cfg.vocab_size
+    cos, sin = model.rope_tables(S, dev)
+    gen = torch.Generator(device=dev).manual_seed(1 + rank)
+    pool = [torch.randint(0, V, (B, S + 1), generator=gen, device=dev) for _ in range(4)]
+
+    def step(t):
+        loss = ddp(t[:, :-1], t[:, 1:], cos, sin)
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=False)
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_ms(v):
+        t = torch.tensor([v], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for i in range(max(3, args.warmup)):
+        loss = step(pool[i % 4])
+    torch.cuda.synchronize()
+    log(f"[torch rank {rank}] warm-up done, loss {loss.item():.4f}, peak mem "
+        f"{torch.cuda.max_memory_allocated() / 2**30:.1f} GiB")
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        loss = step(pool[i % 4])
+    e.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop() if clocks else None
+    ms = max_ms(s.elapsed_time(e) / args.steps)
+    host = [torch.randint(0, V, (B, S + 1), generator=torch.Generator().manual_seed(100 + rank * 1000 + i)).pin_memory()
+            for i in range(4)]
+    buf = torch.empty(B, S + 1, dtype=torch.int64, device=dev)
+    barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for i in range(args.steps):
+        buf.copy_(host[i % 4], non_blocking=True)
+        lv = step(buf).item()
+    e2.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms2 = max_ms(s2.elapsed_time(e2) / args.steps)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "train tok/s Llama-3-8B-shape DDP @1/2/4/8 B200; 70B-shape TP=8 decode tok/s",
+            "value": B * S * world / (ms / 1e3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (uniform random tokens, seeded; random-init N(0,0.02) weights)",
+            "config": {"model": "Llama-3-8B-shape" + ("" if cfg.num_layers == 32 else f" ({cfg.num_layers} layers)"),
+                       "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": S,
+                       "parallelism": f"dp{world}",
+                       "implementation": "plain PyTorch: eager nn modules, cuBLAS, F.scaled_dot_product_attention, "
+                                         "torch.optim.AdamW(fused=True) on bf16 parameters, DDP over NCCL",
+                       "l2": "no flush: working set >> 126 MB L2"},
+            "final_loss": float(loss.item()), "clocks": clk,
+            "e2e": {"value": B * S * world / (ms2 / 1e3), "unit": "tokens/s", "ms_per_step": ms2,
+                    "h2d_bytes_per_step": B * (S + 1) * 8, "d2h_bytes_per_step": 4,
+                    "api": "torch module forward/backward + optimizer.step", "last_loss": lv},
+            "impl": "torch"}), flush=True)
+    del ddp, model, opt
+    if world > 1:
+        dist.destroy_process_group()
     return 0
 
 

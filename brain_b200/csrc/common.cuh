@@ -146,6 +146,22 @@ __device__ __forceinline__ bool bar_sync_and(int id, int nthreads, bool v) {
   return r != 0;
 }
 
+// 2-D tiled TMA store from this CTA's shared memory to global memory (bulk-group completion), and
+// the bulk-group commit / waits that order it: wait_read<N> returns once at most N committed groups
+// still read shared memory (their source buffers may be rewritten); wait_all once every group's
+// writes are done.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map), "r"(src),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 // 2-D tiled TMA load into this CTA's shared memory, completing on `bar` (complete_tx::bytes).
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint32_t dst, uint32_t bar, int x,
                                             int y) {

@@ -124,6 +124,47 @@ __global__ void rope_kernel(__nv_bfloat16* __restrict__ x, int B, int S, int H, 
   }
 }
 
+// Vectorised RoPE: a thread rotates 8 consecutive pairs (16-byte loads and stores of both halves,
+// 32-byte loads of cos and sin); rows (b, s, h) are enumerated with 32-bit index arithmetic.
+// Needs D % 16 == 0, 16-byte aligned rows and fewer than 2^31 8-pair units.
+__global__ void rope_vec_kernel(__nv_bfloat16* __restrict__ x, int S, int H, int D, int64_t sb, int64_t ss, int64_t sh,
+                                const float* __restrict__ cs, const int* __restrict__ pos, int pos_offset, float sign,
+                                int units) {
+  const int half = D / 2, U = half / 8;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < units; i += gridDim.x * blockDim.x) {
+    const int u = i % U;
+    const int row = i / U;
+    const int h = row % H;
+    const int bsi = row / H;
+    const int s = bsi % S, b = bsi / S;
+    const int p = pos ? pos[bsi] : pos_offset + s;
+    const int j = u * 8;
+    __nv_bfloat16* base = x + b * sb + s * ss + h * sh;
+    const uint4 ra = *reinterpret_cast<const uint4*>(base + j);
+    const uint4 rb = *reinterpret_cast<const uint4*>(base + j + half);
+    const float4* cp = reinterpret_cast<const float4*>(cs + (int64_t)p * D + j);
+    const float4* sp = reinterpret_cast<const float4*>(cs + (int64_t)p * D + half + j);
+    const float4 c0 = __ldg(cp), c1 = __ldg(cp + 1), s0 = __ldg(sp), s1 = __ldg(sp + 1);
+    const float cv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+    const float sv[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&ra);
+    const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&rb);
+    uint4 oa, ob;
+    __nv_bfloat162* oa2 = reinterpret_cast<__nv_bfloat162*>(&oa);
+    __nv_bfloat162* ob2 = reinterpret_cast<__nv_bfloat162*>(&ob);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float2 x1 = __bfloat1622float2(a2[k]), x2 = __bfloat1622float2(b2[k]);
+      const float c_lo = cv[2 * k], c_hi = cv[2 * k + 1];
+      const float s_lo = sign * sv[2 * k], s_hi = sign * sv[2 * k + 1];
+      oa2[k] = __floats2bfloat162_rn(x1.x * c_lo - x2.x * s_lo, x1.y * c_hi - x2.y * s_hi);
+      ob2[k] = __floats2bfloat162_rn(x2.x * c_lo + x1.x * s_lo, x2.y * c_hi + x1.y * s_hi);
+    }
+    *reinterpret_cast<uint4*>(base + j) = oa;
+    *reinterpret_cast<uint4*>(base + j + half) = ob;
+  }
+}
+
 // out[m, :] = W[ids[m], :] (+ P[m % S, :])   (rows of D elements, D % 8 == 0)
 __global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ W,
                                      const __nv_bfloat16* __restrict__ P, int S, __nv_bfloat16* __restrict__ out,
@@ -236,8 +277,17 @@ BRAIN_API int brain_rope(void* x, int B, int S, int H, int D, int64_t sb, int64_
   if (D % 2) return (int)cudaErrorInvalidValue;
   const int64_t pairs = (int64_t)B * S * H * (D / 2);
   if (pairs == 0) return 0;
-  rope_kernel<<<grid_for(pairs, 256), 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(x), B, S, H, D, sb, ss, sh, cs,
-                                                   pos, pos_offset, sign);
+  const int64_t units = pairs / 8;
+  const bool vec = D % 16 == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 && sb % 8 == 0 && ss % 8 == 0 &&
+                   sh % 8 == 0 && (reinterpret_cast<uintptr_t>(cs) & 15) == 0 && units < (int64_t)INT32_MAX &&
+                   (int64_t)B * S < (int64_t)INT32_MAX;
+  if (vec) {
+    rope_vec_kernel<<<grid_for(units, 256), 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(x), S, H, D, sb, ss, sh,
+                                                          cs, pos, pos_offset, sign, (int)units);
+  } else {
+    rope_kernel<<<grid_for(pairs, 256), 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(x), B, S, H, D, sb, ss, sh,
+                                                     cs, pos, pos_offset, sign);
+  }
   return (int)cudaGetLastError();
 }
 

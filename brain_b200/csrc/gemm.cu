@@ -51,6 +51,9 @@ struct GemmArgs {
   int push_chunk_rows;
   int64_t push_slot_elems;
   __nv_bfloat16* push_dst[8];
+  // CTA-pair kernel: the output tile leaves through shared memory and TMA stores (tmC) instead of
+  // per-thread row stores
+  int tma_store;
 };
 
 template <int BN, int STAGES>
@@ -75,6 +78,58 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 
 __device__ __forceinline__ void store_chunk_at(const GemmArgs& args, int gm, int gn0, const uint32_t* r, void* cbase,
                                                int64_t crow);
+
+// alpha, bias, residual and beta * C_old for one row x 32 columns (C_old read at row gm of C).
+__device__ __forceinline__ void epi_math(const GemmArgs& args, int gm, int gn0, const uint32_t* r, float* v) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
+  if (gm >= args.M) return;
+  const bool full = gn0 + 32 <= args.N;
+  if (args.bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (full || gn0 + j < args.N) v[j] += __bfloat162float(args.bias[gn0 + j]);
+  }
+  if (args.R) {
+    const __nv_bfloat16* rp = args.R + (int64_t)gm * args.ldr + gn0;
+    if (full && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        float rv[8];
+        load8(rp + j, rv);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[j + u] += rv[u];
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (gn0 + j < args.N) v[j] += __bfloat162float(rp[j]);
+    }
+  }
+  if (args.accumulate) {
+    if (args.c_f32) {
+      const float* cp = reinterpret_cast<const float*>(args.C) + (int64_t)gm * args.ldc + gn0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (full || gn0 + j < args.N) v[j] += args.beta * cp[j];
+    } else {
+      const __nv_bfloat16* cp = reinterpret_cast<const __nv_bfloat16*>(args.C) + (int64_t)gm * args.ldc + gn0;
+      if (full && ((reinterpret_cast<uintptr_t>(cp) & 15) == 0)) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          float old[8];
+          load8(cp + j, old);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[j + u] += args.beta * old[u];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (gn0 + j < args.N) v[j] += args.beta * __bfloat162float(cp[j]);
+      }
+    }
+  }
+}
 
 // Epilogue for one row x 32 columns of f32 accumulator: alpha, bias, residual, beta * C_old, store
 // (or push to the owning ranks' receive buffers).
@@ -343,19 +398,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 // accumulator barriers of both CTAs (one commit per CTA address); each CTA's epilogue drains its
 // own 128 TMEM lanes and releases the accumulator on CTA 0's barrier.
 // ---------------------------------------------------------------------------------------------
-constexpr int kPairStages = 6;
+constexpr int kPairStages = 5;
 struct PairSmem {
   static constexpr int A_BYTES = 128 * BK * 2;
   static constexpr int B_BYTES = 128 * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFFSET = kPairStages * STAGE_BYTES;
+  // output staging: per epilogue warp two 4 KB buffers of 32 rows x 128 B (128-byte swizzle)
+  static constexpr int EPI_OFFSET = kPairStages * STAGE_BYTES;
+  static constexpr int EPI_BYTES = 4 * 2 * 4096;
+  static constexpr int BAR_OFFSET = EPI_OFFSET + EPI_BYTES;
   static constexpr int TOTAL = BAR_OFFSET + (2 * kPairStages + 5) * 8 + 16 + 1024;
 };
 
 template <int A_MN, int B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    GemmArgs args) {
+                    const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
   using S = PairSmem;
   constexpr int ST = kPairStages;
   constexpr int TN = 256;  // pair tile: 256 x 256
@@ -391,6 +449,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (args.tma_store) prefetch_tmap(&tmC);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), 512);
@@ -499,6 +558,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // ---------------- epilogue (warps 2..5 of both CTAs)
     const int q = warp & 3;
     const int row_in_tile = (int)cta * 128 + q * 32 + lane;
+    const uint32_t stg = sbase + S::EPI_OFFSET + (uint32_t)q * 8192u;  // this warp's two staging buffers
+    int ebuf = 0;
     int local = 0;
     for (int t = pid; t < args.num_tiles; t += npairs, ++local) {
       const int acc = local & 1;
@@ -510,20 +571,73 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const int gm = tm * 256 + row_in_tile;
       const int n0 = tn * TN;
       const bool row_ok = gm < args.M;
+      const uint32_t tm_row = tmem_base + (uint32_t)(acc * TN) + ((uint32_t)(q * 32) << 16);
+      if (args.tma_store) {
+        // 128 B of this row per unit (64 bf16 or 32 f32 columns): registers -> swizzled staging buffer
+        // -> one TMA store of the warp's 32 rows; the two buffers alternate, and a buffer is rewritten
+        // only after the store issued from it two units earlier has read it.
+        const int cols = args.c_f32 ? 32 : 64;
+        const int row0 = tm * 256 + (int)cta * 128 + q * 32;
 #pragma unroll 1
-      for (int c = 0; c < TN / 32; ++c) {
-        uint32_t r[32];
-        __syncwarp();
-        tmem_ld32(tmem_base + (uint32_t)(acc * TN + c * 32) + ((uint32_t)(q * 32) << 16), r);
-        tc_wait_ld();
-        const int gn0 = n0 + c * 32;
-        if (row_ok && gn0 < args.N) store_chunk(args, gm, gn0, r);
-        __syncwarp();
+        for (int u = 0; u < TN / cols; ++u) {
+          if (n0 + u * cols >= args.N) break;
+          uint32_t w[32];
+          if (args.c_f32) {
+            uint32_t r[32];
+            tmem_ld32(tm_row + (uint32_t)(u * 32), r);
+            tc_wait_ld();
+            float v[32];
+            epi_math(args, gm, n0 + u * 32, r, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
+          } else {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint32_t r[32];
+              tmem_ld32(tm_row + (uint32_t)(u * 64 + h * 32), r);
+              tc_wait_ld();
+              float v[32];
+              epi_math(args, gm, n0 + u * 64 + h * 32, r, v);
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
+                w[h * 16 + j] = *reinterpret_cast<uint32_t*>(&b2);
+              }
+            }
+          }
+          if (lane == 0) tma_store_wait_read<1>();
+          __syncwarp();
+          const uint32_t sb = stg + (uint32_t)ebuf * 4096u + (uint32_t)lane * 128u;
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sb + (uint32_t)((c ^ (lane & 7)) << 4)),
+                         "r"(w[4 * c]), "r"(w[4 * c + 1]), "r"(w[4 * c + 2]), "r"(w[4 * c + 3])
+                         : "memory");
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, stg + (uint32_t)ebuf * 4096u, n0 + u * cols, row0);
+            tma_store_commit();
+          }
+          ebuf ^= 1;
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < TN / 32; ++c) {
+          uint32_t r[32];
+          __syncwarp();
+          tmem_ld32(tm_row + (uint32_t)(c * 32), r);
+          tc_wait_ld();
+          const int gn0 = n0 + c * 32;
+          if (row_ok && gn0 < args.N) store_chunk(args, gm, gn0, r);
+          __syncwarp();
+        }
       }
       if (args.push) __threadfence_system();
       tc_fence_before();
       mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
     }
+    if (args.tma_store && lane == 0) tma_store_wait_all();
   }
 
   tc_fence_before();
@@ -559,7 +673,8 @@ bool get_map_2d(CUtensorMap* out, const void* ptr, uint64_t inner, uint64_t oute
   static std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  MapKey key{reinterpret_cast<uintptr_t>(ptr) ^ ((uintptr_t)dev << 56), inner, outer, ld_elems, box_inner, box_outer};
+  MapKey key{reinterpret_cast<uintptr_t>(ptr) ^ ((uintptr_t)dev << 56) ^ ((uintptr_t)dt << 48), inner, outer, ld_elems,
+             box_inner, box_outer};
   {
     std::lock_guard<std::mutex> g(mu);
     auto itr = cache.find(key);
@@ -580,6 +695,16 @@ bool get_map_2d(CUtensorMap* out, const void* ptr, uint64_t inner, uint64_t oute
   return true;
 }
 
+// Tensor map of the output C [M, N] (row stride ldc) as boxes of 32 rows x 128 B for the TMA-store
+// epilogue; false when that epilogue cannot be used (push modes, unaligned base or row stride).
+bool output_map(CUtensorMap* out, const GemmArgs& a) {
+  if (a.push) return false;
+  const int esz = a.c_f32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(a.C) & 15) || ((a.ldc * esz) % 16) || a.ldc < a.N) return false;
+  return get_map_2d(out, a.C, (uint64_t)a.N, (uint64_t)a.M, (uint64_t)a.ldc, (uint32_t)(128 / esz), 32,
+                    a.c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, esz);
+}
+
 template <int BN, int STAGES, int A_MN, int B_MN>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
   using S = Smem<BN, STAGES>;
@@ -597,7 +722,8 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, c
 }
 
 template <int A_MN, int B_MN>
-int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, cudaStream_t st) {
+int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
+               cudaStream_t st) {
   auto kern = gemm_tc2_kernel<A_MN, B_MN>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -607,7 +733,7 @@ int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, 
     attr_set[dev & 63] = true;
   }
   int pairs = std::min(a.num_tiles, brain_host::num_sms() / 2);
-  kern<<<2 * pairs, kThreads, PairSmem::TOTAL, st>>>(ta, tb, a);
+  kern<<<2 * pairs, kThreads, PairSmem::TOTAL, st>>>(ta, tb, tc, a);
   return (int)cudaGetLastError();
 }
 
@@ -714,10 +840,12 @@ BRAIN_API int brain_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
                      : get_map_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, 128,
                                   CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2));
     if (!ok) return (int)cudaErrorInvalidValue;
-    if (a_mn == 0 && b_mn == 0) return launch_tc2<0, 0>(ta, tb, a, stream);
-    if (a_mn == 0 && b_mn == 1) return launch_tc2<0, 1>(ta, tb, a, stream);
-    if (a_mn == 1 && b_mn == 0) return launch_tc2<1, 0>(ta, tb, a, stream);
-    return launch_tc2<1, 1>(ta, tb, a, stream);
+    CUtensorMap tc{};
+    a.tma_store = output_map(&tc, a) ? 1 : 0;
+    if (a_mn == 0 && b_mn == 0) return launch_tc2<0, 0>(ta, tb, tc, a, stream);
+    if (a_mn == 0 && b_mn == 1) return launch_tc2<0, 1>(ta, tb, tc, a, stream);
+    if (a_mn == 1 && b_mn == 0) return launch_tc2<1, 0>(ta, tb, tc, a, stream);
+    return launch_tc2<1, 1>(ta, tb, tc, a, stream);
   }
   const int BN = (N <= 128) ? 128 : 256;
   a.tiles_m = (M + BM - 1) / BM;
@@ -783,7 +911,9 @@ BRAIN_API int brain_gemm_bf16_tp(const void* A, int64_t lda, const void* B, int6
                      : get_map_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, 128,
                                   CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2));
     if (!ok) return (int)cudaErrorInvalidValue;
-    return b_mn ? launch_tc2<0, 1>(ta, tb, a, stream) : launch_tc2<0, 0>(ta, tb, a, stream);
+    CUtensorMap tc{};
+    a.tma_store = output_map(&tc, a) ? 1 : 0;
+    return b_mn ? launch_tc2<0, 1>(ta, tb, tc, a, stream) : launch_tc2<0, 0>(ta, tb, tc, a, stream);
   }
   const int BN = (N <= 128) ? 128 : 256;
   a.tiles_m = (M + BM - 1) / BM;

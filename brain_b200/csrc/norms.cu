@@ -42,7 +42,13 @@ __global__ void norm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx
   const int64_t row = blockIdx.x;
   const int nvec = D / 8;
   float v[VPT][8];
+  uint4 wraw[VPT];  // gamma, requested with the row so that its load overlaps the reduction
   float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) {
+    const int vi = threadIdx.x + i * blockDim.x;
+    if (vi < nvec) wraw[i] = __ldg(reinterpret_cast<const uint4*>(w + vi * 8));
+  }
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
@@ -52,10 +58,11 @@ __global__ void norm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx
         float r[8];
         load8(res + row * ldres + vi * 8, r);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[i][j] += r[j];
-        // the sum is rounded to bf16 before normalisation, exactly what a separate add would store
+        for (int j = 0; j < 8; ++j) {
+          // the sum is rounded to bf16 before normalisation, exactly what a separate add would store
+          v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j] + r[j]));
+        }
         store8(sum_out + row * ldsum + vi * 8, v[i]);
-        load8(sum_out + row * ldsum + vi * 8, v[i]);
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) s += LAYERNORM ? v[i][j] : v[i][j] * v[i][j];
@@ -89,7 +96,13 @@ __global__ void norm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx
     const int vi = threadIdx.x + i * blockDim.x;
     if (vi < nvec) {
       float wv[8], o[8];
-      load8(w + vi * 8, wv);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wraw[i]);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = __bfloat1622float2(w2[k]);
+        wv[2 * k] = f.x;
+        wv[2 * k + 1] = f.y;
+      }
       if (LAYERNORM && b) {
         float bv[8];
         load8(b + vi * 8, bv);

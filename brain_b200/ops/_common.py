@@ -81,6 +81,16 @@ def has_main_grad(p: torch.Tensor) -> bool:
     return getattr(p, "main_grad", None) is not None
 
 
+def main_grad_beta(p: torch.Tensor) -> float:
+    """Weight of the existing contents of ``p.main_grad`` for the next gradient written into it: 0.0
+    for the first write since the flat buffer's ``zero_grad`` (which marks parameters instead of
+    clearing memory, so the first producer overwrites), 1.0 afterwards (accumulate)."""
+    if getattr(p, "_main_grad_fresh", False):
+        p._main_grad_fresh = False
+        return 0.0
+    return 1.0
+
+
 def rows2d(x: torch.Tensor) -> torch.Tensor:
     """View x as [rows, last] with unit last-dim stride (copying only if needed)."""
     x2 = x.reshape(-1, x.shape[-1])

@@ -14,7 +14,7 @@ from __future__ import annotations
 import torch
 
 from .. import _native
-from ._common import has_main_grad, ptr, rows2d, stream
+from ._common import has_main_grad, main_grad_beta, ptr, rows2d, stream
 from .gemm import gemm
 
 
@@ -105,7 +105,7 @@ class _LinearCEFn(torch.autograd.Function):
         alpha = float(g)  # scalar loss: fold the upstream gradient into the GEMM alpha
         dh = gemm(dlogits, w, alpha=alpha)
         if has_main_grad(w):
-            gemm(dlogits, h2, trans_a=True, out=w.main_grad, beta=1.0, alpha=alpha)
+            gemm(dlogits, h2, trans_a=True, out=w.main_grad, beta=main_grad_beta(w), alpha=alpha)
             dw = None
         else:
             dw = gemm(dlogits, h2, trans_a=True, out_dtype=torch.float32, alpha=alpha).to(w.dtype)

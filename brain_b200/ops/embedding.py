@@ -10,7 +10,7 @@ from __future__ import annotations
 import torch
 
 from .. import _native
-from ._common import has_main_grad, ptr, stream
+from ._common import has_main_grad, main_grad_beta, ptr, stream
 
 
 class _EmbeddingFn(torch.autograd.Function):
@@ -42,6 +42,8 @@ class _EmbeddingFn(torch.autograd.Function):
         sorted_ids, perm = torch.sort(ids1)
         if has_main_grad(w):
             dw, ret = w.main_grad, None
+            if main_grad_beta(w) == 0.0:  # sparse rows are accumulated: clear the first time
+                dw.zero_()
         else:
             dw = torch.zeros(V, D, device=w.device, dtype=torch.float32)
             ret = dw
@@ -51,6 +53,8 @@ class _EmbeddingFn(torch.autograd.Function):
         if pos is not None:
             if has_main_grad(pos):
                 dp = pos.main_grad
+                if main_grad_beta(pos) == 0.0:
+                    dp.zero_()
             else:
                 dp = torch.zeros(pos.shape, device=pos.device, dtype=torch.float32)
                 dpos = dp

@@ -18,14 +18,14 @@ import torch
 
 from .activations import swiglu_bwd_only, swiglu_fwd_only
 from .gemm import gemm
-from ._common import has_main_grad, rows2d
+from ._common import has_main_grad, main_grad_beta, rows2d
 from . import norms as _norms
 
 
 def _wgrad(dy2, x2, w):
     """Weight gradient dy^T x: into w.main_grad (returns None) or as a new tensor."""
     if has_main_grad(w):
-        gemm(dy2, x2, trans_a=True, out=w.main_grad, beta=1.0)
+        gemm(dy2, x2, trans_a=True, out=w.main_grad, beta=main_grad_beta(w))
         return None
     return gemm(dy2, x2, trans_a=True, out_dtype=torch.float32).to(w.dtype)
 
@@ -35,7 +35,10 @@ def _bgrad(dy2, b):
         return None
     g = dy2.float().sum(0)
     if has_main_grad(b):
-        b.main_grad.add_(g.to(b.main_grad.dtype))
+        if main_grad_beta(b) == 0.0:
+            b.main_grad.copy_(g.to(b.main_grad.dtype))
+        else:
+            b.main_grad.add_(g.to(b.main_grad.dtype))
         return None
     return g.to(b.dtype)
 

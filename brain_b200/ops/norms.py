@@ -13,7 +13,7 @@ from __future__ import annotations
 import torch
 
 from .. import _native
-from ._common import has_main_grad, ptr, rows2d, stream
+from ._common import has_main_grad, main_grad_beta, ptr, rows2d, stream
 
 _RMS, _LN = 0, 1
 
@@ -42,7 +42,12 @@ def _bwd(kind, dy2, x2, w, b, mean, rstd, dres2=None):
         dw = w.main_grad
         db = b.main_grad if (b is not None and has_main_grad(b)) else None
         dw_f32 = int(dw.dtype == torch.float32)
-        acc = 1
+        bw = main_grad_beta(w)
+        bb = main_grad_beta(b) if db is not None else bw
+        if bw != bb:  # one accumulate flag covers both: clear the fresh one and accumulate into both
+            (dw if bw == 0.0 else db).zero_()
+            bw = 1.0
+        acc = int(bw != 0.0)
     else:
         dw = torch.empty(D, device=x2.device, dtype=torch.float32)
         db = torch.empty(D, device=x2.device, dtype=torch.float32) if b is not None else None

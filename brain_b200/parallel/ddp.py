@@ -82,6 +82,7 @@ class DataParallel:
 
     def sync_gradients(self) -> None:
         """All-reduce gradients as the mean over ranks (flat bucket, in place)."""
+        self.flat.absorb_grads()
         if self.world_size > 1:
             self.comm.all_reduce(self.flat.grad_buf)
             self.flat.grad_buf.mul_(1.0 / self.world_size)

@@ -52,18 +52,39 @@ class FlatParams:
         return buf[r * self.shard_size:(r + 1) * self.shard_size]
 
     def zero_grad(self) -> None:
-        self.grad_buf.zero_()
+        """Restart every gradient from zero without clearing memory: each parameter is marked fresh,
+        its first gradient producer overwrites its ``main_grad`` (``ops._common.main_grad_beta``), and
+        ``finalize_grads`` zeroes the parameters no producer wrote."""
         for p in self.params:
             p.grad = None
+            p._main_grad_fresh = True
+
+    def params_in(self, lo: int, hi: int) -> list:
+        """Parameters overlapping flat range [lo, hi)."""
+        return [p for p, o in zip(self.params, self.offsets) if o < hi and o + p.numel() > lo]
+
+    @torch.no_grad()
+    def finalize_grads(self, params=None) -> None:
+        """Zero the gradients still marked fresh (no producer wrote them since ``zero_grad``) among
+        ``params`` (default: all)."""
+        for p in (self.params if params is None else params):
+            if getattr(p, "_main_grad_fresh", False):
+                p.main_grad.zero_()
+                p._main_grad_fresh = False
 
     @torch.no_grad()
     def absorb_grads(self) -> None:
         """Fold gradients that reached ``param.grad`` (ops without a main_grad path, CPU
-        reference ops, user code) into the flat buffer."""
+        reference ops, user code) into the flat buffer, then zero what nothing wrote."""
         for p in self.params:
             if p.grad is not None:
-                p.main_grad.add_(p.grad.to(p.main_grad.dtype))
+                if getattr(p, "_main_grad_fresh", False):
+                    p.main_grad.copy_(p.grad.to(p.main_grad.dtype))
+                    p._main_grad_fresh = False
+                else:
+                    p.main_grad.add_(p.grad.to(p.main_grad.dtype))
                 p.grad = None
+        self.finalize_grads()
 
     def param_ranges(self, lo: int, hi: int):
         """(param, start, end) pieces of parameters overlapping flat range [lo, hi)."""

@@ -110,6 +110,7 @@ class OverlappedStep:
         if mode == "ce":
             most = max(n for _, n, _ in self.pieces)
             self.staging = torch.empty(self.world, max(most, 8), device=flat.grad_buf.device, dtype=flat.grad_buf.dtype)
+        self.bucket_params = [flat.params_in(lo, hi) for lo, hi, _ in self.buckets]
         self.side = torch.cuda.Stream()
         self.fired = [False] * len(self.buckets)
         self.hooks = []
@@ -132,6 +133,7 @@ class OverlappedStep:
         if self.args is None or self.fired[i]:
             return
         self.fired[i] = True
+        self.flat.finalize_grads(self.bucket_params[i])  # parameters of the bucket no producer wrote
         ev = torch.cuda.Event()
         ev.record()
         a, n, s = self.pieces[i]

@@ -63,6 +63,24 @@ def test_gemm_epilogue_bias_residual_accumulate():
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("extra_cols", [0, 24, 3])  # 3: row stride not a multiple of 16 B (row-store epilogue)
+def test_gemm_bf16_out_view_accumulate(extra_cols):
+    """bf16 output into a column slice of a wider buffer, overwrite then accumulate, ragged tiles."""
+    M, N, K = 300, 520, 136
+    a = _mk((M, K), "cuda", 21)
+    w = _mk((N, K), "cuda", 22)
+    big = torch.full((M, N + extra_cols), 7.0, device="cuda", dtype=torch.bfloat16)
+    out = big[:, :N]
+    gemm(a, w, trans_b=True, out=out, beta=0.0)
+    ref = _ref(a, w, False, True)
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=5e-2)
+    gemm(a, w, trans_b=True, out=out, beta=1.0)
+    torch.testing.assert_close(out.float(), 2 * ref, rtol=2e-2, atol=1e-1)
+    if extra_cols:
+        assert torch.all(big[:, N:] == 7.0)  # columns past N untouched
+
+
+@pytest.mark.gpu
 def test_gemm_simt_fallback_matches():
     M, N, K = 100, 70, 48
     a = _mk((M, K), "cuda", 7)

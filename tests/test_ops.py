@@ -119,8 +119,9 @@ def test_swiglu_and_gelu():
 
 # ------------------------------------------------------------------ rope
 @gpu
-def test_rope_inplace_strided_and_inverse():
-    B, S, Hq, Hkv, D = 2, 19, 4, 2, 64
+@pytest.mark.parametrize("D", [64, 128, 40])  # 40: rows not a multiple of 16 elements (scalar kernel)
+def test_rope_inplace_strided_and_inverse(D):
+    B, S, Hq, Hkv = 2, 19, 4, 2
     qkv = rnd(B, S, (Hq + 2 * Hkv) * D, seed=15)
     t = ops.rope_table(D, 64, 500000.0, device="cuda")
     q, k, v = attn.split_qkv(qkv.clone(), Hq, Hkv)
