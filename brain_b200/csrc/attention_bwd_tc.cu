@@ -8,9 +8,11 @@
 //   DQ:   a CTA owns 128 queries of one q head and streams 64-key blocks:
 //                      S = Q K^T, dP = dO V^T,  P = exp2(S * c - lse[row]),  dS = P (dP - delta[row])
 //                      dQ += dS K
-// Roles per CTA (6 warps): warp 0 TMA (4-D tensor maps over the caller's strides, SWIZZLE_128B,
-// CTA-local destinations), warp 1 single-thread MMA issuer, warps 2..5 elementwise (thread = TMEM lane = row),
-// which write P/dS as bf16 K-major tiles that the accumulate MMAs read from shared memory; the
+// Roles per CTA (10 warps): warp 0 TMA (4-D tensor maps over the caller's strides, SWIZZLE_128B,
+// CTA-local destinations), warp 1 single-thread MMA issuer, warps 2..9 elementwise: two warps per TMEM
+// lane quadrant (thread = row), each taking 32 of a block's 64 columns, so two warps per scheduler hide
+// each other's TMEM-load and exponential latency. They write P/dS as bf16 K-major tiles that the
+// accumulate MMAs read from shared memory; the
 // streamed operand is read a second time as an MN-major B operand, so nothing is transposed.
 // Bounded waits report through the status word. Reference: the Value-graph attention VJPs
 // (crates/brain-autograd/src/grad_fns/mod.rs:327-420); mask/scale conventions as in attention_tc.cu.
@@ -21,7 +23,8 @@ using namespace brain;
 namespace {
 
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kEwThreads = 256;  // elementwise threads (warps 2..9)
 constexpr int SUB128 = 128 * 128;  // 128 rows x 64 bf16 (16 KB)
 constexpr int SUB64 = 64 * 128;    // 64 rows x 64 bf16 (8 KB)
 
@@ -40,7 +43,7 @@ struct BwdArgs {
 template <int D, int MODE>
 struct BwdLayout {
   static constexpr int NSUB = D / 64;
-  static constexpr int STAGES = D == 64 ? 4 : 2;
+  static constexpr int STAGES = D == 64 ? 4 : 3;
   static constexpr int A_BYTES = NSUB * SUB128;  // one row operand [128, D]
   static constexpr int B_BYTES = NSUB * SUB64;   // one streamed operand [64, D]
   static constexpr int A_OFF = 0;                // A1, A2
@@ -122,9 +125,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(sd_full(i), 1);
-      mbar_init(sd_free(i), 128);
+      mbar_init(sd_free(i), kEwThreads);
     }
-    mbar_init(c_full, 128);
+    mbar_init(c_full, kEwThreads);
     mbar_init(c_free, 1);
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
@@ -247,8 +250,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- elementwise warps (2..5)
+    // ---------------- elementwise warps (2..9): quadrant q of the TMEM lanes, column half hc
     const int q = warp & 3;
+    const int hc = (warp - 2) >> 2;
+    const int et = (warp - 2) * 32 + lane;  // 0..255
     const int r = q * 32 + lane;
     const int row = r0 + r;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
@@ -259,6 +264,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       row_delta = a.delta[idx];
     }
     const bool row_valid_q = MODE == DQ ? (row < a.Sq) : true;
+    // DKDV: the 64 query statistics (lse * log2e, delta) of block i, one per thread et < 128, loaded
+    // one iteration ahead so that their L2 latency hides behind the previous block's work
+    auto stat = [&](int i) -> float {
+      if (MODE != DKDV || et >= 128 || i >= niter) return 0.f;
+      const int hc_ = hrow * group + i / nblk;
+      const int qi = (first_blk + i % nblk) * 64 + (et & 63);
+      if (qi >= a.Sq) return 0.f;
+      const int64_t base = ((int64_t)b * a.Hq + hc_) * a.Sq + qi;
+      return et < 64 ? __ldg(a.lse + base) * kLog2e : __ldg(a.delta + base);
+    };
+    float v_next = stat(0);
     bool ok = true;
     for (int i = 0; i < niter; ++i) {
       int col0, hcol;
@@ -269,19 +285,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         hcol = hrow;
         col0 = i * 64;
       }
+      (void)hcol;
       float* sld = reinterpret_cast<float*>(smem + L::LD_OFF) + (i & 1) * 128;
       if (MODE == DKDV) {
-        // the block's 64 query statistics, loaded once by the 128 elementwise threads (instead of every
-        // thread loading all 64 from global memory) and read back as shared-memory broadcasts. The
-        // barrier also makes the give-up decision uniform: every thread reaches it after bounded waits
-        // and all of them leave the loop together when any wait gave up.
-        const float* lrow = a.lse + ((int64_t)b * a.Hq + hcol) * a.Sq;
-        const float* drow = a.delta + ((int64_t)b * a.Hq + hcol) * a.Sq;
-        const int qi = col0 + (r & 63);
-        const float v = qi < a.Sq ? (r < 64 ? __ldg(lrow + qi) * kLog2e : __ldg(drow + qi)) : 0.f;
+        // the block's statistics go through shared memory (read back as broadcasts) instead of every
+        // thread loading all 64. The barrier also makes the give-up decision uniform: every thread
+        // reaches it after bounded waits and all of them leave the loop together when any wait gave up.
+        const float v = v_next;
+        v_next = stat(i + 1);
         if (ok) ok = mbar_wait(sd_full(i & 1), (i / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag);
-        sld[r] = v;
-        if (!bar_sync_and(1, 128, ok)) {
+        if (et < 128) sld[et] = v;
+        if (!bar_sync_and(1, kEwThreads, ok)) {
           ok = false;
           break;
         }
@@ -290,27 +304,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      float s[64], dp[64];
-      const uint32_t tb = tmem + (uint32_t)((i & 1) * 128) + lane_addr;
+      float s[32], dp[32];
+      const uint32_t tb = tmem + (uint32_t)((i & 1) * 128 + hc * 32) + lane_addr;
       tmem_ld32(tb, reinterpret_cast<uint32_t*>(s));
-      tmem_ld32(tb + 32, reinterpret_cast<uint32_t*>(s + 32));
       tmem_ld32(tb + 64, reinterpret_cast<uint32_t*>(dp));
-      tmem_ld32(tb + 96, reinterpret_cast<uint32_t*>(dp + 32));
       tc_wait_ld();
       tc_fence_before();
       mbar_arrive(sd_free(i & 1));
-      uint32_t pk[32], dk[32];
+      const int cb = hc * 32;  // this thread's first column of the block
+      uint32_t pk[16], dk[16];
       if (MODE == DKDV) {
         const int key = row;
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
+        for (int c = 0; c < 32; c += 2) {
           float pv[2], dv[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int qi = col0 + c + e;
+            const int qi = col0 + cb + c + e;
             const bool valid = qi < a.Sq && !(a.causal && key > qi + off);
-            const float l2 = valid ? sld[c + e] : 0.f;
-            const float de = valid ? sld[64 + c + e] : 0.f;
+            const float l2 = valid ? sld[cb + c + e] : 0.f;
+            const float de = valid ? sld[64 + cb + c + e] : 0.f;
             const float p = valid ? ex2_fast(s[c + e] * a.scale_log2 - l2) : 0.f;
             pv[e] = p;
             dv[e] = p * (dp[c + e] - de);
@@ -322,11 +335,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
 #pragma unroll
-        for (int c = 0; c < 64; c += 2) {
+        for (int c = 0; c < 32; c += 2) {
           float dv[2];
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
-            const int key = col0 + c + e;
+            const int key = col0 + cb + c + e;
             const bool valid = row_valid_q && key < a.Sk && !(a.causal && key > row + off);
             const float p = valid ? ex2_fast(s[c + e] * a.scale_log2 - row_lse2) : 0.f;
             dv[e] = p * (dp[c + e] - row_delta);
@@ -342,18 +355,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {  // 8 chunks of 8 columns = 128 B per row
+      for (int cc = 0; cc < 4; ++cc) {  // this thread's 4 chunks of 8 columns (of 8 per 128 B row)
+        const int c = hc * 4 + cc;
         const uint32_t o = r * 128 + ((c ^ (r % 8)) * 16);
         if (MODE == DKDV) {
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sC + o), "r"(pk[4 * c]), "r"(pk[4 * c + 1]),
-                       "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sC + o), "r"(pk[4 * cc]),
+                       "r"(pk[4 * cc + 1]), "r"(pk[4 * cc + 2]), "r"(pk[4 * cc + 3])
                        : "memory");
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sC + SUB128 + o), "r"(dk[4 * c]),
-                       "r"(dk[4 * c + 1]), "r"(dk[4 * c + 2]), "r"(dk[4 * c + 3])
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sC + SUB128 + o), "r"(dk[4 * cc]),
+                       "r"(dk[4 * cc + 1]), "r"(dk[4 * cc + 2]), "r"(dk[4 * cc + 3])
                        : "memory");
         } else {
-          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sC + o), "r"(dk[4 * c]), "r"(dk[4 * c + 1]),
-                       "r"(dk[4 * c + 2]), "r"(dk[4 * c + 3])
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sC + o), "r"(dk[4 * cc]),
+                       "r"(dk[4 * cc + 1]), "r"(dk[4 * cc + 2]), "r"(dk[4 * cc + 3])
                        : "memory");
         }
       }
@@ -379,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mul = a.scale;
       }
 #pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {  // this warp's half of the D columns
         uint32_t ov[32];
         if (have) {
           tmem_ld32(tmem + 256 + (uint32_t)(which * D + c * 32) + lane_addr, ov);

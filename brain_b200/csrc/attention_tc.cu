@@ -1,16 +1,19 @@
 // Flash-attention forward on the 5th-generation tensor cores (tcgen05 + TMEM), sm_100a.
 //
 // One CTA computes 128 query rows of one (batch, q-head) against all visible keys, 128 keys per
-// step. Roles (6 warps):
-//   warp 0      TMA producer: Q once, then K/V blocks (4-D tensor maps over [B, S, H, D] with the
-//               caller's strides, SWIZZLE_128B, CTA-local) into a 2-4 stage ring.
+// step. Roles (10 warps):
+//   warp 0      TMA producer: Q once, then K and V blocks (4-D tensor maps over [B, S, H, D] with the
+//               caller's strides, SWIZZLE_128B, CTA-local) into a 2-4 stage ring whose K and V halves
+//               are released separately: K_j right after S_j, V_j after PV_j, so the K of the next
+//               block (needed one block early, for S_{j+1}) is not held up by PV_j.
 //   warp 1      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM S buffers (128 cols
 //               each, f32), then O += P_j V_j into the TMEM O accumulator once softmax has written
 //               P_j; V is consumed as an MN-major operand straight from its [keys, D] tile.
-//   warps 2..5  softmax: thread = query row (TMEM lane). tcgen05.ld of S, causal/length mask,
-//               online max with lazy rescaling (O is only rescaled when the running max grows by
-//               more than 2^8), exp2, P packed to bf16 into a SWIZZLE_128B K-major smem tile, and
-//               the final O / l epilogue with the log-sum-exp.
+//   warps 2..9  softmax: two warps per TMEM lane quadrant, thread = (query row, half of the 128 keys);
+//               the pair exchanges its partial row maxima through shared memory once per block.
+//               tcgen05.ld of S, causal/length mask, online max with lazy rescaling (O is only
+//               rescaled when the running max grows by more than 2^8), exp2, P packed to bf16 into a
+//               SWIZZLE_128B K-major smem tile, and the final O / l epilogue with the log-sum-exp.
 // S_{j+1} is computed while softmax works on S_j, and PV_j runs while softmax computes the
 // exponentials of S_{j+1}. All waits are bounded (globaltimer) and report through the status word.
 //
@@ -25,7 +28,8 @@ namespace {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P values stay <= 256 between rescales
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kSmThreads = 256;  // softmax threads (warps 2..9)
 constexpr int SUB = 128 * 64 * 2;  // one SW128 sub-tile: 128 rows x 64 bf16
 
 struct FwdArgs {
@@ -46,9 +50,10 @@ struct FwdLayout {
   static constexpr int KV_OFF = P_OFF + 2 * SUB;
   static constexpr int K_BYTES = NSUB * SUB;
   static constexpr int STAGE_BYTES = 2 * K_BYTES;
-  static constexpr int BAR_OFF = KV_OFF + STAGES * STAGE_BYTES;
-  // q_full, kv_full[S], kv_empty[S], s_full[2], s_free[2], p_full, o_done, drain
-  static constexpr int NBAR = 1 + 2 * STAGES + 4 + 3;
+  static constexpr int X_OFF = KV_OFF + STAGES * STAGE_BYTES;  // [2 parities][2 halves][128] partial maxima
+  static constexpr int BAR_OFF = X_OFF + 2 * 2 * 128 * 4;
+  // q_full, k_full[S], k_empty[S], v_full[S], v_empty[S], s_full[2], s_free[2], p_full, o_done, drain
+  static constexpr int NBAR = 1 + 4 * STAGES + 4 + 3;
   static constexpr int TOTAL = BAR_OFF + NBAR * 8 + 16 + 1024;
 };
 
@@ -64,13 +69,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sQ = sbase + L::Q_OFF, sP = sbase + L::P_OFF, sKV = sbase + L::KV_OFF;
   const uint32_t bars = sbase + L::BAR_OFF;
   const uint32_t q_full = bars;
-  auto kv_full = [&](int s) { return bars + 8u * (1 + s); };
-  auto kv_empty = [&](int s) { return bars + 8u * (1 + ST + s); };
-  auto s_full = [&](int b) { return bars + 8u * (1 + 2 * ST + b); };
-  auto s_free = [&](int b) { return bars + 8u * (3 + 2 * ST + b); };
-  const uint32_t p_full = bars + 8u * (5 + 2 * ST);
-  const uint32_t o_done = bars + 8u * (6 + 2 * ST);
-  const uint32_t drain = bars + 8u * (7 + 2 * ST);
+  auto k_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto k_empty = [&](int s) { return bars + 8u * (1 + ST + s); };
+  auto v_full = [&](int s) { return bars + 8u * (1 + 2 * ST + s); };
+  auto v_empty = [&](int s) { return bars + 8u * (1 + 3 * ST + s); };
+  auto s_full = [&](int b) { return bars + 8u * (1 + 4 * ST + b); };
+  auto s_free = [&](int b) { return bars + 8u * (3 + 4 * ST + b); };
+  const uint32_t p_full = bars + 8u * (5 + 4 * ST);
+  const uint32_t o_done = bars + 8u * (6 + 4 * ST);
+  const uint32_t drain = bars + 8u * (7 + 4 * ST);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -89,14 +96,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < ST; ++s) {
-      mbar_init(kv_full(s), 1);
-      mbar_init(kv_empty(s), 1);
+      mbar_init(k_full(s), 1);
+      mbar_init(k_empty(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(v_empty(s), 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(s_full(i), 1);
-      mbar_init(s_free(i), 128);
+      mbar_init(s_free(i), kSmThreads);
     }
-    mbar_init(p_full, 128);
+    mbar_init(p_full, kSmThreads);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -119,21 +128,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------- TMA producer
       mbar_arrive_expect_tx(q_full, L::NSUB * SUB);
       for (int c = 0; c < L::NSUB; ++c) tma_load_4d(&tmQ, sQ + c * SUB, q_full, c * 64, m0, h, b);
-      int j = 0;
-      for (; j < nkb; ++j) {
-        const int s = j % ST;
-        if (!mbar_wait(kv_empty(s), ((j / ST) & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 110, abort_flag)) break;
-        const uint32_t kb = sKV + s * L::STAGE_BYTES;
-        mbar_arrive_expect_tx(kv_full(s), L::STAGE_BYTES);
-        for (int c = 0; c < L::NSUB; ++c) {
-          tma_load_4d(&tmK, kb + c * SUB, kv_full(s), c * 64, j * 128, hk, b);
-          tma_load_4d(&tmV, kb + L::K_BYTES + c * SUB, kv_full(s), c * 64, j * 128, hk, b);
+      // K_j, then V_{j-1}: the K ring runs one block ahead of the V ring
+      int nk = 0, nv = 0;  // blocks issued
+      bool ok = true;
+      for (int j = 0; ok && j <= nkb; ++j) {
+        if (j < nkb) {
+          const int s = j % ST;
+          if (!mbar_wait(k_empty(s), ((j / ST) & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 110, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t kb = sKV + s * L::STAGE_BYTES;
+          mbar_arrive_expect_tx(k_full(s), L::K_BYTES);
+          for (int c = 0; c < L::NSUB; ++c) tma_load_4d(&tmK, kb + c * SUB, k_full(s), c * 64, j * 128, hk, b);
+          ++nk;
+        }
+        if (j > 0) {
+          const int jv = j - 1, s = jv % ST;
+          if (!mbar_wait(v_empty(s), ((jv / ST) & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 111, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t vb = sKV + s * L::STAGE_BYTES + L::K_BYTES;
+          mbar_arrive_expect_tx(v_full(s), L::K_BYTES);
+          for (int c = 0; c < L::NSUB; ++c) tma_load_4d(&tmV, vb + c * SUB, v_full(s), c * 64, jv * 128, hk, b);
+          ++nv;
         }
       }
-      if (j < nkb) {  // aborted: let issued copies land
-        for (int i = max(0, j - ST); i < j; ++i) {
+      if (!ok) {  // aborted: let issued copies land
+        for (int i = max(0, nk - ST); i < nk; ++i) {
           uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(kv_full(i % ST), (i / ST) & 1) && globaltimer() - t0 < 100000000ull) {
+          while (!mbar_try_wait(k_full(i % ST), (i / ST) & 1) && globaltimer() - t0 < 100000000ull) {
+          }
+        }
+        for (int i = max(0, nv - ST); i < nv; ++i) {
+          uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(v_full(i % ST), (i / ST) & 1) && globaltimer() - t0 < 100000000ull) {
           }
         }
       }
@@ -155,8 +185,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                      kk > 0 ? 1u : 0u);
         }
         tc_commit(s_full(jj & 1));
+        tc_commit(k_empty(jj % ST));
       };
-      if (ok) ok = mbar_wait(kv_full(0), 0, BRAIN_ERR_TIMEOUT_FULL, 121, abort_flag);
+      if (ok) ok = mbar_wait(k_full(0), 0, BRAIN_ERR_TIMEOUT_FULL, 121, abort_flag);
       if (ok) {
         tc_fence_after();
         issue_s(0);
@@ -165,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; ok && j < nkb; ++j) {
         if (j + 1 < nkb) {
           const int jn = j + 1;
-          if (!mbar_wait(kv_full(jn % ST), (jn / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 122, abort_flag) ||
+          if (!mbar_wait(k_full(jn % ST), (jn / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 122, abort_flag) ||
               !mbar_wait(s_free(jn & 1), ((jn / 2) & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 123, abort_flag)) {
             ok = false;
             break;
@@ -173,7 +204,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_fence_after();
           issue_s(jn);
         }
-        if (!mbar_wait(p_full, j & 1, BRAIN_ERR_TIMEOUT_ACC, 124, abort_flag)) {
+        if (!mbar_wait(p_full, j & 1, BRAIN_ERR_TIMEOUT_ACC, 124, abort_flag) ||
+            !mbar_wait(v_full(j % ST), (j / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 125, abort_flag)) {
           ok = false;
           break;
         }
@@ -186,7 +218,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_mma_f16(tmem + 256, ad, bd, IDESC_O, (j > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(o_done);
-        tc_commit(kv_empty(j % ST));
+        tc_commit(v_empty(j % ST));
       }
       if (!ok && issued) {
         tc_commit(drain);
@@ -196,49 +228,60 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax warpgroup (warps 2..5)
+    // ---------------- softmax warps (2..9): quadrant q of the TMEM lanes, key half hc
     const int q = warp & 3;
+    const int hc = (warp - 2) >> 2;
     const int r = q * 32 + lane;  // row within the tile == TMEM lane
     const int qi = m0 + r;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     const int limit = a.causal ? min(qi + off, a.Sk - 1) : a.Sk - 1;
-    float m_used = -INFINITY, l = 0.f;
+    float* xmax = reinterpret_cast<float*>(smem + L::X_OFF);
+    float m_used = -INFINITY, l = 0.f;  // l: this thread's partial row sum (its 64 keys of every block)
     bool ok = true;
     for (int j = 0; j < nkb; ++j) {
-      if (!mbar_wait(s_full(j & 1), (j / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 130, abort_flag)) {
-        ok = false;
-        break;
-      }
+      if (ok && !mbar_wait(s_full(j & 1), (j / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 130, abort_flag)) ok = false;
       tc_fence_after();
-      float s[128];
+      float s[64];
+      if (ok) {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld32(tmem + (uint32_t)((j & 1) * 128 + c * 32) + lane_addr,
-                                            reinterpret_cast<uint32_t*>(s + c * 32));
-      tc_wait_ld();
+        for (int c = 0; c < 2; ++c) tmem_ld32(tmem + (uint32_t)((j & 1) * 128 + hc * 64 + c * 32) + lane_addr,
+                                              reinterpret_cast<uint32_t*>(s + c * 32));
+        tc_wait_ld();
+      } else {
+#pragma unroll
+        for (int k = 0; k < 64; ++k) s[k] = 0.f;
+      }
       tc_fence_before();
       mbar_arrive(s_free(j & 1));
-      const int n0 = j * 128;
-      const bool need_mask = (n0 + 127 > a.Sk - 1) || (a.causal && n0 + 127 > m0 + off);
-      // Row max and row sum use 8 independent partial accumulators: one warp per SMSP runs this loop,
-      // so a single dependency chain of 128 max / add operations would be pure latency.
+      const int n0 = j * 128 + hc * 64;  // this thread's first key
+      const bool need_mask = (n0 + 63 > a.Sk - 1) || (a.causal && n0 + 63 > m0 + off);
+      // Row max and row sum use 8 independent partial accumulators (no single long dependency chain).
       float mxp[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
       if (need_mask) {
 #pragma unroll
-        for (int k = 0; k < 128; ++k) {
+        for (int k = 0; k < 64; ++k) {
           s[k] = (n0 + k > limit) ? -INFINITY : s[k] * a.scale_log2;
           mxp[k & 7] = fmaxf(mxp[k & 7], s[k]);
         }
       } else {
 #pragma unroll
-        for (int k = 0; k < 128; ++k) {
+        for (int k = 0; k < 64; ++k) {
           s[k] *= a.scale_log2;
           mxp[k & 7] = fmaxf(mxp[k & 7], s[k]);
         }
       }
-      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      float* xm = xmax + (j & 1) * 256;
+      xm[hc * 128 + r] = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                               fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      // the pair's partial maxima; the barrier also makes a give-up uniform (every thread arrives after
+      // bounded waits, and all leave the loop together)
+      if (!bar_sync_and(1, kSmThreads, ok)) {
+        ok = false;
+        break;
+      }
+      const float mx = fmaxf(xm[r], xm[128 + r]);
       float alpha = 1.f;
       if (mx > m_used + kRescaleThreshold || (m_used == -INFINITY && mx > -INFINITY)) {
         alpha = exp2f(m_used - mx);  // 0 when m_used == -inf
@@ -248,9 +291,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       float sp[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) sp[u] = 0.f;
-      uint32_t pk[64];
+      uint32_t pk[32];
 #pragma unroll
-      for (int k = 0; k < 128; k += 2) {
+      for (int k = 0; k < 64; k += 2) {
         const float p0 = ex2_fast(s[k] - mu), p1 = ex2_fast(s[k + 1] - mu);
         sp[(k >> 1) & 7] += p0 + p1;
         __nv_bfloat162 hv = __floats2bfloat162_rn(p0, p1);
@@ -259,21 +302,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float sum = ((sp[0] + sp[1]) + (sp[2] + sp[3])) + ((sp[4] + sp[5]) + (sp[6] + sp[7]));
       l = l * alpha + sum;
       // P buffer and O are free once PV_{j-1} has completed
-      if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, BRAIN_ERR_TIMEOUT_ACC, 131, abort_flag)) {
-        ok = false;
-        break;
-      }
+      if (j > 0 && !mbar_wait(o_done, (j - 1) & 1, BRAIN_ERR_TIMEOUT_ACC, 131, abort_flag)) ok = false;
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 keys
-        const uint32_t addr = sP + (c / 8) * SUB + r * 128 + (((c % 8) ^ (r % 8)) * 16);
+      for (int c = 0; c < 8; ++c) {  // this thread's 8 chunks of 8 keys: sub-tile hc of P
+        const uint32_t addr = sP + hc * SUB + r * 128 + ((c ^ (r % 8)) * 16);
         asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(pk[4 * c]), "r"(pk[4 * c + 1]),
                      "r"(pk[4 * c + 2]), "r"(pk[4 * c + 3])
                      : "memory");
       }
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+      if (ok && j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {  // this warp's half of O's columns
           uint32_t ov[32];
           const uint32_t ta = tmem + 256 + (uint32_t)(c * 32) + lane_addr;
           tmem_ld32(ta, ov);
@@ -288,6 +328,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(p_full);
     }
+    // the pair's partial row sums (the maxima slots are free once every thread passed the last exchange)
+    bar_sync_and(1, kSmThreads, true);
+    xmax[hc * 128 + r] = l;
+    bar_sync_and(1, kSmThreads, true);
+    l += xmax[(1 - hc) * 128 + r];
     // epilogue
     float inv = 0.f;
     bool have = ok && nkb > 0;
@@ -296,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (l > 0.f) inv = 1.f / l;
     __nv_bfloat16* orow = a.o + (int64_t)b * a.ob + (int64_t)h * a.oh + (int64_t)qi * a.os;
 #pragma unroll 1
-    for (int c = 0; c < D / 32; ++c) {
+    for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {
       uint32_t ov[32];
       if (have) {
         tmem_ld32(tmem + 256 + (uint32_t)(c * 32) + lane_addr, ov);
@@ -313,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < 32; k += 8) store8(orow + c * 32 + k, v + k);
       }
     }
-    if (qi < a.Sq && a.lse)
+    if (hc == 0 && qi < a.Sq && a.lse)
       a.lse[((int64_t)b * a.Hq + h) * a.Sq + qi] = l > 0.f ? (m_used + log2f(l)) * kLn2 : -INFINITY;
   }
 
