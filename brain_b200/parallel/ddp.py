@@ -45,7 +45,8 @@ class DataParallel:
         self.loss_fn = loss_fn
         self.steps = 0
         self.overlapped = None
-        if overlap and ctx.world_size > 1 and getattr(self.comm, "name", "") == "nvlink":
+        if overlap and self.flat.grad_buf.is_cuda and (ctx.world_size == 1 or
+                                                         getattr(self.comm, "name", "") == "nvlink"):
             from .overlap import OverlappedStep
             self.overlapped = OverlappedStep(self, bucket_bytes=bucket_bytes, mode=overlap_mode)
 

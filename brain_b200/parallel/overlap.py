@@ -95,17 +95,27 @@ class OverlappedStep:
             b = min(bhi, a + piece)
             self.pieces.append((a, b - a, st))
             st += b - a
+        # the flat optimizer's own shard state is not used: release it before allocating this layout's
+        opt.master = opt.m = opt.v = None
+        if flat.grad_buf.is_cuda:
+            torch.cuda.empty_cache()
         with torch.no_grad():
-            self.master = torch.cat([flat.param_buf[a:a + n].float() for a, n, _ in self.pieces])
+            self.master = torch.empty(st, device=flat.param_buf.device, dtype=torch.float32)
+            for a, n, s in self.pieces:
+                self.master[s:s + n].copy_(flat.param_buf[a:a + n])
         self.m = torch.zeros_like(self.master)
         self.v = torch.zeros_like(self.master)
-        opt.master = opt.m = opt.v = None  # the flat optimizer's own shard state is not used
-        self.gbuf, goff = self.comm._buf_of(flat.grad_buf)
-        self.pbuf, poff = self.comm._buf_of(flat.param_buf)
-        if self.gbuf is None or self.pbuf is None:
-            raise ValueError("overlapped reduction needs symmetric gradient and parameter buffers")
-        self.gpeers = self.gbuf.peer_array(goff)
-        self.ppeers = self.pbuf.peer_array(poff)
+        if self.world == 1:
+            # a single GPU: the per-bucket step is AdamW alone, on this GPU's own buffers
+            self.gpeers = _i64([flat.grad_buf.data_ptr()])
+            self.ppeers = _i64([flat.param_buf.data_ptr()])
+        else:
+            self.gbuf, goff = self.comm._buf_of(flat.grad_buf)
+            self.pbuf, poff = self.comm._buf_of(flat.param_buf)
+            if self.gbuf is None or self.pbuf is None:
+                raise ValueError("overlapped reduction needs symmetric gradient and parameter buffers")
+            self.gpeers = self.gbuf.peer_array(goff)
+            self.ppeers = self.pbuf.peer_array(poff)
         self.gesz = flat.grad_buf.element_size()
         if mode == "ce":
             most = max(n for _, n, _ in self.pieces)
@@ -143,7 +153,8 @@ class OverlappedStep:
         state = (self.master.data_ptr() + 4 * s, self.m.data_ptr() + 4 * s, self.v.data_ptr() + 4 * s)
         with torch.cuda.stream(self.side):
             self.side.wait_event(ev)
-            self.comm.barrier(50)
+            if W > 1:
+                self.comm.barrier(50)
             if n == 0:
                 return
             if self.mode == "sm":
@@ -177,7 +188,8 @@ class OverlappedStep:
         for i in range(len(self.buckets)):
             self._launch(i)
         torch.cuda.current_stream().wait_stream(self.side)
-        self.comm.barrier(51)
+        if self.world > 1:
+            self.comm.barrier(51)
         self.args = None
 
     def close(self) -> None:

@@ -214,6 +214,32 @@ def test_overlapped_ddp_step_matches_fused_step(mode):
         assert abs(a - b) < 2e-2
 
 
+@pytest.mark.gpu
+def test_overlapped_adamw_single_gpu_matches_step_after_backward():
+    """One GPU: per-bucket AdamW on a side stream during backward == AdamW after backward."""
+    from brain_b200.models import LlamaLite, LlamaLiteConfig
+    from brain_b200.parallel import DataParallel, dist as bdist
+    bdist.init(timeout_s=60)
+    cfg = LlamaLiteConfig(vocab_size=512, hidden_dim=256, num_layers=3, num_heads=4, num_kv_heads=2, head_dim=64,
+                          intermediate_dim=512, max_seq_len=128)
+    out = []
+    for overlap in (True, False):
+        model = LlamaLite(cfg, device="cuda", dtype=torch.bfloat16, seed=0)
+        dp = DataParallel(model, lr=1e-3, grad_dtype=torch.bfloat16, comm="nvlink", overlap=overlap,
+                          bucket_bytes=64 << 10)
+        assert (dp.overlapped is not None) == overlap
+        g = torch.Generator(device="cuda").manual_seed(7)
+        losses = [float(dp.train_step(*(lambda t: (t[:, :-1], t[:, 1:]))(
+            torch.randint(0, 512, (2, 129), device="cuda", generator=g)))) for _ in range(3)]
+        out.append((dp.flat.param_buf.float().clone(), losses))
+        if dp.overlapped is not None:
+            dp.overlapped.close()
+    torch.testing.assert_close(out[0][0], out[1][0], rtol=0, atol=2e-2)
+    for a, b in zip(out[0][1], out[1][1]):
+        assert abs(a - b) < 2e-2
+    bdist.shutdown()
+
+
 def _gpu_timeout(rank, world):
     from brain_b200.parallel import dist as bdist
     from brain_b200.parallel.symm import NvlinkComm, PeerTimeout
