@@ -116,6 +116,8 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--new-tokens", type=int, default=256)
     ap.add_argument("--decode-layers", type=int, default=80, help="development only")
+    ap.add_argument("--l2-prefetch", action="store_true",
+                    help="decode step: prefetch the small GEMMs' weights into L2 ahead of them")
     ap.add_argument("--decode-pdl", type=int, default=2,
                     help="programmatic dependent launch in the decode step: 0 off, 1 successors launch at a "
                          "kernel's start, 2 after its main loop")
@@ -531,7 +533,8 @@ def run_decode(args, rank, world, dev) -> dict:
     t0 = time.time()
     shard_of = args.decode_shard_of or None
     set_pdl(args.decode_pdl)
-    srv = LlamaTPServe(cfg, max_batch=B, max_len=S + NEW, block_size=64, seed=0, shard_of=shard_of)
+    srv = LlamaTPServe(cfg, max_batch=B, max_len=S + NEW, block_size=64, seed=0, shard_of=shard_of,
+                       l2_prefetch=args.l2_prefetch)
     torch.cuda.synchronize()
     log(f"{bdist.rank_prefix()} 70B-shape TP={world} shard ready in {time.time() - t0:.1f}s, "
         f"mem {torch.cuda.memory_allocated() / 2**30:.1f} GiB")
@@ -604,7 +607,8 @@ def run_decode(args, rank, world, dev) -> dict:
         "config": {"model": "Llama-3-70B-shape" + ("" if cfg.num_layers == 80 else f" ({cfg.num_layers} layers: NOT the benchmark)"),
                    "batch": B, "prompt_len": S, "new_tokens": NEW,
                    "parallelism": f"tp{world}" if not shard_of else f"one rank's shard of tp{shard_of} (NOT the benchmark)",
-                   "kv_cache": "paged, block 64", "pdl_mode": args.decode_pdl, "decode_step": "one CUDA graph of hand-written kernels",
+                   "kv_cache": "paged, block 64", "pdl_mode": args.decode_pdl,
+                   "l2_prefetch": args.l2_prefetch, "decode_step": "one CUDA graph of hand-written kernels",
                    "l2": "no flush: each step streams the rank's weights (>> 126 MB L2)"},
         "prefill_ms": prefill_ms, "prefill_tok_s": B * S / (prefill_ms / 1e3),
         "hbm_bytes_per_step_per_gpu": hbm, "hbm_gbs_achieved": hbm / (ms / 1e3) / 1e9,

@@ -45,6 +45,8 @@ struct DecodeArgs {
   int64_t ob, oh;  // strides of out [B, Hq, D]
   unsigned long long* trace;  // optional [grid][8] per-CTA phase timestamps (globaltimer ns), else null
   int pdl_late;               // let dependents launch after the main loop instead of at the start
+  const void* pf;             // optional L2 prefetch after the main loop (the next kernel's weights)
+  int64_t pf_bytes;
 };
 
 constexpr int kMaxSplitsDec = 16;  // cluster size limit (non-portable above 8)
@@ -325,6 +327,8 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const __grid_con
   }
   __syncthreads();  // every warp is done with the stages
   if (a.pdl_late) pdl_trigger();
+  // this CTA's K/V stream is done: fill L2 with its share of the next kernel's weights meanwhile
+  if (tid == 0) l2_prefetch_part(a.pf, a.pf_bytes, blockIdx.y * gridDim.x + blockIdx.x, gridDim.x * gridDim.y);
   // peers may push into this CTA's stages once every CTA of the cluster has passed this point
   if (a.splits > 1) cluster_arrive_release();
   dec_trace(a, 5);
@@ -572,7 +576,8 @@ BRAIN_API int brain_decode_splits(int B, int Hkv, int D, int max_len) {
 BRAIN_API int brain_decode_attention(const void* q, int64_t qb, int64_t qh, const void* kpool, const void* vpool,
                                      int num_blocks, const int* table, int max_blocks, const int* seq_lens,
                                      int block_size, void* out, int64_t ob, int64_t oh, int B, int Hq, int Hkv, int D,
-                                     float scale, int splits, unsigned long long* trace, cudaStream_t st) {
+                                     float scale, int splits, unsigned long long* trace, const void* l2_prefetch,
+                                     int64_t l2_prefetch_bytes, cudaStream_t st) {
   if (Hkv <= 0 || Hq % Hkv || Hq / Hkv > kMaxG) return (int)cudaErrorInvalidValue;
   if (D != 64 && D != 128) return (int)cudaErrorInvalidValue;
   if (block_size <= 0 || block_size % kRowsBox) return (int)cudaErrorInvalidValue;
@@ -595,6 +600,8 @@ BRAIN_API int brain_decode_attention(const void* q, int64_t qb, int64_t qh, cons
   a.oh = oh;
   a.trace = trace;
   a.pdl_late = brain_host::g_decode_pdl == 2;
+  a.pf = (reinterpret_cast<uintptr_t>(l2_prefetch) & 15) ? nullptr : l2_prefetch;
+  a.pf_bytes = l2_prefetch_bytes;
   return D == 64 ? launch_decode<64>(tk, tv, a, st) : launch_decode<128>(tk, tv, a, st);
 }
 

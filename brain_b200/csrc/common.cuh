@@ -146,6 +146,22 @@ __device__ __forceinline__ bool bar_sync_and(int id, int nthreads, bool v) {
   return r != 0;
 }
 
+// Spread an L2 prefetch of [base, base + bytes) over `parts` callers: caller `part` requests its slice
+// with cp.async.bulk.prefetch.L2 (fire and forget; a later kernel's loads find the lines in L2).
+// base must be 16-byte aligned.
+__device__ __forceinline__ void l2_prefetch_part(const void* base, int64_t bytes, int part, int parts) {
+  if (base == nullptr || bytes <= 0) return;
+  const int64_t per = ((bytes + parts - 1) / parts + 15) & ~int64_t(15);
+  int64_t lo = (int64_t)part * per;
+  const int64_t hi = lo + per < bytes ? lo + per : bytes;
+  const char* p = reinterpret_cast<const char*>(base);
+  for (; lo < hi; lo += 32768) {
+    const int64_t n = hi - lo < 32768 ? hi - lo : 32768;
+    const uint32_t sz = (uint32_t)((n + 15) & ~int64_t(15));
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p + lo), "r"(sz) : "memory");
+  }
+}
+
 // 2-D tiled TMA store from this CTA's shared memory to global memory (bulk-group completion), and
 // the bulk-group commit / waits that order it: wait_read<N> returns once at most N committed groups
 // still read shared memory (their source buffers may be rewritten); wait_all once every group's

@@ -83,6 +83,8 @@ struct SkinnyArgs {
   // optional per-CTA phase timestamps (globaltimer ns), [cta][8]; null = off
   unsigned long long* trace;
   int pdl_late;  // let dependents launch after the main loop instead of at the start
+  const void* pf;  // optional L2 prefetch once the weights are consumed (the next kernels' weights)
+  int64_t pf_bytes;
 };
 
 __device__ __forceinline__ unsigned long long argmax_key(float v, int64_t idx) {
@@ -283,6 +285,7 @@ __global__ void __launch_bounds__(kThreads) skinny_gemm_kernel(const __grid_cons
   const bool ok = mbar_wait(done_bar, 0, BRAIN_ERR_TIMEOUT_ACC, 112, abort_flag);
   tc_fence_after();
   if (a.pdl_late) pdl_trigger();  // every weight tile consumed: the successor may take the SM slots
+  if (threadIdx.x == 0) l2_prefetch_part(a.pf, a.pf_bytes, tile * nsplit + split, gridDim.x * gridDim.y);
   if (trace) {
     trace[3] = globaltimer();
     trace[8] = clock64();
@@ -771,7 +774,7 @@ BRAIN_API int brain_skinny_splits(int M, int N, int K) {
 //   [0] world [1] rank [2] slot_elems [3] ctrl* [4] keys* [5] vocab_offset [6] hq [7] hkv [8] pos*
 //   [9] cos|sin table* [10] k pool* [11] v pool* [12] block table* [13] max_blocks [14] block_size
 //   [15] optional phase-timestamp buffer (uint64 [ctas][16]: globaltimer ns [0..7), SM clocks [8..16))
-//   [16..24) peer slot bases
+//   [16..24) peer slot bases  [24] optional L2-prefetch base (16-byte aligned)  [25] its size in bytes
 BRAIN_API int brain_skinny_gemm(const void* X, int64_t ldx, const void* W, int64_t ldw, int M, int N, int K, int epi,
                                 float alpha, void* out, int64_t ldc, const void* R, int64_t ldr, int splits,
                                 const int64_t* ext, cudaStream_t st) {
@@ -792,6 +795,10 @@ BRAIN_API int brain_skinny_gemm(const void* X, int64_t ldx, const void* W, int64
   a.ldr = ldr;
   if (ext) a.trace = reinterpret_cast<unsigned long long*>(ext[15]);
   a.pdl_late = brain_host::g_decode_pdl == 2;
+  if (ext && ext[24] && !(ext[24] & 15)) {
+    a.pf = reinterpret_cast<const void*>(ext[24]);
+    a.pf_bytes = ext[25];
+  }
   if (epi == EPI_PUSH || epi == EPI_ARGMAX || epi == EPI_QKV) {
     if (!ext) return (int)cudaErrorInvalidValue;
     a.world = (int)ext[0];

@@ -21,7 +21,7 @@ from ._common import same_device, stream
 
 _native.register({
     "brain_decode_splits": ("brain_kernels", "iiii"),
-    "brain_decode_attention": ("brain_kernels", "pllppipipiplliiiifips"),
+    "brain_decode_attention": ("brain_kernels", "pllppipipiplliiiifippls"),
     "brain_kv_append_rope": ("brain_kernels", "pliiiipppppiis"),
     "brain_status_attention_decode": ("brain_kernels", "pi"),
 })
@@ -33,10 +33,11 @@ def decode_splits(B: int, Hkv: int, D: int, max_len: int) -> int:
 
 
 def paged_decode_attention(q, k_pool, v_pool, block_table, seq_lens, scale=None, splits=None, max_len=None,
-                           out=None, trace=None):
+                           out=None, trace=None, l2_prefetch=None):
     """``trace``: optional int64 CUDA tensor of (B * Hkv * splits * 8) elements that receives per-CTA
     globaltimer stamps (start, length read, after the wait, Q loaded, first chunk, loop end, cluster
-    barrier, end) for profiling."""
+    barrier, end) for profiling. ``l2_prefetch``: optional CUDA tensor (contiguous) that the CTAs ask
+    L2 to load once their K/V stream is done, e.g. the weights of the kernel that follows."""
     B, Hq, D = q.shape
     Hkv = k_pool.shape[2]
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
@@ -54,7 +55,9 @@ def paged_decode_attention(q, k_pool, v_pool, block_table, seq_lens, scale=None,
                  v_pool.data_ptr(), k_pool.shape[0], block_table.data_ptr(), block_table.shape[1],
                  seq_lens.data_ptr(), k_pool.shape[1],
                  out.data_ptr(), out.stride(0), out.stride(1), B, Hq, Hkv, D, float(scale),
-                 int(splits), trace.data_ptr() if trace is not None else 0, stream(q))
+                 int(splits), trace.data_ptr() if trace is not None else 0,
+                 l2_prefetch.data_ptr() if l2_prefetch is not None else 0,
+                 l2_prefetch.numel() * l2_prefetch.element_size() if l2_prefetch is not None else 0, stream(q))
     return out
 
 
@@ -126,8 +129,10 @@ def skinny_splits(M: int, N: int, K: int) -> int:
 
 
 def decode_ext(world=1, rank=0, slot_elems=0, ctrl=None, keys=None, vocab_offset=0, hq=0, hkv=0, pos=None,
-               rope_cs=None, k_pool=None, v_pool=None, block_table=None, peer_slots=(), trace=None):
-    """The int64[32] side-argument block of ``brain_skinny_gemm`` (layout documented in the source)."""
+               rope_cs=None, k_pool=None, v_pool=None, block_table=None, peer_slots=(), trace=None, l2_prefetch=None):
+    """The int64[32] side-argument block of ``brain_skinny_gemm`` (layout documented in the source).
+    ``l2_prefetch``: optional contiguous CUDA tensor that the CTAs ask L2 to load once their weights
+    are consumed (the weights of a kernel that follows)."""
     import ctypes
 
     def p(t):
@@ -140,6 +145,8 @@ def decode_ext(world=1, rank=0, slot_elems=0, ctrl=None, keys=None, vocab_offset
         v[13], v[14] = block_table.shape[1], k_pool.shape[1]
     for i, s in enumerate(peer_slots):
         v[16 + i] = int(s)
+    if l2_prefetch is not None:
+        v[24], v[25] = l2_prefetch.data_ptr(), l2_prefetch.numel() * l2_prefetch.element_size()
     return (ctypes.c_int64 * 32)(*v)
 
 
