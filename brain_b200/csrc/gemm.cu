@@ -54,6 +54,11 @@ struct GemmArgs {
   // CTA-pair kernel: the output tile leaves through shared memory and TMA stores (tmC) instead of
   // per-thread row stores
   int tma_store;
+  // NeoX RoPE on the first rope_cols output columns (q and k heads of a fused QKV projection, head dim
+  // rope_hd in {64, 128}); row r is token (r % rope_S) + rope_off; rope_cs f32 [positions, rope_hd]
+  // (cos | sin halves). TMA-store epilogue only.
+  const float* rope_cs;
+  int rope_cols, rope_hd, rope_S, rope_off;
 };
 
 template <int BN, int STAGES>
@@ -578,9 +583,83 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // only after the store issued from it two units earlier has read it.
         const int cols = args.c_f32 ? 32 : 64;
         const int row0 = tm * 256 + (int)cta * 128 + q * 32;
+        const int rpos = args.rope_cs && row_ok ? gm % args.rope_S + args.rope_off : 0;
+        // RoPE: rotate 32 pairs (x1 at TMEM column c1, x2 at c2; pair index j0 in the head) into bf16 words
+        auto rope32 = [&](int c1, int c2, int j0, uint32_t* w1, uint32_t* w2) {
+          uint32_t r1[32], r2[32];
+          tmem_ld32(tm_row + (uint32_t)c1, r1);
+          tmem_ld32(tm_row + (uint32_t)c2, r2);
+          tc_wait_ld();
+          float v1[32], v2[32];
+          epi_math(args, gm, n0 + c1, r1, v1);
+          epi_math(args, gm, n0 + c2, r2, v2);
+          const float4* cp = reinterpret_cast<const float4*>(args.rope_cs + (int64_t)rpos * args.rope_hd + j0);
+          const float4* sp = reinterpret_cast<const float4*>(args.rope_cs + (int64_t)rpos * args.rope_hd +
+                                                             args.rope_hd / 2 + j0);
+#pragma unroll
+          for (int k4 = 0; k4 < 8; ++k4) {
+            const float4 c4 = __ldg(cp + k4), s4 = __ldg(sp + k4);
+            const float cv[4] = {c4.x, c4.y, c4.z, c4.w}, sv[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+            for (int e = 0; e < 4; e += 2) {
+              const int k = k4 * 4 + e;
+              const float a0 = v1[k] * cv[e] - v2[k] * sv[e], a1 = v1[k + 1] * cv[e + 1] - v2[k + 1] * sv[e + 1];
+              const float b0 = v2[k] * cv[e] + v1[k] * sv[e], b1 = v2[k + 1] * cv[e + 1] + v1[k + 1] * sv[e + 1];
+              __nv_bfloat162 ha = __floats2bfloat162_rn(a0, a1), hb = __floats2bfloat162_rn(b0, b1);
+              w1[k / 2] = *reinterpret_cast<uint32_t*>(&ha);
+              w2[k / 2] = *reinterpret_cast<uint32_t*>(&hb);
+            }
+          }
+        };
+        auto stage_chunks = [&](uint32_t buf, int c0, const uint32_t* w16) {  // 4 chunks of 16 B from chunk c0
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(buf + (uint32_t)lane * 128u +
+                                                                             (uint32_t)(((c0 + c) ^ (lane & 7)) << 4)),
+                         "r"(w16[4 * c]), "r"(w16[4 * c + 1]), "r"(w16[4 * c + 2]), "r"(w16[4 * c + 3])
+                         : "memory");
+        };
 #pragma unroll 1
         for (int u = 0; u < TN / cols; ++u) {
           if (n0 + u * cols >= args.N) break;
+          if (args.rope_cs && n0 + u * cols < args.rope_cols) {
+            // a rotated head: pairs (d, d + hd/2) meet in registers before the store
+            const uint32_t bufA = stg + (uint32_t)ebuf * 4096u, bufB = stg + (uint32_t)(ebuf ^ 1) * 4096u;
+            uint32_t w1[16], w2[16];
+            if (args.rope_hd == 128) {  // units u (first half) and u + 1 (second half) of one head
+              if (lane == 0) tma_store_wait_read<0>();
+              __syncwarp();
+#pragma unroll 1
+              for (int h2 = 0; h2 < 2; ++h2) {
+                rope32(u * 64 + h2 * 32, u * 64 + 64 + h2 * 32, h2 * 32, w1, w2);
+                stage_chunks(bufA, h2 * 4, w1);
+                stage_chunks(bufB, h2 * 4, w2);
+              }
+              fence_proxy_async();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmC, bufA, n0 + u * 64, row0);
+                tma_store_commit();
+                tma_store_2d(&tmC, bufB, n0 + (u + 1) * 64, row0);
+                tma_store_commit();
+              }
+              ++u;  // the head's second unit is done too; ebuf is unchanged (both buffers used once)
+            } else {  // head dim 64: one unit, halves of 32 columns
+              rope32(u * 64, u * 64 + 32, 0, w1, w2);
+              if (lane == 0) tma_store_wait_read<1>();
+              __syncwarp();
+              stage_chunks(bufA, 0, w1);
+              stage_chunks(bufA, 4, w2);
+              fence_proxy_async();
+              __syncwarp();
+              if (lane == 0) {
+                tma_store_2d(&tmC, bufA, n0 + u * 64, row0);
+                tma_store_commit();
+              }
+              ebuf ^= 1;
+            }
+            continue;
+          }
           uint32_t w[32];
           if (args.c_f32) {
             uint32_t r[32];
@@ -871,6 +950,40 @@ BRAIN_API int brain_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
     BRAIN_GEMM_CASE(256, 4)
   }
 #undef BRAIN_GEMM_CASE
+}
+
+// C [M, N] bf16 = A [M, K] B [N, K]^T with NeoX RoPE applied to the first rope_cols columns in the
+// epilogue (a fused QKV projection: q and k heads rotated, v heads stored as they are). Row r is token
+// (r % S) + pos_offset; cs f32 [positions, head_dim] (cos | sin halves). Returns cudaErrorNotSupported
+// when the CTA-pair TMA-store path cannot run (M or N < 256, N % 256, head_dim not 64/128, alignment);
+// the caller then applies the rotation separately.
+BRAIN_API int brain_gemm_bf16_rope(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                                   int M, int N, int K, const float* cs, int rope_cols, int head_dim, int S,
+                                   int pos_offset, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return 0;
+  if (!g_pair_mode || M < 256 || N < 256 || N % 256 || (head_dim != 64 && head_dim != 128) || rope_cols % 256 ||
+      S <= 0 || K < 16 || (lda % 8) || (ldb % 8) || (reinterpret_cast<uintptr_t>(cs) & 15) ||
+      ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15))
+    return (int)cudaErrorNotSupported;
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K;
+  a.C = C; a.ldc = ldc; a.c_f32 = 0; a.accumulate = 0;
+  a.alpha = 1.f; a.beta = 0.f;
+  a.tiles_m = (M + 255) / 256;
+  a.tiles_n = (N + 255) / 256;
+  a.num_tiles = a.tiles_m * a.tiles_n;
+  a.rope_cs = cs;
+  a.rope_cols = rope_cols;
+  a.rope_hd = head_dim;
+  a.rope_S = S;
+  a.rope_off = pos_offset;
+  CUtensorMap ta, tb, tc{};
+  if (!get_map_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, 128, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2) ||
+      !get_map_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, 128, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2) ||
+      !output_map(&tc, a))
+    return (int)cudaErrorNotSupported;
+  a.tma_store = 1;
+  return launch_tc2<0, 0>(ta, tb, tc, a, stream);
 }
 
 // Tensor-parallel GEMM with the communication in its epilogue, C = A B^T (A [M, K] K-major; B [N, K],

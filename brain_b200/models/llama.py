@@ -6,8 +6,8 @@ API parity with crates/brain-transformer/src/models/llama_lite.rs:24-187 (``Llam
 ``generate`` decodes incrementally from a KV cache instead of re-running the whole prefix.
 
 Each block is four fused ops:
-    qkv = norm_linear(h, attn_norm, Wqkv)                 RMSNorm recomputed in backward
-    h   = linear(qkv_attention(qkv, rope), Wo, +h)        in-place RoPE, flash attention, residual epilogue
+    qkv = norm_linear(h, attn_norm, Wqkv, rope)           RMSNorm recomputed in backward, RoPE in the GEMM epilogue
+    h   = linear(qkv_attention(qkv), Wo, +h)              flash attention, residual epilogue
     gu  = norm_linear(h, ffn_norm, Wgate_up)
     h   = swiglu_linear(gu, Wdown, +h)                    SwiGLU recomputed in backward
 and the LM head is a fused linear + cross-entropy.
@@ -39,10 +39,13 @@ class LlamaBlock(Module):
 
     def forward(self, h, rope, cache: KvCache | None = None, layer: int = 0, pos: int = 0):
         c = self.cfg
-        qkv = ops.norm_linear(h, self.attn_norm, self.wqkv, c.norm_eps)
         if cache is None:
-            o = ops.qkv_attention(qkv, c.num_heads, c.num_kv_heads, rope)
+            # RoPE on the q and k heads in the QKV GEMM's epilogue; attention gets them rotated
+            qkv = ops.norm_linear(h, self.attn_norm, self.wqkv, c.norm_eps,
+                                  rope=(rope, c.num_heads + c.num_kv_heads, c.head_dim, h.shape[-2], 0))
+            o = ops.qkv_attention(qkv, c.num_heads, c.num_kv_heads, None)
         else:
+            qkv = ops.norm_linear(h, self.attn_norm, self.wqkv, c.norm_eps)
             o = self._cached_attention(qkv, rope, cache, layer, pos)
         h = ops.linear(o, self.wo, residual=h)
         gu = ops.norm_linear(h, self.ffn_norm, self.w_gate_up, c.norm_eps)

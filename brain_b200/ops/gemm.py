@@ -84,6 +84,36 @@ def gemm(
     return out
 
 
+_NOT_SUPPORTED = 801  # cudaErrorNotSupported
+
+
+def gemm_rope(x: torch.Tensor, w: torch.Tensor, table: torch.Tensor, rope_cols: int, head_dim: int, seq_len: int,
+              offset: int = 0) -> torch.Tensor | None:
+    """y = x @ w.T (bf16) with NeoX RoPE applied in the GEMM epilogue to the first ``rope_cols`` output
+    columns (the q and k heads of a fused QKV projection, heads of ``head_dim``); row r of x is token
+    (r % seq_len) + offset; ``table`` is the f32 [positions, head_dim] cos | sin table of ``ops.rope``.
+    Returns None where the fused epilogue does not apply (small or unaligned shapes): the caller then
+    rotates separately."""
+    if not x.is_cuda or x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or table.dtype != torch.float32:
+        return None
+    x = _row_major(x)
+    w = _row_major(w)
+    if x.stride(1) != 1 or w.stride(1) != 1 or not table.is_contiguous():
+        return None
+    same_device(x, w, table)
+    M, K = x.shape
+    N = w.shape[0]
+    out = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+    rc = _native.fn("brain_gemm_bf16_rope")(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), out.data_ptr(),
+                                            out.stride(0), M, N, K, table.data_ptr(), int(rope_cols), int(head_dim),
+                                            int(seq_len), int(offset), _native.stream_ptr(x.device))
+    if rc == _NOT_SUPPORTED:
+        return None
+    if rc != 0:
+        raise _native.NativeError(f"brain_gemm_bf16_rope failed with status {rc}")
+    return out
+
+
 def set_pair_mode(mode: int) -> int:
     """1: use the CTA-pair (cta_group::2, 256x256 tile) kernel for M, N >= 256; 0: single-CTA
     kernel only. Returns the previous mode."""

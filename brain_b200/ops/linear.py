@@ -17,7 +17,8 @@ from __future__ import annotations
 import torch
 
 from .activations import swiglu_bwd_only, swiglu_fwd_only
-from .gemm import gemm
+from .gemm import gemm, gemm_rope
+from .rope import apply_rope_
 from ._common import has_main_grad, main_grad_beta, rows2d
 from . import norms as _norms
 
@@ -77,32 +78,59 @@ def linear(x, w, b=None, residual=None):
 
 class _NormLinearFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, nw, w, eps):
+    def forward(ctx, x, nw, w, eps, rope):
         x2 = rows2d(x)
         xn, _, _, rstd = _norms._fwd(_norms._RMS, x2, nw, None, eps)
-        y = gemm(xn, w, trans_b=True)
-        ctx.save_for_backward(x2, nw, w, rstd)
+        y = None
+        if rope is not None:  # (table, heads rotated, head_dim, seq_len, offset)
+            table, rot_heads, hd, S, off = rope
+            y = gemm_rope(xn, w, table, rot_heads * hd, hd, S, off)
+            if y is None:  # shapes outside the fused epilogue: rotate the q and k columns separately
+                y = gemm(xn, w, trans_b=True)
+                apply_rope_(y.view(-1, S, w.shape[0] // hd, hd)[:, :, :rot_heads], table, None, off)
+        else:
+            y = gemm(xn, w, trans_b=True)
+        ctx.save_for_backward(x2, nw, w, rstd, rope[0] if rope is not None else torch.empty(0))
+        ctx.rope = None if rope is None else rope[1:]
         ctx.eps = eps
         ctx.xshape = x.shape
         return y.view(*x.shape[:-1], w.shape[0])
 
     @staticmethod
     def backward(ctx, dy):
-        x2, nw, w, rstd = ctx.saved_tensors
+        x2, nw, w, rstd, table = ctx.saved_tensors
         dy2 = rows2d(dy)
+        if ctx.rope is not None:
+            # gradient w.r.t. the unrotated projection: the inverse rotation of its q and k columns
+            # (dy is this op's own gradient buffer, produced by the attention backward)
+            rot_heads, hd, S, off = ctx.rope
+            dy2 = dy2.contiguous() if dy2.stride(1) != 1 else dy2
+            apply_rope_(dy2.view(-1, S, w.shape[0] // hd, hd)[:, :, :rot_heads], table, None, off, inverse=True)
         xn, _, _, _ = _norms._fwd(_norms._RMS, x2, nw, None, ctx.eps)  # recompute
         dxn = gemm(dy2, w)
         dw = _wgrad(dy2, xn, w)
         del xn
         dx, dnw, _ = _norms._bwd(_norms._RMS, dxn, x2, nw, None, None, rstd)
-        return dx.view(ctx.xshape), dnw, dw, None
+        return dx.view(ctx.xshape), dnw, dw, None, None
 
 
-def norm_linear(x, norm_w, w, eps=1e-6):
-    """rms_norm(x, norm_w) @ w.T with the normalised activations recomputed in backward."""
+def norm_linear(x, norm_w, w, eps=1e-6, rope=None):
+    """rms_norm(x, norm_w) @ w.T with the normalised activations recomputed in backward.
+
+    ``rope = (table, rot_heads, head_dim, seq_len, offset)``: NeoX RoPE on the first ``rot_heads``
+    heads of the output (the q and k heads of a fused QKV projection [.., (Hq + 2 Hkv) * head_dim]),
+    applied in the GEMM epilogue where the shapes allow; the backward returns the gradient of the
+    unrotated projection."""
     if x.is_cuda:
-        return _NormLinearFn.apply(x, norm_w, w, eps)
-    return linear(_norms.rms_norm_ref(x, norm_w, eps), w)
+        return _NormLinearFn.apply(x, norm_w, w, eps, rope)
+    y = linear(_norms.rms_norm_ref(x, norm_w, eps), w)
+    if rope is not None:
+        from .rope import rope_ref
+        table, rot_heads, hd, S, off = rope
+        y4 = y.view(-1, S, w.shape[0] // hd, hd)
+        y4 = torch.cat([rope_ref(y4[:, :, :rot_heads], table, None, off), y4[:, :, rot_heads:]], dim=2)
+        y = y4.reshape(y.shape)
+    return y
 
 
 class _SwiGLULinearFn(torch.autograd.Function):

@@ -252,6 +252,36 @@ def test_flash_attention_tcgen05_strided_qkv():
 
 
 @gpu
+@pytest.mark.parametrize("S,Hq,Hkv,D", [(256, 4, 2, 128), (64, 4, 2, 64)])  # fused epilogue; separate rotation
+def test_norm_linear_rope_matches_reference(S, Hq, Hkv, D):
+    """RMSNorm -> QKV GEMM with RoPE on the q/k heads (GEMM epilogue where the shapes allow): forward and
+    gradients against a float32 restatement."""
+    from brain_b200.ops import linear as lin
+    B, d = 2, 256
+    N = (Hq + 2 * Hkv) * D
+    x = rnd(B, S, d, seed=40)
+    nw = rnd(d, seed=41, scale=0.1) + 1
+    w = rnd(N, d, seed=42, scale=0.05)
+    dy = rnd(B, S, N, seed=43)
+    t = ops.rope_table(D, S, 500000.0, device="cuda")
+    y, (xg, nwg, wg) = grads(lambda a, b, c: lin.norm_linear(a, b, c, 1e-5, rope=(t, Hq + Hkv, D, S, 0)), x, nw, w)
+    y.backward(dy)
+
+    def ref(a, b, c):
+        y0 = norms.rms_norm_ref(a.float(), b.float(), 1e-5) @ c.float().t()
+        y4 = y0.view(B, S, Hq + 2 * Hkv, D)
+        rot = rope_mod.rope_ref(y4[:, :, :Hq + Hkv], t.float())
+        return torch.cat([rot, y4[:, :, Hq + Hkv:]], dim=2).reshape(B, S, N)
+    yr, (xr, nwr, wr) = grads(ref, x, nw, w)
+    yr.backward(dy.float())
+    close(y, yr, 3e-2, 3e-2)
+    close(xg.grad, xr.grad, 5e-2, 5e-2)
+    close(wg.grad, wr.grad, 5e-2, 0.3)
+    close(nwg.grad, nwr.grad, 5e-2, 0.5)
+    _no_status()
+
+
+@gpu
 def test_qkv_attention_with_rope():
     B, S, Hq, Hkv, D = 2, 96, 8, 2, 64
     qkv = rnd(B, S, (Hq + 2 * Hkv) * D, seed=26)
