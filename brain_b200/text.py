@@ -1,0 +1,668 @@
+"""Text tokenisation: vocabulary, normaliser, pre-tokeniser, char / word / BPE / WordPiece / unigram
+(SentencePiece-style) / byte-level tokenisers, their trainers, and the post-processor that adds
+special tokens, truncates and pads into id tensors for the models.
+
+Reference: crates/brain-text/src. ``Tokenizer`` trait (tokenizer/mod.rs:28-60: encode, decode,
+tokenize, vocab_size, id/token lookups), ``Vocab`` with special kinds (vocab.rs:19-190), BPE
+segmentation by lowest merge rank (tokenizer/bpe.rs:62-135) and its trainer (tokenizer/trainer.rs:52-136,
+``</w>`` end-of-word suffix), WordPiece greedy longest match with a ``##`` continuation prefix
+(tokenizer/wordpiece.rs:53-100), unigram Viterbi segmentation over ``▁``-marked text
+(tokenizer/sentencepiece.rs:62-140) and its trainer (trainer.rs:138-190), the GPT-2 style byte-to-
+character map (tokenizer/bytelevel.rs:29-100), and the post-processor (tokenizer/post.rs:18-200).
+
+These are host-side string algorithms (the data path hands the ids to the GPU as one tensor per
+batch). The segmentation algorithms are the standard published ones (Sennrich et al. BPE; WordPiece
+greedy longest match; Kudo's unigram model with Viterbi decoding). Unlike the reference's hash-map
+iteration, every training tie is broken by a fixed order, so a trained vocabulary is deterministic.
+"""
+from __future__ import annotations
+
+import collections
+import enum
+import json
+import math
+import re
+import unicodedata
+from dataclasses import dataclass, field
+
+import torch
+
+
+class SpecialKind(enum.Enum):
+    PAD = "pad"
+    UNK = "unk"
+    BOS = "bos"
+    EOS = "eos"
+    MASK = "mask"
+    SEP = "sep"
+    CLS = "cls"
+    CUSTOM = "custom"
+
+
+class Vocab:
+    """Token <-> id table with special tokens."""
+
+    def __init__(self, tokens=None):
+        self._ids: dict[str, int] = {}
+        self._toks: list[str] = []
+        self._special: dict[int, SpecialKind] = {}
+        for t in tokens or []:
+            self.insert(t)
+
+    @classmethod
+    def from_tokens(cls, tokens) -> "Vocab":
+        return cls(tokens)
+
+    def insert(self, token: str) -> int:
+        if token not in self._ids:
+            self._ids[token] = len(self._toks)
+            self._toks.append(token)
+        return self._ids[token]
+
+    def add_special(self, token: str, kind: SpecialKind = SpecialKind.CUSTOM) -> int:
+        i = self.insert(token)
+        self._special[i] = kind
+        return i
+
+    def get_id(self, token: str):
+        return self._ids.get(token)
+
+    def get_token(self, i: int):
+        return self._toks[i] if 0 <= i < len(self._toks) else None
+
+    def __len__(self) -> int:
+        return len(self._toks)
+
+    def contains(self, token: str) -> bool:
+        return token in self._ids
+
+    __contains__ = contains
+
+    def is_special(self, i: int) -> bool:
+        return i in self._special
+
+    def _kind(self, kind: SpecialKind):
+        for i, k in self._special.items():
+            if k == kind:
+                return i
+        return None
+
+    def pad_id(self):
+        return self._kind(SpecialKind.PAD)
+
+    def unk_id(self):
+        return self._kind(SpecialKind.UNK)
+
+    def bos_id(self):
+        return self._kind(SpecialKind.BOS)
+
+    def eos_id(self):
+        return self._kind(SpecialKind.EOS)
+
+    def mask_id(self):
+        return self._kind(SpecialKind.MASK)
+
+    def sep_id(self):
+        return self._kind(SpecialKind.SEP)
+
+    def cls_id(self):
+        return self._kind(SpecialKind.CLS)
+
+    def export_json(self) -> str:
+        return json.dumps({"tokens": self._toks, "special": {str(i): k.value for i, k in self._special.items()}})
+
+    @classmethod
+    def import_json(cls, s: str) -> "Vocab":
+        d = json.loads(s)
+        v = cls(d["tokens"])
+        for i, k in d["special"].items():
+            v._special[int(i)] = SpecialKind(k)
+        return v
+
+
+def default_vocab_specials(v: Vocab) -> Vocab:
+    for tok, kind in (("[PAD]", SpecialKind.PAD), ("[UNK]", SpecialKind.UNK), ("[BOS]", SpecialKind.BOS),
+                      ("[EOS]", SpecialKind.EOS), ("[CLS]", SpecialKind.CLS), ("[SEP]", SpecialKind.SEP),
+                      ("[MASK]", SpecialKind.MASK)):
+        v.add_special(tok, kind)
+    return v
+
+
+@dataclass
+class TokenizedOutput:
+    ids: list[int]
+    tokens: list[str]
+    attention_mask: list[int] = field(default_factory=list)
+    type_ids: list[int] = field(default_factory=list)
+
+    def __post_init__(self):
+        if not self.attention_mask:
+            self.attention_mask = [1] * len(self.ids)
+        if not self.type_ids:
+            self.type_ids = [0] * len(self.ids)
+
+
+# ------------------------------------------------------------------ normaliser / pre-tokeniser
+@dataclass
+class NormalizerConfig:
+    lowercase: bool = True
+    strip_accents: bool = True
+    collapse_whitespace: bool = True
+    nfkc: bool = False
+
+
+class Normalizer:
+    def __init__(self, config: NormalizerConfig | None = None):
+        self.config = config or NormalizerConfig()
+
+    def normalize(self, text: str) -> str:
+        c = self.config
+        if c.nfkc:
+            text = unicodedata.normalize("NFKC", text)
+        if c.lowercase:
+            text = text.lower()
+        if c.strip_accents:
+            text = "".join(ch for ch in unicodedata.normalize("NFD", text) if unicodedata.category(ch) != "Mn")
+        if c.collapse_whitespace:
+            text = " ".join(text.split())
+        return text
+
+
+_PRE = re.compile(r"\w+|[^\w\s]", re.UNICODE)
+
+
+class PreTokenizer:
+    """Splits on whitespace and isolates punctuation; returns (piece, (start, end)) with char offsets."""
+
+    def __init__(self, split_punctuation: bool = True):
+        self.split_punctuation = split_punctuation
+
+    def pre_tokenize(self, text: str):
+        if self.split_punctuation:
+            return [(m.group(), (m.start(), m.end())) for m in _PRE.finditer(text)]
+        return [(m.group(), (m.start(), m.end())) for m in re.finditer(r"\S+", text)]
+
+
+# ------------------------------------------------------------------ tokenisers
+class Tokenizer:
+    """Common interface: encode / decode / tokenize / vocab lookups."""
+
+    vocab: Vocab
+
+    def tokenize(self, text: str) -> list[str]:
+        raise NotImplementedError
+
+    def encode(self, text: str) -> TokenizedOutput:
+        toks = self.tokenize(text)
+        unk = self.vocab.unk_id()
+        ids = []
+        for t in toks:
+            i = self.vocab.get_id(t)
+            if i is None:
+                if unk is None:
+                    raise KeyError(f"token {t!r} not in vocabulary and no [UNK] token")
+                i = unk
+            ids.append(i)
+        return TokenizedOutput(ids, toks)
+
+    def decode(self, ids) -> str:
+        raise NotImplementedError
+
+    def vocab_size(self) -> int:
+        return len(self.vocab)
+
+    def get_vocab(self) -> Vocab:
+        return self.vocab
+
+    def id_to_token(self, i: int):
+        return self.vocab.get_token(i)
+
+    def token_to_id(self, t: str):
+        return self.vocab.get_id(t)
+
+    def pad_token_id(self):
+        return self.vocab.pad_id()
+
+    def unk_token_id(self):
+        return self.vocab.unk_id()
+
+    def _pieces(self, ids):
+        return [self.vocab.get_token(int(i)) for i in ids if not self.vocab.is_special(int(i))]
+
+
+class CharTokenizer(Tokenizer):
+    def __init__(self, vocab: Vocab, lowercase: bool = False):
+        self.vocab, self.lowercase = vocab, lowercase
+
+    @classmethod
+    def from_corpus(cls, corpus, lowercase: bool = False) -> "CharTokenizer":
+        v = default_vocab_specials(Vocab())
+        for ch in sorted({c for doc in corpus for c in (doc.lower() if lowercase else doc)}):
+            v.insert(ch)
+        return cls(v, lowercase)
+
+    def tokenize(self, text):
+        return list(text.lower() if self.lowercase else text)
+
+    def decode(self, ids):
+        return "".join(self._pieces(ids))
+
+
+class WordTokenizer(Tokenizer):
+    def __init__(self, vocab: Vocab, normalizer: Normalizer | None = None):
+        self.vocab, self.normalizer, self.pre = vocab, normalizer or Normalizer(), PreTokenizer()
+
+    @classmethod
+    def from_corpus(cls, corpus, min_frequency: int = 1) -> "WordTokenizer":
+        t = cls(default_vocab_specials(Vocab()))
+        cnt = collections.Counter(w for doc in corpus for w, _ in t.pre.pre_tokenize(t.normalizer.normalize(doc)))
+        for w in sorted(w for w, c in cnt.items() if c >= min_frequency):
+            t.vocab.insert(w)
+        return t
+
+    def tokenize(self, text):
+        return [w for w, _ in self.pre.pre_tokenize(self.normalizer.normalize(text))]
+
+    def decode(self, ids):
+        return " ".join(self._pieces(ids))
+
+
+class BpeTokenizer(Tokenizer):
+    """Words are split into characters (the last carrying ``end_of_word_suffix``); the adjacent pair with
+    the lowest merge rank is merged until no ranked pair is left."""
+
+    def __init__(self, vocab: Vocab, merges, end_of_word_suffix: str = "</w>", normalizer=None):
+        self.vocab = vocab
+        self.ranks = {tuple(p): r for p, r in merges}
+        self.suffix = end_of_word_suffix
+        self.normalizer = normalizer or Normalizer(NormalizerConfig(lowercase=False, strip_accents=False))
+        self.pre = PreTokenizer(split_punctuation=False)
+        self._cache: dict[str, list[str]] = {}
+
+    @classmethod
+    def from_vocab_and_merges(cls, vocab, merges, end_of_word_suffix="</w>"):
+        return cls(vocab, merges, end_of_word_suffix)
+
+    def bpe_segment_word(self, word: str) -> list[str]:
+        if not word:
+            return []
+        hit = self._cache.get(word)
+        if hit is not None:
+            return list(hit)
+        sym = list(word)
+        if self.suffix:
+            sym[-1] += self.suffix
+        while len(sym) > 1:
+            best, idx = None, -1
+            for i in range(len(sym) - 1):
+                r = self.ranks.get((sym[i], sym[i + 1]))
+                if r is not None and (best is None or r < best):
+                    best, idx = r, i
+            if idx < 0:
+                break
+            sym[idx:idx + 2] = [sym[idx] + sym[idx + 1]]
+        self._cache[word] = list(sym)
+        return sym
+
+    def tokenize(self, text):
+        out = []
+        for w, _ in self.pre.pre_tokenize(self.normalizer.normalize(text)):
+            out += self.bpe_segment_word(w)
+        return out
+
+    def decode(self, ids):
+        s = "".join(self._pieces(ids))
+        return s.replace(self.suffix, " ").strip() if self.suffix else s
+
+
+class BpeTrainer:
+    @staticmethod
+    def train(corpus, vocab_size: int, min_frequency: int = 1, special_tokens=("[PAD]", "[UNK]"),
+              end_of_word_suffix: str = "</w>"):
+        """Returns (vocab, merges) with merges as [((a, b), rank)]. Ties between equally frequent pairs go
+        to the lexicographically smallest pair."""
+        words = collections.Counter(w for doc in corpus for w in doc.split())
+        vocab = Vocab()
+        kinds = {"[PAD]": SpecialKind.PAD, "[UNK]": SpecialKind.UNK, "[BOS]": SpecialKind.BOS,
+                 "[EOS]": SpecialKind.EOS}
+        for s in special_tokens:
+            vocab.add_special(s, kinds.get(s, SpecialKind.CUSTOM))
+        splits = {}
+        for w in sorted(words):
+            sym = list(w)
+            sym[-1] += end_of_word_suffix
+            splits[w] = sym
+        for s in sorted({s for sym in splits.values() for s in sym}):
+            vocab.insert(s)
+        merges = []
+        while len(vocab) < vocab_size:
+            pairs = collections.Counter()
+            for w, sym in splits.items():
+                for i in range(len(sym) - 1):
+                    pairs[(sym[i], sym[i + 1])] += words[w]
+            cands = [(c, p) for p, c in pairs.items() if c >= min_frequency]
+            if not cands:
+                break
+            best_c = max(c for c, _ in cands)
+            a, b = min(p for c, p in cands if c == best_c)
+            vocab.insert(a + b)
+            merges.append(((a, b), len(merges)))
+            for w, sym in splits.items():
+                i, new = 0, []
+                while i < len(sym):
+                    if i + 1 < len(sym) and sym[i] == a and sym[i + 1] == b:
+                        new.append(a + b)
+                        i += 2
+                    else:
+                        new.append(sym[i])
+                        i += 1
+                splits[w] = new
+        return vocab, merges
+
+
+class WordPieceTokenizer(Tokenizer):
+    """Greedy longest-prefix match; non-initial pieces carry ``continuation_prefix``; a word with an
+    unmatched remainder (or longer than ``max_input_chars_per_word``) becomes ``[UNK]``."""
+
+    def __init__(self, vocab: Vocab, unk_token: str = "[UNK]", continuation_prefix: str = "##",
+                 max_input_chars_per_word: int = 100, normalizer=None):
+        self.vocab, self.unk, self.prefix, self.max_chars = vocab, unk_token, continuation_prefix, max_input_chars_per_word
+        self.normalizer, self.pre = normalizer or Normalizer(), PreTokenizer()
+
+    def segment_word(self, word: str) -> list[str]:
+        if len(word) > self.max_chars:
+            return [self.unk]
+        out, start = [], 0
+        while start < len(word):
+            end = len(word)
+            piece = None
+            while start < end:
+                cand = word[start:end] if start == 0 else self.prefix + word[start:end]
+                if cand in self.vocab:
+                    piece = cand
+                    break
+                end -= 1
+            if piece is None:
+                return [self.unk]
+            out.append(piece)
+            start = end
+        return out
+
+    def tokenize(self, text):
+        out = []
+        for w, _ in self.pre.pre_tokenize(self.normalizer.normalize(text)):
+            out += self.segment_word(w)
+        return out
+
+    def decode(self, ids):
+        s = ""
+        for p in self._pieces(ids):
+            s += p[len(self.prefix):] if p.startswith(self.prefix) else (" " + p if s else p)
+        return s
+
+
+class WordPieceTrainer:
+    @staticmethod
+    def train(corpus, vocab_size: int, min_frequency: int = 1, continuation_prefix: str = "##") -> Vocab:
+        """BPE merges over words (no end-of-word suffix), pieces after the first written with the
+        continuation prefix; every character appears in both forms so any word in the corpus segments."""
+        norm, pre = Normalizer(), PreTokenizer()
+        words = collections.Counter(w for doc in corpus for w, _ in pre.pre_tokenize(norm.normalize(doc)))
+        vocab = default_vocab_specials(Vocab())
+        splits = {w: [w[0]] + [continuation_prefix + c for c in w[1:]] for w in sorted(words)}
+        for s in sorted({s for sym in splits.values() for s in sym}):
+            vocab.insert(s)
+        strip = lambda t: t[len(continuation_prefix):] if t.startswith(continuation_prefix) else t  # noqa: E731
+        while len(vocab) < vocab_size:
+            pairs = collections.Counter()
+            for w, sym in splits.items():
+                for i in range(len(sym) - 1):
+                    pairs[(sym[i], sym[i + 1])] += words[w]
+            cands = [(c, p) for p, c in pairs.items() if c >= min_frequency]
+            if not cands:
+                break
+            best_c = max(c for c, _ in cands)
+            a, b = min(p for c, p in cands if c == best_c)
+            merged = a + strip(b)
+            vocab.insert(merged)
+            for w, sym in splits.items():
+                i, new = 0, []
+                while i < len(sym):
+                    if i + 1 < len(sym) and sym[i] == a and sym[i + 1] == b:
+                        new.append(merged)
+                        i += 2
+                    else:
+                        new.append(sym[i])
+                        i += 1
+                splits[w] = new
+        return vocab
+
+
+SP_SPACE = "▁"
+
+
+class SentencePieceTokenizer(Tokenizer):
+    """Unigram language model: spaces become ``▁`` (and text is prefixed with one), and the
+    segmentation maximising the sum of piece log-probabilities is found by Viterbi. Characters that no
+    piece covers become ``[UNK]`` with a fixed penalty."""
+
+    UNK_PENALTY = -20.0
+
+    def __init__(self, vocab: Vocab, piece_scores: dict[str, float], add_dummy_prefix: bool = True):
+        self.vocab, self.scores, self.add_dummy_prefix = vocab, dict(piece_scores), add_dummy_prefix
+        self.max_len = max((len(p) for p in self.scores), default=1)
+
+    @classmethod
+    def from_pieces(cls, vocab, piece_scores, add_dummy_prefix=True):
+        return cls(vocab, piece_scores, add_dummy_prefix)
+
+    def preprocess(self, text: str) -> str:
+        text = " ".join(text.split())
+        if self.add_dummy_prefix:
+            text = " " + text
+        return text.replace(" ", SP_SPACE)
+
+    def viterbi_decode(self, text: str) -> list[str]:
+        s = self.preprocess(text)
+        n = len(s)
+        best = [-math.inf] * (n + 1)
+        back = [(-1, None)] * (n + 1)
+        best[0] = 0.0
+        for end in range(1, n + 1):
+            for start in range(max(0, end - self.max_len), end):
+                if best[start] == -math.inf:
+                    continue
+                piece = s[start:end]
+                sc = self.scores.get(piece)
+                if sc is None:
+                    if end - start != 1:
+                        continue
+                    sc, piece = self.UNK_PENALTY, None
+                if best[start] + sc > best[end]:
+                    best[end] = best[start] + sc
+                    back[end] = (start, piece)
+        out, pos = [], n
+        while pos > 0:
+            start, piece = back[pos]
+            out.append(piece if piece is not None else "[UNK]")
+            pos = start
+        return out[::-1]
+
+    def tokenize(self, text):
+        return self.viterbi_decode(text)
+
+    def decode(self, ids):
+        return "".join(self._pieces(ids)).replace(SP_SPACE, " ").strip()
+
+
+class UnigramTrainer:
+    @staticmethod
+    def train(corpus, vocab_size: int, max_piece_len: int = 8, em_iters: int = 3):
+        """Seed with every substring (up to ``max_piece_len``) seen at least twice plus all characters,
+        score by log frequency, then repeat: Viterbi-segment the corpus, re-estimate log probabilities
+        from the segment counts, and keep the ``vocab_size`` most probable pieces (characters are
+        always kept). Returns (vocab, piece_scores)."""
+        docs = [" " + " ".join(d.split()) for d in corpus]
+        docs = [d.replace(" ", SP_SPACE) for d in docs]
+        chars = sorted({c for d in docs for c in d})
+        sub = collections.Counter()
+        for d in docs:
+            for i in range(len(d)):
+                for L in range(2, max_piece_len + 1):
+                    # a piece never spans a word boundary: "▁" may only lead it
+                    if i + L <= len(d) and SP_SPACE not in d[i + 1:i + L]:
+                        sub[d[i:i + L]] += 1
+        cand = {p: c for p, c in sub.items() if c >= 2}
+        seed = dict(cand)
+        for c in chars:
+            cand[c] = cand.get(c, 0) + 1
+        tot = sum(cand.values())
+        scores = {p: math.log(c / tot) for p, c in cand.items()}
+        specials = default_vocab_specials(Vocab())
+        budget = max(len(chars), vocab_size - len(specials))
+        for _ in range(em_iters):
+            tok = SentencePieceTokenizer(Vocab(), scores)
+            counts = collections.Counter()
+            for d in docs:
+                counts.update(p for p in tok.viterbi_decode(d.replace(SP_SPACE, " ")) if p != "[UNK]")
+            for c in chars:
+                counts[c] += 1
+            # pieces the current segmentation does not use keep a tenth of their seed frequency, so a
+            # piece is dropped only when better ones fill the budget
+            for p, c in seed.items():
+                counts[p] += 0.1 * c
+            keep = sorted(counts, key=lambda p: (-counts[p], p))
+            keep = list(dict.fromkeys(chars + [p for p in keep if p not in chars][:max(0, budget - len(chars))]))
+            tot = sum(counts[p] for p in keep)
+            scores = {p: math.log(counts[p] / tot) for p in keep}
+        vocab = specials
+        for p in sorted(scores, key=lambda p: (-scores[p], p)):
+            vocab.insert(p)
+        return vocab, scores
+
+
+def _byte_map() -> dict[int, str]:
+    """Printable bytes map to themselves; the rest to code points from 256 up (GPT-2 byte-level map)."""
+    keep = list(range(ord("!"), ord("~") + 1)) + list(range(0xA1, 0xAC + 1)) + list(range(0xAE, 0xFF + 1))
+    out, extra = {}, 0
+    for b in range(256):
+        if b in keep:
+            out[b] = chr(b)
+        else:
+            out[b] = chr(256 + extra)
+            extra += 1
+    return out
+
+
+class ByteLevelEncoder:
+    def __init__(self):
+        self._b2c = _byte_map()
+        self._c2b = {c: b for b, c in self._b2c.items()}
+
+    def byte_to_char(self, b: int) -> str:
+        return self._b2c[b]
+
+    def char_to_byte(self, c: str):
+        return self._c2b.get(c)
+
+    def encode_bytes(self, data: bytes) -> str:
+        return "".join(self._b2c[b] for b in data)
+
+    def decode_bytes(self, text: str) -> bytes:
+        return bytes(self._c2b[c] for c in text if c in self._c2b)
+
+    def decode_to_string(self, text: str) -> str:
+        return self.decode_bytes(text).decode("utf-8", errors="replace")
+
+
+# ------------------------------------------------------------------ post-processing
+class TruncationStrategy(enum.Enum):
+    LONGEST_FIRST = "longest_first"
+    ONLY_FIRST = "only_first"
+    ONLY_SECOND = "only_second"
+    DO_NOT_TRUNCATE = "do_not_truncate"
+
+
+@dataclass
+class PostConfig:
+    add_bos_eos: bool = False
+    add_cls_sep: bool = False
+    max_length: int = 0
+    pad_to_max_length: bool = False
+    truncation: TruncationStrategy = TruncationStrategy.LONGEST_FIRST
+
+
+class PostProcessor:
+    def __init__(self, vocab: Vocab, config: PostConfig | None = None):
+        self.vocab, self.config = vocab, config or PostConfig()
+
+    def _wrap(self, ids, toks, first: bool, last: bool):
+        c, v = self.config, self.vocab
+        if c.add_cls_sep:
+            pre = [v.cls_id()] if first else []
+            return pre + ids + [v.sep_id()], ([v.get_token(v.cls_id())] if first else []) + toks + [v.get_token(v.sep_id())]
+        if c.add_bos_eos:
+            pre = [v.bos_id()] if first else []
+            post = [v.eos_id()] if last else []
+            return (pre + ids + post, ([v.get_token(v.bos_id())] if first else []) + toks +
+                    ([v.get_token(v.eos_id())] if last else []))
+        return ids, toks
+
+    def _n_special(self, pair: bool) -> int:
+        c = self.config
+        if c.add_cls_sep:
+            return 3 if pair else 2
+        if c.add_bos_eos:
+            return 2
+        return 0
+
+    def _pad(self, out: TokenizedOutput) -> TokenizedOutput:
+        c = self.config
+        if c.max_length and c.pad_to_max_length and len(out.ids) < c.max_length:
+            k = c.max_length - len(out.ids)
+            pad = self.vocab.pad_id() or 0
+            out.ids += [pad] * k
+            out.tokens += [self.vocab.get_token(pad) or ""] * k
+            out.attention_mask += [0] * k
+            out.type_ids += [out.type_ids[-1] if out.type_ids else 0] * k
+        return out
+
+    def process_single(self, out: TokenizedOutput) -> TokenizedOutput:
+        c = self.config
+        ids, toks = list(out.ids), list(out.tokens)
+        if c.max_length and c.truncation != TruncationStrategy.DO_NOT_TRUNCATE:
+            keep = max(0, c.max_length - self._n_special(False))
+            ids, toks = ids[:keep], toks[:keep]
+        ids, toks = self._wrap(ids, toks, True, True)
+        return self._pad(TokenizedOutput(ids, toks))
+
+    def process_pair(self, first: TokenizedOutput, second: TokenizedOutput) -> TokenizedOutput:
+        c = self.config
+        a_ids, a_t, b_ids, b_t = list(first.ids), list(first.tokens), list(second.ids), list(second.tokens)
+        if c.max_length and c.truncation != TruncationStrategy.DO_NOT_TRUNCATE:
+            budget = max(0, c.max_length - self._n_special(True))
+            while len(a_ids) + len(b_ids) > budget:
+                cut_a = (c.truncation == TruncationStrategy.ONLY_FIRST or
+                         (c.truncation == TruncationStrategy.LONGEST_FIRST and len(a_ids) >= len(b_ids)))
+                if cut_a and a_ids:
+                    a_ids.pop(), a_t.pop()
+                elif b_ids and c.truncation != TruncationStrategy.ONLY_FIRST:
+                    b_ids.pop(), b_t.pop()
+                else:
+                    break
+        ai, at = self._wrap(a_ids, a_t, True, False)
+        bi, bt = self._wrap(b_ids, b_t, False, True)
+        return self._pad(TokenizedOutput(ai + bi, at + bt, type_ids=[0] * len(ai) + [1] * len(bi)))
+
+
+def batch_encode(tokenizer: Tokenizer, texts, post: PostProcessor, device=None):
+    """Encodes and pads a batch to its longest sequence; returns (ids [B, L] int64, mask [B, L])."""
+    outs = [post.process_single(tokenizer.encode(t)) for t in texts]
+    L = max(len(o.ids) for o in outs)
+    pad = tokenizer.vocab.pad_id() or 0
+    ids = torch.full((len(outs), L), pad, dtype=torch.int64)
+    mask = torch.zeros((len(outs), L), dtype=torch.int64)
+    for i, o in enumerate(outs):
+        ids[i, :len(o.ids)] = torch.tensor(o.ids)
+        mask[i, :len(o.ids)] = torch.tensor(o.attention_mask)
+    return ids.to(device), mask.to(device)
