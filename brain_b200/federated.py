@@ -274,7 +274,7 @@ class FederatedClient:
                 loss.backward()
                 opt.step()
                 n += x.shape[0]
-                last = float(loss)
+                last = float(loss.detach())
         weights = [p.detach().clone() for p in model.parameters()]
         return ModelDelta(self.client_id, weights, n // max(1, self.local_epochs)), last
 

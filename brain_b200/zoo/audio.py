@@ -1,0 +1,202 @@
+"""Audio features: framing and windows, STFT / inverse STFT, mel filterbank, log-mel spectrogram, MFCC
+(DCT-II), CMVN, pre-emphasis, energy-based voice activity detection, resampling, SpecAugment masks and
+16-bit PCM WAV read / write.
+
+Reference: crates/brain-audio. STFT (feature/stft.rs:14-220), MFCC (feature/mfcc.rs:13-160 incl. CMVN
+at :96), spectral augmentation (augment/spectral.rs), time augmentation (augment/time.rs), VAD
+(vad.rs), resampling (resample.rs), WAV I/O (io/wav.rs).
+
+Batched tensor code: the STFT is ``torch.stft`` (one cuFFT batch on a GPU), the mel projection and the
+DCT are GEMMs against precomputed matrices. Mel scale is HTK (2595 log10(1 + f / 700)).
+"""
+from __future__ import annotations
+
+import math
+import struct
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass
+class STFTConfig:
+    n_fft: int = 512
+    hop_length: int = 160
+    win_length: int = 400
+    window: str = "hann"
+    center: bool = True
+
+
+def _window(cfg: STFTConfig, device=None, dtype=torch.float32):
+    if cfg.window == "hann":
+        return torch.hann_window(cfg.win_length, periodic=True, device=device, dtype=dtype)
+    if cfg.window == "hamming":
+        return torch.hamming_window(cfg.win_length, periodic=True, device=device, dtype=dtype)
+    return torch.ones(cfg.win_length, device=device, dtype=dtype)
+
+
+def stft(signal: torch.Tensor, cfg: STFTConfig | None = None):
+    """signal [..., n] -> (magnitude, phase), each [..., n_fft // 2 + 1, frames]."""
+    cfg = cfg or STFTConfig()
+    spec = torch.stft(signal, cfg.n_fft, cfg.hop_length, cfg.win_length, _window(cfg, signal.device, signal.dtype),
+                      center=cfg.center, return_complex=True)
+    return spec.abs(), spec.angle()
+
+
+def istft(magnitude, phase, cfg: STFTConfig | None = None, length: int | None = None):
+    cfg = cfg or STFTConfig()
+    spec = torch.polar(magnitude, phase)
+    return torch.istft(spec, cfg.n_fft, cfg.hop_length, cfg.win_length, _window(cfg, magnitude.device, magnitude.dtype),
+                       center=cfg.center, length=length)
+
+
+def hz_to_mel(f):
+    return 2595.0 * torch.log10(1.0 + torch.as_tensor(f, dtype=torch.float64) / 700.0)
+
+
+def mel_to_hz(m):
+    return 700.0 * (10.0 ** (torch.as_tensor(m, dtype=torch.float64) / 2595.0) - 1.0)
+
+
+def mel_filterbank(n_mels: int, n_fft: int, sample_rate: int, f_min: float = 0.0, f_max: float | None = None):
+    """Triangular filters [n_mels, n_fft // 2 + 1] evenly spaced on the mel scale."""
+    f_max = f_max or sample_rate / 2
+    mels = torch.linspace(float(hz_to_mel(f_min)), float(hz_to_mel(f_max)), n_mels + 2, dtype=torch.float64)
+    hz = mel_to_hz(mels)
+    bins = torch.linspace(0, sample_rate / 2, n_fft // 2 + 1, dtype=torch.float64)
+    fb = torch.zeros(n_mels, bins.numel(), dtype=torch.float64)
+    for m in range(n_mels):
+        lo, c, hi = hz[m], hz[m + 1], hz[m + 2]
+        up = (bins - lo) / (c - lo)
+        down = (hi - bins) / (hi - c)
+        fb[m] = torch.clamp(torch.minimum(up, down), min=0)
+    return fb.float()
+
+
+def dct_matrix(n_out: int, n_in: int) -> torch.Tensor:
+    """Orthonormal DCT-II [n_out, n_in]."""
+    k = torch.arange(n_out, dtype=torch.float64)[:, None]
+    n = torch.arange(n_in, dtype=torch.float64)[None]
+    m = torch.cos(math.pi / n_in * (n + 0.5) * k) * math.sqrt(2.0 / n_in)
+    m[0] /= math.sqrt(2.0)
+    return m.float()
+
+
+@dataclass
+class MFCCConfig:
+    sample_rate: int = 16000
+    n_mfcc: int = 13
+    n_mels: int = 40
+    stft: STFTConfig = None
+    log_eps: float = 1e-10
+
+    def __post_init__(self):
+        if self.stft is None:
+            self.stft = STFTConfig()
+
+
+def log_mel_spectrogram(signal, cfg: MFCCConfig | None = None):
+    """[..., n] -> [..., n_mels, frames] natural-log mel power."""
+    cfg = cfg or MFCCConfig()
+    mag, _ = stft(signal, cfg.stft)
+    fb = mel_filterbank(cfg.n_mels, cfg.stft.n_fft, cfg.sample_rate).to(signal.device, mag.dtype)
+    return torch.log(torch.matmul(fb, mag ** 2) + cfg.log_eps)
+
+
+def mfcc(signal, cfg: MFCCConfig | None = None):
+    cfg = cfg or MFCCConfig()
+    lm = log_mel_spectrogram(signal, cfg)
+    return torch.matmul(dct_matrix(cfg.n_mfcc, cfg.n_mels).to(lm.device, lm.dtype), lm)
+
+
+def apply_cmvn(features, norm_mean: bool = True, norm_var: bool = True, dim: int = -1):
+    """Cepstral mean (and variance) normalisation along the time axis."""
+    out = features
+    if norm_mean:
+        out = out - out.mean(dim, keepdim=True)
+    if norm_var:
+        out = out / (out.std(dim, keepdim=True, unbiased=False) + 1e-8)
+    return out
+
+
+def pre_emphasis(signal, coef: float = 0.97):
+    return torch.cat([signal[..., :1], signal[..., 1:] - coef * signal[..., :-1]], -1)
+
+
+def frame_energy(signal, frame: int = 400, hop: int = 160):
+    frames = signal.unfold(-1, frame, hop)
+    return (frames ** 2).mean(-1)
+
+
+def energy_vad(signal, frame: int = 400, hop: int = 160, threshold_db: float = -35.0):
+    """True per frame whose energy is within ``threshold_db`` of the loudest frame."""
+    e = frame_energy(signal, frame, hop)
+    db = 10 * torch.log10(e + 1e-12)
+    return db > (db.max(-1, keepdim=True).values + threshold_db)
+
+
+def resample(signal, orig_sr: int, new_sr: int):
+    """Band-limited resampling via linear interpolation after a windowed-sinc low-pass when downsampling."""
+    if orig_sr == new_sr:
+        return signal
+    x = signal
+    if new_sr < orig_sr:
+        cutoff = new_sr / orig_sr / 2
+        half = 32
+        n = torch.arange(-half, half + 1, dtype=torch.float64)
+        h = 2 * cutoff * torch.sinc(2 * cutoff * n) * torch.hann_window(2 * half + 1, periodic=False, dtype=torch.float64)
+        h = (h / h.sum()).to(x.dtype).to(x.device)
+        x = torch.nn.functional.conv1d(x.reshape(-1, 1, x.shape[-1]), h.view(1, 1, -1), padding=half).reshape(x.shape)
+    n_out = int(round(x.shape[-1] * new_sr / orig_sr))
+    return torch.nn.functional.interpolate(x.reshape(-1, 1, x.shape[-1]), size=n_out, mode="linear",
+                                           align_corners=False).reshape(*x.shape[:-1], n_out)
+
+
+def spec_augment(spec, freq_mask: int = 8, time_mask: int = 20, n_freq: int = 1, n_time: int = 1, generator=None):
+    """Zeroes ``n_freq`` random frequency bands and ``n_time`` random time spans of [..., F, T]."""
+    out = spec.clone()
+    F_, T_ = spec.shape[-2], spec.shape[-1]
+    for _ in range(n_freq):
+        w = int(torch.randint(0, freq_mask + 1, (1,), generator=generator))
+        f0 = int(torch.randint(0, max(1, F_ - w), (1,), generator=generator))
+        out[..., f0:f0 + w, :] = 0
+    for _ in range(n_time):
+        w = int(torch.randint(0, time_mask + 1, (1,), generator=generator))
+        t0 = int(torch.randint(0, max(1, T_ - w), (1,), generator=generator))
+        out[..., :, t0:t0 + w] = 0
+    return out
+
+
+def write_wav(path: str, samples: torch.Tensor, sample_rate: int) -> None:
+    """Mono or [channels, n] float samples in [-1, 1] -> 16-bit PCM RIFF/WAVE."""
+    x = samples if samples.dim() == 2 else samples[None]
+    ch, n = x.shape
+    pcm = (x.clamp(-1, 1) * 32767).round().to(torch.int16).t().contiguous().numpy().tobytes()
+    with open(path, "wb") as f:
+        f.write(b"RIFF" + struct.pack("<I", 36 + len(pcm)) + b"WAVE")
+        f.write(b"fmt " + struct.pack("<IHHIIHH", 16, 1, ch, sample_rate, sample_rate * ch * 2, ch * 2, 16))
+        f.write(b"data" + struct.pack("<I", len(pcm)) + pcm)
+
+
+def read_wav(path: str):
+    """16-bit PCM WAV -> (float samples [channels, n], sample_rate)."""
+    import numpy as np
+
+    with open(path, "rb") as f:
+        data = f.read()
+    if data[:4] != b"RIFF" or data[8:12] != b"WAVE":
+        raise ValueError("not a RIFF/WAVE file")
+    pos, fmt, pcm = 12, None, None
+    while pos + 8 <= len(data):
+        cid, size = data[pos:pos + 4], struct.unpack("<I", data[pos + 4:pos + 8])[0]
+        body = data[pos + 8:pos + 8 + size]
+        if cid == b"fmt ":
+            fmt = struct.unpack("<HHIIHH", body[:16])
+        elif cid == b"data":
+            pcm = body
+        pos += 8 + size + (size & 1)
+    if fmt is None or pcm is None or fmt[0] != 1 or fmt[5] != 16:
+        raise ValueError("only 16-bit PCM WAV is supported")
+    ch, sr = fmt[1], fmt[2]
+    x = torch.from_numpy(np.frombuffer(pcm, dtype="<i2").astype("float32") / 32768.0)
+    return x.view(-1, ch).t().contiguous(), sr

@@ -132,3 +132,268 @@ def test_unigram_viterbi_and_postprocess():
     assert p.type_ids[0] == 0 and p.type_ids[-1] == 1 or p.attention_mask[-1] == 0
     ids, mask = batch_encode(sp, ["low", "newest wider"], PostProcessor(vocab))
     assert ids.shape[0] == 2 and mask.sum(1)[0] < mask.sum(1)[1]
+
+
+# ------------------------------------------------------------------ model zoo
+def test_lstm_cell_matches_torch_and_lm_learns():
+    from brain_b200.zoo import rnn
+    torch.manual_seed(0)
+    cell = rnn.LstmCell(5, 7)
+    ref = torch.nn.LSTMCell(5, 7)
+    with torch.no_grad():
+        ref.weight_ih.copy_(cell.ih.weight)
+        ref.bias_ih.copy_(cell.ih.bias)
+        ref.weight_hh.copy_(cell.hh.weight)
+        ref.bias_hh.zero_()
+    x, h, c = torch.randn(3, 5), torch.randn(3, 7), torch.randn(3, 7)
+    h1, c1 = cell(x, (h, c))
+    h2, c2 = ref(x, (h, c))
+    torch.testing.assert_close(h1, h2)
+    torch.testing.assert_close(c1, c2)
+    gru = rnn.GRU(4, 6, num_layers=2, bidirectional=True)
+    y, st = gru(torch.randn(2, 5, 4))
+    assert y.shape == (2, 5, 12) and len(st) == 4
+    lm = rnn.LstmLanguageModel(8, 16, 32)
+    seq = torch.tensor([[0, 1, 2, 3, 4, 5, 6, 7] * 3] * 4)
+    opt = torch.optim.Adam(lm.parameters(), lr=0.03)
+    first = None
+    for _ in range(60):
+        loss = lm.teacher_forcing_loss(seq)
+        first = first if first is not None else float(loss)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+    assert float(loss) < 0.2 * first
+    assert lm.greedy(seq[:1, :3], 5)[0, 3:].tolist() == [3, 4, 5, 6, 7]
+
+
+def test_beam_search_prefers_higher_joint_probability():
+    from brain_b200.zoo.rnn import BeamConfig, beam_search
+    # greedy picks token 1 first (0.6) but the best two-token sequence is 2 -> 3 (0.4 * 1.0)
+    table = {(0,): [0.0, 0.6, 0.4, 0.0], (0, 1): [0.0, 0.0, 0.5, 0.5], (0, 2): [0.0, 0.0, 0.0, 1.0]}
+
+    def step(seqs):
+        out = []
+        for s in seqs:
+            p = torch.tensor(table.get(tuple(s), [0.25] * 4))
+            out.append(torch.log(p + 1e-12))
+        return out
+    best = beam_search(step, 0, BeamConfig(beam_width=2, max_len=3, length_penalty=0.0))
+    assert best.tokens == [0, 2, 3]
+
+
+def test_gcn_matches_dense_formula_and_classifier_trains():
+    from brain_b200.zoo import gnn
+    torch.manual_seed(0)
+    edges = [(0, 1), (1, 2), (2, 0), (3, 4), (4, 5), (5, 3), (2, 3)]
+    g = gnn.Graph.from_undirected(edges, 6)
+    x = torch.randn(6, 4)
+    layer = gnn.GcnLayer(4, 3, bias=False)
+    A = torch.zeros(6, 6)
+    for a, b in edges:
+        A[a, b] = A[b, a] = 1
+    A += torch.eye(6)
+    d = A.sum(1).rsqrt()
+    dense = (d[:, None] * A * d[None]) @ (x @ layer.lin.weight.t())
+    torch.testing.assert_close(layer(g, x), dense)
+    gat = gnn.GatLayer(4, 2, num_heads=3)
+    assert gat(g, x).shape == (6, 6)
+    pooled = gnn.global_mean_pool(x, torch.tensor([0, 0, 0, 1, 1, 1]), 2)
+    torch.testing.assert_close(pooled[1], x[3:].mean(0))
+    for kind in ("gcn", "sage", "gin", "gat"):
+        model = gnn.GnnNodeClassifier(4, 8, 2, kind)
+        y = torch.tensor([0, 0, 0, 1, 1, 1])
+        feats = torch.eye(6)[:, :4] + 0.1
+        opt = torch.optim.Adam(model.parameters(), lr=0.05)
+        for _ in range(80):
+            loss = torch.nn.functional.cross_entropy(model(g, feats), y)
+            opt.zero_grad()
+            loss.backward()
+            opt.step()
+        assert (model(g, feats).argmax(1) == y).float().mean() >= 5 / 6, kind
+
+
+def test_diffusion_schedules_samplers_and_training():
+    from brain_b200.zoo import diffusion as D
+    for s in (D.LinearSchedule(100), D.CosineSchedule(100), D.ScaledLinearSchedule(100)):
+        ac = s.alphas_cumprod
+        assert bool((ac[1:] < ac[:-1]).all()) and 0 < float(ac[-1]) < float(ac[0]) <= 1
+    # with the exact noise predictor for a point mass at x0, deterministic DDIM returns x0
+    sched = D.LinearSchedule(200)
+    x0 = torch.tensor([[1.5, -0.5]])
+
+    def oracle(x, t, cond=None):
+        ac = sched.at("alphas_cumprod", t, x)
+        return (x - ac.sqrt() * x0) / (1 - ac).sqrt()
+    out = D.DdimSampler(sched, eta=0.0).sample(oracle, (1, 2), num_steps=20, generator=torch.Generator().manual_seed(0))
+    torch.testing.assert_close(out, x0, atol=1e-4, rtol=0)
+    ddpm = D.DdpmSampler(D.LinearSchedule(50)).sample(lambda x, t, c=None: torch.zeros_like(x), (4, 2),
+                                                      generator=torch.Generator().manual_seed(1))
+    assert ddpm.shape == (4, 2) and torch.isfinite(ddpm).all()
+    torch.manual_seed(0)
+    model = D.MlpDenoiser(2, 64, num_classes=2)
+    opt = torch.optim.Adam(model.parameters(), lr=3e-3)
+    g = torch.Generator().manual_seed(2)
+    data = torch.randn(256, 2, generator=g) * 0.1 + torch.tensor([1.0, -1.0])
+    losses = []
+    for _ in range(150):
+        loss = D.diffusion_loss(model, sched, data, generator=g)
+        opt.zero_grad()
+        loss.backward()
+        opt.step()
+        losses.append(float(loss))
+    assert sum(losses[-20:]) / 20 < 0.7 * sum(losses[:20]) / 20
+    guided = D.guided_eps(model, data[:3], torch.tensor([5, 5, 5]), torch.tensor([0, 1, 0]), 2.0)
+    assert guided.shape == (3, 2)
+
+
+def test_gan_losses_penalties_and_training():
+    from brain_b200.zoo import gan
+    lin = torch.nn.Linear(3, 1)
+    with torch.no_grad():
+        lin.weight.copy_(torch.tensor([[0.6, 0.8, 0.0]]))  # unit-norm gradient everywhere
+    real, fake = torch.randn(8, 3), torch.randn(8, 3)
+    assert float(gan.gradient_penalty(lambda x: lin(x).squeeze(-1), real, fake)) < 1e-10
+    assert abs(float(gan.r1_penalty(lambda x: lin(x).squeeze(-1), real, gamma=2.0)) - 1.0) < 1e-6
+    d_r, d_f = torch.tensor([2.0, 0.5]), torch.tensor([-2.0, 0.5])
+    assert float(gan.hinge_loss_d(d_r, d_f)) == pytest.approx(0.25 + 0.75)
+    assert float(gan.wgan_loss_d(d_r, d_f)) == pytest.approx(-0.75 - 1.25)
+    torch.manual_seed(0)
+    G, Dn = gan.MlpGenerator(4, 1, 32), gan.MlpDiscriminator(1, 32)
+    og, od = torch.optim.Adam(G.parameters(), 2e-3, betas=(0.5, 0.9)), torch.optim.Adam(Dn.parameters(), 2e-3, betas=(0.5, 0.9))
+    g = torch.Generator().manual_seed(0)
+    for _ in range(300):
+        real = torch.randn(64, 1, generator=g) * 0.5 + 3.0
+        gan.train_step(G, Dn, og, od, real, loss="bce", generator=g)
+    mean = float(G(torch.randn(512, 4)).mean())
+    assert abs(mean - 3.0) < 0.75
+    img = gan.DcganGenerator(16, 1, 16, 3)(torch.randn(2, 16))
+    assert img.shape == (2, 1, 32, 32)
+    assert gan.DcganDiscriminator(1, 16, 3)(img).shape == (2,)
+    assert gan.DcganDiscriminator(1, 16, 3, patch=True)(img).shape[0] == 2
+
+
+def test_rl_gae_buffers_and_dqn_solves_gridworld():
+    from brain_b200.zoo import rl
+    adv, ret = rl.gae([1.0, 0.0, 1.0], [0.5, 0.5, 0.5], [False, False, True], gamma=0.9, lam=1.0)
+    mc = rl.discounted_returns([1.0, 0.0, 1.0], [False, False, True], 0.9)
+    torch.testing.assert_close(ret.float(), mc.float())
+    obj = rl.PpoClippedObjective(0.2)
+    assert float(obj.compute_policy_loss(torch.tensor([1.5]), torch.tensor([1.0]))) == pytest.approx(-1.2)
+    pb = rl.PrioritizedReplayBuffer(10)
+    for i in range(10):
+        pb.push(rl.Transition(torch.zeros(2), 0, float(i), torch.zeros(2), False))
+    batch, w = pb.sample_batch(4)
+    pb.update_priorities([1.0] * 4)
+    assert len(batch) == 4 and float(w.max()) == 1.0
+    env = rl.GridWorldEnv(3, 3, max_steps=30)
+    agent = rl.DqnAgent(9, 4, rl.DqnConfig(epsilon_decay_steps=600, target_update=50, batch_size=32, lr=3e-3), seed=0)
+    s = env.reset()
+    for _ in range(1500):
+        a = agent.act(s)
+        s2, r, d, _ = env.step(a)
+        agent.step(rl.Transition(s, a, r, s2, d))
+        s = env.reset() if d else s2
+    assert rl.evaluate(rl.GridWorldEnv(3, 3, max_steps=30), lambda o: agent.act(o, greedy=True), 1) > 0.9
+    cliff, lake = rl.CliffWalkingEnv(), rl.FrozenLakeEnv(4)
+    assert cliff.reset().shape == (48,) and cliff.step(1)[1] == -100.0
+    assert (0, 0) not in lake.holes
+    venv = rl.VectorEnv(lambda: rl.GridWorldEnv(2, 2, 5), 3)
+    o, r, d = venv.step([1, 1, 1])
+    assert o.shape == (3, 4)
+    ppo = rl.PpoAgent(4, 4, rl.PpoConfig(rollout=32, epochs=2))
+    assert math.isfinite(ppo.update(rl.GridWorldEnv(2, 2, 10)))
+    a2c = rl.A2cAgent(4, 4)
+    assert math.isfinite(a2c.update(rl.GridWorldEnv(2, 2, 10)))
+
+
+def test_audio_features_and_wav(tmp_path):
+    from brain_b200.zoo import audio as A
+    sr = 16000
+    t = torch.arange(sr, dtype=torch.float32) / sr
+    x = 0.5 * torch.sin(2 * math.pi * 440 * t)
+    mag, ph = A.stft(x)
+    back = A.istft(mag, ph, length=x.numel())
+    torch.testing.assert_close(back, x, atol=1e-4, rtol=0)
+    peak_bin = int(mag.mean(-1).argmax())
+    assert abs(peak_bin * sr / 512 - 440) < sr / 512
+    fb = A.mel_filterbank(40, 512, sr)
+    peaks = fb.argmax(1)
+    assert bool((peaks[1:] >= peaks[:-1]).all()) and fb.shape == (40, 257)
+    m = A.mfcc(x)
+    assert m.shape[0] == 13 and torch.isfinite(m).all()
+    cm = A.apply_cmvn(m)
+    assert float(cm.mean(-1).abs().max()) < 1e-4
+    y = A.resample(x, sr, 8000)
+    assert y.numel() == 8000
+    mag8, _ = A.stft(y)
+    assert abs(int(mag8.mean(-1).argmax()) * 8000 / 512 - 440) < 8000 / 512 * 1.5
+    sil = torch.cat([torch.zeros(4000), x[:4000]])
+    vad = A.energy_vad(sil)
+    assert not bool(vad[0]) and bool(vad[-1])
+    p = str(tmp_path / "a.wav")
+    A.write_wav(p, x[:1000], sr)
+    r, sr2 = A.read_wav(p)
+    assert sr2 == sr and r.shape == (1, 1000)
+    torch.testing.assert_close(r[0], x[:1000], atol=1 / 16384, rtol=0)
+    aug = A.spec_augment(mag, 5, 10, generator=torch.Generator().manual_seed(0))
+    assert aug.shape == mag.shape
+
+
+def test_neuroevolution_ga_es_cmaes():
+    from brain_b200.zoo import neuroevolution as N
+    target = torch.tensor([3.0, -2.0, 1.0, 0.5], dtype=torch.float64)
+    f = lambda g: -float(((g - target) ** 2).sum())  # noqa: E731
+    res = N.Ga(N.GaConfig(population=48, genome_len=4, generations=80, mutation_sigma=0.2), seed=0).run(f)
+    assert res.best_fitness > -0.1
+    fb = lambda P: -((P - target) ** 2).sum(1)  # noqa: E731
+    res2 = N.Ga(N.GaConfig(population=48, genome_len=4, generations=80, crossover="blend", selection="rank"),
+                seed=1).run(fb, batched=True)
+    assert res2.best_fitness > -0.5
+    x, fx = N.es_one_plus_one(f, torch.zeros(4), iters=600)
+    assert fx > -1e-3
+    best, bf = N.Cmaes(N.CmaesConfig(dim=4, sigma=1.0, max_iters=150), seed=0).optimize(fb, batched=True)
+    assert bf > -1e-6
+    net = torch.nn.Linear(2, 1)
+    X = torch.randn(32, 2)
+    Y = X @ torch.tensor([[1.0], [-1.0]])
+    r = N.evolve_network(net, lambda m: -float(((m(X) - Y) ** 2).mean()),
+                         N.GaConfig(population=40, generations=60, mutation_sigma=0.2))
+    assert r.best_fitness > -0.05
+
+
+def test_cv_blocks_detection_and_segmentation():
+    from brain_b200.zoo import cv
+    torch.manual_seed(0)
+    net = cv.ResNetLite(3, (8, 16, 32), (1, 1, 1), 5)
+    x = torch.randn(2, 3, 32, 32)
+    feats = net.features(x)
+    assert [f.shape[-1] for f in feats] == [32, 16, 8] and net(x).shape == (2, 5)
+    pyr = cv.FPN([8, 16, 32], 16)(feats)
+    assert [p.shape[1] for p in pyr] == [16, 16, 16]
+    assert cv.DepthwiseSeparableConv(8, 12)(feats[0]).shape == (2, 12, 32, 32)
+    assert cv.GhostConv(8, 12)(feats[0]).shape == (2, 12, 32, 32)
+    assert cv.WSConv2d(8, 4, 3, padding=1)(feats[0]).shape == (2, 4, 32, 32)
+    boxes = torch.tensor([[0, 0, 10, 10], [1, 1, 11, 11], [20, 20, 30, 30.0]])
+    scores = torch.tensor([0.9, 0.8, 0.7])
+    assert cv.nms(boxes, scores, 0.5).tolist() == [0, 2]
+    iou = cv.compute_iou(boxes[:1], boxes[1:2])
+    assert float(iou) == pytest.approx(81 / 119, rel=1e-5)
+    anchors = cv.AnchorGenerator((16.0, 32.0), (0.5, 1.0, 2.0)).generate_grid_anchors(4, 5, 8)
+    assert anchors.shape == (4 * 5 * 6, 4)
+    gt = anchors[:10] + torch.tensor([1.0, -2.0, 3.0, 1.0])
+    torch.testing.assert_close(cv.decode_boxes(cv.encode_boxes(gt, anchors[:10]), anchors[:10]), gt, atol=1e-4, rtol=1e-4)
+    rois = cv.roi_align(torch.arange(64.0).view(1, 8, 8), torch.tensor([[0.0, 0.0, 8.0, 8.0]]), 4)
+    assert rois.shape == (1, 1, 4, 4)
+    head = cv.FcnHead(8, 3)
+    logits = head(feats[0], (32, 32))
+    tgt = torch.randint(0, 3, (2, 32, 32))
+    perfect = torch.nn.functional.one_hot(tgt, 3).permute(0, 3, 1, 2).float() * 50
+    assert float(cv.dice_loss(perfect, tgt)) < 1e-3 < float(cv.dice_loss(logits, tgt))
+    img = torch.rand(3, 16, 16)
+    assert cv.random_crop(img, (12, 12), padding=2).shape == (3, 12, 12)
+    assert cv.color_jitter(img).shape == img.shape
+    xm, ym = cv.mixup(torch.rand(4, 3, 8, 8), torch.eye(4))
+    xc, yc = cv.cutmix(torch.rand(4, 3, 8, 8), torch.eye(4))
+    torch.testing.assert_close(ym.sum(1), torch.ones(4))
+    torch.testing.assert_close(yc.sum(1), torch.ones(4))
