@@ -397,3 +397,97 @@ def test_cv_blocks_detection_and_segmentation():
     xc, yc = cv.cutmix(torch.rand(4, 3, 8, 8), torch.eye(4))
     torch.testing.assert_close(ym.sum(1), torch.ones(4))
     torch.testing.assert_close(yc.sum(1), torch.ones(4))
+
+
+# ------------------------------------------------------------------ graph IR / compile / ONNX
+def _mlp_graph():
+    from brain_b200.graph import GraphIr
+    torch.manual_seed(0)
+    g = GraphIr("mlp")
+    x = g.add_input("x", (4, 8))
+    w1, b1 = g.constant("w1", torch.randn(16, 8)), g.constant("b1", torch.randn(16))
+    w2 = g.constant("w2", torch.randn(8, 16))
+    h = g.add_node("linear", [x, w1, b1])
+    h = g.add_node("gelu", [h])
+    y = g.add_node("linear", [h, w2])
+    y = g.add_node("add", [y, x])
+    # redundant work the passes remove: a duplicate, a double transpose, dead code, foldable constants
+    dup = g.add_node("gelu", [g.add_node("linear", [x, w1, b1])])
+    t = g.add_node("transpose", [g.add_node("transpose", [y])])
+    c = g.add_node("mul", [g.constant("two", torch.tensor(2.0)), g.constant("three", torch.tensor(3.0))])
+    out = g.add_node("mul", [t, c])
+    g.add_node("exp", [dup])  # dead
+    g.mark_output(out)
+    return g
+
+
+def test_graph_passes_interpreter_and_plans():
+    from brain_b200 import graph as G
+    g = _mlp_graph()
+    assert G.verify(g) == []
+    G.infer_shapes(g)
+    x = torch.randn(4, 8)
+    ref = G.GraphInterpreter().run(g, [x])[0]
+    h = g.clone()
+    rep = G.optimize(h, 2)
+    assert rep.nodes_after < rep.nodes_before and G.verify(h) == []
+    ops = [n.op for n in h.nodes]
+    assert "transpose" not in ops and "exp" not in ops and ops.count("linear") == 2
+    torch.testing.assert_close(G.GraphInterpreter().run(h, [x])[0], ref)
+    assert rep.fusion.num_fused() >= 2  # linear+gelu, linear+add
+    d = G.diff_graphs(g, h)
+    assert d.removed_ops and not d.added_ops
+    G.infer_shapes(h)
+    assert G.estimate_flops(h) >= 2 * 4 * 16 * 8 + 2 * 4 * 8 * 16
+    plan = G.plan_memory(h)
+    assert len(plan.buffer_bytes) < len(plan.assignment)  # buffers were reused
+    ip = G.plan_inplace_operations(h)
+    assert ip.inplace
+    back = G.from_json(G.to_json(h))
+    torch.testing.assert_close(G.GraphInterpreter().run(back, [x])[0], ref)
+    assert G.to_dot(h).startswith('digraph "mlp"')
+    cache = G.JitCache()
+    cache.get_or_compile(g)
+    cache.get_or_compile(g)
+    assert cache.hits == 1 and cache.misses == 1
+
+
+def test_graph_from_fx_and_onnx_roundtrip(tmp_path):
+    from brain_b200 import graph as G
+    from brain_b200 import onnx as O
+
+    class Net(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.a = torch.nn.Linear(6, 12)
+            self.act = torch.nn.ReLU()
+            self.b = torch.nn.Linear(12, 3)
+
+        def forward(self, x):
+            return torch.tanh(self.b(self.act(self.a(x)))) * 2.0
+
+    torch.manual_seed(1)
+    net = Net()
+    x = torch.randn(5, 6)
+    g = G.from_fx(net, x)
+    torch.testing.assert_close(G.GraphInterpreter().run(g, [x])[0], net(x))
+    data = O.export_onnx(g, str(tmp_path / "m.onnx"))
+    assert O.check_model(data) == []
+    g2 = O.import_onnx(open(tmp_path / "m.onnx", "rb").read())
+    torch.testing.assert_close(G.GraphInterpreter().run(g2, [x])[0], net(x))
+    # extra op coverage through export -> import
+    h = G.GraphIr("ops")
+    a = h.add_input("a", (2, 3, 4))
+    t = h.add_node("transpose", [a], {"dim0": 1, "dim1": 2})
+    r = h.add_node("reshape", [t], {"shape": [2, 12]})
+    s = h.add_node("softmax", [r], {"dim": -1})
+    m = h.add_node("mean", [s], {"dim": 1, "keepdim": True})
+    q = h.add_node("rsqrt", [h.add_node("add", [m, h.constant("one", torch.tensor(1.0))])])
+    n = h.add_node("rms_norm", [r, h.constant("g", torch.ones(12))], {"eps": 1e-6})
+    h.mark_output(q, h.add_node("swiglu", [n]))
+    G.infer_shapes(h)
+    xa = torch.randn(2, 3, 4)
+    want = G.GraphInterpreter().run(h, [xa])
+    got = G.GraphInterpreter().run(O.import_onnx(O.export_onnx(h)), [xa])
+    for u, v in zip(got, want):
+        torch.testing.assert_close(u, v)
