@@ -14,6 +14,8 @@ Commands mirror the reference dispatcher (crates/brain-cli/src/impl.rs:8-62):
   model    parameter counts and shapes of the model presets.
   dataset  write a synthetic classification CSV.
   doctor   report the CUDA device, native libraries and versions.
+  space / chat / new   create, teach and talk to a BrainMind ``.bn`` (space_cmd.rs:16-200).
+  script   run a file of REPL statements; repl: interactive tensor REPL; init: scaffold a project.
 Exit codes: 0 ok, 1 error, 2 invalid usage, 3 I/O error (the reference's ExitCode values).
 """
 from __future__ import annotations
@@ -373,14 +375,70 @@ def build_parser() -> argparse.ArgumentParser:
     tr.add_argument("--seq", type=int, default=64)
     tr.add_argument("--lr", type=float, default=3e-4)
     tr.add_argument("--save", default="")
+    sp = sub.add_parser("space")
+    sp.add_argument("rest", nargs=argparse.REMAINDER)
+    ch = sub.add_parser("chat", aliases=["chatbot"])
+    ch.add_argument("rest", nargs=argparse.REMAINDER)
+    nw = sub.add_parser("new")
+    nw.add_argument("rest", nargs=argparse.REMAINDER)
+    sc = sub.add_parser("script")
+    sc.add_argument("file")
+    sub.add_parser("repl")
+    ini = sub.add_parser("init")
+    ini.add_argument("name", nargs="?", default="brain_project")
+    sub.add_parser("version")
     b = sub.add_parser("bench")
     b.add_argument("--collectives", action="store_true")
     b.add_argument("rest", nargs=argparse.REMAINDER)
     return p
 
 
+def cmd_space(a) -> int:
+    from .repl import space_command
+    return space_command(a.rest)
+
+
+def cmd_chat(a) -> int:
+    from .repl import space_command
+    return space_command(["chat"] + a.rest)
+
+
+def cmd_new(a) -> int:
+    from .repl import space_command
+    return space_command(["new"] + a.rest)
+
+
+def cmd_script(a) -> int:
+    from .repl import run_script
+    try:
+        with open(a.file) as f:
+            text = f.read()
+    except OSError as e:
+        print(f"error: could not read '{a.file}': {e}")
+        return IO_ERROR
+    return run_script(text)
+
+
+def cmd_repl(a) -> int:
+    from .repl import run_repl
+    return run_repl()
+
+
+def cmd_init(a) -> int:
+    from .repl import scaffold_project
+    return scaffold_project(a.name)
+
+
+def cmd_version(a) -> int:
+    import brain_b200
+    print(f"brain_b200 v{getattr(brain_b200, '__version__', '0.1.0')}")
+    return OK
+
+
 COMMANDS = {"make": cmd_make, "run": cmd_run, "check": cmd_check, "tensor": cmd_tensor, "convert": cmd_convert,
-            "model": cmd_model, "dataset": cmd_dataset, "doctor": cmd_doctor, "train": cmd_train, "bench": cmd_bench}
+            "model": cmd_model, "dataset": cmd_dataset, "doctor": cmd_doctor, "train": cmd_train, "bench": cmd_bench,
+            "space": cmd_space, "chat": cmd_chat, "chatbot": cmd_chat, "new": cmd_new, "script": cmd_script,
+            "repl": cmd_repl, "init": cmd_init, "version": cmd_version}
 
 
 def main(argv=None) -> int:

@@ -77,7 +77,7 @@ class BrainMind(torch.nn.Module):
             loss = torch.nn.functional.cross_entropy(logits.reshape(-1, self.V), chunk[:, 1:].reshape(-1))
             loss.backward()
             opt.step()
-            losses.append(float(loss))
+            losses.append(float(loss.detach()))
         for m in re.finditer(r"(\w[\w ]*?) is ([^.]+)\.", text):
             self.facts[m.group(1).strip().lower()] = m.group(2).strip()
         return losses

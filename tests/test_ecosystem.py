@@ -491,3 +491,52 @@ def test_graph_from_fx_and_onnx_roundtrip(tmp_path):
     got = G.GraphInterpreter().run(O.import_onnx(O.export_onnx(h)), [xa])
     for u, v in zip(got, want):
         torch.testing.assert_close(u, v)
+
+
+# ------------------------------------------------------------------ CLI: repl / script / init / space
+def test_cli_repl_script_init_and_space(tmp_path, capsys):
+    import io
+    import os
+    import subprocess
+    import sys
+
+    import importlib
+
+    from brain_b200.cli.repl import ReplState, run_repl
+    cli = importlib.import_module("brain_b200.cli.main")
+
+    lines = []
+    st = ReplState(device="cpu", out=lines.append)
+    st.eval_line("a = ones(2, 3)")
+    st.eval_line("b = add(mul(a, 2), ones(2, 3))")
+    st.eval_line("sum(b)")
+    assert lines[-1] == "ans: [] = 18"
+    st.eval_line("c = matmul(b, transpose(a))")
+    assert lines[-1] == "c = [2, 2]"
+    st.eval_line(":vars")
+    assert "  c: [2, 2]" in lines
+    out = []
+    run_repl(io.StringIO("x = zeros(4)\nfoo(x)\n:quit\ny = ones(1)\n"), out=out.append)
+    assert any("unknown function 'foo'" in s for s in out) and out[-1] == "Goodbye!"
+    script = tmp_path / "s.bn"
+    script.write_text("# comment\nx = randn(3, 3)\n\ny = add(x, x)\n")
+    assert cli.main(["script", str(script)]) == 0
+    script.write_text("x = ones(2)\ny = sub(x)\n")
+    assert cli.main(["script", str(script)]) == 1
+    assert cli.main(["script", str(tmp_path / "missing.bn")]) == 3
+    proj = tmp_path / "proj"
+    assert cli.main(["init", str(proj)]) == 0
+    assert (proj / "brain.toml").exists() and (proj / "src" / "model.py").exists()
+    assert cli.main(["init", str(proj)]) == 3
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "train.py"], cwd=proj, capture_output=True, text=True, timeout=300,
+                       env={**os.environ, "PYTHONPATH": root, "CUDA_VISIBLE_DEVICES": ""})
+    assert r.returncode == 0, r.stderr[-2000:]
+    teach = tmp_path / "t.txt"
+    teach.write_text("the sky is blue. the grass is green.\n" * 4)
+    bn = tmp_path / "mind.bn"
+    assert cli.main(["new", str(bn), "--teach", str(teach), "--steps", "5"]) == 0 and bn.exists()
+    assert cli.main(["chat", str(bn), "--message", "hello"]) == 0
+    assert "> hello" in capsys.readouterr().out
+    assert cli.main(["space"]) == 2
+    assert cli.main(["version"]) == 0
