@@ -135,7 +135,7 @@ def _matmul(a, b):
     if a.is_cuda and a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16 and a.dim() >= 2 and b.dim() == 2:
         from . import ops
         lead = a.shape[:-1]
-        return ops.gemm(a.reshape(-1, a.shape[-1]), b.t()).reshape(*lead, b.shape[-1])
+        return ops.gemm(a.reshape(-1, a.shape[-1]), b).reshape(*lead, b.shape[-1])
     return torch.matmul(a, b)
 
 

@@ -540,3 +540,46 @@ def test_cli_repl_script_init_and_space(tmp_path, capsys):
     assert "> hello" in capsys.readouterr().out
     assert cli.main(["space"]) == 2
     assert cli.main(["version"]) == 0
+
+
+# ------------------------------------------------------------------ benchmark harness
+def test_bench_harness_statistics_welch_baseline_reports(tmp_path):
+    from brain_b200.bench import harness as H
+    s = H.Statistics.compute([1, 2, 3, 4, 100])
+    assert s.median == 3 and s.min == 1 and s.max == 100 and s.p50 == 3 and s.iqr == 2
+    assert s.ci_95_lower < s.mean < s.ci_95_upper and s.skewness > 0
+    assert H.Statistics.trimmed_mean([1, 2, 3, 4, 100], 20) == 3
+    # Welch: scipy's ttest_ind(equal_var=False) is the oracle
+    from scipy import stats as st
+    a, b = [10.0, 11.0, 9.5, 10.2, 10.8], [12.0, 12.5, 11.8, 13.1, 12.2, 12.9]
+    t, p = H.welch_t_test(a, b)
+    ref = st.ttest_ind(b, a, equal_var=False)
+    assert abs(t - ref.statistic) < 1e-9 and abs(p - ref.pvalue) < 1e-9
+    cfg = H.BenchConfig("op", 0, 5)
+    base, slow = H.BenchResult(cfg, [100.0, 101, 99, 100, 100.5]), H.BenchResult(cfg, [120.0, 121, 119, 120, 122])
+    c = H.compare_runs(base, slow)
+    assert c.verdict == "regression" and c.percent_change > 15
+    store = H.BaselineStore(str(tmp_path / "b.json"))
+    store.add(base)
+    store.save()
+    store2 = H.BaselineStore(str(tmp_path / "b.json"))
+    with pytest.raises(RuntimeError, match="regressed"):
+        store2.evaluate_regressions([slow], 5.0)
+    assert store2.evaluate_regressions([base], 5.0)[0].verdict == "no_change"
+    r = H.Runner.run_benchmark(H.BenchConfig("sleep", 1, 4), lambda: sum(range(1000)))
+    assert r.stats.count == 4 and r.mean_nanos() > 0
+    sw = H.Runner.run_sweep("sum", [10, 1000], lambda n: (lambda: sum(range(n))), warmup_iters=1, measure_iters=3)
+    assert len(sw) == 2
+    for fmt in (H.format_console, H.format_markdown, H.format_csv, H.format_json, H.format_html):
+        assert "sleep" in fmt([r])
+    prom = H.PrometheusExporter.export([r])
+    assert 'brain_bench_mean_seconds{name="sleep"}' in prom
+    assert "brain.bench.mean_ns" in H.OpenTelemetryExporter.export([r])
+    h = H.LogHistogram()
+    for v in range(1, 10001):
+        h.record(v * 1000)
+    assert h.count() == 10000 and abs(h.percentile(50) / 5e6 - 1) < 0.2 and abs(h.percentile(99) / 9.9e6 - 1) < 0.2
+    assert H.HardwareInfo.probe().cpu_count > 0
+    assert H.EnergyEstimator.estimate_joules(2.0, 500.0) == 1000.0
+    suite = H.KernelSuite.run(n=128, iters=2, device="cpu")
+    assert [x.config.name for x in suite] == ["gemm", "rms_norm", "softmax_cross_entropy"] and suite[0].tflops() > 0
