@@ -61,7 +61,7 @@ def quantize_tensor(x: torch.Tensor, dtype: QuantDType = QuantDType.INT8, symmet
         red = 1
     if symmetric:
         amax = xf.abs().amax(red, keepdim=True).clamp_min(1e-12)
-        scale = amax / max(abs(qmin), qmax)
+        scale = amax / qmax  # symmetric: +amax maps to qmax exactly (amax / 128 would clip it)
         zp = torch.zeros_like(scale)
     else:
         lo, hi = xf.amin(red, keepdim=True), xf.amax(red, keepdim=True)
@@ -162,7 +162,7 @@ class MinMaxObserver:
     def scale_zp(self, dtype=QuantDType.INT8, symmetric=True):
         qmin, qmax = dtype.qrange()
         if symmetric:
-            return max(abs(self.lo), abs(self.hi), 1e-12) / max(abs(qmin), qmax), 0
+            return max(abs(self.lo), abs(self.hi), 1e-12) / qmax, 0
         s = max(self.hi - self.lo, 1e-12) / (qmax - qmin)
         return s, round(qmin - self.lo / s)
 

@@ -583,3 +583,50 @@ def test_bench_harness_statistics_welch_baseline_reports(tmp_path):
     assert H.EnergyEstimator.estimate_joules(2.0, 500.0) == 1000.0
     suite = H.KernelSuite.run(n=128, iters=2, device="cpu")
     assert [x.config.name for x in suite] == ["gemm", "rms_norm", "softmax_cross_entropy"] and suite[0].tflops() > 0
+
+
+# ------------------------------------------------------------------ export
+def test_export_formats_zip_quant_and_bn_conversion(tmp_path):
+    import json as _json
+    import zipfile
+
+    from brain_b200 import export as E
+    from brain_b200 import graph as G
+    from brain_b200.checkpoint.formats import BrainModelFile
+    from brain_b200.utils.safetensors import load_safetensors
+
+    g = _mlp_graph()
+    G.optimize(g, 2)
+    G.infer_shapes(g)
+    x = torch.randn(4, 8)
+    s = E.export_all(g, str(tmp_path / "out"), example_inputs=[x])
+    assert set(s.files) == {"onnx", "webnn", "tflite", "coreml"} and not s.skipped
+    web = _json.loads(open(s.files["webnn"]).read())
+    assert [o["op"] for o in web["operations"]][:2] == ["gemm", "gelu"]
+    tfl = _json.loads(open(s.files["tflite"]).read())
+    assert {c["builtin_code"] for c in tfl["operator_codes"]} >= {"FULLY_CONNECTED", "GELU"}
+    with zipfile.ZipFile(s.files["coreml"]) as z:
+        assert set(z.namelist()) == {"model.mil", "weights.bin", "manifest.json"}
+        assert "linear(" in z.read("model.mil").decode()
+    h = G.GraphIr("norm")
+    a = h.add_input("a", (2, 4))
+    h.mark_output(h.add_node("rms_norm", [a]))
+    rep = E.supported_ops_report(h, E.ExportFormat.TFLITE)
+    assert not rep.ok() and rep.unsupported == ["rms_norm"]
+    s2 = E.export_all(h, str(tmp_path / "out2"))
+    assert "tflite" in s2.skipped and "onnx" in s2.files
+    with pytest.raises(E.ExportError):
+        E.verify_export(torch.ones(3), torch.zeros(3), 0.5)
+    w = {"w": torch.randn(16, 32), "b": torch.randn(16)}
+    err = E.export_quantized_safetensors(w, str(tmp_path / "q.safetensors"))
+    q, meta = load_safetensors(str(tmp_path / "q.safetensors"))
+    assert q["w"].dtype == torch.int8 and q["w.scale"].shape == (16,) and meta["format"] == "brain-int8"
+    assert err["w"] <= float(w["w"].abs().max()) / 127 * 0.51
+    m = BrainModelFile("net").with_meta("arch", "mlp")
+    m.add_tensor("layer.weight", torch.randn(3, 2, dtype=torch.float64))
+    m.save_file(str(tmp_path / "m.bn"))
+    E.convert_bn_to_safetensors(str(tmp_path / "m.bn"), str(tmp_path / "m.safetensors"))
+    r = E.convert_safetensors_to_bn(str(tmp_path / "m.safetensors"), str(tmp_path / "m2.bn"))
+    m2 = BrainModelFile.load_file(str(tmp_path / "m2.bn"))
+    assert r.num_tensors == 1 and m2.name == "net" and m2.metadata["arch"] == "mlp"
+    torch.testing.assert_close(m2.archive.get("layer.weight").double(), m.archive.get("layer.weight").double())
