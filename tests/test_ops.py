@@ -256,7 +256,8 @@ def test_flash_attention_tcgen05_strided_qkv():
 def test_norm_linear_rope_matches_reference(S, Hq, Hkv, D):
     """RMSNorm -> QKV GEMM with RoPE on the q/k heads (GEMM epilogue where the shapes allow): forward and
     gradients against a float32 restatement."""
-    from brain_b200.ops import linear as lin
+    import importlib
+    lin = importlib.import_module("brain_b200.ops.linear")
     B, d = 2, 256
     N = (Hq + 2 * Hkv) * D
     x = rnd(B, S, d, seed=40)
