@@ -101,10 +101,11 @@ class _NormLinearFn(torch.autograd.Function):
         x2, nw, w, rstd, table = ctx.saved_tensors
         dy2 = rows2d(dy)
         if ctx.rope is not None:
-            # gradient w.r.t. the unrotated projection: the inverse rotation of its q and k columns
-            # (dy is this op's own gradient buffer, produced by the attention backward)
+            # gradient w.r.t. the unrotated projection: the inverse rotation of its q and k columns, on a
+            # copy (autograd may hand the caller's own gradient tensor to this backward, and rotating
+            # that in place would change it for every other reader)
             rot_heads, hd, S, off = ctx.rope
-            dy2 = dy2.contiguous() if dy2.stride(1) != 1 else dy2
+            dy2 = dy2.clone(memory_format=torch.contiguous_format)
             apply_rope_(dy2.view(-1, S, w.shape[0] // hd, hd)[:, :, :rot_heads], table, None, off, inverse=True)
         xn, _, _, _ = _norms._fwd(_norms._RMS, x2, nw, None, ctx.eps)  # recompute
         dxn = gemm(dy2, w)
