@@ -31,7 +31,7 @@ NVCC_FLAGS = ARCH + [
     "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
     "-Xcompiler", "-fvisibility=hidden", "-DNDEBUG", "-Xptxas", "-warn-spills",
 ]
-CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-Wall", "-Wno-unused-function"]
+CXX_FLAGS = ["-O3", "-std=c++17", "-fPIC", "-fvisibility=hidden", "-pthread", "-Wall", "-Wno-unused-function"]
 
 # library name -> list of sources (relative to csrc/). Every CUDA library links host_utils.cu.
 LIBRARIES = {
@@ -41,9 +41,9 @@ LIBRARIES = {
     ],
     "brain_comm": ["host_utils.cu", "comm.cu"],
 }
-# Host-only C++ libraries (g++): the checkpoint codec and the runtime helpers.
+# Host-only C++ libraries (g++): the checkpoint codec and the native token loader.
 CXX_LIBRARIES = {
-    "brain_runtime": ["codec.cpp"],
+    "brain_runtime": ["codec.cpp", "loader.cpp"],
 }
 
 
@@ -112,7 +112,7 @@ def build(force: bool = False, jobs: int | None = None, only: list[str] | None =
         objs = [os.path.join(OBJDIR, os.path.basename(s) + ".o") for s in srcs]
         so = os.path.join(LIBDIR, f"lib{name}.so")
         if force or _needs_build(so, objs):
-            _run(["g++", "-shared", "-fPIC", "-o", so] + objs)
+            _run(["g++", "-shared", "-fPIC", "-pthread", "-o", so] + objs)
         outs.append(so)
     return outs
 

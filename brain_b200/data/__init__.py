@@ -198,3 +198,289 @@ def random_split(n: int, fractions, seed: int = 0):
 def write_token_file(path: str, tokens, dtype=np.uint16) -> None:
     os.makedirs(os.path.dirname(path) or ".", exist_ok=True)
     np.asarray(tokens, dtype=dtype).tofile(path)
+
+
+# ------------------------------------------------------------------ native token loader
+_LOADER_SIGS = {
+    "brain_loader_open": ("brain_runtime", "piillliiiillp"),
+    "brain_loader_next": ("brain_runtime", "ppp"),
+    "brain_loader_fill": ("brain_runtime", "plp"),
+    "brain_loader_stats": ("brain_runtime", "pp"),
+    "brain_loader_close": ("brain_runtime", "p"),
+}
+_LOADER_ERRORS = {-10: "bad argument", -11: "I/O error", -12: "timed out waiting for a batch", -13: "closed"}
+
+
+def _loader_fn(name):
+    from .. import _native
+
+    return _native.fn(name)
+
+
+def _register_loader():
+    from .. import _native
+
+    _native.register(_LOADER_SIGS)
+
+
+_register_loader()
+
+
+def splitmix64_window_starts(seed: int, batch_index: int, rank: int, world: int, batch: int, seq: int,
+                             n_tokens: int) -> list[int]:
+    """Window starts of one batch, as the native loader draws them (the test oracle)."""
+    m = (1 << 64) - 1
+    st = (seed * 0x9E3779B97F4A7C15 + batch_index * world + rank) & m
+    out = []
+    for _ in range(batch):
+        st = (st + 0x9E3779B97F4A7C15) & m
+        z = st
+        z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & m
+        z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & m
+        z ^= z >> 31
+        out.append(z % (n_tokens - seq))
+    return out
+
+
+class NativeTokenLoader:
+    """Random [batch, seq + 1] windows of a memory-mapped token file, assembled by C++ worker threads
+    into a bounded ring (``depth`` batches ahead: back-pressure), copied into a pinned buffer per call.
+    Iterating yields (inputs, targets) int64 CPU tensors; ``device=`` moves them with a non-blocking
+    copy. Rank r of ``world`` draws its own stream; ``start_batch`` resumes a run at that batch."""
+
+    def __init__(self, path: str, batch: int, seq: int, seed: int = 0, token_dtype=np.uint16, rank: int = 0,
+                 world: int = 1, workers: int = 2, depth: int = 4, start_batch: int = 0, timeout_s: float = 60.0,
+                 pin_memory: bool | None = None, device=None):
+        import ctypes
+
+        tb = np.dtype(token_dtype).itemsize
+        h = ctypes.c_void_p()
+        rc = _loader_fn("brain_loader_open")(path.encode(), tb, 8, batch, seq, seed, rank, world, workers, depth,
+                                              start_batch, int(timeout_s * 1000), ctypes.byref(h))
+        if rc != 0:
+            raise RuntimeError(f"brain_loader_open({path}) failed: {_LOADER_ERRORS.get(rc, rc)}")
+        self._h, self.batch, self.seq, self.device = h, batch, seq, device
+        pin = torch.cuda.is_available() if pin_memory is None else pin_memory
+        self._buf = torch.empty((batch, seq + 1), dtype=torch.int64, pin_memory=pin)
+        self.last_batch_index = start_batch - 1
+
+    def next(self):
+        import ctypes
+
+        if self._h is None:
+            raise RuntimeError("loader is closed")
+        idx = ctypes.c_int64(-1)
+        rc = _loader_fn("brain_loader_next")(self._h, self._buf.data_ptr(), ctypes.byref(idx))
+        if rc != 0:
+            raise RuntimeError(f"brain_loader_next failed: {_LOADER_ERRORS.get(rc, rc)}")
+        self.last_batch_index = idx.value
+        w = self._buf
+        if self.device is not None:
+            w = w.to(self.device, non_blocking=True)
+        else:
+            w = w.clone()
+        return w[:, :-1], w[:, 1:]
+
+    def batch_at(self, b: int) -> torch.Tensor:
+        out = torch.empty((self.batch, self.seq + 1), dtype=torch.int64)
+        _loader_fn("brain_loader_fill")(self._h, b, out.data_ptr())
+        return out
+
+    def stats(self) -> dict:
+        arr = (__import__("ctypes").c_int64 * 5)()
+        _loader_fn("brain_loader_stats")(self._h, arr)
+        return {"produced": arr[0], "consumed": arr[1], "consumer_wait_s": arr[2] * 1e-9,
+                "producer_wait_s": arr[3] * 1e-9, "tokens": arr[4]}
+
+    def checkpoint(self) -> "PipelineCheckpoint":
+        return PipelineCheckpoint(0, self.last_batch_index + 1)
+
+    def __iter__(self):
+        while True:
+            yield self.next()
+
+    def close(self) -> None:
+        if self._h is not None:
+            _loader_fn("brain_loader_close")(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ------------------------------------------------------------------ samples, streams, caching, metrics
+class Sample:
+    """One record: data tensor, optional label and string metadata (brain-data core.rs:10-40)."""
+
+    def __init__(self, id: int, data, label=None, meta=None):
+        self.id, self.data, self.label, self.meta = id, data, label, dict(meta or {})
+
+    def with_label(self, label) -> "Sample":
+        self.label = label
+        return self
+
+    def with_meta(self, k, v) -> "Sample":
+        self.meta[k] = v
+        return self
+
+
+def pad_collate(samples, pad_value: float = 0.0):
+    """Pads variable-length [L, ...] sample tensors to the longest along dim 0 and stacks them;
+    returns (batch, lengths[, labels])."""
+    datas = [s.data if isinstance(s, Sample) else s for s in samples]
+    L = max(d.shape[0] for d in datas)
+    out = datas[0].new_full((len(datas), L) + tuple(datas[0].shape[1:]), pad_value)
+    for i, d in enumerate(datas):
+        out[i, :d.shape[0]] = d
+    lengths = torch.tensor([d.shape[0] for d in datas])
+    if samples and isinstance(samples[0], Sample) and samples[0].label is not None:
+        return out, lengths, default_collate([s.label for s in samples])
+    return out, lengths
+
+
+class StreamDataset:
+    """Iterable dataset over a generator factory; ``shard(rank, world)`` keeps every world-th record."""
+
+    def __init__(self, make_iter, rank: int = 0, world: int = 1):
+        self.make_iter, self.rank, self.world = make_iter, rank, world
+
+    def shard(self, rank: int, world: int) -> "StreamDataset":
+        return StreamDataset(self.make_iter, rank, world)
+
+    def __iter__(self):
+        for i, x in enumerate(self.make_iter()):
+            if i % self.world == self.rank:
+                yield x
+
+    def batches(self, batch_size: int, drop_last: bool = False, collate=default_collate):
+        buf = []
+        for x in self:
+            buf.append(x)
+            if len(buf) == batch_size:
+                yield collate(buf)
+                buf = []
+        if buf and not drop_last:
+            yield collate(buf)
+
+
+class ConcatDataset(Dataset):
+    def __init__(self, *datasets):
+        self.ds = datasets
+        self.cum = np.cumsum([len(d) for d in datasets]).tolist()
+
+    def __len__(self):
+        return self.cum[-1] if self.cum else 0
+
+    def __getitem__(self, i):
+        k = int(np.searchsorted(self.cum, i, side="right"))
+        return self.ds[k][i - (self.cum[k - 1] if k else 0)]
+
+
+class SampleCache:
+    """LRU cache of samples by index with hit / miss counters (brain-data caching.rs:10-40)."""
+
+    def __init__(self, capacity: int):
+        import collections
+
+        self.capacity, self._d = capacity, collections.OrderedDict()
+        self.hits = self.misses = 0
+
+    def get(self, i):
+        if i in self._d:
+            self._d.move_to_end(i)
+            self.hits += 1
+            return self._d[i]
+        self.misses += 1
+        return None
+
+    def put(self, i, v) -> None:
+        self._d[i] = v
+        self._d.move_to_end(i)
+        while len(self._d) > self.capacity:
+            self._d.popitem(last=False)
+
+
+class CachedDataset(Dataset):
+    def __init__(self, ds, capacity: int = 1024):
+        self.ds, self.cache = ds, SampleCache(capacity)
+
+    def __len__(self):
+        return len(self.ds)
+
+    def __getitem__(self, i):
+        v = self.cache.get(i)
+        if v is None:
+            v = self.ds[i]
+            self.cache.put(i, v)
+        return v
+
+
+class PipelineMetrics:
+    """Samples / batches / seconds of a data pipeline and the consumer's time spent waiting on it."""
+
+    def __init__(self):
+        self.samples = self.batches = 0
+        self.wait_s = 0.0
+        self.t0 = None
+
+    def wrap(self, it):
+        import time
+
+        self.t0 = time.perf_counter()
+        it = iter(it)
+        while True:
+            t = time.perf_counter()
+            try:
+                b = next(it)
+            except StopIteration:
+                return
+            self.wait_s += time.perf_counter() - t
+            self.batches += 1
+            first = b[0] if isinstance(b, (tuple, list)) else b
+            self.samples += int(first.shape[0]) if hasattr(first, "shape") and first.dim() else 1
+            yield b
+
+    def throughput(self) -> float:
+        import time
+
+        el = time.perf_counter() - self.t0 if self.t0 else 0.0
+        return self.samples / el if el > 0 else 0.0
+
+
+class PipelineCheckpoint:
+    """Position of a data pipeline (epoch, next sample / batch offset) for resuming."""
+
+    def __init__(self, epoch: int = 0, sample_offset: int = 0):
+        self.epoch, self.sample_offset = epoch, sample_offset
+
+    def to_dict(self) -> dict:
+        return {"epoch": self.epoch, "sample_offset": self.sample_offset}
+
+    @classmethod
+    def from_dict(cls, d) -> "PipelineCheckpoint":
+        return cls(int(d["epoch"]), int(d["sample_offset"]))
+
+
+def rle_encode(data) -> list[tuple[int, int]]:
+    out = []
+    for v in data:
+        if out and out[-1][0] == v:
+            out[-1] = (v, out[-1][1] + 1)
+        else:
+            out.append((v, 1))
+    return out
+
+
+def rle_decode(runs) -> list:
+    return [v for v, n in runs for _ in range(n)]
+
+
+def delta_encode(data) -> list[int]:
+    return [data[0]] + [data[i] - data[i - 1] for i in range(1, len(data))] if len(data) else []
+
+
+def delta_decode(d) -> list[int]:
+    return np.cumsum(d).tolist() if len(d) else []

@@ -2,6 +2,7 @@
 model zoo (RNN, CNN, GNN, diffusion, GAN, RL, audio, neuroevolution), the graph IR, the benchmark
 harness and the CLI commands for BrainMind."""
 import math
+import os
 
 import pytest
 import torch
@@ -630,3 +631,98 @@ def test_export_formats_zip_quant_and_bn_conversion(tmp_path):
     m2 = BrainModelFile.load_file(str(tmp_path / "m2.bn"))
     assert r.num_tensors == 1 and m2.name == "net" and m2.metadata["arch"] == "mlp"
     torch.testing.assert_close(m2.archive.get("layer.weight").double(), m.archive.get("layer.weight").double())
+
+
+# ------------------------------------------------------------------ data: native loader, streams, datasets
+def test_native_token_loader_matches_oracle_and_resumes(tmp_path):
+    import numpy as np
+    from brain_b200 import data as D
+    toks = np.random.default_rng(0).integers(0, 60000, size=50000).astype(np.uint16)
+    p = str(tmp_path / "tok.bin")
+    D.write_token_file(p, toks)
+    L = D.NativeTokenLoader(p, batch=3, seq=16, seed=5, rank=1, world=2, workers=3, depth=2, pin_memory=False)
+    seen = []
+    for b in range(8):
+        x, y = L.next()
+        starts = D.splitmix64_window_starts(5, b, 1, 2, 3, 16, len(toks))
+        ref = torch.stack([torch.from_numpy(toks[s:s + 17].astype(np.int64)) for s in starts])
+        assert torch.equal(x, ref[:, :-1]) and torch.equal(y, ref[:, 1:])
+        seen.append(ref)
+    ck = L.checkpoint()
+    st = L.stats()
+    assert st["consumed"] == 8 and st["tokens"] == len(toks) and ck.sample_offset == 8
+    L.close()
+    R = D.NativeTokenLoader(p, batch=3, seq=16, seed=5, rank=1, world=2, start_batch=ck.sample_offset, pin_memory=False)
+    x, _ = R.next()
+    ref = torch.stack([torch.from_numpy(toks[s:s + 17].astype(np.int64))
+                       for s in D.splitmix64_window_starts(5, 8, 1, 2, 3, 16, len(toks))])
+    assert torch.equal(x, ref[:, :-1]) and torch.equal(R.batch_at(0), seen[0])
+    R.close()
+    other = D.NativeTokenLoader(p, batch=3, seq=16, seed=5, rank=0, world=2, pin_memory=False)
+    assert not torch.equal(other.batch_at(0), seen[0])
+    other.close()
+    with pytest.raises(RuntimeError, match="I/O"):
+        D.NativeTokenLoader(str(tmp_path / "missing.bin"), batch=1, seq=4)
+
+
+def test_streams_cache_metrics_and_codecs():
+    from brain_b200 import data as D
+    s = D.StreamDataset(lambda: iter(range(10)))
+    assert list(s.shard(1, 3)) == [1, 4, 7]
+    assert [b.tolist() for b in s.batches(4)] == [[0, 1, 2, 3], [4, 5, 6, 7], [8, 9]]
+    c = D.CachedDataset(D.SyntheticTokens(100, 8, 10), capacity=2)
+    a = c[0]
+    assert torch.equal(c[0][0], a[0]) and c.cache.hits == 1 and c.cache.misses == 1
+    c[1], c[2], c[0]
+    assert c.cache.misses == 4  # index 0 was evicted
+    m = D.PipelineMetrics()
+    n = sum(1 for _ in m.wrap(D.DataLoader(D.SyntheticTokens(100, 8, 10), batch_size=4)))
+    assert n == 3 and m.samples == 10 and m.throughput() > 0
+    x, lengths = D.pad_collate([torch.ones(2), torch.ones(4), torch.ones(3)], -1.0)
+    assert x.shape == (3, 4) and lengths.tolist() == [2, 4, 3] and float(x[0, 3]) == -1.0
+    cat = D.ConcatDataset(D.SyntheticTokens(100, 4, 3, seed=1), D.SyntheticTokens(100, 4, 2, seed=2))
+    assert len(cat) == 5 and torch.equal(cat[4][0], D.SyntheticTokens(100, 4, 2, seed=2)[1][0])
+    assert D.rle_decode(D.rle_encode([1, 1, 2, 2, 2, 3])) == [1, 1, 2, 2, 2, 3]
+    assert D.delta_decode(D.delta_encode([5, 7, 7, 10])) == [5, 7, 7, 10]
+    ck = D.PipelineCheckpoint.from_dict(D.PipelineCheckpoint(2, 40).to_dict())
+    assert (ck.epoch, ck.sample_offset) == (2, 40)
+
+
+def test_dataset_library(tmp_path):
+    import numpy as np
+    from brain_b200.data import datasets as DS
+    from brain_b200.zoo.audio import write_wav
+    csvp = tmp_path / "t.csv"
+    csvp.write_text("a,b,label\n1,2,0\n3,4,1\n5,6,1\n")
+    ds = DS.TabularDataset(str(csvp), label_column="label")
+    assert len(ds) == 3 and ds.feature_names == ["a", "b"] and ds[1][1].item() == 1
+    st = DS.dataset_stats(ds)
+    assert st.class_counts == {0: 1, 1: 2} and st.imbalance_ratio() == 2.0
+    torch.testing.assert_close(st.feature_mean, torch.tensor([3.0, 4.0]))
+    txt = tmp_path / "t.txt"
+    txt.write_text("pos\tgood movie\nneg\tbad film\n\npos\tgreat\n")
+    tl = DS.TextLineDataset(str(txt), label_sep="\t")
+    assert len(tl) == 3 and tl.label_names == ["neg", "pos"] and tl[1] == ("bad film", 0)
+    for c in ("cat", "dog"):
+        os.makedirs(tmp_path / "img" / c)
+        np.save(tmp_path / "img" / c / "0.npy", np.full((4, 4, 3), 255 if c == "dog" else 0, np.uint8))
+    im = DS.ImageArrayDataset(str(tmp_path / "img"), transform=DS.Compose(DS.Normalize([0.5] * 3, [0.5] * 3)))
+    x, k = im[1]
+    assert x.shape == (3, 4, 4) and k == 1 and float(x.mean()) == 1.0
+    os.makedirs(tmp_path / "aud" / "beep")
+    write_wav(str(tmp_path / "aud" / "beep" / "a.wav"), torch.sin(torch.arange(1600.0)), 16000)
+    au = DS.AudioDataset(str(tmp_path / "aud"), sample_rate=8000)
+    assert au[0][0].numel() == 800
+    sp = DS.random_split_indices(10, 0.6, 0.2)
+    assert len(sp.train) == 6 and len(sp.val) == 2 and sorted(sp.train + sp.val + sp.test) == list(range(10))
+    folds = DS.k_fold_split_indices(10, 3)
+    assert sorted(sum((v for _, v in folds), [])) == list(range(10))
+    tr, va = DS.stratified_split_indices([0] * 10 + [1] * 10, 0.7)
+    assert len(tr) == 14 and len(va) == 6
+    bal = DS.balance_indices([0] * 5 + [1] * 2)
+    assert len(bal) == 10
+    assert DS.WorkerPool(3).map(lambda v: v * v, range(5)) == [0, 1, 4, 9, 16]
+    assert "csv" in DS.list_datasets() and len(DS.create_dataset("synthetic_tokens", vocab_size=10, seq_len=4,
+                                                                  num_samples=3)) == 3
+    with pytest.raises(KeyError):
+        DS.create_dataset("nope")
