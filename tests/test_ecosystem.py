@@ -726,3 +726,91 @@ def test_dataset_library(tmp_path):
                                                                   num_samples=3)) == 3
     with pytest.raises(KeyError):
         DS.create_dataset("nope")
+
+
+# ------------------------------------------------------------------ device / BLAS / pruning / pipelines / parsers
+def test_device_blas_and_quantized_tensor():
+    from brain_b200.device import (CpuBackend, Device, DeviceGuard, DeviceList, DeviceType, QuantizedTensor, blas,
+                                   backend_for)
+    d = Device.parse("cuda:3")
+    assert d.type == DeviceType.CUDA and d.index == 3 and d.name() == "cuda:3" and d.is_accelerator()
+    assert Device.parse("CPU").is_cpu() and DeviceType.METAL.has_unified_memory() and not DeviceType.CUDA.has_unified_memory()
+    with pytest.raises(ValueError):
+        Device.parse("quantum:0")
+    with pytest.raises(RuntimeError):
+        Device.vulkan(0).to_torch()
+    assert DeviceList().cpu() == Device.cpu() and Device.cpu().is_available()
+    with DeviceGuard("cpu") as dev:
+        assert dev.is_cpu()
+    assert isinstance(backend_for("cpu"), CpuBackend)
+    x, y = torch.tensor([1.0, 2.0, 3.0]), torch.tensor([4.0, 5.0, 6.0])
+    assert float(blas.dot(x, y)) == 32.0 and blas.iamax(torch.tensor([1.0, -7.0, 3.0])) == 1
+    assert blas.axpy(2.0, x, y.clone()).tolist() == [6.0, 9.0, 12.0]
+    assert abs(float(blas.nrm2(x)) - 14 ** 0.5) < 1e-6 and float(blas.asum(-x)) == 6.0
+    a, b = torch.randn(3, 4), torch.randn(5, 4)
+    c = torch.randn(3, 5)
+    torch.testing.assert_close(blas.gemm(a, b, c.clone(), 2.0, 0.5, trans_b=True), 2 * a @ b.t() + 0.5 * c)
+    torch.testing.assert_close(blas.gemv(1.0, a, torch.ones(4), 0.0, torch.zeros(3)), a.sum(1))
+    torch.testing.assert_close(blas.ger(1.0, torch.ones(2), torch.ones(3), torch.zeros(2, 3)), torch.ones(2, 3))
+    p, q = torch.tensor([1.0]), torch.tensor([0.0])
+    blas.rot(p, q, 0.0, 1.0)
+    assert p.item() == 0.0 and q.item() == -1.0
+    t = torch.linspace(-2, 5, 50)
+    qt = QuantizedTensor.quantize(t)
+    assert qt.data.dtype == torch.int8 and float((qt.dequantize() - t).abs().max()) <= qt.scale * 0.51
+    qs = QuantizedTensor.quantize(t, symmetric=True)
+    assert qs.zero_point == 0 and float((qs.dequantize() - t).abs().max()) <= qs.scale * 0.51
+
+
+def test_pruning_masks_and_module_pruning():
+    from brain_b200.nn.pruning import PruningMask, prune_module, remove_pruning
+    w = torch.tensor([[0.1, -3.0], [0.5, 2.0]])
+    m = PruningMask.from_magnitude(w, 0.5)
+    assert m.apply(w).tolist() == [[0.0, -3.0], [0.0, 2.0]] and m.sparsity() == 0.5
+    rows = PruningMask.structured_rows(torch.tensor([[1.0, 1.0], [5.0, 5.0], [0.1, 0.0]]), 1 / 3)
+    assert rows.mask.tolist() == [[True, True], [True, True], [False, False]]
+    net = torch.nn.Sequential(torch.nn.Linear(8, 16), torch.nn.ReLU(), torch.nn.Linear(16, 4))
+    masks = prune_module(net, 0.75, global_=True)
+    zeros = sum(int((p == 0).sum()) for n, p in net.named_parameters() if n in masks)
+    total = sum(p.numel() for n, p in net.named_parameters() if n in masks)
+    assert abs(zeros / total - 0.75) < 0.02
+    opt = torch.optim.SGD(net.parameters(), lr=0.5)
+    net(torch.randn(4, 8)).sum().backward()
+    opt.step()
+    net(torch.randn(1, 8))  # the hook re-applies the masks
+    assert sum(int((p == 0).sum()) for n, p in net.named_parameters() if n in masks) >= zeros
+    remove_pruning(net)
+
+
+def test_transformer_builder_and_pipelines():
+    from brain_b200.models.config import BertLiteConfig, GptLiteConfig
+    from brain_b200.models.generate import GenerationConfig
+    from brain_b200.models.pipelines import (SequenceClassificationPipeline, TextGenerationPipeline,
+                                             TransformerBuilder)
+    cfg = TransformerBuilder().arch("gpt").vocab_size(64).hidden_dim(32).num_layers(1).num_heads(4).max_seq_len(16).build_config()
+    assert cfg.learned_positions and not cfg.rope and cfg.norm == "layer"
+    with pytest.raises(ValueError, match="divisible"):
+        TransformerBuilder().hidden_dim(30).num_heads(4).build_config()
+    for arch in ("llama", "gpt", "bert"):
+        m = TransformerBuilder().arch(arch).vocab_size(64).hidden_dim(32).num_layers(1).num_heads(4) \
+            .intermediate_dim(64).max_seq_len(16).build_model()
+        assert type(m).__name__ == {"llama": "LlamaLite", "gpt": "GptLite", "bert": "BertLite"}[arch]
+    cls = SequenceClassificationPipeline(BertLiteConfig(vocab_size=50, hidden_dim=32, num_layers=1, num_heads=4,
+                                                        intermediate_dim=64, max_seq_len=16, num_labels=3))
+    assert cls.predict_class([1, 2, 3]) in (0, 1, 2)
+    torch.testing.assert_close(cls.predict_proba([[1, 2, 3]]).sum(), torch.tensor(1.0))
+    gen = TextGenerationPipeline(GptLiteConfig(vocab_size=50, hidden_dim=32, num_layers=1, num_heads=4,
+                                               intermediate_dim=64, max_seq_len=16))
+    out = gen.generate([1, 2], GenerationConfig(max_new_tokens=5, temperature=0.0))
+    assert out[:2] == [1, 2] and len(out) == 7
+
+
+def test_text_format_parsers():
+    from brain_b200.utils import parsers as P
+    ini = P.parse_ini("top = 1\n[model]\nname = llama\nlayers = 32\nlr = 3e-4\ntied = false\n")
+    assert ini == {"": {"top": 1}, "model": {"name": "llama", "layers": 32, "lr": 3e-4, "tied": False}}
+    assert P.parse_ini(P.dump_ini(ini)) == ini
+    rows = P.parse_csv("a,b\n1,x\n2.5,true\n")
+    assert rows == [{"a": 1, "b": "x"}, {"a": 2.5, "b": True}]
+    assert P.parse_csv(P.dump_csv(rows)) == rows
+    assert P.parse_json(P.dump_json({"k": [1, 2]})) == {"k": [1, 2]}
