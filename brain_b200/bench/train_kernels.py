@@ -87,6 +87,14 @@ def main(argv=None) -> int:
             acc = torch.zeros(N, K, device=dev, dtype=torch.float32)
             report(f"gemm_wgrad_{name}", timeit(lambda: ops.gemm(dy, xi, trans_a=True, out=acc, beta=1.0)), fl,
                    M=N, N=K, K=T)
+    # ---- fused QKV projection with RoPE on the q / k heads in the GEMM epilogue
+    if want("gemm_fwd_qkv_rope"):
+        from ..ops.gemm import gemm_rope
+        N = (Hq + 2 * Hkv) * D
+        wq = rnd(N, d, std=0.02)
+        table = ops.rope_table(D, S, 500000.0, device=dev)
+        report("gemm_fwd_qkv_rope", timeit(lambda: gemm_rope(x, wq, table, (Hq + Hkv) * D, D, S, 0)),
+               2.0 * T * N * d, M=T, N=N, K=d)
     # ---- flash attention (causal): forward 2 GEMMs of S x S x D per head over half the square
     q, k, v = rnd(B, S, Hq, D), rnd(B, S, Hkv, D), rnd(B, S, Hkv, D)
     fwd_flops = 4.0 * B * Hq * S * S * D / 2
