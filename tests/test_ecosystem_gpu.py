@@ -1,0 +1,71 @@
+"""Ecosystem modules on the GPU through the framework's kernels: the graph interpreter's GEMM nodes, the
+BLAS gemm with alpha / beta, the LSTM cell's gate projections, and the native token loader feeding a
+CUDA tensor. Each result is compared with a float32 PyTorch computation of the same op."""
+import numpy as np
+import pytest
+import torch
+
+gpu = pytest.mark.gpu
+
+
+def _close(a, b, tol=3e-2):
+    torch.testing.assert_close(a.float(), b.float(), rtol=tol, atol=tol)
+
+
+@gpu
+def test_graph_interpreter_gemm_nodes_on_tcgen05():
+    from brain_b200 import graph as G
+    from brain_b200 import ops
+    g = G.GraphIr("mlp")
+    x = g.add_input("x", (256, 128), "bfloat16")
+    w1 = g.constant("w1", (torch.randn(256, 128) * 0.05).bfloat16())
+    b1 = g.constant("b1", (torch.randn(256) * 0.1).bfloat16())
+    w2 = g.constant("w2", (torch.randn(256, 64) * 0.05).bfloat16())
+    h = g.add_node("gelu", [g.add_node("linear", [x, w1, b1])])
+    g.mark_output(g.add_node("matmul", [h, w2]))
+    xi = torch.randn(256, 128, device="cuda").bfloat16()
+    out = G.GraphInterpreter().run(g, [xi])[0]
+    cw = {v.name: v.constant.float().cuda() for v in g.values.values() if v.constant is not None}
+    ref = torch.nn.functional.gelu(xi.float() @ cw["w1"].t() + cw["b1"], approximate="tanh") @ cw["w2"]
+    _close(out, ref)
+    assert not ops.check_status()
+
+
+@gpu
+def test_blas_gemm_alpha_beta_bf16():
+    from brain_b200.device import CudaBackend, blas
+    a = torch.randn(256, 512, device="cuda").bfloat16()
+    b = torch.randn(384, 512, device="cuda").bfloat16()
+    c = torch.randn(256, 384, device="cuda", dtype=torch.float32)
+    ref = 0.5 * a.float() @ b.float().t() + 2.0 * c
+    out = blas.gemm(a, b, c.clone(), alpha=0.5, beta=2.0, trans_b=True)
+    _close(out, ref, 0.15)
+    _close(CudaBackend().matmul(a, b.t().contiguous()), a.float() @ b.float().t(), 0.3)
+
+
+@gpu
+def test_lstm_cell_bf16_on_gpu_matches_fp32():
+    from brain_b200.zoo import rnn
+    torch.manual_seed(0)
+    cell = rnn.LstmCell(128, 128)
+    x, h, c = torch.randn(64, 128), torch.randn(64, 128), torch.randn(64, 128)
+    h_ref, c_ref = cell(x, (h, c))
+    cg = rnn.LstmCell(128, 128, device="cuda", dtype=torch.bfloat16)
+    cg.load_state_dict({k: v.bfloat16() for k, v in cell.state_dict().items()})
+    h1, c1 = cg(x.cuda().bfloat16(), (h.cuda().bfloat16(), c.cuda().bfloat16()))
+    _close(h1.cpu(), h_ref, 5e-2)
+    _close(c1.cpu(), c_ref, 5e-2)
+
+
+@gpu
+def test_native_loader_to_device(tmp_path):
+    from brain_b200 import data as D
+    toks = np.random.default_rng(1).integers(0, 32000, size=20000).astype(np.uint16)
+    p = str(tmp_path / "t.bin")
+    D.write_token_file(p, toks)
+    L = D.NativeTokenLoader(p, batch=2, seq=64, seed=3, device="cuda")
+    x, y = L.next()
+    torch.cuda.synchronize()
+    ref = L.batch_at(0)
+    assert x.is_cuda and torch.equal(x.cpu(), ref[:, :-1]) and torch.equal(y.cpu(), ref[:, 1:])
+    L.close()
