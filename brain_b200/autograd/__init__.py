@@ -2,4 +2,5 @@
 from .value import Value, NoGradGuard, no_grad, with_no_grad, is_grad_enabled, backward_from, backward_with_grad  # noqa: F401
 from .tape import Tape, OpRecord, start_recording, stop_recording, with_tape, is_recording, TapePruner, TapeFusionPass  # noqa: F401
 from .functional import (grad, value_and_grad, vjp, jvp, jacobian, hessian, grad_and_hess, numeric_grad,  # noqa: F401
-                         checkpoint, BudgetCheckpoint, GradScaler, parallel_backward)
+                         checkpoint, BudgetCheckpoint, CheckpointPolicy, CpuOffloader, GradScaler,
+                         parallel_backward)

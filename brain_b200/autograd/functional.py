@@ -96,6 +96,75 @@ class BudgetCheckpoint:
         return [i % self.every == 0 for i in range(num_layers)]
 
 
+class CheckpointPolicy:
+    """Which layers recompute their activations in backward: ``"none"``, ``"all"``, ``"sqrt"`` (every
+    round(sqrt(L))-th layer, ``BudgetCheckpoint``) or ``"every:k"`` (reference ``CheckpointPolicy``,
+    crates/brain-autograd/src/checkpoint/mod.rs:15-37)."""
+
+    def __init__(self, kind: str = "none"):
+        self.kind = kind
+
+    def mask(self, num_layers: int) -> list[bool]:
+        if self.kind == "all":
+            return [True] * num_layers
+        if self.kind == "sqrt":
+            return BudgetCheckpoint(num_layers).mask(num_layers)
+        if self.kind.startswith("every:"):
+            k = max(1, int(self.kind.split(":", 1)[1]))
+            return [i % k == 0 for i in range(num_layers)]
+        return [False] * num_layers
+
+
+class CpuOffloader:
+    """Context manager that moves the activations autograd saves for backward to pinned host memory
+    (copied on a side stream) and brings them back when backward needs them (reference ``CpuOffloader``,
+    crates/brain-autograd/src/cpu_offload.rs). Tensors smaller than ``min_bytes`` stay on the device.
+    Trades PCIe / C2C bandwidth for HBM when activations do not fit."""
+
+    def __init__(self, min_bytes: int = 1 << 20):
+        self.min_bytes = min_bytes
+        self.offloaded = 0
+        self._ctx = None
+
+    def _pack(self, t: torch.Tensor):
+        if not t.is_cuda or t.numel() * t.element_size() < self.min_bytes:
+            return t
+        stream = torch.cuda.current_stream(t.device)
+        side = self._side(t.device)
+        side.wait_stream(stream)
+        host = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+        with torch.cuda.stream(side):
+            host.copy_(t, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(side)
+        t.record_stream(side)
+        self.offloaded += t.numel() * t.element_size()
+        return (host, t.device, ev)
+
+    def _unpack(self, packed):
+        if isinstance(packed, torch.Tensor):
+            return packed
+        host, dev, ev = packed
+        ev.synchronize()
+        return host.to(dev, non_blocking=True)
+
+    def _side(self, dev):
+        if not hasattr(self, "_streams"):
+            self._streams = {}
+        if dev not in self._streams:
+            self._streams[dev] = torch.cuda.Stream(dev)
+        return self._streams[dev]
+
+    def __enter__(self):
+        self._ctx = torch.autograd.graph.saved_tensors_hooks(self._pack, self._unpack)
+        self._ctx.__enter__()
+        return self
+
+    def __exit__(self, *exc):
+        self._ctx.__exit__(*exc)
+        return False
+
+
 class GradScaler:
     """Dynamic loss scaling: scale the loss, unscale grads, skip non-finite steps and back off."""
 

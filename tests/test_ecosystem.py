@@ -862,3 +862,9 @@ def test_sharded_checkpoint_resume_and_reshard(tmp_path):
     for key, idx in (("master", 1), ("exp_avg_sq", 2)):
         got = np.concatenate([three[r][idx] for r in range(3)])[:n]
         assert np.array_equal(got, full[key][:n].numpy())
+
+
+def test_checkpoint_policy_masks():
+    from brain_b200.autograd import CheckpointPolicy
+    assert CheckpointPolicy("sqrt").mask(9) == [True, False, False] * 3
+    assert CheckpointPolicy("all").mask(2) == [True, True] and CheckpointPolicy().mask(2) == [False, False]

@@ -69,3 +69,20 @@ def test_native_loader_to_device(tmp_path):
     ref = L.batch_at(0)
     assert x.is_cuda and torch.equal(x.cpu(), ref[:, :-1]) and torch.equal(y.cpu(), ref[:, 1:])
     L.close()
+
+
+@gpu
+def test_cpu_offloader_gives_same_gradients():
+    from brain_b200.autograd import CpuOffloader
+    torch.manual_seed(0)
+    net = torch.nn.Sequential(torch.nn.Linear(512, 1024), torch.nn.GELU(), torch.nn.Linear(1024, 512)).cuda()
+    x = torch.randn(1024, 512, device="cuda")
+    net(x).pow(2).mean().backward()
+    ref = [p.grad.clone() for p in net.parameters()]
+    net.zero_grad()
+    with CpuOffloader(min_bytes=1 << 16) as off:
+        y = net(x)
+    y.pow(2).mean().backward()
+    assert off.offloaded > 0
+    for p, r in zip(net.parameters(), ref):
+        torch.testing.assert_close(p.grad, r)
