@@ -103,3 +103,55 @@ def rank_prefix(rank: int | None = None, world: int | None = None) -> str:
 def new_group(ranks: list[int], name: str = "group") -> ProcessGroup:
     h = dist.new_group(ranks) if dist.is_initialized() else None
     return ProcessGroup(name, list(ranks), h)
+
+
+@dataclass
+class ParallelMesh:
+    """Rank layout (pp, dp, tp) with tensor-parallel ranks adjacent (the fastest-varying coordinate, so
+    a TP group sits on neighbouring GPUs of one NVSwitch domain), then data-parallel, then pipeline.
+    ``tp_group`` / ``dp_group`` / ``pp_group`` are this rank's subgroups."""
+    tp: int
+    dp: int
+    pp: int
+    rank: int
+    tp_rank: int
+    dp_rank: int
+    pp_rank: int
+    tp_group: ProcessGroup
+    dp_group: ProcessGroup
+    pp_group: ProcessGroup
+
+    @staticmethod
+    def coords(rank: int, tp: int, dp: int) -> tuple[int, int, int]:
+        return rank // (tp * dp), (rank // tp) % dp, rank % tp
+
+
+def init_mesh(tp: int = 1, pp: int = 1) -> ParallelMesh:
+    """Collective: builds every TP, DP and PP subgroup (every rank creates all of them, in the same
+    order, as ``torch.distributed.new_group`` requires) and returns this rank's view."""
+    c = context()
+    W = c.world_size
+    if W % (tp * pp):
+        raise ValueError(f"world size {W} is not divisible by tp {tp} x pp {pp}")
+    dp = W // (tp * pp)
+    pr, dr, tr = ParallelMesh.coords(c.rank, tp, dp)
+    mine = {}
+    for p in range(pp):
+        for d in range(dp):
+            ranks = [p * tp * dp + d * tp + t for t in range(tp)]
+            g = new_group(ranks, f"tp{p}.{d}")
+            if c.rank in ranks:
+                mine["tp"] = g
+    for p in range(pp):
+        for t in range(tp):
+            ranks = [p * tp * dp + d * tp + t for d in range(dp)]
+            g = new_group(ranks, f"dp{p}.{t}")
+            if c.rank in ranks:
+                mine["dp"] = g
+    for d in range(dp):
+        for t in range(tp):
+            ranks = [p * tp * dp + d * tp + t for p in range(pp)]
+            g = new_group(ranks, f"pp{d}.{t}")
+            if c.rank in ranks:
+                mine["pp"] = g
+    return ParallelMesh(tp, dp, pp, c.rank, tr, dr, pr, mine["tp"], mine["dp"], mine["pp"])

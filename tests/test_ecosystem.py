@@ -868,3 +868,25 @@ def test_checkpoint_policy_masks():
     from brain_b200.autograd import CheckpointPolicy
     assert CheckpointPolicy("sqrt").mask(9) == [True, False, False] * 3
     assert CheckpointPolicy("all").mask(2) == [True, True] and CheckpointPolicy().mask(2) == [False, False]
+
+
+def _mesh_rank(rank, world):
+    import torch.distributed as dist
+    from brain_b200.parallel import dist as bdist
+    bdist.init(device="cpu", timeout_s=60)
+    try:
+        m = bdist.init_mesh(tp=2, pp=1)
+        t = torch.tensor([float(rank)])
+        dist.all_reduce(t, group=m.tp_group.handle)
+        u = torch.tensor([float(rank)])
+        dist.all_reduce(u, group=m.dp_group.handle)
+        return m.tp_rank, m.dp_rank, m.tp_group.ranks, m.dp_group.ranks, float(t), float(u)
+    finally:
+        bdist.shutdown()
+
+
+def test_parallel_mesh_subgroups():
+    res = run_ranks(_mesh_rank, 4, timeout=120)
+    assert res[0][:4] == (0, 0, [0, 1], [0, 2]) and res[3][:4] == (1, 1, [2, 3], [1, 3])
+    assert res[1][4] == 1.0 and res[2][4] == 5.0  # TP sums: 0+1, 2+3
+    assert res[0][5] == 2.0 and res[1][5] == 4.0  # DP sums: 0+2, 1+3
