@@ -42,6 +42,48 @@ def sdpa_with_bias(q, k, v, bias=None, causal=False, mask=None):
     return (p @ vf).transpose(1, 2).to(q.dtype)
 
 
+def memory_efficient_attention(q, k, v, bias=None, causal=False, q_chunk: int = 512, k_chunk: int = 512):
+    """Tiled attention with an online softmax over key blocks (the reference's xformers-lite / flash-lite
+    CPU tiling, crates/brain-transformer/src/attention/xformers_lite.rs and flash_lite.rs:46-222): memory
+    O(q_chunk * k_chunk) per head instead of O(Sq * Sk), with the same optional additive bias
+    ([H, Sq, Sk] or [B, H, Sq, Sk], sliced per tile) and bottom-right causal alignment as
+    ``sdpa_with_bias``. For biased attention (ALiBi, T5 relative) at lengths where the full score matrix
+    does not fit; unbiased attention uses the tcgen05 flash kernels."""
+    B, Sq, H, D = q.shape
+    Sk = k.shape[1]
+    rep = H // k.shape[2]
+    qf = q.float().transpose(1, 2) / math.sqrt(D)
+    kf, vf = k.float().transpose(1, 2), v.float().transpose(1, 2)
+    if rep > 1:
+        kf, vf = kf.repeat_interleave(rep, 1), vf.repeat_interleave(rep, 1)
+    out = torch.empty_like(qf)
+    for q0 in range(0, Sq, q_chunk):
+        q1 = min(Sq, q0 + q_chunk)
+        m = torch.full((B, H, q1 - q0, 1), float("-inf"), device=q.device)
+        l = torch.zeros((B, H, q1 - q0, 1), device=q.device)
+        acc = torch.zeros((B, H, q1 - q0, D), device=q.device)
+        for k0 in range(0, Sk, k_chunk):
+            k1 = min(Sk, k0 + k_chunk)
+            if causal and k0 > q1 - 1 + (Sk - Sq):
+                break
+            s = qf[:, :, q0:q1] @ kf[:, :, k0:k1].transpose(-1, -2)
+            if bias is not None:
+                s = s + bias[..., q0:q1, k0:k1].float()
+            if causal:
+                i = torch.arange(q0, q1, device=q.device)[:, None]
+                j = torch.arange(k0, k1, device=q.device)[None, :]
+                s = s.masked_fill(j > i + (Sk - Sq), float("-inf"))
+            m_new = torch.maximum(m, s.amax(-1, keepdim=True))
+            safe = torch.where(torch.isinf(m_new), torch.zeros_like(m_new), m_new)
+            p = torch.exp(s - safe)
+            corr = torch.exp(torch.where(torch.isinf(m), torch.full_like(m, float("-inf")), m - safe))
+            l = l * corr + p.sum(-1, keepdim=True)
+            acc = acc * corr + p @ vf[:, :, k0:k1]
+            m = m_new
+        out[:, :, q0:q1] = acc / l.clamp_min(1e-30)
+    return out.transpose(1, 2).to(q.dtype)
+
+
 class SelfAttention(Module):
     def __init__(self, dim, heads, kv_heads=None, bias=False, causal=False, device=None, dtype=None):
         super().__init__()

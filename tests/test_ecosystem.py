@@ -890,3 +890,19 @@ def test_parallel_mesh_subgroups():
     assert res[0][:4] == (0, 0, [0, 1], [0, 2]) and res[3][:4] == (1, 1, [2, 3], [1, 3])
     assert res[1][4] == 1.0 and res[2][4] == 5.0  # TP sums: 0+1, 2+3
     assert res[0][5] == 2.0 and res[1][5] == 4.0  # DP sums: 0+2, 1+3
+
+
+def test_memory_efficient_attention_matches_dense_with_alibi():
+    from brain_b200.models.blocks import memory_efficient_attention, sdpa_with_bias
+    from brain_b200.models.position import alibi_bias
+    torch.manual_seed(0)
+    B, S, H, Hkv, D = 2, 70, 4, 2, 16
+    q, k, v = torch.randn(B, S, H, D), torch.randn(B, S, Hkv, D), torch.randn(B, S, Hkv, D)
+    bias = alibi_bias(H, S, S, causal=False)
+    for causal in (False, True):
+        ref = sdpa_with_bias(q, k, v, bias, causal)
+        got = memory_efficient_attention(q, k, v, bias, causal, q_chunk=16, k_chunk=24)
+        torch.testing.assert_close(got, ref, atol=1e-5, rtol=1e-5)
+    q2 = torch.randn(B, 10, H, D)  # decode-style: fewer queries than keys, bottom-right causal
+    torch.testing.assert_close(memory_efficient_attention(q2, k, v, None, True, 4, 16),
+                               sdpa_with_bias(q2, k, v, None, True), atol=1e-5, rtol=1e-5)
