@@ -906,3 +906,46 @@ def test_memory_efficient_attention_matches_dense_with_alibi():
     q2 = torch.randn(B, 10, H, D)  # decode-style: fewer queries than keys, bottom-right causal
     torch.testing.assert_close(memory_efficient_attention(q2, k, v, None, True, 4, 16),
                                sdpa_with_bias(q2, k, v, None, True), atol=1e-5, rtol=1e-5)
+
+
+def test_memory_arena_pool_linalg_and_heads():
+    from brain_b200 import linalg as LA
+    from brain_b200.memory import BinnedMemoryPool, MemoryArena, aligned_empty, is_aligned, strides_row_major
+    from brain_b200.models.heads import ClsHead, EmbConfig, HeadConfig, LmHead, TransformerEmbedding
+    ar = MemoryArena(1 << 16)
+    a = ar.alloc((10, 3), torch.float32)
+    b = ar.alloc((7,), torch.bfloat16)
+    assert is_aligned(a, 256) and is_aligned(b, 256) and a.data_ptr() != b.data_ptr()
+    m = ar.mark()
+    ar.alloc((100,))
+    ar.release_to(m)
+    assert ar.used() == m
+    with pytest.raises(MemoryError):
+        ar.alloc((1 << 20,))
+    ar.reset()
+    assert ar.used() == 0 and ar.stats.peak_bytes > 0
+    pool = BinnedMemoryPool(min_bytes=256)
+    t = pool.get((100,), torch.float32)
+    p0 = t.data_ptr()
+    pool.put(t)
+    t2 = pool.get((90,), torch.float32)
+    assert t2.data_ptr() == p0 and pool.hits == 1 and pool.misses == 1
+    assert is_aligned(aligned_empty((5, 5)), 256) and strides_row_major((2, 3, 4)) == [12, 4, 1]
+    x = torch.randn(5, 5, dtype=torch.float64)
+    spd = x @ x.t() + 5 * torch.eye(5, dtype=torch.float64)
+    P, L, U = LA.lu(spd)
+    torch.testing.assert_close(P @ L @ U, spd)
+    torch.testing.assert_close(LA.cholesky(spd) @ LA.cholesky(spd).t(), spd)
+    w, V = LA.eigh(spd)
+    torch.testing.assert_close(V @ torch.diag(w) @ V.t(), spd)
+    torch.testing.assert_close(LA.ifft(LA.fft(x[0])).real, x[0])
+    dense = torch.tensor([[0.0, 2.0, 0.0], [1.0, 0.0, 3.0]])
+    csr = LA.CsrMatrix.from_dense(dense)
+    assert csr.nnz() == 3
+    torch.testing.assert_close(LA.spmm(csr, torch.eye(3)), dense)
+    emb = TransformerEmbedding(EmbConfig(50, 16, max_positions=8, type_vocab_size=2, norm="layer"))
+    h = emb(torch.randint(0, 50, (2, 8)))
+    assert h.shape == (2, 8, 16)
+    lm = LmHead.new_tied(HeadConfig(16, 50), emb.tok.weight)
+    assert lm(h).shape == (2, 8, 50)
+    assert LmHead(HeadConfig(16, 50))(h).shape == (2, 8, 50) and ClsHead(HeadConfig(16, num_labels=3))(h).shape == (2, 3)
