@@ -140,6 +140,8 @@ def _matmul(a, b):
 
 
 def run_op(op: str, xs: list, attrs: dict):
+    if op == "gelu" and attrs.get("approximate", "tanh") != "tanh":
+        return torch.nn.functional.gelu(xs[0], approximate=attrs["approximate"])
     if op in ELEMENTWISE_UNARY:
         return _act(op, xs[0])
     if op in ELEMENTWISE_BINARY:
@@ -582,7 +584,8 @@ def from_fx(module: torch.nn.Module, *example_inputs) -> GraphIr:
                       torch.nn.GELU: "gelu", torch.nn.Identity: "identity"}.get(type(m))
                 if op is None:
                     raise GraphError(f"unsupported module {type(m).__name__}")
-                env[node.name] = g.add_node(op, [x], name=node.name)
+                attrs = {"approximate": m.approximate} if op == "gelu" else None
+                env[node.name] = g.add_node(op, [x], attrs, name=node.name)
         elif node.op in ("call_function", "call_method"):
             tgt = node.target
             op = binops.get(tgt) or _FX_FUNCS.get(tgt) or (tgt if isinstance(tgt, str) and tgt in OPS else None)
@@ -594,7 +597,8 @@ def from_fx(module: torch.nn.Module, *example_inputs) -> GraphIr:
                     ins.append(env[a.name])
                 else:
                     ins.append(g.constant(f"c{len(g.values)}", torch.tensor(float(a))))
-            env[node.name] = g.add_node(op, ins, name=node.name)
+            attrs = {"approximate": node.kwargs.get("approximate", "none")} if op == "gelu" else None
+            env[node.name] = g.add_node(op, ins, attrs, name=node.name)
         elif node.op == "output":
             outs = node.args[0] if isinstance(node.args[0], (tuple, list)) else (node.args[0],)
             g.mark_output(*[env[o.name] for o in outs])

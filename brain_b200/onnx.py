@@ -166,7 +166,7 @@ def export_onnx(g: GraphIr, path: str | None = None) -> bytes:
         elif n.op == "concat":
             attrs = {"axis": int(a.get("dim", -1))}
         elif n.op == "gelu":
-            attrs = {"approximate": "tanh"}
+            attrs = {"approximate": a.get("approximate", "tanh")}
         elif n.op == "layer_norm":
             attrs = {"axis": -1, "epsilon": float(a.get("eps", 1e-5))}
         elif n.op == "transpose":
@@ -315,6 +315,8 @@ def import_onnx(data: bytes) -> GraphIr:
             a["dim"] = attrs.get("axis", -1)
         elif op == "layer_norm":
             a["eps"] = attrs.get("epsilon", 1e-5)
+        elif op == "gelu":
+            a["approximate"] = attrs.get("approximate", "none")
         elif op == "linear":
             if attrs.get("transB", 0) != 1 or attrs.get("transA", 0):
                 raise GraphError("only Gemm with transB=1 is supported")

@@ -949,3 +949,13 @@ def test_memory_arena_pool_linalg_and_heads():
     lm = LmHead.new_tied(HeadConfig(16, 50), emb.tok.weight)
     assert lm(h).shape == (2, 8, 50)
     assert LmHead(HeadConfig(16, 50))(h).shape == (2, 8, 50) and ClsHead(HeadConfig(16, num_labels=3))(h).shape == (2, 3)
+
+
+def test_fx_capture_keeps_exact_gelu():
+    from brain_b200 import graph as G
+    from brain_b200 import onnx as O
+    net = torch.nn.Sequential(torch.nn.Linear(4, 8), torch.nn.GELU(), torch.nn.Linear(8, 2))
+    x = torch.randn(3, 4)
+    g = G.from_fx(net, x)
+    torch.testing.assert_close(G.GraphInterpreter().run(g, [x])[0], net(x))
+    torch.testing.assert_close(G.GraphInterpreter().run(O.import_onnx(O.export_onnx(g)), [x])[0], net(x))
