@@ -167,3 +167,59 @@ def concat_chunks(chunks: list[torch.Tensor]) -> torch.Tensor:
 
 def shard_tensor_for_rank(t: torch.Tensor, rank: int, world: int, dim: int = 0) -> torch.Tensor:
     return torch.tensor_split(t, world, dim=dim)[rank].contiguous()
+
+
+class Work:
+    """Handle of a collective started with ``*_async`` (reference ``AsyncCollective::wait``,
+    crates/brain-distributed/src/async_exec.rs:6-18). On CUDA the collective runs on a side stream
+    and ``wait()`` makes the caller's current stream wait for it (no host block); on CPU it wraps the
+    process-group work object."""
+
+    def __init__(self, result, event=None, work=None):
+        self.result, self._event, self._work = result, event, work
+
+    def wait(self):
+        if self._work is not None:
+            self._work.wait()
+        elif self._event is not None:
+            torch.cuda.current_stream().wait_event(self._event)
+        return self.result
+
+    def is_completed(self) -> bool:
+        if self._work is not None:
+            return self._work.is_completed()
+        return self._event is None or self._event.query()
+
+
+_side_streams: dict = {}
+
+
+def _run_async(fn, t: torch.Tensor, *args, **kw) -> Work:
+    if _world(kw.get("group")) == 1:
+        return Work(t)
+    if not t.is_cuda:
+        if fn is all_reduce and kw.get("op", "sum") == "sum":
+            return Work(t, work=dist.all_reduce(t, group=kw.get("group"), async_op=True))
+        return Work(fn(t, *args, **kw))
+    s = _side_streams.get(t.device)
+    if s is None:
+        s = _side_streams[t.device] = torch.cuda.Stream(t.device)
+    s.wait_stream(torch.cuda.current_stream(t.device))
+    with torch.cuda.stream(s):
+        out = fn(t, *args, **kw)
+        ev = torch.cuda.Event()
+        ev.record(s)
+    t.record_stream(s)
+    return Work(out, event=ev)
+
+
+def all_reduce_async(t: torch.Tensor, op: str = "sum", group=None, backend: str | None = None) -> Work:
+    return _run_async(all_reduce, t, op=op, group=group, backend=backend)
+
+
+def all_gather_async(t: torch.Tensor, group=None, backend: str | None = None) -> Work:
+    return _run_async(all_gather, t, group=group, backend=backend)
+
+
+def reduce_scatter_async(t: torch.Tensor, group=None, backend: str | None = None, op: str = "sum") -> Work:
+    return _run_async(reduce_scatter, t, group=group, backend=backend, op=op)

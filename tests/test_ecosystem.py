@@ -959,3 +959,23 @@ def test_fx_capture_keeps_exact_gelu():
     g = G.from_fx(net, x)
     torch.testing.assert_close(G.GraphInterpreter().run(g, [x])[0], net(x))
     torch.testing.assert_close(G.GraphInterpreter().run(O.import_onnx(O.export_onnx(g)), [x])[0], net(x))
+
+
+def _async_rank(rank, world):
+    from brain_b200.parallel import collectives as C
+    from brain_b200.parallel import dist as bdist
+    bdist.init(device="cpu", timeout_s=60)
+    try:
+        t = torch.full((4,), float(rank + 1))
+        w = C.all_reduce_async(t)
+        out = w.wait()
+        g = C.all_gather_async(torch.tensor([float(rank)])).wait()
+        return out.tolist(), w.is_completed(), g.tolist()
+    finally:
+        bdist.shutdown()
+
+
+def test_async_collectives_on_gloo():
+    res = run_ranks(_async_rank, 2, timeout=120)
+    for r in range(2):
+        assert res[r][0] == [3.0] * 4 and res[r][1] and res[r][2] == [0.0, 1.0]
