@@ -666,3 +666,269 @@ def batch_encode(tokenizer: Tokenizer, texts, post: PostProcessor, device=None):
         ids[i, :len(o.ids)] = torch.tensor(o.ids)
         mask[i, :len(o.ids)] = torch.tensor(o.attention_mask)
     return ids.to(device), mask.to(device)
+
+
+# ------------------------------------------------------------------ language-model preprocessing
+class LmPreprocessor:
+    """Batches for causal / masked language modelling (reference tokenizer-side helpers,
+    crates/brain-text/src/lm.rs:52-170)."""
+
+    @staticmethod
+    def prepare_causal_lm(ids: torch.Tensor):
+        """(inputs, labels) with labels shifted left by one."""
+        return ids[..., :-1], ids[..., 1:]
+
+    @staticmethod
+    def prepare_masked_lm(ids: torch.Tensor, mask_id: int, vocab_size: int, prob: float = 0.15,
+                          special_ids=(), generator=None, ignore_index: int = -100):
+        """BERT masking: each non-special position is selected with ``prob``; of those 80 % become
+        ``mask_id``, 10 % a random token and 10 % stay. Labels are the originals at selected positions
+        and ``ignore_index`` elsewhere."""
+        sel = torch.rand(ids.shape, generator=generator) < prob
+        for s in special_ids:
+            sel &= ids != s
+        labels = torch.where(sel, ids, torch.full_like(ids, ignore_index))
+        r = torch.rand(ids.shape, generator=generator)
+        out = ids.clone()
+        out[sel & (r < 0.8)] = mask_id
+        rnd = sel & (r >= 0.8) & (r < 0.9)
+        out[rnd] = torch.randint(0, vocab_size, (int(rnd.sum()),), generator=generator)
+        return out, labels
+
+    @staticmethod
+    def create_causal_mask(seq_len: int) -> torch.Tensor:
+        """1 where query i may attend key j (j <= i)."""
+        return torch.tril(torch.ones(seq_len, seq_len, dtype=torch.uint8))
+
+    @staticmethod
+    def create_prefix_lm_mask(prefix_len: int, total_len: int) -> torch.Tensor:
+        """Bidirectional inside the prefix, causal after it."""
+        m = LmPreprocessor.create_causal_mask(total_len)
+        m[:prefix_len, :prefix_len] = 1
+        return m
+
+    @staticmethod
+    def pack_documents(docs, seq_len: int, eos_id: int) -> torch.Tensor:
+        """Concatenates token lists with ``eos_id`` after each and cuts [N, seq_len] rows (the tail that
+        does not fill a row is dropped)."""
+        flat = [t for d in docs for t in list(d) + [eos_id]]
+        n = len(flat) // seq_len
+        return torch.tensor(flat[:n * seq_len], dtype=torch.int64).view(n, seq_len)
+
+    @staticmethod
+    def sliding_window_chunks(ids, window: int, stride: int):
+        ids = list(ids)
+        if len(ids) <= window:
+            return [ids]
+        out = [ids[i:i + window] for i in range(0, len(ids) - window + 1, stride)]
+        if (len(ids) - window) % stride:
+            out.append(ids[-window:])
+        return out
+
+
+# ------------------------------------------------------------------ text features
+class BagOfWords:
+    def __init__(self, vocab: Vocab | None = None):
+        self.vocab = vocab or Vocab()
+
+    def fit(self, corpus) -> "BagOfWords":
+        for doc in corpus:
+            for t in doc:
+                self.vocab.insert(t)
+        return self
+
+    def transform(self, tokens) -> torch.Tensor:
+        v = torch.zeros(len(self.vocab))
+        for t in tokens:
+            i = self.vocab.get_id(t)
+            if i is not None:
+                v[i] += 1
+        return v
+
+    def fit_transform(self, corpus) -> torch.Tensor:
+        self.fit(corpus)
+        return torch.stack([self.transform(d) for d in corpus])
+
+
+class TfIdf:
+    """tf = count / len(doc); idf = ln((1 + N) / (1 + df)) + 1 (smoothed); rows L2-normalised."""
+
+    def __init__(self, min_df: int = 1, normalize: bool = True):
+        self.min_df, self.normalize = min_df, normalize
+        self.vocab, self.idf = Vocab(), None
+
+    def fit(self, corpus) -> "TfIdf":
+        df = collections.Counter(t for doc in corpus for t in set(doc))
+        for t in sorted(t for t, c in df.items() if c >= self.min_df):
+            self.vocab.insert(t)
+        n = len(corpus)
+        self.idf = torch.tensor([math.log((1 + n) / (1 + df[t])) + 1 for t in self.vocab._toks], dtype=torch.float64)
+        return self
+
+    def transform(self, tokens) -> torch.Tensor:
+        v = torch.zeros(len(self.vocab), dtype=torch.float64)
+        for t in tokens:
+            i = self.vocab.get_id(t)
+            if i is not None:
+                v[i] += 1
+        if tokens:
+            v /= len(tokens)
+        v *= self.idf
+        if self.normalize and v.norm() > 0:
+            v /= v.norm()
+        return v
+
+    def fit_transform(self, corpus) -> torch.Tensor:
+        self.fit(corpus)
+        return torch.stack([self.transform(d) for d in corpus])
+
+
+class Bm25:
+    """Okapi BM25: idf = ln(1 + (N − df + 0.5) / (df + 0.5)), term score
+    idf · tf (k1 + 1) / (tf + k1 (1 − b + b · |d| / avgdl))."""
+
+    def __init__(self, k1: float = 1.5, b: float = 0.75):
+        self.k1, self.b = k1, b
+
+    def fit(self, docs) -> "Bm25":
+        self.docs = [collections.Counter(d) for d in docs]
+        self.lens = [len(d) for d in docs]
+        self.avgdl = sum(self.lens) / max(1, len(docs))
+        df = collections.Counter(t for d in docs for t in set(d))
+        n = len(docs)
+        self.idf = {t: math.log(1 + (n - c + 0.5) / (c + 0.5)) for t, c in df.items()}
+        return self
+
+    def score(self, query, doc_idx: int) -> float:
+        d, L = self.docs[doc_idx], self.lens[doc_idx]
+        s = 0.0
+        for t in query:
+            tf = d.get(t, 0)
+            if tf:
+                s += self.idf[t] * tf * (self.k1 + 1) / (tf + self.k1 * (1 - self.b + self.b * L / self.avgdl))
+        return s
+
+    def score_corpus(self, query) -> list[float]:
+        return [self.score(query, i) for i in range(len(self.docs))]
+
+
+class HashingVectorizer:
+    """Token counts hashed into ``num_features`` buckets (FNV-1a 64-bit of the UTF-8 token)."""
+
+    def __init__(self, num_features: int = 1 << 16):
+        self.n = num_features
+
+    def transform(self, tokens) -> torch.Tensor:
+        from .utils import fnv1a_64
+
+        v = torch.zeros(self.n)
+        for t in tokens:
+            v[fnv1a_64(t.encode()) % self.n] += 1
+        return v
+
+
+# ------------------------------------------------------------------ similarity
+class TextSimilarity:
+    @staticmethod
+    def cosine(a, b) -> float:
+        a, b = torch.as_tensor(a, dtype=torch.float64), torch.as_tensor(b, dtype=torch.float64)
+        den = float(a.norm() * b.norm())
+        return float(a @ b) / den if den > 0 else 0.0
+
+    @staticmethod
+    def dot_product(a, b) -> float:
+        return float(torch.as_tensor(a, dtype=torch.float64) @ torch.as_tensor(b, dtype=torch.float64))
+
+    @staticmethod
+    def euclidean(a, b) -> float:
+        return float((torch.as_tensor(a, dtype=torch.float64) - torch.as_tensor(b, dtype=torch.float64)).norm())
+
+    @staticmethod
+    def manhattan(a, b) -> float:
+        return float((torch.as_tensor(a, dtype=torch.float64) - torch.as_tensor(b, dtype=torch.float64)).abs().sum())
+
+    @staticmethod
+    def levenshtein(s1: str, s2: str) -> int:
+        prev = list(range(len(s2) + 1))
+        for i, c1 in enumerate(s1, 1):
+            cur = [i]
+            for j, c2 in enumerate(s2, 1):
+                cur.append(min(prev[j] + 1, cur[j - 1] + 1, prev[j - 1] + (c1 != c2)))
+            prev = cur
+        return prev[-1]
+
+    @staticmethod
+    def damerau(s1: str, s2: str) -> int:
+        """Optimal string alignment distance (adjacent transpositions count 1)."""
+        n, m = len(s1), len(s2)
+        d = [[0] * (m + 1) for _ in range(n + 1)]
+        for i in range(n + 1):
+            d[i][0] = i
+        for j in range(m + 1):
+            d[0][j] = j
+        for i in range(1, n + 1):
+            for j in range(1, m + 1):
+                cost = s1[i - 1] != s2[j - 1]
+                d[i][j] = min(d[i - 1][j] + 1, d[i][j - 1] + 1, d[i - 1][j - 1] + cost)
+                if i > 1 and j > 1 and s1[i - 1] == s2[j - 2] and s1[i - 2] == s2[j - 1]:
+                    d[i][j] = min(d[i][j], d[i - 2][j - 2] + 1)
+        return d[n][m]
+
+    @staticmethod
+    def levenshtein_similarity(s1: str, s2: str) -> float:
+        m = max(len(s1), len(s2))
+        return 1.0 - TextSimilarity.levenshtein(s1, s2) / m if m else 1.0
+
+    @staticmethod
+    def damerau_similarity(s1: str, s2: str) -> float:
+        m = max(len(s1), len(s2))
+        return 1.0 - TextSimilarity.damerau(s1, s2) / m if m else 1.0
+
+    @staticmethod
+    def jaro(s1: str, s2: str) -> float:
+        if s1 == s2:
+            return 1.0
+        l1, l2 = len(s1), len(s2)
+        if not l1 or not l2:
+            return 0.0
+        win = max(0, max(l1, l2) // 2 - 1)
+        m1, m2 = [False] * l1, [False] * l2
+        matches = 0
+        for i, c in enumerate(s1):
+            for j in range(max(0, i - win), min(l2, i + win + 1)):
+                if not m2[j] and s2[j] == c:
+                    m1[i] = m2[j] = True
+                    matches += 1
+                    break
+        if not matches:
+            return 0.0
+        a = [c for c, f in zip(s1, m1) if f]
+        b = [c for c, f in zip(s2, m2) if f]
+        t = sum(x != y for x, y in zip(a, b)) / 2
+        return (matches / l1 + matches / l2 + (matches - t) / matches) / 3
+
+    @staticmethod
+    def jaro_winkler(s1: str, s2: str, p: float = 0.1) -> float:
+        j = TextSimilarity.jaro(s1, s2)
+        prefix = 0
+        for a, b in zip(s1[:4], s2[:4]):
+            if a != b:
+                break
+            prefix += 1
+        return j + prefix * p * (1 - j)
+
+    @staticmethod
+    def jaccard(a, b) -> float:
+        A, B = set(a), set(b)
+        return len(A & B) / len(A | B) if A | B else 1.0
+
+    @staticmethod
+    def sorensen_dice(a, b) -> float:
+        A, B = set(a), set(b)
+        return 2 * len(A & B) / (len(A) + len(B)) if A or B else 1.0
+
+    @staticmethod
+    def n_gram_overlap(s1: str, s2: str, n: int = 2) -> float:
+        g1 = {s1[i:i + n] for i in range(len(s1) - n + 1)}
+        g2 = {s2[i:i + n] for i in range(len(s2) - n + 1)}
+        return len(g1 & g2) / len(g1 | g2) if g1 | g2 else 1.0

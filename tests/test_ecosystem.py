@@ -979,3 +979,31 @@ def test_async_collectives_on_gloo():
     res = run_ranks(_async_rank, 2, timeout=120)
     for r in range(2):
         assert res[r][0] == [3.0] * 4 and res[r][1] and res[r][2] == [0.0, 1.0]
+
+
+def test_text_lm_features_similarity():
+    from brain_b200.text import Bm25, HashingVectorizer, LmPreprocessor, TextSimilarity as TS, TfIdf
+    ids = torch.arange(10).view(2, 5)
+    x, y = LmPreprocessor.prepare_causal_lm(ids)
+    assert x.tolist()[0] == [0, 1, 2, 3] and y.tolist()[0] == [1, 2, 3, 4]
+    big = torch.randint(5, 100, (64, 64))
+    m, lab = LmPreprocessor.prepare_masked_lm(big, mask_id=3, vocab_size=100, generator=torch.Generator().manual_seed(0))
+    sel = lab != -100
+    assert 0.10 < float(sel.float().mean()) < 0.20 and 0.7 < float((m[sel] == 3).float().mean()) < 0.9
+    assert torch.equal(m[~sel], big[~sel])
+    pm = LmPreprocessor.create_prefix_lm_mask(2, 4)
+    assert pm.tolist() == [[1, 1, 0, 0], [1, 1, 0, 0], [1, 1, 1, 0], [1, 1, 1, 1]]
+    assert LmPreprocessor.pack_documents([[1, 2], [3]], 3, 0).tolist() == [[1, 2, 0]]
+    assert LmPreprocessor.sliding_window_chunks(range(7), 4, 2) == [[0, 1, 2, 3], [2, 3, 4, 5], [3, 4, 5, 6]]
+    docs = [["the", "cat", "sat"], ["the", "dog", "ran"], ["a", "cat", "ran", "fast"]]
+    tf = TfIdf().fit_transform(docs)
+    assert tf.shape[0] == 3 and abs(float(tf[0].norm()) - 1) < 1e-9
+    bm = Bm25().fit(docs)
+    s = bm.score_corpus(["cat"])
+    assert s[1] == 0.0 and s[0] > s[2] > 0  # shorter document ranks higher for the same tf
+    assert float(HashingVectorizer(16).transform(["a", "a", "b"]).sum()) == 3
+    assert TS.levenshtein("kitten", "sitting") == 3 and TS.damerau("ca", "ac") == 1
+    assert abs(TS.jaro("MARTHA", "MARHTA") - 0.944444) < 1e-5
+    assert abs(TS.jaro_winkler("MARTHA", "MARHTA") - 0.961111) < 1e-5
+    assert TS.jaccard(["a", "b"], ["b", "c"]) == 1 / 3 and TS.sorensen_dice(["a", "b"], ["b", "c"]) == 0.5
+    assert abs(TS.cosine([1, 0], [1, 1]) - 2 ** -0.5) < 1e-12 and TS.manhattan([1, 2], [3, 5]) == 5
