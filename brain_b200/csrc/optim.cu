@@ -23,6 +23,33 @@ __device__ __forceinline__ float ld_grad<__nv_bfloat16>(const __nv_bfloat16* g, 
   return __bfloat162float(g[i]);
 }
 
+// Four consecutive gradient elements starting at element 4 * i4 (one 16-byte f32 or 8-byte bf16 load
+// when the pointer allows it).
+template <typename G>
+__device__ __forceinline__ void ld_grad4(const G* g, int64_t i4, bool vec, float* out);
+template <>
+__device__ __forceinline__ void ld_grad4<float>(const float* g, int64_t i4, bool vec, float* out) {
+  if (vec) {
+    const float4 t = reinterpret_cast<const float4*>(g)[i4];
+    out[0] = t.x; out[1] = t.y; out[2] = t.z; out[3] = t.w;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = g[i4 * 4 + j];
+  }
+}
+template <>
+__device__ __forceinline__ void ld_grad4<__nv_bfloat16>(const __nv_bfloat16* g, int64_t i4, bool vec, float* out) {
+  if (vec) {
+    const uint2 t = reinterpret_cast<const uint2*>(g)[i4];
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&t.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&t.y));
+    out[0] = a.x; out[1] = a.y; out[2] = b.x; out[3] = b.y;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[j] = __bfloat162float(g[i4 * 4 + j]);
+  }
+}
+
 struct AdamHyper {
   float lr, b1, b2, eps, wd, bc1, bc2, grad_scale;
   int amsgrad;
@@ -39,13 +66,15 @@ __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ m, float
   const float decay = 1.f - h.lr * h.wd;
   // 4 elements per thread-iteration
   const int64_t n4 = n / 4;
+  const bool gvec = (reinterpret_cast<uintptr_t>(g) & (4 * sizeof(G) - 1)) == 0;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += stride) {
     float4 pp = reinterpret_cast<float4*>(p)[i];
     float4 mm = reinterpret_cast<float4*>(m)[i];
     float4 vv = reinterpret_cast<float4*>(v)[i];
     float gg[4];
+    ld_grad4(g, i, gvec, gg);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) gg[j] = ld_grad(g, i * 4 + j) * h.grad_scale;
+    for (int j = 0; j < 4; ++j) gg[j] *= h.grad_scale;
     float* P = &pp.x;
     float* Mv = &mm.x;
     float* Vv = &vv.x;
