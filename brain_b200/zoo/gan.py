@@ -162,4 +162,4 @@ def train_step(gen, disc, opt_g, opt_d, real, loss: str = "bce", gp: float = 0.0
     opt_g.zero_grad()
     lg.backward()
     opt_g.step()
-    return float(ld), float(lg)
+    return float(ld.detach()), float(lg.detach())
