@@ -200,3 +200,67 @@ def read_wav(path: str):
     ch, sr = fmt[1], fmt[2]
     x = torch.from_numpy(np.frombuffer(pcm, dtype="<i2").astype("float32") / 32768.0)
     return x.view(-1, ch).t().contiguous(), sr
+
+
+def dtw(a: torch.Tensor, b: torch.Tensor):
+    """Dynamic time warping between feature sequences a [N, F] and b [M, F] with Euclidean local cost:
+    returns (total cost, alignment path as (i, j) pairs). Reference: align.rs."""
+    cost = torch.cdist(a.double().reshape(a.shape[0], -1), b.double().reshape(b.shape[0], -1))
+    N, M = cost.shape
+    D = torch.full((N + 1, M + 1), float("inf"), dtype=torch.float64)
+    D[0, 0] = 0.0
+    for i in range(1, N + 1):
+        for j in range(1, M + 1):
+            D[i, j] = cost[i - 1, j - 1] + min(D[i - 1, j], D[i, j - 1], D[i - 1, j - 1])
+    path, i, j = [], N, M
+    while i > 0 and j > 0:
+        path.append((i - 1, j - 1))
+        step = int(torch.argmin(torch.stack([D[i - 1, j - 1], D[i - 1, j], D[i, j - 1]])))
+        i, j = (i - 1, j - 1) if step == 0 else ((i - 1, j) if step == 1 else (i, j - 1))
+    return float(D[N, M]), path[::-1]
+
+
+def yin_pitch(frame: torch.Tensor, sample_rate: int, fmin: float = 50.0, fmax: float = 1000.0,
+              threshold: float = 0.1) -> float:
+    """Fundamental frequency of one frame by the YIN method (de Cheveigné and Kawahara 2002):
+    cumulative-mean-normalised difference function, first dip below ``threshold``, parabolic
+    interpolation. Returns 0.0 for an unvoiced frame. Reference: features_pitch.rs."""
+    x = frame.double()
+    tmin, tmax = int(sample_rate / fmax), min(int(sample_rate / fmin), x.numel() // 2)
+    if tmax <= tmin + 1 or float((x * x).mean()) < 1e-12:  # too short, or silence
+        return 0.0
+    W = x.numel() - tmax
+    d = torch.stack([((x[:W] - x[t:t + W]) ** 2).sum() for t in range(tmax + 1)])
+    cmnd = torch.ones_like(d)
+    cum = torch.cumsum(d[1:], 0)
+    cmnd[1:] = d[1:] * torch.arange(1, tmax + 1, dtype=torch.float64) / cum.clamp_min(1e-12)
+    tau = None
+    for t in range(tmin, tmax):
+        if cmnd[t] < threshold:
+            while t + 1 < tmax and cmnd[t + 1] < cmnd[t]:
+                t += 1
+            tau = t
+            break
+    if tau is None:
+        return 0.0
+    if 0 < tau < tmax:
+        a, b, c = float(cmnd[tau - 1]), float(cmnd[tau]), float(cmnd[tau + 1])
+        den = a - 2 * b + c
+        shift = 0.5 * (a - c) / den if abs(den) > 1e-12 else 0.0
+    else:
+        shift = 0.0
+    return sample_rate / (tau + shift)
+
+
+def chroma(signal: torch.Tensor, sample_rate: int, cfg: STFTConfig | None = None, n_chroma: int = 12) -> torch.Tensor:
+    """Pitch-class energy [12, frames]: every STFT bin above 20 Hz is assigned to the nearest equal-
+    tempered pitch class (A4 = 440 Hz), columns normalised to unit maximum. Reference: feature/tonal.rs."""
+    cfg = cfg or STFTConfig()
+    mag, _ = stft(signal, cfg)
+    freqs = torch.linspace(0, sample_rate / 2, mag.shape[-2])
+    valid = freqs > 20
+    pc = torch.zeros(mag.shape[-2], dtype=torch.long)
+    pc[valid] = (torch.round(12 * torch.log2(freqs[valid] / 440.0)).long() + 9) % n_chroma  # 0 = C
+    out = torch.zeros(n_chroma, mag.shape[-1])
+    out.index_add_(0, pc[valid], (mag[valid] ** 2).float())
+    return out / out.amax(0, keepdim=True).clamp_min(1e-12)

@@ -407,3 +407,18 @@ def evaluate(env, act_fn, episodes: int = 5) -> float:
             s, r, done, _ = env.step(act_fn(s))
             tot += r
     return tot / episodes
+
+
+class DuelingQNet(Module):
+    """Q(s, a) = V(s) + A(s, a) − mean_a A(s, a) (Wang et al. 2016; reference dqn/dueling.rs)."""
+
+    def __init__(self, in_dim, num_actions, hidden=64, device=None, dtype=None):
+        super().__init__()
+        self.body = MlpNet(in_dim, hidden, hidden, device, dtype)
+        self.v = Linear(hidden, 1, True, device, dtype)
+        self.a = Linear(hidden, num_actions, True, device, dtype)
+
+    def forward(self, x):
+        h = torch.relu(self.body(x))
+        adv = self.a(h)
+        return self.v(h) + adv - adv.mean(-1, keepdim=True)

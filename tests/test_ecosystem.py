@@ -1007,3 +1007,21 @@ def test_text_lm_features_similarity():
     assert abs(TS.jaro_winkler("MARTHA", "MARHTA") - 0.961111) < 1e-5
     assert TS.jaccard(["a", "b"], ["b", "c"]) == 1 / 3 and TS.sorensen_dice(["a", "b"], ["b", "c"]) == 0.5
     assert abs(TS.cosine([1, 0], [1, 1]) - 2 ** -0.5) < 1e-12 and TS.manhattan([1, 2], [3, 5]) == 5
+
+
+def test_audio_alignment_pitch_chroma_and_dueling():
+    from brain_b200.zoo import audio as A
+    from brain_b200.zoo import rl
+    a = torch.tensor([[0.0], [1.0], [2.0], [3.0]])
+    b = torch.tensor([[0.0], [0.0], [1.0], [2.0], [3.0]])
+    cost, path = A.dtw(a, b)
+    assert cost == 0.0 and path[0] == (0, 0) and path[-1] == (3, 4)
+    sr = 16000
+    t = torch.arange(2048, dtype=torch.float64) / sr
+    f0 = A.yin_pitch(torch.sin(2 * math.pi * 220.0 * t), sr)
+    assert abs(f0 - 220.0) < 1.0
+    assert A.yin_pitch(torch.zeros(2048), sr) == 0.0
+    c = A.chroma(torch.sin(2 * math.pi * 440.0 * torch.arange(sr) / sr).float(), sr)
+    assert int(c.mean(1).argmax()) == 9  # A
+    q = rl.DuelingQNet(4, 3)(torch.randn(5, 4))
+    assert q.shape == (5, 3)
