@@ -113,6 +113,17 @@ def main(argv=None) -> int:
     if want("swiglu_fwd"):
         gu = rnd(T, 2 * F)
         report("swiglu_fwd", timeit(lambda: ops.activations.swiglu_fwd_only(gu)), nbytes=T * 3 * F * 2)
+    if want("rms_norm_bwd"):
+        from ..ops import norms as _norms
+        wn = torch.ones(d, device=dev, dtype=torch.bfloat16)
+        dy = rnd(T, d)
+        _, _, _, rstd = _norms._fwd(_norms._RMS, x, wn, None, 1e-5)
+        report("rms_norm_bwd", timeit(lambda: _norms._bwd(_norms._RMS, dy, x, wn, None, None, rstd)),
+               nbytes=3 * T * d * 2)
+    if want("swiglu_bwd"):
+        gu = rnd(T, 2 * F)
+        dy = rnd(T, F)
+        report("swiglu_bwd", timeit(lambda: ops.activations.swiglu_bwd_only(dy, gu)), nbytes=T * 5 * F * 2)
     if want("rope_inplace"):
         qkv = rnd(B, S, (Hq + 2 * Hkv) * D)
         table = ops.rope_table(D, S, 500000.0, device=dev)
