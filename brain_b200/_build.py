@@ -41,9 +41,9 @@ LIBRARIES = {
     ],
     "brain_comm": ["host_utils.cu", "comm.cu"],
 }
-# Host-only C++ libraries (g++): the checkpoint codec and the native token loader.
+# Host-only C++ libraries (g++): the checkpoint codec, the native token loader and the BPE encoder.
 CXX_LIBRARIES = {
-    "brain_runtime": ["codec.cpp", "loader.cpp"],
+    "brain_runtime": ["codec.cpp", "loader.cpp", "bpe.cpp"],
 }
 
 

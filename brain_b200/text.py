@@ -310,9 +310,75 @@ class BpeTokenizer(Tokenizer):
             out += self.bpe_segment_word(w)
         return out
 
+    def encode(self, text: str) -> TokenizedOutput:
+        """With ``use_native()`` and whitespace-collapsing normalisation, the merge loop runs in C++."""
+        nat = getattr(self, "_native", None)
+        if nat is not None and self.normalizer.config.collapse_whitespace:
+            ids = nat.encode(self.normalizer.normalize(text))
+            return TokenizedOutput(ids, [self.vocab.get_token(i) for i in ids])
+        return super().encode(text)
+
+    def use_native(self) -> "BpeTokenizer":
+        self._native = NativeBpe(self.vocab, [((a, b), r) for (a, b), r in self.ranks.items()], self.suffix)
+        return self
+
     def decode(self, ids):
         s = "".join(self._pieces(ids))
         return s.replace(self.suffix, " ").strip() if self.suffix else s
+
+
+class NativeBpe:
+    """The BPE merge loop in C++ (``csrc/bpe.cpp``, in ``libbrain_runtime``): same segmentation as
+    ``BpeTokenizer.bpe_segment_word`` on whitespace-separated words, with a per-word cache."""
+
+    def __init__(self, vocab: Vocab, merges, suffix: str = "</w>"):
+        import ctypes
+
+        from . import _native
+
+        lib = _native.load("brain_runtime")
+        self._lib = lib
+        lib.brain_bpe_create.restype = ctypes.c_void_p
+        lib.brain_bpe_create.argtypes = [ctypes.c_char_p]
+        lib.brain_bpe_add_token.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int64, ctypes.c_int, ctypes.c_int]
+        lib.brain_bpe_add_merges.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64]
+        lib.brain_bpe_encode.restype = ctypes.c_int64
+        lib.brain_bpe_encode.argtypes = [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int64, ctypes.c_void_p,
+                                         ctypes.c_int64]
+        lib.brain_bpe_destroy.argtypes = [ctypes.c_void_p]
+        self._h = lib.brain_bpe_create(suffix.encode())
+        unk = vocab.unk_id()
+        for i, t in enumerate(vocab._toks):
+            b = t.encode()
+            lib.brain_bpe_add_token(self._h, b, len(b), i, int(i == unk))
+        trip = []
+        for (a, b), _ in sorted(merges, key=lambda m: m[1]):
+            ia, ib, im = vocab.get_id(a), vocab.get_id(b), vocab.get_id(a + b)
+            if None in (ia, ib, im):
+                raise ValueError(f"merge ({a!r}, {b!r}) refers to tokens missing from the vocabulary")
+            trip += [ia, ib, im]
+        t = torch.tensor(trip, dtype=torch.int32)
+        lib.brain_bpe_add_merges(self._h, t.data_ptr(), len(trip) // 3)
+
+    def encode(self, text: str) -> list[int]:
+        b = text.encode()
+        cap = max(16, len(b) + 1)
+        while True:
+            out = torch.empty(cap, dtype=torch.int32)
+            n = self._lib.brain_bpe_encode(self._h, b, len(b), out.data_ptr(), cap)
+            if n < 0:
+                raise RuntimeError(f"brain_bpe_encode failed ({n})")
+            if n <= cap:
+                return out[:n].tolist()
+            cap = n
+
+    def __del__(self):
+        try:
+            if self._h:
+                self._lib.brain_bpe_destroy(self._h)
+                self._h = None
+        except Exception:
+            pass
 
 
 class BpeTrainer:

@@ -1025,3 +1025,16 @@ def test_audio_alignment_pitch_chroma_and_dueling():
     assert int(c.mean(1).argmax()) == 9  # A
     q = rl.DuelingQNet(4, 3)(torch.randn(5, 4))
     assert q.shape == (5, 3)
+
+
+def test_native_bpe_matches_python():
+    import random as _r
+    from brain_b200.text import BpeTokenizer, BpeTrainer
+    rng = _r.Random(0)
+    words = ["".join(rng.choice("abcdeéfg") for _ in range(rng.randint(1, 8))) for _ in range(300)]
+    corpus = [" ".join(rng.choice(words) for _ in range(20)) for _ in range(50)]
+    vocab, merges = BpeTrainer.train(corpus, vocab_size=200, special_tokens=("[PAD]", "[UNK]"))
+    py = BpeTokenizer(vocab, merges)
+    nat = BpeTokenizer(vocab, merges).use_native()
+    for text in corpus[:20] + ["  unseen  zzz  words\tand\nlines ", ""]:
+        assert nat.encode(text).ids == py.encode(text).ids, text
