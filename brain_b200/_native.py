@@ -118,10 +118,26 @@ class launch_counter:
         return _launches["n"]
 
 
+_nvtx = {"on": os.environ.get("BRAIN_NVTX", "0") == "1"}
+
+
+def set_nvtx(on: bool) -> None:
+    """NVTX range (the entry point's name) around every native call, for Nsight timelines; also
+    enabled by ``BRAIN_NVTX=1``. Off by default (a range push / pop costs host time per call)."""
+    _nvtx["on"] = bool(on)
+
+
 def call(name: str, *args) -> int:
     if _launches["on"]:
         _launches["n"] += KERNELS_PER_CALL.get(name, 1)
-    rc = fn(name)(*args)
+    if _nvtx["on"]:
+        torch.cuda.nvtx.range_push(name)
+        try:
+            rc = fn(name)(*args)
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        rc = fn(name)(*args)
     if rc != 0:
         try:
             msg = fn("brain_error_string")(rc).decode()

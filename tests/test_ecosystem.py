@@ -1038,3 +1038,17 @@ def test_native_bpe_matches_python():
     nat = BpeTokenizer(vocab, merges).use_native()
     for text in corpus[:20] + ["  unseen  zzz  words\tand\nlines ", ""]:
         assert nat.encode(text).ids == py.encode(text).ids, text
+
+
+def test_nvtx_ranges_around_native_calls(monkeypatch):
+    from brain_b200 import _native
+    seen = []
+    monkeypatch.setattr(torch.cuda.nvtx, "range_push", lambda n: seen.append(("push", n)))
+    monkeypatch.setattr(torch.cuda.nvtx, "range_pop", lambda: seen.append(("pop",)))
+    _native.register({"brain_bpe_destroy": ("brain_runtime", "p")})
+    _native.set_nvtx(True)
+    try:
+        assert _native.call("brain_bpe_destroy", None) == 0
+    finally:
+        _native.set_nvtx(False)
+    assert seen == [("push", "brain_bpe_destroy"), ("pop",)]
