@@ -161,3 +161,31 @@ class MlpDenoiser(Module):
             e = e + self.cls(c)
         h = torch.nn.functional.silu(self.l1(torch.cat([x, e], -1)))
         return self.l3(torch.nn.functional.silu(self.l2(h)))
+
+
+class EulerAncestralSampler:
+    """Ancestral sampling in the sigma parameterisation (sigma_t = sqrt((1 − ᾱ_t) / ᾱ_t)), Euler steps
+    with noise re-injected at each step (Karras et al. 2022, "ancestral" variant; reference
+    samplers/ancestral.rs). ``eta = 0`` gives the deterministic Euler sampler."""
+
+    def __init__(self, schedule: NoiseSchedule, eta: float = 1.0):
+        self.s, self.eta = schedule, eta
+
+    @torch.no_grad()
+    def sample(self, model, shape, num_steps: int = 50, device=None, cond=None, guidance_scale: float = 1.0,
+               generator=None, dtype=None):
+        ac = self.s.alphas_cumprod
+        ts = torch.linspace(self.s.timesteps - 1, 0, num_steps).round().long().tolist()
+        sig = [math.sqrt((1 - float(ac[t])) / float(ac[t])) for t in ts] + [0.0]
+        x = torch.randn(shape, generator=generator, device="cpu").to(device=device, dtype=dtype or torch.float32)
+        x = x * math.sqrt(sig[0] ** 2 + 1)
+        for i, t in enumerate(ts):
+            s0, s1 = sig[i], sig[i + 1]
+            tt = torch.full((shape[0],), t, dtype=torch.long, device=x.device)
+            eps = guided_eps(model, x / math.sqrt(s0 ** 2 + 1), tt, cond, guidance_scale)
+            s_up = min(s1, self.eta * math.sqrt(max(0.0, s1 ** 2 * (s0 ** 2 - s1 ** 2) / max(s0 ** 2, 1e-12))))
+            s_down = math.sqrt(max(0.0, s1 ** 2 - s_up ** 2))
+            x = x + eps * (s_down - s0)
+            if s_up > 0:
+                x = x + s_up * torch.randn(x.shape, generator=generator, device="cpu").to(x.device, x.dtype)
+        return x

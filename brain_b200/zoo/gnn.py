@@ -174,3 +174,37 @@ class GnnNodeClassifier(Module):
 
     def forward(self, g: Graph, x):
         return self.l2(g, torch.relu(self.l1(g, x)))
+
+
+class GraphTransformerLayer(Module):
+    """Multi-head scaled dot-product attention restricted to each node's in-edges (self-loop added),
+    with a residual connection and LayerNorm (reference layers/transformer.rs)."""
+
+    def __init__(self, dim: int, heads: int = 4, device=None, dtype=None):
+        super().__init__()
+        self.h, self.d = heads, dim // heads
+        self.q = Linear(dim, dim, False, device, dtype)
+        self.k = Linear(dim, dim, False, device, dtype)
+        self.v = Linear(dim, dim, False, device, dtype)
+        self.o = Linear(dim, dim, True, device, dtype)
+        self.norm = torch.nn.LayerNorm(dim, device=device, dtype=dtype)
+
+    def forward(self, g: Graph, x):
+        gl = g.with_self_loops()
+        src, dst = gl.edge_index
+        N = g.num_nodes
+        q, k, v = (f(x).view(N, self.h, self.d) for f in (self.q, self.k, self.v))
+        e = (q[dst] * k[src]).sum(-1) / self.d ** 0.5  # [E, H]
+        emax = scatter_max(e, dst, N)
+        w = torch.exp(e - emax[dst])
+        alpha = w / scatter_sum(w, dst, N)[dst]
+        out = scatter_sum(v[src] * alpha[..., None], dst, N).reshape(N, -1)
+        return self.norm(x + self.o(out))
+
+
+def jumping_knowledge(layer_outputs, mode: str = "cat"):
+    """Combine the node embeddings of every layer: concatenation, element-wise max or mean (JK-Net)."""
+    if mode == "cat":
+        return torch.cat(layer_outputs, -1)
+    st = torch.stack(layer_outputs)
+    return st.max(0).values if mode == "max" else st.mean(0)

@@ -1052,3 +1052,26 @@ def test_nvtx_ranges_around_native_calls(monkeypatch):
     finally:
         _native.set_nvtx(False)
     assert seen == [("push", "brain_bpe_destroy"), ("pop",)]
+
+
+def test_graph_transformer_jk_and_euler_ancestral():
+    from brain_b200.zoo import diffusion as D
+    from brain_b200.zoo import gnn
+    g = gnn.Graph.from_undirected([(0, 1), (1, 2)], 3)
+    layer = gnn.GraphTransformerLayer(8, 2)
+    h1 = layer(g, torch.randn(3, 8))
+    h2 = layer(g, h1)
+    assert h1.shape == (3, 8) and gnn.jumping_knowledge([h1, h2]).shape == (3, 16)
+    assert gnn.jumping_knowledge([h1, h2], "max").shape == (3, 8)
+    sched = D.LinearSchedule(200)
+    x0 = torch.tensor([[0.7, -1.2]])
+
+    def oracle(x, t, cond=None):
+        ac = sched.at("alphas_cumprod", t, x)
+        return (x - ac.sqrt() * x0) / (1 - ac).sqrt()
+    out = D.EulerAncestralSampler(sched, eta=0.0).sample(oracle, (1, 2), num_steps=30,
+                                                         generator=torch.Generator().manual_seed(0))
+    torch.testing.assert_close(out, x0, atol=1e-3, rtol=0)
+    noisy = D.EulerAncestralSampler(sched, eta=1.0).sample(oracle, (1, 2), num_steps=30,
+                                                           generator=torch.Generator().manual_seed(0))
+    torch.testing.assert_close(noisy, x0, atol=1e-3, rtol=0)
