@@ -197,6 +197,120 @@ __global__ void norm_bwd_kernel(const __nv_bfloat16* __restrict__ dy, int64_t ld
   }
 }
 
+// Backward for rows of up to 8192 values: one 8-element vector per thread (T = D / 8 threads, so
+// twice as many warps per SM as the 4-vector kernel above), and the next row's x, dy and rstd are
+// loaded before the current row's reductions so that their HBM latency overlaps the block sums.
+// Same math and partial-row layout as norm_bwd_kernel.
+template <bool LAYERNORM>
+__global__ void __launch_bounds__(1024, 1)
+    norm_bwd_v1_kernel(const __nv_bfloat16* __restrict__ dy, int64_t lddy, const __nv_bfloat16* __restrict__ x,
+                       int64_t ldx, const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean_in,
+                       const float* __restrict__ rstd_in, __nv_bfloat16* __restrict__ dx, int64_t lddx,
+                       const __nv_bfloat16* __restrict__ dres, int64_t lddres, float* __restrict__ dw_part,
+                       float* __restrict__ db_part, int M, int D) {
+  __shared__ float red[32];
+  const int vi = threadIdx.x;
+  const bool on = vi < D / 8;
+  float wv[8], dwacc[8], dbacc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) dwacc[j] = dbacc[j] = wv[j] = 0.f;
+  if (on) load8(w + vi * 8, wv);
+  // the current and the next row's x and dy stay packed (8 bf16 in 16 bytes) until used
+  const bf16x8 zero = {};
+  bf16x8 xc = zero, dc = zero;
+  int64_t row = blockIdx.x;
+  float rstd_c = 0.f, mean_c = 0.f;
+  if (row < M) {
+    rstd_c = rstd_in[row];
+    if (LAYERNORM) mean_c = mean_in[row];
+    if (on) {
+      xc = *reinterpret_cast<const bf16x8*>(x + row * ldx + vi * 8);
+      dc = *reinterpret_cast<const bf16x8*>(dy + row * lddy + vi * 8);
+    }
+  }
+  for (; row < M; row += gridDim.x) {
+    const int64_t nrow = row + gridDim.x;
+    bf16x8 xn = zero, dn = zero;
+    float rstd_n = 0.f, mean_n = 0.f;
+    if (nrow < M) {
+      rstd_n = rstd_in[nrow];
+      if (LAYERNORM) mean_n = mean_in[nrow];
+      if (on) {
+        xn = *reinterpret_cast<const bf16x8*>(x + nrow * ldx + vi * 8);
+        dn = *reinterpret_cast<const bf16x8*>(dy + nrow * lddy + vi * 8);
+      }
+    }
+    float xh[8], g[8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float2 xf = __bfloat1622float2(xc.h[h]), df = __bfloat1622float2(dc.h[h]);
+      const float xv[2] = {xf.x, xf.y}, dv[2] = {df.x, df.y};
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int j = 2 * h + e;
+        xh[j] = (xv[e] - mean_c) * rstd_c;
+        g[j] = dv[e] * wv[j];
+        dwacc[j] += dv[e] * xh[j];
+        if (LAYERNORM) dbacc[j] += dv[e];
+        s1 += g[j];
+        s2 += g[j] * xh[j];
+      }
+    }
+    const float c2 = block_sum(s2, red) / D;
+    const float c1 = LAYERNORM ? block_sum(s1, red) / D : 0.f;
+    if (on) {
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = rstd_c * (g[j] - c1 - xh[j] * c2);
+      if (dres) {
+        float r[8];
+        load8(dres + row * lddres + vi * 8, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += r[j];
+      }
+      store8(dx + row * lddx + vi * 8, o);
+    }
+    xc = xn;
+    dc = dn;
+    rstd_c = rstd_n;
+    mean_c = mean_n;
+  }
+  if (on) {
+    float* p = dw_part + (int64_t)blockIdx.x * D + vi * 8;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) p[j] = dwacc[j];
+    if (LAYERNORM && db_part) {
+      float* q = db_part + (int64_t)blockIdx.x * D + vi * 8;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = dbacc[j];
+    }
+  }
+}
+
+// out[d] (+)= sum_p part[p, d] with 8 row slices per column (block 32 x 8): each thread sums every
+// 8th partial row of one column, then the 8 slice sums are added in a fixed order (deterministic).
+__global__ void colsum8_kernel(const float* __restrict__ part, int P, int D, void* out, int out_f32, int accumulate) {
+  __shared__ float sm[8][33];
+  const int d = blockIdx.x * 32 + threadIdx.x;
+  float s = 0.f;
+  if (d < D)
+    for (int p = threadIdx.y; p < P; p += 8) s += part[(int64_t)p * D + d];
+  sm[threadIdx.y][threadIdx.x] = s;
+  __syncthreads();
+  if (threadIdx.y != 0 || d >= D) return;
+  float t = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) t += sm[k][threadIdx.x];
+  if (out_f32) {
+    float* o = reinterpret_cast<float*>(out);
+    o[d] = accumulate ? o[d] + t : t;
+  } else {
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out);
+    o[d] = __float2bfloat16_rn(accumulate ? __bfloat162float(o[d]) + t : t);
+  }
+}
+
 // out[d] (+)= sum_p part[p, d]; out dtype bf16 (out_f32 = 0) or f32.
 __global__ void colsum_kernel(const float* __restrict__ part, int P, int D, void* out, int out_f32, int accumulate) {
   const int d = blockIdx.x * blockDim.x + threadIdx.x;
@@ -268,6 +382,18 @@ BRAIN_API int brain_norm_bwd(int kind, const void* dy, int64_t lddy, const void*
   auto W = reinterpret_cast<const __nv_bfloat16*>(w);
   auto DX = reinterpret_cast<__nv_bfloat16*>(dx);
   auto DR = reinterpret_cast<const __nv_bfloat16*>(dres);
+  if (D / 8 <= 1024) {  // one vector per thread, next-row prefetch
+    const int T1 = ((D / 8 + 31) / 32) * 32;
+    if (kind == 0)
+      norm_bwd_v1_kernel<false><<<P, T1, 0, st>>>(DY, lddy, X, ldx, W, mean_in, rstd_in, DX, lddx, DR, lddres, dwp,
+                                                  nullptr, M, D);
+    else
+      norm_bwd_v1_kernel<true><<<P, T1, 0, st>>>(DY, lddy, X, ldx, W, mean_in, rstd_in, DX, lddx, DR, lddres, dwp, dbp,
+                                                 M, D);
+    colsum8_kernel<<<(D + 31) / 32, dim3(32, 8), 0, st>>>(dwp, P, D, dw, dw_f32, accumulate);
+    if (kind == 1 && db) colsum8_kernel<<<(D + 31) / 32, dim3(32, 8), 0, st>>>(dbp, P, D, db, dw_f32, accumulate);
+    return (int)cudaGetLastError();
+  }
   if (kind == 0)
     norm_bwd_kernel<false><<<P, T, 0, st>>>(DY, lddy, X, ldx, W, mean_in, rstd_in, DX, lddx, DR, lddres, dwp, nullptr, M, D);
   else
