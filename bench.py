@@ -471,7 +471,7 @@ def run_gptlite_cpu(args) -> int:
 
     ctx = bdist.init(backend="gloo", device="cpu", timeout_s=300)
     rank, world = ctx.rank, ctx.world_size
-    cfg = GptLiteConfig.baseline_dp()
+    cfg = GptLiteConfig.lite_2x128()
     model = GptLite(cfg, device="cpu", dtype=torch.float32, seed=0)
     opt = AdamW(list(model.parameters()), lr=3e-4)
     g = torch.Generator().manual_seed(1 + rank)

@@ -264,7 +264,7 @@ def cmd_convert(a) -> int:
 def cmd_model(a) -> int:
     from ..models import GptLiteConfig, LlamaLiteConfig
     presets = {"llama3-8b": LlamaLiteConfig.llama3_8b(), "llama3-70b": LlamaLiteConfig.llama3_70b(),
-               "llama-tiny": LlamaLiteConfig.tiny(), "gpt-lite": GptLiteConfig.baseline_dp()}
+               "llama-tiny": LlamaLiteConfig.tiny(), "gpt-lite": GptLiteConfig.lite_2x128()}
     names = [a.name] if a.name else list(presets)
     for n in names:
         c = presets[n]
@@ -303,7 +303,7 @@ def cmd_train(a) -> int:
     from ..parallel import DataParallel, dist as bdist
     ctx = bdist.init()
     if a.model == "gpt-lite":
-        cfg = GptLiteConfig.baseline_dp()
+        cfg = GptLiteConfig.lite_2x128()
         model = GptLite(cfg, device=ctx.device, dtype=torch.float32 if ctx.device.type == "cpu" else torch.bfloat16)
     else:
         cfg = {"llama3-8b": LlamaLiteConfig.llama3_8b(a.seq), "llama-tiny": LlamaLiteConfig.tiny()}[a.model]

@@ -71,7 +71,7 @@ class GptLiteConfig:
     init_std: float = 0.02
 
     @staticmethod
-    def baseline_dp() -> "GptLiteConfig":
+    def lite_2x128() -> "GptLiteConfig":
         """2 layers, d 128, 4 heads, FFN 512 GELU, LN, learned positions, vocab 1024, seq 64."""
         return GptLiteConfig()
 

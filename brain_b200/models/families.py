@@ -2,7 +2,7 @@
 
 * ``GptLite`` (crates/brain-transformer/src/models/gpt_lite.rs:24-171): token + learned position
   embedding followed by an embedding LayerNorm, pre-LN causal decoder with tanh-GELU FFN, final
-  norm, bias-free LM head. BASELINE configuration #1 is ``GptLiteConfig.baseline_dp()``.
+  norm, bias-free LM head. The 2-layer, d 128 data-parallel training workload uses ``GptLiteConfig.lite_2x128()``.
 * ``BertLite`` (bert_lite.rs:23-200): token + position + token-type embeddings with LayerNorm,
   post-LN bidirectional encoder, tanh pooler over [CLS], classification head, optional MLM head.
 * ``T5Lite`` (t5_lite.rs:25-200): RMSNorm pre-norm encoder/decoder with bucketed relative position

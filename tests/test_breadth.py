@@ -284,7 +284,7 @@ def test_fault_policy_retry_and_failfast():
 def test_gpt_lite_matches_float64_oracle_and_trains():
     from brain_b200.models import GptLite, GptLiteConfig
     from brain_b200.optim import AdamW
-    cfg = GptLiteConfig.baseline_dp()
+    cfg = GptLiteConfig.lite_2x128()
     m32 = GptLite(cfg, dtype=torch.float32, seed=0)
     m64 = GptLite(cfg, dtype=torch.float64, seed=0)
     m64.load_state_dict({k: v.double() for k, v in m32.state_dict().items()})
