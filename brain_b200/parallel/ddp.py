@@ -81,6 +81,19 @@ class DataParallel:
         self.steps += 1
         return loss.detach()
 
+    def save_checkpoint(self, directory: str, metadata: dict | None = None) -> None:
+        """Collective: every rank writes its optimizer-state shard, rank 0 the weights
+        (``checkpoint.sharded``)."""
+        from ..checkpoint.sharded import save_sharded
+        save_sharded(self, directory, metadata)
+
+    def load_checkpoint(self, directory: str) -> dict:
+        """Collective: restores weights and this rank's optimizer state, from any saved world size."""
+        from ..checkpoint.sharded import load_sharded
+        meta = load_sharded(self, directory)
+        self.steps = self.optimizer.step_count
+        return meta
+
     def sync_gradients(self) -> None:
         """All-reduce gradients as the mean over ranks (flat bucket, in place)."""
         self.flat.absorb_grads()

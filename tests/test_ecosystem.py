@@ -836,7 +836,7 @@ def _sharded_rank(rank, world, directory, phase):
                 dp.train_step(*batch(s))
             save_sharded(dp, directory, {"note": "two steps"})
         else:
-            meta = load_sharded(dp, directory)
+            meta = load_sharded(dp, directory) if phase != "resume" else dp.load_checkpoint(directory)
             assert meta["note"] == "two steps" and dp.optimizer.step_count == 2
             if phase == "load_only":
                 f = dp.flat
