@@ -119,3 +119,36 @@ class BestModelTracker:
         if better:
             self.best = meta
         return better
+
+
+class PeriodicCheckpointer(TrainingCallback):
+    """Saves ``trainer.state()`` as a ``.brain`` text checkpoint every ``every`` epochs (and the best
+    epoch by loss as ``best.brain``), keeping the ``keep_last`` most recent periodic files
+    (reference checkpointer.rs:9-62 with ``BestModelTracker``). ``latest()`` returns the newest path
+    for resuming with ``Trainer.load_state(ModelState.load_file(path))``."""
+
+    def __init__(self, directory: str, every: int = 1, keep_last: int = 3):
+        import os
+
+        os.makedirs(directory, exist_ok=True)
+        self.dir, self.every, self.keep_last = directory, max(1, every), keep_last
+        self.saved: list[str] = []
+        self.best = BestModelTracker("min")
+
+    def on_epoch_end(self, trainer, epoch, loss):
+        import os
+
+        if (epoch + 1) % self.every == 0:
+            path = os.path.join(self.dir, f"epoch{epoch + 1:06d}.brain")
+            trainer.state({"epoch": str(epoch + 1), "loss": repr(float(loss))}).save_file(path)
+            self.saved.append(path)
+            while len(self.saved) > self.keep_last:
+                old = self.saved.pop(0)
+                if os.path.exists(old):
+                    os.remove(old)
+        if self.best.update(CheckpointMeta(epoch + 1, 0, float(loss), os.path.join(self.dir, "best.brain"))):
+            trainer.state({"epoch": str(epoch + 1), "loss": repr(float(loss))}).save_file(self.best.best.path)
+        return False
+
+    def latest(self):
+        return self.saved[-1] if self.saved else None

@@ -1075,3 +1075,24 @@ def test_graph_transformer_jk_and_euler_ancestral():
     noisy = D.EulerAncestralSampler(sched, eta=1.0).sample(oracle, (1, 2), num_steps=30,
                                                            generator=torch.Generator().manual_seed(0))
     torch.testing.assert_close(noisy, x0, atol=1e-3, rtol=0)
+
+
+def test_periodic_checkpointer_keeps_last_and_resumes(tmp_path):
+    import os
+    from brain_b200.checkpoint.formats import ModelState
+    from brain_b200.train import Batch, TrainerBuilder
+    from brain_b200.train.callbacks import PeriodicCheckpointer
+    torch.manual_seed(0)
+    x, y = torch.randn(32, 4), torch.randint(0, 3, (32,))
+    model = torch.nn.Sequential(torch.nn.Linear(4, 8), torch.nn.ReLU(), torch.nn.Linear(8, 3))
+    tr = TrainerBuilder().model(model).learning_rate(0.1).build()
+    ck = PeriodicCheckpointer(str(tmp_path), every=2, keep_last=2)
+    tr.callbacks.append(ck)
+    tr.fit([Batch(x, y)], epochs=8)
+    files = sorted(f for f in os.listdir(tmp_path) if f.startswith("epoch"))
+    assert files == ["epoch000006.brain", "epoch000008.brain"] and os.path.exists(tmp_path / "best.brain")
+    model2 = torch.nn.Sequential(torch.nn.Linear(4, 8), torch.nn.ReLU(), torch.nn.Linear(8, 3))
+    tr2 = TrainerBuilder().model(model2).learning_rate(0.1).build()
+    tr2.load_state(ModelState.load_file(ck.latest()))
+    for a, b in zip(model.parameters(), model2.parameters()):
+        torch.testing.assert_close(a, b)
