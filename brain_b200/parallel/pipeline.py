@@ -63,13 +63,16 @@ class PipelineStage:
         return t
 
     def _send(self, t, dst):
+        """Non-blocking on every backend: two neighbouring stages may both be sending (an activation
+        forward, a gradient backward) in the same 1F1B phase, and blocking sends would wait on each
+        other. Returns (work, tensor); the tensor is kept alive until the work is waited on."""
+        t = t.contiguous()
         if self.comm_stream is not None:
             self.comm_stream.wait_stream(torch.cuda.current_stream())
             with torch.cuda.stream(self.comm_stream):
-                work = dist.isend(t.contiguous(), dst, group=self.group)
-            return work
-        dist.send(t.contiguous(), dst, group=self.group)
-        return None
+                work = dist.isend(t, dst, group=self.group)
+            return work, t
+        return dist.isend(t, dst, group=self.group), t
 
     def step_1f1b(self, microbatches=None, targets=None) -> float:
         """Run one optimizer-step's worth of micro-batches. Returns the mean loss on the last stage."""
@@ -100,7 +103,7 @@ class PipelineStage:
                     w = self._send(x.grad, self.prev)
                     if w is not None:
                         pending.append(w)
-        for w in pending:
+        for w, _ in pending:
             w.wait()
         if self.comm_stream is not None:
             torch.cuda.current_stream().wait_stream(self.comm_stream)

@@ -1096,3 +1096,72 @@ def test_periodic_checkpointer_keeps_last_and_resumes(tmp_path):
     tr2.load_state(ModelState.load_file(ck.latest()))
     for a, b in zip(model.parameters(), model2.parameters()):
         torch.testing.assert_close(a, b)
+
+
+# ------------------------------------------------------------------ context / pipeline parallel on Gloo
+def _cp_rank(rank, world):
+    from brain_b200.models.blocks import sdpa_with_bias
+    from brain_b200.parallel import dist as bdist
+    from brain_b200.parallel.sequence import gather_sequence, ring_attention, scatter_sequence, ulysses_attention
+    bdist.init(device="cpu", timeout_s=60)
+    try:
+        g = torch.Generator().manual_seed(0)
+        B, S, H, Hkv, D = 2, 24, 4, 2, 8
+        q, k, v = torch.randn(B, S, H, D, generator=g), torch.randn(B, S, Hkv, D, generator=g), \
+            torch.randn(B, S, Hkv, D, generator=g)
+        ref = sdpa_with_bias(q, k, v, None, True)
+        ql, kl, vl = (scatter_sequence(t, rank, world) for t in (q, k, v))
+        ring = gather_sequence(ring_attention(ql, kl, vl, rank, world, causal=True), world)
+        kf, vf = k.repeat_interleave(H // Hkv, 2), v.repeat_interleave(H // Hkv, 2)
+        uly = gather_sequence(ulysses_attention(ql, scatter_sequence(kf, rank, world),
+                                                scatter_sequence(vf, rank, world), world, causal=True), world)
+        return float((ring - ref).abs().max()), float((uly - ref).abs().max())
+    finally:
+        bdist.shutdown()
+
+
+def test_ring_and_ulysses_attention_match_full_attention():
+    res = run_ranks(_cp_rank, 2, timeout=120)
+    for r in range(2):
+        assert res[r][0] < 1e-5 and res[r][1] < 1e-5
+
+
+def _pp_rank(rank, world):
+    import torch.distributed as dist
+    from brain_b200.parallel import dist as bdist
+    from brain_b200.parallel.pipeline import PipelineStage
+    bdist.init(device="cpu", timeout_s=60)
+    try:
+        torch.manual_seed(0)
+        layers = [torch.nn.Linear(8, 8) for _ in range(4)]
+        stage = torch.nn.Sequential(*layers[2 * rank:2 * rank + 2])
+        g = torch.Generator().manual_seed(1)
+        mbs = [torch.randn(3, 8, generator=g) for _ in range(4)]
+        tgts = [torch.randn(3, 8, generator=g) for _ in range(4)]
+        ps = PipelineStage(stage, rank, world, 4, (3, 8), dtype=torch.float32,
+                           loss_fn=lambda y, t: torch.nn.functional.mse_loss(y, t))
+        loss = ps.step_1f1b(mbs if rank == 0 else None, tgts if rank == world - 1 else None)
+        grads = [p.grad.clone() for p in stage.parameters()]
+        return loss, [gr.tolist() for gr in grads]
+    finally:
+        bdist.shutdown()
+
+
+def test_pipeline_1f1b_matches_single_process_gradients():
+    res = run_ranks(_pp_rank, 2, timeout=120)
+    torch.manual_seed(0)
+    layers = [torch.nn.Linear(8, 8) for _ in range(4)]
+    full = torch.nn.Sequential(*layers)
+    g = torch.Generator().manual_seed(1)
+    mbs = [torch.randn(3, 8, generator=g) for _ in range(4)]
+    tgts = [torch.randn(3, 8, generator=g) for _ in range(4)]
+    total = 0.0
+    for x, t in zip(mbs, tgts):
+        loss = torch.nn.functional.mse_loss(full(x), t) / 4
+        loss.backward()
+        total += float(loss) * 4
+    assert abs(res[1][0] - total / 4) < 1e-5
+    ref = [p.grad for p in full.parameters()]
+    got = [torch.tensor(x) for x in res[0][1] + res[1][1]]
+    for a, b in zip(got, ref):
+        torch.testing.assert_close(a, b, atol=1e-6, rtol=1e-5)
