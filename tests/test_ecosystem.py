@@ -1165,3 +1165,26 @@ def test_pipeline_1f1b_matches_single_process_gradients():
     got = [torch.tensor(x) for x in res[0][1] + res[1][1]]
     for a, b in zip(got, ref):
         torch.testing.assert_close(a, b, atol=1e-6, rtol=1e-5)
+
+
+def test_heartbeat_detects_a_rank_that_stops():
+    import time
+    import torch.distributed as dist
+    from brain_b200.parallel.fault import FaultPolicy, Heartbeat, StepFailed, run_step_with_policy
+    store = dist.HashStore()
+    hb = [Heartbeat(store, r, 3, interval_s=0.05, timeout_s=0.4).start() for r in range(3)]
+    time.sleep(0.3)
+    assert hb[0].dead_ranks() == []
+    hb[2].stop()  # rank 2 goes silent (a crashed or hung process)
+    deadline = time.time() + 5
+    dead = []
+    while time.time() < deadline and dead != [2]:
+        dead = hb[0].dead_ranks()
+        time.sleep(0.05)
+    assert dead == [2]
+    with pytest.raises(StepFailed) as e:
+        run_step_with_policy(lambda: (_ for _ in ()).throw(TimeoutError("collective timed out")),
+                             FaultPolicy.EXCLUDE_RANK, heartbeat=hb[0])
+    assert e.value.dead_ranks == [2]
+    for h in hb:
+        h.stop()
