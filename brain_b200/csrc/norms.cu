@@ -33,39 +33,38 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
 
 // ---------------------------------------------------------------- forward
 template <bool LAYERNORM>
-__global__ void norm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ res,
-                                int64_t ldres, const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ b,
-                                __nv_bfloat16* __restrict__ y, int64_t ldy, __nv_bfloat16* __restrict__ sum_out,
-                                int64_t ldsum, float* __restrict__ mean_out, float* __restrict__ rstd_out, int D,
-                                float eps) {
+__global__ void __launch_bounds__(1024) norm_fwd_kernel(
+    const __nv_bfloat16* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ res, int64_t ldres,
+    const __nv_bfloat16* __restrict__ w, const __nv_bfloat16* __restrict__ b, __nv_bfloat16* __restrict__ y,
+    int64_t ldy, __nv_bfloat16* __restrict__ sum_out, int64_t ldsum, float* __restrict__ mean_out,
+    float* __restrict__ rstd_out, int D, float eps) {
   __shared__ float red[32];
   const int64_t row = blockIdx.x;
   const int nvec = D / 8;
-  float v[VPT][8];
-  uint4 wraw[VPT];  // gamma, requested with the row so that its load overlaps the reduction
+  // the row stays packed (8 bf16 per 16 bytes) in registers and is unpacked where it is used: fewer
+  // registers per thread means more resident CTAs, i.e. more rows in flight per SM
+  bf16x8 v[VPT];
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
-    if (vi < nvec) wraw[i] = __ldg(reinterpret_cast<const uint4*>(w + vi * 8));
-  }
-#pragma unroll
-  for (int i = 0; i < VPT; ++i) {
-    const int vi = threadIdx.x + i * blockDim.x;
     if (vi < nvec) {
-      load8(x + row * ldx + vi * 8, v[i]);
+      v[i] = *reinterpret_cast<const bf16x8*>(x + row * ldx + vi * 8);
       if (res) {
-        float r[8];
-        load8(res + row * ldres + vi * 8, r);
+        const bf16x8 r = *reinterpret_cast<const bf16x8*>(res + row * ldres + vi * 8);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int k = 0; k < 4; ++k) {
           // the sum is rounded to bf16 before normalisation, exactly what a separate add would store
-          v[i][j] = __bfloat162float(__float2bfloat16_rn(v[i][j] + r[j]));
+          const float2 a = __bfloat1622float2(v[i].h[k]), c = __bfloat1622float2(r.h[k]);
+          v[i].h[k] = __floats2bfloat162_rn(a.x + c.x, a.y + c.y);
         }
-        store8(sum_out + row * ldsum + vi * 8, v[i]);
+        *reinterpret_cast<bf16x8*>(sum_out + row * ldsum + vi * 8) = v[i];
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) s += LAYERNORM ? v[i][j] : v[i][j] * v[i][j];
+      for (int k = 0; k < 4; ++k) {
+        const float2 a = __bfloat1622float2(v[i].h[k]);
+        s += LAYERNORM ? a.x + a.y : a.x * a.x + a.y * a.y;
+      }
     }
   }
   float mean = 0.f, rstd;
@@ -77,9 +76,9 @@ __global__ void norm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx
       const int vi = threadIdx.x + i * blockDim.x;
       if (vi < nvec) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float d = v[i][j] - mean;
-          q += d * d;
+        for (int k = 0; k < 4; ++k) {
+          const float2 a = __bfloat1622float2(v[i].h[k]);
+          q += (a.x - mean) * (a.x - mean) + (a.y - mean) * (a.y - mean);
         }
       }
     }
@@ -95,22 +94,22 @@ __global__ void norm_fwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx
   for (int i = 0; i < VPT; ++i) {
     const int vi = threadIdx.x + i * blockDim.x;
     if (vi < nvec) {
-      float wv[8], o[8];
-      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wraw[i]);
+      float wv[8], o[8], xv[8];
+      load8(w + vi * 8, wv);
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
-        const float2 f = __bfloat1622float2(w2[k]);
-        wv[2 * k] = f.x;
-        wv[2 * k + 1] = f.y;
+        const float2 a = __bfloat1622float2(v[i].h[k]);
+        xv[2 * k] = a.x;
+        xv[2 * k + 1] = a.y;
       }
       if (LAYERNORM && b) {
         float bv[8];
         load8(b + vi * 8, bv);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = (v[i][j] - mean) * rstd * wv[j] + bv[j];
+        for (int j = 0; j < 8; ++j) o[j] = (xv[j] - mean) * rstd * wv[j] + bv[j];
       } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = (v[i][j] - mean) * rstd * wv[j];
+        for (int j = 0; j < 8; ++j) o[j] = (xv[j] - mean) * rstd * wv[j];
       }
       store8(y + row * ldy + vi * 8, o);
     }
