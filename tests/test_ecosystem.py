@@ -1188,3 +1188,15 @@ def test_heartbeat_detects_a_rank_that_stops():
     assert e.value.dead_ranks == [2]
     for h in hb:
         h.stop()
+
+
+def test_bench_report_scaling_table(tmp_path):
+    import json as _json
+    from brain_b200.bench.report import load_runs, scaling_table
+    p = tmp_path / "runs.log"
+    p.write_text("\n".join(["warming up...", _json.dumps({"value": 18000.0, "n_gpus": 1, "ms_per_step": 450.0,
+                                                          "unit": "tokens/s"}),
+                            _json.dumps({"value": 140000.0, "n_gpus": 8, "ms_per_step": 468.0, "unit": "tokens/s"}),
+                            _json.dumps({"impl": "reference", "unavailable": "x"})]))
+    t = scaling_table(load_runs([str(p)]))
+    assert "| 8 | 140,000 | 468.0 | 17,500 | 0.972 |" in t and t.count("\n") == 3
