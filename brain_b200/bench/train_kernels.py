@@ -30,6 +30,9 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default="")
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--graph", action="store_true",
+                    help="replay each case from a CUDA graph, so short kernels are timed without the per-call "
+                         "host overhead (cases that cannot be captured fall back to eager calls)")
     a = ap.parse_args(argv)
     only = set(x for x in a.only.split(",") if x)
 
@@ -50,10 +53,27 @@ def main(argv=None) -> int:
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
+        run = fn
+        if a.graph:
+            try:
+                graph = torch.cuda.CUDAGraph()
+                side = torch.cuda.Stream()
+                side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(side):
+                    with torch.cuda.graph(graph):
+                        fn()
+                torch.cuda.current_stream().wait_stream(side)
+                run = graph.replay
+                run()
+                torch.cuda.synchronize()
+            except Exception as exc:  # not capturable: time eager calls
+                print(json.dumps({"graph_capture_failed": str(exc)[:200]}), flush=True)
+                torch.cuda.synchronize()
+                run = fn
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         for _ in range(a.iters):
-            fn()
+            run()
         e.record()
         torch.cuda.synchronize()
         return s.elapsed_time(e) / a.iters
