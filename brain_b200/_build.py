@@ -41,9 +41,10 @@ LIBRARIES = {
     ],
     "brain_comm": ["host_utils.cu", "comm.cu"],
 }
-# Host-only C++ libraries (g++): the checkpoint codec, the native token loader and the BPE encoder.
+# Host-only C++ libraries (g++): the checkpoint codec, the native token loader, the BPE encoder and the
+# float64 CPU oracle kernels.
 CXX_LIBRARIES = {
-    "brain_runtime": ["codec.cpp", "loader.cpp", "bpe.cpp"],
+    "brain_runtime": ["codec.cpp", "loader.cpp", "bpe.cpp", "oracle.cpp"],
 }
 
 

@@ -9,6 +9,7 @@ import brain_b200.models.llama_tp  # noqa: F401
 import brain_b200.parallel.overlap  # noqa: F401
 import brain_b200.checkpoint  # noqa: F401
 import brain_b200.data  # noqa: F401
+import brain_b200.oracle  # noqa: F401
 from brain_b200 import _native
 
 CSRC = os.path.join(os.path.dirname(_native.__file__), "csrc")
