@@ -42,3 +42,27 @@ def test_rope_and_attention():
     one = O.attention(_r(1, 1, 1, 8, seed=10), k[:1, :1, :1], v[:1, :1, :1], causal=True)
     torch.testing.assert_close(one[0, 0, 0], v[0, 0, 0])
     assert math.isfinite(float(one.sum()))
+
+
+import pytest  # noqa: E402
+
+
+@pytest.mark.gpu
+def test_gpu_kernels_against_the_float64_oracle():
+    """tcgen05 flash attention, the RMSNorm kernel and the cross-entropy kernel (bf16 inputs) against the
+    C++ float64 oracle on the same bf16 values."""
+    from brain_b200 import ops
+    g = torch.Generator(device="cuda").manual_seed(0)
+    B, S, Hq, Hkv, D = 1, 256, 4, 2, 128
+    q = torch.randn(B, S, Hq, D, device="cuda", generator=g).bfloat16()
+    k = torch.randn(B, S, Hkv, D, device="cuda", generator=g).bfloat16()
+    v = torch.randn(B, S, Hkv, D, device="cuda", generator=g).bfloat16()
+    o = ops.flash_attention(q, k, v, causal=True)
+    torch.testing.assert_close(o.double().cpu(), O.attention(q, k, v, True), rtol=3e-2, atol=3e-2)
+    x = torch.randn(64, 4096, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(4096, device="cuda", generator=g) * 0.1 + 1).bfloat16()
+    torch.testing.assert_close(ops.rms_norm(x, w, 1e-6).double().cpu(), O.rms_norm(x, w, 1e-6), rtol=2e-2, atol=2e-2)
+    logits = torch.randn(32, 1000, device="cuda", generator=g).bfloat16()
+    labels = torch.randint(0, 1000, (32,), device="cuda", generator=g)
+    assert abs(float(ops.cross_entropy(logits, labels)) - float(O.cross_entropy(logits, labels))) < 1e-3
+    assert not ops.check_status()
