@@ -120,6 +120,12 @@ class Tensor(_Base):
     __radd__ = __add__
     __rmul__ = __mul__
 
+    def __rsub__(self, o):
+        return Tensor._of(torch.sub(_unwrap(o), self._t))
+
+    def __neg__(self):
+        return Tensor._of(-self._t)
+
 
 class Value(_Base):
     """Autograd node: ``grad`` is a ``Tensor`` after ``backward()``, ``None`` before."""
