@@ -1200,3 +1200,32 @@ def test_bench_report_scaling_table(tmp_path):
                             _json.dumps({"impl": "reference", "unavailable": "x"})]))
     t = scaling_table(load_runs([str(p)]))
     assert "| 8 | 140,000 | 468.0 | 17,500 | 0.972 |" in t and t.count("\n") == 3
+
+
+def test_bert_t5_vit_train_steps_on_cpu():
+    from brain_b200.models import BertLite, T5Lite, ViT
+    from brain_b200.models.config import BertLiteConfig, T5LiteConfig, ViTConfig
+    torch.manual_seed(0)
+    bert = BertLite(BertLiteConfig(vocab_size=100, hidden_dim=32, num_layers=2, num_heads=4, intermediate_dim=64,
+                                   max_seq_len=16, num_labels=3))
+    t5 = T5Lite(T5LiteConfig(vocab_size=100, hidden_dim=32, num_layers=1, num_decoder_layers=1, num_heads=4,
+                             intermediate_dim=64, max_seq_len=16))
+    vit = ViT(ViTConfig(image_size=32, patch_size=8, hidden_dim=32, num_layers=1, num_heads=4, mlp_dim=64,
+                        num_classes=5))
+    ids, src, tgt = torch.randint(0, 100, (4, 12)), torch.randint(0, 100, (4, 10)), torch.randint(0, 100, (4, 7))
+    imgs, ylab = torch.randn(4, 3, 32, 32), torch.randint(0, 5, (4,))
+    losses = {}
+    for name, model, fn in (
+            ("bert", bert, lambda: torch.nn.functional.cross_entropy(bert(ids), torch.tensor([0, 1, 2, 0]))),
+            ("t5", t5, lambda: torch.nn.functional.cross_entropy(t5(src, tgt).reshape(-1, 100), tgt.reshape(-1))),
+            ("vit", vit, lambda: vit.loss(imgs, ylab))):
+        opt = torch.optim.Adam(model.parameters(), lr=3e-3)
+        seq = []
+        for _ in range(15):
+            loss = fn()
+            opt.zero_grad()
+            loss.backward()
+            opt.step()
+            seq.append(float(loss.detach()))
+        losses[name] = seq
+        assert seq[-1] < seq[0], (name, seq)
