@@ -1229,3 +1229,41 @@ def test_bert_t5_vit_train_steps_on_cpu():
             seq.append(float(loss.detach()))
         losses[name] = seq
         assert seq[-1] < seq[0], (name, seq)
+
+
+def test_kv_caches_contiguous_and_paged():
+    from brain_b200.models.kv_cache import KvCache, KvCacheConfig, PagedKvCache
+    c = KvCache(KvCacheConfig(2, 2, 2, 4, 8, torch.float32, "cpu"))
+    k1, v1 = torch.randn(2, 3, 2, 4), torch.randn(2, 3, 2, 4)
+    fk, fv = c.update(0, k1, v1)
+    k2 = torch.randn(2, 2, 2, 4)
+    fk, fv = c.update(0, k2, k2)
+    assert c.current_seq_len(0) == 5 and c.current_seq_len(1) == 0
+    torch.testing.assert_close(fk, torch.cat([k1, k2], 1))
+    with pytest.raises(ValueError, match="overflow"):
+        c.update(0, torch.randn(2, 4, 2, 4), torch.randn(2, 4, 2, 4))
+    c.clear()
+    assert c.current_seq_len(0) == 0
+    p = PagedKvCache(1, 6, 4, 2, 4, torch.float32, "cpu")
+    seqs = {0: torch.randn(7, 2, 4), 1: torch.randn(5, 2, 4)}
+    for sid in seqs:
+        p.add_sequence(sid)
+    # prefill token by token for seq 0 and in one go for seq 1, interleaving block allocation
+    for t in range(7):
+        p.reserve(0, 1)
+        p.write(0, p.slot_mapping([0], 1), seqs[0][t:t + 1], seqs[0][t:t + 1] * 2)
+        p.advance([0], 1)
+    p.reserve(1, 5)
+    p.write(0, p.slot_mapping([1], 5), seqs[1], seqs[1] * 2)
+    p.advance([1], 5)
+    for sid, ref in seqs.items():
+        k, v = p.gather(0, sid)
+        torch.testing.assert_close(k, ref)
+        torch.testing.assert_close(v, ref * 2)
+    assert p.lengths_tensor([0, 1]).tolist() == [7, 5] and p.block_table_tensor([0, 1]).shape == (2, 2)
+    assert len(p.free) == 2
+    p.free_sequence(0)
+    assert len(p.free) == 4
+    p.add_sequence(2)
+    with pytest.raises(RuntimeError, match="out of blocks"):
+        p.reserve(2, 17)
