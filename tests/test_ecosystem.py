@@ -1267,3 +1267,41 @@ def test_kv_caches_contiguous_and_paged():
     p.add_sequence(2)
     with pytest.raises(RuntimeError, match="out of blocks"):
         p.reserve(2, 17)
+
+
+def test_sampling_penalty_filters_and_greedy():
+    from brain_b200.models.generate import (GenerationConfig, apply_repetition_penalty, filter_logits,
+                                            sample_next_token)
+    logits = torch.tensor([[2.0, -1.0, 0.5, 3.0, 1.0]])
+    hist = torch.tensor([[0, 1]])
+    pen = apply_repetition_penalty(logits, hist, 2.0)
+    assert torch.allclose(pen, torch.tensor([[1.0, -2.0, 0.5, 3.0, 1.0]]))
+    assert apply_repetition_penalty(logits, hist, 1.0) is logits
+    # top-k keeps the k largest
+    fk = filter_logits(logits, top_k=2)
+    assert torch.isfinite(fk).tolist() == [[True, False, False, True, False]]
+    # top-p keeps the smallest prefix whose mass reaches p (the token crossing p stays)
+    p = torch.softmax(logits, -1)[0]
+    order = torch.argsort(p, descending=True)
+    cum = p[order].cumsum(0)
+    keep_n = int((cum - p[order] <= 0.8).sum())
+    fp = filter_logits(logits, top_p=0.8)
+    assert int(torch.isfinite(fp).sum()) == keep_n
+    assert set(torch.nonzero(torch.isfinite(fp[0])).flatten().tolist()) == set(order[:keep_n].tolist())
+    # min-p drops tokens below min_p * max prob
+    fm = filter_logits(logits, min_p=0.3)
+    kept = (p >= p.max() * 0.3).tolist()
+    assert torch.isfinite(fm[0]).tolist() == kept
+    # greedy after the penalty: token 0 (2.0) would beat token 4 (1.0) but not token 3
+    cfg = GenerationConfig(temperature=0.0, repetition_penalty=10.0)
+    assert sample_next_token(torch.tensor([[5.0, 0.0, 0.0, 4.0]]), cfg, torch.tensor([[0]])).item() == 3
+    # sampling with top_k=1 is deterministic
+    cfg = GenerationConfig(temperature=1.0, top_k=1, top_p=1.0, repetition_penalty=1.0)
+    g = torch.Generator().manual_seed(0)
+    out = sample_next_token(logits.repeat(8, 1), cfg, None, g)
+    assert out.tolist() == [3] * 8
+    # empirical distribution follows softmax(logits / T) when nothing is filtered
+    cfg = GenerationConfig(temperature=2.0, top_k=0, top_p=1.0, min_p=0.0, repetition_penalty=1.0)
+    draws = sample_next_token(logits.repeat(20000, 1), cfg, None, torch.Generator().manual_seed(1))
+    freq = torch.bincount(draws, minlength=5).float() / draws.numel()
+    assert torch.allclose(freq, torch.softmax(logits[0] / 2.0, -1), atol=0.015)
