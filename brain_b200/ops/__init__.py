@@ -6,7 +6,7 @@ CPU tensors run a float32 PyTorch restatement of the same op, which is also the 
 from . import _common  # noqa: F401  (registers signatures)
 from ._common import check_status  # noqa: F401
 from .gemm import gemm  # noqa: F401
-from .norms import rms_norm, layer_norm, add_rms_norm, add_layer_norm  # noqa: F401
+from .norms import rms_norm, layer_norm, add_rms_norm, add_layer_norm, fused_layer_norm  # noqa: F401
 from .activations import swiglu, gelu  # noqa: F401
 from .rope import rope_table, apply_rope, apply_rope_  # noqa: F401
 from .attention import flash_attention, flash_attention_fwd, qkv_attention, sdpa_ref  # noqa: F401

@@ -140,3 +140,18 @@ def add_layer_norm(x, r, w, b=None, eps=1e-5):
         return _AddNormFn.apply(x, r, w, b, eps, _LN)
     s = x + r
     return layer_norm_ref(s, w, b, eps), s
+
+
+def fused_layer_norm(x, w, b=None, eps=1e-5):
+    """LayerNorm with the one-pass variance of the reference's fused variant: var = max(E[x^2] - E[x]^2, 0)
+    (crates/brain-transformer/src/ops_fused.rs:62-64). On CUDA tensors the LayerNorm kernel runs; it takes
+    the two-pass variance, which equals the one-pass form in exact arithmetic and does not cancel."""
+    if x.is_cuda:
+        return layer_norm(x, w, b, eps)
+    xf = x.float()
+    mu = xf.mean(-1, keepdim=True)
+    var = (xf.pow(2).mean(-1, keepdim=True) - mu.pow(2)).clamp_min(0.0)
+    y = (xf - mu) * torch.rsqrt(var + eps) * w.float()
+    if b is not None:
+        y = y + b.float()
+    return y.to(x.dtype)

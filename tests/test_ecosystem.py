@@ -1305,3 +1305,15 @@ def test_sampling_penalty_filters_and_greedy():
     draws = sample_next_token(logits.repeat(20000, 1), cfg, None, torch.Generator().manual_seed(1))
     freq = torch.bincount(draws, minlength=5).float() / draws.numel()
     assert torch.allclose(freq, torch.softmax(logits[0] / 2.0, -1), atol=0.015)
+
+
+def test_fused_layer_norm_one_pass_variance():
+    from brain_b200.ops import fused_layer_norm, layer_norm
+    torch.manual_seed(0)
+    x = torch.randn(6, 64, dtype=torch.float64)
+    w, b = torch.randn(64, dtype=torch.float64), torch.randn(64, dtype=torch.float64)
+    assert torch.allclose(fused_layer_norm(x, w, b), layer_norm(x, w, b), atol=1e-5)
+    # a constant row: the one-pass variance may round below zero; the clamp keeps it finite
+    c = torch.full((2, 64), 1e4, dtype=torch.float32) + torch.tensor([[0.0], [1e-3]])
+    y = fused_layer_norm(c, torch.ones(64), None)
+    assert torch.isfinite(y).all()
