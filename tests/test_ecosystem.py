@@ -1317,3 +1317,13 @@ def test_fused_layer_norm_one_pass_variance():
     c = torch.full((2, 64), 1e4, dtype=torch.float32) + torch.tensor([[0.0], [1e-3]])
     y = fused_layer_norm(c, torch.ones(64), None)
     assert torch.isfinite(y).all()
+
+
+def test_adamw_group_weight_decay_overrides_default():
+    from brain_b200.optim.optimizers import AdamW
+    a, b = torch.nn.Parameter(torch.ones(2)), torch.nn.Parameter(torch.ones(2))
+    opt = AdamW([{"params": [a]}, {"params": [b], "weight_decay": 0.0}], lr=0.1, weight_decay=0.5)
+    a.grad, b.grad = torch.zeros(2), torch.zeros(2)
+    opt.step()
+    # decoupled decay p -= lr * wd * p before the moments; a zero gradient leaves only the decay
+    assert torch.allclose(a.data, torch.full((2,), 0.95)) and torch.equal(b.data, torch.ones(2))
