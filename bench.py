@@ -198,12 +198,16 @@ def main():
     bdist.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    trace = []  # device scalars: reading them after the loop adds no synchronisation to it
     with _native.launch_counter() as lc:
         start.record()
         for i in range(args.steps):
             loss = step_dev(args.warmup + i)
+            trace.append(loss)
         end.record()
     torch.cuda.synchronize()
+    if rank == 0:
+        log("losses (timed loop): " + " ".join(f"{float(x):.4f}" for x in trace))
     bdist.barrier()
     clk = clocks.stop() if clocks else None
     ms = start.elapsed_time(end) / args.steps
@@ -328,13 +332,17 @@ def run_torch_baseline(args) -> int:
     barrier()
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    trace = []
     s.record()
     for i in range(args.steps):
         loss = step(pool[i % 4])
+        trace.append(loss.detach())
     e.record()
     torch.cuda.synchronize()
     barrier()
     clk = clocks.stop() if clocks else None
+    if rank == 0:
+        log("losses (timed loop): " + " ".join(f"{float(x):.4f}" for x in trace))
     ms = max_ms(s.elapsed_time(e) / args.steps)
     host = [torch.randint(0, V, (B, S + 1), generator=torch.Generator().manual_seed(100 + rank * 1000 + i)).pin_memory()
             for i in range(4)]
