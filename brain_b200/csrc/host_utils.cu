@@ -50,7 +50,7 @@ bool encode_tiled(CUtensorMap* map, CUtensorMapDataType dt, uint32_t rank, void*
 }  // namespace brain_host
 
 BRAIN_API const char* brain_error_string(int code) {
-  if (code == -2) return "size exceeds the fixed scratch of the no-allocation entry point (D > 8192)";
+  if (code == -1000) return "size exceeds the fixed scratch of the no-allocation entry point (D > 8192)";
   if (code < 0) return "brain runtime error";
   return cudaGetErrorString(static_cast<cudaError_t>(code));
 }

@@ -7,7 +7,7 @@
 //
 // brain_norm_bwd_noalloc is the RMSNorm (kind 0) / LayerNorm (kind 1) backward of
 // brain_norm_bwd (norms.cu) with its f32 partial-sum workspace replaced by a fixed 4 MiB
-// __device__ array inside the library: D <= 8192 (larger D returns BRAIN_NOALLOC_TOO_LARGE = -2),
+// __device__ array inside the library: D <= 8192 (larger D returns BRAIN_NOALLOC_TOO_LARGE = -1000),
 // at most 64 partial rows. The caller still passes every input and output. The first call on
 // each device looks up the array's device address (cudaGetSymbolAddress) with that device
 // current; make it before any stream capture. All calls share the array, which keeps the last
@@ -17,7 +17,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
-#define BRAIN_NOALLOC_TOO_LARGE (-2)
+// A code no other entry point of the library returns.
+#define BRAIN_NOALLOC_TOO_LARGE (-1000)
 
 #ifdef __cplusplus
 extern "C" {

@@ -12,6 +12,8 @@
 //            fused_add_rmsnorm returns (norm, sum)      crates/brain-core/src/tensor/ops_fused.rs:77-125
 //   LayerNorm y = (x - mean) / sqrt(var + eps) * w + b, biased variance
 //                                                      crates/brain-transformer/src/ops.rs:57-101
+#include <atomic>
+
 #include "common.cuh"
 #include "no_alloc.h"
 
@@ -426,38 +428,45 @@ constexpr int kNoAllocPartials = 64;
 constexpr int kNoAllocMaxD = 8192;
 static __device__ __align__(256) float g_norm_bwd_scratch[2 * kNoAllocPartials * kNoAllocMaxD];
 
+// Device address of the array on the current device, looked up once per device. The slots are atomics:
+// two host threads making their first call on the same device at once both look the address up and
+// store the same value, with no data race.
 float* noalloc_scratch_ptr(int* err) {
-  static float* ptrs[64] = {nullptr};
+  static std::atomic<float*> ptrs[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= 64) {
     *err = (e != cudaSuccess) ? (int)e : (int)cudaErrorInvalidDevice;
     return nullptr;
   }
-  if (!ptrs[dev]) {
+  float* cached = ptrs[dev].load(std::memory_order_relaxed);
+  if (!cached) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_norm_bwd_scratch);  // host-side stand-in -> device address
     if (e != cudaSuccess) {
       *err = (int)e;
       return nullptr;
     }
-    ptrs[dev] = static_cast<float*>(p);
+    cached = static_cast<float*>(p);
+    ptrs[dev].store(cached, std::memory_order_relaxed);
   }
   *err = 0;
-  return ptrs[dev];
+  return cached;
 }
 
 }  // namespace
 
-// Same arguments as brain_norm_bwd without the workspace (see no_alloc.h). Returns 0, a cudaError_t,
-// or BRAIN_NOALLOC_TOO_LARGE when D exceeds the fixed scratch (D > 8192).
+// Same arguments as brain_norm_bwd without the workspace (see no_alloc.h). Returns 0, a cudaError_t
+// (cudaErrorInvalidValue for M < 0, D <= 0, D not a multiple of 8 or an unknown kind), or
+// BRAIN_NOALLOC_TOO_LARGE when D exceeds the fixed scratch (D > 8192).
 BRAIN_API int brain_norm_bwd_noalloc(int kind, const void* dy, int64_t lddy, const void* x, int64_t ldx, const void* w,
                                      const float* mean_in, const float* rstd_in, void* dx, int64_t lddx,
                                      const void* dres, int64_t lddres, void* dw, void* db, int dw_f32, int accumulate,
                                      int M, int D, cudaStream_t st) {
-  if (M == 0) return 0;
-  if (D > kNoAllocMaxD) return -2;  // BRAIN_NOALLOC_TOO_LARGE
+  if (M < 0 || D <= 0 || (kind != 0 && kind != 1)) return (int)cudaErrorInvalidValue;
+  if (D > kNoAllocMaxD) return BRAIN_NOALLOC_TOO_LARGE;
   if (D % 8 != 0) return (int)cudaErrorInvalidValue;
+  if (M == 0) return 0;
   int err = 0;
   float* scratch = noalloc_scratch_ptr(&err);
   if (!scratch) return err;
