@@ -58,8 +58,10 @@ struct AdamHyper {
 template <typename G>
 __global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ m, float* __restrict__ v,
                              float* __restrict__ vmax, const G* __restrict__ g, __nv_bfloat16* __restrict__ p16,
-                             int64_t n, AdamHyper h, const int* __restrict__ found_inf) {
+                             int64_t n, AdamHyper h, const int* __restrict__ found_inf,
+                             const float* __restrict__ coef) {
   if (found_inf && *found_inf) return;
+  if (coef) h.grad_scale *= *coef;  // global-norm clipping coefficient computed on the device
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const float one_b1 = 1.f - h.b1, one_b2 = 1.f - h.b2;
   const float inv_bc1 = 1.f / h.bc1, inv_bc2 = 1.f / h.bc2;
@@ -199,6 +201,89 @@ __global__ void clip_coef_kernel(const float* sq, float max_norm, float* coef) {
   *coef = fminf(1.f, max_norm / (norm + 1e-6f));
 }
 
+// Gradient statistics for a guarded optimizer step: per-CTA partial sums of (scale * g)^2 and a per-CTA
+// non-finite flag into ws[2 * blockIdx.x + {0, 1}].
+template <typename G>
+__global__ void grad_stats_kernel(const G* __restrict__ g, int64_t n, float scale, float* __restrict__ ws) {
+  float s = 0.f;
+  float bad = 0.f;
+  const int64_t n4 = n / 4;
+  const bool vec = (reinterpret_cast<uintptr_t>(g) & (4 * sizeof(G) - 1)) == 0;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    float x[4];
+    ld_grad4(g, i, vec, x);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float y = x[j] * scale;
+      if (!isfinite(y)) bad = 1.f;
+      s += y * y;
+    }
+  }
+  for (int64_t i = n4 * 4 + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float y = ld_grad(g, i) * scale;
+    if (!isfinite(y)) bad = 1.f;
+    s += y * y;
+  }
+  s = warp_sum(s);
+  bad = warp_max(bad);
+  __shared__ float red[2][32];
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) {
+    red[0][w] = s;
+    red[1][w] = bad;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const bool in = l < (int)(blockDim.x / 32);
+    float t = warp_sum(in ? red[0][l] : 0.f);
+    float b = warp_max(in ? red[1][l] : 0.f);
+    if (l == 0) {
+      ws[2 * blockIdx.x] = t;
+      ws[2 * blockIdx.x + 1] = b;
+    }
+  }
+}
+
+// stats[0] (+)= sum of the partial squares, stats[1] (+)= 1 if any partial saw a non-finite value
+// (fixed summation order: the result does not depend on scheduling).
+__global__ void grad_stats_finish_kernel(const float* __restrict__ ws, int P, float* __restrict__ stats,
+                                         int accumulate) {
+  float s = 0.f, b = 0.f;
+  for (int i = threadIdx.x; i < P; i += blockDim.x) {
+    s += ws[2 * i];
+    b = fmaxf(b, ws[2 * i + 1]);
+  }
+  s = warp_sum(s);
+  b = warp_max(b);
+  __shared__ float red[2][32];
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) {
+    red[0][w] = s;
+    red[1][w] = b;
+  }
+  __syncthreads();
+  if (w == 0) {
+    const bool in = l < (int)(blockDim.x / 32);
+    float t = warp_sum(in ? red[0][l] : 0.f);
+    float c = warp_max(in ? red[1][l] : 0.f);
+    if (l == 0) {
+      stats[0] = accumulate ? stats[0] + t : t;
+      stats[1] = accumulate ? stats[1] + c : c;
+    }
+  }
+}
+
+// From globally reduced statistics (sum of squares, count of ranks / pieces that saw a non-finite
+// value): found_inf = any non-finite (the step is skipped on every rank alike), coef = global-norm clip
+// coefficient min(1, max_norm / (norm + 1e-6)) or 1 when max_norm <= 0.
+__global__ void step_guard_kernel(const float* __restrict__ stats, float max_norm, int* __restrict__ found_inf,
+                                  float* __restrict__ coef) {
+  const float sq = stats[0];
+  const bool bad = stats[1] != 0.f || !isfinite(sq);
+  *found_inf = bad ? 1 : 0;
+  *coef = (max_norm > 0.f && !bad) ? fminf(1.f, max_norm / (sqrtf(sq) + 1e-6f)) : 1.f;
+}
+
 // f32 -> bf16 copy
 __global__ void cast_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, int64_t n) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
@@ -217,9 +302,11 @@ int grid_for(int64_t n) {
 BRAIN_STATUS_READER(optim)
 
 // grad_f32: 1 = gradient buffer is f32, 0 = bf16. vmax may be null unless amsgrad.
+// found_inf (device int, may be null): skip the step when non-zero. coef (device float, may be null):
+// extra factor on the gradient (global-norm clipping).
 BRAIN_API int brain_adamw(float* p, float* m, float* v, float* vmax, const void* g, int grad_f32, void* p16, int64_t n,
                           float lr, float b1, float b2, float eps, float wd, float bc1, float bc2, float grad_scale,
-                          int amsgrad, const int* found_inf, cudaStream_t st) {
+                          int amsgrad, const int* found_inf, const float* coef, cudaStream_t st) {
   if (n == 0) return 0;
   if ((reinterpret_cast<uintptr_t>(p) | reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v)) & 15)
     return (int)cudaErrorInvalidValue;
@@ -227,10 +314,10 @@ BRAIN_API int brain_adamw(float* p, float* m, float* v, float* vmax, const void*
   AdamHyper h{lr, b1, b2, eps, wd, bc1, bc2, grad_scale, amsgrad};
   if (grad_f32)
     adamw_kernel<float><<<grid_for(n), 256, 0, st>>>(p, m, v, vmax, reinterpret_cast<const float*>(g),
-                                                     reinterpret_cast<__nv_bfloat16*>(p16), n, h, found_inf);
+                                                     reinterpret_cast<__nv_bfloat16*>(p16), n, h, found_inf, coef);
   else
     adamw_kernel<__nv_bfloat16><<<grid_for(n), 256, 0, st>>>(p, m, v, vmax, reinterpret_cast<const __nv_bfloat16*>(g),
-                                                             reinterpret_cast<__nv_bfloat16*>(p16), n, h, found_inf);
+                                                             reinterpret_cast<__nv_bfloat16*>(p16), n, h, found_inf, coef);
   return (int)cudaGetLastError();
 }
 
@@ -274,6 +361,29 @@ BRAIN_API int brain_scale(void* x, int is_f32, int64_t n, const float* s_ptr, fl
     scale_kernel<float><<<grid_for(4 * n), 256, 0, st>>>(reinterpret_cast<float*>(x), n, s_ptr, s_const);
   else
     scale_kernel<__nv_bfloat16><<<grid_for(4 * n), 256, 0, st>>>(reinterpret_cast<__nv_bfloat16*>(x), n, s_ptr, s_const);
+  return (int)cudaGetLastError();
+}
+
+// stats[0:2] (+)= (sum of (scale * g)^2, non-finite seen) over n gradient elements. workspace: f32 [>= 2048].
+BRAIN_API int brain_grad_stats(const void* g, int grad_f32, int64_t n, float scale, float* stats, int accumulate,
+                               float* workspace, cudaStream_t st) {
+  int P = grid_for(4 * n);
+  if (P > 1024) P = 1024;
+  if (n > 0) {
+    if (grad_f32)
+      grad_stats_kernel<float><<<P, 256, 0, st>>>(reinterpret_cast<const float*>(g), n, scale, workspace);
+    else
+      grad_stats_kernel<__nv_bfloat16><<<P, 256, 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(g), n, scale,
+                                                          workspace);
+  } else {
+    P = 0;
+  }
+  grad_stats_finish_kernel<<<1, 1024, 0, st>>>(workspace, P, stats, accumulate);
+  return (int)cudaGetLastError();
+}
+
+BRAIN_API int brain_step_guard(const float* stats, float max_norm, int* found_inf, float* coef, cudaStream_t st) {
+  step_guard_kernel<<<1, 1, 0, st>>>(stats, max_norm, found_inf, coef);
   return (int)cudaGetLastError();
 }
 

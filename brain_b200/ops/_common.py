@@ -23,7 +23,9 @@ _native.register({
     "brain_pos_grad": ("brain_kernels", "ppilii" + "s"),
     "brain_ce_fwd": ("brain_kernels", "plppplilfs"),
     "brain_ce_bwd": ("brain_kernels", "plppppfpllilfs"),
-    "brain_adamw": ("brain_kernels", "pppppiplffffffffips"),
+    "brain_adamw": ("brain_kernels", "pppppiplffffffffipps"),
+    "brain_grad_stats": ("brain_kernels", "pilfpips"),
+    "brain_step_guard": ("brain_kernels", "pfpps"),
     "brain_sgd": ("brain_kernels", "pppiplffffiifps"),
     "brain_sumsq": ("brain_kernels", "pilfpipps"),
     "brain_scale": ("brain_kernels", "pilpfs"),

@@ -14,19 +14,24 @@ from ._common import ptr, stream
 
 
 def adamw_(p, m, v, g, *, lr, beta1, beta2, eps, weight_decay, step, grad_scale=1.0, p16=None, vmax=None,
-           found_inf=None, bias_correction=True):
-    """One AdamW step (reference order: decay, moments, bias-corrected update) over flat buffers."""
+           found_inf=None, bias_correction=True, coef=None):
+    """One AdamW step (reference order: decay, moments, bias-corrected update) over flat buffers.
+
+    ``found_inf`` (device int32 scalar): skip the step when non-zero. ``coef`` (device float32 scalar):
+    an extra factor on the gradient, e.g. the global-norm clipping coefficient of ``step_guard``."""
     bc1 = 1.0 - beta1 ** step if bias_correction else 1.0
     bc2 = 1.0 - beta2 ** step if bias_correction else 1.0
     if p.is_cuda:
         _native.call("brain_adamw", p.data_ptr(), m.data_ptr(), v.data_ptr(), ptr(vmax), g.data_ptr(),
                      int(g.dtype == torch.float32), ptr(p16), p.numel(), float(lr), float(beta1), float(beta2),
                      float(eps), float(weight_decay), float(bc1), float(bc2), float(grad_scale), int(vmax is not None),
-                     ptr(found_inf), stream(p))
+                     ptr(found_inf), ptr(coef), stream(p))
         return
     if found_inf is not None and int(found_inf.item()) != 0:
         return
     gf = g.float() * grad_scale
+    if coef is not None:
+        gf = gf * coef
     p.mul_(1.0 - lr * weight_decay)
     m.mul_(beta1).add_(gf, alpha=1.0 - beta1)
     v.mul_(beta2).addcmul_(gf, gf, value=1.0 - beta2)
@@ -75,6 +80,39 @@ def sumsq(g, scale=1.0, out=None, accumulate=False, found_inf=None):
     if found_inf is not None and not torch.isfinite(gf).all():
         found_inf.fill_(1)
     return out
+
+
+def grad_stats(g, scale=1.0, stats=None, accumulate=False):
+    """stats[0:2] (+)= (sum((scale*g)^2), 1.0 if any scale*g is non-finite) as a float32 device vector."""
+    if stats is None:
+        stats = torch.zeros(2, device=g.device, dtype=torch.float32)
+    if g.is_cuda:
+        ws = torch.empty(2048, device=g.device, dtype=torch.float32)
+        _native.call("brain_grad_stats", g.data_ptr(), int(g.dtype == torch.float32), g.numel(), float(scale),
+                     stats.data_ptr(), int(accumulate), ws.data_ptr(), stream(g))
+        return stats
+    gf = g.float() * scale
+    new = torch.stack([gf.pow(2).sum(), (~torch.isfinite(gf)).any().float()])
+    stats.copy_(stats + new if accumulate else new)
+    return stats
+
+
+def step_guard(stats, max_norm=0.0, found_inf=None, coef=None):
+    """From globally reduced ``grad_stats``: found_inf (int32, 1 = skip the step) and the clip
+    coefficient min(1, max_norm / (norm + 1e-6)) (1 when max_norm <= 0 or the step is skipped)."""
+    if found_inf is None:
+        found_inf = torch.zeros(1, device=stats.device, dtype=torch.int32)
+    if coef is None:
+        coef = torch.ones(1, device=stats.device, dtype=torch.float32)
+    if stats.is_cuda:
+        _native.call("brain_step_guard", stats.data_ptr(), float(max_norm), found_inf.data_ptr(), coef.data_ptr(),
+                     stream(stats))
+        return found_inf, coef
+    sq = float(stats[0])
+    bad = float(stats[1]) != 0.0 or not torch.isfinite(stats[0])
+    found_inf.fill_(1 if bad else 0)
+    coef.fill_(min(1.0, max_norm / (sq ** 0.5 + 1e-6)) if (max_norm > 0 and not bad) else 1.0)
+    return found_inf, coef
 
 
 def scale_(x, s):

@@ -128,15 +128,21 @@ class OverlappedStep:
             if blk is not None:
                 self.hooks.append(blk.register_full_backward_hook(lambda mod, gin, gout, i=i: self._launch(i)))
         self.args = None
+        self.guarded, self.max_norm, self.stats_started = False, 0.0, False
 
-    def arm(self, grad_scale: float) -> None:
-        """Before backward: this step's AdamW constants."""
+    def arm(self, grad_scale: float, guarded: bool = False, max_norm: float = 0.0) -> None:
+        """Before backward: this step's AdamW constants. ``guarded``: during backward each bucket is
+        only reduced (into this rank's piece of the gradient buffer) and its statistics accumulated;
+        AdamW runs in ``finish`` once the statistics of every bucket on every rank are known, so a
+        non-finite element anywhere skips the step on all ranks and clipping uses the global norm."""
         opt = self.opt
         opt.step_count += 1
         t = opt.step_count
         b1, b2 = opt.betas
         self.args = (float(opt.lr), float(b1), float(b2), float(opt.eps), float(opt.weight_decay),
                      float(1 - b1 ** t), float(1 - b2 ** t), float(grad_scale))
+        self.guarded, self.max_norm = guarded, float(max_norm)
+        self.stats_started = False
         self.fired = [False] * len(self.buckets)
 
     def _launch(self, i: int) -> None:
@@ -156,6 +162,9 @@ class OverlappedStep:
             if W > 1:
                 self.comm.barrier(50)
             if n == 0:
+                return
+            if self.guarded:
+                self._reduce_piece(a, n, gs)
                 return
             if self.mode == "sm":
                 _native.call("brain_comm_ddp_step_ctas", self.gpeers, self.ppeers, bf16, r, W, a, n, *state,
@@ -183,11 +192,71 @@ class OverlappedStep:
                 _native.call("brain_comm_copy_async", self.flat.param_buf.data_ptr() + a * pe,
                              self.ppeers[j] + a * pe, n * pe, st)
 
+    def _reduce_piece(self, a: int, n: int, gs: float) -> None:
+        """Guarded mode, on the side stream: this rank's piece of a bucket becomes the scaled sum over the
+        ranks (in place in the local gradient buffer, which no peer reads there) and its squares and
+        non-finite flag are added to the step's statistics."""
+        from ..ops import optim_kernels as K
+        W, r, ge = self.world, self.rank, self.gesz
+        piece = self.flat.grad_buf[a:a + n]
+        if W > 1:
+            dcode = 0 if self.flat.grad_buf.dtype == torch.float32 else 1
+            st = self.side.cuda_stream
+            if self.mode == "sm":
+                peers = self.gpeers
+            else:
+                grads = [0] * W
+                for jj in range(W):
+                    j = (r + jj) % W
+                    if j == r:
+                        grads[j] = self.flat.grad_buf.data_ptr()
+                        continue
+                    dst = self.staging[j].data_ptr()
+                    _native.call("brain_comm_copy_async", self.gpeers[j] + a * ge, dst, n * ge, st)
+                    grads[j] = dst - a * ge  # the kernel adds the piece offset back
+                peers = _i64(grads)
+            _native.call("brain_comm_reduce_pull", peers, a, r, W, piece.data_ptr(), n, dcode, float(gs), st)
+            gs = 1.0
+        K.grad_stats(piece, gs, self.opt.stats, accumulate=self.stats_started)
+        self.stats_started = True
+
+    def _guarded_update(self) -> None:
+        """Guarded mode, after backward: global statistics, then AdamW on every piece (skipped alike on
+        every rank when anything was non-finite) and the new weights pushed to the peers."""
+        from ..ops import optim_kernels as K
+        opt, W = self.opt, self.world
+        if not self.stats_started:
+            opt.stats.zero_()
+        if W > 1:
+            self.comm.all_reduce(opt.stats)
+        fi, coef = K.step_guard(opt.stats, self.max_norm, opt.found_inf, opt.coef)
+        lr, b1, b2, eps, wd, bc1, bc2, gs = self.args
+        t = opt.step_count
+        pe = self.flat.param_buf.element_size()
+        st = torch.cuda.current_stream().cuda_stream
+        for a, n, s in self.pieces:
+            if n == 0:
+                continue
+            K.adamw_(self.master[s:s + n], self.m[s:s + n], self.v[s:s + n], self.flat.grad_buf[a:a + n], lr=lr,
+                     beta1=b1, beta2=b2, eps=eps, weight_decay=wd, step=t, grad_scale=1.0 if W > 1 else gs,
+                     p16=self.flat.param_buf[a:a + n], found_inf=fi, coef=coef)
+            for jj in range(1, W):
+                j = (self.rank + jj) % W
+                _native.call("brain_comm_copy_async", self.flat.param_buf.data_ptr() + a * pe,
+                             self.ppeers[j] + a * pe, n * pe, st)
+
     def finish(self) -> None:
         """After backward: the buckets not yet reduced, then every rank's update visible everywhere."""
+        stray = [p for p in self.flat.params if p.grad is not None]
+        if stray:
+            # an op without a main_grad path left a .grad after its bucket may already have been reduced
+            raise RuntimeError(f"{len(stray)} parameter(s) received .grad instead of main_grad; the overlapped "
+                               "reduction needs every gradient written into the flat buffer (use overlap=False)")
         for i in range(len(self.buckets)):
             self._launch(i)
         torch.cuda.current_stream().wait_stream(self.side)
+        if self.guarded:
+            self._guarded_update()
         if self.world > 1:
             self.comm.barrier(51)
         self.args = None

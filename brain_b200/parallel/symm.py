@@ -215,6 +215,22 @@ class NvlinkComm:
                      out.data_ptr(), n, dcode, 1.0, _stream())
         return out
 
+    def reduce_scatter_inplace(self, full: torch.Tensor, shard: torch.Tensor, scale: float = 1.0) -> torch.Tensor:
+        """shard = scale * sum over ranks of their ``full`` at this rank's shard position, written in
+        place into the local ``full`` (``shard`` is that view): each rank reads only the peers' pieces
+        of its own shard, which no peer reads, so the in-place write races with nothing."""
+        buf, off = self._buf_of(full)
+        esz = full.element_size()
+        n = shard.numel()
+        if buf is None or shard.data_ptr() != full.data_ptr() + self.rank * n * esz:
+            tmp = torch.empty_like(shard)
+            self.reduce_scatter_flat(full, tmp)
+            return shard.copy_(tmp.mul_(scale))
+        self.barrier(10)
+        _native.call("brain_comm_reduce_pull", buf.peer_array(off), self.rank * n, self.rank, self.world,
+                     shard.data_ptr(), n, 0 if full.dtype == torch.float32 else 1, float(scale), _stream())
+        return shard
+
     def all_gather_flat(self, shard: torch.Tensor, full: torch.Tensor) -> torch.Tensor:
         esz = full.element_size()
         n = shard.numel()
