@@ -189,7 +189,9 @@ def test_overlapped_adamw_single_gpu_matches_step_after_backward():
         if dp.overlapped is not None:
             dp.overlapped.close()
     assert O.rel_err(out[0][0], out[1][0]) < 1e-5
-    assert torch.equal(out[0][2], out[1][2])
+    # two AdamW kernels (per-bucket fused step vs flat AdamW): a last-bit difference of a master weight
+    # can move its bf16 rounding, so the compute weights agree to bf16 rounding, not bitwise
+    assert O.rel_err(out[0][2].float(), out[1][2].float()) < 1e-3
     assert out[0][1] == out[1][1]
     bdist.shutdown()
 
