@@ -33,6 +33,8 @@ def main(argv=None) -> int:
     ap.add_argument("--graph", action="store_true",
                     help="replay each case from a CUDA graph, so short kernels are timed without the per-call "
                          "host overhead (cases that cannot be captured fall back to eager calls)")
+    ap.add_argument("--gemm-pair", default="auto", choices=["auto", "off"],
+                    help="off: the single-CTA tcgen05 GEMM even where the CTA-pair kernel would run")
     a = ap.parse_args(argv)
     only = set(x for x in a.only.split(",") if x)
 
@@ -42,6 +44,9 @@ def main(argv=None) -> int:
 
     dev = torch.device("cuda")
     tflops_peak, hbm_peak = _peaks()
+    if a.gemm_pair == "off":
+        from ..ops.gemm import set_pair_mode
+        set_pair_mode(0)
     g = torch.Generator(device=dev).manual_seed(0)
     T, d, F, V = 8192, 4096, 14336, 128256
     B, S, Hq, Hkv, D = 2, 4096, 32, 8, 128

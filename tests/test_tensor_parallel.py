@@ -1,6 +1,7 @@
-"""Tensor-parallel linears with fused communication (GEMM -> reduce-scatter / all-reduce pushed from the
-GEMM epilogue over NVLink, AG -> GEMM with A tiles read from their owners by TMA), forward and backward,
-against the same products computed on full tensors. 2 GPUs."""
+"""Tensor-parallel linears with fused communication (GEMM -> reduce-scatter: the GEMM writes partial products
+into symmetric memory and each rank pulls and sums its rows over NVLink; GEMM -> all-reduce pushed from the
+GEMM epilogue; AG -> GEMM pipelined by row block, each peer block copied over NVLink once into local memory
+before its GEMM), forward and backward, against the same products computed on full tensors. 2 GPUs."""
 import pytest
 import torch
 
