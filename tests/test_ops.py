@@ -366,3 +366,35 @@ def test_adamw_flat_matches_reference_order():
     before = p.clone()
     adamw_(p, m, v, g, lr=1e-3, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.01, step=4, found_inf=flag)
     assert torch.equal(p, before)
+
+
+def _rel(a, b):
+    a, b = a.double(), b.double()
+    return float((a - b).norm() / b.norm())
+
+
+@gpu
+@pytest.mark.slow
+@pytest.mark.parametrize("Hq,Hkv", [(8, 2)])
+def test_flash_attention_tcgen05_production_length(Hq, Hkv):
+    """The training shape's sequence length (4096, causal, d 128, GQA group 4): forward output and
+    all three gradients against a float32 reference over the whole sequence. Sums over 4096 keys of
+    bf16 P / dS tiles leave a few elements of dQ near 0.05 off, so the elementwise bound is looser
+    than at short lengths and the relative Frobenius error carries the check."""
+    B, S, D = 1, 4096, 128
+    q = rnd(B, S, Hq, D, seed=60, scale=2.0)
+    k = rnd(B, S, Hkv, D, seed=61, scale=2.0)
+    v = rnd(B, S, Hkv, D, seed=62)
+    do = rnd(B, S, Hq, D, seed=63)
+    scale = D ** -0.5
+    o, lse = attn._fwd(q, k, v, True, scale, impl="tc")
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    attn._bwd(q, k, v, o, lse, do, dq, dk, dv, True, scale, impl="tc")
+    ref, (qr, kr, vr) = grads(lambda a, b, c: attn.sdpa_ref(a.float(), b.float(), c.float(), True), q, k, v)
+    close(o, ref, 2e-2, 2e-2)
+    assert _rel(o, ref) < 1e-2
+    ref.backward(do.float())
+    for got, want in ((dq, qr.grad), (dk, kr.grad), (dv, vr.grad)):
+        assert _rel(got, want) < 1e-2
+        close(got, want, 5e-2, 1e-1)
+    assert ops.check_status() == []
