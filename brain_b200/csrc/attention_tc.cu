@@ -2,7 +2,9 @@
 //
 // One CTA computes two 128-row query tiles (A: rows m0..m0+127, B: rows m0+128..m0+255) of one
 // (batch, q-head) against all visible keys, 128 keys per step; both tiles share every K/V block the TMA
-// brings in. Roles (10 warps):
+// brings in. Roles (12 warps, three warpgroups; setmaxnreg moves registers from warpgroup 0, which only
+// issues copies and MMAs, to the softmax warpgroups: 4 x 32 x 72 + 8 x 32 x 216 = 384 x 168, the launch
+// budget):
 //   warp 0      TMA producer: Q_A and Q_B once, then K and V blocks (4-D tensor maps over [B, S, H, D]
 //               with the caller's strides, SWIZZLE_128B, CTA-local) into a 2-stage ring whose K and V
 //               halves are released separately (K_j after both score MMAs, V_j after both PV MMAs).
@@ -12,7 +14,7 @@
 //               P_t(j) is read from; tcgen05.mma orders only MMAs on the same accumulator, so the
 //               completion is waited for explicitly). One tile's softmax runs while the tensor core
 //               works on the other tile's MMAs.
-//   warps 2..5  softmax of tile A, warps 6..9 softmax of tile B: thread = one query row (TMEM lane)
+//   warps 4..7  softmax of tile A, warps 8..11 softmax of tile B: thread = one query row (TMEM lane)
 //               and all 128 keys of the block: tcgen05.ld of S, causal/length mask, row max, lazy
 //               rescale of O (only when the running max grows by more than 2^8), exp2, and P packed to
 //               bf16 and stored back over the first 64 columns of S (tcgen05.st). The PV MMA reads P
@@ -32,7 +34,7 @@ namespace {
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: P values stay <= 256 between rescales
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
 constexpr int SUB = 128 * 64 * 2;  // one SW128 sub-tile: 128 rows x 64 bf16
 
 struct FwdArgs {
@@ -132,7 +134,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
+  if (warp < 4) {
+    // warpgroup 0: copies and MMAs (the register hand-over is per warpgroup and dominates each role's code)
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 72;");
   if (warp == 0) {
     if (lane == 0 && nK > 0) {
       // ---------------- TMA producer
@@ -277,9 +281,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 216;");
     // ---------------- softmax warpgroups: tile t, TMEM lane quadrant q, thread = one query row
-    const int t = (warp - 2) >> 2;
+    const int t = (warp - 4) >> 2;
     const int q = warp & 3;
     const int r = q * 32 + lane;  // row within the tile == TMEM lane
     const int qi = m0 + 128 * t + r;
@@ -307,21 +313,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       float mxp[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
+      // raw scores: the log2-domain scale (> 0) is applied in the exponent's FFMA, max(c s) = c max(s)
       if (need_mask) {
 #pragma unroll
         for (int k = 0; k < 128; ++k) {
-          s[k] = (n0 + k > limit) ? -INFINITY : s[k] * a.scale_log2;
+          if (n0 + k > limit) s[k] = -INFINITY;
           mxp[k & 7] = fmaxf(mxp[k & 7], s[k]);
         }
       } else {
 #pragma unroll
-        for (int k = 0; k < 128; ++k) {
-          s[k] *= a.scale_log2;
-          mxp[k & 7] = fmaxf(mxp[k & 7], s[k]);
-        }
+        for (int k = 0; k < 128; ++k) mxp[k & 7] = fmaxf(mxp[k & 7], s[k]);
       }
-      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      const float mx = a.scale_log2 * fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                            fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       float alpha = 1.f;
       if (mx > m_used + kRescaleThreshold || (m_used == -INFINITY && mx > -INFINITY)) {
         alpha = exp2f(m_used - mx);  // 0 when m_used == -inf
@@ -348,7 +352,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int k = 0; k < 32; k += 2) {
-          const float p0 = ex2_fast(s[c * 32 + k] - mu), p1 = ex2_fast(s[c * 32 + k + 1] - mu);
+          const float p0 = ex2_fast(fmaf(s[c * 32 + k], a.scale_log2, -mu));
+          const float p1 = ex2_fast(fmaf(s[c * 32 + k + 1], a.scale_log2, -mu));
           sp[(k >> 1) & 7] += p0 + p1;
           pk[k / 2] = pack_bf16x2(p0, p1);
         }
