@@ -12,7 +12,8 @@
 // CTA-local destinations), warp 1 single-thread MMA issuer, warps 2..9 elementwise: two warps per TMEM
 // lane quadrant (thread = row), each taking 32 of a block's 64 columns, so two warps per scheduler hide
 // each other's TMEM-load and exponential latency. They write P/dS as bf16 K-major tiles that the
-// accumulate MMAs read from shared memory; the
+// accumulate MMAs read from shared memory; the tiles are double-buffered, so the elementwise warps store
+// block i+1 while the accumulate MMAs of block i still read theirs. The
 // streamed operand is read a second time as an MN-major B operand, so nothing is transposed.
 // Bounded waits report through the status word. Reference: the Value-graph attention VJPs
 // (crates/brain-autograd/src/grad_fns/mod.rs:327-420); mask/scale conventions as in attention_tc.cu.
@@ -51,11 +52,17 @@ struct BwdLayout {
   static constexpr int STAGE_BYTES = 2 * B_BYTES;
   static constexpr int NC = MODE == DKDV ? 2 : 1;  // C tiles (P^T, dS^T) or (dS)
   static constexpr int C_OFF = B_OFF + STAGES * STAGE_BYTES;
-  static constexpr int LD_OFF = C_OFF + NC * SUB128;  // DKDV: per block lse*log2e and delta, 2 buffers
+  static constexpr int C_BYTES = NC * SUB128;  // one buffer of C tiles; two buffers
+  static constexpr int LD_OFF = C_OFF + 2 * C_BYTES;  // DKDV: per block lse*log2e and delta, 2 buffers
   static constexpr int BAR_OFF = LD_OFF + 2 * 128 * 4;
-  // a_full, b_full[S], b_empty[S], sd_full[2], sd_free[2], c_full, c_free, acc_done, drain
-  static constexpr int NBAR = 1 + 2 * STAGES + 4 + 4;
+  // TMEM S/dP buffers (double-buffered: the scores of block i+1 are computed while the elementwise warps
+  // work on block i); the accumulators follow them
+  static constexpr int NBUF = 2;
+  static constexpr int ACC = NBUF * 128;  // first accumulator column
+  // a_full, b_full[S], b_empty[S], sd_full[3], sd_free[3], c_full[2], c_free[2], acc_done, drain
+  static constexpr int NBAR = 1 + 2 * STAGES + 6 + 6;
   static constexpr int TOTAL = BAR_OFF + NBAR * 8 + 16 + 1024;
+  static_assert(TOTAL <= 232448, "more dynamic shared memory than one CTA may use");
 };
 
 template <int D, int MODE>
@@ -68,17 +75,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
   const uint32_t sA1 = sbase + L::A_OFF, sA2 = sA1 + L::A_BYTES;
-  const uint32_t sB = sbase + L::B_OFF, sC = sbase + L::C_OFF;
+  const uint32_t sB = sbase + L::B_OFF, sCb = sbase + L::C_OFF;
   const uint32_t bars = sbase + L::BAR_OFF;
   const uint32_t a_full = bars;
   auto b_full = [&](int s) { return bars + 8u * (1 + s); };
   auto b_empty = [&](int s) { return bars + 8u * (1 + ST + s); };
+  constexpr int NB = L::NBUF;
   auto sd_full = [&](int i) { return bars + 8u * (1 + 2 * ST + i); };
-  auto sd_free = [&](int i) { return bars + 8u * (3 + 2 * ST + i); };
-  const uint32_t c_full = bars + 8u * (5 + 2 * ST);
-  const uint32_t c_free = bars + 8u * (6 + 2 * ST);
-  const uint32_t acc_done = bars + 8u * (7 + 2 * ST);
-  const uint32_t drain = bars + 8u * (8 + 2 * ST);
+  auto sd_free = [&](int i) { return bars + 8u * (4 + 2 * ST + i); };
+  auto c_full = [&](int i) { return bars + 8u * (7 + 2 * ST + i); };
+  auto c_free = [&](int i) { return bars + 8u * (9 + 2 * ST + i); };
+  const uint32_t acc_done = bars + 8u * (11 + 2 * ST);
+  const uint32_t drain = bars + 8u * (12 + 2 * ST);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -123,12 +131,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(b_full(s), 1);
       mbar_init(b_empty(s), 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < 3; ++i) {
       mbar_init(sd_full(i), 1);
       mbar_init(sd_free(i), kEwThreads);
     }
-    mbar_init(c_full, kEwThreads);
-    mbar_init(c_free, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(c_full(i), kEwThreads);
+      mbar_init(c_free(i), 1);
+    }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -188,7 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool issued = false;
       auto issue_scores = [&](int i) {
         const uint32_t st = sB + (i % ST) * L::STAGE_BYTES;
-        const uint32_t d = tmem + (uint32_t)((i & 1) * 128);
+        const uint32_t d = tmem + (uint32_t)((i % NB) * 128);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t oa = (kk / 4) * SUB128 + (kk % 4) * 32;
@@ -198,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           tc_mma_f16(d + 64, smem_desc_sw128(sA2 + oa, 16, 1024), smem_desc_sw128(st + L::B_BYTES + ob, 16, 1024),
                      IDESC_S, kk > 0 ? 1u : 0u);
         }
-        tc_commit(sd_full(i & 1));
+        tc_commit(sd_full(i % NB));
       };
       if (ok) ok = mbar_wait(b_full(0), 0, BRAIN_ERR_TIMEOUT_FULL, 221, abort_flag);
       if (ok) {
@@ -206,23 +216,33 @@ __global__ void __launch_bounds__(kThreads, 1)
         issue_scores(0);
         issued = true;
       }
+      // the first NB-1 score blocks go out before the loop; block i+NB-1 then goes out in iteration i
+      for (int in = 1; ok && in < NB - 1 && in < niter; ++in) {
+        if (!mbar_wait(b_full(in % ST), (in / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 222, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_scores(in);
+      }
       for (int i = 0; ok && i < niter; ++i) {
-        if (i + 1 < niter) {
-          const int in = i + 1;
+        if (i + NB - 1 < niter) {
+          const int in = i + NB - 1;
           if (!mbar_wait(b_full(in % ST), (in / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 222, abort_flag) ||
-              !mbar_wait(sd_free(in & 1), ((in / 2) & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 223, abort_flag)) {
+              !mbar_wait(sd_free(in % NB), ((in / NB) & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 223, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           issue_scores(in);
         }
-        if (!mbar_wait(c_full, i & 1, BRAIN_ERR_TIMEOUT_ACC, 224, abort_flag)) {
+        if (!mbar_wait(c_full(i & 1), (i / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 224, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t st = sB + (i % ST) * L::STAGE_BYTES;
+        const uint32_t sC = sCb + (i & 1) * L::C_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 64 / 16; ++kk) {
           const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
@@ -230,14 +250,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (MODE == DKDV) {
             const uint64_t c1 = smem_desc_sw128(sC + SUB128 + kk * 32, 16, 1024);
             // dV += P^T dO   (dO = B2, MN-major);  dK += dS^T Q   (Q = B1, MN-major)
-            tc_mma_f16(tmem + 256, c0, smem_desc_sw128(st + L::B_BYTES + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
-            tc_mma_f16(tmem + 256 + D, c1, smem_desc_sw128(st + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
+            tc_mma_f16(tmem + L::ACC, c0, smem_desc_sw128(st + L::B_BYTES + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
+            tc_mma_f16(tmem + L::ACC + D, c1, smem_desc_sw128(st + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
           } else {
             // dQ += dS K   (K = B1, MN-major)
-            tc_mma_f16(tmem + 256, c0, smem_desc_sw128(st + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
+            tc_mma_f16(tmem + L::ACC, c0, smem_desc_sw128(st + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
           }
         }
-        tc_commit(c_free);
+        tc_commit(c_free(i & 1));
         tc_commit(b_empty(i % ST));
       }
       if (ok) {
@@ -276,79 +296,97 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     float v_next = stat(0);
     bool ok = true;
-    for (int i = 0; i < niter; ++i) {
-      int col0, hcol;
-      if (MODE == DKDV) {
-        hcol = hrow * group + i / nblk;
-        col0 = (first_blk + i % nblk) * 64;
-      } else {
-        hcol = hrow;
-        col0 = i * 64;
-      }
-      (void)hcol;
+    auto tbuf = [&](int i) { return tmem + (uint32_t)((i % NB) * 128 + hc * 32) + lane_addr; };
+    // DKDV leaves the loop only through its per-iteration barrier (all threads together); DQ has no barrier
+    for (int i = 0; i < niter && (MODE == DKDV || ok); ++i) {
+      int col0;
+      if (MODE == DKDV) col0 = (first_blk + i % nblk) * 64;
+      else col0 = i * 64;
       float* sld = reinterpret_cast<float*>(smem + L::LD_OFF) + (i & 1) * 128;
+      float s[32], dp[32];
       if (MODE == DKDV) {
         // the block's statistics go through shared memory (read back as broadcasts) instead of every
         // thread loading all 64. The barrier also makes the give-up decision uniform: every thread
         // reaches it after bounded waits and all of them leave the loop together when any wait gave up.
         const float v = v_next;
         v_next = stat(i + 1);
-        if (ok) ok = mbar_wait(sd_full(i & 1), (i / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag);
+        if (ok) ok = mbar_wait(sd_full(i % NB), (i / NB) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag);
         if (et < 128) sld[et] = v;
         if (!bar_sync_and(1, kEwThreads, ok)) {
           ok = false;
           break;
         }
-      } else if (!mbar_wait(sd_full(i & 1), (i / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag)) {
-        ok = false;
-        break;
+        tc_fence_after();
+        tmem_ld32(tbuf(i), reinterpret_cast<uint32_t*>(s));
+        tmem_ld32(tbuf(i) + 64, reinterpret_cast<uint32_t*>(dp));
+        tc_wait_ld();
+        tc_fence_before();
+        mbar_arrive(sd_free(i % NB));
+      } else {
+        if (!mbar_wait(sd_full(i % NB), (i / NB) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        tmem_ld32(tbuf(i), reinterpret_cast<uint32_t*>(s));
+        tmem_ld32(tbuf(i) + 64, reinterpret_cast<uint32_t*>(dp));
+        tc_wait_ld();
+        tc_fence_before();
+        mbar_arrive(sd_free(i % NB));
       }
-      tc_fence_after();
-      float s[32], dp[32];
-      const uint32_t tb = tmem + (uint32_t)((i & 1) * 128 + hc * 32) + lane_addr;
-      tmem_ld32(tb, reinterpret_cast<uint32_t*>(s));
-      tmem_ld32(tb + 64, reinterpret_cast<uint32_t*>(dp));
-      tc_wait_ld();
-      tc_fence_before();
-      mbar_arrive(sd_free(i & 1));
       const int cb = hc * 32;  // this thread's first column of the block
       uint32_t pk[16], dk[16];
       if (MODE == DKDV) {
         const int key = row;
+        // masking only where this warp's 32 queries reach past Sq or across the causal diagonal: one
+        // warp-uniform branch around a separate loop, so the common path has no per-element tests
+        const bool all_valid = col0 + cb + 31 < a.Sq && !(a.causal && key > col0 + cb + off);
+        const float4* l2v = reinterpret_cast<const float4*>(sld + cb);        // broadcast reads
+        const float4* dev = reinterpret_cast<const float4*>(sld + 64 + cb);
+        float pv[32];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float pv[2], dv[2];
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 l4 = l2v[c4];
+          pv[4 * c4] = ex2_fast(fmaf(s[4 * c4], a.scale_log2, -l4.x));
+          pv[4 * c4 + 1] = ex2_fast(fmaf(s[4 * c4 + 1], a.scale_log2, -l4.y));
+          pv[4 * c4 + 2] = ex2_fast(fmaf(s[4 * c4 + 2], a.scale_log2, -l4.z));
+          pv[4 * c4 + 3] = ex2_fast(fmaf(s[4 * c4 + 3], a.scale_log2, -l4.w));
+        }
+        if (__any_sync(0xffffffffu, !all_valid)) {
+          const int lim = a.causal ? key - off : -0x40000000;  // queries below lim are masked (causal)
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int qi = col0 + cb + c + e;
-            const bool valid = qi < a.Sq && !(a.causal && key > qi + off);
-            const float l2 = valid ? sld[cb + c + e] : 0.f;
-            const float de = valid ? sld[64 + cb + c + e] : 0.f;
-            const float p = valid ? ex2_fast(s[c + e] * a.scale_log2 - l2) : 0.f;
-            pv[e] = p;
-            dv[e] = p * (dp[c + e] - de);
+          for (int c = 0; c < 32; ++c) {
+            const int qi = col0 + cb + c;
+            pv[c] = (qi >= a.Sq || qi < lim) ? 0.f : pv[c];
           }
-          __nv_bfloat162 hp = __floats2bfloat162_rn(pv[0], pv[1]);
-          __nv_bfloat162 hd = __floats2bfloat162_rn(dv[0], dv[1]);
-          pk[c / 2] = *reinterpret_cast<uint32_t*>(&hp);
-          dk[c / 2] = *reinterpret_cast<uint32_t*>(&hd);
+        }
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 d4 = dev[c4];
+          const float d0 = pv[4 * c4] * (dp[4 * c4] - d4.x), d1 = pv[4 * c4 + 1] * (dp[4 * c4 + 1] - d4.y);
+          const float d2 = pv[4 * c4 + 2] * (dp[4 * c4 + 2] - d4.z), d3 = pv[4 * c4 + 3] * (dp[4 * c4 + 3] - d4.w);
+          pk[2 * c4] = pack_bf16x2(pv[4 * c4], pv[4 * c4 + 1]);
+          pk[2 * c4 + 1] = pack_bf16x2(pv[4 * c4 + 2], pv[4 * c4 + 3]);
+          dk[2 * c4] = pack_bf16x2(d0, d1);
+          dk[2 * c4 + 1] = pack_bf16x2(d2, d3);
         }
       } else {
+        const bool all_valid = row_valid_q && col0 + cb + 31 < a.Sk && !(a.causal && col0 + cb + 31 > row + off);
+        float pv[32];
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float dv[2];
+        for (int c = 0; c < 32; ++c) pv[c] = ex2_fast(fmaf(s[c], a.scale_log2, -row_lse2));
+        if (__any_sync(0xffffffffu, !all_valid)) {
+          const int lim = !row_valid_q ? -1 : (a.causal ? min(row + off, a.Sk - 1) : a.Sk - 1);  // last visible key
 #pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int key = col0 + cb + c + e;
-            const bool valid = row_valid_q && key < a.Sk && !(a.causal && key > row + off);
-            const float p = valid ? ex2_fast(s[c + e] * a.scale_log2 - row_lse2) : 0.f;
-            dv[e] = p * (dp[c + e] - row_delta);
-          }
-          __nv_bfloat162 hd = __floats2bfloat162_rn(dv[0], dv[1]);
-          dk[c / 2] = *reinterpret_cast<uint32_t*>(&hd);
+          for (int c = 0; c < 32; ++c) pv[c] = (col0 + cb + c > lim) ? 0.f : pv[c];
         }
+#pragma unroll
+        for (int c = 0; c < 32; c += 2)
+          dk[c / 2] = pack_bf16x2(pv[c] * (dp[c] - row_delta), pv[c + 1] * (dp[c + 1] - row_delta));
       }
-      if (i > 0 && !mbar_wait(c_free, (i - 1) & 1, BRAIN_ERR_TIMEOUT_ACC, 231, abort_flag)) {
+      // C buffer i&1 was last read by the accumulate MMAs of block i-2
+      const uint32_t sC = sCb + (i & 1) * L::C_BYTES;
+      if (i > 1 && !mbar_wait(c_free(i & 1), ((i - 2) / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 231, abort_flag)) {
         ok = false;
         if (MODE == DKDV) continue;  // leaves at the next barrier, together with the other threads
         break;
@@ -373,7 +411,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async();
       tc_fence_before();
-      mbar_arrive(c_full);
+      mbar_arrive(c_full(i & 1));
     }
     bool have = ok && niter > 0;
     if (have && !mbar_wait(acc_done, 0, BRAIN_ERR_TIMEOUT_ACC, 232, abort_flag)) have = false;
@@ -396,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = hc * (D / 64); c < (hc + 1) * (D / 64); ++c) {  // this warp's half of the D columns
         uint32_t ov[32];
         if (have) {
-          tmem_ld32(tmem + 256 + (uint32_t)(which * D + c * 32) + lane_addr, ov);
+          tmem_ld32(tmem + L::ACC + (uint32_t)(which * D + c * 32) + lane_addr, ov);
           tc_wait_ld();
         } else {
 #pragma unroll
