@@ -121,6 +121,9 @@ def main():
     ap.add_argument("--decode-pdl", type=int, default=2,
                     help="programmatic dependent launch in the decode step: 0 off, 1 successors launch at a "
                          "kernel's start, 2 after its main loop")
+    ap.add_argument("--torch-master", default="bf16", choices=["bf16", "fp32"],
+                    help="--impl torch optimizer: fused AdamW on the bf16 parameters, or float32 master weights "
+                         "and moments sharded ZeRO-1 style (the framework's precision)")
     ap.add_argument("--decode-shard-of", type=int, default=0,
                     help="development only: run one rank's shard of an N-way TP group on a single GPU")
     args = ap.parse_args()
@@ -297,7 +300,13 @@ def run_torch_baseline(args) -> int:
     model = build(cfg, dev, seed=0)
     ddp = (torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], gradient_as_bucket_view=True)
            if world > 1 else model)
-    opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, fused=True)
+    if args.torch_master == "fp32":
+        from brain_b200.bench.torch_baseline import MasterAdamW
+        opt = MasterAdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, world=world,
+                          rank=rank)
+    else:
+        opt = torch.optim.AdamW(model.parameters(), lr=3e-4, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+                                fused=True)
     B, S, V = args.micro_batch, args.seq, cfg.vocab_size
     cos, sin = model.rope_tables(S, dev)
     gen = torch.Generator(device=dev).manual_seed(1 + rank)
@@ -320,7 +329,8 @@ def run_torch_baseline(args) -> int:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for i in range(max(3, args.warmup)):
+    warm = max(3, args.warmup)
+    for i in range(warm):
         loss = step(pool[i % 4])
     torch.cuda.synchronize()
     log(f"[torch rank {rank}] warm-up done, loss {loss.item():.4f}, peak mem "
@@ -335,7 +345,7 @@ def run_torch_baseline(args) -> int:
     trace = []
     s.record()
     for i in range(args.steps):
-        loss = step(pool[i % 4])
+        loss = step(pool[(warm + i) % 4])
         trace.append(loss.detach())
     e.record()
     torch.cuda.synchronize()
@@ -369,7 +379,10 @@ def run_torch_baseline(args) -> int:
                        "global_batch": B * world, "micro_batch_per_gpu": B, "seq_len": S,
                        "parallelism": f"dp{world}",
                        "implementation": "plain PyTorch: eager nn modules, cuBLAS, F.scaled_dot_product_attention, "
-                                         "torch.optim.AdamW(fused=True) on bf16 parameters, DDP over NCCL",
+                                         + ("float32 master weights and moments (ZeRO-1 sharded), fused torch AdamW"
+                                            if args.torch_master == "fp32" else
+                                            "torch.optim.AdamW(fused=True) on bf16 parameters")
+                                         + ", DDP over NCCL; same initial weights as the framework's model",
                        "l2": "no flush: working set >> 126 MB L2"},
             "final_loss": float(loss.item()), "clocks": clk,
             "e2e": {"value": B * S * world / (ms2 / 1e3), "unit": "tokens/s", "ms_per_step": ms2,

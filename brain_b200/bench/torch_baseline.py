@@ -5,9 +5,10 @@ eager torch modules and nothing from this framework.
   (causal, grouped-query; PyTorch picks its fastest fused backend), RMSNorm as ``nn.RMSNorm``,
   RoPE (NeoX half rotation) and SwiGLU as torch elementwise ops, the LM head and mean
   cross-entropy with ``F.cross_entropy``;
-- bf16 parameters and gradients, ``torch.optim.AdamW(fused=True)`` (its moments follow the
-  parameter dtype, so this baseline moves fewer optimizer bytes than the framework's f32 master
-  weights and moments);
+- bf16 parameters and gradients; the optimizer is either ``torch.optim.AdamW(fused=True)`` on the bf16
+  parameters (its moments follow the parameter dtype: fewer optimizer bytes than the framework's) or,
+  with ``--torch-master fp32``, :class:`MasterAdamW`: float32 master weights and moments, ZeRO-1
+  sharded over the ranks, the same precision as the framework's sharded AdamW;
 - ``torch.nn.parallel.DistributedDataParallel`` over NCCL when there is more than one rank.
 
 ``bench.py --impl torch`` times it with the same rules as the framework's arm (warm-up, CUDA events,
@@ -76,15 +77,82 @@ class TorchLlama(nn.Module):
 
 
 def build(cfg, device, seed=0):
-    """The model in bf16 on `device`, every weight N(0, 0.02) (norm gains 1), seeded."""
+    """The model in bf16 on `device`, seeded exactly like the framework's ``LlamaLite(cfg, seed=seed)``:
+    one generator on the device walks the weight matrices in LlamaLite's parameter order (embedding, LM
+    head, then per block wqkv, wo, w_gate_up, w_down; the same shapes) and draws float32 N(0, 0.02)
+    samples rounded to bf16; norm gains are 1. Both arms therefore start
+    from identical weights, and their loss trajectories on identical data can be compared directly."""
     torch.manual_seed(seed)
     with torch.device(device):
         model = TorchLlama(cfg).to(torch.bfloat16)
     g = torch.Generator(device=device).manual_seed(seed)
+    # LlamaLite's parameter order: its own tensors (embedding, final norm, LM head) before the blocks'
+    order = [model.embed.weight, model.head.weight]
+    for blk in model.blocks:
+        order += [blk.wqkv.weight, blk.wo.weight, blk.w_gate_up.weight, blk.w_down.weight]
     with torch.no_grad():
-        for name, p in model.named_parameters():
-            if "norm" in name:
+        for p in model.parameters():
+            if p.dim() < 2:
                 p.fill_(1.0)
-            else:
-                p.normal_(0.0, 0.02, generator=g)
+        for p in order:
+            p.copy_((torch.randn(p.shape, generator=g, device=p.device, dtype=torch.float32) * cfg.init_std)
+                    .to(p.dtype))
     return model
+
+
+class MasterAdamW:
+    """AdamW on float32 master weights and float32 moments for a bf16 model, in plain PyTorch.
+
+    Gradients arrive in bf16 on the model's parameters (DDP reduces them there). Each step casts them to
+    float32 in chunks of parameters (so at most one chunk of float32 gradients exists at a time), runs
+    ``torch.optim.AdamW(fused=True)`` on the chunk's master weights and copies the result back to the
+    bf16 parameters. With ``world > 1`` the optimizer state is sharded ZeRO-1 style: parameters are dealt
+    round-robin by size to ranks, each rank steps only its own, and the updated bf16 weights are
+    broadcast from their owners (one NCCL broadcast per parameter, coalesced by torch)."""
+
+    def __init__(self, params, lr, betas, eps, weight_decay, world=1, rank=0, chunk_bytes=2 << 30):
+        import torch.distributed as dist
+        self.params = [p for p in params if p.requires_grad]
+        self.world, self.rank = world, rank
+        owners, load = [], [0] * world
+        for p in sorted(self.params, key=lambda t: -t.numel()):
+            r = min(range(world), key=lambda i: load[i])
+            owners.append((p, r))
+            load[r] += p.numel()
+        self.owner = {id(p): r for p, r in owners}
+        mine = [p for p in self.params if self.owner[id(p)] == rank]
+        self.master = {id(p): torch.nn.Parameter(p.detach().float().clone()) for p in mine}
+        self.chunks, cur, size = [], [], 0
+        for p in mine:
+            cur.append(p)
+            size += p.numel() * 4
+            if size >= chunk_bytes:
+                self.chunks.append(cur)
+                cur, size = [], 0
+        if cur:
+            self.chunks.append(cur)
+        self.opts = [torch.optim.AdamW([self.master[id(p)] for p in c], lr=lr, betas=betas, eps=eps,
+                                       weight_decay=weight_decay, fused=True) for c in self.chunks]
+        self._dist = dist
+
+    @torch.no_grad()
+    def step(self):
+        for chunk, opt in zip(self.chunks, self.opts):
+            for p in chunk:
+                self.master[id(p)].grad = p.grad.float()
+            opt.step()
+            for p in chunk:
+                m = self.master[id(p)]
+                m.grad = None
+                p.copy_(m)
+        if self.world > 1:
+            for p in self.params:
+                self._dist.broadcast(p.data, self.owner[id(p)])
+
+    def zero_grad(self, set_to_none=False):
+        for p in self.params:
+            if p.grad is not None:
+                if set_to_none:
+                    p.grad = None
+                else:
+                    p.grad.zero_()

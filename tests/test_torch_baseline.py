@@ -1,0 +1,42 @@
+"""The plain-PyTorch comparison arm of the benchmark: it starts from exactly the framework model's
+weights, and its float32-master AdamW matches torch.optim.AdamW on float32 weights."""
+import torch
+
+from brain_b200.bench.torch_baseline import MasterAdamW, build
+from brain_b200.models import LlamaLite, LlamaLiteConfig
+
+
+def _cfg():
+    return LlamaLiteConfig(vocab_size=256, hidden_dim=64, num_layers=2, num_heads=4, num_kv_heads=2, head_dim=16,
+                           intermediate_dim=96, max_seq_len=32)
+
+
+def test_same_initial_weights_as_the_framework_model():
+    cfg = _cfg()
+    ours = dict(LlamaLite(cfg, device="cpu", dtype=torch.bfloat16, seed=3).named_parameters())
+    theirs = list(build(cfg, "cpu", seed=3).parameters())
+    names = ["embed"] + [f"layers.{i}.{n}" for i in range(cfg.num_layers)
+                         for n in ("attn_norm", "wqkv", "wo", "ffn_norm", "w_gate_up", "w_down")] + ["final_norm", "lm_head"]
+    assert len(theirs) == len(names)
+    for n, t in zip(names, theirs):
+        assert torch.equal(ours[n].detach(), t.detach()), n
+
+
+def test_master_adamw_matches_float32_adamw():
+    torch.manual_seed(0)
+    p16 = [torch.nn.Parameter(torch.randn(40, 8).bfloat16()), torch.nn.Parameter(torch.randn(8).bfloat16())]
+    p32 = [torch.nn.Parameter(p.detach().float().clone()) for p in p16]
+    opt = MasterAdamW(p16, lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, chunk_bytes=64)
+    ref = torch.optim.AdamW(p32, lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    assert len(opt.chunks) == 2  # chunked float32 gradients
+    for _ in range(3):
+        g = [torch.randn_like(p, dtype=torch.float32) for p in p16]
+        for p, gi in zip(p16, g):
+            p.grad = gi.bfloat16()
+        for p, gi in zip(p32, g):
+            p.grad = gi.bfloat16().float()
+        opt.step()
+        ref.step()
+    for a, b in zip(p16, p32):
+        torch.testing.assert_close(a.float(), b.detach().bfloat16().float())
+        torch.testing.assert_close(opt.master[id(a)].detach(), b.detach(), rtol=1e-5, atol=1e-6)
