@@ -39,6 +39,9 @@ struct BwdArgs {
   int B, Hq, Hkv, Sq, Sk;
   float scale, scale_log2;
   int causal;
+  // optional (BIAS kernels), as in the forward: key padding mask [B, Sk] and relative bias relb[Hq, Sq + Sk - 1]
+  const uint8_t* kmask;
+  const float* relb;
 };
 
 template <int D, int MODE>
@@ -65,7 +68,7 @@ struct BwdLayout {
   static_assert(TOTAL <= 232448, "more dynamic shared memory than one CTA may use");
 };
 
-template <int D, int MODE>
+template <int D, int MODE, bool BIAS>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap mA1, const __grid_constant__ CUtensorMap mA2,
                      const __grid_constant__ CUtensorMap mB1, const __grid_constant__ CUtensorMap mB2, BwdArgs a) {
@@ -344,6 +347,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float4* l2v = reinterpret_cast<const float4*>(sld + cb);        // broadcast reads
         const float4* dev = reinterpret_cast<const float4*>(sld + 64 + cb);
         float pv[32];
+        if constexpr (BIAS) {
+          // this thread's key: padding mask and the bias per query column, every test per element
+          const int hcol = hrow * group + i / nblk;
+          const bool key_ok = key < a.Sk && (!a.kmask || a.kmask[(int64_t)b * a.Sk + key] != 0);
+          const float* rb = a.relb ? a.relb + (int64_t)hcol * (a.Sq + a.Sk - 1) + (key - col0 - cb + a.Sq - 1) : nullptr;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int qi = col0 + cb + c;
+            const bool valid = key_ok && qi < a.Sq && !(a.causal && key > qi + off);
+            const float bias = (rb && valid) ? __ldg(rb - c) * kLog2e : 0.f;
+            pv[c] = valid ? ex2_fast(fmaf(s[c], a.scale_log2, bias - sld[cb + c])) : 0.f;
+          }
+        } else {
 #pragma unroll
         for (int c4 = 0; c4 < 8; ++c4) {
           const float4 l4 = l2v[c4];
@@ -352,7 +368,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           pv[4 * c4 + 2] = ex2_fast(fmaf(s[4 * c4 + 2], a.scale_log2, -l4.z));
           pv[4 * c4 + 3] = ex2_fast(fmaf(s[4 * c4 + 3], a.scale_log2, -l4.w));
         }
-        if (__any_sync(0xffffffffu, !all_valid)) {
+        }
+        if (!BIAS && __any_sync(0xffffffffu, !all_valid)) {
           const int lim = a.causal ? key - off : -0x40000000;  // queries below lim are masked (causal)
 #pragma unroll
           for (int c = 0; c < 32; ++c) {
@@ -373,9 +390,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         const bool all_valid = row_valid_q && col0 + cb + 31 < a.Sk && !(a.causal && col0 + cb + 31 > row + off);
         float pv[32];
+        if constexpr (BIAS) {
+          uint32_t kbits[2] = {~0u, ~0u};  // key col0 + 2 i + t of the block is attended iff bit i of kbits[t]
+          if (a.kmask) {
+            const uint8_t* km = a.kmask + (int64_t)b * a.Sk;
 #pragma unroll
-        for (int c = 0; c < 32; ++c) pv[c] = ex2_fast(fmaf(s[c], a.scale_log2, -row_lse2));
-        if (__any_sync(0xffffffffu, !all_valid)) {
+            for (int t2 = 0; t2 < 2; ++t2) {
+              const int key = col0 + 2 * lane + t2;
+              kbits[t2] = __ballot_sync(0xffffffffu, key < a.Sk && km[key] != 0);
+            }
+          }
+          const float* rb = a.relb ? a.relb + (int64_t)hrow * (a.Sq + a.Sk - 1) + (col0 + cb - row + a.Sq - 1) : nullptr;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            const int key = col0 + cb + c, idx = cb + c;
+            const bool valid = row_valid_q && key < a.Sk && !(a.causal && key > row + off) &&
+                               ((kbits[idx & 1] >> (idx >> 1)) & 1u);
+            const float bias = (rb && valid) ? __ldg(rb + c) * kLog2e : 0.f;
+            pv[c] = valid ? ex2_fast(fmaf(s[c], a.scale_log2, bias - row_lse2)) : 0.f;
+          }
+        } else {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) pv[c] = ex2_fast(fmaf(s[c], a.scale_log2, -row_lse2));
+        }
+        if (!BIAS && __any_sync(0xffffffffu, !all_valid)) {
           const int lim = !row_valid_q ? -1 : (a.causal ? min(row + off, a.Sk - 1) : a.Sk - 1);  // last visible key
 #pragma unroll
           for (int c = 0; c < 32; ++c) pv[c] = (col0 + cb + c > lim) ? 0.f : pv[c];
@@ -492,11 +530,11 @@ bool map4(CUtensorMap* m, const void* base, int D, int S, int H, int B, int64_t 
                                   CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int D, int MODE>
-int launch_mode(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap& b1, const CUtensorMap& b2,
-                const BwdArgs& a, cudaStream_t st) {
+template <int D, int MODE, bool BIAS>
+int launch_kernel(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap& b1, const CUtensorMap& b2,
+                  const BwdArgs& a, cudaStream_t st) {
   using L = BwdLayout<D, MODE>;
-  auto kern = fa_bwd_tc_kernel<D, MODE>;
+  auto kern = fa_bwd_tc_kernel<D, MODE, BIAS>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
   dim3 grid;
   if (MODE == DKDV) grid = dim3((a.Sk + 127) / 128, a.B * a.Hkv);
@@ -505,17 +543,21 @@ int launch_mode(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap&
   return (int)cudaGetLastError();
 }
 
+template <int D, int MODE>
+int launch_mode(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMap& b1, const CUtensorMap& b2,
+                const BwdArgs& a, cudaStream_t st) {
+  if (a.kmask || a.relb) return launch_kernel<D, MODE, true>(a1, a2, b1, b2, a, st);
+  return launch_kernel<D, MODE, false>(a1, a2, b1, b2, a, st);
+}
 }  // namespace
 
 BRAIN_STATUS_READER(attention_bwd_tc)
 
-// Same argument contract as brain_attn_bwd (attention.cu). Returns cudaErrorNotSupported without
-// launching when the layout is outside the tensor-core path (D not 64/128, unaligned strides).
-BRAIN_API int brain_attn_bwd_tc(const void* q, const void* k, const void* v, const int64_t* s9, const void* o,
-                                const int64_t* ostr, const float* lse, const void* dout, const int64_t* dostr,
-                                void* dq, const int64_t* dqstr, void* dk, const int64_t* dkstr, void* dv,
-                                const int64_t* dvstr, float* delta, int B, int Hq, int Hkv, int Sq, int Sk, int D,
-                                float scale, int causal, cudaStream_t st) {
+namespace {
+int bwd_tc(const void* q, const void* k, const void* v, const int64_t* s9, const void* o, const int64_t* ostr,
+           const float* lse, const void* dout, const int64_t* dostr, void* dq, const int64_t* dqstr, void* dk,
+           const int64_t* dkstr, void* dv, const int64_t* dvstr, float* delta, int B, int Hq, int Hkv, int Sq, int Sk,
+           int D, float scale, int causal, const uint8_t* kmask, const float* relb, cudaStream_t st) {
   if (Hkv <= 0 || Hq % Hkv) return (int)cudaErrorInvalidValue;
   if (D != 64 && D != 128) return (int)cudaErrorNotSupported;
   const int64_t* all[6] = {s9, s9 + 3, s9 + 6, dostr, ostr, dqstr};
@@ -552,6 +594,8 @@ BRAIN_API int brain_attn_bwd_tc(const void* q, const void* k, const void* v, con
   a.scale = scale;
   a.scale_log2 = scale * kLog2e;
   a.causal = causal;
+  a.kmask = kmask;
+  a.relb = relb;
   // dK / dV
   a.out1 = reinterpret_cast<__nv_bfloat16*>(dv);
   a.o1b = dvstr[0]; a.o1s = dvstr[1]; a.o1h = dvstr[2];
@@ -566,4 +610,28 @@ BRAIN_API int brain_attn_bwd_tc(const void* q, const void* k, const void* v, con
   a.out2 = nullptr;
   return D == 64 ? launch_mode<64, DQ>(mq128, mdo128, mk64, mv64, a, st)
                  : launch_mode<128, DQ>(mq128, mdo128, mk64, mv64, a, st);
+}
+}  // namespace
+
+// Same argument contract as brain_attn_bwd (attention.cu). Returns cudaErrorNotSupported without
+// launching when the layout is outside the tensor-core path (D not 64/128, unaligned strides).
+BRAIN_API int brain_attn_bwd_tc(const void* q, const void* k, const void* v, const int64_t* s9, const void* o,
+                                const int64_t* ostr, const float* lse, const void* dout, const int64_t* dostr,
+                                void* dq, const int64_t* dqstr, void* dk, const int64_t* dkstr, void* dv,
+                                const int64_t* dvstr, float* delta, int B, int Hq, int Hkv, int Sq, int Sk, int D,
+                                float scale, int causal, cudaStream_t st) {
+  return bwd_tc(q, k, v, s9, o, ostr, lse, dout, dostr, dq, dqstr, dk, dkstr, dv, dvstr, delta, B, Hq, Hkv, Sq, Sk, D,
+                scale, causal, nullptr, nullptr, st);
+}
+
+// Same, with the forward's key padding mask and relative bias (brain_attn_fwd_tc_masked); the bias is
+// treated as a constant (no gradient).
+BRAIN_API int brain_attn_bwd_tc_masked(const void* q, const void* k, const void* v, const int64_t* s9, const void* o,
+                                       const int64_t* ostr, const float* lse, const void* dout, const int64_t* dostr,
+                                       void* dq, const int64_t* dqstr, void* dk, const int64_t* dkstr, void* dv,
+                                       const int64_t* dvstr, float* delta, int B, int Hq, int Hkv, int Sq, int Sk,
+                                       int D, float scale, int causal, const uint8_t* kmask, const float* relb,
+                                       cudaStream_t st) {
+  return bwd_tc(q, k, v, s9, o, ostr, lse, dout, dostr, dq, dqstr, dk, dkstr, dv, dvstr, delta, B, Hq, Hkv, Sq, Sk, D,
+                scale, causal, kmask, relb, st);
 }

@@ -44,6 +44,11 @@ struct FwdArgs {
   int B, Hq, Hkv, Sq, Sk;
   float scale_log2;
   int causal;
+  // optional (BIAS kernels): key padding mask [B, Sk] (non-zero = attend), and an additive bias that depends
+  // only on the key-query offset, per q head: relb[h, (k - q) + Sq - 1], float32 natural-log units
+  // (ALiBi, T5 relative buckets); null when absent
+  const uint8_t* kmask;
+  const float* relb;
 };
 
 template <int D>
@@ -70,7 +75,7 @@ __device__ __forceinline__ int tile_blocks(const FwdArgs& a, int m0, int t) {
   return kend > 0 ? (kend + 127) / 128 : 0;
 }
 
-template <int D>
+template <int D, bool BIAS>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, FwdArgs a) {
@@ -313,8 +318,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       float mxp[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) mxp[u] = -INFINITY;
-      // raw scores: the log2-domain scale (> 0) is applied in the exponent's FFMA, max(c s) = c max(s)
-      if (need_mask) {
+      if constexpr (BIAS) {
+        // scores in log2 units with the bias added, -inf where masked: t = s c + bias log2(e)
+        uint32_t kbits[4] = {~0u, ~0u, ~0u, ~0u};  // key n0 + 4 i + t is attended iff bit i of kbits[t]
+        if (a.kmask) {
+          const uint8_t* km = a.kmask + (int64_t)b * a.Sk;
+#pragma unroll
+          for (int t4 = 0; t4 < 4; ++t4) {
+            const int key = n0 + 4 * lane + t4;
+            kbits[t4] = __ballot_sync(0xffffffffu, key < a.Sk && km[key] != 0);
+          }
+        }
+        const bool row_ok = qi < a.Sq;
+        const float* rb = a.relb ? a.relb + (int64_t)h * (a.Sq + a.Sk - 1) + (n0 - qi + a.Sq - 1) : nullptr;
+#pragma unroll
+        for (int k = 0; k < 128; ++k) {
+          const bool valid = n0 + k <= limit && ((kbits[k & 3] >> (k >> 2)) & 1u);
+          const float bias = (rb && valid && row_ok) ? __ldg(rb + k) * kLog2e : 0.f;
+          s[k] = valid ? fmaf(s[k], a.scale_log2, bias) : -INFINITY;
+          mxp[k & 7] = fmaxf(mxp[k & 7], s[k]);
+        }
+      } else if (need_mask) {
 #pragma unroll
         for (int k = 0; k < 128; ++k) {
           if (n0 + k > limit) s[k] = -INFINITY;
@@ -324,8 +348,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k = 0; k < 128; ++k) mxp[k & 7] = fmaxf(mxp[k & 7], s[k]);
       }
-      const float mx = a.scale_log2 * fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                                            fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      // BIAS: the scores are already scaled; otherwise raw scores, and the log2-domain scale (> 0) is
+      // applied in the exponent's FFMA: max(c s) = c max(s)
+      const float mx = (BIAS ? 1.f : a.scale_log2) * fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                                                           fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       float alpha = 1.f;
       if (mx > m_used + kRescaleThreshold || (m_used == -INFINITY && mx > -INFINITY)) {
         alpha = exp2f(m_used - mx);  // 0 when m_used == -inf
@@ -352,8 +378,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int k = 0; k < 32; k += 2) {
-          const float p0 = ex2_fast(fmaf(s[c * 32 + k], a.scale_log2, -mu));
-          const float p1 = ex2_fast(fmaf(s[c * 32 + k + 1], a.scale_log2, -mu));
+          const float p0 = BIAS ? ex2_fast(s[c * 32 + k] - mu) : ex2_fast(fmaf(s[c * 32 + k], a.scale_log2, -mu));
+          const float p1 = BIAS ? ex2_fast(s[c * 32 + k + 1] - mu)
+                                : ex2_fast(fmaf(s[c * 32 + k + 1], a.scale_log2, -mu));
           sp[(k >> 1) & 7] += p0 + p1;
           pk[k / 2] = pack_bf16x2(p0, p1);
         }
@@ -410,10 +437,10 @@ bool make_map(CUtensorMap* m, const void* base, int D, int S, int H, int B, int6
                                   CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-template <int D>
+template <int D, bool BIAS>
 int launch(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, const FwdArgs& a, cudaStream_t st) {
   using L = FwdLayout<D>;
-  auto kern = fa_fwd_tc_kernel<D>;
+  auto kern = fa_fwd_tc_kernel<D, BIAS>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
   dim3 grid((a.Sq + 255) / 256, a.B * a.Hq);
   kern<<<grid, kThreads, L::TOTAL, st>>>(q, k, v, a);
@@ -424,12 +451,10 @@ int launch(const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v, con
 
 BRAIN_STATUS_READER(attention_tc)
 
-// Returns cudaErrorNotSupported (without launching) when the layout is outside what the tensor-core
-// path handles (D not 64/128, strides not 16-byte multiples, misaligned bases); callers then use the
-// mma.sync kernel.
-BRAIN_API int brain_attn_fwd_tc(const void* q, const void* k, const void* v, const int64_t* s9, void* o,
-                                const int64_t* ostr, float* lse, int B, int Hq, int Hkv, int Sq, int Sk, int D,
-                                float scale, int causal, cudaStream_t st) {
+namespace {
+int fwd_tc(const void* q, const void* k, const void* v, const int64_t* s9, void* o, const int64_t* ostr, float* lse,
+           int B, int Hq, int Hkv, int Sq, int Sk, int D, float scale, int causal, const uint8_t* kmask,
+           const float* relb, cudaStream_t st) {
   if (Hkv <= 0 || Hq % Hkv) return (int)cudaErrorInvalidValue;
   if ((D != 64 && D != 128)) return (int)cudaErrorNotSupported;
   for (int i = 0; i < 9; ++i)
@@ -448,5 +473,28 @@ BRAIN_API int brain_attn_fwd_tc(const void* q, const void* k, const void* v, con
   a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.Sq = Sq; a.Sk = Sk;
   a.scale_log2 = scale * kLog2e;
   a.causal = causal;
-  return D == 64 ? launch<64>(tq, tk, tv, a, st) : launch<128>(tq, tk, tv, a, st);
+  a.kmask = kmask;
+  a.relb = relb;
+  if (kmask || relb) return D == 64 ? launch<64, true>(tq, tk, tv, a, st) : launch<128, true>(tq, tk, tv, a, st);
+  return D == 64 ? launch<64, false>(tq, tk, tv, a, st) : launch<128, false>(tq, tk, tv, a, st);
+}
+}  // namespace
+
+// Returns cudaErrorNotSupported (without launching) when the layout is outside what the tensor-core
+// path handles (D not 64/128, strides not 16-byte multiples, misaligned bases); callers then use the
+// mma.sync kernel.
+BRAIN_API int brain_attn_fwd_tc(const void* q, const void* k, const void* v, const int64_t* s9, void* o,
+                                const int64_t* ostr, float* lse, int B, int Hq, int Hkv, int Sq, int Sk, int D,
+                                float scale, int causal, cudaStream_t st) {
+  return fwd_tc(q, k, v, s9, o, ostr, lse, B, Hq, Hkv, Sq, Sk, D, scale, causal, nullptr, nullptr, st);
+}
+
+// Same, with a key padding mask kmask [B, Sk] (uint8, non-zero = attend; may be null) and an additive bias
+// relb [Hq, Sq + Sk - 1] (float32, natural-log units; element (k - q) + Sq - 1 is added to score (q, k);
+// may be null). Query rows whose keys are all masked get a zero output and lse = -inf.
+BRAIN_API int brain_attn_fwd_tc_masked(const void* q, const void* k, const void* v, const int64_t* s9, void* o,
+                                       const int64_t* ostr, float* lse, int B, int Hq, int Hkv, int Sq, int Sk, int D,
+                                       float scale, int causal, const uint8_t* kmask, const float* relb,
+                                       cudaStream_t st) {
+  return fwd_tc(q, k, v, s9, o, ostr, lse, B, Hq, Hkv, Sq, Sk, D, scale, causal, kmask, relb, st);
 }

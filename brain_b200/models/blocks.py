@@ -3,8 +3,9 @@
 Mirrors the reference's encoder/decoder stacks (crates/brain-transformer/src/encoder/*.rs,
 decoder/mod.rs:60-150, decoder/layer.rs:60-260): pre- or post-norm, LayerNorm or RMSNorm, GELU
 (tanh) or SwiGLU FFN, optional causal self-attention and cross-attention, and a final norm.
-Self-attention runs the flash kernels through a fused QKV projection; attention with an additive
-bias (T5 relative buckets, ALiBi) uses the float32 reference SDPA.
+Self-attention runs the flash kernels through a fused QKV projection; key padding masks and relative
+biases (ALiBi, T5 buckets without a gradient) run on the masked tcgen05 kernels
+(``ops.attention.masked_attention``), a learned bias that needs its gradient on the float32 reference SDPA.
 """
 from __future__ import annotations
 
@@ -21,14 +22,16 @@ def make_norm(kind: str, dim: int, eps: float, device=None, dtype=None):
     return RMSNorm(dim, eps, device, dtype) if kind == "rms" else LayerNorm(dim, eps, True, device, dtype)
 
 
-def sdpa_with_bias(q, k, v, bias=None, causal=False, mask=None):
+def sdpa_with_bias(q, k, v, bias=None, causal=False, mask=None, scale=None):
     """[B, S, H, D] attention with an additive [H, Sq, Sk] / [B, H, Sq, Sk] bias (float32)."""
     D = q.shape[-1]
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
     qf, kf, vf = (x.float().transpose(1, 2) for x in (q, k, v))
     if kf.shape[1] != qf.shape[1]:
         rep = qf.shape[1] // kf.shape[1]
         kf, vf = kf.repeat_interleave(rep, 1), vf.repeat_interleave(rep, 1)
-    s = qf @ kf.transpose(-1, -2) / math.sqrt(D)
+    s = (qf @ kf.transpose(-1, -2)) * scale
     if bias is not None:
         s = s + bias.float()
     Sq, Sk = s.shape[-2], s.shape[-1]
@@ -98,8 +101,10 @@ class SelfAttention(Module):
         if attn_bias is None and mask is None:
             o = ops.qkv_attention(qkv, self.h, self.hkv, rope, causal=self.causal)
         else:
+            # padding masks and relative biases (ALiBi, T5 buckets) on the tcgen05 kernels where possible
             q, k, v = ops.attention.split_qkv(qkv, self.h, self.hkv)
-            o = sdpa_with_bias(q, k, v, attn_bias, self.causal, mask).reshape(x.shape[0], x.shape[1], -1)
+            o = ops.attention.masked_attention(q, k, v, self.causal, mask, attn_bias)
+            o = o.reshape(x.shape[0], x.shape[1], -1)
         return self.out(o, residual)
 
 
@@ -119,7 +124,7 @@ class CrossAttention(Module):
         if mem_mask is None and x.is_cuda:
             o = ops.flash_attention(q, k, v, causal=False)
         else:
-            o = sdpa_with_bias(q, k, v, None, False, mem_mask)
+            o = ops.attention.masked_attention(q, k, v, False, mem_mask)
         return self.out(o.reshape(B, S, -1), residual)
 
 

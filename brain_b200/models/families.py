@@ -134,10 +134,13 @@ class T5Lite(Module):
         _init.init_normal_(self, 0.02, seed)
 
     def _bias(self, table, Sq, Sk, bidirectional, device):
+        """The bucketed bias as a function of the key-query offset k - q (``RelativeBias``, [H, Sq + Sk - 1]):
+        the masked flash kernels read it directly when it needs no gradient."""
+        from ..ops.attention import RelativeBias
         c = self.config
-        rel = torch.arange(Sk, device=device)[None, :] - torch.arange(Sq, device=device)[:, None]
+        rel = torch.arange(-(Sq - 1), Sk, device=device)
         b = relative_position_bucket(rel, bidirectional, c.relative_buckets, c.max_distance)
-        return table[b].permute(2, 0, 1)  # [H, Sq, Sk]
+        return RelativeBias(table[b].t().float(), Sq, Sk)  # [H, Sq + Sk - 1]
 
     def forward(self, src_ids, tgt_ids):
         Ss, St = src_ids.shape[1], tgt_ids.shape[1]

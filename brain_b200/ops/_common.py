@@ -36,6 +36,8 @@ _native.register({
     "brain_attn_fwd_tc": ("brain_kernels", "pppppppiiiiiifis"),
     "brain_status_attention_tc": ("brain_kernels", "pi"),
     "brain_attn_bwd_tc": ("brain_kernels", "pppppppppppppppp" + "iiiiiifis"),
+    "brain_attn_fwd_tc_masked": ("brain_kernels", "pppppppiiiiiifipps"),
+    "brain_attn_bwd_tc_masked": ("brain_kernels", "pppppppppppppppp" + "iiiiiifipps"),
     "brain_status_attention_bwd_tc": ("brain_kernels", "pi"),
     "brain_status_norms": ("brain_kernels", "pi"),
     "brain_status_elementwise": ("brain_kernels", "pi"),

@@ -182,3 +182,94 @@ def qkv_attention(qkv: torch.Tensor, Hq: int, Hkv: int, rope_table: torch.Tensor
         k = rope_ref(k, rope_table, None, offset)
     o = sdpa_ref(q, k, v, causal, scale)
     return o.reshape(qkv.shape[0], qkv.shape[1], -1)
+
+
+# --------------------------------------------------------------------------- masks and relative biases
+class RelativeBias:
+    """An additive attention bias that depends only on the key-query offset: ``vec[h, (k - q) + Sq - 1]``
+    (float32, natural-log units, ``[Hq, Sq + Sk - 1]``), as ALiBi and T5's relative buckets are. The
+    tcgen05 kernels read the vector directly; ``dense()`` materialises ``[Hq, Sq, Sk]`` for the
+    float32 reference path (differentiable when ``vec`` is)."""
+
+    def __init__(self, vec: torch.Tensor, Sq: int, Sk: int):
+        if vec.shape[-1] != Sq + Sk - 1:
+            raise ValueError(f"relative bias length {vec.shape[-1]} != Sq + Sk - 1 = {Sq + Sk - 1}")
+        self.vec, self.Sq, self.Sk = vec, Sq, Sk
+
+    def dense(self) -> torch.Tensor:
+        q = torch.arange(self.Sq, device=self.vec.device)[:, None]
+        k = torch.arange(self.Sk, device=self.vec.device)[None, :]
+        return self.vec[:, k - q + self.Sq - 1]
+
+
+def alibi_relative_bias(num_heads: int, Sq: int, Sk: int, causal: bool = True, device=None) -> RelativeBias:
+    """ALiBi (crates/brain-transformer/src/position/alibi.rs:49-120) as a relative bias: -slope_h times the
+    distance between the bottom-right aligned query position q + Sk - Sq and key k (absolute distance
+    when not causal); the same values as ``models.position.alibi_bias``."""
+    from ..models.position import alibi_slopes
+    d = torch.arange(-(Sq - 1), Sk, device=device, dtype=torch.float32) - (Sk - Sq)  # k - (q + Sk - Sq)
+    dist = -d if causal else d.abs()
+    return RelativeBias((-alibi_slopes(num_heads).to(device)[:, None] * dist[None]).contiguous(), Sq, Sk)
+
+
+def _tc_ok(q, k, v):
+    D = q.shape[-1]
+    return (q.is_cuda and q.dtype == torch.bfloat16 and D in (64, 128)
+            and all(t.stride(-1) == 1 and all((s * 2) % 16 == 0 for s in t.stride()[:-1]) for t in (q, k, v)))
+
+
+class _MaskedFlashFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, causal, scale, kmask, relb):
+        B, Sq, Hq, D = q.shape
+        Sk, Hkv = k.shape[1], k.shape[2]
+        o = torch.empty(B, Sq, Hq, D, device=q.device, dtype=q.dtype)
+        lse = torch.empty(B, Hq, Sq, device=q.device, dtype=torch.float32)
+        _native.call("brain_attn_fwd_tc_masked", q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                     i64_array(_strides3(q) + _strides3(k) + _strides3(v)), o.data_ptr(), i64_array(_strides3(o)),
+                     lse.data_ptr(), B, Hq, Hkv, Sq, Sk, D, float(scale), int(causal),
+                     0 if kmask is None else kmask.data_ptr(), 0 if relb is None else relb.data_ptr(), stream(q))
+        ctx.save_for_backward(q, k, v, o, lse, *(t for t in (kmask, relb) if t is not None))
+        ctx.meta = (causal, scale, kmask is not None, relb is not None)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        causal, scale, has_m, has_b = ctx.meta
+        q, k, v, o, lse, *rest = ctx.saved_tensors
+        kmask = rest.pop(0) if has_m else None
+        relb = rest.pop(0) if has_b else None
+        do = do if do.stride(3) == 1 else do.contiguous()
+        B, Sq, Hq, D = q.shape
+        Sk, Hkv = k.shape[1], k.shape[2]
+        dq = torch.empty_like(q, memory_format=torch.contiguous_format)
+        dk = torch.empty(k.shape, device=k.device, dtype=k.dtype)
+        dv = torch.empty(v.shape, device=v.device, dtype=v.dtype)
+        delta = torch.empty(B * Hq * Sq, device=q.device, dtype=torch.float32)
+        _native.call("brain_attn_bwd_tc_masked", q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                     i64_array(_strides3(q) + _strides3(k) + _strides3(v)), o.data_ptr(), i64_array(_strides3(o)),
+                     lse.data_ptr(), do.data_ptr(), i64_array(_strides3(do)), dq.data_ptr(), i64_array(_strides3(dq)),
+                     dk.data_ptr(), i64_array(_strides3(dk)), dv.data_ptr(), i64_array(_strides3(dv)), delta.data_ptr(),
+                     B, Hq, Hkv, Sq, Sk, D, float(scale), int(causal), 0 if kmask is None else kmask.data_ptr(),
+                     0 if relb is None else relb.data_ptr(), stream(q))
+        return dq, dk, dv, None, None, None, None
+
+
+def masked_attention(q, k, v, causal: bool = False, key_mask: torch.Tensor | None = None,
+                     bias: "RelativeBias | torch.Tensor | None" = None, scale: float | None = None):
+    """Attention on [B, S, H, D] (GQA allowed) with a key padding mask ``[B, Sk]`` (True = attend) and/or an
+    additive bias: a :class:`RelativeBias` (ALiBi, T5 buckets) or a dense ``[H, Sq, Sk]`` /
+    ``[B, H, Sq, Sk]`` tensor (crates/brain-transformer/src/core.rs:81-107 ``AttentionMask::{Padding,
+    AdditiveBias, CausalWithPadding}``). The tcgen05 kernels run it when the inputs are bf16 CUDA tensors
+    with head_dim 64 / 128 and the bias is a relative one that needs no gradient; otherwise the float32
+    reference SDPA does, which also gives the gradient of a learned bias."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    rel = bias if isinstance(bias, RelativeBias) else None
+    kernel = _tc_ok(q, k, v) and (bias is None or (rel is not None and not rel.vec.requires_grad))
+    if kernel:
+        km = None if key_mask is None else key_mask.to(device=q.device, dtype=torch.uint8).contiguous()
+        rb = None if rel is None else rel.vec.detach().to(device=q.device, dtype=torch.float32).contiguous()
+        return _MaskedFlashFn.apply(q, k, v, causal, scale, km, rb)
+    dense = rel.dense() if rel is not None else bias
+    from ..models.blocks import sdpa_with_bias
+    return sdpa_with_bias(q, k, v, dense, causal, key_mask, scale=scale)

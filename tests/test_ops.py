@@ -398,3 +398,39 @@ def test_flash_attention_tcgen05_production_length(Hq, Hkv):
         assert _rel(got, want) < 1e-2
         close(got, want, 5e-2, 1e-1)
     assert ops.check_status() == []
+
+
+@gpu
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("case", ["mask", "alibi_causal", "alibi_mask", "t5", "mask_causal_gqa"])
+def test_masked_attention_tcgen05_matches_reference(D, case):
+    """Key padding masks and relative biases (ALiBi, T5 buckets) on the tcgen05 kernels, forward and all
+    three gradients, against the float32 reference SDPA with the dense bias."""
+    from brain_b200.models.blocks import sdpa_with_bias
+    from brain_b200.models.families import relative_position_bucket
+    B, Sq, Sk, Hq, Hkv = 2, 200, 200, 4, 4
+    if case == "mask_causal_gqa":
+        Hkv = 2
+    causal = case in ("alibi_causal", "mask_causal_gqa")
+    q, k, v = rnd(B, Sq, Hq, D, seed=70), rnd(B, Sk, Hkv, D, seed=71), rnd(B, Sk, Hkv, D, seed=72)
+    do = rnd(B, Sq, Hq, D, seed=73)
+    mask, bias = None, None
+    if "mask" in case:
+        lens = torch.tensor([Sk, 137], device="cuda")
+        mask = torch.arange(Sk, device="cuda")[None, :] < lens[:, None]
+    if "alibi" in case:
+        bias = attn.alibi_relative_bias(Hq, Sq, Sk, causal=causal, device="cuda")
+    if case == "t5":
+        table = torch.randn(32, Hq, device="cuda") * 0.5
+        rel = torch.arange(-(Sq - 1), Sk, device="cuda")
+        bias = attn.RelativeBias(table[relative_position_bucket(rel, True, 32, 128)].t().contiguous(), Sq, Sk)
+    o, (qg, kg, vg) = grads(lambda a, b, c: attn.masked_attention(a, b, c, causal, mask, bias), q, k, v)
+    o.backward(do)
+    dense = bias.dense() if bias is not None else None
+    ref, (qr, kr, vr) = grads(lambda a, b, c: sdpa_with_bias(a.float(), b.float(), c.float(), dense, causal, mask), q, k, v)
+    ref.backward(do.float())
+    close(o, ref, 2e-2, 2e-2)
+    close(qg.grad, qr.grad, 3e-2, 3e-2)
+    close(kg.grad, kr.grad, 3e-2, 3e-2)
+    close(vg.grad, vr.grad, 3e-2, 3e-2)
+    _no_status()
