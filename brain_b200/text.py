@@ -998,3 +998,87 @@ class TextSimilarity:
         g1 = {s1[i:i + n] for i in range(len(s1) - n + 1)}
         g2 = {s2[i:i + n] for i in range(len(s2) - n + 1)}
         return len(g1 & g2) / len(g1 | g2) if g1 | g2 else 1.0
+
+
+# --------------------------------------------------------------------------- fastText subword embeddings
+@dataclass
+class FastTextConfig:
+    """crates/brain-text/src/embedding/fasttext.rs:FastTextConfig (same fields and defaults)."""
+    min_n: int = 3
+    max_n: int = 6
+    bucket_size: int = 10000
+    dim: int = 100
+
+
+class FastTextEmbedding:
+    """Word vectors composed from character n-grams (Bojanowski et al. 2017), so that out-of-vocabulary
+    words get vectors from the subwords they share with known ones. A word's n-grams are taken from
+    "<word>" for n in [min_n, max_n] and hashed into ``bucket_size`` rows of an n-gram table with 64-bit
+    FNV-1a (the published hash; the same bucket indices as the reference). ``insert_word`` stores the
+    word vector and spreads an equal share of it (vector / (n-grams + 1)) over its n-gram rows;
+    ``get_word_vector`` averages the stored vector (if any) and the word's n-gram rows. The table is a
+    tensor (``device`` selectable) and ``word_vectors`` batches the lookup with one ``embedding_bag``."""
+
+    def __init__(self, config: FastTextConfig | None = None, device=None):
+        self.config = c = config or FastTextConfig()
+        self.word_vectors_: dict[str, torch.Tensor] = {}
+        self.ngram_buckets = torch.zeros(c.bucket_size, c.dim, device=device)
+
+    @staticmethod
+    def compute_ngram_hash(ngram: str, bucket_size: int) -> int:
+        h = 0xCBF29CE484222325
+        for b in ngram.encode("utf-8"):
+            h = ((h ^ b) * 0x100000001B3) & 0xFFFFFFFFFFFFFFFF
+        return h % bucket_size
+
+    def extract_subwords(self, word: str) -> list[str]:
+        chars = "<" + word + ">"
+        return [chars[i:i + n] for n in range(self.config.min_n, self.config.max_n + 1)
+                for i in range(len(chars) - n + 1)]
+
+    def _buckets(self, word: str) -> list[int]:
+        return [self.compute_ngram_hash(s, self.config.bucket_size) for s in self.extract_subwords(word)]
+
+    def insert_word(self, word: str, vector) -> None:
+        v = torch.as_tensor(vector, dtype=torch.float32, device=self.ngram_buckets.device)
+        idx = self._buckets(word)
+        share = v / (len(idx) + 1)
+        self.ngram_buckets.index_add_(0, torch.tensor(idx, dtype=torch.long, device=v.device),
+                                      share.expand(len(idx), -1).contiguous())
+        self.word_vectors_[word] = v
+
+    def get_word_vector(self, word: str) -> torch.Tensor:
+        idx = self._buckets(word)
+        total = torch.zeros(self.config.dim, device=self.ngram_buckets.device)
+        count = 0
+        if word in self.word_vectors_:
+            total += self.word_vectors_[word]
+            count += 1
+        if idx:
+            total += self.ngram_buckets[torch.tensor(idx, dtype=torch.long, device=total.device)].sum(0)
+            count += len(idx)
+        return total / count if count else total
+
+    def word_vectors(self, words: list[str]) -> torch.Tensor:
+        """[len(words), dim] in one embedding_bag over the n-gram rows (stored word vectors added)."""
+        dev = self.ngram_buckets.device
+        flat, offsets, extra, counts = [], [], torch.zeros(len(words), self.config.dim, device=dev), []
+        for i, w in enumerate(words):
+            offsets.append(len(flat))
+            idx = self._buckets(w)
+            flat += idx
+            n = len(idx)
+            if w in self.word_vectors_:
+                extra[i] = self.word_vectors_[w]
+                n += 1
+            counts.append(max(n, 1))
+        sums = torch.nn.functional.embedding_bag(torch.tensor(flat, dtype=torch.long, device=dev),
+                                                 self.ngram_buckets, torch.tensor(offsets, dtype=torch.long, device=dev),
+                                                 mode="sum")
+        return (sums + extra) / torch.tensor(counts, dtype=torch.float32, device=dev)[:, None]
+
+    def most_similar(self, word: str, candidates: list[str], top_k: int) -> list[tuple[str, float]]:
+        target = self.get_word_vector(word)
+        scored = [(c, TextSimilarity.cosine(target.cpu(), self.get_word_vector(c).cpu())) for c in candidates if c != word]
+        scored.sort(key=lambda t: -t[1])
+        return scored[:top_k]

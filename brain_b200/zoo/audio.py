@@ -264,3 +264,59 @@ def chroma(signal: torch.Tensor, sample_rate: int, cfg: STFTConfig | None = None
     out = torch.zeros(n_chroma, mag.shape[-1])
     out.index_add_(0, pc[valid], (mag[valid] ** 2).float())
     return out / out.amax(0, keepdim=True).clamp_min(1e-12)
+
+
+# --------------------------------------------------------------------------- denoising
+def spectral_subtraction(signal: torch.Tensor, cfg: STFTConfig | None = None, oversubtraction: float = 1.0,
+                         spectral_floor: float = 0.01, noise_frames: int = 5) -> torch.Tensor:
+    """Spectral subtraction (Boll 1979; crates/brain-audio/src/denoise.rs:13-62): the noise power per
+    frequency bin is the mean over the first ``noise_frames`` frames; each bin keeps
+    sqrt(max(|X|^2 - oversubtraction * noise, spectral_floor * |X|^2)) with the noisy phase; the inverse
+    STFT restores the original length."""
+    cfg = cfg or STFTConfig()
+    mag, phase = stft(signal, cfg)
+    power = mag ** 2
+    noise = power[..., : min(noise_frames, power.shape[-1])].mean(-1, keepdim=True)
+    clean = torch.sqrt(torch.maximum(power - oversubtraction * noise, spectral_floor * power))
+    return istft(clean, phase, cfg, length=signal.shape[-1])
+
+
+def minimum_statistics_noise(power: torch.Tensor, window: int = 50, smoothing: float = 0.8) -> torch.Tensor:
+    """Stationary noise-floor estimate by minimum statistics (Martin 2001, simplified): the power
+    spectrum [.., bins, frames] is smoothed recursively over time and the noise floor of each frame is
+    the minimum of the smoothed power over the last ``window`` frames."""
+    sm = power.clone()
+    for t in range(1, power.shape[-1]):
+        sm[..., t] = smoothing * sm[..., t - 1] + (1 - smoothing) * power[..., t]
+    pad = torch.nn.functional.pad(sm, (window - 1, 0), value=float("inf"))
+    return -torch.nn.functional.max_pool1d(-pad.reshape(-1, 1, pad.shape[-1]), window, 1).reshape(sm.shape)
+
+
+def wiener_filter(signal: torch.Tensor, cfg: STFTConfig | None = None, noise_frames: int = 5, dd_alpha: float = 0.98,
+                  gain_floor: float = 0.05, min_stats: bool = False) -> torch.Tensor:
+    """Wiener filtering with the decision-directed a-priori SNR estimate (Ephraim and Malah 1984):
+    xi_t = a G_{t-1}^2 |X_{t-1}|^2 / N + (1 - a) max(|X_t|^2 / N - 1, 0), gain G = xi / (1 + xi)
+    (floored). The noise power N comes from the first frames, or from minimum statistics per frame."""
+    cfg = cfg or STFTConfig()
+    mag, phase = stft(signal, cfg)
+    power = mag ** 2
+    if min_stats:
+        noise = minimum_statistics_noise(power).clamp_min(1e-12)
+    else:
+        noise = power[..., : min(noise_frames, power.shape[-1])].mean(-1, keepdim=True).clamp_min(1e-12)
+        noise = noise.expand_as(power)
+    gains = torch.empty_like(power)
+    prev = torch.zeros_like(power[..., 0])
+    for t in range(power.shape[-1]):
+        post = power[..., t] / noise[..., t]
+        xi = dd_alpha * prev / noise[..., t] + (1 - dd_alpha) * (post - 1).clamp_min(0)
+        g = (xi / (1 + xi)).clamp_min(gain_floor)
+        gains[..., t] = g
+        prev = (g ** 2) * power[..., t]
+    return istft(mag * gains, phase, cfg, length=signal.shape[-1])
+
+
+def snr_db(clean: torch.Tensor, estimate: torch.Tensor) -> float:
+    """10 log10(|clean|^2 / |clean - estimate|^2)."""
+    err = (clean - estimate).pow(2).sum().clamp_min(1e-30)
+    return float(10 * torch.log10(clean.pow(2).sum() / err))

@@ -12,6 +12,7 @@ Objectives follow Mnih et al. 2015 (DQN), van Hasselt et al. 2016 (double DQN), 
 """
 from __future__ import annotations
 
+import math
 import random
 from collections import deque
 from dataclasses import dataclass
@@ -422,3 +423,176 @@ class DuelingQNet(Module):
         h = torch.relu(self.body(x))
         adv = self.a(h)
         return self.v(h) + adv - adv.mean(-1, keepdim=True)
+
+
+# --------------------------------------------------------------------------- soft actor-critic
+@dataclass
+class SacConfig:
+    """crates/brain-rl/src/sac/mod.rs:SacConfig (same fields and defaults)."""
+    gamma: float = 0.99
+    tau: float = 0.005
+    alpha: float = 0.2
+    auto_entropy_tuning: bool = True
+    target_entropy: float = -1.0
+    lr: float = 3e-4
+    hidden: int = 64
+
+
+class SacAgent:
+    """Soft actor-critic for continuous actions (Haarnoja et al. 2018): a tanh-squashed Gaussian policy,
+    twin Q critics with Polyak-averaged targets, and a learned temperature alpha (``log_alpha``) driven
+    towards ``target_entropy`` when ``auto_entropy_tuning``. The reference's ``SacAgent`` holds the
+    configuration and ``alpha()``; the update here is the full algorithm."""
+
+    def __init__(self, state_dim: int, action_dim: int, config: SacConfig | None = None, device=None, seed: int = 0):
+        self.config = c = config or SacConfig()
+        self.state_dim, self.action_dim = state_dim, action_dim
+        torch.manual_seed(seed)
+        self.actor = MlpNet(state_dim, 2 * action_dim, c.hidden, device)
+        self.q1 = MlpNet(state_dim + action_dim, 1, c.hidden, device)
+        self.q2 = MlpNet(state_dim + action_dim, 1, c.hidden, device)
+        self.q1_t = MlpNet(state_dim + action_dim, 1, c.hidden, device)
+        self.q2_t = MlpNet(state_dim + action_dim, 1, c.hidden, device)
+        self.q1_t.load_state_dict(self.q1.state_dict())
+        self.q2_t.load_state_dict(self.q2.state_dict())
+        self.log_alpha = torch.tensor(math.log(c.alpha), device=device, requires_grad=True)
+        self.opt_actor = torch.optim.Adam(self.actor.parameters(), lr=c.lr)
+        self.opt_q = torch.optim.Adam(list(self.q1.parameters()) + list(self.q2.parameters()), lr=c.lr)
+        self.opt_alpha = torch.optim.Adam([self.log_alpha], lr=c.lr)
+
+    def alpha(self) -> float:
+        return float(self.log_alpha.exp())
+
+    def _policy(self, s):
+        mu, log_std = self.actor(s).chunk(2, -1)
+        log_std = log_std.clamp(-20, 2)
+        std = log_std.exp()
+        u = mu + std * torch.randn_like(mu)
+        a = torch.tanh(u)
+        # log-density of the squashed sample: Gaussian log-prob minus log|d tanh / du|
+        logp = (-0.5 * ((u - mu) / std) ** 2 - log_std - 0.5 * math.log(2 * math.pi)).sum(-1)
+        logp = logp - torch.log(1 - a.pow(2) + 1e-6).sum(-1)
+        return a, logp, torch.tanh(mu)
+
+    @torch.no_grad()
+    def act(self, state, deterministic: bool = False) -> torch.Tensor:
+        a, _, mean = self._policy(torch.as_tensor(state, dtype=torch.float32)[None])
+        return (mean if deterministic else a)[0]
+
+    def update(self, s, a, r, s2, done) -> dict:
+        """One gradient step on a batch (tensors [B, ...]); returns the losses and alpha."""
+        c = self.config
+        r, done = r.reshape(-1).float(), done.reshape(-1).float()
+        with torch.no_grad():
+            a2, logp2, _ = self._policy(s2)
+            x2 = torch.cat([s2, a2], -1)
+            q_t = torch.minimum(self.q1_t(x2), self.q2_t(x2)).reshape(-1) - self.alpha() * logp2
+            y = r + c.gamma * (1 - done) * q_t
+        x = torch.cat([s, a], -1)
+        q_loss = ((self.q1(x).reshape(-1) - y) ** 2).mean() + ((self.q2(x).reshape(-1) - y) ** 2).mean()
+        self.opt_q.zero_grad()
+        q_loss.backward()
+        self.opt_q.step()
+        an, logp, _ = self._policy(s)
+        xn = torch.cat([s, an], -1)
+        actor_loss = (self.alpha() * logp - torch.minimum(self.q1(xn), self.q2(xn)).reshape(-1)).mean()
+        self.opt_actor.zero_grad()
+        actor_loss.backward()
+        self.opt_actor.step()
+        alpha_loss = torch.zeros(())
+        if c.auto_entropy_tuning:
+            alpha_loss = -(self.log_alpha * (logp.detach() + c.target_entropy)).mean()
+            self.opt_alpha.zero_grad()
+            alpha_loss.backward()
+            self.opt_alpha.step()
+        with torch.no_grad():
+            for net, tgt in ((self.q1, self.q1_t), (self.q2, self.q2_t)):
+                for p, pt in zip(net.parameters(), tgt.parameters()):
+                    pt.mul_(1 - c.tau).add_(p, alpha=c.tau)
+        return {"q_loss": float(q_loss), "actor_loss": float(actor_loss), "alpha_loss": float(alpha_loss),
+                "alpha": self.alpha()}
+
+
+# --------------------------------------------------------------------------- world model and curiosity
+class WorldModel(Module):
+    """Predicts the next state and the reward from (state, action) (crates/brain-rl/src/world_model.rs):
+    h = ReLU(W_e [s, a] + b_e), s' = W_s h + b_s + s (residual), r = w_r . h + b_r, with the reference's
+    deterministic initial weights (sin(0.1337 i), cos(0.7331 i), sin(0.4242 i) times sqrt(2 / in_dim)).
+    Batched and differentiable, so it trains with ``loss`` (state MSE + 0.5 reward MSE)."""
+
+    def __init__(self, state_dim: int, action_dim: int, hidden_dim: int, device=None):
+        super().__init__()
+        self.state_dim, self.action_dim, self.hidden_dim = state_dim, action_dim, hidden_dim
+        in_dim = state_dim + action_dim
+        scale = math.sqrt(2.0 / in_dim)
+        i_e = torch.arange(hidden_dim * in_dim, dtype=torch.float64)
+        i_s = torch.arange(state_dim * hidden_dim, dtype=torch.float64)
+        i_r = torch.arange(hidden_dim, dtype=torch.float64)
+        f = dict(device=device, dtype=torch.float32)
+        self.w_embed = torch.nn.Parameter((torch.sin(i_e * 0.1337) * scale).view(hidden_dim, in_dim).to(**f))
+        self.b_embed = torch.nn.Parameter(torch.zeros(hidden_dim, **f))
+        self.w_state = torch.nn.Parameter((torch.cos(i_s * 0.7331) * scale).view(state_dim, hidden_dim).to(**f))
+        self.b_state = torch.nn.Parameter(torch.zeros(state_dim, **f))
+        self.w_reward = torch.nn.Parameter((torch.sin(i_r * 0.4242) * scale).view(1, hidden_dim).to(**f))
+        self.b_reward = torch.nn.Parameter(torch.zeros(1, **f))
+
+    def predict(self, state, action):
+        """(next state [.., state_dim], reward [..]) for state [.., state_dim], action [.., action_dim]."""
+        state, action = torch.as_tensor(state, dtype=torch.float32), torch.as_tensor(action, dtype=torch.float32)
+        if state.shape[-1] != self.state_dim or action.shape[-1] != self.action_dim:
+            raise ValueError(f"world model expects state [.., {self.state_dim}] and action [.., {self.action_dim}]")
+        h = torch.relu(torch.cat([state, action], -1) @ self.w_embed.t() + self.b_embed)
+        return h @ self.w_state.t() + self.b_state + state, (h @ self.w_reward.t() + self.b_reward).squeeze(-1)
+
+    def loss(self, state, action, target_next_state, target_reward):
+        s_pred, r_pred = self.predict(state, action)
+        target_next_state = torch.as_tensor(target_next_state, dtype=torch.float32)
+        target_reward = torch.as_tensor(target_reward, dtype=torch.float32)
+        return ((s_pred - target_next_state) ** 2).mean(-1).mean() + 0.5 * ((r_pred - target_reward) ** 2).mean()
+
+
+class IntrinsicCuriosityModule(Module):
+    """Curiosity reward from a forward model's error in a learned feature space (Pathak et al. 2017;
+    crates/brain-rl/src/curiosity.rs): phi(s) = LeakyReLU_0.01(W_enc s + b), phi_pred = W_f [phi(s), a] + b,
+    reward = eta / 2 * ||phi_pred - phi(s')||^2, with the reference's initial weights (sin(0.177 i),
+    cos(0.288 i) times sqrt(2 / state_dim)). ``inverse_head`` adds the inverse-dynamics model (predict a
+    from phi(s), phi(s')) whose loss trains the encoder, as in the published method."""
+
+    def __init__(self, state_dim: int, action_dim: int, feature_dim: int, eta: float = 0.1, device=None):
+        super().__init__()
+        self.state_dim, self.action_dim, self.feature_dim, self.eta = state_dim, action_dim, feature_dim, eta
+        scale = math.sqrt(2.0 / state_dim)
+        in_fwd = feature_dim + action_dim
+        f = dict(device=device, dtype=torch.float32)
+        i_e = torch.arange(feature_dim * state_dim, dtype=torch.float64)
+        i_f = torch.arange(feature_dim * in_fwd, dtype=torch.float64)
+        self.w_enc = torch.nn.Parameter((torch.sin(i_e * 0.177) * scale).view(feature_dim, state_dim).to(**f))
+        self.b_enc = torch.nn.Parameter(torch.zeros(feature_dim, **f))
+        self.w_forward = torch.nn.Parameter((torch.cos(i_f * 0.288) * scale).view(feature_dim, in_fwd).to(**f))
+        self.b_forward = torch.nn.Parameter(torch.zeros(feature_dim, **f))
+        self.inverse_head = Linear(2 * feature_dim, action_dim, True, device)
+
+    def encode_state(self, state):
+        state = torch.as_tensor(state, dtype=torch.float32)
+        if state.shape[-1] != self.state_dim:
+            raise ValueError(f"curiosity module expects states [.., {self.state_dim}]")
+        return torch.nn.functional.leaky_relu(state @ self.w_enc.t() + self.b_enc, 0.01)
+
+    def forward_error(self, state, action, next_state):
+        phi = self.encode_state(state)
+        action = torch.as_tensor(action, dtype=torch.float32)
+        if action.shape[-1] != self.action_dim:
+            raise ValueError(f"curiosity module expects actions [.., {self.action_dim}]")
+        pred = torch.cat([phi, action], -1) @ self.w_forward.t() + self.b_forward
+        return ((pred - self.encode_state(next_state)) ** 2).sum(-1)
+
+    def compute_intrinsic_reward(self, state, action, next_state):
+        """eta / 2 * forward-model error (no gradient)."""
+        with torch.no_grad():
+            return 0.5 * self.eta * self.forward_error(state, action, next_state)
+
+    def loss(self, state, action, next_state, beta: float = 0.2):
+        """ICM training loss: (1 - beta) * inverse-dynamics MSE + beta * forward error."""
+        phi, phi2 = self.encode_state(state), self.encode_state(next_state)
+        inv = ((self.inverse_head(torch.cat([phi, phi2], -1)) - torch.as_tensor(action, dtype=torch.float32)) ** 2)
+        return (1 - beta) * inv.mean() + beta * self.forward_error(state, action, next_state).mean()
