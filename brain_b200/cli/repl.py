@@ -269,11 +269,13 @@ def space_command(args: list[str], out=print) -> int:
         if "--teach" in rest:
             f = rest[rest.index("--teach") + 1]
             try:
-                losses = mind.teach_file(f, steps=steps)
+                summary = mind.teach_file(f, steps=steps)
             except OSError as e:
                 out(f"error reading '{f}': {e}")
                 return IO_ERROR
-            out(f"[*] Taught from '{f}': loss {losses[0]:.3f} -> {losses[-1]:.3f}")
+            out(f"[*] Taught from '{f}': {summary.lines_processed} lines, {summary.facts_indexed} facts, "
+                f"{summary.words_learned} new words, {summary.synapses_upgraded} synapses, "
+                f"neural loss {summary.neural_loss:.3f}")
         mind.save(path)
         out(f"[ok] brain saved to '{path}' (BRAIN_BN v1, CRC-32 checked on load)")
         return OK

@@ -325,4 +325,4 @@ def test_brain_mind_learns_and_roundtrips(tmp_path):
     bm.save(p)
     bm2 = BrainMind.load(p)
     assert bm2.talk("hello", max_new=5) == bm.talk("hello", max_new=5)
-    assert bm.talk("what is 2 + 3") == "5"
+    assert bm.talk("what is 2 + 3") == "2 + 3 = 5"
