@@ -227,3 +227,34 @@ def test_device_barrier_gives_up_on_missing_peer():
     outs = run_ranks(_gpu_timeout, 2, env={"NCCL_NVLS_ENABLE": "0"})
     assert outs[0].startswith("timeout"), outs[0]
     assert outs[1] == "no error"
+
+
+def _gpu_ring(rank, world):
+    from brain_b200 import ops
+    from brain_b200.parallel import dist as bdist
+    from brain_b200.parallel.sequence import ring_attention, scatter_sequence
+    bdist.init(timeout_s=120)
+    g = torch.Generator().manual_seed(3)
+    B, S, H, Hkv, D = 1, 2048, 8, 2, 128
+    q, k, v, do = (torch.randn(B, S, h, D, generator=g).cuda().bfloat16() for h in (H, Hkv, Hkv, H))
+    full = [t.clone().requires_grad_(True) for t in (q, k, v)]
+    ops.flash_attention(*full, causal=True).backward(do)
+    loc = [scatter_sequence(t, rank, world).requires_grad_(True) for t in (q, k, v)]
+    o = ring_attention(*loc, rank, world, causal=True)
+    o.backward(scatter_sequence(do, rank, world))
+    ref_o = scatter_sequence(ops.flash_attention(q, k, v, causal=True), rank, world)
+    errs = [float((o.float() - ref_o.float()).abs().max())]
+    for a, b in zip(loc, full):
+        ref = scatter_sequence(b.grad, rank, world).float()
+        errs.append(float((a.grad.float() - ref).norm() / ref.norm()))
+    bdist.shutdown()
+    return errs
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_ring_attention_training_on_gpus_matches_single_gpu():
+    """Context parallelism on 2 GPUs (NCCL point-to-point, tcgen05 flash kernels per block): output and
+    gradients agree with one GPU's flash attention over the whole sequence."""
+    for errs in run_ranks(_gpu_ring, 2, env={"NCCL_NVLS_ENABLE": "0"}):
+        assert errs[0] < 2e-2 and max(errs[1:]) < 2e-2, errs

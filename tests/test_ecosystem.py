@@ -1126,6 +1126,36 @@ def test_ring_and_ulysses_attention_match_full_attention():
         assert res[r][0] < 1e-5 and res[r][1] < 1e-5
 
 
+def _cp_train_rank(rank, world, causal):
+    """Context-parallel training: ring attention forward and backward against full attention."""
+    from brain_b200.models.blocks import sdpa_with_bias
+    from brain_b200.parallel import dist as bdist
+    from brain_b200.parallel.sequence import ring_attention, scatter_sequence
+    bdist.init(device="cpu", timeout_s=60)
+    try:
+        g = torch.Generator().manual_seed(1)
+        B, S, H, Hkv, D = 2, 30, 4, 2, 8
+        q, k, v = (torch.randn(B, S, h, D, generator=g, dtype=torch.float64).requires_grad_(True)
+                   for h in (H, Hkv, Hkv))
+        do = torch.randn(B, S, H, D, generator=g, dtype=torch.float64)
+        sdpa_with_bias(q, k, v, None, causal).double().backward(do)
+        ql, kl, vl = (scatter_sequence(t.detach(), rank, world).requires_grad_(True) for t in (q, k, v))
+        o = ring_attention(ql, kl, vl, rank, world, causal=causal)
+        o.backward(scatter_sequence(do, rank, world))
+        errs = [float((a.grad if hasattr(a, "grad") and a.grad is not None else a) .sub(scatter_sequence(b, rank, world)).abs().max())
+                for a, b in ((ql, q.grad), (kl, k.grad), (vl, v.grad))]
+        return errs
+    finally:
+        bdist.shutdown()
+
+
+@pytest.mark.parametrize("world,causal", [(2, True), (3, True), (3, False)])
+def test_ring_attention_gradients_match_full_attention(world, causal):
+    res = run_ranks(_cp_train_rank, world, causal, timeout=120)
+    for errs in res:
+        assert max(errs) < 1e-5, errs
+
+
 def _pp_rank(rank, world):
     import torch.distributed as dist
     from brain_b200.parallel import dist as bdist
