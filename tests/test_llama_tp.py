@@ -70,3 +70,61 @@ def test_llama_tp_two_gpus(S):
         assert (g == e).all()
         assert worst < 0.06, worst
     assert (outs[0][0] == outs[1][0]).all()
+
+
+def _cfg_wide():
+    from brain_b200.models import LlamaLiteConfig
+    # 16 q / 8 kv heads and 2048 FFN columns: every rank of an 8-way group gets whole heads and 64-row groups
+    return LlamaLiteConfig(vocab_size=1024, hidden_dim=1024, num_layers=2, num_heads=16, num_kv_heads=8, head_dim=128,
+                           intermediate_dim=2048, max_seq_len=256, rope_theta=500000.0)
+
+
+def _tp_worker_n(rank, world, S, new):
+    """Greedy decode at TP=world against the 1-GPU model forward, then the same generation again with
+    random per-rank delays before every decode step (host sleeps and GPU spin kernels of different
+    lengths on each rank), which must reproduce the tokens: the all-reduce slots (sentinel-marked,
+    no flags) may not be reused before every rank consumed them, however the ranks drift."""
+    import random
+    import time
+    from brain_b200.models import LlamaLite
+    from brain_b200.models.llama_tp import LlamaTPServe
+    from brain_b200.parallel import dist as bdist
+    bdist.init(timeout_s=120)
+    try:
+        cfg = _cfg_wide()
+        model = LlamaLite(cfg, device="cuda", seed=5)
+        B = 4
+        prompt = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(13))
+        srv = LlamaTPServe(cfg, max_batch=B, max_len=S + new + 8, block_size=16, init=False).load_from(model)
+        out = srv.generate(prompt, new, use_graph=True)
+        srv.check()
+        worst = _check_greedy(model, out, S)
+        rng = random.Random(1000 + rank)
+        with torch.no_grad():
+            srv.prefill(prompt)
+            srv.step()
+            for _ in range(new - 2):
+                time.sleep(rng.random() * 2e-3)
+                torch.cuda._sleep(rng.randrange(0, 400_000))
+                srv.replay()
+            torch.cuda.synchronize()
+        stressed = srv.hist[:, :S + new].to("cpu", torch.int64)
+        srv.check()
+        srv.close()
+        return out.numpy(), stressed.numpy(), worst
+    finally:
+        bdist.shutdown()
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+@pytest.mark.parametrize("world", [4, 8])
+def test_llama_tp_decode_wide_groups_and_drift(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    outs = run_ranks(_tp_worker_n, world, 32, 16, env={"NCCL_NVLS_ENABLE": "0"}, timeout=300)
+    for g, stressed, worst in outs:
+        assert worst < 0.06, worst
+        assert (g == stressed).all()
+    for g, _, _ in outs[1:]:
+        assert (g == outs[0][0]).all()
