@@ -121,6 +121,29 @@ __global__ void gather_pull_kernel(Peers bufs, int rank, int world, int64_t chun
     reinterpret_cast<int4*>(dst)[i] = reinterpret_cast<const int4*>(src)[i];
 }
 
+// all-gather push: copy bytes [rank*chunk, (rank+1)*chunk) of the local buffer into the same range of every
+// peer's buffer (blockIdx.y selects the peer). Remote stores need no round trip, so four 16-byte vectors
+// per thread are in flight at once. The caller orders it: no peer may still use that range (a barrier, or a
+// protocol step after which nobody reads it) before, and a barrier after it publishes the data.
+__global__ void gather_push_kernel(Peers bufs, int rank, int world, int64_t chunk_bytes, int64_t base_off) {
+  const int j = (rank + 1 + blockIdx.y) % world;
+  if (j == rank) return;
+  const int4* src = reinterpret_cast<const int4*>(reinterpret_cast<const uint8_t*>(bufs.p[rank]) + base_off +
+                                                  rank * chunk_bytes);
+  int4* dst = reinterpret_cast<int4*>(reinterpret_cast<uint8_t*>(bufs.p[j]) + base_off + rank * chunk_bytes);
+  const int64_t nv = chunk_bytes / 16;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  for (; i + 3 * stride < nv; i += 4 * stride) {
+    const int4 a = src[i], b = src[i + stride], c = src[i + 2 * stride], d = src[i + 3 * stride];
+    dst[i] = a;
+    dst[i + stride] = b;
+    dst[i + 2 * stride] = c;
+    dst[i + 3 * stride] = d;
+  }
+  for (; i < nv; i += stride) dst[i] = src[i];
+}
+
 // Fused data-parallel optimizer step over this rank's shard [off, off + n):
 //   g = grad_scale * sum_j grad_j[off + i]       (pull over NVLink, f32 accumulate)
 //   AdamW (decay, moments, bias-corrected update) on the f32 master shard
@@ -265,6 +288,16 @@ BRAIN_API int brain_comm_gather_pull(const int64_t* bufs, int rank, int world, i
   if (world <= 1) return 0;
   dim3 grid(std::max(1, grid_for(chunk_bytes / 16) / (world - 1)), world - 1);
   gather_pull_kernel<<<grid, 256, 0, st>>>(to_peers(bufs, world), rank, world, chunk_bytes, base_off);
+  return (int)cudaGetLastError();
+}
+
+// peer_j[base + rank*chunk, ...) = local[base + rank*chunk, ...) for all j != rank (push; see gather_push_kernel).
+BRAIN_API int brain_comm_gather_push(const int64_t* bufs, int rank, int world, int64_t chunk_bytes, int64_t base_off,
+                                     cudaStream_t st) {
+  if (chunk_bytes % 16 || base_off % 16) return (int)cudaErrorInvalidValue;
+  if (world <= 1) return 0;
+  dim3 grid(std::max(1, grid_for(chunk_bytes / 64) / (world - 1)), world - 1);
+  gather_push_kernel<<<grid, 256, 0, st>>>(to_peers(bufs, world), rank, world, chunk_bytes, base_off);
   return (int)cudaGetLastError();
 }
 

@@ -29,6 +29,7 @@ _native.register({
     "brain_comm_barrier": ("brain_comm", "piiilis"),
     "brain_comm_reduce_pull": ("brain_comm", "pliiplifs"),
     "brain_comm_gather_pull": ("brain_comm", "piills"),
+    "brain_comm_gather_push": ("brain_comm", "piills"),
     "brain_comm_copy": ("brain_comm", "llls"),
     "brain_comm_ddp_step": ("brain_comm", "ppiiillpppffffffffs"),
     "brain_status_comm": ("brain_comm", "pi"),
@@ -108,6 +109,7 @@ class NvlinkComm:
 
     name = "nvlink"
     ONE_SHOT_BYTES = 256 * 1024
+    PUSH_BYTES = 4 << 20  # all-gather shards from this size are pushed (one more barrier, more bytes in flight)
 
     def __init__(self, group=None, timeout_s: float = 60.0):
         _native.load("brain_comm")
@@ -196,8 +198,10 @@ class NvlinkComm:
         mine = sv[self.rank * chunk:(self.rank + 1) * chunk]
         _native.call("brain_comm_reduce_pull", st.ptr_array, self.rank * chunk, self.rank, self.world, mine.data_ptr(),
                      chunk, dcode, scale, _stream())
+        # once this rank has reduced chunk r no peer reads chunk r anywhere: push it straight into every
+        # peer's copy (remote stores), then one barrier publishes all chunks
+        _native.call("brain_comm_gather_push", st.ptr_array, self.rank, self.world, chunk * esz, 0, _stream())
         self.barrier(3)
-        _native.call("brain_comm_gather_pull", st.ptr_array, self.rank, self.world, chunk * esz, 0, _stream())
         t.view(-1).copy_(sv[:n])
         return t
 
@@ -245,7 +249,12 @@ class NvlinkComm:
             if shard.data_ptr() != full.data_ptr() + self.rank * n * esz:
                 full.view(-1)[self.rank * n:(self.rank + 1) * n].copy_(shard.view(-1))
         self.barrier(5)
-        _native.call("brain_comm_gather_pull", buf.peer_array(0), self.rank, self.world, n * esz, off, _stream())
+        if n * esz >= self.PUSH_BYTES:
+            # large shards: remote stores into every peer, then a second barrier publishes them
+            _native.call("brain_comm_gather_push", buf.peer_array(0), self.rank, self.world, n * esz, off, _stream())
+            self.barrier(11)
+        else:
+            _native.call("brain_comm_gather_pull", buf.peer_array(0), self.rank, self.world, n * esz, off, _stream())
         if target is not None:
             full.view(-1).copy_(target)
         return full
