@@ -4,11 +4,11 @@
 // with 1 x 128 activation scales sa [M, K/128] and 128 x 128 weight-block scales sb [N/128, K/128]
 // (f32). These are general f32 scales, not power-of-two MX scales, so the scaling cannot ride on the
 // tensor core's block-scale path: each 128-wide K block is accumulated by tcgen05.mma kind::f8f6f4
-// into one of two TMEM partial buffers, and the epilogue warps promote it in registers
-// (acc += partial * sa * sb) while the tensor core already computes the next block into the other
-// buffer. Roles (6 warps, persistent): warp 0 TMA (SWIZZLE_128B, 128 B = 128 fp8 per row), warp 1
-// single-thread MMA issuer, warps 2..5 promotion + bf16 epilogue (thread = output row). Waits are
-// bounded and report through the status word.
+// into one of four TMEM partial buffers (4 x 128 columns = all of TMEM), and the epilogue warps promote
+// it in registers (acc += partial * sa * sb) while the tensor core runs up to three blocks ahead. Roles (10 warps, persistent): warp 0 TMA (SWIZZLE_128B, 128 B = 128 fp8 per row), warp 1
+// single-thread MMA issuer, warps 2..9 promotion + bf16 epilogue: two warps per TMEM lane quadrant, each
+// thread one output row and 64 of the tile's 128 columns, so a K block's promotion (128 x 128 loads and
+// FMAs) keeps up with its 256-cycle MMA. Waits are bounded and report through the status word.
 //
 // Reference: the FP8E4M3 / FP8E5M2 dtypes are declared without arithmetic
 // (crates/brain-quantization/src/core.rs:19-31); group-wise scaling mirrors BlockQuantizer
@@ -19,10 +19,12 @@ using namespace brain;
 
 namespace {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kPromoThreads = 256;  // warps 2..9
 constexpr int TM = 128, TN = 128, TK = 128;  // tile and scale-block sizes
 constexpr int STAGES = 4;
 constexpr int OP_BYTES = TM * TK;  // 16 KB of fp8 per operand per stage
+constexpr int NPART = 4;            // TMEM partial buffers
 
 struct Fp8Args {
   int M, N, K;
@@ -51,9 +53,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto full = [&](int s) { return bars + 8u * s; };
   auto empty = [&](int s) { return bars + 8u * (STAGES + s); };
   auto pfull = [&](int b) { return bars + 8u * (2 * STAGES + b); };
-  auto pempty = [&](int b) { return bars + 8u * (2 * STAGES + 2 + b); };
-  const uint32_t drain = bars + 8u * (2 * STAGES + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * 2 * OP_BYTES + (2 * STAGES + 5) * 8);
+  auto pempty = [&](int b) { return bars + 8u * (2 * STAGES + NPART + b); };
+  const uint32_t drain = bars + 8u * (2 * STAGES + 2 * NPART);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + STAGES * 2 * OP_BYTES + (2 * STAGES + 2 * NPART + 1) * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
 
@@ -62,16 +64,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(full(s), 1);
       mbar_init(empty(s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NPART; ++b) {
       mbar_init(pfull(b), 1);
-      mbar_init(pempty(b), 128);
+      mbar_init(pempty(b), kPromoThreads);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_alloc(smem_u32(tmem_slot), 128 * NPART);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -110,13 +112,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_f8(TM, TN, 0u, 0u, 0u, 0u);
-      uint32_t it = 0, pb = 0;  // pb: global K-block counter (partial buffer = pb & 1)
+      uint32_t it = 0, pb = 0;  // pb: global K-block counter (partial buffer = pb % NPART)
       bool ok = true, issued = false;
       for (int t = blockIdx.x; t < a.num_tiles && ok; t += gridDim.x) {
         for (int kb = 0; kb < nkb; ++kb, ++it, ++pb) {
           const int s = it % STAGES;
-          const int b = pb & 1;
-          if (!mbar_wait(pempty(b), ((pb >> 1) & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 320, abort_flag) ||
+          const int b = pb % NPART;
+          if (!mbar_wait(pempty(b), ((pb / NPART) & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 320, abort_flag) ||
               !mbar_wait(full(s), (it / STAGES) & 1, BRAIN_ERR_TIMEOUT_FULL, 321, abort_flag)) {
             ok = false;
             break;
@@ -140,7 +142,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
+    constexpr int HC = TN / 2;  // columns per promotion thread
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = q * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     uint32_t pb = 0;
@@ -150,37 +154,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       fp8_tile(t, a.tiles_m, tm, tn);
       const int gm = tm * TM + r;
       const bool row_ok = gm < a.M;
-      float acc[TN];
+      float acc[HC];
 #pragma unroll
-      for (int j = 0; j < TN; ++j) acc[j] = 0.f;
+      for (int j = 0; j < HC; ++j) acc[j] = 0.f;
+      const float* sarow = a.sa + (int64_t)(row_ok ? gm : 0) * a.ksb;
+      const float* sbrow = a.sb + (int64_t)tn * a.ksb;
+      auto scale_of = [&](int kb) { return (row_ok && kb < nkb) ? __ldg(sarow + kb) * __ldg(sbrow + kb) : 0.f; };
+      float s1 = scale_of(0), s2 = scale_of(1), s3 = scale_of(2);  // scales loaded three blocks ahead
       for (int kb = 0; kb < nkb; ++kb, ++pb) {
-        const int b = pb & 1;
-        const float scale = (row_ok ? a.sa[(int64_t)gm * a.ksb + kb] : 0.f) * a.sb[(int64_t)tn * a.ksb + kb];
-        if (!mbar_wait(pfull(b), (pb >> 1) & 1, BRAIN_ERR_TIMEOUT_ACC, 330, abort_flag)) {
+        const int b = pb % NPART;
+        const float scale = s1;
+        s1 = s2;
+        s2 = s3;
+        s3 = scale_of(kb + 3);
+        if (!mbar_wait(pfull(b), (pb / NPART) & 1, BRAIN_ERR_TIMEOUT_ACC, 330, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < TN / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tmem + (uint32_t)(b * 128 + c * 32) + lane_addr, v);
-          tc_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[c * 32 + j] += scale * __uint_as_float(v[j]);
-        }
+        uint32_t v0[32], v1[32];
+        const uint32_t ta = tmem + (uint32_t)(b * 128 + half * HC) + lane_addr;
+        tmem_ld32(ta, v0);
+        tmem_ld32(ta + 32, v1);
+        tc_wait_ld();
         tc_fence_before();
-        mbar_arrive(pempty(b));
+        mbar_arrive(pempty(b));  // the partial is in registers: the tensor core may refill the buffer
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          acc[j] = fmaf(scale, __uint_as_float(v0[j]), acc[j]);
+          acc[32 + j] = fmaf(scale, __uint_as_float(v1[j]), acc[32 + j]);
+        }
       }
       if (!ok) break;
       if (row_ok) {
-        const int n0 = tn * TN;
+        const int n0 = tn * TN + half * HC;
         __nv_bfloat16* crow = a.C + (int64_t)gm * a.ldc;
-        if (n0 + TN <= a.N) {
+        if (n0 + HC <= a.N) {
           if (a.R) {
             const __nv_bfloat16* rrow = a.R + (int64_t)gm * a.ldr + n0;
 #pragma unroll
-            for (int j = 0; j < TN; j += 8) {
+            for (int j = 0; j < HC; j += 8) {
               float rv[8];
               load8(rrow + j, rv);
 #pragma unroll
@@ -188,10 +201,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
 #pragma unroll
-          for (int j = 0; j < TN; j += 8) store8(crow + n0 + j, acc + j);
+          for (int j = 0; j < HC; j += 8) store8(crow + n0 + j, acc + j);
         } else {
 #pragma unroll
-          for (int j = 0; j < TN; ++j)
+          for (int j = 0; j < HC; ++j)
             if (n0 + j < a.N)
               crow[n0 + j] = __float2bfloat16_rn(acc[j] + (a.R ? __bfloat162float(a.R[(int64_t)gm * a.ldr + n0 + j]) : 0.f));
         }
@@ -202,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 128 * NPART);
   }
 }
 
@@ -259,7 +272,7 @@ BRAIN_API int brain_fp8_gemm(const void* A, int64_t lda, const void* B, int64_t 
   a.ldc = ldc;
   a.R = reinterpret_cast<const __nv_bfloat16*>(R);
   a.ldr = ldr;
-  const int smem = STAGES * 2 * OP_BYTES + (2 * STAGES + 5) * 8 + 16 + 1024;
+  const int smem = STAGES * 2 * OP_BYTES + (2 * STAGES + 2 * NPART + 1) * 8 + 16 + 1024;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
