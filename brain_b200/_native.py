@@ -33,6 +33,8 @@ SIGNATURES: dict[str, tuple[str, str]] = {
     "brain_status_gemm": ("brain_kernels", "pi"),
     "brain_gemm_set_pair_mode": ("brain_kernels", "i"),
     "brain_gemm_bf16_rope": ("brain_kernels", "plplpliiipiiiis"),
+    "brain_gemm_bf16_ws": ("brain_kernels", "pliplipliiiififpplpls"),
+    "brain_gemm_splitk_plan": ("brain_kernels", "iiip"),
 }
 
 _lock = threading.Lock()
@@ -98,7 +100,7 @@ def stream_ptr(device: torch.device | None = None) -> int:
 # library's launches inside a timed region (``launch_counter``).
 KERNELS_PER_CALL = {
     "brain_norm_bwd": 2, "brain_attn_bwd": 4, "brain_sumsq": 2, "brain_error_string": 0,
-    "brain_norm_bwd_partials": 0,
+    "brain_norm_bwd_partials": 0, "brain_gemm_splitk_plan": 0, "brain_gemm_bf16_ws": 2,
 }
 _launches = {"on": False, "n": 0}
 

@@ -497,28 +497,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// delta[b, h, i] = sum_d dO * O   (one warp per row, 16-byte loads)
+// delta[b, h, i] = sum_d dO * O: L = D / 8 lanes per row (16-byte loads), 32 / L rows per warp, so short
+// rows (d 64) keep every lane busy.
 __global__ void bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, int64_t ob, int64_t os, int64_t oh,
                                  const __nv_bfloat16* __restrict__ dO, int64_t db, int64_t ds, int64_t dh,
                                  float* __restrict__ delta, int B, int H, int S, int D) {
-  const int64_t rowid = (int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int L = D / 8;               // lanes per row (D = 64 -> 8, D = 128 -> 16)
+  const int rows_per_warp = 32 / L;
   const int lane = threadIdx.x % 32;
-  if (rowid >= (int64_t)B * H * S) return;
-  const int i = (int)(rowid % S);
-  const int bh = (int)(rowid / S);
-  const int b = bh / H, h = bh % H;
-  const __nv_bfloat16* po = o + b * ob + h * oh + (int64_t)i * os;
-  const __nv_bfloat16* pd = dO + b * db + h * dh + (int64_t)i * ds;
+  const int64_t rowid = ((int64_t)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32) * rows_per_warp + lane / L;
+  const int sub = lane % L;
   float acc = 0.f;
-  for (int d = lane * 8; d < D; d += 256) {
+  if (rowid < (int64_t)B * H * S) {
+    const int i = (int)(rowid % S);
+    const int bh = (int)(rowid / S);
+    const int b = bh / H, h = bh % H;
     float x[8], y[8];
-    load8(po + d, x);
-    load8(pd + d, y);
+    load8(o + b * ob + h * oh + (int64_t)i * os + sub * 8, x);
+    load8(dO + b * db + h * dh + (int64_t)i * ds + sub * 8, y);
 #pragma unroll
     for (int k = 0; k < 8; ++k) acc += x[k] * y[k];
   }
-  acc = warp_sum(acc);
-  if (lane == 0) delta[rowid] = acc;
+  for (int off = L / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (sub == 0 && rowid < (int64_t)B * H * S) delta[rowid] = acc;
 }
 
 bool map4(CUtensorMap* m, const void* base, int D, int S, int H, int B, int64_t ss, int64_t sh, int64_t sb,
@@ -573,7 +574,8 @@ int bwd_tc(const void* q, const void* k, const void* v, const int64_t* s9, const
   // delta = rowsum(dO * O)
   {
     const int64_t rows = (int64_t)B * Hq * Sq;
-    bwd_delta_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, st>>>(
+    const int64_t rows_per_block = 8 * (32 / (D / 8));
+    bwd_delta_kernel<<<(unsigned)((rows + rows_per_block - 1) / rows_per_block), 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(o), ostr[0], ostr[1], ostr[2],
         reinterpret_cast<const __nv_bfloat16*>(dout), dostr[0], dostr[1], dostr[2], delta, B, Hq, Sq, D);
   }

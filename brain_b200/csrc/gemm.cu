@@ -59,6 +59,10 @@ struct GemmArgs {
   // (cos | sin halves). TMA-store epilogue only.
   const float* rope_cs;
   int rope_cols, rope_hd, rope_S, rope_off;
+  // Split-K (CTA-pair kernel, TMA-store epilogue): work unit t covers output tile t % (tiles_m * tiles_n)
+  // over k-blocks [s * kb_split, (s + 1) * kb_split) with s = t / (tiles_m * tiles_n); its raw f32 sums go
+  // to rows [s * split_rows, ...) of the workspace C, and a second kernel adds the slices in order.
+  int splits, kb_split, split_rows;
 };
 
 template <int BN, int STAGES>
@@ -79,6 +83,22 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
   int r = t - group * group_size;
   tm = first_m + r % gm;
   tn = r / gm;
+}
+
+// Work unit t -> output tile coordinates, k-block range and split index (split-K or a plain tile).
+__device__ __forceinline__ void unit_coords(const GemmArgs& a, int t, int num_kb, int& tm, int& tn, int& kb0,
+                                            int& kb1, int& split) {
+  split = 0;
+  kb0 = 0;
+  kb1 = num_kb;
+  if (a.splits > 1) {
+    const int per = a.tiles_m * a.tiles_n;
+    split = t / per;
+    t -= split * per;
+    kb0 = split * a.kb_split;
+    kb1 = min(num_kb, kb0 + a.kb_split);
+  }
+  tile_coords(t, a.tiles_m, a.tiles_n, tm, tn);
 }
 
 __device__ __forceinline__ void store_chunk_at(const GemmArgs& args, int gm, int gn0, const uint32_t* r, void* cbase,
@@ -473,10 +493,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int t = pid; t < args.num_tiles && ok; t += npairs) {
-        int tm, tn;
-        tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+        int tm, tn, kb0, kb1, split;
+        unit_coords(args, t, num_kb, tm, tn, kb0, kb1, split);
         const int m0 = tm * 256 + (int)cta * 128, n0 = tn * TN + (int)cta * 128;
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % ST;
           const uint32_t round = it / ST;
           if (!mbar_wait(empty_bar(s), (round & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 40, abort_flag)) {
@@ -527,7 +547,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * TN);
-        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+        int tm_, tn_, kb0, kb1, split_;
+        unit_coords(args, t, num_kb, tm_, tn_, kb0, kb1, split_);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % ST;
           if (!mbar_wait(full_bar(s), (it / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 51, abort_flag)) {
             ok = false;
@@ -542,7 +564,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                   : smem_desc_sw128(sa + kk * 32, 16, 1024);
             uint64_t bdesc = B_MN ? smem_desc_sw128(sb + kk * 2048, 64 * BK * 2, 1024)
                                   : smem_desc_sw128(sb + kk * 32, 16, 1024);
-            tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+            tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           issued = true;
           tc_commit_pair(empty_bar(s));
@@ -571,8 +593,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       const uint32_t acc_round = (uint32_t)(local >> 1);
       if (!mbar_wait(tfull_bar(acc), acc_round & 1, BRAIN_ERR_TIMEOUT_ACC, 60, abort_flag)) break;
       tc_fence_after();
-      int tm, tn;
-      tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+      int tm, tn, kb0_, kb1_, split;
+      unit_coords(args, t, num_kb, tm, tn, kb0_, kb1_, split);
       const int gm = tm * 256 + row_in_tile;
       const int n0 = tn * TN;
       const bool row_ok = gm < args.M;
@@ -582,7 +604,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // -> one TMA store of the warp's 32 rows; the two buffers alternate, and a buffer is rewritten
         // only after the store issued from it two units earlier has read it.
         const int cols = args.c_f32 ? 32 : 64;
-        const int row0 = tm * 256 + (int)cta * 128 + q * 32;
+        const int row0 = split * args.split_rows + tm * 256 + (int)cta * 128 + q * 32;
         const int rpos = args.rope_cs && row_ok ? gm % args.rope_S + args.rope_off : 0;
         // RoPE: rotate 32 pairs (x1 at TMEM column c1, x2 at c2; pair index j0 in the head) into bf16 words
         auto rope32 = [&](int c1, int c2, int j0, uint32_t* w1, uint32_t* w2) {
@@ -862,6 +884,43 @@ __global__ void gemm_simt_kernel(const __nv_bfloat16* A, int64_t lda, int a_mn, 
   }
 }
 
+// Split-K epilogue: C = alpha * sum_s ws[s] (+ bias) (+ R) (+ beta * C), the slices added in index order
+// (deterministic). ws slices are f32 [rows >= M, N] with row stride N; four columns per thread.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int64_t slice, int M, int N, void* C,
+                                     int64_t ldc, int c_f32, float alpha, int accumulate, float beta,
+                                     const __nv_bfloat16* __restrict__ bias, const __nv_bfloat16* __restrict__ R,
+                                     int64_t ldr) {
+  const int n4 = N / 4;
+  const int64_t total = (int64_t)M * n4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / n4), n = (int)(i % n4) * 4;
+    const float* src = ws + (int64_t)m * N + n;
+    float4 acc = *reinterpret_cast<const float4*>(src);
+    for (int sp = 1; sp < splits; ++sp) {
+      const float4 v = *reinterpret_cast<const float4*>(src + sp * slice);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    float v[4] = {acc.x * alpha, acc.y * alpha, acc.z * alpha, acc.w * alpha};
+    if (bias) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] += __bfloat162float(bias[n + j]);
+    }
+    if (R) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] += __bfloat162float(R[(int64_t)m * ldr + n + j]);
+    }
+    if (c_f32) {
+      float* cp = reinterpret_cast<float*>(C) + (int64_t)m * ldc + n;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cp[j] = v[j] + (accumulate ? beta * cp[j] : 0.f);
+    } else {
+      __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(C) + (int64_t)m * ldc + n;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) cp[j] = __float2bfloat16_rn(v[j] + (accumulate ? beta * __bfloat162float(cp[j]) : 0.f));
+    }
+  }
+}
+
 }  // namespace
 
 BRAIN_STATUS_READER(gemm)
@@ -877,6 +936,43 @@ BRAIN_API int brain_gemm_set_pair_mode(int mode) {
   return old;
 }
 
+
+// Split-K plan for the CTA-pair kernel: returns the number of K slices (1 = no split) and the k-blocks per
+// slice. Splitting pays when the output has fewer 256 x 256 tiles than there are SM pairs (weight gradients
+// of narrow layers: dW [768, 768] over 12k tokens has 9 tiles for 74 pairs). The cost model counts waves of
+// k-block steps (about 0.42 us per 256 x 256 x 64 step on one pair) plus the reduction's launch and its f32
+// traffic (each slice written once and read once).
+BRAIN_API int brain_gemm_splitk_plan(int M, int N, int K, int* kb_split) {
+  const int pairs = brain_host::num_sms() / 2;
+  const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  const int num_kb = (K + BK - 1) / BK;
+  if (kb_split) *kb_split = num_kb;
+  if (M < 256 || N < 256 || N % 4 != 0 || tiles >= pairs || num_kb < 16) return 1;
+  const double step_us = 0.42;
+  double best = (double)num_kb * step_us;
+  int best_s = 1;
+  for (int sp = 2; sp <= 16 && num_kb / sp >= 4; ++sp) {
+    const int per = (num_kb + sp - 1) / sp;
+    const int used = (num_kb + per - 1) / per;  // slices actually non-empty
+    const int waves = (tiles * used + pairs - 1) / pairs;
+    const double red_us = 3.0 + 2.0 * used * (double)((M + 255) / 256 * 256) * N * 4 / 6.0e6;
+    const double cost = waves * per * step_us + red_us;
+    if (cost < best * 0.9) {
+      best = cost;
+      best_s = used;
+      if (kb_split) *kb_split = per;
+    }
+  }
+  if (best_s == 1 && kb_split) *kb_split = num_kb;
+  return best_s;
+}
+
+namespace {
+int gemm_bf16_impl(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn, void* C, int64_t ldc,
+                   int c_f32, int M, int N, int K, float alpha, int accumulate, float beta, const void* bias,
+                   const void* R, int64_t ldr, int force_simt, float* ws, int64_t ws_elems, cudaStream_t stream);
+}  // namespace
+
 // C = alpha * op(A) op(B) (+ beta*C if accumulate) (+ bias) (+ R).
 //   a_mn = 0: A is [M,K] with row stride lda; a_mn = 1: A is [K,M] with row stride lda.
 //   b_mn = 0: B is [N,K] with row stride ldb; b_mn = 1: B is [K,N] with row stride ldb.
@@ -884,6 +980,24 @@ BRAIN_API int brain_gemm_set_pair_mode(int mode) {
 BRAIN_API int brain_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn, void* C,
                               int64_t ldc, int c_f32, int M, int N, int K, float alpha, int accumulate, float beta,
                               const void* bias, const void* R, int64_t ldr, int force_simt, cudaStream_t stream) {
+  return gemm_bf16_impl(A, lda, a_mn, B, ldb, b_mn, C, ldc, c_f32, M, N, K, alpha, accumulate, beta, bias, R, ldr,
+                        force_simt, nullptr, 0, stream);
+}
+
+// brain_gemm_bf16 with an f32 split-K workspace of ws_elems elements (at least splits * round_up(M, 256) * N
+// for the plan of brain_gemm_splitk_plan); without room it runs unsplit.
+BRAIN_API int brain_gemm_bf16_ws(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn, void* C,
+                                 int64_t ldc, int c_f32, int M, int N, int K, float alpha, int accumulate, float beta,
+                                 const void* bias, const void* R, int64_t ldr, float* ws, int64_t ws_elems,
+                                 cudaStream_t stream) {
+  return gemm_bf16_impl(A, lda, a_mn, B, ldb, b_mn, C, ldc, c_f32, M, N, K, alpha, accumulate, beta, bias, R, ldr, 0,
+                        ws, ws_elems, stream);
+}
+
+namespace {
+int gemm_bf16_impl(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn, void* C, int64_t ldc,
+                   int c_f32, int M, int N, int K, float alpha, int accumulate, float beta, const void* bias,
+                   const void* R, int64_t ldr, int force_simt, float* ws, int64_t ws_elems, cudaStream_t stream) {
   if (M <= 0 || N <= 0) return 0;
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K;
@@ -920,6 +1034,33 @@ BRAIN_API int brain_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
                                   CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2));
     if (!ok) return (int)cudaErrorInvalidValue;
     CUtensorMap tc{};
+    int kbs = 0;
+    const int splits = ws ? brain_gemm_splitk_plan(M, N, K, &kbs) : 1;
+    const int rows = a.tiles_m * 256;
+    if (splits > 1 && (int64_t)splits * rows * N <= ws_elems && (reinterpret_cast<uintptr_t>(ws) & 15) == 0) {
+      // raw partial sums into the workspace slices, then alpha / bias / residual / beta * C in the reduction
+      GemmArgs p = a;
+      p.C = ws; p.ldc = N; p.c_f32 = 1; p.accumulate = 0; p.alpha = 1.f; p.beta = 0.f;
+      p.bias = nullptr; p.R = nullptr;
+      p.M = splits * rows;  // the map spans every slice
+      if (output_map(&tc, p)) {
+        p.M = M;
+        p.tma_store = 1;
+        p.splits = splits; p.kb_split = kbs; p.split_rows = rows;
+        p.num_tiles = a.num_tiles * splits;
+        int rc;
+        if (a_mn == 0 && b_mn == 0) rc = launch_tc2<0, 0>(ta, tb, tc, p, stream);
+        else if (a_mn == 0 && b_mn == 1) rc = launch_tc2<0, 1>(ta, tb, tc, p, stream);
+        else if (a_mn == 1 && b_mn == 0) rc = launch_tc2<1, 0>(ta, tb, tc, p, stream);
+        else rc = launch_tc2<1, 1>(ta, tb, tc, p, stream);
+        if (rc) return rc;
+        const int64_t work = (int64_t)M * (N / 4);
+        const int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)brain_host::num_sms() * 8);
+        splitk_reduce_kernel<<<grid, 256, 0, stream>>>(ws, splits, (int64_t)rows * N, M, N, C, ldc, c_f32, alpha,
+                                                       accumulate, beta, a.bias, a.R, ldr);
+        return (int)cudaGetLastError();
+      }
+    }
     a.tma_store = output_map(&tc, a) ? 1 : 0;
     if (a_mn == 0 && b_mn == 0) return launch_tc2<0, 0>(ta, tb, tc, a, stream);
     if (a_mn == 0 && b_mn == 1) return launch_tc2<0, 1>(ta, tb, tc, a, stream);
@@ -951,6 +1092,7 @@ BRAIN_API int brain_gemm_bf16(const void* A, int64_t lda, int a_mn, const void* 
   }
 #undef BRAIN_GEMM_CASE
 }
+}  // namespace
 
 // C [M, N] bf16 = A [M, K] B [N, K]^T with NeoX RoPE applied to the first rope_cols columns in the
 // epilogue (a fused QKV projection: q and k heads rotated, v heads stored as they are). Row r is token

@@ -289,6 +289,97 @@ __global__ void __launch_bounds__(1024, 1)
   }
 }
 
+// Backward for short rows (D <= 1024, e.g. 768 for ViT-B): one warp per row with V 8-element vectors per
+// lane, so a block of 8 warps works on 8 rows at once with shuffle-only reductions (the block-per-row
+// kernel above gets only D/8 threads per block at these widths). Each warp accumulates dgamma/dbeta for its
+// rows; the block adds its 8 warps' sums in a fixed order into one partial row (deterministic).
+template <bool LAYERNORM, int V>
+__global__ void __launch_bounds__(256)
+    norm_bwd_warp_kernel(const __nv_bfloat16* __restrict__ dy, int64_t lddy, const __nv_bfloat16* __restrict__ x,
+                         int64_t ldx, const __nv_bfloat16* __restrict__ w, const float* __restrict__ mean_in,
+                         const float* __restrict__ rstd_in, __nv_bfloat16* __restrict__ dx, int64_t lddx,
+                         const __nv_bfloat16* __restrict__ dres, int64_t lddres, float* __restrict__ dw_part,
+                         float* __restrict__ db_part, int M, int D) {
+  extern __shared__ float wsum[];  // [8 warps][2][D]
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int nvec = D / 8;
+  float wv[V][8], dwacc[V][8], dbacc[V][8];
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) wv[v][j] = dwacc[v][j] = dbacc[v][j] = 0.f;
+    const int vi = lane + 32 * v;
+    if (vi < nvec) load8(w + vi * 8, wv[v]);
+  }
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < M; row += (int64_t)gridDim.x * 8) {
+    const float rstd = rstd_in[row];
+    const float mean = LAYERNORM ? mean_in[row] : 0.f;
+    float xh[V][8], g[V][8];
+    float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int vi = lane + 32 * v;
+      float xv[8], dv[8];
+      if (vi < nvec) {
+        load8(x + row * ldx + vi * 8, xv);
+        load8(dy + row * lddy + vi * 8, dv);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xv[j] = dv[j] = 0.f;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        xh[v][j] = (xv[j] - mean) * rstd;
+        g[v][j] = dv[j] * wv[v][j];
+        dwacc[v][j] += dv[j] * xh[v][j];
+        if (LAYERNORM) dbacc[v][j] += dv[j];
+        s1 += g[v][j];
+        s2 += g[v][j] * xh[v][j];
+      }
+    }
+    const float c2 = warp_sum(s2) / D;
+    const float c1 = LAYERNORM ? warp_sum(s1) / D : 0.f;
+#pragma unroll
+    for (int v = 0; v < V; ++v) {
+      const int vi = lane + 32 * v;
+      if (vi >= nvec) continue;
+      float o[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = rstd * (g[v][j] - c1 - xh[v][j] * c2);
+      if (dres) {
+        float r[8];
+        load8(dres + row * lddres + vi * 8, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o[j] += r[j];
+      }
+      store8(dx + row * lddx + vi * 8, o);
+    }
+  }
+  float* mine = wsum + warp * 2 * D;
+#pragma unroll
+  for (int v = 0; v < V; ++v) {
+    const int vi = lane + 32 * v;
+    if (vi < nvec) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        mine[vi * 8 + j] = dwacc[v][j];
+        mine[D + vi * 8 + j] = dbacc[v][j];
+      }
+    }
+  }
+  __syncthreads();
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float sw = 0.f, sb = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      sw += wsum[k * 2 * D + d];
+      sb += wsum[k * 2 * D + D + d];
+    }
+    dw_part[(int64_t)blockIdx.x * D + d] = sw;
+    if (LAYERNORM && db_part) db_part[(int64_t)blockIdx.x * D + d] = sb;
+  }
+}
+
 // out[d] (+)= sum_p part[p, d] with 8 row slices per column (block 32 x 8): each thread sums every
 // 8th partial row of one column, then the 8 slice sums are added in a fixed order (deterministic).
 __global__ void colsum8_kernel(const float* __restrict__ part, int P, int D, void* out, int out_f32, int accumulate) {
@@ -383,6 +474,28 @@ BRAIN_API int brain_norm_bwd(int kind, const void* dy, int64_t lddy, const void*
   auto W = reinterpret_cast<const __nv_bfloat16*>(w);
   auto DX = reinterpret_cast<__nv_bfloat16*>(dx);
   auto DR = reinterpret_cast<const __nv_bfloat16*>(dres);
+  if (D <= 1024) {  // short rows: one warp per row
+    const size_t sm = (size_t)8 * 2 * D * sizeof(float);
+    const int vecs = (D / 8 + 31) / 32;
+#define BRAIN_NORM_WARP(VV)                                                                                         \
+  do {                                                                                                              \
+    cudaFuncSetAttribute(norm_bwd_warp_kernel<false, VV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);   \
+    cudaFuncSetAttribute(norm_bwd_warp_kernel<true, VV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);    \
+    if (kind == 0)                                                                                                  \
+      norm_bwd_warp_kernel<false, VV><<<P, 256, sm, st>>>(DY, lddy, X, ldx, W, mean_in, rstd_in, DX, lddx, DR,      \
+                                                         lddres, dwp, nullptr, M, D);                              \
+    else                                                                                                            \
+      norm_bwd_warp_kernel<true, VV><<<P, 256, sm, st>>>(DY, lddy, X, ldx, W, mean_in, rstd_in, DX, lddx, DR,       \
+                                                        lddres, dwp, dbp, M, D);                                   \
+  } while (0)
+    if (vecs <= 1) BRAIN_NORM_WARP(1);
+    else if (vecs <= 2) BRAIN_NORM_WARP(2);
+    else BRAIN_NORM_WARP(4);
+#undef BRAIN_NORM_WARP
+    colsum8_kernel<<<(D + 31) / 32, dim3(32, 8), 0, st>>>(dwp, P, D, dw, dw_f32, accumulate);
+    if (kind == 1 && db) colsum8_kernel<<<(D + 31) / 32, dim3(32, 8), 0, st>>>(dbp, P, D, db, dw_f32, accumulate);
+    return (int)cudaGetLastError();
+  }
   if (D / 8 <= 1024) {  // one vector per thread, next-row prefetch
     const int T1 = ((D / 8 + 31) / 32) * 32;
     if (kind == 0)

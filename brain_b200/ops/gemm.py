@@ -11,6 +11,8 @@ CUDA tensors always take the native kernel.
 """
 from __future__ import annotations
 
+import functools
+
 import torch
 
 from .. import _native
@@ -69,6 +71,24 @@ def gemm(
         residual = _row_major(residual)
         if residual.dtype != torch.bfloat16 or residual.shape != (M, N):
             raise TypeError("residual must be bfloat16 [M, N]")
+    splits = _splitk_plan(M, N, K) if (M >= 256 and N >= 256 and not force_simt) else 1
+    if splits > 1:
+        # few output tiles over a long K (weight gradients of narrow layers): K slices on separate SM
+        # pairs into an f32 workspace, added in order by a second kernel
+        ws = torch.empty(splits * ((M + 255) // 256) * 256 * N, device=a.device, dtype=torch.float32)
+        _native.call(
+            "brain_gemm_bf16_ws",
+            a.data_ptr(), a.stride(0), int(trans_a),
+            b.data_ptr(), b.stride(0), int(not trans_b),
+            out.data_ptr(), out.stride(0), int(out.dtype == torch.float32),
+            M, N, K, float(alpha), int(accumulate), float(beta),
+            bias.data_ptr() if bias is not None else None,
+            residual.data_ptr() if residual is not None else None,
+            residual.stride(0) if residual is not None else 0,
+            ws.data_ptr(), ws.numel(),
+            _native.stream_ptr(a.device),
+        )
+        return out
     _native.call(
         "brain_gemm_bf16",
         a.data_ptr(), a.stride(0), int(trans_a),
@@ -85,6 +105,27 @@ def gemm(
 
 
 _NOT_SUPPORTED = 801  # cudaErrorNotSupported
+_SPLIT_ON = {"on": True}
+
+
+@functools.lru_cache(maxsize=4096)
+def _plan(M: int, N: int, K: int) -> int:
+    return int(_native.fn("brain_gemm_splitk_plan")(M, N, K, None))
+
+
+def _splitk_plan(M: int, N: int, K: int) -> int:
+    """Number of K slices the CTA-pair kernel uses for this shape (1: no split). Only shapes with fewer
+    256 x 256 output tiles than SM pairs and at least 16 k-blocks are split."""
+    if not _SPLIT_ON["on"] or K < 1024:
+        return 1
+    return _plan(M, N, K)
+
+
+def set_splitk(on: bool) -> bool:
+    """Enable or disable split-K for under-filled GEMMs (tests compare both); returns the previous state."""
+    old = _SPLIT_ON["on"]
+    _SPLIT_ON["on"] = bool(on)
+    return old
 
 
 def gemm_rope(x: torch.Tensor, w: torch.Tensor, table: torch.Tensor, rope_cols: int, head_dim: int, seq_len: int,

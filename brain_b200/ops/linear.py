@@ -34,7 +34,7 @@ def _wgrad(dy2, x2, w):
 def _bgrad(dy2, b):
     if b is None:
         return None
-    g = dy2.float().sum(0)
+    g = dy2.sum(0, dtype=torch.float32)  # f32 accumulation without an f32 copy of dy
     if has_main_grad(b):
         if main_grad_beta(b) == 0.0:
             b.main_grad.copy_(g.to(b.main_grad.dtype))

@@ -149,3 +149,34 @@ def test_gemm_rejects_operand_on_other_device():
     b = _mk((64, 128), "cpu", 41)
     with pytest.raises(ValueError):
         gemm(a, b)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ta,tb", [(True, False), (False, True), (False, False)])
+@pytest.mark.parametrize("shape", [(768, 768, 12608), (2304, 768, 8192), (300, 520, 6144)])
+def test_gemm_splitk_matches_oracle(ta, tb, shape):
+    """Under-filled GEMMs (fewer 256 x 256 tiles than SM pairs, long K) take the split-K path: each
+    K slice on its own SM pair into an f32 workspace, then an ordered reduction with the epilogue."""
+    from brain_b200.ops.gemm import _splitk_plan
+    from brain_b200 import _native
+    M, N, K = shape
+    assert _splitk_plan(M, N, K) > 1
+    a = _mk((K, M) if ta else (M, K), "cuda", 31)
+    b = _mk((N, K) if tb else (K, N), "cuda", 32)
+    ref = _ref(a, b, ta, tb)
+    tol = dict(rtol=2e-3, atol=2e-3 * K ** 0.5)
+    c = gemm(a, b, ta, tb, out_dtype=torch.float32)
+    torch.testing.assert_close(c, ref, **tol)
+    acc = torch.randn(M, N, device="cuda")  # main-grad style accumulation into f32
+    acc0 = acc.clone()
+    gemm(a, b, ta, tb, out=acc, beta=1.0)
+    torch.testing.assert_close(acc, acc0 + ref, **tol)
+    bias = _mk((N,), "cuda", 33)
+    res = _mk((M, N), "cuda", 34)
+    y = gemm(a, b, ta, tb, bias=bias, residual=res, alpha=0.25)
+    torch.testing.assert_close(y.float(), _ref(a, b, ta, tb, alpha=0.25, bias=bias, residual=res), rtol=1e-2,
+                               atol=0.25 * 2e-3 * K ** 0.5 + 0.1)
+    c2 = gemm(a, b, ta, tb, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(c, c2)  # the slices are added in a fixed order
+    assert _native.status("gemm")[0] == 0
