@@ -101,6 +101,7 @@ def stream_ptr(device: torch.device | None = None) -> int:
 KERNELS_PER_CALL = {
     "brain_norm_bwd": 2, "brain_attn_bwd": 4, "brain_sumsq": 2, "brain_error_string": 0,
     "brain_norm_bwd_partials": 0, "brain_gemm_splitk_plan": 0, "brain_gemm_bf16_ws": 2,
+    "brain_colsum_partials": 0, "brain_colsum_bf16": 2,
 }
 _launches = {"on": False, "n": 0}
 

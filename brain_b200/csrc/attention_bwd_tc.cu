@@ -50,8 +50,9 @@ struct BwdLayout {
   static constexpr int STAGES = D == 64 ? 4 : 3;
   static constexpr int A_BYTES = NSUB * SUB128;  // one row operand [128, D]
   static constexpr int B_BYTES = NSUB * SUB64;   // one streamed operand [64, D]
-  static constexpr int A_OFF = 0;                // A1, A2
-  static constexpr int B_OFF = 2 * A_BYTES;      // stages of (B1, B2)
+  static constexpr int ABUF = D == 64 ? 2 : 1;   // row-operand buffers: the next item's load overlaps this one
+  static constexpr int A_OFF = 0;                // ABUF x (A1, A2)
+  static constexpr int B_OFF = ABUF * 2 * A_BYTES;  // stages of (B1, B2)
   static constexpr int STAGE_BYTES = 2 * B_BYTES;
   static constexpr int NC = MODE == DKDV ? 2 : 1;  // C tiles (P^T, dS^T) or (dS)
   static constexpr int C_OFF = B_OFF + STAGES * STAGE_BYTES;
@@ -62,8 +63,9 @@ struct BwdLayout {
   // work on block i); the accumulators follow them
   static constexpr int NBUF = 2;
   static constexpr int ACC = NBUF * 128;  // first accumulator column
-  // a_full, b_full[S], b_empty[S], sd_full[3], sd_free[3], c_full[2], c_free[2], acc_done, drain
-  static constexpr int NBAR = 1 + 2 * STAGES + 6 + 6;
+  // a_full[ABUF], a_empty[ABUF], b_full[S], b_empty[S], sd_full[3], sd_free[3], c_full[2], c_free[2], acc_done,
+  // drain
+  static constexpr int NBAR = 2 * ABUF + 2 * STAGES + 6 + 6;
   static constexpr int TOTAL = BAR_OFF + NBAR * 8 + 16 + 1024;
   static_assert(TOTAL <= 232448, "more dynamic shared memory than one CTA may use");
 };
@@ -74,22 +76,24 @@ __global__ void __launch_bounds__(kThreads, 1)
                      const __grid_constant__ CUtensorMap mB1, const __grid_constant__ CUtensorMap mB2, BwdArgs a) {
   using L = BwdLayout<D, MODE>;
   constexpr int ST = L::STAGES;
+  constexpr int AB = L::ABUF;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t sA1 = sbase + L::A_OFF, sA2 = sA1 + L::A_BYTES;
   const uint32_t sB = sbase + L::B_OFF, sCb = sbase + L::C_OFF;
   const uint32_t bars = sbase + L::BAR_OFF;
-  const uint32_t a_full = bars;
-  auto b_full = [&](int s) { return bars + 8u * (1 + s); };
-  auto b_empty = [&](int s) { return bars + 8u * (1 + ST + s); };
+  auto a_full = [&](int i) { return bars + 8u * i; };
+  auto a_empty = [&](int i) { return bars + 8u * (AB + i); };
+  constexpr int B0 = 2 * AB;
+  auto b_full = [&](int s) { return bars + 8u * (B0 + s); };
+  auto b_empty = [&](int s) { return bars + 8u * (B0 + ST + s); };
   constexpr int NB = L::NBUF;
-  auto sd_full = [&](int i) { return bars + 8u * (1 + 2 * ST + i); };
-  auto sd_free = [&](int i) { return bars + 8u * (4 + 2 * ST + i); };
-  auto c_full = [&](int i) { return bars + 8u * (7 + 2 * ST + i); };
-  auto c_free = [&](int i) { return bars + 8u * (9 + 2 * ST + i); };
-  const uint32_t acc_done = bars + 8u * (11 + 2 * ST);
-  const uint32_t drain = bars + 8u * (12 + 2 * ST);
+  auto sd_full = [&](int i) { return bars + 8u * (B0 + 2 * ST + i); };
+  auto sd_free = [&](int i) { return bars + 8u * (B0 + 3 + 2 * ST + i); };
+  auto c_full = [&](int i) { return bars + 8u * (B0 + 6 + 2 * ST + i); };
+  auto c_free = [&](int i) { return bars + 8u * (B0 + 8 + 2 * ST + i); };
+  const uint32_t acc_done = bars + 8u * (B0 + 10 + 2 * ST);
+  const uint32_t drain = bars + 8u * (B0 + 11 + 2 * ST);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -97,39 +101,47 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int group = a.Hq / a.Hkv;
   const int off = a.Sk - a.Sq;
 
-  // ---- work decomposition
+  // ---- work items: one 128-row block of the row operand (keys for DKDV, queries for DQ) of one head;
+  // the block index is the slow coordinate, heaviest blocks first under a causal mask; CTAs take items
+  // round-robin and every barrier's phase count runs on across items
+  const int nrb = MODE == DKDV ? (a.Sk + 127) / 128 : (a.Sq + 127) / 128;
+  const int BHr = MODE == DKDV ? a.B * a.Hkv : a.B * a.Hq;
+  const int items = nrb * BHr;
   int b, hrow;      // batch and head of the row operand (kv head for DKDV, q head for DQ)
   int r0;           // first row (key for DKDV, query for DQ)
   int first_blk;    // first streamed 64-block index
   int nblk;         // streamed blocks per head
   int niter;        // total iterations (DKDV: x group)
-  if (MODE == DKDV) {
-    const int bh = blockIdx.y;
-    b = bh / a.Hkv;
-    hrow = bh % a.Hkv;
-    r0 = blockIdx.x * 128;
-    int qstart = 0;
-    if (a.causal) qstart = max(0, r0 - off);
-    first_blk = qstart / 64;
-    const int tot = (a.Sq + 63) / 64;
-    nblk = max(0, tot - first_blk);
-    niter = nblk * group;
-  } else {
-    const int nmb = (a.Sq + 127) / 128;
-    const int mb = a.causal ? (nmb - 1 - (int)blockIdx.x) : (int)blockIdx.x;
-    const int bh = blockIdx.y;
-    b = bh / a.Hq;
-    hrow = bh % a.Hq;
-    r0 = mb * 128;
-    first_blk = 0;
-    int kend = a.Sk;
-    if (a.causal) kend = min(a.Sk, r0 + 128 + off);
-    nblk = kend > 0 ? (kend + 63) / 64 : 0;
-    niter = nblk;
-  }
+  auto decomp = [&](int w) {
+    const int rbi = w / BHr, bh = w - rbi * BHr;
+    if (MODE == DKDV) {
+      b = bh / a.Hkv;
+      hrow = bh % a.Hkv;
+      r0 = rbi * 128;
+      int qstart = 0;
+      if (a.causal) qstart = max(0, r0 - off);
+      first_blk = qstart / 64;
+      const int tot = (a.Sq + 63) / 64;
+      nblk = max(0, tot - first_blk);
+      niter = nblk * group;
+    } else {
+      const int mb = a.causal ? (nrb - 1 - rbi) : rbi;
+      b = bh / a.Hq;
+      hrow = bh % a.Hq;
+      r0 = mb * 128;
+      first_blk = 0;
+      int kend = a.Sk;
+      if (a.causal) kend = min(a.Sk, r0 + 128 + off);
+      nblk = kend > 0 ? (kend + 63) / 64 : 0;
+      niter = nblk;
+    }
+  };
 
   if (threadIdx.x == 0) {
-    mbar_init(a_full, 1);
+    for (int i = 0; i < AB; ++i) {
+      mbar_init(a_full(i), 1);
+      mbar_init(a_empty(i), 1);
+    }
     for (int s = 0; s < ST; ++s) {
       mbar_init(b_full(s), 1);
       mbar_init(b_empty(s), 1);
@@ -157,115 +169,153 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;  // buf b: S at b*128, dP at b*128+64; acc1 at 256; acc2 at 256 + D
 
   if (warp == 0) {
-    if (lane == 0 && niter > 0) {
+    if (lane == 0) {
       // ---------------- TMA producer
-      mbar_arrive_expect_tx(a_full, 2 * L::A_BYTES);
-      const int ha = MODE == DKDV ? hrow : hrow;
-      for (int c = 0; c < L::NSUB; ++c) {
-        tma_load_4d(&mA1, sA1 + c * SUB128, a_full, c * 64, r0, ha, b);
-        tma_load_4d(&mA2, sA2 + c * SUB128, a_full, c * 64, r0, ha, b);
-      }
-      int i = 0;
-      for (; i < niter; ++i) {
-        const int s = i % ST;
-        if (!mbar_wait(b_empty(s), ((i / ST) & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 210, abort_flag)) break;
-        int hb, row;
-        if (MODE == DKDV) {
-          hb = hrow * group + i / nblk;
-          row = (first_blk + i % nblk) * 64;
-        } else {
-          hb = hrow / group;
-          row = i * 64;
+      int g = 0;   // streamed blocks issued (ring position)
+      int an = 0;  // items with work so far (row-operand buffer position)
+      bool ok = true;
+      for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
+        decomp(w);
+        if (niter == 0) continue;
+        const int ab = an % AB;
+        if (!mbar_wait(a_empty(ab), ((an / AB) & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 209, abort_flag)) {
+          ok = false;
+          break;
         }
-        const uint32_t st = sB + s * L::STAGE_BYTES;
-        mbar_arrive_expect_tx(b_full(s), L::STAGE_BYTES);
+        const uint32_t sA1 = sbase + L::A_OFF + ab * 2 * L::A_BYTES, sA2 = sA1 + L::A_BYTES;
+        mbar_arrive_expect_tx(a_full(ab), 2 * L::A_BYTES);
         for (int c = 0; c < L::NSUB; ++c) {
-          tma_load_4d(&mB1, st + c * SUB64, b_full(s), c * 64, row, hb, b);
-          tma_load_4d(&mB2, st + L::B_BYTES + c * SUB64, b_full(s), c * 64, row, hb, b);
+          tma_load_4d(&mA1, sA1 + c * SUB128, a_full(ab), c * 64, r0, hrow, b);
+          tma_load_4d(&mA2, sA2 + c * SUB128, a_full(ab), c * 64, r0, hrow, b);
+        }
+        ++an;
+        for (int i = 0; i < niter; ++i, ++g) {
+          const int s = g % ST;
+          if (!mbar_wait(b_empty(s), ((g / ST) & 1) ^ 1, BRAIN_ERR_TIMEOUT_EMPTY, 210, abort_flag)) {
+            ok = false;
+            break;
+          }
+          int hb, row;
+          if (MODE == DKDV) {
+            hb = hrow * group + i / nblk;
+            row = (first_blk + i % nblk) * 64;
+          } else {
+            hb = hrow / group;
+            row = i * 64;
+          }
+          const uint32_t st = sB + s * L::STAGE_BYTES;
+          mbar_arrive_expect_tx(b_full(s), L::STAGE_BYTES);
+          for (int c = 0; c < L::NSUB; ++c) {
+            tma_load_4d(&mB1, st + c * SUB64, b_full(s), c * 64, row, hb, b);
+            tma_load_4d(&mB2, st + L::B_BYTES + c * SUB64, b_full(s), c * 64, row, hb, b);
+          }
         }
       }
-      if (i < niter) {
-        for (int j = max(0, i - ST); j < i; ++j) {
+      if (!ok) {  // aborted: let the copies still in flight land (the last ST streamed blocks, the last rows)
+        for (int j = max(0, g - ST); j < g; ++j) {
           uint64_t t0 = globaltimer();
           while (!mbar_try_wait(b_full(j % ST), (j / ST) & 1) && globaltimer() - t0 < 100000000ull) {
+          }
+        }
+        if (an > 0) {
+          const int j = an - 1;
+          uint64_t t0 = globaltimer();
+          while (!mbar_try_wait(a_full(j % AB), (j / AB) & 1) && globaltimer() - t0 < 100000000ull) {
           }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && niter > 0) {
+    if (lane == 0) {
       // ---------------- MMA issuer
       constexpr uint32_t IDESC_S = idesc_f16(128, 64, 1u, 0u, 0u);
       constexpr uint32_t IDESC_ACC = idesc_f16(128, D, 1u, 0u, 1u);
-      bool ok = mbar_wait(a_full, 0, BRAIN_ERR_TIMEOUT_FULL, 220, abort_flag);
-      bool issued = false;
-      auto issue_scores = [&](int i) {
-        const uint32_t st = sB + (i % ST) * L::STAGE_BYTES;
-        const uint32_t d = tmem + (uint32_t)((i % NB) * 128);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t oa = (kk / 4) * SUB128 + (kk % 4) * 32;
-          const uint32_t ob = (kk / 4) * SUB64 + (kk % 4) * 32;
-          tc_mma_f16(d, smem_desc_sw128(sA1 + oa, 16, 1024), smem_desc_sw128(st + ob, 16, 1024), IDESC_S,
-                     kk > 0 ? 1u : 0u);
-          tc_mma_f16(d + 64, smem_desc_sw128(sA2 + oa, 16, 1024), smem_desc_sw128(st + L::B_BYTES + ob, 16, 1024),
-                     IDESC_S, kk > 0 ? 1u : 0u);
-        }
-        tc_commit(sd_full(i % NB));
-      };
-      if (ok) ok = mbar_wait(b_full(0), 0, BRAIN_ERR_TIMEOUT_FULL, 221, abort_flag);
-      if (ok) {
-        tc_fence_after();
-        issue_scores(0);
-        issued = true;
-      }
-      // the first NB-1 score blocks go out before the loop; block i+NB-1 then goes out in iteration i
-      for (int in = 1; ok && in < NB - 1 && in < niter; ++in) {
-        if (!mbar_wait(b_full(in % ST), (in / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 222, abort_flag)) {
+      bool ok = true, issued = false;
+      int g = 0, an = 0;
+      for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
+        decomp(w);
+        if (niter == 0) continue;
+        const int ab = an % AB;
+        const uint32_t sA1 = sbase + L::A_OFF + ab * 2 * L::A_BYTES, sA2 = sA1 + L::A_BYTES;
+        if (!mbar_wait(a_full(ab), (an / AB) & 1, BRAIN_ERR_TIMEOUT_FULL, 220, abort_flag)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        issue_scores(in);
-      }
-      for (int i = 0; ok && i < niter; ++i) {
-        if (i + NB - 1 < niter) {
-          const int in = i + NB - 1;
-          if (!mbar_wait(b_full(in % ST), (in / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 222, abort_flag) ||
-              !mbar_wait(sd_free(in % NB), ((in / NB) & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 223, abort_flag)) {
+        auto issue_scores = [&](int i) {
+          const int gi = g + i;
+          const uint32_t st = sB + (gi % ST) * L::STAGE_BYTES;
+          const uint32_t d = tmem + (uint32_t)((gi % NB) * 128);
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t oa = (kk / 4) * SUB128 + (kk % 4) * 32;
+            const uint32_t ob = (kk / 4) * SUB64 + (kk % 4) * 32;
+            tc_mma_f16(d, smem_desc_sw128(sA1 + oa, 16, 1024), smem_desc_sw128(st + ob, 16, 1024), IDESC_S,
+                       kk > 0 ? 1u : 0u);
+            tc_mma_f16(d + 64, smem_desc_sw128(sA2 + oa, 16, 1024),
+                       smem_desc_sw128(st + L::B_BYTES + ob, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
+          }
+          tc_commit(sd_full(gi % NB));
+        };
+        // score block i waits for its streamed operands and for its TMEM buffer (freed by the elementwise
+        // warps' reads of global block gi - NB)
+        auto wait_scores = [&](int i) {
+          const int gi = g + i;
+          return mbar_wait(b_full(gi % ST), (gi / ST) & 1, BRAIN_ERR_TIMEOUT_FULL, 222, abort_flag) &&
+                 mbar_wait(sd_free(gi % NB), ((gi / NB) & 1) ^ 1, BRAIN_ERR_TIMEOUT_ACC, 223, abort_flag);
+        };
+        // the first NB-1 score blocks go out before the loop; block i+NB-1 then goes out in iteration i
+        for (int in = 0; ok && in < NB - 1 && in < niter; ++in) {
+          if (!wait_scores(in)) {
             ok = false;
             break;
           }
           tc_fence_after();
           issue_scores(in);
+          issued = true;
         }
-        if (!mbar_wait(c_full(i & 1), (i / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 224, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t st = sB + (i % ST) * L::STAGE_BYTES;
-        const uint32_t sC = sCb + (i & 1) * L::C_BYTES;
-#pragma unroll
-        for (int kk = 0; kk < 64 / 16; ++kk) {
-          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          const uint64_t c0 = smem_desc_sw128(sC + kk * 32, 16, 1024);
-          if (MODE == DKDV) {
-            const uint64_t c1 = smem_desc_sw128(sC + SUB128 + kk * 32, 16, 1024);
-            // dV += P^T dO   (dO = B2, MN-major);  dK += dS^T Q   (Q = B1, MN-major)
-            tc_mma_f16(tmem + L::ACC, c0, smem_desc_sw128(st + L::B_BYTES + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
-            tc_mma_f16(tmem + L::ACC + D, c1, smem_desc_sw128(st + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
-          } else {
-            // dQ += dS K   (K = B1, MN-major)
-            tc_mma_f16(tmem + L::ACC, c0, smem_desc_sw128(st + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
+        for (int i = 0; ok && i < niter; ++i) {
+          if (i + NB - 1 < niter) {
+            const int in = i + NB - 1;
+            if (!wait_scores(in)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_scores(in);
           }
+          const int gi = g + i;
+          if (!mbar_wait(c_full(gi & 1), (gi / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 224, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t st = sB + (gi % ST) * L::STAGE_BYTES;
+          const uint32_t sC = sCb + (gi & 1) * L::C_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < 64 / 16; ++kk) {
+            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+            const uint64_t c0 = smem_desc_sw128(sC + kk * 32, 16, 1024);
+            if (MODE == DKDV) {
+              const uint64_t c1 = smem_desc_sw128(sC + SUB128 + kk * 32, 16, 1024);
+              // dV += P^T dO   (dO = B2, MN-major);  dK += dS^T Q   (Q = B1, MN-major)
+              tc_mma_f16(tmem + L::ACC, c0, smem_desc_sw128(st + L::B_BYTES + kk * 2048, SUB64, 1024), IDESC_ACC,
+                         acc);
+              tc_mma_f16(tmem + L::ACC + D, c1, smem_desc_sw128(st + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
+            } else {
+              // dQ += dS K   (K = B1, MN-major)
+              tc_mma_f16(tmem + L::ACC, c0, smem_desc_sw128(st + kk * 2048, SUB64, 1024), IDESC_ACC, acc);
+            }
+          }
+          tc_commit(c_free(gi & 1));
+          tc_commit(b_empty(gi % ST));
         }
-        tc_commit(c_free(i & 1));
-        tc_commit(b_empty(i % ST));
-      }
-      if (ok) {
+        if (!ok) break;
+        tc_commit(a_empty(ab));  // every score MMA of the item was issued: its row operands free when done
         tc_commit(acc_done);
-      } else if (issued) {
+        ++an;
+        g += niter;
+      }
+      if (!ok && issued) {
         tc_commit(drain);
         uint64_t t0 = globaltimer();
         while (!mbar_try_wait(drain, 0) && globaltimer() - t0 < 100000000ull) {
@@ -278,8 +328,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int hc = (warp - 2) >> 2;
     const int et = (warp - 2) * 32 + lane;  // 0..255
     const int r = q * 32 + lane;
-    const int row = r0 + r;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+    bool ok = true;
+    int g = 0, nacc = 0;  // streamed blocks of earlier items; items whose accumulators were read
+    for (int w = blockIdx.x; ok && w < items; w += gridDim.x) {
+    decomp(w);
+    const int row = r0 + r;
     float row_lse2 = 0.f, row_delta = 0.f;
     if (MODE == DQ && row < a.Sq) {
       const int64_t idx = ((int64_t)b * a.Hq + hrow) * a.Sq + row;
@@ -298,14 +352,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       return et < 64 ? __ldg(a.lse + base) * kLog2e : __ldg(a.delta + base);
     };
     float v_next = stat(0);
-    bool ok = true;
-    auto tbuf = [&](int i) { return tmem + (uint32_t)((i % NB) * 128 + hc * 32) + lane_addr; };
+    auto tbuf = [&](int gi) { return tmem + (uint32_t)((gi % NB) * 128 + hc * 32) + lane_addr; };
     // DKDV leaves the loop only through its per-iteration barrier (all threads together); DQ has no barrier
     for (int i = 0; i < niter && (MODE == DKDV || ok); ++i) {
+      const int gi = g + i;
       int col0;
       if (MODE == DKDV) col0 = (first_blk + i % nblk) * 64;
       else col0 = i * 64;
-      float* sld = reinterpret_cast<float*>(smem + L::LD_OFF) + (i & 1) * 128;
+      float* sld = reinterpret_cast<float*>(smem + L::LD_OFF) + (gi & 1) * 128;
       float s[32], dp[32];
       if (MODE == DKDV) {
         // the block's statistics go through shared memory (read back as broadcasts) instead of every
@@ -313,29 +367,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         // reaches it after bounded waits and all of them leave the loop together when any wait gave up.
         const float v = v_next;
         v_next = stat(i + 1);
-        if (ok) ok = mbar_wait(sd_full(i % NB), (i / NB) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag);
+        if (ok) ok = mbar_wait(sd_full(gi % NB), (gi / NB) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag);
         if (et < 128) sld[et] = v;
         if (!bar_sync_and(1, kEwThreads, ok)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        tmem_ld32(tbuf(i), reinterpret_cast<uint32_t*>(s));
-        tmem_ld32(tbuf(i) + 64, reinterpret_cast<uint32_t*>(dp));
+        tmem_ld32(tbuf(gi), reinterpret_cast<uint32_t*>(s));
+        tmem_ld32(tbuf(gi) + 64, reinterpret_cast<uint32_t*>(dp));
         tc_wait_ld();
         tc_fence_before();
-        mbar_arrive(sd_free(i % NB));
+        mbar_arrive(sd_free(gi % NB));
       } else {
-        if (!mbar_wait(sd_full(i % NB), (i / NB) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag)) {
+        if (!mbar_wait(sd_full(gi % NB), (gi / NB) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        tmem_ld32(tbuf(i), reinterpret_cast<uint32_t*>(s));
-        tmem_ld32(tbuf(i) + 64, reinterpret_cast<uint32_t*>(dp));
+        tmem_ld32(tbuf(gi), reinterpret_cast<uint32_t*>(s));
+        tmem_ld32(tbuf(gi) + 64, reinterpret_cast<uint32_t*>(dp));
         tc_wait_ld();
         tc_fence_before();
-        mbar_arrive(sd_free(i % NB));
+        mbar_arrive(sd_free(gi % NB));
       }
       const int cb = hc * 32;  // this thread's first column of the block
       uint32_t pk[16], dk[16];
@@ -422,9 +476,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 32; c += 2)
           dk[c / 2] = pack_bf16x2(pv[c] * (dp[c] - row_delta), pv[c + 1] * (dp[c + 1] - row_delta));
       }
-      // C buffer i&1 was last read by the accumulate MMAs of block i-2
-      const uint32_t sC = sCb + (i & 1) * L::C_BYTES;
-      if (i > 1 && !mbar_wait(c_free(i & 1), ((i - 2) / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 231, abort_flag)) {
+      // C buffer gi&1 was last read by the accumulate MMAs of global block gi-2
+      const uint32_t sC = sCb + (gi & 1) * L::C_BYTES;
+      if (gi > 1 && !mbar_wait(c_free(gi & 1), ((gi - 2) / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 231, abort_flag)) {
         ok = false;
         if (MODE == DKDV) continue;  // leaves at the next barrier, together with the other threads
         break;
@@ -449,11 +503,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       fence_proxy_async();
       tc_fence_before();
-      mbar_arrive(c_full(i & 1));
+      mbar_arrive(c_full(gi & 1));
     }
-    bool have = ok && niter > 0;
-    if (have && !mbar_wait(acc_done, 0, BRAIN_ERR_TIMEOUT_ACC, 232, abort_flag)) have = false;
-    tc_fence_after();
+    ok = bar_sync_and(1, kEwThreads, ok);  // a give-up in the last block: all threads leave together
+    if (!ok) break;
+    g += niter;
+    bool have = niter > 0;
+    if (have) {
+      if (!mbar_wait(acc_done, nacc & 1, BRAIN_ERR_TIMEOUT_ACC, 232, abort_flag)) ok = false;
+      ++nacc;
+      // the next item's first accumulate MMA (issued after every thread's c_full arrival) overwrites the
+      // accumulators: all threads leave together when a wait gave up
+      ok = bar_sync_and(1, kEwThreads, ok);
+      if (!ok) break;
+      tc_fence_after();
+    }
     // epilogue: DKDV writes dV (acc1) and dK * scale (acc2); DQ writes dQ * scale (acc1)
     const bool store = MODE == DKDV ? (row < a.Sk) : (row < a.Sq);
 #pragma unroll 1
@@ -486,6 +550,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 32; k += 8) store8(base + c * 32 + k, v + k);
         }
       }
+    }
     }
   }
 
@@ -537,9 +602,8 @@ int launch_kernel(const CUtensorMap& a1, const CUtensorMap& a2, const CUtensorMa
   using L = BwdLayout<D, MODE>;
   auto kern = fa_bwd_tc_kernel<D, MODE, BIAS>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL);
-  dim3 grid;
-  if (MODE == DKDV) grid = dim3((a.Sk + 127) / 128, a.B * a.Hkv);
-  else grid = dim3((a.Sq + 127) / 128, a.B * a.Hq);
+  const int items = MODE == DKDV ? ((a.Sk + 127) / 128) * a.B * a.Hkv : ((a.Sq + 127) / 128) * a.B * a.Hq;
+  const int grid = std::min(items, brain_host::num_sms());  // persistent: CTAs loop over work items
   kern<<<grid, kThreads, L::TOTAL, st>>>(a1, a2, b1, b2, a);
   return (int)cudaGetLastError();
 }

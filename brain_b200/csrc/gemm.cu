@@ -104,17 +104,32 @@ __device__ __forceinline__ void unit_coords(const GemmArgs& a, int t, int num_kb
 __device__ __forceinline__ void store_chunk_at(const GemmArgs& args, int gm, int gn0, const uint32_t* r, void* cbase,
                                                int64_t crow);
 
+// v[j] += bias[gn0 + j] for 32 columns: one 16-byte load per 8 columns when the row chunk is whole and
+// aligned (every lane of a warp reads the same address: a broadcast), else per column within N.
+__device__ __forceinline__ void add_bias32(const GemmArgs& args, int gn0, bool full, float* v) {
+  const __nv_bfloat16* bp = args.bias + gn0;
+  if (full && ((reinterpret_cast<uintptr_t>(bp) & 15) == 0)) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float bv[8];
+      load8(bp + j, bv);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[j + u] += bv[u];
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (gn0 + j < args.N) v[j] += __bfloat162float(bp[j]);
+  }
+}
+
 // alpha, bias, residual and beta * C_old for one row x 32 columns (C_old read at row gm of C).
 __device__ __forceinline__ void epi_math(const GemmArgs& args, int gm, int gn0, const uint32_t* r, float* v) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
   if (gm >= args.M) return;
   const bool full = gn0 + 32 <= args.N;
-  if (args.bias) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (full || gn0 + j < args.N) v[j] += __bfloat162float(args.bias[gn0 + j]);
-  }
+  if (args.bias) add_bias32(args, gn0, full, v);
   if (args.R) {
     const __nv_bfloat16* rp = args.R + (int64_t)gm * args.ldr + gn0;
     if (full && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
@@ -181,11 +196,7 @@ __device__ __forceinline__ void store_chunk_at(const GemmArgs& args, int gm, int
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
   const bool full = gn0 + 32 <= args.N;
-  if (args.bias) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (full || gn0 + j < args.N) v[j] += __bfloat162float(args.bias[gn0 + j]);
-  }
+  if (args.bias) add_bias32(args, gn0, full, v);
   if (args.R) {
     const __nv_bfloat16* rp = args.R + (int64_t)gm * args.ldr + gn0;
 #pragma unroll

@@ -403,6 +403,39 @@ __global__ void colsum8_kernel(const float* __restrict__ part, int P, int D, voi
   }
 }
 
+// Column sums of a bf16 matrix x [M, N] (bias gradients): block (32, 8) covers 32 column vectors of 8 and
+// strides over rows with its 8 row lanes; each lane keeps 8 f32 sums, the 8 lanes are added in order and the
+// block writes one f32 partial row (part[blockIdx.y, :]); colsum8_kernel then adds the partial rows.
+__global__ void colsum_bf16_part_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int M, int N,
+                                        float* __restrict__ part) {
+  __shared__ float sm[8][32 * 8 + 1];
+  const int v = blockIdx.x * 32 + threadIdx.x;  // column vector
+  const bool col_ok = v * 8 < N;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+  if (col_ok) {
+    for (int64_t r = (int64_t)blockIdx.y * 8 + threadIdx.y; r < M; r += (int64_t)gridDim.y * 8) {
+      float f[8];
+      load8(x + r * ldx + v * 8, f);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += f[j];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) sm[threadIdx.y][threadIdx.x * 8 + j] = acc[j];
+  __syncthreads();
+  // 256 threads finalise the block's 256 columns: column c = threadIdx.y * 32 + threadIdx.x
+  const int c = threadIdx.y * 32 + threadIdx.x;
+  const int col = blockIdx.x * 256 + c;
+  if (col < N) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += sm[k][c];
+    part[(int64_t)blockIdx.y * N + col] = t;
+  }
+}
+
 // out[d] (+)= sum_p part[p, d]; out dtype bf16 (out_f32 = 0) or f32.
 __global__ void colsum_kernel(const float* __restrict__ part, int P, int D, void* out, int out_f32, int accumulate) {
   const int d = blockIdx.x * blockDim.x + threadIdx.x;
@@ -447,6 +480,30 @@ BRAIN_API int brain_norm_fwd(int kind, const void* x, int64_t ldx, const void* r
     norm_fwd_kernel<false><<<M, T, 0, st>>>(X, ldx, R, ldres, W, Bp, Y, ldy, S, ldsum, mean_out, rstd_out, D, eps);
   else
     norm_fwd_kernel<true><<<M, T, 0, st>>>(X, ldx, R, ldres, W, Bp, Y, ldy, S, ldsum, mean_out, rstd_out, D, eps);
+  return (int)cudaGetLastError();
+}
+
+// Number of f32 partial rows brain_colsum_bf16 needs in its workspace (f32 [partials, N]).
+BRAIN_API int brain_colsum_partials(int M) {
+  const int p = 2 * brain_host::num_sms();
+  return M < 8 * p ? (M + 7) / 8 > 0 ? (M + 7) / 8 : 1 : p;
+}
+
+// out[n] (+)= sum_m x[m, n] for bf16 x [M, N] (row stride ldx, N % 8 == 0, 16-byte aligned rows); out is
+// bf16 or f32 (out_f32), accumulated when accumulate != 0. Deterministic (fixed summation order).
+BRAIN_API int brain_colsum_bf16(const void* x, int64_t ldx, int M, int N, void* out, int out_f32, int accumulate,
+                                float* workspace, cudaStream_t st) {
+  if (N == 0) return 0;
+  if (N % 8 != 0 || ldx % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15)) return (int)cudaErrorInvalidValue;
+  const int P = brain_colsum_partials(M);
+  if (M > 0) {
+    dim3 grid((N / 8 + 31) / 32, P);
+    colsum_bf16_part_kernel<<<grid, dim3(32, 8), 0, st>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx, M, N,
+                                                         workspace);
+  } else {
+    cudaMemsetAsync(workspace, 0, sizeof(float) * N, st);
+  }
+  colsum8_kernel<<<(N + 31) / 32, dim3(32, 8), 0, st>>>(workspace, M > 0 ? P : 1, N, out, out_f32, accumulate);
   return (int)cudaGetLastError();
 }
 

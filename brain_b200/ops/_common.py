@@ -12,6 +12,8 @@ from .. import _native
 _native.register({
     "brain_norm_fwd": ("brain_kernels", "iplplppplplppiifs"),
     "brain_norm_bwd_partials": ("brain_kernels", "i"),
+    "brain_colsum_partials": ("brain_kernels", "i"),
+    "brain_colsum_bf16": ("brain_kernels", "pliipiips"),
     "brain_norm_bwd": ("brain_kernels", "iplplpppplplppiipiis"),
     "brain_swiglu_fwd": ("brain_kernels", "plpllis"),
     "brain_swiglu_bwd": ("brain_kernels", "plplpllis"),

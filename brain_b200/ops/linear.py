@@ -20,6 +20,7 @@ from .activations import swiglu_bwd_only, swiglu_fwd_only
 from .gemm import gemm, gemm_rope
 from .rope import apply_rope_
 from ._common import has_main_grad, main_grad_beta, rows2d
+from .. import _native
 from . import norms as _norms
 
 
@@ -31,9 +32,32 @@ def _wgrad(dy2, x2, w):
     return gemm(dy2, x2, trans_a=True, out_dtype=torch.float32).to(w.dtype)
 
 
+def _colsum_ok(dy2, out):
+    return (dy2.is_cuda and dy2.dtype == torch.bfloat16 and dy2.stride(1) == 1 and dy2.size(1) % 8 == 0
+            and dy2.stride(0) % 8 == 0 and dy2.data_ptr() % 16 == 0 and out.is_contiguous()
+            and out.dtype in (torch.bfloat16, torch.float32))
+
+
+def colsum_(dy2, out, accumulate=False):
+    """out (+)= dy2.sum(0) with f32 accumulation on the native column-sum kernel (bias gradients)."""
+    M, N = dy2.shape
+    P = _native.fn("brain_colsum_partials")(M)
+    ws = torch.empty(P * N, device=dy2.device, dtype=torch.float32)
+    _native.call("brain_colsum_bf16", dy2.data_ptr(), dy2.stride(0), M, N, out.data_ptr(),
+                 int(out.dtype == torch.float32), int(accumulate), ws.data_ptr(), _native.stream_ptr(dy2.device))
+    return out
+
+
 def _bgrad(dy2, b):
     if b is None:
         return None
+    if has_main_grad(b) and _colsum_ok(dy2, b.main_grad):
+        colsum_(dy2, b.main_grad, accumulate=main_grad_beta(b) != 0.0)
+        return None
+    if dy2.is_cuda and b.dtype in (torch.bfloat16, torch.float32):
+        g = torch.empty(b.shape, device=b.device, dtype=b.dtype)
+        if _colsum_ok(dy2, g):
+            return colsum_(dy2, g)
     g = dy2.sum(0, dtype=torch.float32)  # f32 accumulation without an f32 copy of dy
     if has_main_grad(b):
         if main_grad_beta(b) == 0.0:

@@ -207,7 +207,9 @@ def test_flash_attention(D, causal, Sq, Sk, Hq, Hkv):
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("B,Sq,Sk,Hq,Hkv", [(1, 128, 128, 2, 2), (2, 300, 300, 8, 2), (1, 200, 517, 4, 1),
-                                            (2, 1, 333, 4, 2), (1, 1024, 1024, 4, 4)])
+                                            (2, 1, 333, 4, 2), (1, 1024, 1024, 4, 4),
+                                            # more work items than SMs: each persistent CTA runs several
+                                            (64, 197, 197, 12, 12), (4, 600, 700, 32, 8)])
 def test_flash_attention_tcgen05_forward(D, causal, B, Sq, Sk, Hq, Hkv):
     q = rnd(B, Sq, Hq, D, seed=40, scale=2.0)
     k = rnd(B, Sk, Hkv, D, seed=41, scale=2.0)
@@ -224,7 +226,9 @@ def test_flash_attention_tcgen05_forward(D, causal, B, Sq, Sk, Hq, Hkv):
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("causal", [True, False])
 @pytest.mark.parametrize("B,Sq,Sk,Hq,Hkv", [(1, 128, 128, 2, 2), (2, 300, 300, 8, 2), (1, 200, 517, 4, 1),
-                                            (1, 640, 640, 4, 4), (2, 1, 129, 4, 2)])
+                                            (1, 640, 640, 4, 4), (2, 1, 129, 4, 2),
+                                            # more work items than SMs: each persistent CTA runs several
+                                            (64, 197, 197, 12, 12), (4, 600, 700, 32, 8)])
 def test_flash_attention_tcgen05_backward(D, causal, B, Sq, Sk, Hq, Hkv):
     q = rnd(B, Sq, Hq, D, seed=44)
     k = rnd(B, Sk, Hkv, D, seed=45)
@@ -434,3 +438,25 @@ def test_masked_attention_tcgen05_matches_reference(D, case):
     close(kg.grad, kr.grad, 3e-2, 3e-2)
     close(vg.grad, vr.grad, 3e-2, 3e-2)
     _no_status()
+
+
+@gpu
+@pytest.mark.parametrize("M,N", [(50432, 768), (3000, 2304), (7, 3072), (1, 8)])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_colsum_bias_grad_matches_fp32(M, N, out_dtype):
+    from brain_b200.ops.linear import colsum_
+    g = torch.Generator(device="cpu").manual_seed(M + N)
+    x = torch.randn(M, N, generator=g).to("cuda", torch.bfloat16)
+    ref = x.float().sum(0)
+    out = torch.empty(N, device="cuda", dtype=out_dtype)
+    colsum_(x, out)
+    tol = 1e-4 * M ** 0.5 + 1e-5 if out_dtype == torch.float32 else 1e-2 * (1 + ref.abs().max().item())
+    torch.testing.assert_close(out.float(), ref, rtol=1e-3 if out_dtype == torch.float32 else 1e-2, atol=tol)
+    base = torch.randn(N, device="cuda").to(out_dtype)
+    acc = base.clone()
+    colsum_(x, acc, accumulate=True)
+    torch.testing.assert_close(acc.float(), base.float() + ref, rtol=1e-2, atol=tol + 1e-2)
+    out2 = torch.empty_like(out)
+    colsum_(x, out2)
+    assert torch.equal(out, out2)  # fixed summation order
+    assert ops.check_status() == []
