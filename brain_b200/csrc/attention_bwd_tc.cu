@@ -64,8 +64,8 @@ struct BwdLayout {
   static constexpr int NBUF = 2;
   static constexpr int ACC = NBUF * 128;  // first accumulator column
   // a_full[ABUF], a_empty[ABUF], b_full[S], b_empty[S], sd_full[3], sd_free[3], c_full[2], c_free[2], acc_done,
-  // drain
-  static constexpr int NBAR = 2 * ABUF + 2 * STAGES + 6 + 6;
+  // drain, st_free[2]
+  static constexpr int NBAR = 2 * ABUF + 2 * STAGES + 6 + 6 + 2;
   static constexpr int TOTAL = BAR_OFF + NBAR * 8 + 16 + 1024;
   static_assert(TOTAL <= 232448, "more dynamic shared memory than one CTA may use");
 };
@@ -94,6 +94,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto c_free = [&](int i) { return bars + 8u * (B0 + 8 + 2 * ST + i); };
   const uint32_t acc_done = bars + 8u * (B0 + 10 + 2 * ST);
   const uint32_t drain = bars + 8u * (B0 + 11 + 2 * ST);
+  // DKDV: a group's statistics slot may be rewritten once all its threads have read it for the previous block
+  auto st_free = [&](int grp) { return bars + 8u * (B0 + 12 + 2 * ST + grp); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::BAR_OFF + L::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -148,14 +150,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 3; ++i) {
       mbar_init(sd_full(i), 1);
-      mbar_init(sd_free(i), kEwThreads);
+      mbar_init(sd_free(i), kEwThreads / 2);  // read by one group of elementwise warps
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(c_full(i), kEwThreads);
+      mbar_init(c_full(i), kEwThreads / 2);
       mbar_init(c_free(i), 1);
     }
     mbar_init(acc_done, 1);
     mbar_init(drain, 1);
+    mbar_init(st_free(0), kEwThreads / 2);
+    mbar_init(st_free(1), kEwThreads / 2);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -323,10 +327,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- elementwise warps (2..9): quadrant q of the TMEM lanes, column half hc
+    // ---------------- elementwise warps (2..9): quadrant q of the TMEM lanes. Two groups of four warps
+    // take alternate blocks (group hc the blocks of global index parity hc, so each TMEM score buffer, C tile
+    // and statistics slot has one owner): while one group waits for its next scores the other computes.
+    // Each thread covers its row's 64 columns of a block in two chunks of 32.
     const int q = warp & 3;
-    const int hc = (warp - 2) >> 2;
-    const int et = (warp - 2) * 32 + lane;  // 0..255
+    const int hc = (warp - 2) >> 2;                  // group; also the column half of the epilogue
+    const int et = (warp - 2 - 4 * hc) * 32 + lane;  // 0..127 within the group
     const int r = q * 32 + lane;
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
     bool ok = true;
@@ -344,17 +351,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     // DKDV: the 64 query statistics (lse * log2e, delta) of block i, one per thread et < 128, loaded
     // one iteration ahead so that their L2 latency hides behind the previous block's work
     auto stat = [&](int i) -> float {
-      if (MODE != DKDV || et >= 128 || i >= niter) return 0.f;
+      if (MODE != DKDV || i >= niter) return 0.f;
       const int hc_ = hrow * group + i / nblk;
       const int qi = (first_blk + i % nblk) * 64 + (et & 63);
       if (qi >= a.Sq) return 0.f;
       const int64_t base = ((int64_t)b * a.Hq + hc_) * a.Sq + qi;
       return et < 64 ? __ldg(a.lse + base) * kLog2e : __ldg(a.delta + base);
     };
-    float v_next = stat(0);
-    auto tbuf = [&](int gi) { return tmem + (uint32_t)((gi % NB) * 128 + hc * 32) + lane_addr; };
-    // DKDV leaves the loop only through its per-iteration barrier (all threads together); DQ has no barrier
-    for (int i = 0; i < niter && (MODE == DKDV || ok); ++i) {
+    const int i0 = (hc ^ g) & 1;  // this group's first block of the item
+    float v_next = stat(i0);
+    auto tbuf = [&](int gi, int h) { return tmem + (uint32_t)((gi % NB) * 128 + h * 32) + lane_addr; };
+    // DKDV leaves the loop only through its per-iteration group barrier (the group's threads together); DQ
+    // has no barrier in the loop
+    for (int i = i0; i < niter && (MODE == DKDV || ok); i += 2) {
       const int gi = g + i;
       int col0;
       if (MODE == DKDV) col0 = (first_blk + i % nblk) * 64;
@@ -366,32 +375,41 @@ __global__ void __launch_bounds__(kThreads, 1)
         // thread loading all 64. The barrier also makes the give-up decision uniform: every thread
         // reaches it after bounded waits and all of them leave the loop together when any wait gave up.
         const float v = v_next;
-        v_next = stat(i + 1);
+        v_next = stat(i + 2);
         if (ok) ok = mbar_wait(sd_full(gi % NB), (gi / NB) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag);
-        if (et < 128) sld[et] = v;
-        if (!bar_sync_and(1, kEwThreads, ok)) {
+        // the group's slot held the statistics of its previous block (k - 1): wait until every thread of
+        // the group has read them
+        const int k = gi >> 1;
+        if (ok && k > 0) ok = mbar_wait(st_free(hc), (k - 1) & 1, BRAIN_ERR_TIMEOUT_ACC, 233, abort_flag);
+        sld[et] = v;
+        if (!bar_sync_and(1 + hc, kEwThreads / 2, ok)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        tmem_ld32(tbuf(gi), reinterpret_cast<uint32_t*>(s));
-        tmem_ld32(tbuf(gi) + 64, reinterpret_cast<uint32_t*>(dp));
-        tc_wait_ld();
-        tc_fence_before();
-        mbar_arrive(sd_free(gi % NB));
       } else {
         if (!mbar_wait(sd_full(gi % NB), (gi / NB) & 1, BRAIN_ERR_TIMEOUT_ACC, 230, abort_flag)) {
           ok = false;
           break;
         }
-        tc_fence_after();
-        tmem_ld32(tbuf(gi), reinterpret_cast<uint32_t*>(s));
-        tmem_ld32(tbuf(gi) + 64, reinterpret_cast<uint32_t*>(dp));
-        tc_wait_ld();
+      }
+      // C buffer gi&1 was last read by the accumulate MMAs of global block gi-2 (this group's previous one)
+      const uint32_t sC = sCb + (gi & 1) * L::C_BYTES;
+      if (gi > 1 && !mbar_wait(c_free(gi & 1), ((gi - 2) / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 231, abort_flag)) {
+        ok = false;
+        if (MODE == DKDV) continue;  // leaves at the next barrier, together with the group's other threads
+        break;
+      }
+      tc_fence_after();
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+      tmem_ld32(tbuf(gi, h), reinterpret_cast<uint32_t*>(s));
+      tmem_ld32(tbuf(gi, h) + 64, reinterpret_cast<uint32_t*>(dp));
+      tc_wait_ld();
+      if (h == 1) {  // both chunks are in registers: the score buffer may take the next block
         tc_fence_before();
         mbar_arrive(sd_free(gi % NB));
       }
-      const int cb = hc * 32;  // this thread's first column of the block
+      const int cb = h * 32;  // this chunk's first column of the block
       uint32_t pk[16], dk[16];
       if (MODE == DKDV) {
         const int key = row;
@@ -476,17 +494,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int c = 0; c < 32; c += 2)
           dk[c / 2] = pack_bf16x2(pv[c] * (dp[c] - row_delta), pv[c + 1] * (dp[c + 1] - row_delta));
       }
-      // C buffer gi&1 was last read by the accumulate MMAs of global block gi-2
-      const uint32_t sC = sCb + (gi & 1) * L::C_BYTES;
-      if (gi > 1 && !mbar_wait(c_free(gi & 1), ((gi - 2) / 2) & 1, BRAIN_ERR_TIMEOUT_ACC, 231, abort_flag)) {
-        ok = false;
-        if (MODE == DKDV) continue;  // leaves at the next barrier, together with the other threads
-        break;
-      }
-      tc_fence_after();
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {  // this thread's 4 chunks of 8 columns (of 8 per 128 B row)
-        const int c = hc * 4 + cc;
+      for (int cc = 0; cc < 4; ++cc) {  // this chunk's 4 pieces of 8 columns (of 8 per 128 B row)
+        const int c = h * 4 + cc;
         const uint32_t o = r * 128 + ((c ^ (r % 8)) * 16);
         if (MODE == DKDV) {
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sC + o), "r"(pk[4 * cc]),
@@ -501,11 +511,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                        : "memory");
         }
       }
+      }
+      if (MODE == DKDV) mbar_arrive(st_free(hc));  // this thread's reads of the statistics slot are done
       fence_proxy_async();
       tc_fence_before();
       mbar_arrive(c_full(gi & 1));
     }
-    ok = bar_sync_and(1, kEwThreads, ok);  // a give-up in the last block: all threads leave together
+    ok = bar_sync_and(3, kEwThreads, ok);  // a give-up in the last block: all threads leave together
     if (!ok) break;
     g += niter;
     bool have = niter > 0;
@@ -514,7 +526,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++nacc;
       // the next item's first accumulate MMA (issued after every thread's c_full arrival) overwrites the
       // accumulators: all threads leave together when a wait gave up
-      ok = bar_sync_and(1, kEwThreads, ok);
+      ok = bar_sync_and(3, kEwThreads, ok);
       if (!ok) break;
       tc_fence_after();
     }

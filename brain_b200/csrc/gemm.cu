@@ -63,6 +63,9 @@ struct GemmArgs {
   // over k-blocks [s * kb_split, (s + 1) * kb_split) with s = t / (tiles_m * tiles_n); its raw f32 sums go
   // to rows [s * split_rows, ...) of the workspace C, and a second kernel adds the slices in order.
   int splits, kb_split, split_rows;
+  // CTA-pair TMA-store epilogue with a bf16 output: the residual tile arrives by TMA (tmR) into per-warp
+  // swizzled buffers one 64-column unit ahead, instead of per-row global loads
+  int r_tma;
 };
 
 template <int BN, int STAGES>
@@ -124,13 +127,14 @@ __device__ __forceinline__ void add_bias32(const GemmArgs& args, int gn0, bool f
 }
 
 // alpha, bias, residual and beta * C_old for one row x 32 columns (C_old read at row gm of C).
-__device__ __forceinline__ void epi_math(const GemmArgs& args, int gm, int gn0, const uint32_t* r, float* v) {
+__device__ __forceinline__ void epi_math(const GemmArgs& args, int gm, int gn0, const uint32_t* r, float* v,
+                                         bool skip_r = false) {
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
   if (gm >= args.M) return;
   const bool full = gn0 + 32 <= args.N;
   if (args.bias) add_bias32(args, gn0, full, v);
-  if (args.R) {
+  if (args.R && !skip_r) {
     const __nv_bfloat16* rp = args.R + (int64_t)gm * args.ldr + gn0;
     if (full && ((reinterpret_cast<uintptr_t>(rp) & 15) == 0)) {
 #pragma unroll
@@ -439,17 +443,23 @@ struct PairSmem {
   static constexpr int A_BYTES = 128 * BK * 2;
   static constexpr int B_BYTES = 128 * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  // output staging: per epilogue warp two 4 KB buffers of 32 rows x 128 B (128-byte swizzle)
+  // output staging: per epilogue warp two 4 KB buffers of 32 rows x 128 B (128-byte swizzle); then per warp
+  // two 4 KB residual buffers (same layout) filled by TMA
   static constexpr int EPI_OFFSET = kPairStages * STAGE_BYTES;
   static constexpr int EPI_BYTES = 4 * 2 * 4096;
-  static constexpr int BAR_OFFSET = EPI_OFFSET + EPI_BYTES;
-  static constexpr int TOTAL = BAR_OFFSET + (2 * kPairStages + 5) * 8 + 16 + 1024;
+  static constexpr int RES_OFFSET = EPI_OFFSET + EPI_BYTES;
+  static constexpr int RES_BYTES = 4 * 2 * 4096;
+  static constexpr int BAR_OFFSET = RES_OFFSET + RES_BYTES;
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], drain, res_full[4 warps][2]
+  static constexpr int NBAR = 2 * kPairStages + 5 + 8;
+  static constexpr int TOTAL = BAR_OFFSET + NBAR * 8 + 16 + 1024;
+  static_assert(TOTAL <= 232448, "more dynamic shared memory than one CTA may use");
 };
 
 template <int A_MN, int B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, GemmArgs args) {
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, GemmArgs args) {
   using S = PairSmem;
   constexpr int ST = kPairStages;
   constexpr int TN = 256;  // pair tile: 256 x 256
@@ -462,7 +472,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   auto tfull_bar = [&](int a) { return bar_base + 8u * (2 * ST + a); };
   auto tempty_bar = [&](int a) { return bar_base + 8u * (2 * ST + 2 + a); };
   const uint32_t drain_bar = bar_base + 8u * (2 * ST + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::BAR_OFFSET + (2 * ST + 5) * 8);
+  auto res_bar = [&](int q, int slot) { return bar_base + 8u * (2 * ST + 5 + 2 * q + slot); };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + S::BAR_OFFSET + S::NBAR * 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
@@ -481,11 +492,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_init(tempty_bar(a), 256);  // 128 epilogue threads of each CTA arrive on CTA 0's barrier
     }
     mbar_init(drain_bar, 1);
+    for (int i = 0; i < 8; ++i) mbar_init(res_bar(i / 2, i % 2), 1);
     *abort_flag = 0;
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if (args.tma_store) prefetch_tmap(&tmC);
+    if (args.r_tma) prefetch_tmap(&tmR);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), 512);
@@ -599,6 +612,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t stg = sbase + S::EPI_OFFSET + (uint32_t)q * 8192u;  // this warp's two staging buffers
     int ebuf = 0;
     int local = 0;
+    // residual by TMA: this warp's stream of (tile, 64-column unit) boxes, loaded one unit ahead into two
+    // slots; rc units consumed, r_issued units requested
+    const uint32_t rbase = sbase + S::RES_OFFSET + (uint32_t)q * 8192u;
+    int rc = 0, r_issued = 0, r_done = 0;
+    bool r_ok = true;
+    auto res_units = [&](int tt) {
+      int tm_, tn_, k0_, k1_, sp_;
+      unit_coords(args, tt, num_kb, tm_, tn_, k0_, k1_, sp_);
+      return min(TN / 64, (args.N - tn_ * TN + 63) / 64);
+    };
+    auto res_issue = [&](int tt, int uu) {  // lane 0
+      int tm_, tn_, k0_, k1_, sp_;
+      unit_coords(args, tt, num_kb, tm_, tn_, k0_, k1_, sp_);
+      const int slot = r_issued & 1;
+      mbar_arrive_expect_tx(res_bar(q, slot), 4096);
+      tma_load_2d(&tmR, rbase + (uint32_t)slot * 4096u, res_bar(q, slot), tn_ * TN + uu * 64,
+                  tm_ * 256 + (int)cta * 128 + q * 32);
+    };
+    if (args.r_tma && pid < args.num_tiles) {
+      if (lane == 0) res_issue(pid, 0);
+      ++r_issued;
+    }
     for (int t = pid; t < args.num_tiles; t += npairs, ++local) {
       const int acc = local & 1;
       const uint32_t acc_round = (uint32_t)(local >> 1);
@@ -703,13 +738,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) w[j] = __float_as_uint(v[j]);
           } else {
+            uint32_t rslot = 0;
+            if (args.r_tma) {
+              // request the next unit's residual box (this tile's next unit or the next tile's first) into
+              // the other slot, whose previous box every lane has read by now
+              int nt = t, nu = u + 1;
+              if (nu >= res_units(t)) {
+                nt = t + npairs;
+                nu = 0;
+              }
+              __syncwarp();
+              if (nt < args.num_tiles && r_ok) {
+                if (lane == 0) {
+                  fence_proxy_async();
+                  res_issue(nt, nu);
+                }
+                ++r_issued;
+              }
+              rslot = rbase + (uint32_t)(rc & 1) * 4096u;
+              if (r_ok) r_ok = mbar_wait(res_bar(q, rc & 1), (rc >> 1) & 1, BRAIN_ERR_TIMEOUT_FULL, 61, abort_flag);
+              if (r_ok) r_done = rc + 1;
+              ++rc;
+            }
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
               uint32_t r[32];
               tmem_ld32(tm_row + (uint32_t)(u * 64 + h * 32), r);
               tc_wait_ld();
               float v[32];
-              epi_math(args, gm, n0 + u * 64 + h * 32, r, v);
+              epi_math(args, gm, n0 + u * 64 + h * 32, r, v, args.r_tma != 0);
+              if (args.r_tma) {
+                // this row's 32 residual columns: 4 swizzled 16-byte pieces of the 128-byte row
+#pragma unroll
+                for (int cc = 0; cc < 4; ++cc) {
+                  uint32_t x0, x1, x2, x3;
+                  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                               : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3)
+                               : "r"(rslot + (uint32_t)lane * 128u + (uint32_t)(((h * 4 + cc) ^ (lane & 7)) << 4)));
+                  const uint32_t xs[4] = {x0, x1, x2, x3};
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xs[e]));
+                    v[cc * 8 + 2 * e] += f.x;
+                    v[cc * 8 + 2 * e + 1] += f.y;
+                  }
+                }
+              }
 #pragma unroll
               for (int j = 0; j < 16; ++j) {
                 __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
@@ -750,6 +824,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       mbar_arrive_cluster(mapa_shared(tempty_bar(acc), 0));
     }
     if (args.tma_store && lane == 0) tma_store_wait_all();
+    // residual boxes requested and not consumed (an abort): let them land before the CTA exits
+    for (int j = r_done; j < r_issued; ++j) {
+      uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(res_bar(q, j & 1), (j >> 1) & 1) && globaltimer() - t0 < 100000000ull) {
+      }
+    }
   }
 
   tc_fence_before();
@@ -835,7 +915,8 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, c
 
 template <int A_MN, int B_MN>
 int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
-               cudaStream_t st) {
+               cudaStream_t st, const CUtensorMap* tr = nullptr) {
+  static const CUtensorMap no_map{};
   auto kern = gemm_tc2_kernel<A_MN, B_MN>;
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -845,7 +926,7 @@ int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
     attr_set[dev & 63] = true;
   }
   int pairs = std::min(a.num_tiles, brain_host::num_sms() / 2);
-  kern<<<2 * pairs, kThreads, PairSmem::TOTAL, st>>>(ta, tb, tc, a);
+  kern<<<2 * pairs, kThreads, PairSmem::TOTAL, st>>>(ta, tb, tc, tr ? *tr : no_map, a);
   return (int)cudaGetLastError();
 }
 
@@ -1073,10 +1154,15 @@ int gemm_bf16_impl(const void* A, int64_t lda, int a_mn, const void* B, int64_t 
       }
     }
     a.tma_store = output_map(&tc, a) ? 1 : 0;
-    if (a_mn == 0 && b_mn == 0) return launch_tc2<0, 0>(ta, tb, tc, a, stream);
-    if (a_mn == 0 && b_mn == 1) return launch_tc2<0, 1>(ta, tb, tc, a, stream);
-    if (a_mn == 1 && b_mn == 0) return launch_tc2<1, 0>(ta, tb, tc, a, stream);
-    return launch_tc2<1, 1>(ta, tb, tc, a, stream);
+    CUtensorMap tr{};
+    if (a.tma_store && a.R && !c_f32 && ldr % 8 == 0 && (reinterpret_cast<uintptr_t>(R) & 15) == 0 &&
+        get_map_2d(&tr, R, (uint64_t)N, (uint64_t)M, (uint64_t)ldr, 64, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2))
+      a.r_tma = 1;
+    const CUtensorMap* trp = a.r_tma ? &tr : nullptr;
+    if (a_mn == 0 && b_mn == 0) return launch_tc2<0, 0>(ta, tb, tc, a, stream, trp);
+    if (a_mn == 0 && b_mn == 1) return launch_tc2<0, 1>(ta, tb, tc, a, stream, trp);
+    if (a_mn == 1 && b_mn == 0) return launch_tc2<1, 0>(ta, tb, tc, a, stream, trp);
+    return launch_tc2<1, 1>(ta, tb, tc, a, stream, trp);
   }
   const int BN = (N <= 128) ? 128 : 256;
   a.tiles_m = (M + BM - 1) / BM;

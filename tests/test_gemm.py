@@ -180,3 +180,24 @@ def test_gemm_splitk_matches_oracle(ta, tb, shape):
     torch.cuda.synchronize()
     assert torch.equal(c, c2)  # the slices are added in a fixed order
     assert _native.status("gemm")[0] == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("shape", [(300, 520, 136), (8192, 1024, 256), (4096, 768, 768), (256, 2304, 64)])
+def test_gemm_residual_by_tma_matches_oracle(shape):
+    """bf16 output with bias and residual on the CTA-pair kernel: the residual boxes arrive by TMA one
+    64-column unit ahead (across tiles too when a pair runs several); ragged edges are zero-filled."""
+    M, N, K = shape
+    a = _mk((M, K), "cuda", 41)
+    w = _mk((N, K), "cuda", 42)
+    bias = _mk((N,), "cuda", 43)
+    res = _mk((M, N), "cuda", 44)
+    y = gemm(a, w, trans_b=True, bias=bias, residual=res)
+    ref = _ref(a, w, False, True, bias=bias, residual=res)
+    torch.testing.assert_close(y.float(), ref, rtol=1e-2, atol=2e-3 * K ** 0.5 + 0.05)
+    big = torch.randn(M, N + 64, device="cuda").to(torch.bfloat16)  # residual as a strided view
+    y2 = gemm(a, w, trans_b=True, residual=big[:, 8:8 + N])
+    torch.testing.assert_close(y2.float(), _ref(a, w, False, True, residual=big[:, 8:8 + N]), rtol=1e-2,
+                               atol=2e-3 * K ** 0.5 + 0.05)
+    from brain_b200 import _native
+    assert _native.status("gemm")[0] == 0
