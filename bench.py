@@ -133,7 +133,7 @@ def main():
         return 0
 
     if args.impl == "torch":
-        return run_torch_baseline(args)
+        return run_torch_vit(args) if args.workload == "vit" else run_torch_baseline(args)
 
     import torch
     import torch.distributed as dist
@@ -387,6 +387,99 @@ def run_torch_baseline(args) -> int:
             "final_loss": float(loss.item()), "clocks": clk,
             "e2e": {"value": B * S * world / (ms2 / 1e3), "unit": "tokens/s", "ms_per_step": ms2,
                     "h2d_bytes_per_step": B * (S + 1) * 8, "d2h_bytes_per_step": 4,
+                    "api": "torch module forward/backward + optimizer.step", "last_loss": lv},
+            "impl": "torch"}), flush=True)
+    del ddp, model, opt
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def run_torch_vit(args) -> int:
+    """The ViT-B/16 config on plain PyTorch (``brain_b200.bench.torch_baseline.TorchViT``): eager modules,
+    cuBLAS, SDPA, fused torch AdamW, DistributedDataParallel over NCCL; same data, batch and timing."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from brain_b200.bench.torch_baseline import TorchViT
+    from brain_b200.models.config import ViTConfig
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    cfg = ViTConfig.vit_b16()
+    B = 256
+    model = TorchViT(cfg, dev)
+    ddp = (torch.nn.parallel.DistributedDataParallel(model, device_ids=[local], gradient_as_bucket_view=True)
+           if world > 1 else model)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-4, betas=(0.9, 0.999), eps=1e-8, weight_decay=0.05, fused=True)
+    gen = torch.Generator(device=dev).manual_seed(10 + rank)
+    pool = [(torch.randn(B, 3, cfg.image_size, cfg.image_size, device=dev, generator=gen).bfloat16(),
+             torch.randint(0, cfg.num_classes, (B,), device=dev, generator=gen)) for _ in range(2)]
+
+    def step(x, y):
+        loss = ddp(x, y)
+        loss.backward()
+        opt.step()
+        opt.zero_grad(set_to_none=False)
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    warm = max(3, args.warmup)
+    for i in range(warm):
+        loss = step(*pool[i % 2])
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        loss = step(*pool[i % 2])
+    e.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop() if clocks else None
+    ms = _max_over_ranks(s.elapsed_time(e) / args.steps, dev)
+    host = [(x.cpu().pin_memory(), y.cpu().pin_memory()) for x, y in pool]
+    xb, yb = torch.empty_like(pool[0][0]), torch.empty_like(pool[0][1])
+    barrier()
+    torch.cuda.synchronize()
+    s2, e2 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for i in range(args.steps):
+        xb.copy_(host[i % 2][0], non_blocking=True)
+        yb.copy_(host[i % 2][1], non_blocking=True)
+        lv = step(xb, yb).item()
+    e2.record()
+    torch.cuda.synchronize()
+    ms2 = _max_over_ranks(s2.elapsed_time(e2) / args.steps, dev)
+    if rank == 0:
+        print(json.dumps({
+            "metric": "train images/s ViT-B/16 DDP", "value": B * world / (ms / 1e3), "unit": "images/s",
+            "n_gpus": world, "steps": args.steps, "warmup": warm, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (images ~N(0,1), uniform labels, seeded; random-init weights)",
+            "config": {"model": "ViT-B/16", "global_batch": B * world, "image_size": cfg.image_size,
+                       "parallelism": f"dp{world}",
+                       "implementation": "plain PyTorch: eager nn modules, cuBLAS, F.scaled_dot_product_attention, "
+                                         "torch.optim.AdamW(fused=True), DDP over NCCL",
+                       "l2": "no flush: activations of 256 images >> 126 MB L2"},
+            "final_loss": float(loss.item()), "clocks": clk,
+            "e2e": {"value": B * world / (ms2 / 1e3), "unit": "images/s", "ms_per_step": ms2,
+                    "h2d_bytes_per_step": B * 3 * cfg.image_size ** 2 * 2 + B * 8, "d2h_bytes_per_step": 4,
                     "api": "torch module forward/backward + optimizer.step", "last_loss": lv},
             "impl": "torch"}), flush=True)
     del ddp, model, opt

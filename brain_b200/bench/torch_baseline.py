@@ -156,3 +156,61 @@ class MasterAdamW:
                     p.grad = None
                 else:
                     p.grad.zero_()
+
+
+class _VitBlock(nn.Module):
+    """Pre-norm encoder block: LayerNorm, fused-QKV attention through F.scaled_dot_product_attention, tanh
+    GELU MLP; every Linear with a bias (cuBLAS)."""
+
+    def __init__(self, d, heads, mlp, eps, device, dtype):
+        super().__init__()
+        kw = dict(device=device, dtype=dtype)
+        self.heads = heads
+        self.n1 = nn.LayerNorm(d, eps=eps, **kw)
+        self.qkv = nn.Linear(d, 3 * d, **kw)
+        self.proj = nn.Linear(d, d, **kw)
+        self.n2 = nn.LayerNorm(d, eps=eps, **kw)
+        self.fc1 = nn.Linear(d, mlp, **kw)
+        self.fc2 = nn.Linear(mlp, d, **kw)
+
+    def forward(self, x):
+        B, S, D = x.shape
+        q, k, v = self.qkv(self.n1(x)).view(B, S, 3, self.heads, D // self.heads).permute(2, 0, 3, 1, 4)
+        o = F.scaled_dot_product_attention(q, k, v)
+        x = x + self.proj(o.transpose(1, 2).reshape(B, S, D))
+        return x + self.fc2(F.gelu(self.fc1(self.n2(x)), approximate="tanh"))
+
+
+class TorchViT(nn.Module):
+    """ViT-B/16 in plain PyTorch for the comparison arm: patch embedding as one Linear over the 16x16
+    patches (a stride-16 convolution), class token, learned positions, 12 pre-norm blocks, final
+    LayerNorm, linear head on the class token; the same architecture as ``models.families.ViT``."""
+
+    def __init__(self, cfg, device, dtype=torch.bfloat16):
+        super().__init__()
+        self.cfg = cfg
+        P, d = cfg.patch_size, cfg.hidden_dim
+        kw = dict(device=device, dtype=dtype)
+        self.patch = nn.Linear(cfg.in_channels * P * P, d, **kw)
+        self.cls_token = nn.Parameter(torch.zeros(1, 1, d, **kw))
+        self.pos = nn.Parameter(torch.zeros(1, cfg.num_patches + 1, d, **kw))
+        self.blocks = nn.ModuleList([_VitBlock(d, cfg.num_heads, cfg.mlp_dim, cfg.norm_eps, device, dtype)
+                                     for _ in range(cfg.num_layers)])
+        self.norm = nn.LayerNorm(d, eps=cfg.norm_eps, **kw)
+        self.head = nn.Linear(d, cfg.num_classes, **kw)
+        g = torch.Generator(device="cpu").manual_seed(0)
+        with torch.no_grad():
+            for name, p in self.named_parameters():
+                if p.dim() >= 2 or name in ("cls_token", "pos"):
+                    p.copy_((torch.randn(p.shape, generator=g) * 0.02).to(dtype))
+
+    def forward(self, images, labels):
+        B, C, H, W = images.shape
+        P = self.cfg.patch_size
+        x = images.reshape(B, C, H // P, P, W // P, P).permute(0, 2, 4, 1, 3, 5).reshape(B, -1, C * P * P)
+        x = self.patch(x)
+        x = torch.cat([self.cls_token.expand(B, -1, -1), x], 1) + self.pos
+        for blk in self.blocks:
+            x = blk(x)
+        logits = self.head(self.norm(x)[:, 0])
+        return F.cross_entropy(logits.float(), labels)

@@ -504,4 +504,24 @@ __device__ __forceinline__ float ex2_fast(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
+// tanh with the hardware approximation (tanh.approx.f32, about 2^-11 relative error: below bf16 rounding).
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// tanh-approximate GELU, 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), and its derivative, for GEMM
+// epilogues (the standalone elementwise kernels use the same formula).
+__device__ __forceinline__ float gelu_tanh_fast(float x) {
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+  return 0.5f * x * (1.f + tanh_fast(u));
+}
+__device__ __forceinline__ float gelu_tanh_grad_fast(float x) {
+  const float x2 = x * x;
+  const float u = 0.7978845608028654f * fmaf(0.044715f * x, x2, x);
+  const float t = tanh_fast(u);
+  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * 0.7978845608028654f * fmaf(3.f * 0.044715f, x2, 1.f);
+}
 }  // namespace brain

@@ -63,9 +63,14 @@ struct GemmArgs {
   // over k-blocks [s * kb_split, (s + 1) * kb_split) with s = t / (tiles_m * tiles_n); its raw f32 sums go
   // to rows [s * split_rows, ...) of the workspace C, and a second kernel adds the slices in order.
   int splits, kb_split, split_rows;
-  // CTA-pair TMA-store epilogue with a bf16 output: the residual tile arrives by TMA (tmR) into per-warp
-  // swizzled buffers one 64-column unit ahead, instead of per-row global loads
-  int r_tma;
+  // CTA-pair TMA-store epilogue with a bf16 output: the residual tile arrives by TMA (extra map tmE) into
+  // per-warp swizzled buffers one 64-column unit ahead, instead of per-row global loads. r_op 0 adds it;
+  // r_op 1 multiplies the product by gelu'(R) (the data gradient of a GELU MLP's first layer, R = its
+  // pre-activation)
+  int r_tma, r_op;
+  // dual output (CTA-pair TMA-store, bf16): C = the product (+ bias) and a second matrix (map tmE, same
+  // shape) = gelu(C): the first layer of a GELU MLP keeps its pre-activation and feeds the second layer
+  int dual_gelu;
 };
 
 template <int BN, int STAGES>
@@ -459,7 +464,7 @@ struct PairSmem {
 template <int A_MN, int B_MN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, GemmArgs args) {
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmE, GemmArgs args) {
   using S = PairSmem;
   constexpr int ST = kPairStages;
   constexpr int TN = 256;  // pair tile: 256 x 256
@@ -498,7 +503,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if (args.tma_store) prefetch_tmap(&tmC);
-    if (args.r_tma) prefetch_tmap(&tmR);
+    if (args.r_tma || args.dual_gelu) prefetch_tmap(&tmE);
   }
   if (warp == 1) {
     tmem_alloc_pair(smem_u32(tmem_slot), 512);
@@ -627,7 +632,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       unit_coords(args, tt, num_kb, tm_, tn_, k0_, k1_, sp_);
       const int slot = r_issued & 1;
       mbar_arrive_expect_tx(res_bar(q, slot), 4096);
-      tma_load_2d(&tmR, rbase + (uint32_t)slot * 4096u, res_bar(q, slot), tn_ * TN + uu * 64,
+      tma_load_2d(&tmE, rbase + (uint32_t)slot * 4096u, res_bar(q, slot), tn_ * TN + uu * 64,
                   tm_ * 256 + (int)cta * 128 + q * 32);
     };
     if (args.r_tma && pid < args.num_tiles) {
@@ -779,8 +784,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                   for (int e = 0; e < 4; ++e) {
                     const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xs[e]));
-                    v[cc * 8 + 2 * e] += f.x;
-                    v[cc * 8 + 2 * e + 1] += f.y;
+                    if (args.r_op == 0) {
+                      v[cc * 8 + 2 * e] += f.x;
+                      v[cc * 8 + 2 * e + 1] += f.y;
+                    } else {
+                      v[cc * 8 + 2 * e] *= gelu_tanh_grad_fast(f.x);
+                      v[cc * 8 + 2 * e + 1] *= gelu_tanh_grad_fast(f.y);
+                    }
                   }
                 }
               }
@@ -788,6 +798,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               for (int j = 0; j < 16; ++j) {
                 __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * j], v[2 * j + 1]);
                 w[h * 16 + j] = *reinterpret_cast<uint32_t*>(&b2);
+              }
+              if (args.dual_gelu) {
+                // gelu of the bf16-rounded pre-activation (what the backward pass reads back), staged in
+                // this unit's slot of the residual buffers and stored by a second TMA store
+                uint32_t g[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[h * 16 + j]));
+                  __nv_bfloat162 b2 = __floats2bfloat162_rn(gelu_tanh_fast(f.x), gelu_tanh_fast(f.y));
+                  g[j] = *reinterpret_cast<uint32_t*>(&b2);
+                }
+                if (h == 0 && lane == 0) tma_store_wait_read<1>();
+                __syncwarp();
+                const uint32_t gb = rbase + (uint32_t)ebuf * 4096u + (uint32_t)lane * 128u;
+#pragma unroll
+                for (int c = 0; c < 4; ++c)
+                  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(gb + (uint32_t)(((h * 4 + c) ^ (lane & 7)) << 4)),
+                               "r"(g[4 * c]), "r"(g[4 * c + 1]), "r"(g[4 * c + 2]), "r"(g[4 * c + 3])
+                               : "memory");
               }
             }
           }
@@ -803,6 +832,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) {
             tma_store_2d(&tmC, stg + (uint32_t)ebuf * 4096u, n0 + u * cols, row0);
+            if (args.dual_gelu) tma_store_2d(&tmE, rbase + (uint32_t)ebuf * 4096u, n0 + u * cols, row0);
             tma_store_commit();
           }
           ebuf ^= 1;
@@ -1028,6 +1058,24 @@ BRAIN_API int brain_gemm_set_pair_mode(int mode) {
   return old;
 }
 
+
+namespace {
+// A / B tensor maps of the CTA-pair kernel (each CTA stages 128 rows of A and 128 columns of B per k-block).
+bool pair_maps(const void* A, int64_t lda, int a_mn, const void* B, int64_t ldb, int b_mn, int M, int N, int K,
+               CUtensorMap* ta, CUtensorMap* tb) {
+  bool ok = a_mn ? get_map_2d(ta, A, (uint64_t)M, (uint64_t)K, (uint64_t)lda, 64, BK, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2)
+                 : get_map_2d(ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, BK, 128, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2);
+  return ok && (b_mn ? get_map_2d(tb, B, (uint64_t)N, (uint64_t)K, (uint64_t)ldb, 64, BK,
+                                  CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2)
+                     : get_map_2d(tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, BK, 128,
+                                  CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2));
+}
+
+bool pair_aligned(const void* A, int64_t lda, const void* B, int64_t ldb, int K) {
+  return (lda % 8 == 0) && (ldb % 8 == 0) && ((reinterpret_cast<uintptr_t>(A) & 15) == 0) &&
+         ((reinterpret_cast<uintptr_t>(B) & 15) == 0) && K >= 16;
+}
+}  // namespace
 
 // Split-K plan for the CTA-pair kernel: returns the number of K slices (1 = no split) and the k-blocks per
 // slice. Splitting pays when the output has fewer 256 x 256 tiles than there are SM pairs (weight gradients
@@ -1280,4 +1328,56 @@ BRAIN_API int brain_gemm_bf16_tp(const void* A, int64_t lda, const void* B, int6
   if (!ok) return (int)cudaErrorInvalidValue;
   if (BN == 128) return b_mn ? launch_tc<128, 6, 0, 1>(ta, tb, a, stream) : launch_tc<128, 6, 0, 0>(ta, tb, a, stream);
   return b_mn ? launch_tc<256, 4, 0, 1>(ta, tb, a, stream) : launch_tc<256, 4, 0, 0>(ta, tb, a, stream);
+}
+
+// GELU MLP first layer: C = A B^T (+ bias) and C2 = gelu(C), both bf16 [M, N] (A [M, K], B [N, K] row-major),
+// in one CTA-pair GEMM with two TMA stores per output unit. cudaErrorNotSupported (nothing launched) when the
+// pair path cannot run (M or N < 256, misaligned operands or outputs); the caller then runs the GEMM and the
+// activation separately.
+BRAIN_API int brain_gemm_bf16_gelu_dual(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                                        void* C2, int64_t ldc2, int M, int N, int K, const void* bias,
+                                        cudaStream_t stream) {
+  if (!g_pair_mode || M < 256 || N < 256 || !pair_aligned(A, lda, B, ldb, K)) return (int)cudaErrorNotSupported;
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K;
+  a.C = C; a.ldc = ldc; a.alpha = 1.f;
+  a.bias = reinterpret_cast<const __nv_bfloat16*>(bias);
+  a.tiles_m = (M + 255) / 256;
+  a.tiles_n = (N + 255) / 256;
+  a.num_tiles = a.tiles_m * a.tiles_n;
+  CUtensorMap ta, tb, tc, t2;
+  if (!pair_maps(A, lda, 0, B, ldb, 0, M, N, K, &ta, &tb) || !output_map(&tc, a)) return (int)cudaErrorNotSupported;
+  GemmArgs a2 = a;
+  a2.C = C2; a2.ldc = ldc2;
+  if (!output_map(&t2, a2)) return (int)cudaErrorNotSupported;
+  a.tma_store = 1;
+  a.dual_gelu = 1;
+  return launch_tc2<0, 0>(ta, tb, tc, a, stream, &t2);
+}
+
+// GELU MLP data gradient through the activation: C = (A op(B)) * gelu'(H), bf16 [M, N]; A [M, K] row-major,
+// B [K, N] (b_mn = 1, the second layer's weight read in place) or [N, K]; H [M, N] the saved pre-activation
+// (row stride ldh). cudaErrorNotSupported as above.
+BRAIN_API int brain_gemm_bf16_gelu_grad(const void* A, int64_t lda, const void* B, int64_t ldb, int b_mn, void* C,
+                                        int64_t ldc, const void* H, int64_t ldh, int M, int N, int K,
+                                        cudaStream_t stream) {
+  if (!g_pair_mode || M < 256 || N < 256 || !pair_aligned(A, lda, B, ldb, K) || ldh % 8 != 0 ||
+      (reinterpret_cast<uintptr_t>(H) & 15))
+    return (int)cudaErrorNotSupported;
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K;
+  a.C = C; a.ldc = ldc; a.alpha = 1.f;
+  a.tiles_m = (M + 255) / 256;
+  a.tiles_n = (N + 255) / 256;
+  a.num_tiles = a.tiles_m * a.tiles_n;
+  CUtensorMap ta, tb, tc, th;
+  if (!pair_maps(A, lda, 0, B, ldb, b_mn, M, N, K, &ta, &tb) || !output_map(&tc, a) ||
+      !get_map_2d(&th, H, (uint64_t)N, (uint64_t)M, (uint64_t)ldh, 64, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2))
+    return (int)cudaErrorNotSupported;
+  a.tma_store = 1;
+  a.R = reinterpret_cast<const __nv_bfloat16*>(H);  // read only through the map (r_tma)
+  a.ldr = ldh;
+  a.r_tma = 1;
+  a.r_op = 1;
+  return b_mn ? launch_tc2<0, 1>(ta, tb, tc, a, stream, &th) : launch_tc2<0, 0>(ta, tb, tc, a, stream, &th);
 }

@@ -197,10 +197,13 @@ class FeedForward(Module):
     """Transformer FFN: gated (SwiGLU over a fused gate/up weight) or plain (GELU)."""
 
     def __init__(self, dim: int, hidden: int, gated: bool = True, bias: bool = False, device=None, dtype=None,
-                 act: str = "gelu"):
+                 act: str = "gelu", fused_gelu: bool = False):
         super().__init__()
         self.gated = gated
         self.act = act
+        # GELU inside the GEMM epilogues (``ops.gelu_mlp``). Off by default: at d_model 768 the four epilogue
+        # warps of the GEMM become the bottleneck and the fused pair measured slower than GEMM + activation.
+        self.fused_gelu = fused_gelu
         if gated:
             self.gate_up = Linear(dim, 2 * hidden, bias=bias, device=device, dtype=dtype)
         else:
@@ -212,6 +215,8 @@ class FeedForward(Module):
             if self.down.bias is None:
                 return ops.swiglu_linear(self.gate_up(x), self.down.weight, residual)
             return self.down(ops.swiglu(self.gate_up(x)), residual)
+        if self.act == "gelu" and self.fused_gelu:
+            return ops.gelu_mlp(x, self.up.weight, self.up.bias, self.down.weight, self.down.bias, residual)
         h = self.up(x)
         h = torch.relu(h) if self.act == "relu" else ops.gelu(h)
         return self.down(h, residual)

@@ -10,7 +10,7 @@ from .norms import rms_norm, layer_norm, add_rms_norm, add_layer_norm, fused_lay
 from .activations import swiglu, gelu  # noqa: F401
 from .rope import rope_table, apply_rope, apply_rope_  # noqa: F401
 from .attention import flash_attention, flash_attention_fwd, qkv_attention, sdpa_ref  # noqa: F401
-from .linear import linear, norm_linear, swiglu_linear  # noqa: F401
+from .linear import linear, norm_linear, swiglu_linear, gelu_mlp  # noqa: F401
 from .cross_entropy import cross_entropy, linear_cross_entropy  # noqa: F401
 from .embedding import embedding  # noqa: F401
 from .decode import paged_decode_attention, kv_append_rope  # noqa: F401

@@ -14,6 +14,8 @@ _native.register({
     "brain_norm_bwd_partials": ("brain_kernels", "i"),
     "brain_colsum_partials": ("brain_kernels", "i"),
     "brain_colsum_bf16": ("brain_kernels", "pliipiips"),
+    "brain_gemm_bf16_gelu_dual": ("brain_kernels", "plplplpliiips"),
+    "brain_gemm_bf16_gelu_grad": ("brain_kernels", "plpliplpliiis"),
     "brain_norm_bwd": ("brain_kernels", "iplplpppplplppiipiis"),
     "brain_swiglu_fwd": ("brain_kernels", "plpllis"),
     "brain_swiglu_bwd": ("brain_kernels", "plplpllis"),

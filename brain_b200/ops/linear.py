@@ -187,3 +187,78 @@ def swiglu_linear(gu, w, residual=None):
         return _SwiGLULinearFn.apply(gu, w, residual)
     from .activations import swiglu_ref
     return linear(swiglu_ref(gu), w, residual=residual)
+
+
+_NOT_SUPPORTED = 801  # cudaErrorNotSupported: the fused GEMM does not apply to this shape
+
+
+def _gelu_dual(x2, w1, b1):
+    """(h, gelu(h)) with h = x2 @ w1.T (+ b1): one GEMM with two outputs when it applies."""
+    M, K = x2.shape
+    F = w1.shape[0]
+    h = torch.empty(M, F, device=x2.device, dtype=torch.bfloat16)
+    a = torch.empty_like(h)
+    rc = _native.fn("brain_gemm_bf16_gelu_dual")(
+        x2.data_ptr(), x2.stride(0), w1.data_ptr(), w1.stride(0), h.data_ptr(), h.stride(0), a.data_ptr(),
+        a.stride(0), M, F, K, b1.data_ptr() if b1 is not None else None, _native.stream_ptr(x2.device))
+    if rc == _NOT_SUPPORTED:
+        from .activations import gelu
+        h = gemm(x2, w1, trans_b=True, bias=b1)
+        return h, gelu(h)
+    if rc != 0:
+        raise _native.NativeError(f"brain_gemm_bf16_gelu_dual failed with status {rc}")
+    return h, a
+
+
+def _gelu_grad(dy2, w2, h):
+    """(dy2 @ w2) * gelu'(h): the second layer's data gradient through the activation, one GEMM when it applies."""
+    M, D = dy2.shape
+    F = w2.shape[1]
+    dh = torch.empty(M, F, device=dy2.device, dtype=torch.bfloat16)
+    rc = _native.fn("brain_gemm_bf16_gelu_grad")(
+        dy2.data_ptr(), dy2.stride(0), w2.data_ptr(), w2.stride(0), 1, dh.data_ptr(), dh.stride(0), h.data_ptr(),
+        h.stride(0), M, F, D, _native.stream_ptr(dy2.device))
+    if rc == _NOT_SUPPORTED:
+        da = gemm(dy2, w2)
+        _native.call("brain_gelu_bwd", da.data_ptr(), h.data_ptr(), dh.data_ptr(), dh.numel(),
+                     _native.stream_ptr(dy2.device))
+        return dh
+    if rc != 0:
+        raise _native.NativeError(f"brain_gemm_bf16_gelu_grad failed with status {rc}")
+    return dh
+
+
+class _GeluMLPFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w1, b1, w2, b2, residual):
+        x2 = rows2d(x)
+        h, a = _gelu_dual(x2, w1, b1)
+        r2 = rows2d(residual) if residual is not None else None
+        y = gemm(a, w2, trans_b=True, bias=b2, residual=r2)
+        ctx.save_for_backward(x2, w1, b1, h, a, w2, b2)
+        ctx.xshape = x.shape
+        ctx.has_res = residual is not None
+        return y.view(*x.shape[:-1], w2.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, w1, b1, h, a, w2, b2 = ctx.saved_tensors
+        dy2 = rows2d(dy).contiguous()
+        nig = ctx.needs_input_grad
+        dw2 = _wgrad(dy2, a, w2) if nig[3] else None
+        db2 = _bgrad(dy2, b2) if (b2 is not None and nig[4]) else None
+        dh = _gelu_grad(dy2, w2, h)
+        dx = gemm(dh, w1).view(ctx.xshape) if nig[0] else None
+        dw1 = _wgrad(dh, x2, w1) if nig[1] else None
+        db1 = _bgrad(dh, b1) if (b1 is not None and nig[2]) else None
+        return dx, dw1, db1, dw2, db2, (dy if ctx.has_res else None)
+
+
+def gelu_mlp(x, w1, b1, w2, b2, residual=None):
+    """gelu(x @ w1.T + b1) @ w2.T + b2 (+ residual) with tanh GELU (the plain transformer MLP). On CUDA the
+    first GEMM also writes gelu of its output (two TMA stores per tile), and the second layer's data
+    gradient applies gelu' in its epilogue, so the activation costs no separate pass either way."""
+    if x.is_cuda and x.dtype == torch.bfloat16:
+        return _GeluMLPFn.apply(x, w1, b1, w2, b2, residual)
+    from .activations import gelu
+    return linear(gelu(linear(x, w1, b1)), w2, b2, residual)

@@ -460,3 +460,32 @@ def test_colsum_bias_grad_matches_fp32(M, N, out_dtype):
     colsum_(x, out2)
     assert torch.equal(out, out2)  # fixed summation order
     assert ops.check_status() == []
+
+
+@gpu
+@pytest.mark.parametrize("M,D,F,res", [(600, 768, 3072, True), (4096, 256, 1024, False), (100, 64, 128, True)])
+def test_gelu_mlp_fused_matches_fp32(M, D, F, res):
+    """GELU MLP with the first GEMM writing h and gelu(h) and the data gradient applying gelu' in the second
+    layer's backward GEMM (shapes below 256 take the unfused path); forward and all gradients against fp32."""
+    from brain_b200.ops.linear import gelu_mlp
+    g = torch.Generator(device="cpu").manual_seed(M + F)
+    mk = lambda *s, sc=1.0: (torch.randn(*s, generator=g) * sc).to("cuda", torch.bfloat16).requires_grad_()
+    x, w1, b1 = mk(M, D), mk(F, D, sc=D ** -0.5), mk(F, sc=0.1)
+    w2, b2 = mk(D, F, sc=F ** -0.5), mk(D, sc=0.1)
+    r = mk(M, D) if res else None
+    y = gelu_mlp(x, w1, b1, w2, b2, r)
+    dy = torch.randn(M, D, generator=g).to("cuda", torch.bfloat16)
+    y.backward(dy)
+    leaves = [x, w1, b1, w2, b2] + ([r] if res else [])
+    ref_leaves = [t.detach().float().requires_grad_() for t in leaves]
+    xr, w1r, b1r, w2r, b2r = ref_leaves[:5]
+    yr = torch.nn.functional.gelu(xr @ w1r.t() + b1r, approximate="tanh") @ w2r.t() + b2r
+    if res:
+        yr = yr + ref_leaves[5]
+    yr.backward(dy.float())
+    def rel(a, b):
+        return float((a.float() - b).norm() / b.norm())
+    assert rel(y, yr) < 1e-2
+    for t, tr in zip(leaves, ref_leaves):
+        assert rel(t.grad, tr.grad) < 2e-2, (t.shape, rel(t.grad, tr.grad))
+    assert ops.check_status() == []

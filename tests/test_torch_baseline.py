@@ -40,3 +40,26 @@ def test_master_adamw_matches_float32_adamw():
     for a, b in zip(p16, p32):
         torch.testing.assert_close(a.float(), b.detach().bfloat16().float())
         torch.testing.assert_close(opt.master[id(a)].detach(), b.detach(), rtol=1e-5, atol=1e-6)
+
+
+def test_torch_vit_arm_matches_framework_architecture():
+    """The ViT comparison arm has the framework ViT's parameter count and trains on CPU."""
+    import torch
+    from brain_b200.bench.torch_baseline import TorchViT
+    from brain_b200.models.config import ViTConfig
+    from brain_b200.models.families import ViT
+    cfg = ViTConfig(image_size=32, patch_size=16, hidden_dim=64, num_layers=2, num_heads=4, mlp_dim=128,
+                    num_classes=10)
+    tv = TorchViT(cfg, "cpu", dtype=torch.float32)
+    fv = ViT(cfg, device="cpu", dtype=torch.float32)
+    assert sum(p.numel() for p in tv.parameters()) == sum(p.numel() for p in fv.parameters())
+    x = torch.randn(4, 3, 32, 32)
+    y = torch.randint(0, 10, (4,))
+    opt = torch.optim.AdamW(tv.parameters(), lr=1e-3)
+    l0 = tv(x, y)
+    for _ in range(5):
+        opt.zero_grad()
+        loss = tv(x, y)
+        loss.backward()
+        opt.step()
+    assert torch.isfinite(loss) and loss.item() < l0.item()
