@@ -32,6 +32,7 @@ SIGNATURES: dict[str, tuple[str, str]] = {
     "brain_gemm_bf16": ("brain_kernels", "pliplipliiiififpplis"),
     "brain_status_gemm": ("brain_kernels", "pi"),
     "brain_gemm_set_pair_mode": ("brain_kernels", "i"),
+    "brain_gemm_set_push_stage": ("brain_kernels", "i"),
     "brain_gemm_bf16_rope": ("brain_kernels", "plplpliiipiiiis"),
     "brain_gemm_bf16_ws": ("brain_kernels", "pliplipliiiififpplpls"),
     "brain_gemm_splitk_plan": ("brain_kernels", "iiip"),

@@ -17,6 +17,24 @@ import torch
 import torch.distributed as dist
 
 
+def _peaks() -> dict:
+    """Roofline denominators: the measured cuBLAS bf16 burst (MEASURED_PEAKS.json next to the package, else
+    1,590 TFLOP/s) and 770 GB/s per direction for a peer copy over NVLink."""
+    import os
+    out = {"bf16_tflops": 1590.0, "nvlink_gbs": 770.0}
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                        "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        v = d.get("bf16_tflops") or d.get("cublas_bf16_tflops")
+        if isinstance(v, (int, float)) and v > 0:
+            out["bf16_tflops"] = float(v)
+    except (OSError, ValueError):
+        pass
+    return out
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens-per-rank", type=int, default=8192)
@@ -69,10 +87,21 @@ def main(argv=None) -> int:
                M=T * W, N=qkv, K=d)
     tp.ag_copy = "sm"
     report("local_gemm_o_all_rows", timed(lambda: gemm(a_full, w_o, trans_b=True)), 0, M=T * W, N=d, K=attn)
-    for mode in ("pull", "push"):
-        tp.rs_mode = mode
-        report(f"gemm_rs_{mode}_o", timed(lambda: gemm_push(tp, a_full, w_o, 1, T)), (W - 1) * T * d * 2,
-               M=T * W, N=d, K=attn)
+    from .. import _native
+    peaks = _peaks()
+    flops_o = 2.0 * T * W * d * attn
+    for mode in ("pull", "push", "push_rowstore"):
+        # pull: GEMM into symmetric memory, barrier, each rank pulls and sums its rows; push: the GEMM
+        # epilogue stores each row block into its owner's slot from the shared-memory staging (owner-rotated
+        # tile order), barrier, local sum; push_rowstore: the same push with per-row stores
+        tp.rs_mode = "pull" if mode == "pull" else "push"
+        old = _native.fn("brain_gemm_set_push_stage")(0 if mode == "push_rowstore" else 1)
+        ms = timed(lambda: gemm_push(tp, a_full, w_o, 1, T))
+        _native.fn("brain_gemm_set_push_stage")(old)
+        nbytes = (W - 1) * T * d * 2
+        target = max(flops_o / (peaks["bf16_tflops"] * 1e12), nbytes / (peaks["nvlink_gbs"] * 1e9)) * 1e3
+        report(f"gemm_rs_{mode}_o", ms, nbytes, M=T * W, N=d, K=attn, roofline_ms=round(target, 3),
+               roofline_fraction=round(target / ms, 3))
     tp.rs_mode = "pull"
     report("all_gather_rows", timed(lambda: all_gather_rows(tp, x)), (W - 1) * T * d * 2)
     # block-scaled fp8 row-parallel Linear d x d (K split over ranks), GEMM -> reduce-scatter

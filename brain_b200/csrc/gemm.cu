@@ -51,6 +51,11 @@ struct GemmArgs {
   int push_chunk_rows;
   int64_t push_slot_elems;
   __nv_bfloat16* push_dst[8];
+  // CTA-pair kernel: the pushed rows leave through the swizzled staging buffer, each warp writing its
+  // 32 rows x 128 B with coalesced 16-byte stores (4 rows of 128 B per instruction), and tile rows are
+  // visited from owner push_rank + 1 on (push_rot = that shift in tile rows), so at any time the ranks
+  // push to different owners and a rank's own rows come last
+  int push_stage, push_rot;
   // CTA-pair kernel: the output tile leaves through shared memory and TMA stores (tmC) instead of
   // per-thread row stores
   int tma_store;
@@ -107,6 +112,7 @@ __device__ __forceinline__ void unit_coords(const GemmArgs& a, int t, int num_kb
     kb1 = min(num_kb, kb0 + a.kb_split);
   }
   tile_coords(t, a.tiles_m, a.tiles_n, tm, tn);
+  if (a.push_rot) tm = (tm + a.push_rot) % a.tiles_m;
 }
 
 __device__ __forceinline__ void store_chunk_at(const GemmArgs& args, int gm, int gn0, const uint32_t* r, void* cbase,
@@ -502,7 +508,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
-    if (args.tma_store) prefetch_tmap(&tmC);
+    if (args.tma_store && !args.push_stage) prefetch_tmap(&tmC);
     if (args.r_tma || args.dual_gelu) prefetch_tmap(&tmE);
   }
   if (warp == 1) {
@@ -820,7 +826,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
               }
             }
           }
-          if (lane == 0) tma_store_wait_read<1>();
+          if (lane == 0 && !args.push_stage) tma_store_wait_read<1>();
           __syncwarp();
           const uint32_t sb = stg + (uint32_t)ebuf * 4096u + (uint32_t)lane * 128u;
 #pragma unroll
@@ -828,6 +834,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(sb + (uint32_t)((c ^ (lane & 7)) << 4)),
                          "r"(w[4 * c]), "r"(w[4 * c + 1]), "r"(w[4 * c + 2]), "r"(w[4 * c + 3])
                          : "memory");
+          if (args.push_stage) {
+            // the warp's 32 staged rows to their owners: lane l takes 16-byte piece l % 8 of rows l / 8 + 4 i
+            __syncwarp();
+            const uint32_t buf = stg + (uint32_t)ebuf * 4096u;
+            const int gn = n0 + u * cols + (lane & 7) * 8;
+#pragma unroll 2
+            for (int i = 0; i < 8; ++i) {
+              const int rr = i * 4 + (lane >> 3);
+              const int gmr = row0 + rr;
+              if (gmr >= args.M || gn >= args.N) continue;
+              uint32_t x0, x1, x2, x3;
+              asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+                           : "=r"(x0), "=r"(x1), "=r"(x2), "=r"(x3)
+                           : "r"(buf + (uint32_t)rr * 128u + (uint32_t)((((lane & 7) ^ (rr & 7))) << 4)));
+              const uint4 v4 = make_uint4(x0, x1, x2, x3);
+              if (args.push == 1) {
+                const int j = gmr / args.push_chunk_rows;
+                __nv_bfloat16* d = args.push_dst[j] + (int64_t)args.push_rank * args.push_slot_elems +
+                                   (int64_t)(gmr - j * args.push_chunk_rows) * args.ldc + gn;
+                *reinterpret_cast<uint4*>(d) = v4;
+              } else {
+                for (int jj = 0; jj < args.push_world; ++jj) {
+                  const int dd = (args.push_rank + 1 + jj) % args.push_world;
+                  __nv_bfloat16* d = args.push_dst[dd] + (int64_t)args.push_rank * args.push_slot_elems +
+                                     (int64_t)gmr * args.ldc + gn;
+                  *reinterpret_cast<uint4*>(d) = v4;
+                }
+              }
+            }
+            __syncwarp();  // every lane has read the buffer before a later unit rewrites it
+            ebuf ^= 1;
+            continue;
+          }
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
@@ -1048,7 +1087,15 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
 BRAIN_STATUS_READER(gemm)
 
 namespace {
-int g_pair_mode = 1;  // 1: CTA-pair kernel for M, N >= 256; 0: single-CTA kernel only
+int g_pair_mode = 1;   // 1: CTA-pair kernel for M, N >= 256; 0: single-CTA kernel only
+int g_push_stage = 1;  // 1: pushed GEMM rows leave through shared-memory staging (coalesced); 0: per-row stores
+}
+
+// Select how the CTA-pair kernel pushes rows to peers (tests compare both); returns the previous mode.
+BRAIN_API int brain_gemm_set_push_stage(int mode) {
+  const int old = g_push_stage;
+  g_push_stage = mode;
+  return old;
 }
 
 // Select the GEMM kernel family (tests exercise both); returns the previous mode.
@@ -1313,6 +1360,13 @@ BRAIN_API int brain_gemm_bf16_tp(const void* A, int64_t lda, const void* B, int6
     if (!ok) return (int)cudaErrorInvalidValue;
     CUtensorMap tc{};
     a.tma_store = output_map(&tc, a) ? 1 : 0;
+    if (a.push && g_push_stage && N % 8 == 0 && ldc % 8 == 0) {
+      // staged push (no TMA store: tc stays unused)
+      a.tma_store = 1;
+      a.push_stage = 1;
+      if (a.push == 1 && a.push_chunk_rows % 256 == 0 && a.push_chunk_rows < M)
+        a.push_rot = ((push_rank + 1) * (a.push_chunk_rows / 256)) % a.tiles_m;
+    }
     return b_mn ? launch_tc2<0, 1>(ta, tb, tc, a, stream) : launch_tc2<0, 0>(ta, tb, tc, a, stream);
   }
   const int BN = (N <= 128) ? 128 : 256;

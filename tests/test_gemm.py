@@ -124,23 +124,34 @@ def _tp_call(A, lda, B, ldb, b_mn, C, ldc, push_peers, mode, rank, world, push_c
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("staged", [1, 0])
 @pytest.mark.parametrize("mode", [1, 2])
-@pytest.mark.parametrize("M,N", [(256, 384), (512, 256), (256, 128)])
-def test_gemm_push_local_slots(mode, M, N):
-    """GEMM -> reduce-scatter (mode 1) / all-reduce (mode 2) pushes into W local receive buffers."""
-    K, W, rank = 256, 2, 1
+@pytest.mark.parametrize("M,N,W,rank", [(256, 384, 2, 1), (512, 256, 2, 1), (256, 128, 2, 1), (2048, 768, 4, 2),
+                                        (3072, 520, 4, 3)])
+def test_gemm_push_local_slots(staged, mode, M, N, W, rank):
+    """GEMM -> reduce-scatter (mode 1) / all-reduce (mode 2) pushes into W local receive buffers: through the
+    shared-memory staging with owner-rotated tile order (staged 1) or with per-row stores (staged 0)."""
+    from brain_b200 import _native
+    K = 256
     a, w = _mk((M, K), "cuda", 30), _mk((N, K), "cuda", 31)
     rows = M // W if mode == 1 else M
     slot = rows * N
     recv = [torch.zeros(W * slot, device="cuda", dtype=torch.bfloat16) for _ in range(W)]
-    _tp_call(a.data_ptr(), K, w, K, 0, 0, N, [r.data_ptr() for r in recv], mode, rank, W, rows if mode == 1 else M,
-             slot, M, N, K)
+    old = _native.fn("brain_gemm_set_push_stage")(staged)
+    try:
+        _tp_call(a.data_ptr(), K, w, K, 0, 0, N, [r.data_ptr() for r in recv], mode, rank, W,
+                 rows if mode == 1 else M, slot, M, N, K)
+        torch.cuda.synchronize()
+    finally:
+        _native.fn("brain_gemm_set_push_stage")(old)
     ref = a.float() @ w.float().t()
     for j in range(W):
         got = recv[j][rank * slot:(rank + 1) * slot].view(rows, N).float()
         exp = ref[j * rows:(j + 1) * rows] if mode == 1 else ref
         torch.testing.assert_close(got, exp, rtol=2e-2, atol=2e-1)
-        assert recv[j][(1 - rank) * slot:(2 - rank) * slot].abs().sum().item() == 0
+        others = torch.cat([recv[j][:rank * slot], recv[j][(rank + 1) * slot:]])
+        assert others.abs().sum().item() == 0  # nothing outside this rank's slot
+    assert _native.status("gemm")[0] == 0
 
 
 @pytest.mark.gpu
