@@ -124,6 +124,8 @@ def main():
     ap.add_argument("--torch-master", default="bf16", choices=["bf16", "fp32"],
                     help="--impl torch optimizer: fused AdamW on the bf16 parameters, or float32 master weights "
                          "and moments sharded ZeRO-1 style (the framework's precision)")
+    ap.add_argument("--torch-graph", default="on", choices=["on", "off"],
+                    help="--impl torch --workload decode: replay the decode step from a CUDA graph, or run it eagerly")
     ap.add_argument("--decode-shard-of", type=int, default=0,
                     help="development only: run one rank's shard of an N-way TP group on a single GPU")
     args = ap.parse_args()
@@ -133,6 +135,8 @@ def main():
         return 0
 
     if args.impl == "torch":
+        if args.workload == "decode":
+            return run_torch_decode(args)
         return run_torch_vit(args) if args.workload == "vit" else run_torch_baseline(args)
 
     import torch
@@ -627,6 +631,108 @@ def run_gptlite_cpu(args) -> int:
             "config": {"model": "GPT-lite 2x128", "batch_per_rank": B, "seq_len": S, "parallelism": f"dp{world}"},
             "first_loss": losses[0], "last_loss": losses[-1], "impl": "brain"}), flush=True)
     bdist.shutdown()
+    return 0
+
+
+def run_torch_decode(args) -> int:
+    """The 70B-shape TP=N greedy decode on plain PyTorch (``brain_b200.bench.torch_decode``): cuBLAS GEMMs,
+    SDPA over a contiguous KV cache, NCCL all-reduce, the step replayed from one CUDA graph (or eager with
+    ``--torch-graph off``); same batch, prompt, token counts and timing rules as the framework's arm."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from brain_b200.bench.torch_decode import TorchTPDecoder
+    from brain_b200.models.config import LlamaLiteConfig
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    B, S, NEW = args.decode_batch, args.prompt_len, args.new_tokens
+    cfg = LlamaLiteConfig.llama3_70b(max_seq_len=S + NEW)
+    if args.decode_layers != cfg.num_layers:
+        cfg = cfg.replace(num_layers=args.decode_layers)
+    shard_of = args.decode_shard_of or None
+    graph = args.torch_graph == "on"
+    srv = TorchTPDecoder(cfg, B, S + NEW, dev, world=world, rank=rank, shard_of=shard_of, seed=0)
+    prompts = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(1))
+    warm = max(3, args.warmup)
+    timed = NEW - 1 - warm
+    if timed < 1:
+        raise ValueError("--new-tokens must exceed warm-up + 1")
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    dev_prompts = prompts.to(dev)
+    barrier()
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    srv.prefill(dev_prompts)
+    p1.record()
+    srv.step(graph=False)
+    if graph:
+        srv.capture()
+    for _ in range(warm - 1):
+        srv.step(graph)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    time.sleep(0.3)
+    barrier()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record()
+    for _ in range(timed):
+        srv.step(graph)
+    s1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop() if clocks else None
+    ms = _max_over_ranks(s0.elapsed_time(s1) / timed, dev)
+    prefill_ms = _max_over_ranks(p0.elapsed_time(p1), dev)
+    e2e = None
+    if not args.no_e2e:
+        pinned = prompts.pin_memory()
+        barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = srv.generate(pinned.to(dev, non_blocking=True), NEW, graph=graph)
+        host = out.cpu()
+        e1.record()
+        torch.cuda.synchronize()
+        e2e_ms = _max_over_ranks(e0.elapsed_time(e1), dev)
+        e2e = {"value": B * NEW / (e2e_ms / 1e3), "unit": "generated tokens/s (prefill included)",
+               "ms_total": e2e_ms, "h2d_bytes_per_step": B * S * 8 / NEW, "d2h_bytes_per_step": host.numel() * 8 / NEW,
+               "api": "brain_b200.bench.torch_decode.TorchTPDecoder.generate"}
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode tok/s Llama-3-70B-shape TP=N", "value": B / (ms / 1e3), "unit": "tokens/s",
+            "ms_per_step": ms, "n_gpus": world, "steps": timed, "warmup": warm, "higher_is_better": True,
+            "dtype": "bf16", "data": "synthetic prompts (uniform tokens, seeded); random-init N(0,0.02) weights",
+            "config": {"model": "Llama-3-70B-shape" + ("" if cfg.num_layers == 80 else f" ({cfg.num_layers} layers: NOT the benchmark)"),
+                       "batch": B, "prompt_len": S, "new_tokens": NEW,
+                       "parallelism": f"tp{world}" if not shard_of else f"one rank's shard of tp{shard_of} (NOT the benchmark)",
+                       "kv_cache": "contiguous, read to capacity under a mask",
+                       "decode_step": "one CUDA graph of torch ops" if graph else "eager torch ops",
+                       "implementation": "plain PyTorch: F.linear (cuBLAS), F.scaled_dot_product_attention, "
+                                         "F.rms_norm, NCCL all_reduce / all_gather",
+                       "l2": "no flush: each step streams the rank's weights (>> 126 MB L2)"},
+            "prefill_ms": prefill_ms, "prefill_tok_s": B * S / (prefill_ms / 1e3),
+            "clocks": clk, "e2e": e2e, "impl": "torch"}), flush=True)
+    srv.close()
+    del srv
+    if world > 1:
+        dist.destroy_process_group()
     return 0
 
 

@@ -102,6 +102,57 @@ __global__ void reduce_pull_kernel(Peers src, int64_t src_off, int world, int fi
   }
 }
 
+// Small-message all-reduce in one launch. CTA c owns elements [c * per, (c + 1) * per): it copies them from
+// `in` into this rank's staging (half `parity` of the symmetric buffer), publishes flag c to every rank with
+// a system-scope release store of `epoch`, waits until every rank's flag c carries `epoch`, then sums chunk
+// c of all ranks' staging into `out` (which may alias `in`). The staging is double-buffered by call parity:
+// a rank can only begin the call after next once every peer has entered the next call, i.e. has finished
+// reading this one, so one signal phase per call suffices. This needs each rank's calls to execute in issue
+// order (one stream, or the host orders a stream switch with an event). Every rank sums the ranks' copies in
+// the same order, so the results agree bitwise. flags: peer j's int32 [kOneShotCtas][kMaxRanks].
+constexpr int kOneShotCtas = 32;
+template <typename T>
+__global__ void oneshot_allreduce_kernel(const T* in, T* out, int64_t n, Peers stage, Peers flags, int rank, int world,
+                                         int epoch, int64_t budget_ns, float scale) {
+  constexpr int V = Vec<T>::N;
+  const int64_t nv = n / V;
+  const int64_t per = (nv + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = blockIdx.x * per, v1 = v0 + per < nv ? v0 + per : nv;
+  T* mine = reinterpret_cast<T*>(stage.p[rank]);
+  for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x)
+    *reinterpret_cast<uint4*>(mine + i * V) = *reinterpret_cast<const uint4*>(in + i * V);
+  __syncthreads();
+  if (threadIdx.x < world) {
+    const int j = threadIdx.x;
+    __threadfence_system();
+    st_release_sys(reinterpret_cast<int*>(flags.p[j]) + blockIdx.x * kMaxRanks + rank, epoch);
+    const int* f = reinterpret_cast<const int*>(flags.p[rank]) + blockIdx.x * kMaxRanks + j;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_sys(f) < epoch) {
+      if (globaltimer() - t0 > (uint64_t)budget_ns) {
+        set_status(BRAIN_ERR_TIMEOUT_PEER, 1200 + j);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x) {
+    float acc[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) acc[k] = 0.f;
+    // rank order 0..world-1 on every rank, so all ranks produce bitwise identical sums
+    for (int j = 0; j < world; ++j) {
+      float x[V];
+      ld_vec(reinterpret_cast<const T*>(stage.p[j]) + i * V, x);
+#pragma unroll
+      for (int k = 0; k < V; ++k) acc[k] += x[k];
+    }
+#pragma unroll
+    for (int k = 0; k < V; ++k) acc[k] *= scale;
+    st_vec(out + i * V, acc);
+  }
+}
+
 // dst[dst_off + i] = peer_src[src_off + i]  (copy of n elements, 16-byte vectors)
 __global__ void copy_pull_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t nbytes) {
   const int64_t nv = nbytes / 16;
@@ -355,5 +406,30 @@ BRAIN_API int brain_comm_ddp_step_ctas(const int64_t* grads, const int64_t* para
     ddp_step_kernel<float><<<grid, 256, 0, st>>>(g, p, rank, world, push_world, off, n, master, m, v, lr, b1, b2,
                                                 eps, wd, 1.f / bc1, 1.f / bc2, grad_scale);
 
+  return (int)cudaGetLastError();
+}
+
+// One-launch all-reduce of n elements (dtype 0 = f32, 1 = bf16; n a multiple of the 16-byte vector; in and
+// out 16-byte aligned, may alias). stage: int64[world] peer pointers of this call's staging half (>= n
+// elements each); flags: int64[world] peer pointers of the flag arrays (int32 [32][8] each, zeroed once).
+// epoch grows by one per call. A peer that does not arrive within budget_ns records BRAIN_ERR_TIMEOUT_PEER.
+BRAIN_API int brain_comm_allreduce_oneshot(const void* in, void* out, int64_t n, int dtype, float scale,
+                                           const int64_t* stage, const int64_t* flags, int rank, int world, int epoch,
+                                           int64_t budget_ns, cudaStream_t st) {
+  if (world > kMaxRanks) return (int)cudaErrorInvalidValue;
+  const int V = dtype == 0 ? 4 : 8;
+  if (n % V || (reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
+    return (int)cudaErrorInvalidValue;
+  const int64_t nv = n / V;
+  const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>(kOneShotCtas, (nv + 511) / 512));
+  Peers sp = to_peers(stage, world), fp = to_peers(flags, world);
+  if (dtype == 0)
+    oneshot_allreduce_kernel<float><<<ctas, 256, 0, st>>>(reinterpret_cast<const float*>(in),
+                                                          reinterpret_cast<float*>(out), n, sp, fp, rank, world, epoch,
+                                                          budget_ns, scale);
+  else
+    oneshot_allreduce_kernel<__nv_bfloat16><<<ctas, 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), n, sp, fp, rank, world,
+        epoch, budget_ns, scale);
   return (int)cudaGetLastError();
 }

@@ -21,6 +21,7 @@ import torch.distributed as dist
 from .. import _native
 
 _native.register({
+    "brain_comm_allreduce_oneshot": ("brain_comm", "pplifppiiils"),
     "brain_ipc_alloc": ("brain_comm", "lpp"),
     "brain_ipc_handle_size": ("brain_comm", ""),
     "brain_ipc_open": ("brain_comm", "pp"),
@@ -123,6 +124,12 @@ class NvlinkComm:
         self.epoch = 0
         self.staging: SymmetricBuffer | None = None
         self.registered: dict[int, SymmetricBuffer] = {}
+        # one-launch small all-reduce: staging halves by call parity and per-CTA flags (int32 [32][8])
+        self.os_stage = SymmetricBuffer(2 * self.ONE_SHOT_BYTES, group)
+        self.os_stage_arr = [self.os_stage.peer_array(0), self.os_stage.peer_array(self.ONE_SHOT_BYTES)]
+        self.os_flags = SymmetricBuffer(32 * 8 * 4, group)
+        self.os_epoch = 0
+        self.os_stream: torch.cuda.Stream | None = None  # stream of the last one-shot launch
         dist.barrier(group)
 
     # ------------------------------------------------------------------ plumbing
@@ -173,6 +180,19 @@ class NvlinkComm:
         vec = 4 if t.dtype == torch.float32 else 8
         esz = t.element_size()
         dcode = 0 if t.dtype == torch.float32 else 1
+        if n * esz <= self.ONE_SHOT_BYTES and n % vec == 0 and t.data_ptr() % 16 == 0:
+            # one launch: copy into this rank's staging half, signal, pull-sum every rank's copy into t.
+            # Reusing a staging half two calls later is safe only if this rank's calls run in issue order,
+            # so a call on another stream than the previous one first waits for that one.
+            cur = torch.cuda.current_stream()
+            if self.os_stream is not None and cur != self.os_stream:
+                cur.wait_stream(self.os_stream)
+            self.os_stream = cur
+            self.os_epoch += 1
+            _native.call("brain_comm_allreduce_oneshot", t.data_ptr(), t.data_ptr(), n, dcode, scale,
+                         self.os_stage_arr[self.os_epoch & 1], self.os_flags.ptr_array, self.rank, self.world,
+                         self.os_epoch, self.timeout_ns, cur.cuda_stream)
+            return t
         if n * esz <= self.ONE_SHOT_BYTES:
             npad = -(-n // vec) * vec
             st = self._staging(npad * esz)
@@ -182,7 +202,8 @@ class NvlinkComm:
                 sv[n:].zero_()
             self.barrier(1)
             out = torch.empty(npad, device=t.device, dtype=t.dtype)
-            _native.call("brain_comm_reduce_pull", st.ptr_array, 0, self.rank, self.world, out.data_ptr(), npad, dcode,
+            # every rank reduces the whole vector: the same summation order (first rank 0) on all of them
+            _native.call("brain_comm_reduce_pull", st.ptr_array, 0, 0, self.world, out.data_ptr(), npad, dcode,
                          scale, _stream())
             t.copy_(out[:n].view_as(t))
             return t

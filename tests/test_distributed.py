@@ -159,6 +159,66 @@ def test_nvlink_collectives():
         assert all(o.values()), o
 
 
+def _gpu_oneshot(rank, world):
+    """Many small all-reduces in a row through the one-launch path (staging reused by call parity),
+    with random per-rank GPU delays and a stream switch, against a float64 sum of the gathered inputs."""
+    import random
+
+    import torch.distributed as dist
+
+    from brain_b200.parallel import dist as bdist
+    from brain_b200.parallel.symm import NvlinkComm
+    bdist.init(timeout_s=120)
+    comm = NvlinkComm(timeout_s=10)
+    rng = random.Random(1234)  # same sizes on every rank
+    delay = random.Random(rank)  # different delays per rank
+    side = torch.cuda.Stream()
+    worst, agree, calls = 0.0, True, 0
+    for it in range(48):
+        dtype = torch.float32 if it % 3 else torch.bfloat16
+        vec = 4 if dtype == torch.float32 else 8
+        n = vec * rng.randint(1, comm.ONE_SHOT_BYTES // (vec * (4 if dtype == torch.float32 else 2)))
+        if it % 11 == 5:
+            n += 1  # not a whole vector: the staged fallback
+        g = torch.Generator(device="cuda").manual_seed(1000 * it + rank)
+        x = torch.randn(n, device="cuda", generator=g).to(dtype)
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x)
+        exact = torch.stack([p.double() for p in parts]).sum(0)
+        op = "mean" if it % 4 == 1 else "sum"
+        if op == "mean":
+            exact = exact / world
+        if delay.random() < 0.5:
+            torch.cuda._sleep(delay.randint(1, 200_000))
+        if it % 7 == 3:
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                comm.all_reduce(x, op=op)
+            torch.cuda.current_stream().wait_stream(side)
+        else:
+            comm.all_reduce(x, op=op)
+        calls += 1
+        tol = 1e-5 if dtype == torch.float32 else 1e-2
+        err = float(((x.double() - exact).abs() / (exact.abs() + 1.0)).max())
+        worst = max(worst, err / tol)
+        outs = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(outs, x)
+        agree = agree and all(torch.equal(o, outs[0]) for o in outs)
+    comm.check()
+    comm.close()
+    bdist.shutdown()
+    return {"within_tol": worst <= 1.0, "ranks_agree_bitwise": agree, "calls": calls == 48}
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_nvlink_oneshot_allreduce_many_calls():
+    n = min(torch.cuda.device_count(), 8)
+    outs = run_ranks(_gpu_oneshot, n, env={"NCCL_NVLS_ENABLE": "0"})
+    for o in outs:
+        assert all(o.values()), o
+
+
 @pytest.mark.gpu
 def test_overlapped_adamw_single_gpu_matches_step_after_backward():
     """One GPU: per-bucket AdamW on a side stream during backward == AdamW after backward. The first step

@@ -212,3 +212,31 @@ def test_gemm_residual_by_tma_matches_oracle(shape):
                                atol=2e-3 * K ** 0.5 + 0.05)
     from brain_b200 import _native
     assert _native.status("gemm")[0] == 0
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("ta,tb,shape", [
+    (False, True, (8192, 28672, 4096)),   # gate_up forward: many waves of the persistent scheduler
+    (False, True, (8192, 4096, 14336)),   # down forward: K = 14336 through the stage ring
+    (False, False, (8192, 14336, 4096)),  # dgrad of down
+    (True, False, (4096, 6144, 8192)),    # weight gradient of qkv (A transposed)
+    (False, True, (4096, 128256, 4096)),  # LM head: N = 128256 with a ragged last tile column
+])
+def test_gemm_production_shapes_sampled_rows(ta, tb, shape):
+    """Llama-3-8B training shapes on the CTA-pair kernel: full GEMM in bf16, then 96 sampled rows (the
+    first and last rows, rows around 256-row tile edges, random rows) against a float32 oracle."""
+    from brain_b200 import _native
+    M, N, K = shape
+    a = (torch.randn((K, M) if ta else (M, K), device="cuda") * 0.5).to(torch.bfloat16)
+    b = (torch.randn((N, K) if tb else (K, N), device="cuda") * 0.5).to(torch.bfloat16)
+    c = gemm(a, b, ta, tb)
+    torch.cuda.synchronize()
+    g = torch.Generator(device="cpu").manual_seed(M + N + K)
+    edges = [0, 1, 255, 256, 257, M // 2 - 1, M // 2, M - 257, M - 256, M - 2, M - 1]
+    rows = torch.tensor(sorted(set(edges + torch.randint(0, M, (96 - len(edges),), generator=g).tolist())),
+                        device="cuda")
+    A = a.float().t()[rows] if ta else a.float()[rows]
+    B = b.float().t() if tb else b.float()
+    ref = A @ B
+    torch.testing.assert_close(c[rows].float(), ref, rtol=1e-2, atol=2e-3 * K ** 0.5 * 0.25 + 0.02)
+    assert _native.status("gemm")[0] == 0

@@ -63,3 +63,28 @@ def test_torch_vit_arm_matches_framework_architecture():
         loss.backward()
         opt.step()
     assert torch.isfinite(loss) and loss.item() < l0.item()
+
+
+def test_torch_decode_arm_cached_steps_match_full_recompute():
+    """The PyTorch decode arm's static-shape cached step (masked cache read, device position) produces
+    the same greedy tokens as re-running the whole prefix, in float32 on the CPU."""
+    from brain_b200.bench.torch_decode import TorchTPDecoder
+    cfg = _cfg()
+    B, S, NEW = 3, 7, 6
+    dec = TorchTPDecoder(cfg, B, S + NEW, "cpu", seed=1, dtype=torch.float32)
+    prompts = torch.randint(0, cfg.vocab_size, (B, S), generator=torch.Generator().manual_seed(2))
+    out = dec.generate(prompts, NEW, graph=False)
+    assert out.shape == (B, S + NEW) and torch.equal(out[:, :S], prompts)
+    for i in range(NEW):
+        ref = dec.prefill(out[:, :S + i], chunk=2)  # full recompute of the prefix
+        assert torch.equal(ref, out[:, S + i]), i
+
+
+def test_torch_decode_arm_shard_shapes():
+    from brain_b200.bench.torch_decode import TorchTPDecoder
+    cfg = _cfg()
+    dec = TorchTPDecoder(cfg, 2, 16, "cpu", shard_of=2, dtype=torch.float32)
+    assert (dec.hq, dec.hkv, dec.ffn, dec.vloc) == (2, 1, 48, 128)
+    assert dec.layers[0]["wqkv"].shape == ((2 + 2) * 16, 64) and dec.layers[0]["wd"].shape == (64, 48)
+    tok = dec.generate(torch.zeros(2, 4, dtype=torch.long), 3, graph=False)
+    assert int(tok.max()) < dec.vloc  # a lone shard picks within its own vocabulary slice
