@@ -38,6 +38,7 @@ LIBRARIES = {
     "brain_kernels": [
         "host_utils.cu", "gemm.cu", "norms.cu", "elementwise.cu", "cross_entropy.cu", "optim.cu",
         "attention.cu", "attention_tc.cu", "attention_bwd_tc.cu", "attention_decode.cu", "decode_tp.cu", "fp8.cu",
+        "linalg.cu",
     ],
     "brain_comm": ["host_utils.cu", "comm.cu"],
 }

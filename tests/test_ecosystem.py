@@ -933,16 +933,18 @@ def test_memory_arena_pool_linalg_and_heads():
     assert is_aligned(aligned_empty((5, 5)), 256) and strides_row_major((2, 3, 4)) == [12, 4, 1]
     x = torch.randn(5, 5, dtype=torch.float64)
     spd = x @ x.t() + 5 * torch.eye(5, dtype=torch.float64)
-    P, L, U = LA.lu(spd)
-    torch.testing.assert_close(P @ L @ U, spd)
+    L, U, perm = LA.lu(spd)
+    torch.testing.assert_close(L @ U, spd[perm])
     torch.testing.assert_close(LA.cholesky(spd) @ LA.cholesky(spd).t(), spd)
     w, V = LA.eigh(spd)
     torch.testing.assert_close(V @ torch.diag(w) @ V.t(), spd)
-    torch.testing.assert_close(LA.ifft(LA.fft(x[0])).real, x[0])
-    dense = torch.tensor([[0.0, 2.0, 0.0], [1.0, 0.0, 3.0]])
-    csr = LA.CsrMatrix.from_dense(dense)
-    assert csr.nnz() == 3
-    torch.testing.assert_close(LA.spmm(csr, torch.eye(3)), dense)
+    torch.testing.assert_close(LA.ifft_complex(LA.fft_complex(x[0])).real, x[0])
+    coo = LA.SparseCOO((2, 3))
+    for r, c, v in ((0, 1, 2.0), (1, 0, 1.0), (1, 2, 3.0)):
+        coo.insert(r, c, v)
+    dense = torch.tensor([[0.0, 2.0, 0.0], [1.0, 0.0, 3.0]], dtype=torch.float64)
+    assert coo.nnz == 3
+    torch.testing.assert_close(coo.spmm(torch.eye(3, dtype=torch.float64)), dense)
     emb = TransformerEmbedding(EmbConfig(50, 16, max_positions=8, type_vocab_size=2, norm="layer"))
     h = emb(torch.randint(0, 50, (2, 8)))
     assert h.shape == (2, 8, 16)
