@@ -100,3 +100,35 @@ _DEFAULT = BrainRng.from_seed(0x123456789ABCDEF0)
 def with_rng(fn):
     """Run fn(rng) with the thread's default reference-stream generator."""
     return fn(_DEFAULT)
+
+
+LCG64_A = 6364136223846793005  # Knuth's MMIX multiplier and increment (public constants)
+LCG64_C = 1442695040888963407
+
+
+def lcg64_stream(state: int, count: int) -> np.ndarray:
+    """The next ``count`` states of the 64-bit LCG s' = A s + C (mod 2^64) after ``state``, as uint64.
+    Several reference crates draw from this generator one value at a time; here it is produced in
+    blocks of 4096: within a block state_j = A_j s + C_j with (A_j, C_j) precomputed once, so each
+    block is one vector multiply-add."""
+    B = 4096
+    a_j = np.empty(B, dtype=np.uint64)
+    c_j = np.empty(B, dtype=np.uint64)
+    a, c = 1, 0
+    for j in range(B):
+        a, c = (a * LCG64_A) & _M64, (c * LCG64_A + LCG64_C) & _M64
+        a_j[j], c_j[j] = a, c
+    out = np.empty(count, dtype=np.uint64)
+    s = np.uint64(state & _M64)
+    with np.errstate(over="ignore"):
+        for b0 in range(0, count, B):
+            blk = a_j * s + c_j
+            k = min(B, count - b0)
+            out[b0:b0 + k] = blk[:k]
+            s = blk[B - 1]
+    return out
+
+
+def lcg64_unit(state: int, count: int) -> np.ndarray:
+    """Uniform [0, 1) doubles (top 53 bits of each LCG state)."""
+    return (lcg64_stream(state, count) >> np.uint64(11)).astype(np.float64) / float(1 << 53)

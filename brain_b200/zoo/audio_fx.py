@@ -28,8 +28,8 @@ from functools import lru_cache
 import numpy as np
 import torch
 
-_LCG_A = 6364136223846793005  # Knuth's MMIX linear congruential generator, as the reference's noise
-_LCG_C = 1442695040888963407
+from ..utils.random import LCG64_A as _LCG_A, LCG64_C as _LCG_C, lcg64_stream
+
 _M64 = (1 << 64) - 1
 
 
@@ -194,27 +194,6 @@ def time_mask(signal: torch.Tensor, start: int, mask_len: int) -> torch.Tensor:
     return signal
 
 
-def _lcg_stream(state: int, count: int) -> np.ndarray:
-    """The next `count` states of the 64-bit LCG after `state`, by blocks: within a block of B steps
-    state_{j} = A_j * s + C_j (mod 2^64) with A_j, C_j precomputed once, one vector op per block."""
-    B = 4096
-    a_j = np.empty(B, dtype=np.uint64)
-    c_j = np.empty(B, dtype=np.uint64)
-    a, c = 1, 0
-    for j in range(B):
-        a, c = (a * _LCG_A) & _M64, (c * _LCG_A + _LCG_C) & _M64
-        a_j[j], c_j[j] = a, c
-    out = np.empty(count, dtype=np.uint64)
-    s = np.uint64(state)
-    with np.errstate(over="ignore"):
-        for b0 in range(0, count, B):
-            blk = a_j * s + c_j
-            k = min(B, count - b0)
-            out[b0:b0 + k] = blk[:k]
-            s = blk[B - 1]
-    return out
-
-
 def add_noise(signal: torch.Tensor, snr_db: float, seed: int) -> torch.Tensor:
     """Add Gaussian noise at the given SNR (signal power / noise power) in place, per row, with the
     reference's generator: state = seed + 0x9e3779b97f4a7c15, then per sample two LCG draws
@@ -225,7 +204,7 @@ def add_noise(signal: torch.Tensor, snr_db: float, seed: int) -> torch.Tensor:
     x = _f64(signal)
     power = x.square().mean(-1, keepdim=True)
     std = (power / max(10.0 ** (snr_db / 10.0), 1e-6)).sqrt()
-    st = _lcg_stream((seed + 0x9E3779B97F4A7C15) & _M64, 2 * n)
+    st = lcg64_stream((seed + 0x9E3779B97F4A7C15) & _M64, 2 * n)
     u = ((st >> np.uint64(32)).astype(np.float64) + 1.0) / 4294967297.0
     normal = np.sqrt(-2.0 * np.log(u[0::2])) * np.cos(2.0 * math.pi * u[1::2])
     signal.copy_((x + std * torch.from_numpy(normal).to(x.device)).to(signal.dtype))
