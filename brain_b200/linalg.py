@@ -32,8 +32,8 @@ import torch
 from . import _native
 
 _native.register({
-    "brain_jacobi_svd": ("brain_kernels", "ppppplliidp"),
-    "brain_csr_spmm": ("brain_kernels", "pppplplllp"),
+    "brain_jacobi_svd": ("brain_kernels", "pppppliiids"),
+    "brain_csr_spmm": ("brain_kernels", "pppplpllls"),
 })
 
 _PIVOT_EPS = 1e-15
