@@ -34,6 +34,7 @@ from . import _native
 _native.register({
     "brain_jacobi_svd": ("brain_kernels", "pppppliiids"),
     "brain_csr_spmm": ("brain_kernels", "pppplpllls"),
+    "brain_status_linalg": ("brain_kernels", "pi"),
 })
 
 _PIVOT_EPS = 1e-15
