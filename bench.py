@@ -266,6 +266,7 @@ def main():
                                           else "after backward"),
                        "l2": "no flush: working set (weights+optimizer+activations) >> 126 MB L2"},
             "mfu_model_tflops_per_gpu": flops_tok * tok_s / world / 1e12,
+            "nvlink": _ddp_link_roofline(cfg.num_params(), world, ms),
             "final_loss": final_loss,
             "clocks": clk,
             "e2e": e2e,
@@ -632,6 +633,20 @@ def run_gptlite_cpu(args) -> int:
             "first_loss": losses[0], "last_loss": losses[-1], "impl": "brain"}), flush=True)
     bdist.shutdown()
     return 0
+
+
+def _ddp_link_roofline(params: int, world: int, step_ms: float) -> dict | None:
+    """Bytes each rank must receive over NVLink per data-parallel step and the time they take at the
+    measured peer-copy rate: the reduce-scatter pulls (N-1)/N of the bf16 gradients, the all-gather
+    returns (N-1)/N of the bf16 weights. ``share_of_step`` is that transfer time over the step time:
+    the link-bound floor that the per-bucket overlap hides behind backward."""
+    if world <= 1:
+        return None
+    link_gbs = 770.0  # measured peer copy per direction per GPU on this B200 NVSwitch system
+    nbytes = 2 * (world - 1) / world * params * 2
+    t_ms = nbytes / (link_gbs * 1e9) * 1e3
+    return {"bytes_in_per_rank_per_step": nbytes, "link_gbs": link_gbs, "transfer_ms_at_link_rate": t_ms,
+            "share_of_step": t_ms / step_ms}
 
 
 def run_torch_decode(args) -> int:
