@@ -144,14 +144,16 @@ def add_layer_norm(x, r, w, b=None, eps=1e-5):
 
 def fused_layer_norm(x, w, b=None, eps=1e-5):
     """LayerNorm with the one-pass variance of the reference's fused variant: var = max(E[x^2] - E[x]^2, 0)
-    (crates/brain-transformer/src/ops_fused.rs:62-64). On CUDA tensors the LayerNorm kernel runs; it takes
-    the two-pass variance, which equals the one-pass form in exact arithmetic and does not cancel."""
+    (crates/brain-core/src/tensor/ops_fused.rs:43-70). On CUDA tensors the LayerNorm kernel runs; it takes
+    the two-pass variance, which equals the one-pass form in exact arithmetic and does not cancel. On the
+    CPU float64 inputs are computed in float64 (the reference's precision), others in float32."""
     if x.is_cuda:
         return layer_norm(x, w, b, eps)
-    xf = x.float()
+    ct = torch.float64 if x.dtype == torch.float64 else torch.float32
+    xf = x.to(ct)
     mu = xf.mean(-1, keepdim=True)
     var = (xf.pow(2).mean(-1, keepdim=True) - mu.pow(2)).clamp_min(0.0)
-    y = (xf - mu) * torch.rsqrt(var + eps) * w.float()
+    y = (xf - mu) * torch.rsqrt(var + eps) * w.to(ct)
     if b is not None:
-        y = y + b.float()
+        y = y + b.to(ct)
     return y.to(x.dtype)
