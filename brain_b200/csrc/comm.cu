@@ -102,15 +102,16 @@ __global__ void reduce_pull_kernel(Peers src, int64_t src_off, int world, int fi
   }
 }
 
-// Small-message all-reduce in one launch. CTA c owns elements [c * per, (c + 1) * per): it copies them from
-// `in` into this rank's staging (half `parity` of the symmetric buffer), publishes flag c to every rank with
-// a system-scope release store of `epoch`, waits until every rank's flag c carries `epoch`, then sums chunk
-// c of all ranks' staging into `out` (which may alias `in`). The staging is double-buffered by call parity:
-// a rank can only begin the call after next once every peer has entered the next call, i.e. has finished
-// reading this one, so one signal phase per call suffices. This needs each rank's calls to execute in issue
-// order (one stream, or the host orders a stream switch with an event). Every rank sums the ranks' copies in
-// the same order, so the results agree bitwise. flags: peer j's int32 [kOneShotCtas][kMaxRanks].
-constexpr int kOneShotCtas = 32;
+// Small- and mid-size all-reduce in one launch. CTA c owns vectors [c * per, (c + 1) * per) (the last CTA
+// also the scalar tail when n is not a whole number of vectors): it copies them from `in` into this rank's
+// staging (half `parity` of the symmetric buffer), publishes flag c to every rank with a system-scope release
+// store of `epoch`, waits until every rank's flag c carries `epoch`, then sums its part of all ranks' staging
+// into `out` (which may alias `in`). The staging is double-buffered by call parity: a rank can only begin
+// the call after next once every peer has entered the next call, i.e. has finished reading this one, so one
+// signal phase per call suffices. This needs each rank's calls to execute in issue order (one stream, or the
+// host orders a stream switch). Every rank sums the ranks' copies in the same order (rank 0 first), so the
+// results agree bitwise. flags: peer j's int32 [kOneShotCtas][kMaxRanks].
+constexpr int kOneShotCtas = 128;
 template <typename T>
 __global__ void oneshot_allreduce_kernel(const T* in, T* out, int64_t n, Peers stage, Peers flags, int rank, int world,
                                          int epoch, int64_t budget_ns, float scale) {
@@ -118,9 +119,12 @@ __global__ void oneshot_allreduce_kernel(const T* in, T* out, int64_t n, Peers s
   const int64_t nv = n / V;
   const int64_t per = (nv + gridDim.x - 1) / gridDim.x;
   const int64_t v0 = blockIdx.x * per, v1 = v0 + per < nv ? v0 + per : nv;
+  const bool tail_cta = blockIdx.x == gridDim.x - 1;
   T* mine = reinterpret_cast<T*>(stage.p[rank]);
   for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x)
     *reinterpret_cast<uint4*>(mine + i * V) = *reinterpret_cast<const uint4*>(in + i * V);
+  if (tail_cta)
+    for (int64_t e = nv * V + threadIdx.x; e < n; e += blockDim.x) mine[e] = in[e];
   __syncthreads();
   if (threadIdx.x < world) {
     const int j = threadIdx.x;
@@ -140,7 +144,6 @@ __global__ void oneshot_allreduce_kernel(const T* in, T* out, int64_t n, Peers s
     float acc[V];
 #pragma unroll
     for (int k = 0; k < V; ++k) acc[k] = 0.f;
-    // rank order 0..world-1 on every rank, so all ranks produce bitwise identical sums
     for (int j = 0; j < world; ++j) {
       float x[V];
       ld_vec(reinterpret_cast<const T*>(stage.p[j]) + i * V, x);
@@ -151,6 +154,12 @@ __global__ void oneshot_allreduce_kernel(const T* in, T* out, int64_t n, Peers s
     for (int k = 0; k < V; ++k) acc[k] *= scale;
     st_vec(out + i * V, acc);
   }
+  if (tail_cta)
+    for (int64_t e = nv * V + threadIdx.x; e < n; e += blockDim.x) {
+      float acc = 0.f;
+      for (int j = 0; j < world; ++j) acc += static_cast<float>(reinterpret_cast<const T*>(stage.p[j])[e]);
+      out[e] = static_cast<T>(acc * scale);
+    }
 }
 
 // dst[dst_off + i] = peer_src[src_off + i]  (copy of n elements, 16-byte vectors)
@@ -409,19 +418,19 @@ BRAIN_API int brain_comm_ddp_step_ctas(const int64_t* grads, const int64_t* para
   return (int)cudaGetLastError();
 }
 
-// One-launch all-reduce of n elements (dtype 0 = f32, 1 = bf16; n a multiple of the 16-byte vector; in and
-// out 16-byte aligned, may alias). stage: int64[world] peer pointers of this call's staging half (>= n
-// elements each); flags: int64[world] peer pointers of the flag arrays (int32 [32][8] each, zeroed once).
-// epoch grows by one per call. A peer that does not arrive within budget_ns records BRAIN_ERR_TIMEOUT_PEER.
+// One-launch all-reduce of n elements (dtype 0 = f32, 1 = bf16; any n >= 1; in and out 16-byte aligned, may
+// alias). stage: int64[world] peer pointers of this call's staging half (>= n elements each); flags:
+// int64[world] peer pointers of the flag arrays (int32 [128][8] each, zeroed once). epoch grows by one per
+// call. A peer that does not arrive within budget_ns records BRAIN_ERR_TIMEOUT_PEER.
 BRAIN_API int brain_comm_allreduce_oneshot(const void* in, void* out, int64_t n, int dtype, float scale,
                                            const int64_t* stage, const int64_t* flags, int rank, int world, int epoch,
                                            int64_t budget_ns, cudaStream_t st) {
-  if (world > kMaxRanks) return (int)cudaErrorInvalidValue;
+  if (world > kMaxRanks || n < 1) return (int)cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return (int)cudaErrorInvalidValue;
   const int V = dtype == 0 ? 4 : 8;
-  if (n % V || (reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15))
-    return (int)cudaErrorInvalidValue;
   const int64_t nv = n / V;
-  const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>(kOneShotCtas, (nv + 511) / 512));
+  // about 1024 vectors (16 KB) per CTA, so mid-size messages spread over up to 128 SMs
+  const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>(kOneShotCtas, (nv + 1023) / 1024));
   Peers sp = to_peers(stage, world), fp = to_peers(flags, world);
   if (dtype == 0)
     oneshot_allreduce_kernel<float><<<ctas, 256, 0, st>>>(reinterpret_cast<const float*>(in),

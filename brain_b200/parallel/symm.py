@@ -109,7 +109,8 @@ class NvlinkComm:
     """Collectives as P2P kernels over symmetric memory (one process per GPU, one node)."""
 
     name = "nvlink"
-    ONE_SHOT_BYTES = 256 * 1024
+    ONE_SHOT_BYTES = 256 * 1024  # staged fallback (unaligned tensors) up to this size
+    ONE_LAUNCH_BYTES = 2 << 20  # one-launch all-reduce up to this size (each rank reads every rank's copy)
     PUSH_BYTES = 4 << 20  # all-gather shards from this size are pushed (one more barrier, more bytes in flight)
 
     def __init__(self, group=None, timeout_s: float = 60.0):
@@ -124,10 +125,10 @@ class NvlinkComm:
         self.epoch = 0
         self.staging: SymmetricBuffer | None = None
         self.registered: dict[int, SymmetricBuffer] = {}
-        # one-launch small all-reduce: staging halves by call parity and per-CTA flags (int32 [32][8])
-        self.os_stage = SymmetricBuffer(2 * self.ONE_SHOT_BYTES, group)
-        self.os_stage_arr = [self.os_stage.peer_array(0), self.os_stage.peer_array(self.ONE_SHOT_BYTES)]
-        self.os_flags = SymmetricBuffer(32 * 8 * 4, group)
+        # one-launch all-reduce: staging halves by call parity and per-CTA flags (int32 [128][8])
+        self.os_stage = SymmetricBuffer(2 * self.ONE_LAUNCH_BYTES, group)
+        self.os_stage_arr = [self.os_stage.peer_array(0), self.os_stage.peer_array(self.ONE_LAUNCH_BYTES)]
+        self.os_flags = SymmetricBuffer(128 * 8 * 4, group)
         self.os_epoch = 0
         self.os_stream: torch.cuda.Stream | None = None  # stream of the last one-shot launch
         dist.barrier(group)
@@ -180,7 +181,7 @@ class NvlinkComm:
         vec = 4 if t.dtype == torch.float32 else 8
         esz = t.element_size()
         dcode = 0 if t.dtype == torch.float32 else 1
-        if n * esz <= self.ONE_SHOT_BYTES and n % vec == 0 and t.data_ptr() % 16 == 0:
+        if n * esz <= self.ONE_LAUNCH_BYTES and t.data_ptr() % 16 == 0:
             # one launch: copy into this rank's staging half, signal, pull-sum every rank's copy into t.
             # Reusing a staging half two calls later is safe only if this rank's calls run in issue order,
             # so a call on another stream than the previous one first waits for that one.

@@ -160,8 +160,9 @@ def test_nvlink_collectives():
 
 
 def _gpu_oneshot(rank, world):
-    """Many small all-reduces in a row through the one-launch path (staging reused by call parity),
-    with random per-rank GPU delays and a stream switch, against a float64 sum of the gathered inputs."""
+    """Many all-reduces up to 2 MB in a row through the one-launch path (staging reused by call parity), odd
+    lengths, unaligned views (staged fallback), random per-rank GPU delays and a stream switch, against a
+    float64 sum of the gathered inputs; every rank must hold bitwise the same result."""
     import random
 
     import torch.distributed as dist
@@ -177,11 +178,13 @@ def _gpu_oneshot(rank, world):
     for it in range(48):
         dtype = torch.float32 if it % 3 else torch.bfloat16
         vec = 4 if dtype == torch.float32 else 8
-        n = vec * rng.randint(1, comm.ONE_SHOT_BYTES // (vec * (4 if dtype == torch.float32 else 2)))
-        if it % 11 == 5:
-            n += 1  # not a whole vector: the staged fallback
+        n = vec * rng.randint(1, comm.ONE_LAUNCH_BYTES // (vec * (4 if dtype == torch.float32 else 2)))
+        if it % 5 == 2:
+            n = rng.randint(1, 3000)  # any length: the last CTA also sums the scalar tail
         g = torch.Generator(device="cuda").manual_seed(1000 * it + rank)
         x = torch.randn(n, device="cuda", generator=g).to(dtype)
+        if it % 11 == 5 and n * x.element_size() <= comm.ONE_SHOT_BYTES:
+            x = torch.cat([x.new_zeros(1), x])[1:]  # not 16-byte aligned: the staged fallback
         parts = [torch.empty_like(x) for _ in range(world)]
         dist.all_gather(parts, x)
         exact = torch.stack([p.double() for p in parts]).sum(0)
