@@ -1,0 +1,73 @@
+"""Regularisation extras (crates/brain-regularization/src/dropout/adaptive.rs, perturb.rs, consistency.rs,
+dropout_uncertainty.rs, stopping.rs, utils.rs, normalization/, registry.rs, regularizers.rs)."""
+import math
+
+import pytest
+import torch
+
+from brain_b200 import reg_extras as RX
+
+
+def test_concrete_dropout_learns_and_matches_form():
+    cd = RX.ConcreteDropout(0.2, 0.1)
+    assert cd.current_p() == pytest.approx(0.2)
+    x = torch.ones(1000)
+    y = cd(x, generator=torch.Generator().manual_seed(0))
+    assert abs(float(y.mean()) - 1.0) < 0.1  # unbiased in expectation
+    y.sum().backward()
+    assert cd.logit_p.grad is not None and torch.isfinite(cd.logit_p.grad)
+    reg = cd.regularizer(torch.tensor(4.0), 10)
+    p = 0.2
+    want = 1e-6 * 4.0 / (1 - p) + 1e-5 * 10 * (p * math.log(p) + (1 - p) * math.log(1 - p))
+    assert float(reg) == pytest.approx(want, rel=1e-5)
+    cd.eval()
+    assert torch.equal(cd(x), x)
+
+
+def test_noise_fgsm_consistency_mc():
+    gn = RX.GaussianNoise(0.5)
+    y = gn(torch.zeros(20000), generator=torch.Generator().manual_seed(1))
+    assert abs(float(y.std()) - 0.5) < 0.02
+    gn.eval()
+    assert float(gn(torch.zeros(3)).abs().sum()) == 0
+    x, g = torch.tensor([1.0, 2.0, 3.0]), torch.tensor([0.5, -2.0, 0.0])
+    assert RX.apply_fgsm_perturbation(x, g, 0.1).tolist() == pytest.approx([1.1, 1.9, 3.0])
+    lin = torch.nn.Linear(3, 2)
+    adv = RX.fgsm_example(lin, torch.nn.functional.cross_entropy, torch.randn(4, 3), torch.tensor([0, 1, 0, 1]), 0.05)
+    assert adv.shape == (4, 3)
+    assert float(RX.compute_consistency_loss(torch.ones(2, 2), torch.zeros(2, 2), 0.5)) == 0.5
+    samples = [torch.tensor([1.0, 2.0]), torch.tensor([3.0, 2.0])]
+    r = RX.compute_mc_dropout_statistics(samples)
+    assert r.mean.tolist() == [2.0, 2.0] and r.variance.tolist() == [1.0, 0.0]
+    net = torch.nn.Sequential(torch.nn.Linear(4, 16), torch.nn.Dropout(0.5), torch.nn.Linear(16, 1)).eval()
+    outs = RX.mc_dropout_samples(net, torch.randn(3, 4), 8)
+    assert outs.shape == (8, 3, 1) and not net.training and float(outs.std(0).sum()) > 0
+
+
+def test_stop_policies_welford_norm_wrappers_registry():
+    assert RX.StopOnBudget(5).should_stop(5, 0.0) and not RX.StopOnBudget(5).should_stop(4, 0.0)
+    sp = RX.StopOnPlateau(2, 0.01)
+    assert [sp.should_stop(i, l) for i, l in enumerate([1.0, 0.995, 0.99, 0.5, 0.6, 0.7])] == \
+        [False, False, True, False, False, True]
+    data = torch.randn(50, 3, dtype=torch.float64)
+    a, b = RX.WelfordAccumulator(), RX.WelfordAccumulator()
+    for row in data[:20]:
+        a.update(row)
+    for row in data[20:]:
+        b.update(row)
+    a.merge(b)
+    torch.testing.assert_close(a.mean, data.mean(0))
+    torch.testing.assert_close(a.variance(), data.var(0, unbiased=False))
+    torch.testing.assert_close(a.variance(True), data.var(0, unbiased=True))
+    wn = RX.weight_norm(torch.nn.Linear(4, 3))
+    assert hasattr(wn.parametrizations, "weight")
+    sn = RX.spectral_norm(torch.nn.Linear(4, 3))
+    sn(torch.randn(2, 4))
+    assert float(torch.linalg.matrix_norm(sn.weight.detach(), 2)) == pytest.approx(1.0, rel=0.2)
+    assert RX.RegRegistry.parse_kind("LayerNorm") == "layer_norm"
+    with pytest.raises(ValueError):
+        RX.RegRegistry.parse_kind("nope")
+    p = [torch.tensor([1.0, -2.0])]
+    assert float(RX.WeightedRegularizer("l1", 0.1)(p)) == pytest.approx(0.3)
+    st = RX.RegStack().add(RX.WeightedRegularizer("l1", 0.1)).add(RX.WeightedRegularizer("l2", 1.0))
+    assert float(st(p)) == pytest.approx(0.3 + 0.5 * 5.0)
