@@ -329,3 +329,69 @@ LOSSES = {c.__name__: c for c in [CrossEntropyLoss, NLLLoss, BCELoss, BCEWithLog
                                  QuantileLoss, PoissonNLLLoss, GaussianNLLLoss, CosineEmbeddingLoss,
                                  MarginRankingLoss, TripletLoss, ContrastiveLoss, InfoNCELoss, NTXentLoss, DiceLoss,
                                  CEDiceLoss, IoULoss, WassersteinLoss, GANLoss, HingeGANLoss, DistillationLoss]}
+
+
+# ------------------------------------------------------------------ metric learning / robust / adversarial extras
+class ArcFaceLoss(Loss):
+    """Additive angular margin (Deng et al. 2019) on cosine logits [B, C]: the target class's logit is
+    s cos(theta + m) with theta = acos(clamp(cos, -1, 1)), the others s cos; cross-entropy over the row
+    (crates/brain-loss/src/metric_loss/mod.rs:30-74)."""
+
+    def __init__(self, scale: float = 64.0, margin: float = 0.5, reduction: str = "mean"):
+        self.s, self.m, self.reduction = scale, margin, reduction
+
+    def forward(self, cos_thetas, targets):
+        c = cos_thetas.clamp(-1.0, 1.0)
+        t = targets.long()
+        tgt = torch.cos(torch.acos(c.gather(1, t[:, None])) + self.m)
+        logits = self.s * c.scatter(1, t[:, None], tgt)
+        return _reduce(F.cross_entropy(logits, t, reduction="none"), self.reduction)
+
+
+class AngularDistanceLoss(Loss):
+    """acos of the cosine similarity between prediction and target rows, in radians."""
+
+    def __init__(self, reduction: str = "mean"):
+        self.reduction = reduction
+
+    def forward(self, pred, target):
+        cos = F.cosine_similarity(pred, target, dim=-1, eps=1e-12).clamp(-1.0, 1.0)
+        return _reduce(torch.acos(cos), self.reduction)
+
+
+class CauchyLoss(Loss):
+    """0.5 c^2 ln(1 + r^2 / c^2) per residual r (robust to outliers; crates/brain-loss/src/regression/robust.rs)."""
+
+    def __init__(self, c: float = 1.0, reduction: str = "mean"):
+        self.c, self.reduction = c, reduction
+
+    def forward(self, pred, target):
+        if pred.shape != target.shape:
+            raise ValueError(f"shape mismatch: {tuple(pred.shape)} vs {tuple(target.shape)}")
+        c2 = self.c * self.c
+        return _reduce(0.5 * c2 * torch.log1p((pred - target) ** 2 / c2), self.reduction)
+
+
+class LSGANLoss:
+    """Least-squares GAN: D: mean 0.5 (D(x) - 1)^2 + mean 0.5 D(G(z))^2; G: mean 0.5 (D(G(z)) - 1)^2."""
+
+    @staticmethod
+    def discriminator_loss(d_real, d_fake):
+        return 0.5 * ((d_real - 1) ** 2).mean() + 0.5 * (d_fake ** 2).mean()
+
+    @staticmethod
+    def generator_loss(d_fake):
+        return 0.5 * ((d_fake - 1) ** 2).mean()
+
+
+class RelativisticLoss:
+    """Relativistic average GAN losses with the logistic link: D pushes D(x) - mean D(G(z)) up and
+    D(G(z)) - mean D(x) down; G the reverse."""
+
+    @staticmethod
+    def discriminator_loss(d_real, d_fake):
+        return F.softplus(-(d_real - d_fake.mean())).mean() + F.softplus(d_fake - d_real.mean()).mean()
+
+    @staticmethod
+    def generator_loss(d_real, d_fake):
+        return F.softplus(-(d_fake - d_real.mean())).mean() + F.softplus(d_real - d_fake.mean()).mean()

@@ -71,3 +71,26 @@ def test_stop_policies_welford_norm_wrappers_registry():
     assert float(RX.WeightedRegularizer("l1", 0.1)(p)) == pytest.approx(0.3)
     st = RX.RegStack().add(RX.WeightedRegularizer("l1", 0.1)).add(RX.WeightedRegularizer("l2", 1.0))
     assert float(st(p)) == pytest.approx(0.3 + 0.5 * 5.0)
+
+
+def test_metric_robust_adversarial_losses():
+    import torch.nn.functional as F
+
+    from brain_b200 import losses as L
+    cos = torch.tensor([[0.9, 0.1, -0.2], [0.3, 0.5, 0.0]])
+    y = torch.tensor([0, 1])
+    s, m = 10.0, 0.3
+    want = []
+    for r in range(2):
+        logits = [s * math.cos(math.acos(float(cos[r, c])) + m) if c == int(y[r]) else s * float(cos[r, c])
+                  for c in range(3)]
+        want.append(-math.log(math.exp(logits[int(y[r])]) / sum(math.exp(v) for v in logits)))
+    assert float(L.ArcFaceLoss(s, m)(cos, y)) == pytest.approx(sum(want) / 2, rel=1e-5)
+    a, b = torch.tensor([[1.0, 0.0]]), torch.tensor([[0.0, 1.0]])
+    assert float(L.AngularDistanceLoss()(a, b)) == pytest.approx(math.pi / 2)
+    assert float(L.CauchyLoss(2.0)(torch.tensor([3.0]), torch.tensor([1.0]))) == pytest.approx(0.5 * 4 * math.log(2.0))
+    dr, df = torch.tensor([0.8, 1.2]), torch.tensor([0.1, -0.3])
+    assert float(L.LSGANLoss.discriminator_loss(dr, df)) == pytest.approx(
+        0.5 * float(((dr - 1) ** 2).mean()) + 0.5 * float((df ** 2).mean()))
+    assert float(L.RelativisticLoss.discriminator_loss(dr, df)) == pytest.approx(
+        float(F.softplus(-(dr - df.mean())).mean() + F.softplus(df - dr.mean()).mean()))
