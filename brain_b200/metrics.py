@@ -5,6 +5,7 @@ from __future__ import annotations
 
 import math
 from collections import Counter
+from dataclasses import dataclass, field
 
 import torch
 
@@ -349,3 +350,182 @@ class MetricTracker:
     def report(self) -> str:
         return "\n".join(f"{k}: mean={s['mean']:.6g} min={s['min']:.6g} max={s['max']:.6g} n={s['count']}"
                          for k, s in self.summary().items())
+
+
+# ------------------------------------------------------------------ reports, calibration, imbalance, time series
+def g_mean_score(tp: int, tn: int, fp: int, fn: int) -> float:
+    """sqrt(sensitivity x specificity), each 0 when its denominator is 0
+    (crates/brain-metric/src/imbalance.rs)."""
+    sens = tp / (tp + fn) if tp + fn else 0.0
+    spec = tn / (tn + fp) if tn + fp else 0.0
+    return math.sqrt(sens * spec)
+
+
+def mase_score(forecast, actual, seasonality_lag: int = 1) -> float:
+    """MAE of the forecast over the MAE of the seasonal-naive forecast y[t - lag] (1 when that is 0; 0 for
+    series no longer than the lag; crates/brain-metric/src/time_series.rs)."""
+    f, y = _f(forecast).reshape(-1), _f(actual).reshape(-1)
+    n = min(f.numel(), y.numel())
+    if n <= seasonality_lag:
+        return 0.0
+    mae_f = float((f[:n] - y[:n]).abs().mean())
+    mae_n = float((y[seasonality_lag:n] - y[:n - seasonality_lag]).abs().mean())
+    return mae_f / mae_n if mae_n > 0 else 1.0
+
+
+def forecast_bias(forecast, actual) -> float:
+    f, y = _f(forecast).reshape(-1), _f(actual).reshape(-1)
+    n = min(f.numel(), y.numel())
+    return float((f[:n] - y[:n]).mean()) if n else 0.0
+
+
+def median_absolute_error(p, t) -> float:
+    return float((_f(p) - _f(t)).abs().median())
+
+
+def huber_metric(p, t, delta: float = 1.0) -> float:
+    r = (_f(p) - _f(t)).abs()
+    return float(torch.where(r <= delta, 0.5 * r * r, delta * (r - 0.5 * delta)).mean())
+
+
+def meteor_score_lite(hypothesis, reference) -> float:
+    """Unigram-set matches m: P = m / |hyp|, R = m / |ref|, score 10 P R / (R + 9 P) (0 without matches)."""
+    m = len(set(hypothesis) & set(reference))
+    if m == 0:
+        return 0.0
+    p, r = m / max(len(hypothesis), 1), m / max(len(reference), 1)
+    return 10 * p * r / (r + 9 * p)
+
+
+def cluster_purity(assignments, labels) -> float:
+    """Fraction of points that carry their cluster's majority label."""
+    a, y = torch.as_tensor(assignments).long().reshape(-1), torch.as_tensor(labels).long().reshape(-1)
+    n = min(a.numel(), y.numel())
+    if n == 0:
+        return 0.0
+    a, y = a[:n], y[:n]
+    ny = int(y.max()) + 1
+    counts = torch.zeros(int(a.max()) + 1, ny, dtype=torch.long).index_put_((a, y), torch.ones(n, dtype=torch.long),
+                                                                           accumulate=True)
+    return float(counts.max(1).values.sum()) / n
+
+
+def threshold_sweep_roc(probs, targets, num_thresholds: int = 100):
+    """(TPR, FPR) at thresholds k / num_thresholds, k = 0..num_thresholds (predict positive when p >= t),
+    all thresholds at once as one [T, N] comparison."""
+    p, y = _f(probs).reshape(-1), torch.as_tensor(targets).reshape(-1) == 1
+    th = torch.arange(num_thresholds + 1, dtype=p.dtype) / num_thresholds
+    pred = p[None, :] >= th[:, None]
+    npos, nneg = int(y.sum()), int((~y).sum())
+    tpr = (pred & y).sum(1).double() / npos if npos else torch.zeros(len(th), dtype=torch.float64)
+    fpr = (pred & ~y).sum(1).double() / nneg if nneg else torch.zeros(len(th), dtype=torch.float64)
+    return tpr, fpr
+
+
+def pr_auc_score(scores, target) -> float:
+    """Area under the precision-recall curve by the trapezoid rule over the sorted scores."""
+    s, y = _f(scores).reshape(-1), torch.as_tensor(target).reshape(-1).double()
+    order = torch.argsort(s, descending=True, stable=True)
+    y = y[order]
+    tp = torch.cumsum(y, 0)
+    prec = tp / torch.arange(1, len(y) + 1, dtype=torch.float64)
+    rec = tp / y.sum().clamp_min(1)
+    rec = torch.cat([torch.zeros(1, dtype=torch.float64), rec])
+    prec = torch.cat([prec[:1], prec])
+    return float(torch.trapz(prec, rec))
+
+
+def multiclass_roc_auc(probs, target) -> float:
+    """Macro one-vs-rest ROC AUC over the classes present in ``target``."""
+    pr = _f(probs)
+    t = torch.as_tensor(target).long().reshape(-1)
+    aucs = [roc_auc(pr[:, c], (t == c).long()) for c in range(pr.shape[1]) if bool((t == c).any()) and bool((t != c).any())]
+    return float(sum(aucs) / len(aucs)) if aucs else 0.0
+
+
+@dataclass
+class CalibrationReport:
+    ece: float = 0.0
+    mce: float = 0.0
+    bin_accuracies: list = field(default_factory=list)
+    bin_confidences: list = field(default_factory=list)
+
+
+def compute_calibration(confidences, correct, num_bins: int = 15) -> CalibrationReport:
+    """Expected and maximum calibration error over uniform confidence bins (confidence clamped below 1)."""
+    c = _f(confidences).reshape(-1).clamp(0.0, 1.0 - 1e-9)
+    ok = torch.as_tensor(correct).reshape(-1).double()
+    b = (c * num_bins).floor().long().clamp(max=num_bins - 1)
+    cnt = torch.bincount(b, minlength=num_bins).double()
+    acc = torch.bincount(b, ok, minlength=num_bins) / cnt.clamp_min(1)
+    conf = torch.bincount(b, c, minlength=num_bins) / cnt.clamp_min(1)
+    gap = (acc - conf).abs() * (cnt > 0)
+    n = c.numel()
+    return CalibrationReport(float((cnt / max(n, 1) * gap).sum()), float(gap.max()) if n else 0.0, acc.tolist(),
+                             conf.tolist())
+
+
+@dataclass
+class AggregateReport:
+    mean: float = 0.0
+    std_dev: float = 0.0
+    min: float = 0.0
+    max: float = 0.0
+    ci_95_lower: float = 0.0
+    ci_95_upper: float = 0.0
+
+
+def aggregate_metric_runs(values) -> AggregateReport:
+    """Mean, sample standard deviation and a normal 95 % interval mean +- 1.96 sd / sqrt(n) over runs."""
+    v = torch.as_tensor(list(values), dtype=torch.float64)
+    n = v.numel()
+    if n == 0:
+        return AggregateReport()
+    sd = float(v.std()) if n > 1 else 0.0
+    mg = 1.96 * sd / math.sqrt(n) if n > 1 else 0.0
+    m = float(v.mean())
+    return AggregateReport(m, sd, float(v.min()), float(v.max()), m - mg, m + mg)
+
+
+@dataclass
+class CompareReport:
+    delta: float
+    relative_gain_pct: float
+    is_model_a_better: bool
+
+
+def compare_models(score_a: float, score_b: float) -> CompareReport:
+    d = score_a - score_b
+    return CompareReport(d, d / score_b * 100.0 if abs(score_b) > 1e-12 else 0.0, d > 0)
+
+
+class MetricTracker:
+    """Count-weighted running means of named metrics."""
+
+    def __init__(self):
+        self.sums: dict[str, float] = {}
+        self.counts: dict[str, int] = {}
+
+    def update(self, name: str, value: float, count: int = 1) -> None:
+        self.sums[name] = self.sums.get(name, 0.0) + float(value) * count
+        self.counts[name] = self.counts.get(name, 0) + count
+
+    def mean(self, name: str):
+        c = self.counts.get(name, 0)
+        return self.sums[name] / c if c else None
+
+    def summary(self) -> dict:
+        return {k: self.sums[k] / c for k, c in self.counts.items() if c}
+
+    def reset(self) -> None:
+        self.sums.clear()
+        self.counts.clear()
+
+
+def format_markdown_report(metrics: dict, title: str = "Metrics") -> str:
+    rows = "\n".join(f"| {k} | {v:.4f} |" for k, v in sorted(metrics.items()))
+    return f"## {title}\n\n| metric | value |\n|---|---|\n{rows}\n"
+
+
+def format_csv_report(metrics: dict) -> str:
+    return "metric,value\n" + "".join(f"{k},{v}\n" for k, v in sorted(metrics.items()))

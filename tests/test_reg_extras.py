@@ -94,3 +94,32 @@ def test_metric_robust_adversarial_losses():
         0.5 * float(((dr - 1) ** 2).mean()) + 0.5 * float((df ** 2).mean()))
     assert float(L.RelativisticLoss.discriminator_loss(dr, df)) == pytest.approx(
         float(F.softplus(-(dr - df.mean())).mean() + F.softplus(df - dr.mean()).mean()))
+
+
+def test_metric_extras():
+    from brain_b200 import metrics as M
+    assert M.g_mean_score(8, 9, 1, 2) == pytest.approx(math.sqrt(0.8 * 0.9)) and M.g_mean_score(0, 0, 0, 0) == 0.0
+    y = torch.tensor([1.0, 2.0, 4.0, 7.0])
+    f = torch.tensor([1.5, 2.5, 3.5, 6.0])
+    assert M.mase_score(f, y, 1) == pytest.approx((0.5 + 0.5 + 0.5 + 1.0) / 4 / ((1 + 2 + 3) / 3))
+    assert M.forecast_bias(f, y) == pytest.approx(-0.125)
+    assert M.meteor_score_lite("a b c".split(), "a b d e".split()) == pytest.approx(
+        10 * (2 / 3) * 0.5 / (0.5 + 9 * (2 / 3)))
+    assert M.cluster_purity([0, 0, 1, 1, 1], [1, 1, 0, 0, 1]) == pytest.approx(4 / 5)
+    tpr, fpr = M.threshold_sweep_roc(torch.tensor([0.9, 0.2, 0.6, 0.4]), torch.tensor([1, 0, 1, 0]), 4)
+    assert tpr.tolist() == [1.0, 1.0, 1.0, 0.5, 0.0] and fpr.tolist() == [1.0, 0.5, 0.0, 0.0, 0.0]
+    assert M.pr_auc_score(torch.tensor([0.9, 0.8, 0.1]), torch.tensor([1, 1, 0])) == pytest.approx(1.0)
+    probs = torch.tensor([[0.8, 0.1, 0.1], [0.1, 0.8, 0.1], [0.1, 0.1, 0.8], [0.6, 0.3, 0.1]])
+    assert M.multiclass_roc_auc(probs, torch.tensor([0, 1, 2, 0])) == pytest.approx(1.0)
+    rep = M.compute_calibration(torch.tensor([0.95, 0.95, 0.15, 0.15]), torch.tensor([1, 0, 0, 0]), 10)
+    assert rep.ece == pytest.approx(0.5 * 0.45 + 0.5 * 0.15) and rep.mce == pytest.approx(0.45)
+    ag = M.aggregate_metric_runs([1.0, 2.0, 3.0])
+    assert ag.mean == 2.0 and ag.std_dev == pytest.approx(1.0) and ag.ci_95_upper == pytest.approx(2 + 1.96 / math.sqrt(3))
+    cr = M.compare_models(0.9, 0.8)
+    assert cr.is_model_a_better and cr.relative_gain_pct == pytest.approx(12.5)
+    tr = M.MetricTracker()
+    tr.update("loss", 1.0, 2)
+    tr.update("loss", 4.0, 1)
+    assert tr.mean("loss") == pytest.approx(2.0) and tr.mean("x") is None
+    assert "| loss | 2.0000 |" in M.format_markdown_report(tr.summary()) and M.format_csv_report({"a": 1}) == "metric,value\na,1\n"
+    assert M.huber_metric(torch.tensor([0.0, 3.0]), torch.tensor([0.5, 0.0])) == pytest.approx((0.125 + 2.5) / 2)
