@@ -429,8 +429,9 @@ BRAIN_API int brain_comm_allreduce_oneshot(const void* in, void* out, int64_t n,
   if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return (int)cudaErrorInvalidValue;
   const int V = dtype == 0 ? 4 : 8;
   const int64_t nv = n / V;
-  // about 1024 vectors (16 KB) per CTA, so mid-size messages spread over up to 128 SMs
-  const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>(kOneShotCtas, (nv + 1023) / 1024));
+  // one vector per thread where possible: the time is a few NVLink load latencies per loop trip, so trips
+  // (not bytes) set the cost up to 128 CTAs x 256 threads x 16 bytes = 512 KB per trip
+  const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>(kOneShotCtas, (nv + 255) / 256));
   Peers sp = to_peers(stage, world), fp = to_peers(flags, world);
   if (dtype == 0)
     oneshot_allreduce_kernel<float><<<ctas, 256, 0, st>>>(reinterpret_cast<const float*>(in),
