@@ -217,3 +217,43 @@ class LRFinder:
             if not math.isfinite(loss) or (losses and loss > 4 * min(losses)):
                 break
         return lrs, losses
+
+
+class NoamLR(LRScheduler):
+    """Transformer schedule (Vaswani et al. 2017): factor d_model^-0.5 min(s^-0.5, s warmup^-1.5) with
+    s = max(step, 1) (crates/brain-optim/src/schedulers/warmup.rs, NoamLR)."""
+
+    def __init__(self, optimizer, d_model: int, warmup_steps: int = 4000, factor: float = 1.0):
+        super().__init__(optimizer)
+        self.d, self.w, self.f = d_model, max(warmup_steps, 1), factor
+
+    def lr_at(self, step: int) -> float:
+        s = max(step, 1)
+        return self.f * self.d ** -0.5 * min(s ** -0.5, s * self.w ** -1.5)
+
+
+class ChainedScheduler:
+    """Several schedulers stepped together; each one's lr_at acts as a multiplicative factor on the base
+    learning rate relative to its own base, so e.g. warmup x cosine compose."""
+
+    def __init__(self, optimizer, schedulers):
+        self.optimizer, self.schedulers = optimizer, list(schedulers)
+        self.base_lr = optimizer.get_lr()
+        self.last_step = 0
+
+    def lr_at(self, step: int) -> float:
+        lr = self.base_lr
+        for s in self.schedulers:
+            lr *= s.lr_at(step) / s.base_lr if s.base_lr else 1.0
+        return lr
+
+    def get_lr(self) -> float:
+        return self.lr_at(self.last_step)
+
+    def step(self, *_):
+        self.last_step += 1
+        for s in self.schedulers:
+            s.last_step = self.last_step
+        lr = self.lr_at(self.last_step)
+        self.optimizer.set_lr(lr)
+        return lr

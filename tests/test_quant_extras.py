@@ -93,3 +93,48 @@ def test_pruning_schedules():
     w0 = net[0].weight
     m = lt.masks["0.weight"]
     assert torch.equal(w0[m], lt.init["0.weight"][m]) and float(w0[~m].abs().sum()) == 0.0
+
+
+def test_noam_chained_and_loss_landscape():
+    from brain_b200.optim import schedulers as S
+    from brain_b200.optim.landscape import LossLandscapeConfig, create_filter_normalized_direction, interpolate_1d, loss_surface
+
+    class Opt:
+        lr = 1.0
+
+        def get_lr(self):
+            return self.lr
+
+        def set_lr(self, v):
+            self.lr = v
+
+    o = Opt()
+    n = S.NoamLR(o, d_model=512, warmup_steps=100)
+    assert n.lr_at(50) == pytest.approx(512 ** -0.5 * 50 * 100 ** -1.5)
+    assert n.lr_at(400) == pytest.approx(512 ** -0.5 * 400 ** -0.5)
+    o2 = Opt()
+    o2.lr = 0.1
+
+    class Half(S.LRScheduler):
+        def lr_at(self, step):
+            return self.base_lr * 0.5
+
+    ch = S.ChainedScheduler(o2, [Half(o2), Half(o2)])
+    assert ch.step() == pytest.approx(0.025) and o2.lr == pytest.approx(0.025)
+    w = torch.randn(4, 6)
+    d = create_filter_normalized_direction(w, generator=torch.Generator().manual_seed(0))
+    torch.testing.assert_close(d.norm(dim=1), w.norm(dim=1))
+    assert float(create_filter_normalized_direction(torch.randn(5)).abs().sum()) == 0.0
+    dc = create_filter_normalized_direction(w, kind="constant")
+    assert float(dc.norm()) == pytest.approx(float(w.norm()), rel=1e-5) and torch.allclose(dc, dc.flatten()[0].expand_as(dc))
+    assert torch.equal(interpolate_1d([w], [d], 0.0)[0], w)
+    lin = torch.nn.Linear(3, 1)
+    x, y = torch.randn(16, 3), torch.randn(16, 1)
+    before = [p.detach().clone() for p in lin.parameters()]
+    xs, ls = loss_surface(lin, lambda m: torch.nn.functional.mse_loss(m(x), y), LossLandscapeConfig(num_points=5),
+                          generator=torch.Generator().manual_seed(1))
+    assert ls.shape == (5,) and float(ls[2]) == pytest.approx(float(torch.nn.functional.mse_loss(lin(x), y)))
+    assert all(torch.equal(a, b) for a, b in zip(before, lin.parameters()))
+    _, _, surf = loss_surface(lin, lambda m: torch.nn.functional.mse_loss(m(x), y), LossLandscapeConfig(num_points=3),
+                              two_d=True)
+    assert surf.shape == (3, 3)
