@@ -162,6 +162,68 @@ __global__ void oneshot_allreduce_kernel(const T* in, T* out, int64_t n, Peers s
     }
 }
 
+// Mid- and large-size all-reduce in one launch (reduce-scatter + all-gather, two signal phases). The vector
+// is split into `world` shards; CTA c owns slice c of every shard (the same element positions on every
+// rank). Phase A: copy this CTA's slices of `in` into this rank's staging, signal flag c (epoch e1), wait for
+// every rank's flag c. Phase B: sum slice c of shard `rank` over all ranks' staging (rank 0 first), scale,
+// and store the result into that position of every rank's staging (only this rank reads or writes shard
+// `rank` there), signal flag c (epoch e1 + 1), wait for every rank's flag c. Phase C: copy this CTA's
+// slices of all shards from the staging into `out` (which may alias `in`). A rank starts its next call only
+// after all its CTAs saw every peer finish phase B, so one staging buffer is enough. flags: int32 [128][8].
+template <typename T>
+__global__ void twoshot_allreduce_kernel(const T* in, T* out, int64_t n, Peers stage, Peers flags, int rank,
+                                         int world, int e1, int64_t budget_ns, float scale) {
+  constexpr int V = Vec<T>::N;
+  const int64_t S = n / world;  // shard length (a whole number of vectors)
+  const int64_t nvs = S / V;
+  const int64_t per = (nvs + gridDim.x - 1) / gridDim.x;
+  const int64_t v0 = blockIdx.x * per, v1 = v0 + per < nvs ? v0 + per : nvs;
+  T* mine = reinterpret_cast<T*>(stage.p[rank]);
+  for (int s = 0; s < world; ++s)
+    for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x)
+      *reinterpret_cast<uint4*>(mine + s * S + i * V) = *reinterpret_cast<const uint4*>(in + s * S + i * V);
+  for (int phase = 0; phase < 2; ++phase) {
+    __syncthreads();
+    if (threadIdx.x < world) {
+      const int j = threadIdx.x;
+      __threadfence_system();
+      st_release_sys(reinterpret_cast<int*>(flags.p[j]) + blockIdx.x * kMaxRanks + rank, e1 + phase);
+      const int* f = reinterpret_cast<const int*>(flags.p[rank]) + blockIdx.x * kMaxRanks + j;
+      const uint64_t t0 = globaltimer();
+      while (ld_acquire_sys(f) < e1 + phase) {
+        if (globaltimer() - t0 > (uint64_t)budget_ns) {
+          set_status(BRAIN_ERR_TIMEOUT_PEER, 1300 + phase * 16 + j);
+          break;
+        }
+      }
+    }
+    __syncthreads();
+    if (phase == 0) {
+      const int64_t base = rank * S;
+      for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x) {
+        float acc[V];
+#pragma unroll
+        for (int k = 0; k < V; ++k) acc[k] = 0.f;
+        for (int j = 0; j < world; ++j) {
+          float x[V];
+          ld_vec(reinterpret_cast<const T*>(stage.p[j]) + base + i * V, x);
+#pragma unroll
+          for (int k = 0; k < V; ++k) acc[k] += x[k];
+        }
+#pragma unroll
+        for (int k = 0; k < V; ++k) acc[k] *= scale;
+        for (int jj = 0; jj < world; ++jj) {
+          const int j = (rank + jj) % world;  // stagger the pushes so ranks do not all hit one peer
+          st_vec(reinterpret_cast<T*>(stage.p[j]) + base + i * V, acc);
+        }
+      }
+    }
+  }
+  for (int s = 0; s < world; ++s)
+    for (int64_t i = v0 + threadIdx.x; i < v1; i += blockDim.x)
+      *reinterpret_cast<uint4*>(out + s * S + i * V) = *reinterpret_cast<const uint4*>(mine + s * S + i * V);
+}
+
 // dst[dst_off + i] = peer_src[src_off + i]  (copy of n elements, 16-byte vectors)
 __global__ void copy_pull_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, int64_t nbytes) {
   const int64_t nv = nbytes / 16;
@@ -441,5 +503,29 @@ BRAIN_API int brain_comm_allreduce_oneshot(const void* in, void* out, int64_t n,
     oneshot_allreduce_kernel<__nv_bfloat16><<<ctas, 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), n, sp, fp, rank, world,
         epoch, budget_ns, scale);
+  return (int)cudaGetLastError();
+}
+
+// One-launch two-phase all-reduce (dtype 0 = f32, 1 = bf16; n a multiple of world x the 16-byte vector; in,
+// out 16-byte aligned, may alias). stage: int64[world] peer pointers of staging buffers of >= n elements;
+// flags: int64[world] peer pointers of int32 [128][8] flag arrays (zeroed once, not shared with other
+// kernels). e1: this call's first epoch; the call uses e1 and e1 + 1.
+BRAIN_API int brain_comm_allreduce_twoshot(const void* in, void* out, int64_t n, int dtype, float scale,
+                                           const int64_t* stage, const int64_t* flags, int rank, int world, int e1,
+                                           int64_t budget_ns, cudaStream_t st) {
+  const int V = dtype == 0 ? 4 : 8;
+  if (world > kMaxRanks || world < 1 || n < 1 || n % ((int64_t)world * V)) return (int)cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(in) & 15) || (reinterpret_cast<uintptr_t>(out) & 15)) return (int)cudaErrorInvalidValue;
+  const int64_t nvs = n / world / V;
+  const int ctas = (int)std::max<int64_t>(1, std::min<int64_t>(kOneShotCtas, (nvs + 255) / 256));
+  Peers sp = to_peers(stage, world), fp = to_peers(flags, world);
+  if (dtype == 0)
+    twoshot_allreduce_kernel<float><<<ctas, 256, 0, st>>>(reinterpret_cast<const float*>(in),
+                                                          reinterpret_cast<float*>(out), n, sp, fp, rank, world, e1,
+                                                          budget_ns, scale);
+  else
+    twoshot_allreduce_kernel<__nv_bfloat16><<<ctas, 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(in), reinterpret_cast<__nv_bfloat16*>(out), n, sp, fp, rank, world,
+        e1, budget_ns, scale);
   return (int)cudaGetLastError();
 }

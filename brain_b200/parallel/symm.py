@@ -22,6 +22,7 @@ from .. import _native
 
 _native.register({
     "brain_comm_allreduce_oneshot": ("brain_comm", "pplifppiiils"),
+    "brain_comm_allreduce_twoshot": ("brain_comm", "pplifppiiils"),
     "brain_ipc_alloc": ("brain_comm", "lpp"),
     "brain_ipc_handle_size": ("brain_comm", ""),
     "brain_ipc_open": ("brain_comm", "pp"),
@@ -111,6 +112,7 @@ class NvlinkComm:
     name = "nvlink"
     ONE_SHOT_BYTES = 256 * 1024  # staged fallback (unaligned tensors) up to this size
     ONE_LAUNCH_BYTES = 2 << 20  # one-launch all-reduce up to this size (each rank reads every rank's copy)
+    TWO_PHASE_BYTES = 256 << 20  # one-launch reduce-scatter + all-gather up to this size
     PUSH_BYTES = 4 << 20  # all-gather shards from this size are pushed (one more barrier, more bytes in flight)
 
     def __init__(self, group=None, timeout_s: float = 60.0):
@@ -130,7 +132,11 @@ class NvlinkComm:
         self.os_stage_arr = [self.os_stage.peer_array(0), self.os_stage.peer_array(self.ONE_LAUNCH_BYTES)]
         self.os_flags = SymmetricBuffer(128 * 8 * 4, group)
         self.os_epoch = 0
-        self.os_stream: torch.cuda.Stream | None = None  # stream of the last one-shot launch
+        self.os_stream: torch.cuda.Stream | None = None  # stream of the last one-launch all-reduce
+        # one-launch two-phase all-reduce: its own staging (grown on demand) and flags
+        self.ts_stage: SymmetricBuffer | None = None
+        self.ts_flags = SymmetricBuffer(128 * 8 * 4, group)
+        self.ts_epoch = 0
         dist.barrier(group)
 
     # ------------------------------------------------------------------ plumbing
@@ -166,6 +172,15 @@ class NvlinkComm:
         torch.cuda.synchronize()
         _check_status()
 
+    def _ordered_stream(self):
+        """The current stream, made to wait for the stream of the previous one-launch all-reduce when it
+        differs: the flag protocols of those kernels rely on each rank's calls running in issue order."""
+        cur = torch.cuda.current_stream()
+        if self.os_stream is not None and cur != self.os_stream:
+            cur.wait_stream(self.os_stream)
+        self.os_stream = cur
+        return cur
+
     # ------------------------------------------------------------------ collectives
     def all_reduce(self, t: torch.Tensor, op: str = "sum") -> torch.Tensor:
         if op not in ("sum", "mean", "avg"):
@@ -185,14 +200,23 @@ class NvlinkComm:
             # one launch: copy into this rank's staging half, signal, pull-sum every rank's copy into t.
             # Reusing a staging half two calls later is safe only if this rank's calls run in issue order,
             # so a call on another stream than the previous one first waits for that one.
-            cur = torch.cuda.current_stream()
-            if self.os_stream is not None and cur != self.os_stream:
-                cur.wait_stream(self.os_stream)
-            self.os_stream = cur
+            cur = self._ordered_stream()
             self.os_epoch += 1
             _native.call("brain_comm_allreduce_oneshot", t.data_ptr(), t.data_ptr(), n, dcode, scale,
                          self.os_stage_arr[self.os_epoch & 1], self.os_flags.ptr_array, self.rank, self.world,
                          self.os_epoch, self.timeout_ns, cur.cuda_stream)
+            return t
+        if (n * esz <= self.TWO_PHASE_BYTES and n % (self.world * vec) == 0 and t.data_ptr() % 16 == 0):
+            # one launch: copy in, reduce this rank's shard and push it to every rank, copy out
+            if self.ts_stage is None or self.ts_stage.nbytes < n * esz:
+                if self.ts_stage is not None:
+                    self.ts_stage.close()
+                self.ts_stage = SymmetricBuffer(max(n * esz, 8 << 20), self.group)
+            cur = self._ordered_stream()
+            _native.call("brain_comm_allreduce_twoshot", t.data_ptr(), t.data_ptr(), n, dcode, scale,
+                         self.ts_stage.ptr_array, self.ts_flags.ptr_array, self.rank, self.world, self.ts_epoch + 1,
+                         self.timeout_ns, cur.cuda_stream)
+            self.ts_epoch += 2
             return t
         if n * esz <= self.ONE_SHOT_BYTES:
             npad = -(-n // vec) * vec
@@ -321,4 +345,8 @@ class NvlinkComm:
         if self.staging is not None:
             self.staging.close()
             self.staging = None
+        for b in (self.os_stage, self.os_flags, self.ts_flags, self.ts_stage):
+            if b is not None:
+                b.close()
+        self.ts_stage = None
         self.pads.close()

@@ -160,9 +160,10 @@ def test_nvlink_collectives():
 
 
 def _gpu_oneshot(rank, world):
-    """Many all-reduces up to 2 MB in a row through the one-launch path (staging reused by call parity), odd
-    lengths, unaligned views (staged fallback), random per-rank GPU delays and a stream switch, against a
-    float64 sum of the gathered inputs; every rank must hold bitwise the same result."""
+    """Many all-reduces in a row: up to 2 MB through the one-launch kernel (staging reused by call parity),
+    2-6 MB through the one-launch two-phase kernel, odd lengths, unaligned views (staged fallback), random
+    per-rank GPU delays and a stream switch, against a float64 sum of the gathered inputs; every rank must
+    hold bitwise the same result."""
     import random
 
     import torch.distributed as dist
@@ -179,6 +180,8 @@ def _gpu_oneshot(rank, world):
         dtype = torch.float32 if it % 3 else torch.bfloat16
         vec = 4 if dtype == torch.float32 else 8
         n = vec * rng.randint(1, comm.ONE_LAUNCH_BYTES // (vec * (4 if dtype == torch.float32 else 2)))
+        if it % 6 == 4:  # past the one-launch size: the two-phase kernel (a multiple of world x vector)
+            n = world * vec * rng.randint(comm.ONE_LAUNCH_BYTES // (world * vec * 2) + 1, (6 << 20) // (world * vec * 2))
         if it % 5 == 2:
             n = rng.randint(1, 3000)  # any length: the last CTA also sums the scalar tail
         g = torch.Generator(device="cuda").manual_seed(1000 * it + rank)
