@@ -330,26 +330,42 @@ def adjusted_rand_index(a: torch.Tensor, b: torch.Tensor) -> float:
 
 # ------------------------------------------------------------------ streaming
 class MetricTracker:
-    """Streaming mean/min/max/count of named scalars (track.rs / aggregate.rs)."""
+    """Streaming count-weighted mean and min/max of named scalars (track.rs / aggregate.rs):
+    ``update(loss=0.3, acc=0.9)`` adds one sample per name; ``update("loss", 0.3, count=32)`` adds a
+    batch-mean weighted by its sample count (the reference's form)."""
 
     def __init__(self):
-        self.data: dict[str, list[float]] = {}
+        self.sums: dict[str, float] = {}
+        self.counts: dict[str, int] = {}
+        self.mins: dict[str, float] = {}
+        self.maxs: dict[str, float] = {}
 
-    def update(self, **kv):
-        for k, v in kv.items():
-            self.data.setdefault(k, []).append(float(v))
+    def update(self, name: str | None = None, value: float | None = None, count: int = 1, **kv):
+        items = dict(kv)
+        if name is not None:
+            items[name] = value
+        for k, v in items.items():
+            v = float(v)
+            self.sums[k] = self.sums.get(k, 0.0) + v * count
+            self.counts[k] = self.counts.get(k, 0) + count
+            self.mins[k] = min(self.mins.get(k, v), v)
+            self.maxs[k] = max(self.maxs.get(k, v), v)
 
     def mean(self, k) -> float:
-        v = self.data.get(k, [])
-        return sum(v) / len(v) if v else float("nan")
+        c = self.counts.get(k, 0)
+        return self.sums[k] / c if c else float("nan")
 
     def summary(self) -> dict:
-        return {k: {"mean": sum(v) / len(v), "min": min(v), "max": max(v), "count": len(v)}
-                for k, v in self.data.items() if v}
+        return {k: {"mean": self.sums[k] / c, "min": self.mins[k], "max": self.maxs[k], "count": c}
+                for k, c in self.counts.items() if c}
 
     def report(self) -> str:
         return "\n".join(f"{k}: mean={s['mean']:.6g} min={s['min']:.6g} max={s['max']:.6g} n={s['count']}"
                          for k, s in self.summary().items())
+
+    def reset(self) -> None:
+        for d in (self.sums, self.counts, self.mins, self.maxs):
+            d.clear()
 
 
 # ------------------------------------------------------------------ reports, calibration, imbalance, time series
@@ -497,29 +513,6 @@ class CompareReport:
 def compare_models(score_a: float, score_b: float) -> CompareReport:
     d = score_a - score_b
     return CompareReport(d, d / score_b * 100.0 if abs(score_b) > 1e-12 else 0.0, d > 0)
-
-
-class MetricTracker:
-    """Count-weighted running means of named metrics."""
-
-    def __init__(self):
-        self.sums: dict[str, float] = {}
-        self.counts: dict[str, int] = {}
-
-    def update(self, name: str, value: float, count: int = 1) -> None:
-        self.sums[name] = self.sums.get(name, 0.0) + float(value) * count
-        self.counts[name] = self.counts.get(name, 0) + count
-
-    def mean(self, name: str):
-        c = self.counts.get(name, 0)
-        return self.sums[name] / c if c else None
-
-    def summary(self) -> dict:
-        return {k: self.sums[k] / c for k, c in self.counts.items() if c}
-
-    def reset(self) -> None:
-        self.sums.clear()
-        self.counts.clear()
 
 
 def format_markdown_report(metrics: dict, title: str = "Metrics") -> str:

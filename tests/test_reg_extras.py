@@ -120,6 +120,8 @@ def test_metric_extras():
     tr = M.MetricTracker()
     tr.update("loss", 1.0, 2)
     tr.update("loss", 4.0, 1)
-    assert tr.mean("loss") == pytest.approx(2.0) and tr.mean("x") is None
-    assert "| loss | 2.0000 |" in M.format_markdown_report(tr.summary()) and M.format_csv_report({"a": 1}) == "metric,value\na,1\n"
+    assert tr.mean("loss") == pytest.approx(2.0) and math.isnan(tr.mean("x"))
+    assert tr.summary()["loss"]["count"] == 3 and tr.summary()["loss"]["max"] == 4.0
+    assert "| loss | 2.0000 |" in M.format_markdown_report({"loss": tr.mean("loss")})
+    assert M.format_csv_report({"a": 1}) == "metric,value\na,1\n"
     assert M.huber_metric(torch.tensor([0.0, 3.0]), torch.tensor([0.5, 0.0])) == pytest.approx((0.125 + 2.5) / 2)
