@@ -1,5 +1,6 @@
 """The plain-PyTorch comparison arm of the benchmark: it starts from exactly the framework model's
 weights, and its float32-master AdamW matches torch.optim.AdamW on float32 weights."""
+import pytest
 import torch
 
 from brain_b200.bench.torch_baseline import MasterAdamW, build
@@ -88,3 +89,16 @@ def test_torch_decode_arm_shard_shapes():
     assert dec.layers[0]["wqkv"].shape == ((2 + 2) * 16, 64) and dec.layers[0]["wd"].shape == (64, 48)
     tok = dec.generate(torch.zeros(2, 4, dtype=torch.long), 3, graph=False)
     assert int(tok.max()) < dec.vloc  # a lone shard picks within its own vocabulary slice
+
+
+def test_bench_link_roofline_fields():
+    import importlib.util
+    import os
+    spec = importlib.util.spec_from_file_location("bench_main", os.path.join(os.path.dirname(__file__), "..", "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    assert bench._ddp_link_roofline(8_000_000_000, 1, 430.0) is None
+    r = bench._ddp_link_roofline(8_000_000_000, 8, 440.0)
+    assert r["bytes_in_per_rank_per_step"] == 2 * 7 / 8 * 8e9 * 2
+    assert r["transfer_ms_at_link_rate"] == pytest.approx(r["bytes_in_per_rank_per_step"] / 770e9 * 1e3)
+    assert 0 < r["share_of_step"] < 1
