@@ -99,3 +99,25 @@ def init_normal_(module: torch.nn.Module, std: float = 0.02, seed: int = 0) -> N
             zeros_(p)
         else:
             ones_(p)
+
+
+def calculate_fan(shape) -> tuple[int, int]:
+    """(fan_in, fan_out) of a weight shape: [out, in, *kernel] -> (in * k, out * k); 1-D -> (n, n)."""
+    shape = tuple(shape)
+    if len(shape) < 2:
+        n = shape[0] if shape else 1
+        return n, n
+    rf = 1
+    for d in shape[2:]:
+        rf *= d
+    return shape[1] * rf, shape[0] * rf
+
+
+def scaled_residual_init(weight: torch.Tensor, num_residual_layers: int) -> torch.Tensor:
+    """weight / sqrt(2 L): the GPT-2 scaling of residual-branch output projections."""
+    return weight * (1.0 / math.sqrt(2.0 * max(num_residual_layers, 1)))
+
+
+def zero_init_last_layer(shape, dtype=torch.float32, device=None) -> torch.Tensor:
+    """A zero weight, so a residual block starts as the identity."""
+    return torch.zeros(tuple(shape), dtype=dtype, device=device)

@@ -328,3 +328,119 @@ def num_params(m: torch.nn.Module) -> int:
 
 __all__ = [n for n in dir() if not n.startswith("_") and n[0].isupper()] + ["scaled_dot_product_attention",
                                                                              "num_params", "math"]
+
+
+# ------------------------------------------------------------------ further activations (crates/brain-nn/src/activations/extra.rs, extended.rs)
+class CELU(Module):
+    """x for x > 0, alpha (exp(x / alpha) - 1) otherwise (alpha > 0)."""
+
+    def __init__(self, alpha: float = 1.0):
+        super().__init__()
+        if alpha <= 0:
+            raise ValueError("CELU alpha must be positive")
+        self.alpha = alpha
+
+    def forward(self, x):
+        return torch.where(x > 0, x, self.alpha * torch.expm1(x / self.alpha))
+
+
+class HardShrink(Module):
+    """x where |x| > lambda, else 0."""
+
+    def __init__(self, lambd: float = 0.5):
+        super().__init__()
+        self.lambd = lambd
+
+    def forward(self, x):
+        return torch.where(x.abs() > self.lambd, x, torch.zeros_like(x))
+
+
+class SoftShrink(Module):
+    """x - lambda above lambda, x + lambda below -lambda, else 0."""
+
+    def __init__(self, lambd: float = 0.5):
+        super().__init__()
+        self.lambd = lambd
+
+    def forward(self, x):
+        return torch.sign(x) * (x.abs() - self.lambd).clamp_min(0)
+
+
+class Shrink(Module):
+    """ONNX Shrink: x - bias above lambda, x + bias below -lambda, else 0."""
+
+    def __init__(self, lambd: float = 0.5, bias: float = 0.5):
+        super().__init__()
+        self.lambd, self.bias = lambd, bias
+
+    def forward(self, x):
+        return torch.where(x > self.lambd, x - self.bias, torch.where(x < -self.lambd, x + self.bias,
+                                                                      torch.zeros_like(x)))
+
+
+class TanhShrink(Module):
+    def forward(self, x):
+        return x - torch.tanh(x)
+
+
+class ThresholdedReLU(Module):
+    """x where x > theta, else 0."""
+
+    def __init__(self, theta: float = 1.0):
+        super().__init__()
+        self.theta = theta
+
+    def forward(self, x):
+        return torch.where(x > self.theta, x, torch.zeros_like(x))
+
+
+class Softmin(Module):
+    def __init__(self, dim: int = -1):
+        super().__init__()
+        self.dim = dim
+
+    def forward(self, x):
+        return torch.softmax(-x, self.dim)
+
+
+def quiet_softmax(x: torch.Tensor, dim: int = -1) -> torch.Tensor:
+    """Softmax of x / (1 + exp(x)) along ``dim`` (the reference's "quiet" variant damps large logits)."""
+    return torch.softmax(x / (1.0 + torch.exp(x)), dim)
+
+
+class QuietSoftmax(Module):
+    def __init__(self, dim: int = -1):
+        super().__init__()
+        self.dim = dim
+
+    def forward(self, x):
+        return quiet_softmax(x, self.dim)
+
+
+class FusedDropout(Module):
+    """dropout(x) + residual in one call (inverted dropout; identity in eval)."""
+
+    def __init__(self, p: float = 0.1):
+        super().__init__()
+        self.p = p
+
+    def forward_add(self, x, residual):
+        return torch.nn.functional.dropout(x, self.p, self.training) + residual
+
+    forward = forward_add
+
+
+class SequentialNamed(Module):
+    """Sequential container with explicit child names (``[(name, module), ...]``)."""
+
+    def __init__(self, named):
+        super().__init__()
+        self._order = []
+        for name, m in named:
+            self.add_module(name, m)
+            self._order.append(name)
+
+    def forward(self, x):
+        for name in self._order:
+            x = getattr(self, name)(x)
+        return x

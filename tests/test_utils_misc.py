@@ -102,3 +102,30 @@ def test_schema_version_system_metrics_timing():
         t[0] += 0.25
     rep = tree.report()
     assert "step: 1 call(s), 750.00 ms" in rep and "  fwd: 1 call(s), 500.00 ms" in rep
+
+
+def test_nn_activation_and_init_extras():
+    import math
+
+    import torch
+
+    from brain_b200.nn import init as I
+    from brain_b200.nn import layers as L
+    x = torch.tensor([-2.0, -0.3, 0.0, 0.4, 1.5])
+    assert L.CELU(2.0)(x).tolist() == pytest.approx([2 * math.expm1(-1.0), 2 * math.expm1(-0.15), 0.0, 0.4, 1.5])
+    assert L.HardShrink(0.5)(x).tolist() == [-2.0, 0.0, 0.0, 0.0, 1.5]
+    assert L.SoftShrink(0.5)(x).tolist() == pytest.approx([-1.5, 0.0, 0.0, 0.0, 1.0])
+    assert L.Shrink(0.5, 0.25)(x).tolist() == pytest.approx([-1.75, 0.0, 0.0, 0.0, 1.25])
+    assert L.ThresholdedReLU(1.0)(x).tolist() == [0.0, 0.0, 0.0, 0.0, 1.5]
+    assert L.TanhShrink()(x)[4].item() == pytest.approx(1.5 - math.tanh(1.5))
+    assert torch.allclose(L.Softmin()(x), torch.softmax(-x, -1))
+    q = L.QuietSoftmax()(x[None])
+    s = x / (1 + torch.exp(x))
+    assert torch.allclose(q[0], torch.softmax(s, -1)) and float(q.sum()) == pytest.approx(1.0)
+    fd = L.FusedDropout(0.5).eval()
+    assert torch.equal(fd(x, torch.ones(5)), x + 1)
+    seq = L.SequentialNamed([("a", L.ThresholdedReLU(0.0)), ("b", L.TanhShrink())])
+    assert hasattr(seq, "a") and torch.allclose(seq(x), L.TanhShrink()(L.ThresholdedReLU(0.0)(x)))
+    assert I.calculate_fan((16, 8, 3, 3)) == (72, 144) and I.calculate_fan((5,)) == (5, 5)
+    assert torch.allclose(I.scaled_residual_init(torch.ones(2), 8), torch.full((2,), 0.25))
+    assert float(I.zero_init_last_layer((3, 4)).abs().sum()) == 0.0
