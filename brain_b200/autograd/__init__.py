@@ -4,3 +4,4 @@ from .tape import Tape, OpRecord, start_recording, stop_recording, with_tape, is
 from .functional import (grad, value_and_grad, vjp, jvp, jacobian, hessian, grad_and_hess, numeric_grad,  # noqa: F401
                          checkpoint, BudgetCheckpoint, CheckpointPolicy, CpuOffloader, GradScaler,
                          parallel_backward)
+from .graph import topological_sort, compute_dag_levels, values_close, TapeBuilder, RecomputeGraph  # noqa: F401

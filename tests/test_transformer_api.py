@@ -1,0 +1,130 @@
+"""Transformer front-ends and backward-graph utilities against plain fp32 PyTorch references."""
+import math
+
+import pytest
+import torch
+
+from brain_b200.autograd import (Value, topological_sort, compute_dag_levels, values_close, TapeBuilder,
+                                 RecomputeGraph, OpRecord)
+from brain_b200.models import (FlashAttentionLite, FlashLiteConfig, XformersAttentionLite, XformersConfig,
+                               RelativeAttention, AlibiPositionalBias, LayerKvCache, TransformerDecoderLayer,
+                               TransformerDecoder, repeat_kv, quick_gelu, all_close)
+
+
+def _ref(q, k, v, causal, scale=None, bias=None):
+    qh, kh, vh = (t.transpose(1, 2).double() for t in (q, k, v))
+    if kh.shape[1] != qh.shape[1]:
+        kh = repeat_kv(kh, qh.shape[1] // kh.shape[1])
+        vh = repeat_kv(vh, qh.shape[1] // vh.shape[1])
+    s = qh @ kh.transpose(-1, -2) * (scale if scale is not None else qh.shape[-1] ** -0.5)
+    if bias is not None:
+        s = s + bias.double()
+    if causal:
+        Sq, Sk = s.shape[-2:]
+        m = torch.ones(Sq, Sk, dtype=torch.bool).tril(Sk - Sq)
+        s = s.masked_fill(~m, float("-inf"))
+    return (s.softmax(-1) @ vh).transpose(1, 2).float()
+
+
+@pytest.mark.parametrize("causal", [False, True])
+def test_flash_and_xformers_lite_match_reference(causal):
+    torch.manual_seed(0)
+    q = torch.randn(2, 37, 4, 16)
+    k = torch.randn(2, 53, 2, 16)
+    v = torch.randn(2, 53, 2, 16)
+    ref = _ref(q, k, v, causal)
+    a = FlashAttentionLite(FlashLiteConfig(block_m=8, block_n=16, is_causal=causal))(q, k, v)
+    b = XformersAttentionLite(XformersConfig(chunk_size=7, is_causal=causal))(q, k, v)
+    assert torch.allclose(a, ref, atol=1e-5) and torch.allclose(b, ref, atol=1e-5)
+    c = FlashAttentionLite(FlashLiteConfig(8, 8, scale=0.05, is_causal=causal))(q, k, v)
+    assert torch.allclose(c, _ref(q, k, v, causal, scale=0.05), atol=1e-5)
+
+
+def test_alibi_and_relative_attention():
+    torch.manual_seed(1)
+    q, k, v = torch.randn(1, 9, 4, 8), torch.randn(1, 9, 4, 8), torch.randn(1, 9, 4, 8)
+    ab = AlibiPositionalBias(4)
+    dense = ab.bias(9, 9).dense()
+    assert dense.shape == (4, 9, 9)
+    assert torch.allclose(dense[:, 5, 2], -ab.slopes * 3)
+    ra = RelativeAttention(4, num_buckets=8, max_distance=16)
+    torch.nn.init.normal_(ra.table)
+    out = ra(q, k, v)
+    assert torch.allclose(out, _ref(q, k, v, False, bias=ra.bias(9, 9)), atol=1e-5)
+    out.sum().backward()
+    assert ra.table.grad is not None and ra.table.grad.abs().sum() > 0
+
+
+def test_layer_kv_cache_and_helpers():
+    c = LayerKvCache(2, 2, 4, 6, dtype=torch.float32)
+    k1, v1 = c.update(torch.ones(2, 2, 4, 4), torch.zeros(2, 2, 4, 4))
+    assert k1.shape == (2, 2, 4, 4) and c.current_seq_len == 4
+    k2, _ = c.update(torch.full((2, 2, 2, 4), 2.0), torch.zeros(2, 2, 2, 4))
+    assert k2.shape[2] == 6 and float(k2[0, 0, 5, 0]) == 2.0
+    with pytest.raises(ValueError):
+        c.update(torch.zeros(2, 2, 1, 4), torch.zeros(2, 2, 1, 4))
+    c.clear()
+    assert c.current_seq_len == 0
+    x = torch.arange(12.0).reshape(1, 2, 3, 2)
+    r = repeat_kv(x, 3)
+    assert r.shape == (1, 6, 3, 2) and torch.equal(r[:, 2], x[:, 0]) and torch.equal(r[:, 3], x[:, 1])
+    t = torch.linspace(-3, 3, 11)
+    assert torch.allclose(quick_gelu(t), t / (1 + torch.exp(-1.702 * t)))
+    assert all_close(t, t + 1e-9) and not all_close(t, t + 1e-3) and not all_close(t, t[:5])
+
+
+def test_transformer_decoder_cross_attends():
+    torch.manual_seed(2)
+    dec = TransformerDecoder(2, 32, 4, 64)
+    x, mem = torch.randn(2, 5, 32), torch.randn(2, 7, 32)
+    y = dec(x, memory=mem)
+    assert y.shape == (2, 5, 32)
+    mem2 = mem.clone()
+    mem2[:, 3] += 1.0
+    assert not torch.allclose(dec(x, memory=mem2), y)
+    # causal self-attention: the first position ignores later ones
+    x2 = x.clone()
+    x2[:, 4] += 1.0
+    assert torch.allclose(dec(x2, memory=mem)[:, 0], y[:, 0], atol=1e-5)
+    assert isinstance(dec.layers[0], TransformerDecoderLayer)
+
+
+def test_topological_sort_and_levels():
+    a = torch.randn(3, requires_grad=True)
+    b = torch.randn(3, requires_grad=True)
+    c = a * b
+    d = c.exp() + a
+    order = topological_sort(Value(d) if not isinstance(d, Value) else d)
+    assert order[-1] is d.grad_fn
+    pos = {id(n): i for i, n in enumerate(order)}
+    for n in order:
+        for p, _ in n.next_functions:
+            if p is not None:
+                assert pos[id(p)] < pos[id(n)]
+    levels = compute_dag_levels(order)
+    assert {type(n).__name__ for n in levels[0]} == {"AccumulateGrad"}
+    assert levels[-1] == [d.grad_fn]
+    level_of = {id(n): i for i, lv in enumerate(levels) for n in lv}
+    for n in order:
+        for p, _ in n.next_functions:
+            if p is not None:
+                assert level_of[id(p)] < level_of[id(n)]
+    # a deep chain does not exhaust the Python stack
+    x = torch.ones(1, requires_grad=True)
+    y = x
+    for _ in range(5000):
+        y = y * 1.0
+    assert len(topological_sort(y)) == 5001
+    assert topological_sort(torch.ones(2)) == []
+
+
+def test_values_close_tape_builder_recompute():
+    assert values_close(Value(torch.ones(3)), Value(torch.ones(3) + 1e-4), 1e-3)
+    assert not values_close(Value(torch.ones(3)), Value(torch.ones(3) + 1e-2), 1e-3)
+    assert not values_close(Value(torch.ones(3)), Value(torch.ones(4)), 1.0)
+    tape = TapeBuilder().add_op(OpRecord("mul", [0, 1], 2, (3,))).add_op(OpRecord("exp", [2], 3, (3,))).build()
+    assert tape.ops() == ["mul", "exp"]
+    g = RecomputeGraph([torch.tensor(2.0), torch.tensor(3.0)], "mul", lambda a, b: a * b)
+    assert g.input_count() == 2 and g.op_name() == "mul" and float(g.recompute()) == 6.0
+    with pytest.raises(RuntimeError):
+        RecomputeGraph([], "noop").recompute()
