@@ -7,4 +7,7 @@ from .families import GptLite, BertLite, T5Lite, ViT  # noqa: F401
 from .blocks import TransformerBlock, TransformerStack  # noqa: F401
 from .transformer_api import (FlashAttentionLite, FlashLiteConfig, XformersAttentionLite, XformersConfig,  # noqa: F401
                               RelativeAttention, AlibiPositionalBias, LayerKvCache, TransformerDecoderLayer,
-                              TransformerDecoder, repeat_kv, quick_gelu, all_close)
+                              TransformerDecoder, repeat_kv, quick_gelu, all_close,
+                              TransformerEncoder, TransformerEncoderLayer, EncoderLayer, TransformerEncoderBlock,
+                              build_encoder, build_decoder, RopeConfig, RotaryEmbedding, PositionalEncoding,
+                              RelativePositionBias, split_heads, merge_heads)

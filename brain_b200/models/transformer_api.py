@@ -172,3 +172,145 @@ class TransformerDecoder(Module):
         for layer in self.layers:
             x = layer(x, mem=memory, mem_mask=mem_mask)
         return self.norm(x) if self.norm is not None else x
+
+
+# ------------------------------------------------------------------ encoder side, rotary and positional encodings
+# Reference: crates/brain-transformer/src/encoder/{mod,layer,block}.rs, position/rope.rs:15-200,
+# position/mod.rs (PositionalEncoding: learned / sinusoidal), attention/multi_head.rs (split/merge heads),
+# builder.rs (build_encoder / build_decoder).
+
+class TransformerEncoderLayer(TransformerBlock):
+    """Bidirectional self-attention + feed-forward (pre- or post-norm)."""
+
+    def __init__(self, dim, heads, ffn_dim, **kw):
+        kw.setdefault("causal", False)
+        super().__init__(dim, heads, ffn_dim, **kw)
+
+
+EncoderLayer = TransformerEncoderLayer
+TransformerEncoderBlock = TransformerEncoderLayer
+
+
+class TransformerEncoder(Module):
+    def __init__(self, num_layers, dim, heads, ffn_dim, final_norm: bool = True, **kw):
+        super().__init__()
+        self.layers = torch.nn.ModuleList([TransformerEncoderLayer(dim, heads, ffn_dim, **kw)
+                                           for _ in range(num_layers)])
+        self.norm = make_norm(kw.get("norm", "layer"), dim, kw.get("eps", 1e-5), kw.get("device"),
+                              kw.get("dtype")) if final_norm else None
+
+    def forward(self, x, mask=None, attn_bias=None):
+        for layer in self.layers:
+            x = layer(x, mask=mask, attn_bias=attn_bias)
+        return self.norm(x) if self.norm is not None else x
+
+
+def build_encoder(num_layers, dim, heads, ffn_dim, **kw) -> TransformerEncoder:
+    return TransformerEncoder(num_layers, dim, heads, ffn_dim, **kw)
+
+
+def build_decoder(num_layers, dim, heads, ffn_dim, **kw) -> TransformerDecoder:
+    return TransformerDecoder(num_layers, dim, heads, ffn_dim, **kw)
+
+
+@dataclass
+class RopeConfig:
+    dim: int = 64
+    max_seq_len: int = 2048
+    theta: float = 10000.0
+    scaling_factor: float = 1.0
+    is_2d: bool = False
+
+
+class RotaryEmbedding:
+    """Rotary position embedding with the half-split pairing (x_i, x_{i + D/2}) and angle
+    (pos / scaling_factor) theta^(-2i/D). The float32 cos/sin table lives on the device; ``apply_rope_4d``
+    rotates [B, H, S, D] in place with the rope kernel on CUDA (positions at or past max_seq_len are left
+    unrotated, as in the reference)."""
+
+    def __init__(self, config: RopeConfig | None = None, device=None):
+        from ..ops.rope import rope_table
+        self.config = c = config or RopeConfig()
+        self.table = rope_table(c.dim, c.max_seq_len, c.theta, device or "cpu", 1.0 / c.scaling_factor)
+
+    @staticmethod
+    def compute_frequencies(dim, max_seq_len, theta, scaling_factor=1.0):
+        """(cos, sin), each float64 [max_seq_len, dim / 2]."""
+        th = float(torch.tensor(theta, dtype=torch.float32))
+        freq = 1.0 / th ** (torch.arange(dim // 2, dtype=torch.float64) * 2 / dim)
+        ang = (torch.arange(max_seq_len, dtype=torch.float64) / scaling_factor)[:, None] * freq[None]
+        return ang.cos(), ang.sin()
+
+    def _table_for(self, x):
+        if self.table.device != x.device:
+            self.table = self.table.to(x.device)
+        return self.table
+
+    def apply_rope_4d(self, x: torch.Tensor, pos_offset: int = 0) -> torch.Tensor:
+        from ..ops.rope import apply_rope_
+        if x.dim() != 4:
+            raise ValueError(f"apply_rope_4d expects [B, H, S, D], got {tuple(x.shape)}")
+        n = max(0, min(x.shape[2], self.config.max_seq_len - pos_offset))
+        if n:
+            apply_rope_(x[:, :, :n].transpose(1, 2), self._table_for(x), offset=pos_offset)
+        return x
+
+    def apply_rope_2d(self, x: torch.Tensor, height: int, width: int) -> torch.Tensor:
+        """[B, H, height*width, D] patches: quarter 1/2 of D rotate with the row, quarter 3/4 with the
+        column, each with the table's first D/4 frequencies."""
+        B, H, N, D = x.shape
+        if N != height * width:
+            raise ValueError(f"{N} patches != {height} x {width}")
+        q = D // 4
+        t = self._table_for(x)
+        half = self.config.dim // 2
+        cos, sin = t[:, :half][:, :q], t[:, half:][:, :q]
+        rows = torch.arange(height, device=x.device).repeat_interleave(width)
+        cols = torch.arange(width, device=x.device).repeat(height)
+        xf = x.float()
+        out = xf.clone()
+        for base, idx in ((0, rows), (2 * q, cols)):
+            c, s = cos[idx], sin[idx]
+            a, b = xf[..., base:base + q], xf[..., base + q:base + 2 * q]
+            out[..., base:base + q] = a * c - b * s
+            out[..., base + q:base + 2 * q] = a * s + b * c
+        x.copy_(out.to(x.dtype))
+        return x
+
+
+class PositionalEncoding(Module):
+    """Absolute positions added to token embeddings [B, S, D]: ``kind`` "sinusoidal" (fixed table) or
+    "learned" (a trained [max_len, D] table)."""
+
+    def __init__(self, dim: int, max_len: int = 2048, kind: str = "sinusoidal", device=None, dtype=None):
+        super().__init__()
+        from .position import sinusoidal
+        self.kind = kind
+        if kind == "sinusoidal":
+            self.register_buffer("pe", sinusoidal(max_len, dim).to(device=device, dtype=dtype or torch.float32))
+        elif kind == "learned":
+            self.pe = torch.nn.Parameter(torch.randn(max_len, dim, device=device, dtype=dtype or torch.float32) * 0.02)
+        else:
+            raise ValueError(f"unknown positional encoding {kind!r}")
+
+    def forward(self, x, offset: int = 0):
+        return x + self.pe[offset:offset + x.shape[1]].to(x.dtype)
+
+
+class RelativePositionBias(RelativeAttention):
+    """The T5 bucketed bias on its own: ``compute_bias(sq, sk)`` -> [H, sq, sk]."""
+
+    def compute_bias(self, sq: int, sk: int) -> torch.Tensor:
+        return self.bias(sq, sk)
+
+
+def split_heads(x: torch.Tensor, num_heads: int) -> torch.Tensor:
+    """[B, S, H*D] -> [B, H, S, D]."""
+    B, S, E = x.shape
+    return x.view(B, S, num_heads, E // num_heads).transpose(1, 2)
+
+
+def merge_heads(x: torch.Tensor) -> torch.Tensor:
+    """[B, H, S, D] -> [B, S, H*D]."""
+    B, H, S, D = x.shape
+    return x.transpose(1, 2).reshape(B, S, H * D)

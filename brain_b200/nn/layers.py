@@ -326,8 +326,6 @@ def num_params(m: torch.nn.Module) -> int:
     return sum(p.numel() for p in m.parameters())
 
 
-__all__ = [n for n in dir() if not n.startswith("_") and n[0].isupper()] + ["scaled_dot_product_attention",
-                                                                             "num_params", "math"]
 
 
 # ------------------------------------------------------------------ further activations (crates/brain-nn/src/activations/extra.rs, extended.rs)
@@ -444,3 +442,12 @@ class SequentialNamed(Module):
         for name in self._order:
             x = getattr(self, name)(x)
         return x
+
+
+# The reference's spellings (crates/brain-transformer/src/attention/multi_head.rs, ffn/mod.rs).
+MultiHeadAttention = MultiheadAttention
+FeedForwardNetwork = FeedForward
+
+
+__all__ = [n for n in dir() if not n.startswith("_") and n[0].isupper()] + ["scaled_dot_product_attention",
+                                                                             "num_params", "math", "quiet_softmax"]

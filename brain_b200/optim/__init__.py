@@ -4,3 +4,5 @@ from .flat_adamw import FlatAdamW  # noqa: F401
 from .optimizers import *  # noqa: F401,F403
 from .schedulers import *  # noqa: F401,F403
 from ..autograd.functional import GradScaler  # noqa: F401
+from .builder import (OptimizerKind, OptimizerBuilder, ParamGroup, ParamGroupConfig, GradEntry,  # noqa: F401
+                      Rmsprop, SophiaG, SwAOptimizer, ModelEma, LrFinder, LrScheduler, SgdNesterov)
