@@ -100,6 +100,8 @@ def main(argv=None) -> int:
     # ---- GEMMs of one layer: x W^T forward, dy W (dgrad), dy^T x (wgrad, f32 accumulate)
     x = rnd(T, d)
     for name, N, K in (("qkv", (Hq + 2 * Hkv) * D, d), ("o", d, Hq * D), ("gate_up", 2 * F, d), ("down", d, F)):
+        if not any(want(f"gemm_{kind}_{name}") for kind in ("fwd", "dgrad", "wgrad")):
+            continue  # allocate only what the selected cases use
         w = rnd(N, K, std=0.02)
         xi = x if K == d else rnd(T, K)
         dy = rnd(T, N)

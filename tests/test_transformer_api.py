@@ -188,3 +188,23 @@ def test_encoder_positional_encoding_and_heads():
     h = split_heads(t, 3)
     assert h.shape == (2, 3, 5, 4) and torch.equal(merge_heads(h), t)
     assert MultiHeadAttention is MultiheadAttention and FeedForwardNetwork is FeedForward
+
+
+@pytest.mark.gpu
+def test_front_ends_on_cuda_kernels():
+    from brain_b200.models import RopeConfig, RotaryEmbedding
+    torch.manual_seed(5)
+    dev = "cuda"
+    q = torch.randn(2, 256, 8, 64, device=dev).bfloat16()
+    k = torch.randn(2, 256, 2, 64, device=dev).bfloat16()
+    v = torch.randn(2, 256, 2, 64, device=dev).bfloat16()
+    for causal in (False, True):
+        out = FlashAttentionLite(FlashLiteConfig(is_causal=causal))(q, k, v)
+        ref = _ref(q.float().cpu(), k.float().cpu(), v.float().cpu(), causal)
+        assert float((out.float().cpu() - ref).norm() / ref.norm()) < 1e-2
+    re = RotaryEmbedding(RopeConfig(dim=64, max_seq_len=300), device=dev)
+    cos, sin = RotaryEmbedding.compute_frequencies(64, 300, 10000.0)
+    x = torch.randn(2, 4, 256, 64, device=dev)
+    y = re.apply_rope_4d(x.clone(), pos_offset=10)
+    ref = _rope_oracle(x.double().cpu(), cos, sin, torch.arange(10, 266)).float()
+    assert torch.allclose(y.cpu(), ref, atol=1e-4)
