@@ -32,9 +32,10 @@ def rope_table(dim: int, max_pos: int, theta: float = 10000.0, device="cpu", sca
 
 def apply_rope_(x: torch.Tensor, table: torch.Tensor, positions: torch.Tensor | None = None, offset: int = 0,
                 inverse: bool = False) -> torch.Tensor:
-    """Rotate x [B, S, H, D] in place (any strides, unit stride on D). Returns x."""
+    """Rotate x [B, S, H, D] in place (any strides, unit stride on D). Returns x. bf16 CUDA tensors go
+    through the rope kernel; other dtypes are rotated with tensor ops on their device."""
     B, S, H, D = x.shape
-    if x.is_cuda:
+    if x.is_cuda and x.dtype == torch.bfloat16:
         if x.stride(3) != 1:
             raise ValueError("rope needs unit stride on the head dimension")
         pos = positions.to(torch.int32).contiguous() if positions is not None else None

@@ -205,6 +205,10 @@ def test_front_ends_on_cuda_kernels():
     re = RotaryEmbedding(RopeConfig(dim=64, max_seq_len=300), device=dev)
     cos, sin = RotaryEmbedding.compute_frequencies(64, 300, 10000.0)
     x = torch.randn(2, 4, 256, 64, device=dev)
-    y = re.apply_rope_4d(x.clone(), pos_offset=10)
     ref = _rope_oracle(x.double().cpu(), cos, sin, torch.arange(10, 266)).float()
+    y = re.apply_rope_4d(x.clone(), pos_offset=10)  # float32: tensor ops
     assert torch.allclose(y.cpu(), ref, atol=1e-4)
+    xb = x.bfloat16()
+    refb = _rope_oracle(xb.double().cpu(), cos, sin, torch.arange(10, 266)).float()
+    yb = re.apply_rope_4d(xb.clone(), pos_offset=10)  # bf16: the rope kernel, strided [B, S, H, D] view
+    assert float((yb.float().cpu() - refb).abs().max()) < 3e-2
