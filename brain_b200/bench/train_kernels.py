@@ -123,8 +123,9 @@ def main(argv=None) -> int:
         report("gemm_fwd_qkv_rope", timeit(lambda: gemm_rope(x, wq, table, (Hq + Hkv) * D, D, S, 0)),
                2.0 * T * N * d, M=T, N=N, K=d)
     # ---- block-scaled fp8 GEMM (1 x 128 activation, 128 x 128 weight scales) against bf16, 16384 x 8192 x 4096
-    if want("gemm_fp8") or want("gemm_bf16_square"):
-        from ..quantization.fp8 import fp8_gemm_blockscaled, quantize_fp8_blockwise, quantize_fp8_weight_blocks
+    if want("gemm_fp8") or want("gemm_bf16_square") or want("gemm_fp8_rowwise"):
+        from ..quantization.fp8 import (fp8_gemm_blockscaled, fp8_gemm_rowwise, quantize_fp8_blockwise,
+                                        quantize_fp8_rowwise, quantize_fp8_weight_blocks)
         Mq, Nq, Kq = 16384, 8192, 4096
         xa, wb = rnd(Mq, Kq), rnd(Nq, Kq, std=0.02)
         fl = 2.0 * Mq * Nq * Kq
@@ -137,6 +138,13 @@ def main(argv=None) -> int:
                    note="tensor FLOPs at fp8; the bf16 figure is the denominator for both")
             report("fp8_quantize_activations", timeit(lambda: quantize_fp8_blockwise(xa)), None,
                    nbytes=Mq * Kq * 3 + Mq * Kq // 128 * 4)
+        if want("gemm_fp8_rowwise"):
+            aq, sa = quantize_fp8_rowwise(xa)
+            bq, sb = quantize_fp8_rowwise(wb)
+            report("gemm_fp8_rowwise", timeit(lambda: fp8_gemm_rowwise(aq, sa, bq, sb)), fl, M=Mq, N=Nq, K=Kq,
+                   note="tensor FLOPs at fp8 (CTA pair, scales in the epilogue); bf16 peak as the denominator")
+            report("fp8_quantize_rowwise", timeit(lambda: quantize_fp8_rowwise(xa)), None,
+                   nbytes=Mq * Kq * 3 + Mq * 4)
     # ---- flash attention (causal): forward 2 GEMMs of S x S x D per head over half the square
     q, k, v = rnd(B, S, Hq, D), rnd(B, S, Hkv, D), rnd(B, S, Hkv, D)
     fwd_flops = 4.0 * B * Hq * S * S * D / 2

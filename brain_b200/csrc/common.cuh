@@ -334,6 +334,15 @@ __device__ __forceinline__ void tc_mma_f16_pair(uint32_t d_tmem, uint64_t adesc,
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// kind::f8f6f4 on a CTA pair (e4m3/e5m2 operands, f32 accumulate), same operand split as the f16 form.
+__device__ __forceinline__ void tc_mma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                               uint32_t accumulate) {
+  asm volatile(
+      "{ .reg .pred p; setp.ne.b32 p, %4, 0; "
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p; }" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive on one mbarrier (shared::cluster address, any CTA of the pair) when the pair MMAs issued
 // so far by this thread have completed.
 __device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster) {

@@ -76,6 +76,10 @@ struct GemmArgs {
   // dual output (CTA-pair TMA-store, bf16): C = the product (+ bias) and a second matrix (map tmE, same
   // shape) = gelu(C): the first layer of a GELU MLP keeps its pre-activation and feeds the second layer
   int dual_gelu;
+  // row-wise scaled fp8 operands (CTA-pair kernel with F8 = 1): the product is multiplied by
+  // row_scale[m] * col_scale[n] instead of alpha
+  const float* row_scale;
+  const float* col_scale;
 };
 
 template <int BN, int STAGES>
@@ -137,11 +141,35 @@ __device__ __forceinline__ void add_bias32(const GemmArgs& args, int gn0, bool f
   }
 }
 
+// v = acc * alpha, or acc * row_scale[gm] * col_scale[n] for row-wise scaled fp8 operands (the column
+// scales as 16-byte loads when the 32 columns are whole and aligned; every lane reads the same address).
+__device__ __forceinline__ void scale32(const GemmArgs& args, int gm, int gn0, const uint32_t* r, float* v) {
+  if (!args.row_scale) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
+    return;
+  }
+  const float rs = gm < args.M ? __ldg(args.row_scale + gm) : 0.f;
+  const float* cs = args.col_scale + gn0;
+  if (gn0 + 32 <= args.N && (reinterpret_cast<uintptr_t>(cs) & 15) == 0) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + j));
+      v[j] = __uint_as_float(r[j]) * rs * c4.x;
+      v[j + 1] = __uint_as_float(r[j + 1]) * rs * c4.y;
+      v[j + 2] = __uint_as_float(r[j + 2]) * rs * c4.z;
+      v[j + 3] = __uint_as_float(r[j + 3]) * rs * c4.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = gn0 + j < args.N ? __uint_as_float(r[j]) * rs * __ldg(cs + j) : 0.f;
+  }
+}
+
 // alpha, bias, residual and beta * C_old for one row x 32 columns (C_old read at row gm of C).
 __device__ __forceinline__ void epi_math(const GemmArgs& args, int gm, int gn0, const uint32_t* r, float* v,
                                          bool skip_r = false) {
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
+  scale32(args, gm, gn0, r, v);
   if (gm >= args.M) return;
   const bool full = gn0 + 32 <= args.N;
   if (args.bias) add_bias32(args, gn0, full, v);
@@ -208,8 +236,7 @@ __device__ __forceinline__ void store_chunk(const GemmArgs& args, int gm, int gn
 __device__ __forceinline__ void store_chunk_at(const GemmArgs& args, int gm, int gn0, const uint32_t* r, void* cbase,
                                                int64_t crow) {
   float v[32];
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * args.alpha;
+  scale32(args, gm, gn0, r, v);
   const bool full = gn0 + 32 <= args.N;
   if (args.bias) add_bias32(args, gn0, full, v);
   if (args.R) {
@@ -467,7 +494,10 @@ struct PairSmem {
   static_assert(TOTAL <= 232448, "more dynamic shared memory than one CTA may use");
 };
 
-template <int A_MN, int B_MN>
+// F8 = 1: e4m3 operands (K-major only) through tcgen05.mma kind::f8f6f4. A K block is then 128 fp8 =
+// the same 128-byte swizzle row as 64 bf16, and each MMA still consumes 32 bytes of K (32 fp8 instead of
+// 16 bf16), so shared-memory layouts, descriptors and stage sizes are those of the bf16 kernel.
+template <int A_MN, int B_MN, int F8 = 0>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmE, GemmArgs args) {
@@ -520,7 +550,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   cluster_sync();  // both CTAs' barriers are initialised before anyone signals a peer
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int num_kb = (args.K + BK - 1) / BK;
+  static_assert(!F8 || (A_MN == 0 && B_MN == 0), "fp8 operands are K-major");
+  constexpr int KE = F8 ? 2 * BK : BK;  // elements per K block (128 bytes either way)
+  const int num_kb = (args.K + KE - 1) / KE;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -542,7 +574,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           const uint32_t sb = sa + S::A_BYTES;
           const uint32_t fb = mapa_shared(full_bar(s), 0);
           if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * S::STAGE_BYTES);
-          const int k0 = kb * BK;
+          const int k0 = kb * KE;
           if (A_MN) {
             tma_load_2d_pair(&tmA, sa, fb, m0, k0);
             tma_load_2d_pair(&tmA, sa + 64 * BK * 2, fb, m0 + 64, k0);
@@ -569,7 +601,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- MMA issuer (CTA 0 only)
-      constexpr uint32_t idesc = idesc_f16(256, TN, 1u, (uint32_t)A_MN, (uint32_t)B_MN);
+      constexpr uint32_t idesc = F8 ? idesc_f8(256, TN, 0u, 0u, 0u, 0u)
+                                    : idesc_f16(256, TN, 1u, (uint32_t)A_MN, (uint32_t)B_MN);
       uint32_t it = 0;
       int local = 0;
       bool ok = true, issued = false;
@@ -599,7 +632,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                   : smem_desc_sw128(sa + kk * 32, 16, 1024);
             uint64_t bdesc = B_MN ? smem_desc_sw128(sb + kk * 2048, 64 * BK * 2, 1024)
                                   : smem_desc_sw128(sb + kk * 32, 16, 1024);
-            tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            if constexpr (F8)
+              tc_mma_f8_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            else
+              tc_mma_f16_pair(d_tmem, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
           }
           issued = true;
           tc_commit_pair(empty_bar(s));
@@ -982,11 +1018,11 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, c
   return (int)cudaGetLastError();
 }
 
-template <int A_MN, int B_MN>
+template <int A_MN, int B_MN, int F8 = 0>
 int launch_tc2(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& a,
                cudaStream_t st, const CUtensorMap* tr = nullptr) {
   static const CUtensorMap no_map{};
-  auto kern = gemm_tc2_kernel<A_MN, B_MN>;
+  auto kern = gemm_tc2_kernel<A_MN, B_MN, F8>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1434,4 +1470,40 @@ BRAIN_API int brain_gemm_bf16_gelu_grad(const void* A, int64_t lda, const void* 
   a.r_tma = 1;
   a.r_op = 1;
   return b_mn ? launch_tc2<0, 1>(ta, tb, tc, a, stream, &th) : launch_tc2<0, 0>(ta, tb, tc, a, stream, &th);
+}
+
+// Row-wise scaled fp8 GEMM on the CTA pair: C [M, N] bf16 = (Aq [M, K] . Bq [N, K]^T) * sa[m] * sb[n] (+ R),
+// e4m3 operands K-major (row strides lda / ldb in bytes), f32 scales sa [M], sb [N]. 256 x 256 tiles,
+// kind::f8f6f4 with the bf16 kernel's pipeline and TMA-store epilogue. Returns cudaErrorNotSupported
+// when the pair path cannot run (M or N < 256, pair mode off, unaligned output): the caller then uses
+// the single-CTA row-wise kernel.
+BRAIN_API int brain_fp8_gemm_rowwise_pair(const void* A, int64_t lda, const void* B, int64_t ldb, const float* sa,
+                                          const float* sb, void* C, int64_t ldc, const void* R, int64_t ldr, int M,
+                                          int N, int K, cudaStream_t stream) {
+  if (M <= 0 || N <= 0) return 0;
+  if (K <= 0 || K % 16 || lda % 16 || ldb % 16 ||
+      ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) || !sa || !sb)
+    return (int)cudaErrorInvalidValue;
+  if (!g_pair_mode || M < 256 || N < 256) return (int)cudaErrorNotSupported;
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K;
+  a.C = C; a.ldc = ldc; a.c_f32 = 0;
+  a.alpha = 1.f;
+  a.row_scale = sa; a.col_scale = sb;
+  a.R = reinterpret_cast<const __nv_bfloat16*>(R);
+  a.ldr = ldr;
+  a.tiles_m = (M + 255) / 256;
+  a.tiles_n = (N + 255) / 256;
+  a.num_tiles = a.tiles_m * a.tiles_n;
+  CUtensorMap ta, tb, tc{};
+  if (!get_map_2d(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)lda, 2 * BK, 128, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1) ||
+      !get_map_2d(&tb, B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb, 2 * BK, 128, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1))
+    return (int)cudaErrorInvalidValue;
+  if (!output_map(&tc, a)) return (int)cudaErrorNotSupported;
+  a.tma_store = 1;
+  CUtensorMap tr{};
+  if (a.R && ldr % 8 == 0 && (reinterpret_cast<uintptr_t>(R) & 15) == 0 &&
+      get_map_2d(&tr, R, (uint64_t)N, (uint64_t)M, (uint64_t)ldr, 64, 32, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2))
+    a.r_tma = 1;
+  return launch_tc2<0, 0, 1>(ta, tb, tc, a, stream, a.r_tma ? &tr : nullptr);
 }

@@ -1,8 +1,16 @@
-"""FP8 E4M3 block-scaled quantisation and GEMM front-end (``csrc/fp8.cu``).
+"""FP8 E4M3 quantisation and GEMM front-ends (``csrc/fp8.cu``, ``csrc/gemm.cu``).
 
-Activations: 1 x 128 blocks along K (scale = amax / 448 per row and block). Weights [N, K]:
-128 x 128 blocks. ``fp8_gemm_blockscaled`` computes ``sum_kb (Aq . Bq^T) * sa * sb`` into bf16 on the
-tcgen05 kernel; on CPU the same contract is evaluated by dequantising in float32 (the oracle).
+Block-scaled: activations in 1 x 128 blocks along K (scale = amax / 448 per row and block), weights
+[N, K] in 128 x 128 blocks; ``fp8_gemm_blockscaled`` computes ``sum_kb (Aq . Bq^T) * sa * sb`` into
+bf16, promoting each 128-wide K block on the CUDA cores.
+
+Row-wise: one scale per activation row (token) and one per weight row (output channel);
+``fp8_gemm_rowwise`` accumulates the whole K reduction on the tensor core (tcgen05 kind::f8f6f4,
+256 x 256 CTA-pair tiles, the bf16 GEMM's pipeline) and applies ``sa[m] * sb[n]`` once in the epilogue,
+so it runs at the fp8 tensor rate. Coarser scales than the block-scaled path (an outlier costs its
+whole row or channel precision), the usual trade of a row-wise fp8 training / serving recipe.
+
+On CPU both contracts are evaluated by dequantising in float32 (the oracle).
 """
 from __future__ import annotations
 
@@ -15,7 +23,11 @@ _native.register({
     "brain_fp8_gemm": ("brain_kernels", "plplppplpliiis"),
     "brain_fp8_quant_rows": ("brain_kernels", "plplpiis"),
     "brain_status_fp8": ("brain_kernels", "pi"),
+    "brain_fp8_gemm_rowwise": ("brain_kernels", "plplppplpliiis"),
+    "brain_fp8_gemm_rowwise_pair": ("brain_kernels", "plplppplpliiis"),
+    "brain_fp8_quant_rowwise": ("brain_kernels", "plplpiis"),
 })
+_NOT_SUPPORTED = 801  # cudaErrorNotSupported
 
 E4M3_MAX = 448.0
 
@@ -86,3 +98,70 @@ def fp8_linear(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, residual=Non
     aq, sa = quantize_fp8_blockwise(x2)
     r2 = residual.reshape(-1, wq.shape[0]) if residual is not None else None
     return fp8_gemm_blockscaled(aq, sa, wq, ws, r2).view(*shp[:-1], wq.shape[0])
+
+
+# ------------------------------------------------------------------ row-wise scaling
+def _aligned_rows(t: torch.Tensor) -> torch.Tensor:
+    """t itself when its rows are unit-stride, 16-byte aligned and a multiple of 8 elements apart, else a
+    copy into such a buffer (a view of its first N columns)."""
+    if t.stride(1) == 1 and t.stride(0) % 8 == 0 and t.data_ptr() % 16 == 0:
+        return t
+    M, N = t.shape
+    buf = torch.empty(M, -(-N // 8) * 8, device=t.device, dtype=t.dtype)[:, :N]
+    buf.copy_(t)
+    return buf
+
+
+def quantize_fp8_rowwise(x: torch.Tensor):
+    """x [M, K] -> (q [M, K] float8_e4m3fn, scales [M] f32), scale = amax(|row|) / 448."""
+    M, K = x.shape
+    if x.is_cuda and x.dtype == torch.bfloat16 and K % 8 == 0:
+        xc = x if (x.stride(1) == 1 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0) else x.contiguous()
+        q = torch.empty(M, K, device=x.device, dtype=torch.float8_e4m3fn)
+        s = torch.empty(M, device=x.device, dtype=torch.float32)
+        _native.call("brain_fp8_quant_rowwise", xc.data_ptr(), xc.stride(0), q.data_ptr(), q.stride(0), s.data_ptr(),
+                     M, K, stream(x))
+        return q, s
+    xf = x.float()
+    s = xf.abs().amax(-1) / E4M3_MAX
+    s = torch.where(s > 0, s, torch.ones_like(s))
+    return (xf / s[:, None]).to(torch.float8_e4m3fn), s
+
+
+def fp8_gemm_rowwise(aq, sa, bq, sb, residual: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 C = (aq . bq^T) * sa[:, None] * sb[None, :] (+ residual): the CTA-pair tcgen05 kernel for
+    M, N >= 256, the single-CTA 128 x 256 kernel otherwise."""
+    M, K = aq.shape
+    N = bq.shape[0]
+    if aq.is_cuda:
+        if K % 16 or aq.stride(1) != 1 or bq.stride(1) != 1:
+            raise ValueError("fp8_gemm_rowwise needs K % 16 == 0 and row-major operands")
+        sa = sa.float().contiguous()
+        sb = sb.float().contiguous()
+        ld = -(-N // 8) * 8  # 16-byte output rows for the vector / TMA stores
+        out = torch.empty(M, ld, device=aq.device, dtype=torch.bfloat16)[:, :N]
+        if residual is not None:
+            residual = _aligned_rows(residual.to(torch.bfloat16))
+        args = (aq.data_ptr(), aq.stride(0), bq.data_ptr(), bq.stride(0), sa.data_ptr(), sb.data_ptr(),
+                out.data_ptr(), out.stride(0), ptr(residual), residual.stride(0) if residual is not None else 0,
+                M, N, K, stream(aq))
+        rc = _native.fn("brain_fp8_gemm_rowwise_pair")(*args)
+        if rc == _NOT_SUPPORTED:
+            rc = _native.fn("brain_fp8_gemm_rowwise")(*args)
+        if rc != 0:
+            raise _native.NativeError(f"fp8 row-wise GEMM failed with status {rc}")
+        return out
+    c = (aq.float() * sa.float()[:, None]) @ (bq.float() * sb.float()[:, None]).t()
+    if residual is not None:
+        c = c + residual.float()
+    return c.to(torch.bfloat16)
+
+
+def fp8_linear_rowwise(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, residual=None) -> torch.Tensor:
+    """y = x @ W^T with x quantised per token on the fly and W quantised per output channel
+    (``quantize_fp8_rowwise(w)``)."""
+    shp = x.shape
+    x2 = x.reshape(-1, shp[-1])
+    aq, sa = quantize_fp8_rowwise(x2)
+    r2 = residual.reshape(-1, wq.shape[0]) if residual is not None else None
+    return fp8_gemm_rowwise(aq, sa, wq, ws, r2).view(*shp[:-1], wq.shape[0])

@@ -63,3 +63,47 @@ def test_int_group_quant_and_qlinear():
     w = _rnd(16, 16, seed=7)
     m = Q.magnitude_prune_(w, 0.5)
     assert int(m.sum()) == 128 and int((w == 0).sum()) == 128
+
+
+def test_fp8_rowwise_roundtrip_cpu():
+    x = _rnd(40, 200, seed=8)
+    q, s = F8.quantize_fp8_rowwise(x)
+    assert s.shape == (40,)
+    assert torch.allclose(s, x.abs().amax(1) / 448.0)
+    back = q.float() * s[:, None]
+    assert ((back - x).abs() <= x.abs().amax(1, keepdim=True) * 0.07).all()
+    z, sz = F8.quantize_fp8_rowwise(torch.zeros(3, 16))
+    assert torch.equal(sz, torch.ones(3)) and torch.equal(z.float(), torch.zeros(3, 16))
+    w = _rnd(24, 200, seed=9, scale=0.1)
+    wq, ws = F8.quantize_fp8_rowwise(w)
+    out = F8.fp8_gemm_rowwise(q, s, wq, ws, residual=torch.ones(40, 24))
+    ref = (q.float() * s[:, None]) @ (wq.float() * ws[:, None]).t() + 1
+    torch.testing.assert_close(out.float(), ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K,res", [(512, 768, 512, False),     # CTA-pair kernel, whole tiles
+                                       (300, 520, 4096, True),     # pair kernel, ragged M and N, residual
+                                       (100, 203, 160, True),      # single-CTA kernel, K tail, N % 8 != 0
+                                       (64, 8192, 1024, False)])   # single-CTA kernel (M < 256)
+def test_fp8_rowwise_gemm_matches_fp32_oracle(M, N, K, res):
+    x = _rnd(M, K, seed=10, device="cuda").bfloat16()
+    w = _rnd(N, K, seed=11, scale=0.05, device="cuda").bfloat16()
+    aq, sa = F8.quantize_fp8_rowwise(x)  # CUDA quantiser kernel
+    aq_ref, sa_ref = F8.quantize_fp8_rowwise(x.cpu())
+    torch.testing.assert_close(sa.cpu(), sa_ref, rtol=1e-6, atol=0)
+    assert (aq.cpu().float() - aq_ref.float()).abs().max() <= 32  # at most one e4m3 step apart
+    wq, ws = F8.quantize_fp8_rowwise(w)
+    r = _rnd(M, N, seed=12, device="cuda").bfloat16() if res else None
+    out = F8.fp8_gemm_rowwise(aq, sa, wq, ws, residual=r)
+    ref = (aq.cpu().float() * sa.cpu()[:, None]) @ (wq.cpu().float() * ws.cpu()[:, None]).t()
+    if res:
+        ref = ref + r.cpu().float()
+    torch.cuda.synchronize()
+    torch.testing.assert_close(out.cpu().float(), ref, rtol=2e-2, atol=2e-2 * (K / 128) ** 0.5)
+    from brain_b200 import _native
+    assert _native.status("fp8")[0] == 0 and _native.status("gemm")[0] == 0
+    # against the unquantised bf16 product: the row-wise fp8 error stays within a few percent
+    exact = x.float() @ w.float().t() + (r.float() if res else 0)
+    rel = float((out.float() - exact).norm() / exact.norm())
+    assert rel < 0.05, rel
