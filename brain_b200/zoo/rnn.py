@@ -90,6 +90,18 @@ class LstmCell(Module):
         return self.step(self.ih(x), *state)
 
 
+class PeepholeLstmCell(LstmCell):
+    """LSTM with diagonal peephole weights (input and forget gates see c_{t-1}, the output gate sees c_t),
+    started at 0.1 as the reference's cell does (crates/brain-rnn/src/cells/lstm_peephole.rs:21-50)."""
+
+    def __init__(self, input_dim: int, hidden_dim: int, device=None, dtype=None):
+        super().__init__(input_dim, hidden_dim, peephole=True, device=device, dtype=dtype)
+        with torch.no_grad():
+            self.peep.fill_(0.1)
+
+
+VanillaRnnCell = RnnCell  # the reference's name for the Elman cell (cells/rnn.rs)
+
 _CELLS = {"rnn": RnnCell, "gru": GruCell, "lstm": LstmCell}
 
 

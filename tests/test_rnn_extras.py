@@ -99,3 +99,17 @@ def test_teacher_forcing_and_streamer():
     torch.testing.assert_close(torch.cat([a, b[:, None], c], 1), full)
     st.reset([0])
     assert float(st.state[0][0].abs().sum()) == 0.0 and float(st.state[0][1].abs().sum()) > 0
+
+
+def test_peephole_lstm_cell_gate_equations():
+    from brain_b200.zoo.rnn import PeepholeLstmCell, VanillaRnnCell, RnnCell
+    torch.manual_seed(3)
+    cell = PeepholeLstmCell(3, 4)
+    assert torch.equal(cell.peep.detach(), torch.full((3, 4), 0.1))
+    x, h, c = torch.randn(2, 3), torch.randn(2, 4), torch.randn(2, 4)
+    h2, c2 = cell(x, (h, c))
+    i, f, g, o = (cell.ih(x) + cell.hh(h)).chunk(4, -1)
+    cn = torch.sigmoid(f + 0.1 * c) * c + torch.sigmoid(i + 0.1 * c) * torch.tanh(g)
+    hn = torch.sigmoid(o + 0.1 * cn) * torch.tanh(cn)
+    assert torch.allclose(c2, cn, atol=1e-6) and torch.allclose(h2, hn, atol=1e-6)
+    assert VanillaRnnCell is RnnCell
