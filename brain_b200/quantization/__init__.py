@@ -12,7 +12,7 @@ import enum
 import torch
 
 from .fp8 import (dequantize_fp8_blockwise, fp8_linear, fp8_gemm_blockscaled, quantize_fp8_blockwise,  # noqa: F401
-                  quantize_fp8_weight_blocks, quantize_fp8_rowwise, fp8_gemm_rowwise, fp8_linear_rowwise)
+                  quantize_fp8_weight_blocks, quantize_fp8_rowwise, fp8_gemm_rowwise, fp8_linear_rowwise, Fp8Linear)
 
 
 class QuantDType(enum.Enum):

@@ -165,3 +165,33 @@ def fp8_linear_rowwise(x: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor, resi
     aq, sa = quantize_fp8_rowwise(x2)
     r2 = residual.reshape(-1, wq.shape[0]) if residual is not None else None
     return fp8_gemm_rowwise(aq, sa, wq, ws, r2).view(*shp[:-1], wq.shape[0])
+
+
+class Fp8Linear(torch.nn.Module):
+    """Inference Linear with e4m3 weights: ``scaling="rowwise"`` (one scale per output channel; tokens
+    quantised per row on the fly; the CTA-pair fp8 kernel) or ``"block"`` (128 x 128 weight blocks,
+    1 x 128 activation blocks). Built from a float Linear with ``from_linear``; the bias is added in
+    bf16 after the GEMM."""
+
+    def __init__(self, wq: torch.Tensor, ws: torch.Tensor, bias: torch.Tensor | None = None, scaling: str = "rowwise"):
+        super().__init__()
+        if scaling not in ("rowwise", "block"):
+            raise ValueError(f"unknown fp8 scaling {scaling!r}")
+        self.scaling = scaling
+        self.register_buffer("wq", wq)
+        self.register_buffer("ws", ws)
+        self.register_buffer("bias", bias)
+        self.out_features, self.in_features = wq.shape
+
+    @classmethod
+    def from_linear(cls, lin: torch.nn.Module, scaling: str = "rowwise") -> "Fp8Linear":
+        w = lin.weight.detach()
+        wq, ws = quantize_fp8_rowwise(w.to(torch.bfloat16) if w.is_cuda else w) if scaling == "rowwise" \
+            else quantize_fp8_weight_blocks(w)
+        b = lin.bias.detach().to(torch.bfloat16) if getattr(lin, "bias", None) is not None else None
+        return cls(wq, ws, b, scaling)
+
+    def forward(self, x: torch.Tensor, residual: torch.Tensor | None = None) -> torch.Tensor:
+        f = fp8_linear_rowwise if self.scaling == "rowwise" else fp8_linear
+        y = f(x.to(torch.bfloat16) if x.is_cuda else x, self.wq, self.ws, residual)
+        return y + self.bias if self.bias is not None else y

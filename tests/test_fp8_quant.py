@@ -107,3 +107,30 @@ def test_fp8_rowwise_gemm_matches_fp32_oracle(M, N, K, res):
     exact = x.float() @ w.float().t() + (r.float() if res else 0)
     rel = float((out.float() - exact).norm() / exact.norm())
     assert rel < 0.05, rel
+
+
+@pytest.mark.parametrize("scaling", ["rowwise", "block"])
+def test_fp8_linear_module_cpu(scaling):
+    torch.manual_seed(13)
+    lin = torch.nn.Linear(256, 384)
+    f = F8.Fp8Linear.from_linear(lin, scaling)
+    x = torch.randn(5, 7, 256)
+    y = f(x)
+    ref = lin(x).detach()
+    assert y.shape == (5, 7, 384)
+    rel = float((y.float() - ref).norm() / ref.norm())
+    assert rel < 0.05, rel
+    with pytest.raises(ValueError):
+        F8.Fp8Linear(f.wq, f.ws, None, "tensor")
+
+
+@pytest.mark.gpu
+def test_fp8_linear_module_cuda_matches_cpu_oracle():
+    torch.manual_seed(14)
+    lin = torch.nn.Linear(512, 768).cuda()
+    f = F8.Fp8Linear.from_linear(lin, "rowwise")
+    x = torch.randn(3, 100, 512, device="cuda")
+    y = f(x)
+    ref = lin(x).detach()
+    rel = float((y.float() - ref).norm() / ref.norm())
+    assert rel < 0.05, rel
