@@ -5,3 +5,5 @@ from .functional import (grad, value_and_grad, vjp, jvp, jacobian, hessian, grad
                          checkpoint, BudgetCheckpoint, CheckpointPolicy, CpuOffloader, GradScaler,
                          parallel_backward)
 from .graph import topological_sort, compute_dag_levels, values_close, TapeBuilder, RecomputeGraph  # noqa: F401
+from . import vjps  # noqa: F401
+from .vjps import unbroadcast  # noqa: F401
