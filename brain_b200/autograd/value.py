@@ -256,6 +256,49 @@ class Value:
     def max_pool2d(self, k, stride=None):
         return Value._wrap(torch.nn.functional.max_pool2d(self.tensor, k, stride), "max_pool2d", self)
 
+    def adaptive_avg_pool2d(self, out_hw):
+        return Value._wrap(torch.nn.functional.adaptive_avg_pool2d(self.tensor, out_hw), "adaptive_avg_pool2d", self)
+
+    def adaptive_max_pool2d(self, out_hw):
+        return Value._wrap(torch.nn.functional.adaptive_max_pool2d(self.tensor, out_hw), "adaptive_max_pool2d", self)
+
+    def conv_transpose2d(self, weight, bias=None, stride=1, padding=0):
+        w, b = _t(weight), (None if bias is None else _t(bias))
+        return Value._wrap(torch.nn.functional.conv_transpose2d(self.tensor, w, b, stride, padding), "conv_transpose2d",
+                           self, weight, bias)
+
+    def where_cond(self, cond, other):
+        """self where cond else other (the reference's ``where_cond``)."""
+        return self.where(cond, other)
+
+    # ------------------------------------------------------------------ in-place state (reference value.rs setters)
+    @staticmethod
+    def from_tensor(t, requires_grad: bool = False) -> "Value":
+        return Value(t, requires_grad)
+
+    @staticmethod
+    def from_slice(data, shape, requires_grad: bool = False) -> "Value":
+        return Value(torch.as_tensor(data, dtype=torch.float32).reshape(tuple(shape)), requires_grad)
+
+    def set_data(self, t) -> None:
+        """Replace the values in place (shape must match), outside the graph."""
+        with torch.no_grad():
+            self.tensor.copy_(_t(t))
+
+    def set_name(self, name: str) -> "Value":
+        self.name = name
+        return self
+
+    def set_requires_grad(self, flag: bool) -> "Value":
+        if self.tensor.is_leaf:
+            self.tensor.requires_grad_(flag)
+        elif not flag:
+            self.tensor = self.tensor.detach()
+        return self
+
+    def to_vec(self) -> list[float]:
+        return [float(v) for v in self.tensor.detach().reshape(-1).cpu().tolist()]
+
     def avg_pool2d(self, k, stride=None):
         return Value._wrap(torch.nn.functional.avg_pool2d(self.tensor, k, stride), "avg_pool2d", self)
 
@@ -283,6 +326,37 @@ def with_no_grad(fn, *args, **kw):
 
 def is_grad_enabled() -> bool:
     return torch.is_grad_enabled()
+
+
+def set_grad_enabled(flag: bool):
+    """Context manager (or plain call) that turns gradient recording on or off."""
+    return torch.set_grad_enabled(flag)
+
+
+def with_enable_grad(fn, *args, **kw):
+    with torch.enable_grad():
+        return fn(*args, **kw)
+
+
+def grad_of(v: Value):
+    return v.grad()
+
+
+def zero_grad_from(root: Value) -> None:
+    """Clear the gradients of every leaf that ``root`` depends on."""
+    seen, keep, stack = set(), [], [root.tensor.grad_fn]
+    while stack:
+        n = stack.pop()
+        if n is None or id(n) in seen:
+            continue
+        seen.add(id(n))
+        keep.append(n)  # node wrappers stay alive, so their ids are not reused during the walk
+        var = getattr(n, "variable", None)
+        if var is not None:
+            var.grad = None
+        stack.extend(p for p, _ in getattr(n, "next_functions", ()))
+    if root.tensor.is_leaf:
+        root.tensor.grad = None
 
 
 def backward_from(v: Value) -> None:

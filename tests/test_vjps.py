@@ -123,3 +123,28 @@ def test_shape_index_linalg_pool_conv_vjps():
     gz = torch.complex(_r(8, seed=47), _r(8, seed=48))
     (ref,) = _auto(torch.fft.fft, z, g=gz)
     assert torch.allclose(V.grad_fft1d(gz), ref)
+
+
+def test_value_setters_and_grad_helpers():
+    from brain_b200.autograd import Value, set_grad_enabled, with_enable_grad, grad_of, zero_grad_from, no_grad
+    a = Value.from_slice([1.0, 2.0, 3.0], (3,), requires_grad=True).set_name("a")
+    b = Value.from_tensor(torch.tensor([0.5, 0.5, 0.5]), requires_grad=True)
+    y = (a * b).sum()
+    y.backward()
+    assert a.name == "a" and torch.equal(grad_of(a), torch.full((3,), 0.5))
+    zero_grad_from(y)
+    assert a.grad() is None and b.grad() is None
+    a.set_data(torch.tensor([4.0, 5.0, 6.0]))
+    assert a.to_vec() == [4.0, 5.0, 6.0]
+    a.set_requires_grad(False)
+    assert not a.requires_grad
+    w = Value(torch.tensor([1.0, -1.0, 2.0])).where_cond(torch.tensor([True, False, True]), torch.zeros(3))
+    assert w.to_vec() == [1.0, 0.0, 2.0]
+    with set_grad_enabled(False):
+        assert not torch.is_grad_enabled()
+    with no_grad():
+        assert with_enable_grad(torch.is_grad_enabled)
+    img = Value(torch.randn(1, 2, 6, 6), requires_grad=True)
+    assert img.adaptive_avg_pool2d(3).shape == (1, 2, 3, 3) and img.adaptive_max_pool2d(2).shape == (1, 2, 2, 2)
+    out = img.conv_transpose2d(torch.randn(2, 3, 3, 3), stride=2)
+    assert out.shape == (1, 3, 13, 13)
