@@ -395,3 +395,63 @@ class RelativisticLoss:
     @staticmethod
     def generator_loss(d_real, d_fake):
         return F.softplus(-(d_fake - d_real.mean())).mean() + F.softplus(d_real - d_fake.mean()).mean()
+
+
+# ------------------------------------------------------------------ the reference's spellings and helpers
+# crates/brain-loss/src: regression/mse.rs (MAELoss), classification/other.rs (KLDivergenceLoss),
+# distillation.rs (KnowledgeDistillationLoss), contrastive/simclr.rs (SimCLRLoss), contrastive/triplet.rs
+# (TripletMarginLoss), adversarial/{mod,other}.rs, combine.rs (CompositeLoss), masked.rs (apply_loss_mask),
+# ops.rs (one_hot_target, log_sum_exp_2d), utils.rs (reduction_apply, weighted_average, clamp_eps).
+MAELoss = L1Loss
+KLDivergenceLoss = KLDivLoss
+KnowledgeDistillationLoss = DistillationLoss
+SimCLRLoss = NTXentLoss
+TripletMarginLoss = TripletLoss
+AdversarialLoss = GANLoss
+HingeAdversarialLoss = HingeGANLoss
+CompositeLoss = CombinedLoss
+
+
+def apply_loss_mask(per_element: torch.Tensor, mask: torch.Tensor) -> torch.Tensor:
+    """Mean of the per-element loss over the positions where mask is nonzero (0 when none are)."""
+    m = mask.to(per_element.dtype)
+    return (per_element * m).sum() / m.sum().clamp_min(1.0)
+
+
+def one_hot_target(indices: torch.Tensor, num_classes: int, dtype=torch.float32) -> torch.Tensor:
+    return torch.nn.functional.one_hot(indices.long(), num_classes).to(dtype)
+
+
+def log_sum_exp_2d(x: torch.Tensor) -> torch.Tensor:
+    """Row-wise log-sum-exp of a [N, C] matrix (max-shifted)."""
+    return torch.logsumexp(x, dim=-1)
+
+
+def reduction_apply(x: torch.Tensor, reduction: str = "mean") -> torch.Tensor:
+    return _reduce(x, reduction)
+
+
+def weighted_average(values: torch.Tensor, weights: torch.Tensor) -> torch.Tensor:
+    w = weights.to(values.dtype)
+    return (values * w).sum() / w.sum().clamp_min(torch.finfo(values.dtype).tiny)
+
+
+def clamp_eps(x: torch.Tensor, eps: float = 1e-7) -> torch.Tensor:
+    return x.clamp(eps, 1 - eps)
+
+
+_LOSSES = {"mse": MSELoss, "mae": L1Loss, "l1": L1Loss, "huber": HuberLoss, "smooth_l1": SmoothL1Loss,
+           "log_cosh": LogCoshLoss, "cross_entropy": CrossEntropyLoss, "nll": NLLLoss, "bce": BCELoss,
+           "bce_with_logits": BCEWithLogitsLoss, "focal": FocalLoss, "hinge": HingeLoss, "kl_div": KLDivLoss,
+           "dice": DiceLoss, "iou": IoULoss, "cosine_embedding": CosineEmbeddingLoss}
+
+
+def loss_names() -> list[str]:
+    return sorted(_LOSSES)
+
+
+def compute_loss(kind: str, pred: torch.Tensor, target: torch.Tensor, **kw) -> torch.Tensor:
+    """One call by name: ``compute_loss("huber", pred, target, delta=0.5)``."""
+    if kind not in _LOSSES:
+        raise ValueError(f"unknown loss {kind!r}; known: {', '.join(loss_names())}")
+    return _LOSSES[kind](**kw)(pred, target)

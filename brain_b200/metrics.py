@@ -522,3 +522,82 @@ def format_markdown_report(metrics: dict, title: str = "Metrics") -> str:
 
 def format_csv_report(metrics: dict) -> str:
     return "metric,value\n" + "".join(f"{k},{v}\n" for k, v in sorted(metrics.items()))
+
+
+# ------------------------------------------------------------------ the reference's spellings and helpers
+# crates/brain-metric/src: classification/mod.rs (accuracy_score), classification/auc.rs (roc_auc_score),
+# imbalance.rs (matthews_correlation_coefficient), regression/mod.rs (mse/rmse/mae/mape_score),
+# stats/mod.rs (pearson_correlation), nlp (sentence_bleu, perplexity_score, edit_distance_levenshtein),
+# multilabel.rs (exact_match_ratio), segmentation/mod.rs (miou_and_pixel_accuracy), detection (bbox_iou),
+# ops.rs (logits_to_predictions, binarize_probs), utils.rs (topk_indices, stable_divide, bin_values_uniform).
+accuracy_score = accuracy
+roc_auc_score = roc_auc
+matthews_correlation_coefficient = matthews_corrcoef
+mse_score = mse
+rmse_score = rmse
+mae_score = mae
+mape_score = mape
+pearson_correlation = pearson
+perplexity_score = perplexity
+bbox_iou = box_iou
+
+
+def sentence_bleu(candidate, references, max_n: int = 4, smooth: bool = True) -> float:
+    return bleu(candidate, references, max_n, smooth)
+
+
+def edit_distance_levenshtein(a, b) -> int:
+    from .text_ops import levenshtein_distance
+    return levenshtein_distance(a, b)
+
+
+def exact_match_ratio(pred: torch.Tensor, target: torch.Tensor) -> float:
+    """Share of samples whose whole label vector matches (multi-label subset accuracy)."""
+    return float((pred.bool() == target.bool()).all(-1).float().mean())
+
+
+def miou_and_pixel_accuracy(pred: torch.Tensor, target: torch.Tensor, num_classes: int):
+    """(mean IoU over classes present in either map, pixel accuracy) of integer label maps."""
+    p, t = pred.reshape(-1).long(), target.reshape(-1).long()
+    cm = torch.bincount(t * num_classes + p, minlength=num_classes * num_classes).reshape(num_classes, num_classes)
+    inter = cm.diag().double()
+    union = cm.sum(0).double() + cm.sum(1).double() - inter
+    present = union > 0
+    miou = float((inter[present] / union[present]).mean()) if present.any() else 0.0
+    return miou, float(inter.sum() / cm.sum().clamp_min(1))
+
+
+def logits_to_predictions(logits: torch.Tensor) -> torch.Tensor:
+    return logits.argmax(-1)
+
+
+def binarize_probs(probs: torch.Tensor, threshold: float = 0.5) -> torch.Tensor:
+    return (probs >= threshold).long()
+
+
+def topk_indices(values: torch.Tensor, k: int) -> torch.Tensor:
+    return torch.topk(values, min(k, values.shape[-1]), dim=-1).indices
+
+
+def stable_divide(num: float, den: float, default: float = 0.0) -> float:
+    return num / den if den != 0 else default
+
+
+def bin_values_uniform(values: torch.Tensor, num_bins: int, lo: float = 0.0, hi: float = 1.0) -> torch.Tensor:
+    """Bin index in [0, num_bins) of each value over the uniform partition of [lo, hi] (edges clamp)."""
+    idx = ((values - lo) / (hi - lo) * num_bins).floor().long()
+    return idx.clamp(0, num_bins - 1)
+
+
+_METRICS = {"accuracy": accuracy, "mse": mse, "rmse": rmse, "mae": mae, "mape": mape, "r2": r2_score,
+            "pearson": pearson, "spearman": spearman, "roc_auc": roc_auc, "mcc": matthews_corrcoef}
+
+
+def metric_names() -> list[str]:
+    return sorted(_METRICS)
+
+
+def compute_metric(kind: str, pred, target, **kw):
+    if kind not in _METRICS:
+        raise ValueError(f"unknown metric {kind!r}; known: {', '.join(metric_names())}")
+    return _METRICS[kind](pred, target, **kw)
