@@ -301,3 +301,187 @@ class StyleGanLite(Module):
     def forward(self, z: torch.Tensor) -> torch.Tensor:
         w = self.mapping(z)
         return self.synthesize([w] * self.num_layers)
+
+
+# ------------------------------------------------------------------------------------------ more architectures
+# Reference: discriminator/patch.rs (PatchDiscriminator, num_patches), generator/resnet.rs
+# (ResnetGenerator: residual blocks between down- and up-sampling), generator/conditional.rs
+# (class embedding concatenated to z), discriminator/conditional.rs (class projection added to the
+# score), train/mod.rs + train/loop_.rs (GanTrainer, n_critic, per-epoch statistics), eval/samples.rs
+# (assemble_grid).
+
+def _norm2d(kind: str, c: int, device=None, dtype=None):
+    if kind == "batch":
+        return torch.nn.BatchNorm2d(c, device=device, dtype=dtype)
+    if kind == "instance":
+        return torch.nn.InstanceNorm2d(c, affine=True, device=device, dtype=dtype)
+    return torch.nn.Identity()
+
+
+class PatchDiscriminator(Module):
+    """PatchGAN: 4x4 stride-2 convs (LeakyReLU 0.2, normalised after the first) then a stride-1 conv to
+    one logit per receptive-field patch: [B, 1, h, w]."""
+
+    def __init__(self, in_channels: int = 3, base: int = 64, n_layers: int = 3, norm: str = "batch", device=None,
+                 dtype=None):
+        super().__init__()
+        layers, c = [], in_channels
+        for i in range(n_layers):
+            co = base * 2 ** i
+            layers.append(torch.nn.Conv2d(c, co, 4, 2, 1, device=device, dtype=dtype))
+            if i > 0:
+                layers.append(_norm2d(norm, co, device, dtype))
+            layers.append(torch.nn.LeakyReLU(0.2))
+            c = co
+        layers.append(torch.nn.Conv2d(c, 1, 3, 1, 1, device=device, dtype=dtype))
+        self.net = torch.nn.Sequential(*layers)
+        self.n_layers = n_layers
+
+    def num_patches(self, h: int, w: int) -> int:
+        return (h >> self.n_layers) * (w >> self.n_layers)
+
+    def forward(self, x):
+        return self.net(x)
+
+
+class _ResBlock(Module):
+    def __init__(self, c, norm, device=None, dtype=None):
+        super().__init__()
+        self.body = torch.nn.Sequential(
+            torch.nn.ReflectionPad2d(1), torch.nn.Conv2d(c, c, 3, device=device, dtype=dtype), _norm2d(norm, c, device, dtype),
+            torch.nn.ReLU(), torch.nn.ReflectionPad2d(1), torch.nn.Conv2d(c, c, 3, device=device, dtype=dtype),
+            _norm2d(norm, c, device, dtype))
+
+    def forward(self, x):
+        return x + self.body(x)
+
+
+class ResnetGenerator(Module):
+    """Image-to-image generator: 7x7 stem, two stride-2 down-samplings, ``n_blocks`` residual blocks,
+    two stride-2 transposed-conv up-samplings, 7x7 head with tanh. Output has the input's H x W."""
+
+    def __init__(self, in_channels: int = 3, out_channels: int = 3, base: int = 64, n_blocks: int = 6,
+                 norm: str = "batch", device=None, dtype=None):
+        super().__init__()
+        kw = dict(device=device, dtype=dtype)
+        layers = [torch.nn.ReflectionPad2d(3), torch.nn.Conv2d(in_channels, base, 7, **kw), _norm2d(norm, base, **kw),
+                  torch.nn.ReLU()]
+        c = base
+        for _ in range(2):
+            layers += [torch.nn.Conv2d(c, 2 * c, 3, 2, 1, **kw), _norm2d(norm, 2 * c, **kw), torch.nn.ReLU()]
+            c *= 2
+        layers += [_ResBlock(c, norm, **kw) for _ in range(n_blocks)]
+        for _ in range(2):
+            layers += [torch.nn.ConvTranspose2d(c, c // 2, 3, 2, 1, output_padding=1, **kw), _norm2d(norm, c // 2, **kw),
+                       torch.nn.ReLU()]
+            c //= 2
+        layers += [torch.nn.ReflectionPad2d(3), torch.nn.Conv2d(c, out_channels, 7, **kw), torch.nn.Tanh()]
+        self.net = torch.nn.Sequential(*layers)
+
+    def forward(self, x):
+        return self.net(x)
+
+
+class ConditionalGenerator(Module):
+    """G(z, y): a learned class embedding of size latent_dim is concatenated to z and fed to an MLP
+    generator producing ``out_dim`` values in (-1, 1)."""
+
+    def __init__(self, latent_dim: int, num_classes: int, out_dim: int, hidden: int = 256, device=None, dtype=None):
+        super().__init__()
+        self.latent_dim, self.num_classes = latent_dim, num_classes
+        self.embed = torch.nn.Embedding(num_classes, latent_dim, device=device, dtype=dtype)
+        self.net = torch.nn.Sequential(Linear(2 * latent_dim, hidden, True, device, dtype), torch.nn.ReLU(),
+                                       Linear(hidden, hidden, True, device, dtype), torch.nn.ReLU(),
+                                       Linear(hidden, out_dim, True, device, dtype), torch.nn.Tanh())
+
+    def embed_class(self, y):
+        return self.embed(torch.as_tensor(y, device=self.embed.weight.device).long())
+
+    def forward(self, z, y):
+        return self.net(torch.cat([z, self.embed_class(y)], -1))
+
+
+class ConditionalDiscriminator(Module):
+    """Projection discriminator (Miyato & Koyama 2018): D(x, y) = w . phi(x) + <e_y, phi(x)>."""
+
+    def __init__(self, in_dim: int, num_classes: int, hidden: int = 256, device=None, dtype=None):
+        super().__init__()
+        self.phi = torch.nn.Sequential(Linear(in_dim, hidden, True, device, dtype), torch.nn.LeakyReLU(0.2),
+                                       Linear(hidden, hidden, True, device, dtype), torch.nn.LeakyReLU(0.2))
+        self.out = Linear(hidden, 1, True, device, dtype)
+        self.class_embed = torch.nn.Embedding(num_classes, hidden, device=device, dtype=dtype)
+
+    def class_projection(self, features, y):
+        e = self.class_embed(torch.as_tensor(y, device=features.device).long())
+        return (e * features).sum(-1, keepdim=True)
+
+    def forward(self, x, y):
+        h = self.phi(x)
+        return self.out(h) + self.class_projection(h, y)
+
+
+@dataclass
+class GanTrainStats:
+    epoch: int
+    d_loss: float
+    g_loss: float
+    steps: int
+
+
+class GanTrainer:
+    """Alternating updates over a data iterable: ``n_critic`` discriminator steps per generator step,
+    an optional gradient penalty, per-epoch mean losses. ``loss`` is one of bce / hinge / lsgan / wgan."""
+
+    def __init__(self, gen, disc, opt_g, opt_d, loss: str = "bce", n_critic: int = 1, gp_weight: float = 0.0,
+                 clip: float | None = None, seed: int = 0):
+        from .gan import (bce_loss_d, bce_loss_g, gradient_penalty, hinge_loss_d, hinge_loss_g, lsgan_loss_d,
+                          lsgan_loss_g, wgan_loss_d, wgan_loss_g)
+        self.gen, self.disc, self.opt_g, self.opt_d = gen, disc, opt_g, opt_d
+        self.ld = {"bce": bce_loss_d, "hinge": hinge_loss_d, "lsgan": lsgan_loss_d, "wgan": wgan_loss_d}[loss]
+        self.lg = {"bce": bce_loss_g, "hinge": hinge_loss_g, "lsgan": lsgan_loss_g, "wgan": wgan_loss_g}[loss]
+        self.gp, self.gp_weight, self.n_critic, self.clip = gradient_penalty, gp_weight, n_critic, clip
+        self.g = torch.Generator().manual_seed(seed)
+        self.history: list[GanTrainStats] = []
+
+    def _z(self, n, ref):
+        return torch.randn((n, self.gen.latent_dim), generator=self.g).to(ref.device, ref.dtype)
+
+    def discriminator_step(self, real) -> float:
+        fake = self.gen(self._z(real.shape[0], real)).detach()
+        ld = self.ld(self.disc(real), self.disc(fake))
+        if self.gp_weight > 0:
+            ld = ld + self.gp(self.disc, real, fake, self.gp_weight, self.g)
+        self.opt_d.zero_grad()
+        ld.backward()
+        self.opt_d.step()
+        if self.clip is not None:  # WGAN weight clipping
+            with torch.no_grad():
+                for prm in self.disc.parameters():
+                    prm.copy_(clip_weights(prm, self.clip))
+        return float(ld.detach())
+
+    def generator_step(self, batch_size: int, ref) -> float:
+        lg = self.lg(self.disc(self.gen(self._z(batch_size, ref))))
+        self.opt_g.zero_grad()
+        lg.backward()
+        self.opt_g.step()
+        return float(lg.detach())
+
+    def train_epoch(self, data) -> GanTrainStats:
+        dl, gl, nd, ng = 0.0, 0.0, 0, 0
+        for i, real in enumerate(data):
+            dl += self.discriminator_step(real)
+            nd += 1
+            if (i + 1) % self.n_critic == 0:
+                gl += self.generator_step(real.shape[0], real)
+                ng += 1
+        st = GanTrainStats(len(self.history), dl / max(nd, 1), gl / max(ng, 1), nd)
+        self.history.append(st)
+        return st
+
+    def fit(self, data_fn, epochs: int) -> list[GanTrainStats]:
+        return [self.train_epoch(data_fn()) for _ in range(epochs)]
+
+
+def assemble_grid(images: torch.Tensor, ncols: int, pad: int = 2, value: float = 1.0) -> torch.Tensor:
+    return image_grid(images, ncols, pad, value)

@@ -97,3 +97,35 @@ def test_stylegan_and_cyclegan_modules_train():
         loss.backward()
         opt.step()
     assert float(loss) < first
+
+
+def test_patch_resnet_conditional_and_trainer():
+    import torch
+    from brain_b200.zoo import gan_extras as GX
+    from brain_b200.zoo.gan import MlpDiscriminator, MlpGenerator
+    torch.manual_seed(0)
+    pd = GX.PatchDiscriminator(3, base=8, n_layers=3)
+    out = pd(torch.randn(2, 3, 64, 64))
+    assert out.shape == (2, 1, 8, 8) and pd.num_patches(64, 64) == 64
+    rg = GX.ResnetGenerator(3, 3, base=8, n_blocks=2, norm="instance")
+    y = rg(torch.randn(1, 3, 32, 32))
+    assert y.shape == (1, 3, 32, 32) and y.abs().max() <= 1
+    cg = GX.ConditionalGenerator(8, 4, 10, hidden=16)
+    cd = GX.ConditionalDiscriminator(10, 4, hidden=16)
+    z = torch.randn(5, 8)
+    labels = torch.tensor([0, 1, 2, 3, 0])
+    x = cg(z, labels)
+    assert x.shape == (5, 10)
+    assert not torch.allclose(cg(z, torch.zeros(5, dtype=torch.long)), cg(z, torch.ones(5, dtype=torch.long)))
+    s = cd(x, labels)
+    h = cd.phi(x)
+    assert torch.allclose(s, cd.out(h) + (cd.class_embed(labels) * h).sum(-1, keepdim=True))
+    gen = MlpGenerator(4, 2, hidden=16)
+    disc = MlpDiscriminator(2, hidden=16)
+    tr = GX.GanTrainer(gen, disc, torch.optim.Adam(gen.parameters(), 1e-3), torch.optim.Adam(disc.parameters(), 1e-3),
+                       loss="wgan", n_critic=2, clip=0.05)
+    data = lambda: [torch.randn(16, 2) * 0.1 + 1.0 for _ in range(4)]
+    hist = tr.fit(data, 2)
+    assert len(hist) == 2 and hist[1].steps == 4 and all(p.abs().max() <= 0.05 + 1e-7 for p in disc.parameters())
+    g = GX.assemble_grid(torch.zeros(3, 1, 4, 4), 2, pad=1)
+    assert g.shape == (1, 9, 9)
