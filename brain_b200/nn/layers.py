@@ -298,6 +298,14 @@ class InstanceNorm2d(torch.nn.InstanceNorm2d, Module):
     pass
 
 
+class BatchNorm1d(torch.nn.BatchNorm1d, Module):
+    pass
+
+
+class InstanceNorm1d(torch.nn.InstanceNorm1d, Module):
+    pass
+
+
 class Flatten(torch.nn.Flatten, Module):
     pass
 

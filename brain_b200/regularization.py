@@ -176,3 +176,30 @@ class EarlyStopper:
         else:
             self.bad += 1
         return self.bad >= self.patience
+
+
+# The reference's spellings (crates/brain-regularization/src: label_smooth.rs smooth_targets, augment.rs
+# apply_mixup / apply_cutout_2d, ewc.rs ElasticWeightConsolidation, regularizers.rs ElasticNetRegularizer,
+# normalization/{batch,group}.rs BatchNorm1d / InstanceNorm1d).
+smooth_targets = smooth_labels
+apply_mixup = mixup
+apply_cutout_2d = cutout
+ElasticWeightConsolidation = EWC
+
+
+class ElasticNetRegularizer:
+    """alpha * (l1_ratio * sum|w| + (1 - l1_ratio) / 2 * sum w^2) over the given parameters."""
+
+    def __init__(self, alpha: float = 1e-4, l1_ratio: float = 0.5):
+        self.alpha, self.l1_ratio = alpha, l1_ratio
+
+    def penalty(self, params) -> torch.Tensor:
+        params = list(params)
+        l1 = sum(p.abs().sum() for p in params)
+        l2 = sum((p * p).sum() for p in params)
+        return self.alpha * (self.l1_ratio * l1 + (1 - self.l1_ratio) * 0.5 * l2)
+
+    __call__ = penalty
+
+
+from .nn.layers import BatchNorm1d, InstanceNorm1d  # noqa: E402,F401

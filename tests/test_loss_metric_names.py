@@ -39,3 +39,13 @@ def test_metric_aliases_and_helpers():
     assert M.sentence_bleu("a b c d".split(), ["a b c d".split()]) == pytest.approx(1.0)
     assert M.compute_metric("mae", torch.tensor([1.0, 3.0]), torch.tensor([2.0, 2.0])) == pytest.approx(1.0)
     assert "roc_auc" in M.metric_names()
+
+
+def test_regularization_names():
+    from brain_b200 import regularization as R
+    from brain_b200.nn import BatchNorm1d, InstanceNorm1d
+    e = R.ElasticNetRegularizer(0.1, 0.5)
+    assert float(e([torch.tensor([1.0, -2.0])])) == pytest.approx(0.1 * (0.5 * 3 + 0.25 * 5))
+    assert R.ElasticWeightConsolidation is R.EWC and R.apply_mixup is R.mixup
+    assert BatchNorm1d(4)(torch.randn(3, 4)).shape == (3, 4)
+    assert InstanceNorm1d(2)(torch.randn(1, 2, 5)).shape == (1, 2, 5)
