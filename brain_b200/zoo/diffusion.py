@@ -13,6 +13,7 @@ fused elementwise ops plus the denoiser's forward.
 from __future__ import annotations
 
 import math
+from dataclasses import dataclass
 
 import torch
 
@@ -189,3 +190,69 @@ class EulerAncestralSampler:
             if s_up > 0:
                 x = x + s_up * torch.randn(x.shape, generator=generator, device="cpu").to(x.device, x.dtype)
         return x
+
+
+# ------------------------------------------------------------------ the reference's entry points
+# crates/brain-diffusion/src: unet/embeddings.rs (sinusoidal_timestep_embedding), diffusion/losses.rs
+# (eps_loss), diffusion/train.rs (training_step), utils.rs (linspace_timesteps, extract_at_t),
+# diffusion/mod.rs + impl.rs (DiffusionModel / DiffusionRunner: denoiser + schedule + sampler),
+# guidance.rs (GuidanceConfig).
+sinusoidal_timestep_embedding = timestep_embedding
+
+
+def eps_loss(pred_eps: torch.Tensor, true_eps: torch.Tensor) -> torch.Tensor:
+    return torch.nn.functional.mse_loss(pred_eps.float(), true_eps.float())
+
+
+def linspace_timesteps(num_train_steps: int, num_steps: int) -> torch.Tensor:
+    """Descending sampling timesteps spread evenly over [0, num_train_steps - 1]."""
+    return torch.linspace(num_train_steps - 1, 0, num_steps).round().long()
+
+
+def extract_at_t(values: torch.Tensor, t: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+    """values[t] reshaped to broadcast against ``like`` ([B, 1, 1, ...])."""
+    v = values.to(like.device)[t.to(like.device)].to(like.dtype)
+    return v.view(-1, *([1] * (like.dim() - 1)))
+
+
+def training_step(model, schedule: NoiseSchedule, optimizer, x0, cond=None, generator=None,
+                  cond_drop_prob: float = 0.0) -> float:
+    """One epsilon-prediction update; with ``cond_drop_prob`` the condition is dropped for the whole
+    batch with that probability (training for classifier-free guidance)."""
+    if cond is not None and cond_drop_prob > 0:
+        u = float(torch.rand((), generator=generator))
+        cond = None if u < cond_drop_prob else cond
+    loss = diffusion_loss(model, schedule, x0, cond, generator)
+    optimizer.zero_grad()
+    loss.backward()
+    optimizer.step()
+    return float(loss.detach())
+
+
+@dataclass
+class GuidanceConfig:
+    scale: float = 1.0
+    cond_drop_prob: float = 0.1
+
+
+class DiffusionModel:
+    """A denoiser with its noise schedule and a sampler: ``train_step(x0)`` and ``sample(shape)``."""
+
+    def __init__(self, denoiser, schedule: NoiseSchedule | None = None, sampler: str = "ddim",
+                 guidance: GuidanceConfig | None = None):
+        self.denoiser = denoiser
+        self.schedule = schedule or LinearSchedule()
+        self.sampler = {"ddpm": DdpmSampler, "ddim": DdimSampler, "euler_a": EulerAncestralSampler}[sampler](self.schedule)
+        self.guidance = guidance or GuidanceConfig()
+
+    def train_step(self, optimizer, x0, cond=None, generator=None) -> float:
+        return training_step(self.denoiser, self.schedule, optimizer, x0, cond, generator,
+                             self.guidance.cond_drop_prob if cond is not None else 0.0)
+
+    @torch.no_grad()
+    def sample(self, shape, device=None, cond=None, generator=None, **kw):
+        return self.sampler.sample(self.denoiser, shape, device=device, cond=cond,
+                                   guidance_scale=self.guidance.scale, generator=generator, **kw)
+
+
+DiffusionRunner = DiffusionModel

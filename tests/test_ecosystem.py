@@ -1359,3 +1359,24 @@ def test_adamw_group_weight_decay_overrides_default():
     opt.step()
     # decoupled decay p -= lr * wd * p before the moments; a zero gradient leaves only the decay
     assert torch.allclose(a.data, torch.full((2,), 0.95)) and torch.equal(b.data, torch.ones(2))
+
+
+def test_diffusion_model_wrapper_and_helpers():
+    import torch
+    from brain_b200.zoo import diffusion as D
+    torch.manual_seed(0)
+    assert D.linspace_timesteps(1000, 5).tolist() == [999, 749, 500, 250, 0]
+    vals = torch.arange(10.0)
+    assert D.extract_at_t(vals, torch.tensor([2, 7]), torch.zeros(2, 3, 4)).shape == (2, 1, 1)
+    assert float(D.eps_loss(torch.ones(3), torch.zeros(3))) == 1.0
+    net = D.MlpDenoiser(2, hidden=32, time_dim=16, num_classes=3)
+    dm = D.DiffusionModel(net, D.LinearSchedule(50), sampler="ddim", guidance=D.GuidanceConfig(scale=2.0))
+    opt = torch.optim.Adam(net.parameters(), 1e-2)
+    g = torch.Generator().manual_seed(1)
+    x0 = torch.randn(64, 2, generator=g) * 0.1 + torch.tensor([1.0, -1.0])
+    cond = torch.randint(0, 3, (64,), generator=g)
+    losses = [dm.train_step(opt, x0, cond, generator=g) for _ in range(30)]
+    assert sum(losses[-5:]) < sum(losses[:5])
+    out = dm.sample((8, 2), cond=cond[:8], generator=g, num_steps=10)
+    assert out.shape == (8, 2) and torch.isfinite(out).all()
+    assert D.DiffusionRunner is D.DiffusionModel and D.sinusoidal_timestep_embedding is D.timestep_embedding
