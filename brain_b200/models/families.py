@@ -171,12 +171,18 @@ class ViT(Module):
         x = images.reshape(B, C, H // P, P, W // P, P).permute(0, 2, 4, 1, 3, 5)
         return x.reshape(B, (H // P) * (W // P), C * P * P)
 
-    def forward(self, images):
+    def embed_patches(self, images):
+        """[B, C, H, W] -> [B, 1 + N, D]: patch projection (one GEMM), class token, position embedding."""
         x = self.patch(self.patchify(images).to(self.patch.weight.dtype))
         cls = self.cls_token.expand(x.shape[0], -1, -1)
-        x = torch.cat([cls, x], 1) + self.pos
-        h = self.encoder(x)
-        return self.head(h[:, 0])
+        return torch.cat([cls, x], 1) + self.pos
+
+    def forward_features(self, images):
+        """Encoder output for every token [B, 1 + N, D] (class token first)."""
+        return self.encoder(self.embed_patches(images))
+
+    def forward(self, images):
+        return self.head(self.forward_features(images)[:, 0])
 
     def loss(self, images, labels):
         return ops.cross_entropy(self.forward(images), labels)

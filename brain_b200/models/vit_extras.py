@@ -189,3 +189,72 @@ class ModelCard:
             lines += ["", "## Metrics", "", "| metric | value |", "|---|---|"] + \
                      [f"| {k} | {v:.4f} |" for k, v in sorted(self.metrics.items())]
         return "\n".join(lines) + "\n"
+
+
+# ------------------------------------------------------------------ the reference's ViT entry points
+# crates/brain-vit/src: patch/mod.rs (PatchEmbed, num_patches_for), impl.rs (VitModel, embed_patches,
+# forward_features), vit/heads.rs (VitHead: class-token or mean pooling -> linear), training/mod.rs
+# (label_smooth_ce, GradientClipper), ops.rs (position_ids, reconstruct_patches).
+
+def num_patches_for(image_size: int, patch_size: int) -> int:
+    if image_size % patch_size:
+        raise ValueError(f"image size {image_size} is not a multiple of patch size {patch_size}")
+    return (image_size // patch_size) ** 2
+
+
+class PatchEmbed(torch.nn.Module):
+    """Non-overlapping P x P patches -> D features: a reshape then one GEMM (the framework's Linear),
+    the same product as a stride-P convolution without an im2col pass."""
+
+    def __init__(self, in_channels: int, patch_size: int, dim: int, device=None, dtype=None):
+        super().__init__()
+        from ..nn.layers import Linear
+        self.P = patch_size
+        self.proj = Linear(in_channels * patch_size * patch_size, dim, True, device, dtype)
+
+    def forward(self, images):
+        B, C, H, W = images.shape
+        P = self.P
+        x = images.reshape(B, C, H // P, P, W // P, P).permute(0, 2, 4, 1, 3, 5).reshape(B, -1, C * P * P)
+        return self.proj(x.to(self.proj.weight.dtype))
+
+
+class VitHead(torch.nn.Module):
+    """Pooling ("cls": the class token, "mean": mean of the patch tokens) -> LayerNorm -> Linear."""
+
+    def __init__(self, dim: int, num_classes: int, pool: str = "cls", device=None, dtype=None):
+        super().__init__()
+        from ..nn.layers import Linear
+        self.pool = pool
+        self.norm = torch.nn.LayerNorm(dim, device=device, dtype=dtype)
+        self.fc = Linear(dim, num_classes, True, device, dtype)
+
+    def forward(self, tokens):
+        x = tokens[:, 0] if self.pool == "cls" else tokens[:, 1:].mean(1)
+        return self.fc(self.norm(x))
+
+
+def position_ids(num_tokens: int, batch: int = 1, device=None) -> torch.Tensor:
+    return torch.arange(num_tokens, device=device).expand(batch, num_tokens)
+
+
+def reconstruct_patches(patches: torch.Tensor, image_size: int, patch_size: int, channels: int) -> torch.Tensor:
+    """[B, N, C*P*P] -> [B, C, H, W] (inverse of patchify)."""
+    g = image_size // patch_size
+    B = patches.shape[0]
+    x = patches.reshape(B, g, g, channels, patch_size, patch_size).permute(0, 3, 1, 4, 2, 5)
+    return x.reshape(B, channels, image_size, image_size)
+
+
+def label_smooth_ce(logits: torch.Tensor, labels: torch.Tensor, smoothing: float = 0.1) -> torch.Tensor:
+    return torch.nn.functional.cross_entropy(logits.float(), labels, label_smoothing=smoothing)
+
+
+class GradientClipper:
+    """Global-norm clipping of a parameter set; ``clip`` returns the norm before clipping."""
+
+    def __init__(self, max_norm: float = 1.0):
+        self.max_norm = max_norm
+
+    def clip(self, params) -> float:
+        return float(torch.nn.utils.clip_grad_norm_(list(params), self.max_norm))

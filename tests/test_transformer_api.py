@@ -212,3 +212,26 @@ def test_front_ends_on_cuda_kernels():
     refb = _rope_oracle(xb.double().cpu(), cos, sin, torch.arange(10, 266)).float()
     yb = re.apply_rope_4d(xb.clone(), pos_offset=10)  # bf16: the rope kernel, strided [B, S, H, D] view
     assert float((yb.float().cpu() - refb).abs().max()) < 3e-2
+
+
+def test_vit_entry_points():
+    from brain_b200.models import ViT, ViTConfig, VitModel
+    from brain_b200.models import vit_extras as VX
+    torch.manual_seed(6)
+    cfg = ViTConfig(image_size=32, patch_size=8, in_channels=3, hidden_dim=32, num_layers=1, num_heads=2, mlp_dim=64,
+                    num_classes=5)
+    m = VitModel(cfg)
+    img = torch.randn(2, 3, 32, 32)
+    feats = m.forward_features(img)
+    assert feats.shape == (2, 17, 32) and torch.allclose(m(img), m.head(feats[:, 0]))
+    assert VX.num_patches_for(32, 8) == 16
+    pe = VX.PatchEmbed(3, 8, 32)
+    conv = torch.nn.functional.conv2d(img, pe.proj.weight.view(32, 3, 8, 8), pe.proj.bias, stride=8)
+    assert torch.allclose(pe(img), conv.flatten(2).transpose(1, 2), atol=1e-5)
+    assert torch.equal(VX.reconstruct_patches(m.patchify(img), 32, 8, 3), img)
+    head = VX.VitHead(32, 5, pool="mean")
+    assert head(feats).shape == (2, 5)
+    assert VX.position_ids(4, 2).tolist() == [[0, 1, 2, 3]] * 2
+    logits = torch.randn(3, 5, requires_grad=True)
+    VX.label_smooth_ce(logits, torch.tensor([0, 1, 2])).backward()
+    assert VX.GradientClipper(1e-3).clip([logits]) > 1e-3 and float(logits.grad.norm()) <= 1e-3 + 1e-9
