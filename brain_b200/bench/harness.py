@@ -455,3 +455,135 @@ class KernelSuite:
                 BenchConfig("rms_norm", 2, iters, device=device, bytes_per_iter=2.0 * n * n * es),
                 BenchConfig("softmax_cross_entropy", 2, iters, device=device, bytes_per_iter=1.0 * n * n * es)]
         return [Runner.run_benchmark(c, f) for c, f in zip(cfgs, (mm, norm, ce))]
+
+
+# ------------------------------------------------------------------ suites, timers, formatting
+# Reference: crates/brain-benchmark/src/suite.rs (BenchmarkSuite::run_all / run_filtered),
+# impl.rs (FnBenchmark::from_fn, flop_count), timer.rs (BenchTimer start_new / elapsed_*, calibrate_timer_overhead),
+# utils.rs (format_gflops, format_throughput, round_places), hardware.rs (estimate_memory_bandwidth_gbps),
+# memory_bench.rs (get_peak_rss_kb).
+
+class FnBenchmark:
+    """A named callable with its work per call; ``run`` times it with ``Runner.run_benchmark``."""
+
+    def __init__(self, name: str, fn, flops: float = 0.0, nbytes: float = 0.0, device=None, warmup: int = 3,
+                 iters: int = 20, tags=()):
+        self.name, self.fn, self.tags = name, fn, set(tags)
+        self.config = BenchConfig(name, warmup, iters, 1, device, flops, nbytes)
+
+    @classmethod
+    def from_fn(cls, name: str, fn, **kw) -> "FnBenchmark":
+        return cls(name, fn, **kw)
+
+    def flop_count(self) -> float:
+        return self.config.flops_per_iter
+
+    def run(self) -> BenchResult:
+        return Runner.run_benchmark(self.config, self.fn)
+
+
+class BenchmarkSuite:
+    def __init__(self, name: str = "suite"):
+        self.name, self.benchmarks = name, []
+
+    def add(self, bench: FnBenchmark) -> "BenchmarkSuite":
+        self.benchmarks.append(bench)
+        return self
+
+    def run_all(self) -> dict:
+        return {b.name: b.run() for b in self.benchmarks}
+
+    def run_filtered(self, pattern: str = "", tag: str | None = None) -> dict:
+        return {b.name: b.run() for b in self.benchmarks
+                if pattern in b.name and (tag is None or tag in b.tags)}
+
+
+class BenchTimer:
+    """Wall-clock stopwatch (perf_counter_ns)."""
+
+    def __init__(self):
+        self._t0, self._t1 = None, None
+
+    @classmethod
+    def start_new(cls) -> "BenchTimer":
+        t = cls()
+        t.start()
+        return t
+
+    def start(self):
+        self._t0, self._t1 = time.perf_counter_ns(), None
+
+    def stop(self):
+        self._t1 = time.perf_counter_ns()
+
+    def is_running(self) -> bool:
+        return self._t0 is not None and self._t1 is None
+
+    def elapsed_nanos(self) -> int:
+        end = self._t1 if self._t1 is not None else time.perf_counter_ns()
+        return end - self._t0
+
+    def elapsed_micros(self) -> float:
+        return self.elapsed_nanos() / 1e3
+
+    def elapsed_millis(self) -> float:
+        return self.elapsed_nanos() / 1e6
+
+    def elapsed_secs(self) -> float:
+        return self.elapsed_nanos() / 1e9
+
+
+def calibrate_timer_overhead(samples: int = 1000) -> float:
+    """Median cost in ns of reading the clock twice back to back."""
+    d = []
+    for _ in range(samples):
+        a = time.perf_counter_ns()
+        b = time.perf_counter_ns()
+        d.append(b - a)
+    d.sort()
+    return float(d[len(d) // 2])
+
+
+def round_places(x: float, places: int) -> float:
+    return round(x, places)
+
+
+def format_gflops(flops: float, seconds: float) -> str:
+    v = flops / seconds / 1e9 if seconds > 0 else 0.0
+    return f"{v / 1e3:.2f} TFLOP/s" if v >= 1e3 else f"{v:.2f} GFLOP/s"
+
+
+def format_throughput(items: float, seconds: float, unit: str = "items") -> str:
+    v = items / seconds if seconds > 0 else 0.0
+    for s, f in (("G", 1e9), ("M", 1e6), ("k", 1e3)):
+        if v >= f:
+            return f"{v / f:.2f} {s}{unit}/s"
+    return f"{v:.2f} {unit}/s"
+
+
+def estimate_memory_bandwidth_gbps(nbytes: int = 1 << 28, device=None, iters: int = 5) -> float:
+    """Copy bandwidth (read + write bytes per second) of one device buffer into another."""
+    dev = torch.device(device) if device is not None else torch.device("cuda" if torch.cuda.is_available() else "cpu")
+    a = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    b = torch.empty_like(a)
+    b.copy_(a)
+    if dev.type == "cuda":
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(iters):
+            b.copy_(a)
+        e.record()
+        torch.cuda.synchronize()
+        sec = s.elapsed_time(e) / 1e3
+    else:
+        t0 = time.perf_counter()
+        for _ in range(iters):
+            b.copy_(a)
+        sec = time.perf_counter() - t0
+    return 2.0 * nbytes * iters / sec / 1e9
+
+
+def get_peak_rss_kb() -> int:
+    import resource
+    return int(resource.getrusage(resource.RUSAGE_SELF).ru_maxrss)

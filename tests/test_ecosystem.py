@@ -1380,3 +1380,23 @@ def test_diffusion_model_wrapper_and_helpers():
     out = dm.sample((8, 2), cond=cond[:8], generator=g, num_steps=10)
     assert out.shape == (8, 2) and torch.isfinite(out).all()
     assert D.DiffusionRunner is D.DiffusionModel and D.sinusoidal_timestep_embedding is D.timestep_embedding
+
+
+def test_benchmark_suite_and_timers():
+    import torch
+    from brain_b200.bench import harness as H
+    suite = H.BenchmarkSuite("s")
+    suite.add(H.FnBenchmark.from_fn("matmul_64", lambda: torch.randn(64, 64) @ torch.randn(64, 64), flops=2 * 64 ** 3,
+                                    iters=3, tags=["kernel"]))
+    suite.add(H.FnBenchmark.from_fn("copy", lambda: torch.zeros(1000).clone(), iters=3))
+    res = suite.run_all()
+    assert set(res) == {"matmul_64", "copy"} and len(res["copy"].raw_nanos) == 3
+    assert set(suite.run_filtered(tag="kernel")) == {"matmul_64"} and set(suite.run_filtered("cop")) == {"copy"}
+    t = H.BenchTimer.start_new()
+    assert t.is_running()
+    t.stop()
+    assert not t.is_running() and t.elapsed_nanos() >= 0 and t.elapsed_secs() == t.elapsed_nanos() / 1e9
+    assert H.calibrate_timer_overhead(50) >= 0
+    assert H.format_gflops(2e12, 1.0) == "2.00 TFLOP/s" and H.format_gflops(5e9, 1.0) == "5.00 GFLOP/s"
+    assert H.format_throughput(2.5e6, 1.0, "tok") == "2.50 Mtok/s"
+    assert H.estimate_memory_bandwidth_gbps(1 << 20, "cpu", 2) > 0 and H.get_peak_rss_kb() > 0
