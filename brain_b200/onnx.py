@@ -362,3 +362,120 @@ def check_model(data: bytes) -> list[str]:
         if _decode_value_info(b)[0] not in defined:
             errs.append("graph output never produced")
     return errs
+
+
+# ------------------------------------------------------------------ the reference's ONNX entry points
+# crates/brain-onnx/src: impl_.rs (load_onnx, import_and_optimize), ir2graph.rs / graph2onnx.rs (lowering to
+# and from the graph IR), eval/mod.rs (evaluate_onnx_model), optimize/onnx_passes.rs (fold_constant_nodes,
+# fuse_matmul_add), tools.rs (onnx_summary), model_zoo.rs (create_mlp_zoo_model), utils.rs (varints,
+# little-endian reads, CRC-32), version.rs (default_opset, is_valid_opset).
+DEFAULT_OPSET = 17
+
+
+def default_opset() -> int:
+    return DEFAULT_OPSET
+
+
+def is_valid_opset(v: int) -> bool:
+    return 1 <= int(v) <= 23
+
+
+def encode_varint(v: int) -> bytes:
+    return _varint(v)
+
+
+def decode_varint(b: bytes, pos: int = 0) -> tuple[int, int]:
+    """(value, position after it) of the protobuf varint starting at ``pos``."""
+    out, shift = 0, 0
+    while True:
+        c = b[pos]
+        pos += 1
+        out |= (c & 0x7F) << shift
+        shift += 7
+        if not c & 0x80:
+            return out, pos
+
+
+def read_f32_le(b: bytes, offset: int = 0) -> float:
+    return struct.unpack_from("<f", b, offset)[0]
+
+
+def read_f64_le(b: bytes, offset: int = 0) -> float:
+    return struct.unpack_from("<d", b, offset)[0]
+
+
+def compute_crc32(b: bytes) -> int:
+    import zlib
+    return zlib.crc32(b) & 0xFFFFFFFF
+
+
+def load_onnx(path: str) -> GraphIr:
+    with open(path, "rb") as f:
+        return import_onnx(f.read())
+
+
+lower_to_graph_ir = import_onnx
+
+
+def lower_from_graph_ir(g: GraphIr) -> bytes:
+    return export_onnx(g)
+
+
+def fold_constant_nodes(g: GraphIr) -> bool:
+    from .graph import fold_constants
+    return fold_constants(g)
+
+
+def fuse_matmul_add(g: GraphIr) -> int:
+    """matmul(x, W) followed by add(., b) with a constant 1-D b becomes linear(x, W^T, b). Returns the count."""
+    from .graph import _rename
+    cons = g.consumers()
+    n_f = 0
+    for n in list(g.nodes):
+        if n.op != "matmul" or len(cons.get(n.outputs[0], [])) != 1:
+            continue
+        add = cons[n.outputs[0]][0]
+        if add.op != "add" or n.outputs[0] in g.outputs:
+            continue
+        other = add.inputs[1] if add.inputs[0] == n.outputs[0] else add.inputs[0]
+        w, b = g.values[n.inputs[1]].constant, g.values[other].constant
+        if w is None or b is None or w.dim() != 2 or b.dim() != 1 or b.shape[0] != w.shape[1]:
+            continue
+        wt = g.constant(f"{g.values[n.inputs[1]].name}_t", w.t().contiguous())
+        lin_out = g.add_node("linear", [n.inputs[0], wt, other])
+        lin = g.nodes.pop()  # the node just appended goes where the add was
+        g.nodes.insert(g.nodes.index(add), lin)
+        g.nodes.remove(add)
+        g.nodes.remove(n)
+        _rename(g, add.outputs[0], lin_out)
+        n_f += 1
+    return n_f
+
+
+def import_and_optimize(data: bytes, level: int = 2) -> GraphIr:
+    from .graph import optimize
+    g = import_onnx(data)
+    fuse_matmul_add(g)
+    optimize(g, level)
+    return g
+
+
+def evaluate_onnx_model(data: bytes, inputs) -> list:
+    """Run an ONNX model through the graph interpreter (the framework's kernels for bf16 CUDA inputs)."""
+    from .graph import GraphInterpreter
+    return GraphInterpreter().run(import_onnx(data), list(inputs))
+
+
+def onnx_summary(data: bytes) -> dict:
+    g = import_onnx(data)
+    ops: dict[str, int] = {}
+    for n in g.nodes:
+        ops[n.op] = ops.get(n.op, 0) + 1
+    params = sum(v.constant.numel() for v in g.values.values() if v.constant is not None)
+    return {"name": g.name, "nodes": len(g.nodes), "inputs": len(g.inputs), "outputs": len(g.outputs),
+            "parameters": int(params), "ops": dict(sorted(ops.items())), "problems": check_model(data)}
+
+
+def create_mlp_zoo_model(dims=(4, 8, 2), seed: int = 0) -> bytes:
+    from .graph_tools import build_mlp_graph
+    return export_onnx(build_mlp_graph(list(dims), seed=seed))

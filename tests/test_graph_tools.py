@@ -62,3 +62,38 @@ def test_execution_engine_cuda_graph_replay():
         (ref,) = T.run_graph(g, [x])
         assert torch.allclose(y, ref, atol=1e-5)
     assert eng._graph is not None
+
+
+def test_onnx_entry_points(tmp_path):
+    from brain_b200 import onnx as O
+    data = O.create_mlp_zoo_model((4, 8, 2))
+    summ = O.onnx_summary(data)
+    assert summ["nodes"] == 3 and summ["parameters"] == 4 * 8 + 8 + 8 * 2 + 2 and summ["problems"] == []
+    x = torch.randn(1, 4)
+    ref = T.run_graph(T.build_mlp_graph([4, 8, 2]), [x])[0]
+    assert torch.allclose(O.evaluate_onnx_model(data, [x])[0], ref, atol=1e-6)
+    p = tmp_path / "m.onnx"
+    p.write_bytes(data)
+    assert len(O.load_onnx(str(p)).nodes) == 3
+    # matmul + bias add -> one linear
+    b = T.GraphBuilder("mm")
+    xi = b.input("x", [2, 3])
+    w = b.add_constant("w", torch.randn(3, 5))
+    bias = b.add_constant("b", torch.randn(5))
+    y = b.op("relu", b.op("add", b.op("matmul", xi, w), bias))
+    b.output(y)
+    g = b.build()
+    xin = torch.randn(2, 3)
+    before = T.run_graph(g, [xin])[0]
+    assert O.fuse_matmul_add(g) == 1 and [n.op for n in g.nodes] == ["linear", "relu"]
+    assert torch.allclose(T.run_graph(g, [xin])[0], before, atol=1e-6)
+    assert len(O.import_and_optimize(O.lower_from_graph_ir(g)).nodes) == 2
+    v = 300
+    enc = O.encode_varint(v)
+    assert O.decode_varint(enc) == (300, 2) and O.default_opset() == 17 and O.is_valid_opset(13)
+    assert O.read_f32_le(struct_pack_f(1.5)) == 1.5 and O.compute_crc32(b"123456789") == 0xCBF43926
+
+
+def struct_pack_f(x):
+    import struct
+    return struct.pack("<f", x)
