@@ -308,3 +308,111 @@ class FederatedServer:
         stats = RoundStats(rid, len(clients), sum(r[1] for r in results) / max(1, len(results)), norm)
         self.history.append(stats)
         return stats
+
+
+# ------------------------------------------------------------------ analysis and client helpers
+# crates/brain-federated/src: utils.rs (sample_clients, stddev), ops.rs (l2_norm_delta, scale_delta),
+# transform.rs (polyak_average, normalize_weights), analyze.rs (cosine_similarity_deltas,
+# communication_cost_bytes, estimate_heterogeneity), monitor/mod.rs (FedMonitor: latest_loss,
+# has_converged), process.rs (cosine_lr), client/trainer.rs (LocalTrainer / SgdTrainer).
+
+def sample_clients(num_clients: int, fraction: float, round_idx: int, seed: int = 0, min_clients: int = 1) -> list[int]:
+    """A seeded, round-dependent subset of max(min_clients, round(fraction * N)) client ids, sorted."""
+    k = max(min_clients, int(round(fraction * num_clients)))
+    g = torch.Generator().manual_seed(seed * 1_000_003 + round_idx)
+    return sorted(torch.randperm(num_clients, generator=g)[:k].tolist())
+
+
+def _flat(delta) -> torch.Tensor:
+    ts = delta.tensors if hasattr(delta, "tensors") else delta
+    return torch.cat([t.reshape(-1).double() for t in ts])
+
+
+def l2_norm_delta(delta) -> float:
+    return float(_flat(delta).norm())
+
+
+def scale_delta(delta, s: float) -> list[torch.Tensor]:
+    ts = delta.tensors if hasattr(delta, "tensors") else delta
+    return [t * s for t in ts]
+
+
+def cosine_similarity_deltas(a, b) -> float:
+    fa, fb = _flat(a), _flat(b)
+    d = fa.norm() * fb.norm()
+    return float(fa @ fb / d) if d > 0 else 0.0
+
+
+def estimate_heterogeneity(deltas) -> float:
+    """1 - mean pairwise cosine similarity of the client updates (0: identical directions)."""
+    n = len(deltas)
+    if n < 2:
+        return 0.0
+    sims = [cosine_similarity_deltas(deltas[i], deltas[j]) for i in range(n) for j in range(i + 1, n)]
+    return 1.0 - sum(sims) / len(sims)
+
+
+def communication_cost_bytes(num_params: int, num_clients: int, rounds: int, bytes_per_param: float = 4.0,
+                             bidirectional: bool = True) -> int:
+    return int(num_params * bytes_per_param * num_clients * rounds * (2 if bidirectional else 1))
+
+
+def polyak_average(avg: list[torch.Tensor], new: list[torch.Tensor], beta: float = 0.99) -> list[torch.Tensor]:
+    return [beta * a + (1 - beta) * n for a, n in zip(avg, new)]
+
+
+def normalize_weights(weights) -> list[float]:
+    s = float(sum(weights))
+    return [float(w) / s for w in weights] if s > 0 else [1.0 / len(weights)] * len(weights)
+
+
+def stddev(values) -> float:
+    v = torch.as_tensor(list(values), dtype=torch.float64)
+    return float(v.std(unbiased=False)) if v.numel() else 0.0
+
+
+def cosine_lr(base_lr: float, round_idx: int, total_rounds: int, min_lr: float = 0.0) -> float:
+    import math
+    t = min(max(round_idx / max(total_rounds, 1), 0.0), 1.0)
+    return min_lr + 0.5 * (base_lr - min_lr) * (1 + math.cos(math.pi * t))
+
+
+class FedMonitor:
+    """Per-round global losses; converged when the last ``window`` rounds improved by less than ``tol``."""
+
+    def __init__(self, window: int = 3, tol: float = 1e-4):
+        self.window, self.tol, self.losses = window, tol, []
+
+    def record(self, loss: float) -> None:
+        self.losses.append(float(loss))
+
+    def latest_loss(self):
+        return self.losses[-1] if self.losses else None
+
+    def has_converged(self) -> bool:
+        if len(self.losses) <= self.window:
+            return False
+        return self.losses[-self.window - 1] - min(self.losses[-self.window:]) < self.tol
+
+
+class LocalTrainer:
+    """Local SGD epochs of a client on its data: returns the parameter delta (new - old) and sample count."""
+
+    def __init__(self, model, loss_fn, lr: float = 0.01, epochs: int = 1, weight_decay: float = 0.0):
+        self.model, self.loss_fn, self.lr, self.epochs, self.wd = model, loss_fn, lr, epochs, weight_decay
+
+    def train(self, batches):
+        params = [p for p in self.model.parameters() if p.requires_grad]
+        before = [p.detach().clone() for p in params]
+        opt = torch.optim.SGD(params, lr=self.lr, weight_decay=self.wd)
+        n = 0
+        for _ in range(self.epochs):
+            for x, y in batches:
+                opt.zero_grad()
+                self.loss_fn(self.model(x), y).backward()
+                opt.step()
+                n += x.shape[0]
+        return [p.detach() - b for p, b in zip(params, before)], n // max(self.epochs, 1)
+
+
+SgdTrainer = LocalTrainer

@@ -279,3 +279,31 @@ def dice_loss(logits, target, eps=1.0):
     inter = (p * t).sum((0, 2, 3))
     den = p.sum((0, 2, 3)) + t.sum((0, 2, 3))
     return 1 - ((2 * inter + eps) / (den + eps)).mean()
+
+
+# ------------------------------------------------------------------ the reference's names
+# crates/brain-cv/src: conv/{depthwise,grouped,ghost,ws}.rs, detection/{nms,roi_align}.rs, augmentation/mix.rs.
+DepthwiseSeparableConv2d = DepthwiseSeparableConv
+GroupedConv2d = GroupedConv
+GhostModule = GhostConv
+Conv2dWS = WSConv2d
+non_max_suppression = nms
+
+
+class RoIAlign(Module):
+    """Module form of ``roi_align``: (feat [C, H, W], boxes [K, 4] xyxy) -> [K, C, S, S]."""
+
+    def __init__(self, output_size: int = 7, spatial_scale: float = 1.0):
+        super().__init__()
+        self.output_size, self.spatial_scale = output_size, spatial_scale
+
+    def forward(self, feat, boxes):
+        return roi_align(feat, boxes, self.output_size, self.spatial_scale)
+
+
+def sample_cutmix_box(H: int, W: int, lam: float, generator=None):
+    """(y0, y1, x0, x1) of a box covering (1 - lam) of an H x W image, centred uniformly at random."""
+    rh, rw = int(H * (1 - lam) ** 0.5), int(W * (1 - lam) ** 0.5)
+    cy = int(torch.randint(0, H, (1,), generator=generator))
+    cx = int(torch.randint(0, W, (1,), generator=generator))
+    return max(cy - rh // 2, 0), min(cy + rh // 2, H), max(cx - rw // 2, 0), min(cx + rw // 2, W)

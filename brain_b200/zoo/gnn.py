@@ -208,3 +208,80 @@ def jumping_knowledge(layer_outputs, mode: str = "cat"):
         return torch.cat(layer_outputs, -1)
     st = torch.stack(layer_outputs)
     return st.max(0).values if mode == "max" else st.mean(0)
+
+
+# ------------------------------------------------------------------ the reference's names
+# crates/brain-gnn/src: models/{mod,gin_model}.rs (GcnModel, SageModel, GatModel, GinModel with forward_node /
+# forward_graph / embed_nodes), ops.rs (aggregate_sum, aggregate_max), datasets/loader.rs (GraphLoader,
+# GraphBatch), readout/jumping.rs (JkMode).
+aggregate_sum = scatter_sum
+aggregate_max = scatter_max
+
+
+class _GnnModel(GnnNodeClassifier):
+    LAYER = "gcn"
+
+    def __init__(self, in_dim: int, hidden: int, num_classes: int, **kw):
+        super().__init__(in_dim, hidden, num_classes, layer=self.LAYER, **kw)
+
+    def forward_node(self, g: Graph, x):
+        """Per-node logits."""
+        return self.forward(g, x)
+
+    def embed_nodes(self, g: Graph, x):
+        """Hidden node embeddings after the first layer."""
+        return torch.relu(self.l1(g, x))
+
+    def forward_graph(self, g: Graph, x, batch=None, pool: str = "mean"):
+        """Graph-level logits: node logits pooled per graph (``batch`` maps nodes to graphs)."""
+        h = self.forward(g, x)
+        if batch is None:
+            batch = torch.zeros(h.shape[0], dtype=torch.long, device=h.device)
+        n = int(batch.max()) + 1 if batch.numel() else 0
+        return {"mean": global_mean_pool, "add": global_add_pool, "max": global_max_pool}[pool](h, batch, n)
+
+
+class GcnModel(_GnnModel):
+    LAYER = "gcn"
+
+
+class SageModel(_GnnModel):
+    LAYER = "sage"
+
+
+class GatModel(_GnnModel):
+    LAYER = "gat"
+
+
+class GinModel(_GnnModel):
+    LAYER = "gin"
+
+
+class JkMode:
+    CONCAT, MAX, LAST = "cat", "max", "last"
+
+
+class GraphLoader:
+    """Mini-batches of small graphs, a list of (Graph, node features x, label y): each batch is
+    (BatchGraph of the disjoint union, concatenated x, stacked y)."""
+
+    def __init__(self, graphs, batch_size: int, shuffle: bool = False, seed: int = 0):
+        self.graphs, self.bs, self.shuffle, self.seed, self.epoch = list(graphs), batch_size, shuffle, seed, 0
+
+    def num_batches(self) -> int:
+        return -(-len(self.graphs) // self.bs)
+
+    def get_batch(self, i: int, order=None):
+        from .gnn_extras import collate_graphs
+        order = order if order is not None else list(range(len(self.graphs)))
+        items = [self.graphs[j] for j in order[i * self.bs:(i + 1) * self.bs]]
+        bg = collate_graphs([it[0] for it in items])
+        return bg, torch.cat([it[1] for it in items]), torch.stack([torch.as_tensor(it[2]) for it in items])
+
+    def __iter__(self):
+        order = list(range(len(self.graphs)))
+        if self.shuffle:
+            order = torch.randperm(len(order), generator=torch.Generator().manual_seed(self.seed + self.epoch)).tolist()
+        self.epoch += 1
+        for i in range(self.num_batches()):
+            yield self.get_batch(i, order)

@@ -1,0 +1,56 @@
+"""Reference-named CV, GNN and federated helpers."""
+import pytest
+import torch
+
+
+def test_cv_names():
+    from brain_b200.zoo import cv as CV
+    assert CV.GhostModule is CV.GhostConv and CV.non_max_suppression is CV.nms
+    feat = torch.randn(3, 16, 16)
+    boxes = torch.tensor([[0.0, 0.0, 8.0, 8.0]])
+    assert torch.allclose(CV.RoIAlign(4)(feat, boxes), CV.roi_align(feat, boxes, 4))
+    y0, y1, x0, x1 = CV.sample_cutmix_box(32, 32, 0.75, torch.Generator().manual_seed(0))
+    assert 0 <= y0 <= y1 <= 32 and 0 <= x0 <= x1 <= 32 and (y1 - y0) <= 16 and (x1 - x0) <= 16
+
+
+def test_gnn_models_and_loader():
+    from brain_b200.zoo import gnn as GN
+    torch.manual_seed(0)
+    g = GN.Graph.from_undirected([(0, 1), (1, 2), (2, 3)], 4)
+    x = torch.randn(4, 5)
+    for cls in (GN.GcnModel, GN.SageModel, GN.GinModel, GN.GatModel):
+        m = cls(5, 8, 3)
+        assert m.forward_node(g, x).shape == (4, 3) and m.forward_graph(g, x).shape == (1, 3)
+        assert m.embed_nodes(g, x).shape[0] == 4
+    data = [(GN.Graph.from_undirected([(0, 1)], 2), torch.randn(2, 5), k % 2) for k in range(5)]
+    ld = GN.GraphLoader(data, batch_size=2)
+    batches = list(ld)
+    assert ld.num_batches() == 3 and len(batches) == 3
+    bg, xb, yb = batches[0]
+    assert bg.num_graphs == 2 and xb.shape == (4, 5) and yb.tolist() == [0, 1] and bg.graph.num_nodes == 4
+    out = GN.GcnModel(5, 8, 2).forward_graph(bg.graph, xb, bg.batch, pool="add")
+    assert out.shape == (2, 2)
+    assert GN.aggregate_sum is GN.scatter_sum
+
+
+def test_federated_helpers():
+    from brain_b200 import federated as F
+    s = F.sample_clients(100, 0.1, round_idx=3, seed=1)
+    assert len(s) == 10 and s == F.sample_clients(100, 0.1, 3, 1) and s != F.sample_clients(100, 0.1, 4, 1)
+    a, b = [torch.tensor([3.0, 4.0])], [torch.tensor([-3.0, -4.0])]
+    assert F.l2_norm_delta(a) == 5.0 and F.cosine_similarity_deltas(a, b) == pytest.approx(-1.0)
+    assert F.estimate_heterogeneity([a, a]) == pytest.approx(0.0) and F.estimate_heterogeneity([a, b]) == pytest.approx(2.0)
+    assert F.scale_delta(a, 2)[0].tolist() == [6.0, 8.0]
+    assert F.communication_cost_bytes(1000, 10, 5) == 1000 * 4 * 10 * 5 * 2
+    assert F.polyak_average([torch.zeros(1)], [torch.ones(1)], 0.9)[0].item() == pytest.approx(0.1)
+    assert F.normalize_weights([1, 3]) == [0.25, 0.75] and F.stddev([1, 3]) == 1.0
+    assert F.cosine_lr(0.1, 0, 10) == pytest.approx(0.1) and F.cosine_lr(0.1, 10, 10) == pytest.approx(0.0)
+    mon = F.FedMonitor(window=2, tol=1e-3)
+    for l in (1.0, 0.5, 0.49999, 0.49998):
+        mon.record(l)
+    assert mon.latest_loss() == 0.49998 and mon.has_converged()
+    model = torch.nn.Linear(2, 1)
+    tr = F.LocalTrainer(model, torch.nn.functional.mse_loss, lr=0.1, epochs=2)
+    xs = torch.randn(8, 2)
+    delta, n = tr.train([(xs, xs.sum(1, keepdim=True))])
+    assert n == 8 and len(delta) == 2 and F.l2_norm_delta(delta) > 0
