@@ -491,3 +491,115 @@ class BatchedDqnTrainer:
         if self.steps % self.tu == 0:
             self.q_t.load_state_dict(self.q.state_dict())
         return float(loss.detach())
+
+
+# ------------------------------------------------------------------ the reference's names
+# crates/brain-rl/src: env/{gym,atari_lite,mujoco_lite,wrappers,vector}.rs, dqn/dueling.rs,
+# actor_critic/mod.rs (ActorCriticNet, compute_gae), policy/mod.rs (EpsilonSchedule, EpsilonGreedyPolicy),
+# value/mod.rs (soft_update_target, VTable / update_td), buffer/prioritized.rs (SumTree), agents/mod.rs (make_agent).
+from . import rl as _rl, rl_envs as _envs  # noqa: E402
+
+CartPoleEnv = _envs.CartPole
+MountainCarEnv = _envs.MountainCar
+PendulumEnv = _envs.Pendulum
+PongLiteEnv = _envs.PongLite
+BreakoutLiteEnv = _envs.BreakoutLite
+HalfCheetahLiteEnv = _envs.HalfCheetahLite
+ReacherLiteEnv = _envs.ReacherLite
+FrameStackWrapper = _envs.FrameStack
+TimeLimitWrapper = _envs.TimeLimit
+RewardScaleWrapper = _envs.RewardScale
+DummyVecEnv = _rl.VectorEnv
+ActorCriticNet = _rl.ActorCritic
+compute_gae = _rl.gae
+
+
+class EpsilonSchedule:
+    """Linear decay from ``start`` to ``end`` over ``decay_steps``, then constant."""
+
+    def __init__(self, start: float = 1.0, end: float = 0.05, decay_steps: int = 10000):
+        self.start, self.end, self.decay = start, end, max(1, decay_steps)
+
+    def get_epsilon(self, step: int) -> float:
+        f = min(step / self.decay, 1.0)
+        return self.start + f * (self.end - self.start)
+
+
+class EpsilonGreedyPolicy:
+    """Batched epsilon-greedy: random actions where a uniform draw is below epsilon, argmax elsewhere."""
+
+    def __init__(self, schedule: EpsilonSchedule, num_actions: int, seed: int = 0):
+        self.schedule, self.n = schedule, num_actions
+        self.g = torch.Generator().manual_seed(seed)
+
+    def select_action(self, q_values: torch.Tensor, step: int) -> torch.Tensor:
+        eps = self.schedule.get_epsilon(step)
+        greedy = q_values.argmax(-1)
+        rnd = torch.randint(0, self.n, greedy.shape, generator=self.g).to(greedy.device)
+        explore = (torch.rand(greedy.shape, generator=self.g) < eps).to(greedy.device)
+        return torch.where(explore, rnd, greedy)
+
+
+def soft_update_target(target: torch.nn.Module, source: torch.nn.Module, tau: float = 0.005) -> None:
+    """theta_target <- tau theta + (1 - tau) theta_target (Polyak)."""
+    with torch.no_grad():
+        for t, s in zip(target.parameters(), source.parameters()):
+            t.lerp_(s, tau)
+
+
+class VTable:
+    """Tabular state values with TD(0) updates."""
+
+    def __init__(self, num_states: int, gamma: float = 0.99, lr: float = 0.1):
+        self.v, self.gamma, self.lr = torch.zeros(num_states, dtype=torch.float64), gamma, lr
+
+    def update_td(self, s: int, r: float, s_next: int, done: bool) -> float:
+        target = r + (0.0 if done else self.gamma * float(self.v[s_next]))
+        err = target - float(self.v[s])
+        self.v[s] += self.lr * err
+        return err
+
+
+class SumTree:
+    """Binary sum tree over ``capacity`` priorities: O(log n) update and prefix-sum sampling."""
+
+    def __init__(self, capacity: int):
+        self.cap = 1
+        while self.cap < capacity:
+            self.cap *= 2
+        self.tree = [0.0] * (2 * self.cap)
+
+    def update(self, idx: int, priority: float) -> None:
+        i = idx + self.cap
+        self.tree[i] = float(priority)
+        i //= 2
+        while i:
+            self.tree[i] = self.tree[2 * i] + self.tree[2 * i + 1]
+            i //= 2
+
+    def total_priority(self) -> float:
+        return self.tree[1]
+
+    def get_leaf(self, value: float) -> tuple[int, float]:
+        """(index, priority) of the leaf whose prefix-sum interval contains ``value``."""
+        i = 1
+        while i < self.cap:
+            left = self.tree[2 * i]
+            if value < left:
+                i = 2 * i
+            else:
+                value -= left
+                i = 2 * i + 1
+        return i - self.cap, self.tree[i]
+
+
+def make_agent(kind: str, obs_dim: int, num_actions: int, **kw):
+    """Construct an agent by name: dqn, double_dqn, rainbow, a2c, ppo, sac."""
+    table = {"dqn": (_rl.DqnAgent, _rl.DqnConfig), "double_dqn": (DoubleDqnAgent, _rl.DqnConfig),
+             "rainbow": (RainbowAgent, _rl.DqnConfig), "a2c": (_rl.A2cAgent, _rl.A2cConfig),
+             "ppo": (_rl.PpoAgent, _rl.PpoConfig), "sac": (_rl.SacAgent, _rl.SacConfig)}
+    if kind not in table:
+        raise ValueError(f"unknown agent {kind!r}")
+    seed = kw.pop("seed", 0)
+    cls, cfg = table[kind]
+    return cls(obs_dim, num_actions, cfg(**kw), seed=seed)

@@ -54,3 +54,28 @@ def test_federated_helpers():
     xs = torch.randn(8, 2)
     delta, n = tr.train([(xs, xs.sum(1, keepdim=True))])
     assert n == 8 and len(delta) == 2 and F.l2_norm_delta(delta) > 0
+
+
+def test_rl_names():
+    from brain_b200.zoo import rl_agents as RA, rl as RL
+    sch = RA.EpsilonSchedule(1.0, 0.1, 100)
+    assert sch.get_epsilon(0) == 1.0 and sch.get_epsilon(50) == pytest.approx(0.55) and sch.get_epsilon(500) == pytest.approx(0.1)
+    pol = RA.EpsilonGreedyPolicy(RA.EpsilonSchedule(0.0, 0.0, 1), 4)
+    assert pol.select_action(torch.tensor([[0.0, 3.0, 1.0, 2.0]]), 10).tolist() == [1]
+    tgt, src = torch.nn.Linear(2, 2), torch.nn.Linear(2, 2)
+    before = tgt.weight.detach().clone()
+    RA.soft_update_target(tgt, src, 0.5)
+    assert torch.allclose(tgt.weight, 0.5 * before + 0.5 * src.weight)
+    vt = RA.VTable(3, gamma=0.5, lr=1.0)
+    vt.v[2] = 4.0
+    assert vt.update_td(0, 1.0, 2, False) == 3.0 and float(vt.v[0]) == 3.0
+    st = RA.SumTree(5)
+    for i, p in enumerate([1.0, 2.0, 3.0, 4.0, 0.5]):
+        st.update(i, p)
+    assert st.total_priority() == 10.5
+    assert st.get_leaf(0.5)[0] == 0 and st.get_leaf(1.5)[0] == 1 and st.get_leaf(6.2)[0] == 3 and st.get_leaf(10.2)[0] == 4
+    ag = RA.make_agent("dqn", 4, 2)
+    assert isinstance(ag, RL.DqnAgent) and isinstance(RA.make_agent("ppo", 4, 2), RL.PpoAgent)
+    with pytest.raises(ValueError):
+        RA.make_agent("nope", 4, 2)
+    assert RA.compute_gae is RL.gae and RA.CartPoleEnv is RA._envs.CartPole
