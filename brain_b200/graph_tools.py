@@ -293,6 +293,10 @@ class ExecutionEngine:
         self._static_out = None
 
     def _capture(self, inputs):
+        dev = inputs[0].device
+        for v in self.g.values.values():  # constants live on the device, so the capture copies nothing from the host
+            if v.constant is not None and v.constant.device != dev:
+                v.constant = v.constant.to(dev)
         self._static_in = [x.clone() for x in inputs]
         interp = GraphInterpreter()
         side = torch.cuda.Stream()
