@@ -115,6 +115,11 @@ def main(argv=None) -> int:
     ms = timed(lambda: fp8_gemm_rs(tp, x8, w8q, w8s, T))
     report("fp8_linear_gemm_rs", ms, (W - 1) * T * d * 2, M=T * W, N=d, K=kr,
            tflops_per_rank=round(flops / (ms / 1e3) / 1e12, 1))
+    from ..quantization.fp8 import quantize_fp8_rowwise
+    w8rq, w8rs = quantize_fp8_rowwise(w8)
+    ms_rw = timed(lambda: fp8_gemm_rs(tp, x8, w8rq, w8rs, T, scaling="rowwise"))
+    report("fp8_rowwise_linear_gemm_rs", ms_rw, (W - 1) * T * d * 2, M=T * W, N=d, K=kr,
+           tflops_per_rank=round(flops / (ms_rw / 1e3) / 1e12, 1))
     ms_bf = timed(lambda: gemm_push(tp, x8, w8, 1, T))
     report("bf16_linear_gemm_rs", ms_bf, (W - 1) * T * d * 2, M=T * W, N=d, K=kr,
            tflops_per_rank=round(flops / (ms_bf / 1e3) / 1e12, 1))

@@ -142,22 +142,39 @@ def gemm_push(ctx: TPContext, a: torch.Tensor, w: torch.Tensor, mode: int, rows_
 
 
 def fp8_gemm_rs(ctx: TPContext, x_local: torch.Tensor, wq: torch.Tensor, ws: torch.Tensor,
-                rows_per_rank: int) -> torch.Tensor:
+                rows_per_rank: int, scaling: str = "block") -> torch.Tensor:
     """Row-parallel block-scaled fp8 Linear with reduce-scatter: x_local [M, K/W] (bf16, this rank's
     input columns) is quantised 1 x 128 on the fly, multiplied by this rank's pre-quantised weight
     shard wq [N, K/W] (128 x 128 scales ws) on the tcgen05 fp8 kernel straight into symmetric memory,
     and after a peer barrier each rank pulls and sums its rows [rank * rows_per_rank, ...) from all
-    ranks' products with coalesced NVLink loads. Returns [rows_per_rank, N] bf16."""
-    from ..quantization.fp8 import quantize_fp8_blockwise
+    ranks' products with coalesced NVLink loads. Returns [rows_per_rank, N] bf16.
+
+    ``scaling="rowwise"``: x_local is quantised per token and wq carries one scale per output channel
+    (``quantize_fp8_rowwise`` of this rank's weight columns); the product then runs on the CTA-pair
+    ``kind::f8f6f4`` kernel with the scales applied in its epilogue."""
+    from ..quantization.fp8 import quantize_fp8_blockwise, quantize_fp8_rowwise
     M = x_local.shape[0]
     N = wq.shape[0]
     W = ctx.world
     same_device(x_local, wq, ws)
-    xq, sx = quantize_fp8_blockwise(x_local)
     par = ctx.next_parity()
     full = ctx.symm("rs_full", M * N * 2, par)
-    _native.call("brain_fp8_gemm", xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), sx.data_ptr(),
-                 ws.data_ptr(), full.local, N, None, 0, M, N, xq.shape[1], _stream())
+    if scaling == "rowwise":
+        if N % 8:
+            raise ValueError("row-wise fp8 GEMM -> RS needs N % 8 == 0")
+        xq, sx = quantize_fp8_rowwise(x_local)
+        wsf = ws.float().contiguous()
+        args = (xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), sx.data_ptr(), wsf.data_ptr(),
+                full.local, N, None, 0, M, N, xq.shape[1], _stream())
+        rc = _native.fn("brain_fp8_gemm_rowwise_pair")(*args)
+        if rc == 801:  # cudaErrorNotSupported: M or N below the pair tile, the single-CTA kernel runs
+            rc = _native.fn("brain_fp8_gemm_rowwise")(*args)
+        if rc:
+            raise _native.NativeError(f"row-wise fp8 GEMM failed with status {rc}")
+    else:
+        xq, sx = quantize_fp8_blockwise(x_local)
+        _native.call("brain_fp8_gemm", xq.data_ptr(), xq.stride(0), wq.data_ptr(), wq.stride(0), sx.data_ptr(),
+                     ws.data_ptr(), full.local, N, None, 0, M, N, xq.shape[1], _stream())
     ctx.comm.barrier(41)
     slot = rows_per_rank * N
     out = torch.empty(rows_per_rank, N, device=x_local.device, dtype=torch.bfloat16)

@@ -104,6 +104,42 @@ def _fp8_rs_worker(rank, world):
     return err, scale
 
 
+def _fp8_rs_rowwise_worker(rank, world):
+    from brain_b200.parallel import dist as bdist
+    from brain_b200.parallel.tensor_parallel import TPContext, fp8_gemm_rs
+    from brain_b200.quantization.fp8 import quantize_fp8_rowwise
+    bdist.init(timeout_s=60)
+    ctx = TPContext()
+    g = torch.Generator(device="cuda").manual_seed(9)
+    T, K, N = 384, 1024, 512  # M = T * world >= 256: the CTA-pair kernel
+    x_full = torch.randn(T * world, K, device="cuda", generator=g).bfloat16()
+    w_full = (torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16()
+    kr = K // world
+    x_local = x_full[:, rank * kr:(rank + 1) * kr].contiguous()
+    wq, ws = quantize_fp8_rowwise(w_full[:, rank * kr:(rank + 1) * kr].contiguous())
+    y = fp8_gemm_rs(ctx, x_local, wq, ws, T, scaling="rowwise")
+    ref = torch.zeros(T * world, N, device="cuda")
+    for r in range(world):
+        xq, sx = quantize_fp8_rowwise(x_full[:, r * kr:(r + 1) * kr].contiguous())
+        wq_r, ws_r = quantize_fp8_rowwise(w_full[:, r * kr:(r + 1) * kr].contiguous())
+        ref += (xq.float() * sx[:, None]) @ (wq_r.float() * ws_r[:, None]).t()
+    err = float((y.float() - ref[rank * T:(rank + 1) * T]).abs().max())
+    scale = float(ref.abs().max())
+    ctx.comm.check()
+    ctx.close()
+    ctx.comm.close()
+    bdist.shutdown()
+    return err, scale
+
+
+@pytest.mark.gpu
+@pytest.mark.multigpu
+def test_fp8_rowwise_row_parallel_gemm_reduce_scatter():
+    outs = run_ranks(_fp8_rs_rowwise_worker, 2, env={"NCCL_NVLS_ENABLE": "0"})
+    for err, scale in outs:
+        assert err < 2e-2 * max(1.0, scale), (err, scale)
+
+
 @pytest.mark.gpu
 @pytest.mark.multigpu
 def test_fp8_row_parallel_gemm_reduce_scatter():
