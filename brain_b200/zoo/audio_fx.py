@@ -545,3 +545,164 @@ def trim_silence(signal: torch.Tensor, threshold_db: float = -40.0, frame_size: 
         e -= 1
     a, b = s * hop_size, min(e * hop_size + frame_size, n)
     return x.clone() if a >= b else x[..., a:b].clone()
+
+
+# ------------------------------------------------------------------ the reference's remaining names
+# crates/brain-audio/src: features.rs (amplitude/power <-> dB), window.rs (Bartlett, Blackman), scales.rs
+# (ERB), analysis.rs (Hilbert envelope, real cepstrum), vocoder.rs (PhaseVocoder), distance.rs
+# (vector_distance with a DistanceMetric), config.rs (MelConfig presets default_speech / default_music),
+# util.rs (samples_from_duration, ensure_length, nyquist_hz, fft_freqs), preprocess.rs (de_emphasis).
+
+def amplitude_to_db(x: torch.Tensor, amin: float = 1e-10, top_db: float | None = None) -> torch.Tensor:
+    d = 20.0 * torch.log10(x.abs().clamp_min(amin))
+    return torch.maximum(d, d.max() - top_db) if top_db is not None else d
+
+
+def power_to_db(x: torch.Tensor, amin: float = 1e-10, top_db: float | None = None) -> torch.Tensor:
+    d = 10.0 * torch.log10(x.clamp_min(amin))
+    return torch.maximum(d, d.max() - top_db) if top_db is not None else d
+
+
+def db_to_amplitude(d: torch.Tensor) -> torch.Tensor:
+    return torch.pow(10.0, d / 20.0)
+
+
+def db_to_power(d: torch.Tensor) -> torch.Tensor:
+    return torch.pow(10.0, d / 10.0)
+
+
+def bartlett_window(n: int, periodic: bool = True, dtype=torch.float32) -> torch.Tensor:
+    return torch.bartlett_window(n, periodic=periodic, dtype=dtype)
+
+
+def blackman_window(n: int, periodic: bool = True, dtype=torch.float32) -> torch.Tensor:
+    return torch.blackman_window(n, periodic=periodic, dtype=dtype)
+
+
+def hz_to_erb(f):
+    """Glasberg & Moore (1990) ERB-rate scale: 21.4 log10(1 + 0.00437 f)."""
+    f = torch.as_tensor(f, dtype=torch.float64)
+    return 21.4 * torch.log10(1.0 + 0.00437 * f)
+
+
+def erb_to_hz(e):
+    e = torch.as_tensor(e, dtype=torch.float64)
+    return (torch.pow(10.0, e / 21.4) - 1.0) / 0.00437
+
+
+def hilbert_envelope(x: torch.Tensor) -> torch.Tensor:
+    """|analytic signal| along the last axis (FFT, doubled positive frequencies, zeroed negative ones)."""
+    n = x.shape[-1]
+    X = torch.fft.fft(x.double(), dim=-1)
+    h = torch.zeros(n, dtype=torch.float64, device=x.device)
+    h[0] = 1.0
+    if n % 2 == 0:
+        h[n // 2] = 1.0
+        h[1:n // 2] = 2.0
+    else:
+        h[1:(n + 1) // 2] = 2.0
+    return torch.fft.ifft(X * h, dim=-1).abs().to(x.dtype)
+
+
+def real_cepstrum(x: torch.Tensor, eps: float = 1e-12) -> torch.Tensor:
+    return torch.fft.ifft(torch.log(torch.fft.fft(x.double(), dim=-1).abs().clamp_min(eps)), dim=-1).real.to(x.dtype)
+
+
+def de_emphasis(x: torch.Tensor, coef: float = 0.97) -> torch.Tensor:
+    """Inverse of pre-emphasis: y[n] = x[n] + coef y[n-1]."""
+    y = torch.empty_like(x)
+    acc = torch.zeros_like(x[..., 0])
+    for i in range(x.shape[-1]):
+        acc = x[..., i] + coef * acc
+        y[..., i] = acc
+    return y
+
+
+def samples_from_duration(seconds: float, sample_rate: int) -> int:
+    return int(round(seconds * sample_rate))
+
+
+def nyquist_hz(sample_rate: int) -> float:
+    return sample_rate / 2.0
+
+
+def fft_freqs(n_fft: int, sample_rate: int) -> torch.Tensor:
+    return torch.fft.rfftfreq(n_fft, 1.0 / sample_rate)
+
+
+def ensure_length(x: torch.Tensor, n: int) -> torch.Tensor:
+    """Zero-pad or cut the last axis to n samples."""
+    if x.shape[-1] >= n:
+        return x[..., :n]
+    return torch.nn.functional.pad(x, (0, n - x.shape[-1]))
+
+
+class DistanceMetric:
+    EUCLIDEAN, COSINE, MANHATTAN = "euclidean", "cosine", "manhattan"
+
+
+def vector_distance(a: torch.Tensor, b: torch.Tensor, metric: str = "euclidean") -> float:
+    a, b = a.double().reshape(-1), b.double().reshape(-1)
+    if metric == "euclidean":
+        return float((a - b).norm())
+    if metric == "manhattan":
+        return float((a - b).abs().sum())
+    if metric == "cosine":
+        d = a.norm() * b.norm()
+        return float(1.0 - a @ b / d) if d > 0 else 1.0
+    raise ValueError(f"unknown distance {metric!r}")
+
+
+class PhaseVocoder:
+    """Time-scale modification in the STFT domain (Flanagan & Golden; Laroche & Dolson phase propagation):
+    frames are read at ``rate`` times the hop, magnitudes interpolated and phases advanced by the
+    measured instantaneous frequency."""
+
+    def __init__(self, n_fft: int = 1024, hop: int = 256):
+        self.n_fft, self.hop = n_fft, hop
+
+    def stretch(self, x: torch.Tensor, rate: float) -> torch.Tensor:
+        win = torch.hann_window(self.n_fft, dtype=torch.float64)
+        S = torch.stft(x.double(), self.n_fft, self.hop, window=win, return_complex=True)  # [F, T]
+        F_, T = S.shape
+        steps = torch.arange(0, T - 1, rate, dtype=torch.float64)
+        omega = torch.linspace(0, torch.pi * self.hop, F_, dtype=torch.float64)
+        phase = torch.angle(S[:, 0])
+        out = torch.empty(F_, len(steps), dtype=torch.complex128)
+        for k, t in enumerate(steps):
+            i = int(t)
+            frac = float(t - i)
+            a, b = S[:, i], S[:, i + 1]
+            mag = (1 - frac) * a.abs() + frac * b.abs()
+            out[:, k] = torch.polar(mag, phase)
+            dphi = torch.angle(b) - torch.angle(a) - omega
+            dphi = dphi - 2 * torch.pi * torch.round(dphi / (2 * torch.pi))
+            phase = phase + omega + dphi
+        y = torch.istft(out, self.n_fft, self.hop, window=win, length=int(round(x.shape[-1] / rate)))
+        return y.to(x.dtype)
+
+
+@dataclass
+class MelConfig:
+    sample_rate: int = 16000
+    n_fft: int = 400
+    hop_length: int = 160
+    n_mels: int = 80
+    f_min: float = 0.0
+    f_max: float | None = None
+
+    @classmethod
+    def default_speech(cls) -> "MelConfig":
+        return cls(16000, 400, 160, 80)
+
+    @classmethod
+    def default_speech_80(cls) -> "MelConfig":
+        return cls.default_speech()
+
+    @classmethod
+    def default_music(cls) -> "MelConfig":
+        return cls(22050, 2048, 512, 128)
+
+    @classmethod
+    def default_music_128(cls) -> "MelConfig":
+        return cls.default_music()
