@@ -285,3 +285,143 @@ def convert_safetensors_to_bn(st_path: str, bn_path: str, name: str = "model") -
         m.add_tensor(k, t)
     m.save_file(bn_path)
     return ConversionReport(len(tensors), "safetensors", "bn")
+
+
+# ------------------------------------------------------------------ exporter objects and the builder
+# crates/brain-export/src: onnx/mod.rs, tflite/mod.rs, coreml/mod.rs, webnn/mod.rs (one exporter per
+# format), builder.rs (ExportBuilder), model/mod.rs (ModelExporter), ops.rs (is_op_supported),
+# common/dtype_map.rs (map_dtype_to_onnx / map_dtype_to_tflite), name_gen.rs (sanitize_name),
+# utils.rs (align4, encode_uleb128), safetensors.rs (SafetensorsArchive).
+
+class _Exporter:
+    FORMAT: ExportFormat
+
+    def export(self, g: GraphIr):
+        raise NotImplementedError
+
+    def save(self, g: GraphIr, path: str) -> str:
+        data = self.export(g)
+        mode = "wb" if isinstance(data, (bytes, bytearray)) else "w"
+        with open(path, mode) as f:
+            f.write(data)
+        return path
+
+    def supports(self, g: GraphIr) -> bool:
+        return all(n.op in OP_TABLES[self.FORMAT] for n in g.nodes)
+
+
+class OnnxExporter(_Exporter):
+    FORMAT = ExportFormat.ONNX
+
+    def export(self, g):
+        return _onnx.export_onnx(g)
+
+    def supports(self, g):
+        return True
+
+
+class TfliteExporter(_Exporter):
+    FORMAT = ExportFormat.TFLITE
+
+    def export(self, g):
+        return export_tflite_json(g)
+
+
+class CoreMlExporter(_Exporter):
+    FORMAT = ExportFormat.COREML
+
+    def export(self, g):
+        return export_coreml_package(g)
+
+
+class WebnnExporter(_Exporter):
+    FORMAT = ExportFormat.WEBNN
+
+    def export(self, g):
+        return export_webnn(g)
+
+
+_EXPORTERS = {ExportFormat.ONNX: OnnxExporter, ExportFormat.TFLITE: TfliteExporter,
+              ExportFormat.COREML: CoreMlExporter, ExportFormat.WEBNN: WebnnExporter}
+
+
+def is_op_supported(op: str, fmt: ExportFormat) -> bool:
+    return fmt == ExportFormat.ONNX or op in OP_TABLES[fmt]
+
+
+class ExportBuilder:
+    """``ExportBuilder(graph).format("webnn").build().save(path)``: picks the exporter for a format."""
+
+    def __init__(self, g: GraphIr):
+        self.g, self.fmt = g, ExportFormat.ONNX
+
+    def format(self, fmt) -> "ExportBuilder":
+        self.fmt = ExportFormat(fmt) if not isinstance(fmt, ExportFormat) else fmt
+        return self
+
+    def build(self) -> _Exporter:
+        ex = _EXPORTERS[self.fmt]()
+        if not ex.supports(self.g):
+            bad = sorted({n.op for n in self.g.nodes if not is_op_supported(n.op, self.fmt)})
+            raise ExportError(f"{self.fmt.value} cannot express: {', '.join(bad)}")
+        return ex
+
+
+def export_model(g: GraphIr, fmt, path: str) -> str:
+    return ExportBuilder(g).format(fmt).build().save(g, path)
+
+
+_ONNX_DTYPES = {torch.float32: 1, torch.uint8: 2, torch.int8: 3, torch.int16: 5, torch.int32: 6, torch.int64: 7,
+                torch.bool: 9, torch.float16: 10, torch.float64: 11, torch.bfloat16: 16,
+                torch.float8_e4m3fn: 17, torch.float8_e5m2: 19}
+_TFLITE_DTYPES = {torch.float32: 0, torch.float16: 1, torch.int32: 2, torch.uint8: 3, torch.int64: 4, torch.bool: 6,
+                  torch.int16: 7, torch.int8: 9, torch.float64: 10}
+
+
+def map_dtype_to_onnx(dtype: torch.dtype) -> int:
+    return _ONNX_DTYPES[dtype]
+
+
+def map_dtype_to_tflite(dtype: torch.dtype) -> int:
+    return _TFLITE_DTYPES[dtype]
+
+
+def sanitize_name(name: str) -> str:
+    import re
+    s = re.sub(r"[^0-9A-Za-z_]", "_", name)
+    return s if s and not s[0].isdigit() else "_" + s
+
+
+def align4(n: int) -> int:
+    return (n + 3) & ~3
+
+
+def encode_uleb128(v: int) -> bytes:
+    out = bytearray()
+    while True:
+        b = v & 0x7F
+        v >>= 7
+        out.append(b | (0x80 if v else 0))
+        if not v:
+            return bytes(out)
+
+
+class SafetensorsArchive:
+    """Named tensors written to / read from one ``.safetensors`` file."""
+
+    def __init__(self, tensors: dict | None = None, metadata: dict | None = None):
+        self.tensors, self.metadata = dict(tensors or {}), dict(metadata or {})
+
+    def add(self, name: str, t: torch.Tensor) -> "SafetensorsArchive":
+        self.tensors[name] = t
+        return self
+
+    def save(self, path: str) -> None:
+        from .utils.safetensors import save_safetensors
+        save_safetensors(path, self.tensors, {k: str(v) for k, v in self.metadata.items()})
+
+    @classmethod
+    def load(cls, path: str) -> "SafetensorsArchive":
+        from .utils.safetensors import load_safetensors
+        t, m = load_safetensors(path)
+        return cls(t, m)

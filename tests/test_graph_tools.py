@@ -97,3 +97,20 @@ def test_onnx_entry_points(tmp_path):
 def struct_pack_f(x):
     import struct
     return struct.pack("<f", x)
+
+
+def test_exporters_and_builder(tmp_path):
+    from brain_b200 import export as E
+    g = T.build_mlp_graph([4, 8, 2])
+    for fmt in ("onnx", "webnn", "tflite", "coreml"):
+        p = E.export_model(g, fmt, str(tmp_path / f"m.{fmt}"))
+        assert (tmp_path / f"m.{fmt}").stat().st_size > 0 and p.endswith(fmt)
+    assert E.is_op_supported("linear", E.ExportFormat.ONNX)
+    assert E.map_dtype_to_onnx(torch.bfloat16) == 16 and E.map_dtype_to_tflite(torch.int8) == 9
+    assert E.sanitize_name("1 layer.w") == "_1_layer_w" and E.align4(5) == 8
+    assert E.encode_uleb128(624485) == bytes([0xE5, 0x8E, 0x26])
+    ar = E.SafetensorsArchive().add("w", torch.arange(4.0))
+    ar.metadata["step"] = 3
+    ar.save(str(tmp_path / "a.safetensors"))
+    back = E.SafetensorsArchive.load(str(tmp_path / "a.safetensors"))
+    assert torch.equal(back.tensors["w"], torch.arange(4.0)) and back.metadata.get("step") == "3"
