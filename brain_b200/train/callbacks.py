@@ -152,3 +152,59 @@ class PeriodicCheckpointer(TrainingCallback):
 
     def latest(self):
         return self.saved[-1] if self.saved else None
+
+
+# ------------------------------------------------------------------ the reference's remaining names
+# crates/brain-train/src: callbacks.rs (CallbackAction), checkpointer.rs (check_improvement), lib.rs
+# (argmax_rows, L2Regularization, TrainableModule / TensorModuleAdapter), metrics.rs (windowed averages).
+
+class CallbackAction:
+    """What a callback asks of the loop: keep going or stop."""
+    CONTINUE, STOP = "continue", "stop"
+
+    @staticmethod
+    def from_bool(stop: bool) -> str:
+        return CallbackAction.STOP if stop else CallbackAction.CONTINUE
+
+
+def check_improvement(new: float, best: float | None, mode: str = "min", min_delta: float = 0.0) -> bool:
+    if best is None:
+        return True
+    return new < best - min_delta if mode == "min" else new > best + min_delta
+
+
+def argmax_rows(x) -> list[int]:
+    import torch
+    return torch.as_tensor(x).argmax(-1).tolist()
+
+
+class WindowedAverage:
+    """Mean of the last ``window`` values (the reference's RunningAverage with_window)."""
+
+    def __init__(self, window: int = 100):
+        from collections import deque
+        self.window, self.values = window, deque(maxlen=window)
+
+    def update(self, v: float) -> float:
+        self.values.append(float(v))
+        return self.value
+
+    @property
+    def value(self) -> float:
+        return sum(self.values) / len(self.values) if self.values else 0.0
+
+
+class TensorModuleAdapter:
+    """Wraps a plain function of tensors as a trainable module: parameters are the given tensors."""
+
+    def __init__(self, fn, params):
+        self.fn, self._params = fn, list(params)
+
+    def parameters(self):
+        return iter(self._params)
+
+    def __call__(self, *args):
+        return self.fn(*args)
+
+
+TrainableModule = TensorModuleAdapter

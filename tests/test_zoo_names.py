@@ -79,3 +79,19 @@ def test_rl_names():
     with pytest.raises(ValueError):
         RA.make_agent("nope", 4, 2)
     assert RA.compute_gae is RL.gae and RA.CartPoleEnv is RA._envs.CartPole
+
+
+def test_train_names():
+    from brain_b200 import train as TR
+    assert TR.CallbackAction.from_bool(True) == "stop" and TR.CallbackAction.from_bool(False) == "continue"
+    assert TR.check_improvement(0.5, None) and TR.check_improvement(0.5, 0.6) and not TR.check_improvement(0.59, 0.6, min_delta=0.05)
+    assert TR.check_improvement(0.9, 0.8, mode="max")
+    assert TR.argmax_rows([[0.1, 0.9], [0.7, 0.3]]) == [1, 0]
+    w = TR.WindowedAverage(2)
+    w.update(1.0)
+    w.update(3.0)
+    assert w.update(5.0) == 4.0
+    p = torch.ones(2, requires_grad=True)
+    m = TR.TrainableModule(lambda x: x * p, [p])
+    assert list(m.parameters())[0] is p and m(torch.tensor([2.0, 3.0])).tolist() == [2.0, 3.0]
+    assert TR.L2Regularization is TR.L2Regularizer
