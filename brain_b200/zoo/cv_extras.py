@@ -438,3 +438,84 @@ class SegMetrics:
         tp = self.cm.diag().double()
         den = self.cm.sum(0).double() + self.cm.sum(1).double()
         return torch.where(den > 0, 2 * tp / den.clamp_min(1), torch.full_like(tp, float("nan")))
+
+
+# ------------------------------------------------------------------ MobileNetV3 (Howard et al. 2019), small / large
+# crates/brain-cv/src/feature/backbones.rs (mobilenet_v3). Inverted residual blocks: 1x1 expansion,
+# depthwise k x k (stride s), optional squeeze-excitation (hard-sigmoid gate), 1x1 projection,
+# residual when the shape is kept; hard-swish or ReLU per block.
+
+class _SqueezeExcite(torch.nn.Module):
+    def __init__(self, c: int, r: int = 4):
+        super().__init__()
+        m = max(8, c // r)
+        self.fc1, self.fc2 = torch.nn.Conv2d(c, m, 1), torch.nn.Conv2d(m, c, 1)
+
+    def forward(self, x):
+        s = F.adaptive_avg_pool2d(x, 1)
+        return x * F.hardsigmoid(self.fc2(F.relu(self.fc1(s))))
+
+
+class InvertedResidual(torch.nn.Module):
+    def __init__(self, cin: int, k: int, exp: int, cout: int, se: bool, act: str, stride: int):
+        super().__init__()
+        a = torch.nn.Hardswish if act == "hs" else torch.nn.ReLU
+        layers = []
+        if exp != cin:
+            layers += [torch.nn.Conv2d(cin, exp, 1, bias=False), torch.nn.BatchNorm2d(exp), a()]
+        layers += [torch.nn.Conv2d(exp, exp, k, stride, k // 2, groups=exp, bias=False), torch.nn.BatchNorm2d(exp), a()]
+        if se:
+            layers.append(_SqueezeExcite(exp))
+        layers += [torch.nn.Conv2d(exp, cout, 1, bias=False), torch.nn.BatchNorm2d(cout)]
+        self.block = torch.nn.Sequential(*layers)
+        self.residual = stride == 1 and cin == cout
+
+    def forward(self, x):
+        y = self.block(x)
+        return x + y if self.residual else y
+
+
+_MBV3 = {  # (kernel, expansion, out, squeeze-excite, activation, stride)
+    "small": [(3, 16, 16, True, "re", 2), (3, 72, 24, False, "re", 2), (3, 88, 24, False, "re", 1),
+              (5, 96, 40, True, "hs", 2), (5, 240, 40, True, "hs", 1), (5, 240, 40, True, "hs", 1),
+              (5, 120, 48, True, "hs", 1), (5, 144, 48, True, "hs", 1), (5, 288, 96, True, "hs", 2),
+              (5, 576, 96, True, "hs", 1), (5, 576, 96, True, "hs", 1)],
+    "large": [(3, 16, 16, False, "re", 1), (3, 64, 24, False, "re", 2), (3, 72, 24, False, "re", 1),
+              (5, 72, 40, True, "re", 2), (5, 120, 40, True, "re", 1), (5, 120, 40, True, "re", 1),
+              (3, 240, 80, False, "hs", 2), (3, 200, 80, False, "hs", 1), (3, 184, 80, False, "hs", 1),
+              (3, 184, 80, False, "hs", 1), (3, 480, 112, True, "hs", 1), (3, 672, 112, True, "hs", 1),
+              (5, 672, 160, True, "hs", 2), (5, 960, 160, True, "hs", 1), (5, 960, 160, True, "hs", 1)],
+}
+
+
+class MobileNetV3(torch.nn.Module):
+    """``variant`` small or large; ``width`` scales every channel count (rounded to multiples of 8)."""
+
+    def __init__(self, num_classes: int = 1000, variant: str = "small", width: float = 1.0, in_channels: int = 3):
+        super().__init__()
+
+        def c(v):
+            return max(8, int(v * width + 4) // 8 * 8)
+        layers = [torch.nn.Conv2d(in_channels, c(16), 3, 2, 1, bias=False), torch.nn.BatchNorm2d(c(16)),
+                  torch.nn.Hardswish()]
+        cin = c(16)
+        for k, e, o, se, act, s in _MBV3[variant]:
+            layers.append(InvertedResidual(cin, k, c(e), c(o), se, act, s))
+            cin = c(o)
+        last = c(576 if variant == "small" else 960)
+        layers += [torch.nn.Conv2d(cin, last, 1, bias=False), torch.nn.BatchNorm2d(last), torch.nn.Hardswish()]
+        self.features = torch.nn.Sequential(*layers)
+        hidden = 1024 if variant == "small" else 1280
+        self.classifier = torch.nn.Sequential(torch.nn.Linear(last, hidden), torch.nn.Hardswish(),
+                                              torch.nn.Dropout(0.2), torch.nn.Linear(hidden, num_classes))
+        self.out_channels = last
+
+    def forward_features(self, x):
+        return self.features(x)
+
+    def forward(self, x):
+        return self.classifier(F.adaptive_avg_pool2d(self.features(x), 1).flatten(1))
+
+
+def mobilenet_v3(num_classes: int = 1000, variant: str = "small", width: float = 1.0) -> MobileNetV3:
+    return MobileNetV3(num_classes, variant, width)

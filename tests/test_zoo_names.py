@@ -95,3 +95,20 @@ def test_train_names():
     m = TR.TrainableModule(lambda x: x * p, [p])
     assert list(m.parameters())[0] is p and m(torch.tensor([2.0, 3.0])).tolist() == [2.0, 3.0]
     assert TR.L2Regularization is TR.L2Regularizer
+
+
+def test_mobilenet_v3():
+    from brain_b200.zoo.cv_extras import mobilenet_v3, InvertedResidual
+    torch.manual_seed(0)
+    m = mobilenet_v3(10, "small")
+    y = m(torch.randn(2, 3, 64, 64))
+    assert y.shape == (2, 10)
+    n = sum(p.numel() for p in m.parameters())
+    assert 1.3e6 < n < 1.7e6  # the published small variant: about 2.5 M parameters with a 1000-class head
+    assert m.forward_features(torch.randn(1, 3, 64, 64)).shape == (1, 576, 2, 2)
+    blk = InvertedResidual(16, 3, 64, 16, True, "hs", 1)
+    assert blk.residual and blk(torch.randn(1, 16, 8, 8)).shape == (1, 16, 8, 8)
+    m.train()
+    loss = torch.nn.functional.cross_entropy(m(torch.randn(4, 3, 32, 32)), torch.tensor([0, 1, 2, 3]))
+    loss.backward()
+    assert all(p.grad is not None for p in m.parameters() if p.requires_grad)
